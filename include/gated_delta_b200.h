@@ -1,0 +1,111 @@
+/* gated_delta_b200.h -- C ABI of the B200 (sm_100a) chunked gated delta rule.
+ *
+ * The reference (AbstractEyes/Mac-ai-engineering, package macai) reaches its GPU code through Metal kernels compiled by
+ * torch.mps.compile_shader and dispatched as lib.<kernel>(...). Each entry point below replaces one of those dispatch
+ * sites (cited as reference file:line), or one autograd step that sequences them. Every function:
+ *   - takes raw device pointers, sizes and a CUDA stream (cudaStream_t passed as void*), no torch types;
+ *   - allocates nothing: intermediates live in a caller-provided workspace of gd_workspace_bytes();
+ *   - launches on the given stream and does not synchronise (graph-capturable), except gd_read_error;
+ *   - returns a status code (GD_OK or a GD_ERR_*) and never aborts or traps.
+ *
+ * Layouts (all contiguous, row-major):
+ *   q, k        [B, T, HK, DK]   dtype GD_FLOAT32 / GD_FLOAT16 / GD_BFLOAT16 (q, k, v, o, do share one dtype)
+ *   v, o, do    [B, T, H, DV]    H = value heads; HK = key heads, H % HK == 0 (HK < H: each key head serves H/HK
+ *                                consecutive value heads, the repeat_interleave of the Qwen3.5 layer)
+ *   g, beta     [B, T, H]        float32 (g = log decay <= 0)
+ *   s0, sT, dsT, ds0 [B, H, DK, DV] float32
+ *   dg, dbeta   [B, T, H]        float32;  dq, dk [B, T, HK, DK] and dv [B, T, H, DV] in the q/k/v dtype
+ * Supported head widths: DK = DV = 128 (the Qwen3.5 / Qwen3-Next shapes). Chunk length 64 (fixed).
+ */
+#ifndef GATED_DELTA_B200_H
+#define GATED_DELTA_B200_H
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes */
+#define GD_OK 0
+#define GD_ERR_ARG 1       /* null pointer, unknown dtype or flag */
+#define GD_ERR_SHAPE 2     /* unsupported sizes (head widths, H % HK) */
+#define GD_ERR_ALIGN 3     /* a pointer is not 16-byte aligned */
+#define GD_ERR_WORKSPACE 4 /* workspace smaller than gd_workspace_bytes() */
+#define GD_ERR_LAUNCH 5    /* the CUDA launch failed */
+#define GD_ERR_TIMEOUT 6   /* a bounded device-side wait gave up (recorded in the workspace's error word) */
+#define GD_ERR_DEVICE 7    /* the current device is not sm_100 */
+
+/* dtypes of q / k / v / o / do and of dq / dk / dv */
+#define GD_FLOAT32 0
+#define GD_FLOAT16 1
+#define GD_BFLOAT16 2
+
+/* flags */
+#define GD_L2NORM 1        /* use_qk_l2norm_in_kernel: q and k rows are l2-normalised (eps 1e-6) in the prep kernel */
+#define GD_STORE_STATES 2  /* the state pass keeps each chunk's entering state S_c and Vn for the backward */
+#define GD_SCALE_Q 4       /* q is multiplied by DK^-1/2 (after the l2 norm): the drop-in's query scaling */
+
+/* Text for a status code. */
+const char* gd_status_string(int status);
+
+/* Workspace bytes for one call of these sizes. for_backward != 0: enough for gd_backward (and for gd_forward). */
+size_t gd_workspace_bytes(int B, int T, int H, int HK, int DK, int DV, int for_backward);
+
+/* Per chunk (64 tokens) of every (batch row, value head), all independent: the l2 prologue of q and k, the in-chunk
+ * cumulative log decay G, M = (Q K^T) * exp(G_i - G_j) (lower, diagonal included), the inverse A = (I + L)^-1 of
+ * L = diag(beta) (K K^T) * exp(G_i - G_j) (strictly lower), W = A diag(beta gamma) K and U = A diag(beta) V, all into
+ * the workspace.
+ * Replaces: lib.gdc_prep (src/macai/gated_delta/op.py:63-72, kernel _chunked.py:220-313) and the fused prologue
+ * l2n_fwd_* (src/macai/gated_delta/_norm.py:27-43, applied at op.py:276-278), with W and U of gdc_fwd's first stage. */
+int gd_prep(const void* q, const void* k, const void* v, const float* g, const float* beta, int dtype, int B, int T,
+            int H, int HK, int DK, int DV, int flags, void* workspace, size_t workspace_bytes, void* stream);
+
+/* The sequential state pass, one CTA per (batch row, value head): for each chunk in order,
+ * Vn = U - W S, O = diag(gamma) Q S + M Vn, S <- exp(G_last) S + K^T diag(e) Vn; writes o (q's dtype) and, when sT is
+ * not NULL, the final state. s0 NULL = zero initial state. flags & GD_STORE_STATES: keeps S_c and Vn per chunk in
+ * the workspace (the backward's recompute; o and sT may then be NULL).
+ * Replaces: lib.gdc_fwd (src/macai/gated_delta/op.py:159 and :217, kernel _chunked.py:315-659). Requires gd_prep. */
+int gd_fwd_state(const float* s0, void* o, float* sT, int dtype, int B, int T, int H, int HK, int DK, int DV,
+                 int flags, void* workspace, size_t workspace_bytes, void* stream);
+
+/* The reverse state pass, one CTA per (batch row, value head), chunks last to first, carrying dS:
+ * dVn = M^T dO + diag(e) K dS, dS <- exp(G_last) dS + (diag(gamma) Q)^T dO - W^T dVn; keeps dS_{c+1} and dVn per
+ * chunk in the workspace and writes ds0 (may be NULL). dsT NULL = zero. Requires gd_prep and
+ * gd_fwd_state(GD_STORE_STATES) on the same workspace.
+ * Replaces: lib.gdc_bwd_state (src/macai/gated_delta/op.py:234, kernel _chunked.py:661-903). */
+int gd_bwd_state(const void* d_o, const float* dsT, float* ds0, int dtype, int B, int T, int H, int HK, int DK, int DV,
+                 int flags, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Every per-chunk gradient, one CTA per (chunk, key head, batch row), all independent and without atomics: dq, dk
+ * (through the l2 prologue when GD_L2NORM; summed over the value heads of a key head in a fixed order), dv, dg (with
+ * the in-chunk reverse cumulative sum) and dbeta. Requires gd_bwd_state on the same workspace.
+ * Replaces: lib.gdc_bwd_chunk (src/macai/gated_delta/op.py:241-242, kernel _chunked.py:905-1177) and the fused
+ * prologue's backward l2n_bwd_* (src/macai/gated_delta/_norm.py:44-56, applied at :102-114). */
+int gd_bwd_chunk(const void* q, const void* k, const void* v, const float* beta, const void* d_o, void* dq, void* dk,
+                 void* dv, float* dg, float* dbeta, int dtype, int B, int T, int H, int HK, int DK, int DV, int flags,
+                 void* workspace, size_t workspace_bytes, void* stream);
+
+/* The forward of the autograd function: gd_prep then gd_fwd_state.
+ * Replaces: GatedDeltaRule.forward (src/macai/gated_delta/op.py:119-185) as called by the drop-in (op.py:296). */
+int gd_forward(const void* q, const void* k, const void* v, const float* g, const float* beta, const float* s0,
+               void* o, float* sT, int dtype, int B, int T, int H, int HK, int DK, int DV, int flags, void* workspace,
+               size_t workspace_bytes, void* stream);
+
+/* The backward with the chunk states recomputed from the inputs: gd_prep, gd_fwd_state(GD_STORE_STATES),
+ * gd_bwd_state, gd_bwd_chunk. d_o / dsT NULL = zero cotangents; ds0 may be NULL.
+ * Replaces: GatedDeltaRule.backward in its recompute mode (src/macai/gated_delta/op.py:187-243, :207-218). */
+int gd_backward(const void* q, const void* k, const void* v, const float* g, const float* beta, const float* s0,
+                const void* d_o, const float* dsT, void* dq, void* dk, void* dv, float* dg, float* dbeta, float* ds0,
+                int dtype, int B, int T, int H, int HK, int DK, int DV, int flags, void* workspace,
+                size_t workspace_bytes, void* stream);
+
+/* Synchronises the stream and returns the first device-side failure recorded in the workspace's error word (GD_OK if
+ * none), with the kernel stage that recorded it in *where (may be NULL); then clears the word. */
+int gd_read_error(void* workspace, void* stream, int* where);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GATED_DELTA_B200_H */

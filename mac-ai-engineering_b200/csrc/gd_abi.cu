@@ -1,0 +1,224 @@
+// The C ABI (include/gated_delta_b200.h): argument checks, dispatch on dtype and head widths, kernel sequencing.
+// No entry point allocates, synchronises (except gd_read_error) or aborts.
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "gd_common.cuh"
+#include "gd_layout.cuh"
+
+namespace gd {
+template <typename T, int DK, int DV>
+cudaError_t launch_prep(const void*, const void*, const void*, const float*, const float*, const Layout&, int,
+                        unsigned char*, cudaStream_t);
+template <typename T, int DK, int DV>
+cudaError_t launch_state(const float*, void*, float*, const Layout&, int, unsigned char*, cudaStream_t);
+template <typename T, int DK, int DV>
+cudaError_t launch_bwd_state(const void*, const float*, float*, const Layout&, int, unsigned char*, cudaStream_t);
+template <typename T, int DK, int DV>
+cudaError_t launch_bwd_chunk(const void*, const void*, const void*, const float*, const void*, void*, void*, void*,
+                             float*, float*, const Layout&, int, unsigned char*, cudaStream_t);
+}  // namespace gd
+
+namespace {
+
+using gd::Layout;
+
+bool aligned16(const void* p) { return p == nullptr || (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int check_dims(int B, int T, int H, int HK, int DK, int DV, int dtype) {
+  if (B <= 0 || T <= 0 || H <= 0 || HK <= 0) return GD_ERR_SHAPE;
+  if (H % HK != 0) return GD_ERR_SHAPE;
+  if (DK != 128 || DV != 128) return GD_ERR_SHAPE;
+  if (dtype != GD_FLOAT32 && dtype != GD_FLOAT16 && dtype != GD_BFLOAT16) return GD_ERR_ARG;
+  if ((long long)B * H * ((T + 63) / 64) > (1ll << 31) - 1) return GD_ERR_SHAPE;
+  if (H > 65535 || B > 65535) return GD_ERR_SHAPE;
+  return GD_OK;
+}
+
+int check_device() {
+  static int cached = -1;  // per process; the library serves sm_100 devices only
+  if (cached >= 0) return cached;
+  int dev = 0, major = 0, minor = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return GD_ERR_DEVICE;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return GD_ERR_DEVICE;
+  if (cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess) return GD_ERR_DEVICE;
+  cached = (major == 10 && minor == 0) ? GD_OK : GD_ERR_DEVICE;
+  return cached;
+}
+
+int launched(cudaError_t e) { return e == cudaSuccess ? GD_OK : GD_ERR_LAUNCH; }
+
+int prep(const void* q, const void* k, const void* v, const float* g, const float* beta, int dtype, const Layout& L,
+         int flags, void* ws, cudaStream_t st) {
+  auto w = static_cast<unsigned char*>(ws);
+  switch (dtype) {
+    case GD_BFLOAT16: return launched(gd::launch_prep<__nv_bfloat16, 128, 128>(q, k, v, g, beta, L, flags, w, st));
+    case GD_FLOAT16: return launched(gd::launch_prep<__half, 128, 128>(q, k, v, g, beta, L, flags, w, st));
+    default: return launched(gd::launch_prep<float, 128, 128>(q, k, v, g, beta, L, flags, w, st));
+  }
+}
+
+int fwd_state(const float* s0, void* o, float* sT, int dtype, const Layout& L, int flags, void* ws, cudaStream_t st) {
+  auto w = static_cast<unsigned char*>(ws);
+  switch (dtype) {
+    case GD_BFLOAT16: return launched(gd::launch_state<__nv_bfloat16, 128, 128>(s0, o, sT, L, flags, w, st));
+    case GD_FLOAT16: return launched(gd::launch_state<__half, 128, 128>(s0, o, sT, L, flags, w, st));
+    default: return launched(gd::launch_state<float, 128, 128>(s0, o, sT, L, flags, w, st));
+  }
+}
+
+int bwd_state(const void* d_o, const float* dsT, float* ds0, int dtype, const Layout& L, int flags, void* ws,
+              cudaStream_t st) {
+  auto w = static_cast<unsigned char*>(ws);
+  switch (dtype) {
+    case GD_BFLOAT16: return launched(gd::launch_bwd_state<__nv_bfloat16, 128, 128>(d_o, dsT, ds0, L, flags, w, st));
+    case GD_FLOAT16: return launched(gd::launch_bwd_state<__half, 128, 128>(d_o, dsT, ds0, L, flags, w, st));
+    default: return launched(gd::launch_bwd_state<float, 128, 128>(d_o, dsT, ds0, L, flags, w, st));
+  }
+}
+
+int bwd_chunk(const void* q, const void* k, const void* v, const float* beta, const void* d_o, void* dq, void* dk,
+              void* dv, float* dg, float* dbeta, int dtype, const Layout& L, int flags, void* ws, cudaStream_t st) {
+  auto w = static_cast<unsigned char*>(ws);
+  switch (dtype) {
+    case GD_BFLOAT16:
+      return launched(gd::launch_bwd_chunk<__nv_bfloat16, 128, 128>(q, k, v, beta, d_o, dq, dk, dv, dg, dbeta, L,
+                                                                     flags, w, st));
+    case GD_FLOAT16:
+      return launched(
+          gd::launch_bwd_chunk<__half, 128, 128>(q, k, v, beta, d_o, dq, dk, dv, dg, dbeta, L, flags, w, st));
+    default:
+      return launched(
+          gd::launch_bwd_chunk<float, 128, 128>(q, k, v, beta, d_o, dq, dk, dv, dg, dbeta, L, flags, w, st));
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* gd_status_string(int status) {
+  switch (status) {
+    case GD_OK: return "ok";
+    case GD_ERR_ARG: return "invalid argument (null pointer, dtype or flag)";
+    case GD_ERR_SHAPE: return "unsupported sizes (head widths must be 128; value heads a multiple of key heads)";
+    case GD_ERR_ALIGN: return "a pointer is not 16-byte aligned";
+    case GD_ERR_WORKSPACE: return "workspace smaller than gd_workspace_bytes()";
+    case GD_ERR_LAUNCH: return "CUDA kernel launch failed";
+    case GD_ERR_TIMEOUT: return "a device-side wait gave up (kernel stage recorded in the error word)";
+    case GD_ERR_DEVICE: return "the current CUDA device is not sm_100 (B200)";
+    default: return "unknown status";
+  }
+}
+
+size_t gd_workspace_bytes(int B, int T, int H, int HK, int DK, int DV, int for_backward) {
+  if (check_dims(B, T, H, HK, DK, DV, GD_BFLOAT16) != GD_OK) return 0;
+  return Layout::make(B, T, H, HK, DK, DV, for_backward != 0).total;
+}
+
+int gd_prep(const void* q, const void* k, const void* v, const float* g, const float* beta, int dtype, int B, int T,
+            int H, int HK, int DK, int DV, int flags, void* workspace, size_t workspace_bytes, void* stream) {
+  int s = check_dims(B, T, H, HK, DK, DV, dtype);
+  if (s) return s;
+  if (!q || !k || !v || !g || !beta || !workspace) return GD_ERR_ARG;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(workspace)) return GD_ERR_ALIGN;
+  if ((s = check_device())) return s;
+  // the layout kind (forward-only or backward) follows the workspace size the caller provides
+  Layout L = Layout::make(B, T, H, HK, DK, DV, true);
+  if (workspace_bytes < L.total) L = Layout::make(B, T, H, HK, DK, DV, false);
+  if (workspace_bytes < L.total) return GD_ERR_WORKSPACE;
+  // every call sequence starts here: clear the error word (stream-ordered, no allocation)
+  if (cudaMemsetAsync(workspace, 0, sizeof(gd::ErrorWord), static_cast<cudaStream_t>(stream)) != cudaSuccess)
+    return GD_ERR_LAUNCH;
+  return prep(q, k, v, g, beta, dtype, L, flags, workspace, static_cast<cudaStream_t>(stream));
+}
+
+int gd_fwd_state(const float* s0, void* o, float* sT, int dtype, int B, int T, int H, int HK, int DK, int DV,
+                 int flags, void* workspace, size_t workspace_bytes, void* stream) {
+  int s = check_dims(B, T, H, HK, DK, DV, dtype);
+  if (s) return s;
+  if (!workspace) return GD_ERR_ARG;
+  if (!aligned16(workspace)) return GD_ERR_ALIGN;
+  if ((s = check_device())) return s;
+  Layout L = Layout::make(B, T, H, HK, DK, DV, true);
+  if (workspace_bytes < L.total) {
+    if (flags & GD_STORE_STATES) return GD_ERR_WORKSPACE;
+    L = Layout::make(B, T, H, HK, DK, DV, false);
+  }
+  if (workspace_bytes < L.total) return GD_ERR_WORKSPACE;
+  return fwd_state(s0, o, sT, dtype, L, flags, workspace, static_cast<cudaStream_t>(stream));
+}
+
+int gd_bwd_state(const void* d_o, const float* dsT, float* ds0, int dtype, int B, int T, int H, int HK, int DK, int DV,
+                 int flags, void* workspace, size_t workspace_bytes, void* stream) {
+  int s = check_dims(B, T, H, HK, DK, DV, dtype);
+  if (s) return s;
+  if (!workspace) return GD_ERR_ARG;
+  if (!aligned16(workspace) || !aligned16(d_o)) return GD_ERR_ALIGN;
+  if ((s = check_device())) return s;
+  Layout L = Layout::make(B, T, H, HK, DK, DV, true);
+  if (workspace_bytes < L.total) return GD_ERR_WORKSPACE;
+  return bwd_state(d_o, dsT, ds0, dtype, L, flags, workspace, static_cast<cudaStream_t>(stream));
+}
+
+int gd_bwd_chunk(const void* q, const void* k, const void* v, const float* beta, const void* d_o, void* dq, void* dk,
+                 void* dv, float* dg, float* dbeta, int dtype, int B, int T, int H, int HK, int DK, int DV, int flags,
+                 void* workspace, size_t workspace_bytes, void* stream) {
+  int s = check_dims(B, T, H, HK, DK, DV, dtype);
+  if (s) return s;
+  if (!q || !k || !v || !beta || !dq || !dk || !dv || !dg || !dbeta || !workspace) return GD_ERR_ARG;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(d_o) || !aligned16(dq) || !aligned16(dk) ||
+      !aligned16(dv) || !aligned16(workspace))
+    return GD_ERR_ALIGN;
+  if ((s = check_device())) return s;
+  Layout L = Layout::make(B, T, H, HK, DK, DV, true);
+  if (workspace_bytes < L.total) return GD_ERR_WORKSPACE;
+  return bwd_chunk(q, k, v, beta, d_o, dq, dk, dv, dg, dbeta, dtype, L, flags, workspace,
+                   static_cast<cudaStream_t>(stream));
+}
+
+int gd_forward(const void* q, const void* k, const void* v, const float* g, const float* beta, const float* s0,
+               void* o, float* sT, int dtype, int B, int T, int H, int HK, int DK, int DV, int flags, void* workspace,
+               size_t workspace_bytes, void* stream) {
+  int s = gd_prep(q, k, v, g, beta, dtype, B, T, H, HK, DK, DV, flags & (GD_L2NORM | GD_SCALE_Q), workspace,
+                  workspace_bytes, stream);
+  if (s) return s;
+  if (!o) return GD_ERR_ARG;
+  if (!aligned16(o)) return GD_ERR_ALIGN;
+  return gd_fwd_state(s0, o, sT, dtype, B, T, H, HK, DK, DV, flags & ~GD_STORE_STATES, workspace, workspace_bytes,
+                      stream);
+}
+
+int gd_backward(const void* q, const void* k, const void* v, const float* g, const float* beta, const float* s0,
+                const void* d_o, const float* dsT, void* dq, void* dk, void* dv, float* dg, float* dbeta, float* ds0,
+                int dtype, int B, int T, int H, int HK, int DK, int DV, int flags, void* workspace,
+                size_t workspace_bytes, void* stream) {
+  int s = check_dims(B, T, H, HK, DK, DV, dtype);
+  if (s) return s;
+  if (workspace_bytes < Layout::make(B, T, H, HK, DK, DV, true).total) return GD_ERR_WORKSPACE;
+  const int f = flags & (GD_L2NORM | GD_SCALE_Q);
+  if ((s = gd_prep(q, k, v, g, beta, dtype, B, T, H, HK, DK, DV, f, workspace, workspace_bytes, stream))) return s;
+  if ((s = gd_fwd_state(s0, nullptr, nullptr, dtype, B, T, H, HK, DK, DV, f | GD_STORE_STATES, workspace,
+                        workspace_bytes, stream)))
+    return s;
+  if ((s = gd_bwd_state(d_o, dsT, ds0, dtype, B, T, H, HK, DK, DV, f, workspace, workspace_bytes, stream))) return s;
+  return gd_bwd_chunk(q, k, v, beta, d_o, dq, dk, dv, dg, dbeta, dtype, B, T, H, HK, DK, DV, f, workspace,
+                      workspace_bytes, stream);
+}
+
+int gd_read_error(void* workspace, void* stream, int* where) {
+  if (!workspace) return GD_ERR_ARG;
+  gd::ErrorWord w{};
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (cudaMemcpyAsync(&w, workspace, sizeof(w), cudaMemcpyDeviceToHost, st) != cudaSuccess) return GD_ERR_LAUNCH;
+  if (cudaStreamSynchronize(st) != cudaSuccess) return GD_ERR_LAUNCH;
+  if (w.code != 0) {
+    gd::ErrorWord zero{};
+    cudaMemcpyAsync(workspace, &zero, sizeof(zero), cudaMemcpyHostToDevice, st);
+    cudaStreamSynchronize(st);
+  }
+  if (where) *where = w.where;
+  return w.code;
+}
+
+}  // extern "C"

@@ -1,0 +1,350 @@
+// Shared device helpers for the chunked gated delta rule kernels (sm_100a only).
+//
+// - tcgen05 tensor-core primitives: TMEM allocation, bf16 x bf16 -> fp32 MMA from shared-memory descriptors, commit to an
+//   mbarrier, TMEM -> register loads. Encodings follow the PTX ISA (tcgen05 instruction and shared-memory matrix
+//   descriptors, the SWIZZLE_NONE canonical layouts).
+// - bounded mbarrier waits: every wait gives up after a fixed number of SM clocks, records GD_ERR_TIMEOUT in the call's error
+//   word and lets the kernel fall through to its clean-up (TMEM is always freed); no kernel traps or spins forever.
+// - the "blocked" bf16 tile layout used for every MMA operand: a [R x C] matrix (R, C multiples of 8) is stored as 8 x 8
+//   core matrices of 128 contiguous bytes (8 rows of 16 bytes), core (rb, cb) at byte ((rb * C/8) + cb) * 128. The same
+//   bytes serve as a K-major operand (rows = M or N, cols = K) or an MN-major one (rows = K, cols = M or N); only the
+//   descriptor's two strides differ.
+#pragma once
+
+#include <cstdint>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "gated_delta_b200.h"
+
+namespace gd {
+
+constexpr int C = 64;                      // chunk length (tokens); every chunk matrix is C x C
+constexpr long long kWaitCycles = 4000000000ll;  // SM clocks a wait may take before it gives up (~2 s at 1.9 GHz)
+
+// ------------------------------------------------------------------------------------------------------------------
+// error word: the first 64 bytes of every workspace; kernels set the first failure code and the place it happened
+
+struct ErrorWord {
+  int code;
+  int where;
+  int block;
+  int pad[13];
+};
+
+__device__ __forceinline__ void report(ErrorWord* err, int code, int where) {
+  if (err != nullptr && atomicCAS(&err->code, 0, code) == 0) {
+    err->where = where;
+    err->block = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+  }
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// shared memory, fences, mbarriers, bulk copies
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Waits for the phase with this parity to complete. Returns false (and records a timeout) if it does not within the
+// poll limit; callers then skip their remaining work and go to clean-up.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, ErrorWord* err, int where) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (clock64() - t0 > kWaitCycles) {
+      report(err, GD_ERR_TIMEOUT, where);
+      return false;
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+// 1-D bulk copy (TMA engine) global -> shared, completion counted on the mbarrier in bytes. Both addresses 16-byte
+// aligned, size a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// 1-D bulk copy shared -> global (TMA engine), tracked by the issuing thread's bulk async-group.
+__device__ __forceinline__ void bulk_s2g(void* dst, const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(smem_u32(src)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// generic-proxy shared-memory writes -> visible to the async proxy (tensor core, bulk copies)
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// ------------------------------------------------------------------------------------------------------------------
+// tcgen05
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {  // one full warp
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {  // one full warp
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Instruction descriptor, kind::f16 with bf16 A and B, fp32 accumulator. a_mn / b_mn: operand is MN-major.
+__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, bool a_mn, bool b_mn) {
+  return (1u << 4)                          // D format: f32
+         | (1u << 7)                        // A format: bf16
+         | (1u << 10)                       // B format: bf16
+         | ((a_mn ? 1u : 0u) << 15)         // A major
+         | ((b_mn ? 1u : 0u) << 16)         // B major
+         | ((uint32_t)(N >> 3) << 17)       // N / 8
+         | ((uint32_t)(M >> 4) << 24);      // M / 16
+}
+
+// Shared-memory matrix descriptor, SWIZZLE_NONE. lbo: byte stride between 8-element groups along K;
+// sbo: byte stride between 8-row groups along M (or N).
+__device__ __forceinline__ uint64_t sdesc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+  return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+         ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
+}
+
+__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+// A bf16 tile in the blocked layout: smem byte address and its column count (the row-block stride is cols/8 * 128 B).
+struct Tile {
+  uint32_t addr;
+  uint32_t cols;
+  __device__ __forceinline__ uint32_t rowblk_bytes() const { return (cols / 8) * 128; }
+};
+
+// D[M x N] (+)= X[M x K] . Y[K x N], every operand a blocked tile.
+//   x_rows_m: X's tile rows index M (K-major A); otherwise the tile is X^T (rows index K: MN-major A).
+//   y_rows_k: Y's tile rows index K (MN-major B); otherwise the tile is Y^T (rows index N: K-major B).
+// (m0, n0, k0) select a sub-block of the tiles (multiples of 8, 8, 16). Issued by one thread.
+__device__ __forceinline__ void mma_tiles(uint32_t d_tmem, int M, int N, int K, Tile x, bool x_rows_m, int m0, int k0,
+                                          Tile y, bool y_rows_k, int n0, bool accumulate) {
+  const uint32_t idesc = idesc_bf16(M, N, !x_rows_m, y_rows_k);
+  uint32_t xa, x_lbo, x_sbo, x_step, ya, y_lbo, y_sbo, y_step;
+  if (x_rows_m) {  // K-major: K groups adjacent (128 B), M groups one row block apart
+    xa = x.addr + (m0 / 8) * x.rowblk_bytes() + (k0 / 8) * 128;
+    x_lbo = 128;
+    x_sbo = x.rowblk_bytes();
+    x_step = 256;
+  } else {  // MN-major: M groups adjacent, K groups one row block apart
+    xa = x.addr + (k0 / 8) * x.rowblk_bytes() + (m0 / 8) * 128;
+    x_lbo = x.rowblk_bytes();
+    x_sbo = 128;
+    x_step = 2 * x.rowblk_bytes();
+  }
+  if (y_rows_k) {  // MN-major B
+    ya = y.addr + (k0 / 8) * y.rowblk_bytes() + (n0 / 8) * 128;
+    y_lbo = y.rowblk_bytes();
+    y_sbo = 128;
+    y_step = 2 * y.rowblk_bytes();
+  } else {  // K-major B
+    ya = y.addr + (n0 / 8) * y.rowblk_bytes() + (k0 / 8) * 128;
+    y_lbo = 128;
+    y_sbo = y.rowblk_bytes();
+    y_step = 256;
+  }
+  for (int kk = 0; kk < K / 16; ++kk) {
+    mma_bf16(d_tmem, sdesc(xa + kk * x_step, x_lbo, x_sbo), sdesc(ya + kk * y_step, y_lbo, y_sbo), idesc,
+             (accumulate || kk > 0) ? 1u : 0u);
+  }
+}
+
+// TMEM -> registers: this warp's 32 lanes, 32 consecutive fp32 columns each (thread t gets lane (lane_base + t)).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// TMEM address of column `col` in the lane quadrant of this warp (warps w and w+4 share a quadrant).
+__device__ __forceinline__ uint32_t tmem_lane_addr(uint32_t base, int warp, int col) {
+  return base + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)col;
+}
+
+// The accumulator row a thread owns after a tcgen05.ld 32x32b: M = 128 -> row = lane; M = 64 -> rows live in lanes
+// 0-15 of each quadrant (row = 16 * quadrant + lane), lanes 16-31 hold nothing.
+__device__ __forceinline__ int acc_row(int M, int warp, int lane) {
+  return M == 128 ? 32 * (warp & 3) + lane : (lane < 16 ? 16 * (warp & 3) + lane : -1);
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// blocked-tile element addressing and conversions
+
+__host__ __device__ constexpr uint32_t blk_off(int r, int c, int cols) {  // byte offset of bf16 element (r, c)
+  return (uint32_t)((((r >> 3) * (cols >> 3) + (c >> 3)) << 7) + ((r & 7) << 4) + ((c & 7) << 1));
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Split x into hi + lo, both bf16: hi = bf16(x), lo = bf16(x - hi). hi + lo carries ~16 significant bits.
+__device__ __forceinline__ void split_bf16(float x, float& hi, float& lo) {
+  hi = __bfloat162float(__float2bfloat16_rn(x));
+  lo = x - hi;
+}
+
+// 8 consecutive floats of one tile row -> one 16-byte blocked-row segment (bf16)
+__device__ __forceinline__ void store8_bf16(unsigned char* tile, int r, int c0, int cols, const float* v) {
+  uint4 u;
+  u.x = pack_bf16(v[0], v[1]);
+  u.y = pack_bf16(v[2], v[3]);
+  u.z = pack_bf16(v[4], v[5]);
+  u.w = pack_bf16(v[6], v[7]);
+  *reinterpret_cast<uint4*>(tile + blk_off(r, c0, cols)) = u;
+}
+
+// the same with a hi / lo split into two tiles
+__device__ __forceinline__ void store8_split(unsigned char* hi_tile, unsigned char* lo_tile, int r, int c0, int cols,
+                                             const float* v) {
+  float h[8], l[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) split_bf16(v[i], h[i], l[i]);
+  store8_bf16(hi_tile, r, c0, cols, h);
+  store8_bf16(lo_tile, r, c0, cols, l);
+}
+
+template <typename T>
+__device__ __forceinline__ float to_f32(T x);
+template <>
+__device__ __forceinline__ float to_f32<float>(float x) { return x; }
+template <>
+__device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 x) { return __bfloat162float(x); }
+template <>
+__device__ __forceinline__ float to_f32<__half>(__half x) { return __half2float(x); }
+
+template <typename T>
+__device__ __forceinline__ T from_f32(float x);
+template <>
+__device__ __forceinline__ float from_f32<float>(float x) { return x; }
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
+template <>
+__device__ __forceinline__ __half from_f32<__half>(float x) { return __float2half_rn(x); }
+
+// Load 8 consecutive elements (16-byte aligned for 16-bit types, 32-byte for fp32) as floats.
+template <typename T>
+__device__ __forceinline__ void load8(const T* p, float* v);
+template <>
+__device__ __forceinline__ void load8<__nv_bfloat16>(const __nv_bfloat16* p, float* v) {
+  uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 f = __bfloat1622float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+template <>
+__device__ __forceinline__ void load8<__half>(const __half* p, float* v) {
+  uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
+  const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 f = __half22float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+template <>
+__device__ __forceinline__ void load8<float>(const float* p, float* v) {
+  float4 a = __ldg(reinterpret_cast<const float4*>(p));
+  float4 b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+  v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
+template <typename T>
+__device__ __forceinline__ void store8(T* p, const float* v);
+template <>
+__device__ __forceinline__ void store8<__nv_bfloat16>(__nv_bfloat16* p, const float* v) {
+  uint4 u;
+  u.x = pack_bf16(v[0], v[1]);
+  u.y = pack_bf16(v[2], v[3]);
+  u.z = pack_bf16(v[4], v[5]);
+  u.w = pack_bf16(v[6], v[7]);
+  *reinterpret_cast<uint4*>(p) = u;
+}
+template <>
+__device__ __forceinline__ void store8<__half>(__half* p, const float* v) {
+  uint4 u;
+  __half2 h[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+  u = *reinterpret_cast<uint4*>(h);
+  *reinterpret_cast<uint4*>(p) = u;
+}
+template <>
+__device__ __forceinline__ void store8<float>(float* p, const float* v) {
+  reinterpret_cast<float4*>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
+  reinterpret_cast<float4*>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
+}
+
+__device__ __forceinline__ float warp_sum(float x) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+  return x;
+}
+
+}  // namespace gd

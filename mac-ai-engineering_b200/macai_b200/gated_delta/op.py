@@ -1,0 +1,215 @@
+"""The gated delta rule on B200: torch custom ops over the sm_100a kernels (libgated_delta_b200.so, C ABI in
+include/gated_delta_b200.h), and the drop-in for transformers' torch_chunk_gated_delta_rule (same arguments, same
+returns). Mirrors the reference's src/macai/gated_delta/op.py: `chunk_gated_delta_rule` (:264-298), the autograd
+function `GatedDeltaRule` (:116-257), `l2norm` (:260-261) and `recurrent_reference` (:301-314).
+
+There is no CPU or PyTorch fallback: on anything but a CUDA tensor on an sm_100 device the ops raise.
+"""
+from __future__ import annotations
+
+import collections
+import ctypes
+import math
+from typing import Optional
+
+import torch
+
+from .. import _lib
+
+# The chunk length of every kernel (tokens). The drop-in accepts `chunk_size` for signature compatibility and, like the
+# reference (op.py:268-269), runs its own chunking; 64 is also the value every caller passes.
+CHUNK = 64
+# Head widths the kernels are built for (the Qwen3.5 / Qwen3-Next linear-attention shapes).
+HEAD_DIMS = (128,)
+# What each call ran, as the reference's op.CALLS (op.py:44-46): "fwd", "bwd", by (B, T, H, HK) shape class.
+CALLS: collections.Counter = collections.Counter()
+
+_DTYPES = {torch.float32: _lib.GD_FLOAT32, torch.float16: _lib.GD_FLOAT16, torch.bfloat16: _lib.GD_BFLOAT16}
+
+
+def _p(t: Optional[torch.Tensor]):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(device: torch.device):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _dims(q: torch.Tensor, v: torch.Tensor):
+    B, T, HK, DK = q.shape
+    H, DV = v.shape[2], v.shape[3]
+    return B, T, H, HK, DK, DV
+
+
+def check_shapes(q, k, v, g, beta, s0=None) -> None:
+    """The refusals the kernels need, raised before any launch (ValueError / NotImplementedError, as the reference's
+    op.py:124-131 and _chunked.py:1228-1231)."""
+    if q.dim() != 4 or k.shape != q.shape or v.dim() != 4:
+        raise ValueError(f"query/key must be [B, T, H, DK] and value [B, T, H, DV]; got {tuple(q.shape)}, "
+                         f"{tuple(k.shape)}, {tuple(v.shape)}")
+    B, T, H, HK, DK, DV = _dims(q, v)
+    if v.shape[:2] != q.shape[:2]:
+        raise ValueError("query and value must share batch and sequence dimensions")
+    if H % HK != 0:
+        raise ValueError(f"value heads ({H}) must be a multiple of key heads ({HK})")
+    if DK not in HEAD_DIMS or DV not in HEAD_DIMS:
+        raise NotImplementedError(f"the B200 kernels are built for head widths {HEAD_DIMS}; got DK={DK}, DV={DV}")
+    if g.shape != (B, T, H) or beta.shape != (B, T, H):
+        raise ValueError(f"g and beta must be [B, T, H] = {(B, T, H)}; got {tuple(g.shape)}, {tuple(beta.shape)}")
+    if s0 is not None and s0.shape != (B, H, DK, DV):
+        raise ValueError(f"initial_state must be [B, H, DK, DV] = {(B, H, DK, DV)}; got {tuple(s0.shape)}")
+    if q.device.type != "cuda":
+        raise RuntimeError("macai_b200's gated delta rule runs on CUDA (B200) tensors only; there is no CPU path")
+
+
+def workspace_bytes(B, T, H, HK, DK, DV, backward: bool) -> int:
+    n = _lib.load().gd_workspace_bytes(B, T, H, HK, DK, DV, int(backward))
+    if n == 0:
+        raise NotImplementedError(f"unsupported sizes B={B} T={T} H={H} HK={HK} DK={DK} DV={DV}")
+    return n
+
+
+# ------------------------------------------------------------------------------------------------------------------
+# custom ops
+
+@torch.library.custom_op("macai_b200::gated_delta_fwd", mutates_args=(), device_types="cuda")
+def gated_delta_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Tensor, beta: torch.Tensor,
+                    s0: Optional[torch.Tensor], flags: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """o [B, T, H, DV] (q's dtype) and S_T [B, H, DK, DV] fp32. q, k [B, T, HK, DK]; v [B, T, H, DV] in q's dtype;
+    g, beta fp32 [B, T, H]; s0 fp32 or None. flags: GD_L2NORM | GD_SCALE_Q."""
+    B, T, H, HK, DK, DV = _dims(q, v)
+    lib = _lib.load()
+    dev = q.device
+    o = torch.empty(B, T, H, DV, dtype=q.dtype, device=dev)
+    sT = torch.empty(B, H, DK, DV, dtype=torch.float32, device=dev)
+    nbytes = workspace_bytes(B, T, H, HK, DK, DV, False)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        st = lib.gd_forward(_p(q), _p(k), _p(v), _p(g), _p(beta), _p(s0), _p(o), _p(sT), _DTYPES[q.dtype], B, T, H, HK,
+                            DK, DV, flags, _p(ws), nbytes, _stream(dev))
+    _lib.check(st, "gd_forward")
+    CALLS["fwd"] += 1
+    return o, sT
+
+
+@gated_delta_fwd.register_fake
+def _(q, k, v, g, beta, s0, flags):
+    B, T, H, HK, DK, DV = _dims(q, v)
+    return q.new_empty(B, T, H, DV), q.new_empty(B, H, DK, DV, dtype=torch.float32)
+
+
+@torch.library.custom_op("macai_b200::gated_delta_bwd", mutates_args=(), device_types="cuda")
+def gated_delta_bwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Tensor, beta: torch.Tensor,
+                    s0: Optional[torch.Tensor], do: torch.Tensor, dsT: Optional[torch.Tensor],
+                    flags: int) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor,
+                                         torch.Tensor]:
+    """(dq, dk, dv, dg, dbeta, ds0): the chunk states recomputed from the inputs (the reference's recompute mode,
+    op.py:207-218), then the reverse state pass and the per-chunk gradients."""
+    B, T, H, HK, DK, DV = _dims(q, v)
+    lib = _lib.load()
+    dev = q.device
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    dg = torch.empty(B, T, H, dtype=torch.float32, device=dev)
+    dbeta = torch.empty(B, T, H, dtype=torch.float32, device=dev)
+    ds0 = torch.empty(B, H, DK, DV, dtype=torch.float32, device=dev)
+    nbytes = workspace_bytes(B, T, H, HK, DK, DV, True)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        st = lib.gd_backward(_p(q), _p(k), _p(v), _p(g), _p(beta), _p(s0), _p(do), _p(dsT), _p(dq), _p(dk), _p(dv),
+                             _p(dg), _p(dbeta), _p(ds0), _DTYPES[q.dtype], B, T, H, HK, DK, DV, flags, _p(ws), nbytes,
+                             _stream(dev))
+    _lib.check(st, "gd_backward")
+    CALLS["bwd"] += 1
+    return dq, dk, dv, dg, dbeta, ds0
+
+
+@gated_delta_bwd.register_fake
+def _(q, k, v, g, beta, s0, do, dsT, flags):
+    B, T, H, HK, DK, DV = _dims(q, v)
+    f32 = dict(dtype=torch.float32)
+    return (torch.empty_like(q), torch.empty_like(k), torch.empty_like(v), q.new_empty(B, T, H, **f32),
+            q.new_empty(B, T, H, **f32), q.new_empty(B, H, DK, DV, **f32))
+
+
+def _setup_context(ctx, inputs, output):
+    q, k, v, g, beta, s0, flags = inputs
+    ctx.save_for_backward(q, k, v, g, beta, s0)
+    ctx.flags = flags
+    ctx.has_s0 = s0 is not None
+
+
+def _backward(ctx, do, dsT):
+    q, k, v, g, beta, s0 = ctx.saved_tensors
+    if do is None:
+        do = torch.zeros(*v.shape, dtype=q.dtype, device=q.device)
+    do = do.to(q.dtype).contiguous()
+    dsT = None if dsT is None else dsT.to(torch.float32).contiguous()
+    dq, dk, dv, dg, dbeta, ds0 = gated_delta_bwd(q, k, v, g, beta, s0, do, dsT, ctx.flags)
+    return dq, dk, dv, dg, dbeta, (ds0 if ctx.has_s0 else None), None
+
+
+gated_delta_fwd.register_autograd(_backward, setup_context=_setup_context)
+
+
+# ------------------------------------------------------------------------------------------------------------------
+# the reference's Python surface
+
+class GatedDeltaRule:
+    """o, S_T = recurrence(q, k, v, g, beta, S_0) on [B, T, H, D] tensors with q already normalised and scaled, as the
+    reference's autograd function (op.py:116-257): `GatedDeltaRule.apply(q, k, v, g, beta, s0, save)`. `save` is
+    accepted for signature compatibility; autograd records the op whenever an input requires grad. The backward always
+    recomputes the chunk states (the reference's default, op.py:27-33)."""
+
+    @staticmethod
+    def apply(q, k, v, g, beta, s0, save: bool = True):
+        dt = q.dtype
+        k, v = k.to(dt), v.to(dt)
+        check_shapes(q, k, v, g, beta, s0)
+        return gated_delta_fwd(q.contiguous(), k.contiguous(), v.contiguous(), g.float().contiguous(),
+                               beta.float().contiguous(), None if s0 is None else s0.float().contiguous(), 0)
+
+
+def l2norm(x: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+    """x * rsqrt(sum(x^2) + eps) over the last dimension (the reference's op.py:260-261; transformers' l2norm)."""
+    return x * torch.rsqrt((x * x).sum(dim=-1, keepdim=True) + eps)
+
+
+def chunk_gated_delta_rule(query, key, value, g, beta, chunk_size: int = 64, initial_state=None,
+                           output_final_state: bool = False, use_qk_l2norm_in_kernel: bool = False, **kwargs):
+    """Drop-in for transformers' torch_chunk_gated_delta_rule: query, key [B, T, HK, DK]; value [B, T, H, DV]
+    (H = HK, or a multiple of it: each key head then serves H / HK consecutive value heads); g (log decay, <= 0) and
+    beta [B, T, H]; initial_state [B, H, DK, DV] or None. Returns the output [B, T, H, DV] in the query's dtype and the
+    final state (float32) when output_final_state, else None. chunk_size is accepted and not used (the kernels chunk by
+    64 tokens), as in the reference (op.py:264-269). Raises NotImplementedError for packed rows (cu_seqlens), as the
+    reference does (op.py:270-273)."""
+    if kwargs.get("cu_seqlens") is not None:
+        # packed rows: the state must restart at each boundary; running without it would silently carry state
+        # across sequences
+        raise NotImplementedError("macai_b200's gated delta rule does not take packed rows (cu_seqlens) yet")
+    dt = query.dtype
+    if dt not in _DTYPES:
+        raise TypeError(f"query dtype {dt} is not supported (float32, float16, bfloat16)")
+    # the kernels read q, k, v in one dtype: key and value follow the query's (differentiably, so their gradients
+    # come back in their own dtypes)
+    k, v = key.to(dt), value.to(dt)
+    check_shapes(query, k, v, g, beta, initial_state)
+    flags = _lib.GD_SCALE_Q | (_lib.GD_L2NORM if use_qk_l2norm_in_kernel else 0)
+    s0 = None if initial_state is None else initial_state.to(torch.float32).contiguous()
+    o, sT = gated_delta_fwd(query.contiguous(), k.contiguous(), v.contiguous(), g.to(torch.float32).contiguous(),
+                            beta.to(torch.float32).contiguous(), s0, flags)
+    return o, (sT if output_final_state else None)
+
+
+def recurrent_reference(q, k, v, g, beta, s0):
+    """The recurrence step by step in plain PyTorch ([B, T, H, D] inputs, q already normalised and scaled), the
+    reference's parity utility (op.py:301-314) kept for users' own checks. Not used by the ops."""
+    s = s0.clone()
+    outs = []
+    for t in range(q.shape[1]):
+        a = g[:, t].exp()[..., None, None]
+        st = s * a
+        u = (st * k[:, t, :, :, None]).sum(-2)
+        d = beta[:, t, :, None] * (v[:, t] - u)
+        s = st + k[:, t, :, :, None] * d[:, :, None, :]
+        outs.append((s * q[:, t, :, :, None]).sum(-2))
+    return torch.stack(outs, 1), s
