@@ -347,4 +347,97 @@ __device__ __forceinline__ float warp_sum(float x) {
   return x;
 }
 
+
+// Loads 64 rows x D of a [B, T, heads, D] tensor into a blocked bf16 tile; with norm, each row is scaled by
+// rsqrt(sum x^2 + eps) * scale (the l2 prologue of src/macai/gated_delta/_norm.py:27-43), else by `scale`.
+// Rows past T, and every row when x is null, are zero. With lo_tile, the rounding remainder goes there (hi + lo).
+// NWARPS warps share the 64 rows; each warp stores 8 rows x 32 columns per instruction (512 contiguous bytes: no bank
+// conflict).
+template <typename T, int D, int NWARPS = 4>
+__device__ __forceinline__ void load_rows(const T* x, int b, int t0, int T_, int heads, int hh, bool norm, float scale,
+                                          unsigned char* tile, float* rsq_out, unsigned char* lo_tile = nullptr) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr int J = D / 32;              // 8-column groups per lane
+  constexpr int RB = 64 / (8 * NWARPS);  // row blocks per warp
+#pragma unroll 1
+  for (int rbi = 0; rbi < RB; ++rbi) {
+    const int r = 8 * (RB * warp + rbi) + (lane & 7);
+    const int t = t0 + r;
+    const bool valid = x != nullptr && t < T_;
+    const T* row = x + (((size_t)b * T_ + (valid ? t : 0)) * heads + hh) * D;
+    float vals[J][8];
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+      const int c0 = 8 * ((lane >> 3) + 4 * j);
+      if (valid) {
+        load8<T>(row + c0, vals[j]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) vals[j][e] = 0.f;
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ss = fmaf(vals[j][e], vals[j][e], ss);
+    }
+    float f = scale;
+    if (norm) {
+      ss += __shfl_xor_sync(0xffffffffu, ss, 8);
+      ss += __shfl_xor_sync(0xffffffffu, ss, 16);
+      const float rs = rsqrtf(ss + 1e-6f);
+      f = rs * scale;
+      if (rsq_out != nullptr && valid && lane < 8) rsq_out[((size_t)b * T_ + t) * heads + hh] = rs;
+    }
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) vals[j][e] *= f;
+      if (lo_tile != nullptr) {
+        store8_split(tile, lo_tile, r, 8 * ((lane >> 3) + 4 * j), D, vals[j]);
+      } else {
+        store8_bf16(tile, r, 8 * ((lane >> 3) + 4 * j), D, vals[j]);
+      }
+    }
+  }
+}
+
+// fp32 [R][Cc] row-major -> blocked bf16 tile(s): hi, and lo = x - hi when lo is not null. Eight consecutive threads
+// fill one 128-byte core matrix (no bank conflicts) and each reads one 32-byte sector.
+template <int R, int Cc, int NTHREADS>
+__device__ __forceinline__ void f32_to_tiles(const float* __restrict__ src, unsigned char* hi, unsigned char* lo) {
+  constexpr int NCHUNK = R * Cc / 8;
+  for (int idx = threadIdx.x; idx < NCHUNK; idx += NTHREADS) {
+    const int rl = idx & 7, cb = (idx >> 3) % (Cc / 8), rb = idx / (8 * (Cc / 8));
+    const int r = 8 * rb + rl;
+    const float4* p = reinterpret_cast<const float4*>(src + (size_t)r * Cc + 8 * cb);
+    const float4 a = p[0], b4 = p[1];
+    float v[8] = {a.x, a.y, a.z, a.w, b4.x, b4.y, b4.z, b4.w};
+    if (lo != nullptr) {
+      store8_split(hi, lo, r, 8 * cb, Cc, v);
+    } else {
+      store8_bf16(hi, r, 8 * cb, Cc, v);
+    }
+  }
+}
+
+// Reduce-scatter across a warp: each lane holds v[0..31]; returns, in lane l, the sum over the warp's lanes of v[l]
+// (31 shuffles instead of 32 x 5).
+__device__ __forceinline__ float warp_reduce_scatter32(float (&v)[32]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int s = 16; s >= 1; s >>= 1) {
+    const bool upper = (lane & s) != 0;
+#pragma unroll
+    for (int k = 0; k < s; ++k) {
+      const float send = upper ? v[k] : v[k + s];
+      const float keep = upper ? v[k + s] : v[k];
+      v[k] = keep + __shfl_xor_sync(0xffffffffu, send, s);
+    }
+  }
+  return v[0];
+}
+
+// [64][64] fp32 C x C scratch, columns XOR-swizzled by row so that both row-wise and column-wise thread patterns are
+// free of bank conflicts.
+__device__ __forceinline__ int cc_idx(int i, int j) { return i * 64 + (j ^ (i & 31)); }
+
 }  // namespace gd

@@ -28,6 +28,9 @@ struct PrepSmem {
   static constexpr size_t a2l = a2h + 64 * 64 * 2;        //                           lo
   static constexpr size_t L = a2l + 64 * 64 * 2;          // [64][65] fp32, L (strictly lower)
   static constexpr size_t Ai = L + 64 * 65 * 4;           // [64][65] fp32, A
+  static constexpr size_t ql = L;                         // [64 x DK] low half of q, then k: live only until the
+  static constexpr size_t kl = ql + 64 * DK * 2;          //   Q K^T / K K^T product is done (L and A reuse them)
+  static_assert(2 * 64 * DK * 2 <= 2 * 64 * 65 * 4, "the q / k low halves must fit in the L and A buffers");
   static constexpr size_t T3 = Ai + 64 * 65 * 4;          // [3][16][17] fp32 block products of the inverse
   static constexpr size_t G = T3 + 3 * 16 * 17 * 4;       // [64] cumulative log decay
   static constexpr size_t beta = G + 64 * 4;              // [64]
@@ -36,51 +39,6 @@ struct PrepSmem {
   static constexpr size_t tmem = bar + 8;
   static constexpr size_t total = tmem + 16;
 };
-
-// Loads 64 rows x D of a [B, T, heads, D] tensor into a blocked bf16 tile; with norm, each row is scaled by
-// rsqrt(sum x^2 + eps) * scale (the l2 prologue of src/macai/gated_delta/_norm.py:27-43), else by `scale`.
-// Rows past T are zero. Each warp stores 8 rows x 32 columns per instruction (512 contiguous bytes: no bank conflict).
-template <typename T, int D>
-__device__ __forceinline__ void load_rows(const T* x, int b, int t0, int T_, int heads, int hh, bool norm, float scale,
-                                          unsigned char* tile, float* rsq_out) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  constexpr int J = D / 32;  // 8-column groups per lane
-#pragma unroll 1
-  for (int rbi = 0; rbi < 2; ++rbi) {
-    const int r = 16 * warp + 8 * rbi + (lane & 7);
-    const int t = t0 + r;
-    const bool valid = t < T_;
-    const T* row = x + (((size_t)b * T_ + (valid ? t : 0)) * heads + hh) * D;
-    float vals[J][8];
-    float ss = 0.f;
-#pragma unroll
-    for (int j = 0; j < J; ++j) {
-      const int c0 = 8 * ((lane >> 3) + 4 * j);
-      if (valid) {
-        load8<T>(row + c0, vals[j]);
-      } else {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) vals[j][e] = 0.f;
-      }
-#pragma unroll
-      for (int e = 0; e < 8; ++e) ss = fmaf(vals[j][e], vals[j][e], ss);
-    }
-    float f = scale;
-    if (norm) {
-      ss += __shfl_xor_sync(0xffffffffu, ss, 8);
-      ss += __shfl_xor_sync(0xffffffffu, ss, 16);
-      const float rs = rsqrtf(ss + 1e-6f);
-      f = rs * scale;
-      if (rsq_out != nullptr && valid && lane < 8) rsq_out[((size_t)b * T_ + t) * heads + hh] = rs;
-    }
-#pragma unroll
-    for (int j = 0; j < J; ++j) {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) vals[j][e] *= f;
-      store8_bf16(tile, r, 8 * ((lane >> 3) + 4 * j), D, vals[j]);
-    }
-  }
-}
 
 // A = (I + L)^-1 for the 64 x 64 strictly lower L (fp32, row stride 65), by substitution inside the four 16 x 16
 // diagonal blocks and block merges below them, A_IJ = -A_II sum_{m=J}^{I-1} L_Im A_mJ (one block distance at a time),
@@ -170,8 +128,8 @@ __global__ void __launch_bounds__(128) prep_kernel(const T* __restrict__ q, cons
   float* rq = bwd ? reinterpret_cast<float*>(ws + lay.rq) : nullptr;
   float* rk = bwd ? reinterpret_cast<float*>(ws + lay.rk) : nullptr;
   const float qscale = (flags & GD_SCALE_Q) ? rsqrtf((float)DK) : 1.f;
-  load_rows<T, DK>(q, b, t0, lay.T, lay.HK, hk, norm, qscale, smem + S::q, rq);
-  load_rows<T, DK>(k, b, t0, lay.T, lay.HK, hk, norm, 1.f, smem + S::k, rk);
+  load_rows<T, DK>(q, b, t0, lay.T, lay.HK, hk, norm, qscale, smem + S::q, rq, smem + S::ql);
+  load_rows<T, DK>(k, b, t0, lay.T, lay.HK, hk, norm, 1.f, smem + S::k, rk, smem + S::kl);
   load_rows<T, DV>(v, b, t0, lay.T, lay.H, h, false, 1.f, smem + S::v, nullptr);
 
   // cumulative log decay (padding rows: g = 0, beta = 0, which leaves G constant past the last token)
@@ -199,13 +157,21 @@ __global__ void __launch_bounds__(128) prep_kernel(const T* __restrict__ q, cons
   tc_fence_after();
   const uint32_t tm = *tslot;
 
-  // [Q; K] K^T: lanes 0-63 hold Q K^T rows, lanes 64-127 K K^T rows
+  // [Q; K] K^T with q and k carried as bf16 hi + lo (three products): lanes 0-63 hold Q K^T rows, 64-127 K K^T rows
   if (tid == 0) {
-    mma_tiles(tm, 128, 64, DK, Tile{smem_u32(smem + S::q), DK}, true, 0, 0, Tile{smem_u32(smem + S::k), DK}, false, 0,
-              false);
+    const Tile qkh{smem_u32(smem + S::q), DK}, qkl{smem_u32(smem + S::ql), DK};
+    const Tile kh{smem_u32(smem + S::k), DK}, kl{smem_u32(smem + S::kl), DK};
+    mma_tiles(tm, 128, 64, DK, qkh, true, 0, 0, kh, false, 0, false);
+    mma_tiles(tm, 128, 64, DK, qkh, true, 0, 0, kl, false, 0, true);
+    mma_tiles(tm, 128, 64, DK, qkl, true, 0, 0, kh, false, 0, true);
     mma_commit(bar);
   }
   __syncthreads();  // sG complete for everyone
+  {  // the low halves go out before L and A overwrite them
+    const uint4* src = reinterpret_cast<const uint4*>(smem + S::ql);
+    uint4* dst = reinterpret_cast<uint4*>(ws + lay.qkl + cidx * lay.qk_bytes());
+    for (int idx = tid; idx < (int)(lay.qk_bytes() / 16); idx += 128) dst[idx] = src[idx];
+  }
   bool ok = mbar_wait(bar, 0, err, 10);
   ok = __syncthreads_and(ok);
   tc_fence_after();
@@ -214,6 +180,8 @@ __global__ void __launch_bounds__(128) prep_kernel(const T* __restrict__ q, cons
     const float Gi = sG[i];
     float acc[32];
     unsigned char* mimg = ws + lay.m + cidx * lay.m_bytes();
+    float* mf = lay.backward() ? reinterpret_cast<float*>(ws + lay.mf + cidx * lay.ainv_bytes()) + i * 64 : nullptr;
+    float* kgf = lay.backward() ? reinterpret_cast<float*>(ws + lay.kg + cidx * lay.ainv_bytes()) + i * 64 : nullptr;
 #pragma unroll 1
     for (int half = 0; half < 2; ++half) {
       tmem_ld32(tmem_lane_addr(tm, warp, 32 * half), acc);
@@ -226,12 +194,20 @@ __global__ void __launch_bounds__(128) prep_kernel(const T* __restrict__ q, cons
         }
 #pragma unroll
         for (int q8 = 0; q8 < 4; ++q8) store8_bf16(mimg, i, 32 * half + 8 * q8, 64, mv + 8 * q8);
+        if (mf != nullptr) {
+#pragma unroll
+          for (int q8 = 0; q8 < 4; ++q8) store8<float>(mf + 32 * half + 8 * q8, mv + 8 * q8);
+        }
       } else {
         const float bi = sB[i];
 #pragma unroll
         for (int jj = 0; jj < 32; ++jj) {
           const int j = 32 * half + jj;
           sL[i * 65 + j] = (j < i) ? bi * acc[jj] * __expf(Gi - sG[j]) : 0.f;
+        }
+        if (kgf != nullptr) {
+#pragma unroll
+          for (int q8 = 0; q8 < 4; ++q8) store8<float>(kgf + 32 * half + 8 * q8, acc + 8 * q8);
         }
       }
     }
@@ -326,14 +302,15 @@ struct StateSmem {
   static constexpr size_t eh = vl + DV * 64 * 2;         // [DV x 64] (e Vn)^T hi
   static constexpr size_t el = eh + DV * 64 * 2;         //               lo
   static constexpr size_t qk = el + DV * 64 * 2;         // stage: [2][64 x DK] q, k images
-  static constexpr size_t wt = qk + 2 * 64 * DK * 2;     // stage: [DK x 64] W^T image
+  static constexpr size_t kl = qk + 2 * 64 * DK * 2;     // stage: [64 x DK] low half of the k image
+  static constexpr size_t wt = kl + 64 * DK * 2;         // stage: [DK x 64] W^T image
   static constexpr size_t m = wt + DK * 64 * 2;          // stage: [64 x 64] M image
   static constexpr size_t g = m + 64 * 64 * 2;           // stage: [64] G
   static constexpr size_t u = g + 64 * 4;                // [64][DV] fp32 U
   static constexpr size_t bar = u + 64 * DV * 4;         // 3 mbarriers: mma, inputs, U
   static constexpr size_t tmem = bar + 3 * 8;
   static constexpr size_t total = tmem + 8;
-  static constexpr uint32_t stage_bytes = 2 * 64 * DK * 2 + DK * 64 * 2 + 64 * 64 * 2 + 64 * 4;
+  static constexpr uint32_t stage_bytes = 3 * 64 * DK * 2 + DK * 64 * 2 + 64 * 64 * 2 + 64 * 4;
 };
 
 template <int DK, int DV>
@@ -342,6 +319,7 @@ __device__ __forceinline__ void issue_stage(unsigned char* smem, const unsigned 
   using S = StateSmem<DK, DV>;
   mbar_arrive_expect_tx(bar, S::stage_bytes);
   bulk_g2s(smem + S::qk, ws + lay.qk + cidx * lay.qk_bytes(), (uint32_t)lay.qk_bytes(), bar);
+  bulk_g2s(smem + S::kl, ws + lay.qkl + cidx * lay.qk_bytes() + 64 * DK * 2, 64 * DK * 2, bar);
   bulk_g2s(smem + S::wt, ws + lay.wt + cidx * lay.wt_bytes(), (uint32_t)lay.wt_bytes(), bar);
   bulk_g2s(smem + S::m, ws + lay.m + cidx * lay.m_bytes(), (uint32_t)lay.m_bytes(), bar);
   bulk_g2s(smem + S::g, ws + lay.gc + cidx * lay.gc_bytes(), (uint32_t)lay.gc_bytes(), bar);
@@ -460,10 +438,11 @@ __global__ void __launch_bounds__(128) state_kernel(const float* __restrict__ s0
                 0, false);
       mma_tiles(tMV, DV, 64, 64, Tile{smem_u32(smem + S::vl), 64}, true, 0, 0, Tile{smem_u32(smem + S::m), 64}, false,
                 0, true);
-      mma_tiles(tDS, DV, DK, 64, Tile{smem_u32(smem + S::eh), 64}, true, 0, 0,
-                Tile{smem_u32(smem + S::qk + 64 * DK * 2), DK}, true, 0, false);
-      mma_tiles(tDS, DV, DK, 64, Tile{smem_u32(smem + S::el), 64}, true, 0, 0,
-                Tile{smem_u32(smem + S::qk + 64 * DK * 2), DK}, true, 0, true);
+      // e Vn and k both split: hi hi + hi lo + lo hi (the state carries the sequence: it gets the extra bits)
+      const Tile tkh{smem_u32(smem + S::qk + 64 * DK * 2), DK}, tkl{smem_u32(smem + S::kl), DK};
+      mma_tiles(tDS, DV, DK, 64, Tile{smem_u32(smem + S::eh), 64}, true, 0, 0, tkh, true, 0, false);
+      mma_tiles(tDS, DV, DK, 64, Tile{smem_u32(smem + S::eh), 64}, true, 0, 0, tkl, true, 0, true);
+      mma_tiles(tDS, DV, DK, 64, Tile{smem_u32(smem + S::el), 64}, true, 0, 0, tkh, true, 0, true);
       mma_commit(bar_mma);
     }
     ok = mbar_wait(bar_mma, ph_mma, err, 23);

@@ -7,8 +7,10 @@
 //   m    [64 x 64]    bf16 blocked   M = (Q K^T) * exp(G_i - G_j), lower with the diagonal
 //   u    [64][DV]     fp32           U = A diag(beta) V
 //   gc   [64]         fp32           G, the in-chunk inclusive cumulative sum of g
+//   qkl  [2][64 x DK] bf16 blocked   the low halves of normalised q and k (q = hi + lo to ~16 significant bits)
 // and for the backward also
 //   ainv [64][64]     fp32           A = (I + L)^-1
+//   mf, kg [64][64]   fp32           M (with its decay mask) and K K^T
 //   rq, rk [B*T*HK]   fp32           the l2 prologue's rsqrt per raw q / k row
 // The state pass with GD_STORE_STATES writes sc [DK][DV] fp32 (the state entering the chunk) and vn [64][DV] fp32;
 // the reverse pass writes dsn [DK][DV] fp32 (dLoss/dS_{c+1}) and dvn [64][DV] fp32.
@@ -23,7 +25,7 @@ namespace gd {
 struct Layout {
   int B, T, H, HK, DK, DV, NT, rep;
   size_t nch;  // B * H * NT chunks
-  size_t err, qk, wt, m, u, gc, ainv, rq, rk, sc, vn, dsn, dvn, total;
+  size_t err, qk, wt, m, u, gc, qkl, ainv, mf, kg, rq, rk, sc, vn, dsn, dvn, total;
 
   __host__ __device__ static size_t up(size_t x) { return (x + 255) & ~size_t(255); }
 
@@ -48,8 +50,11 @@ struct Layout {
     L.m = o; o = up(o + L.nch * L.m_bytes());
     L.u = o; o = up(o + L.nch * L.u_bytes());
     L.gc = o; o = up(o + L.nch * L.gc_bytes());
+    L.qkl = o; o = up(o + L.nch * L.qk_bytes());
     if (backward) {
       L.ainv = o; o = up(o + L.nch * L.ainv_bytes());
+      L.mf = o; o = up(o + L.nch * L.ainv_bytes());
+      L.kg = o; o = up(o + L.nch * L.ainv_bytes());
       L.rq = o; o = up(o + (size_t)B * T * HK * 4);
       L.rk = o; o = up(o + (size_t)B * T * HK * 4);
       L.sc = o; o = up(o + L.nch * L.s_bytes());
@@ -57,7 +62,7 @@ struct Layout {
       L.dsn = o; o = up(o + L.nch * L.s_bytes());
       L.dvn = o; o = up(o + L.nch * L.u_bytes());
     } else {
-      L.ainv = L.rq = L.rk = L.sc = L.vn = L.dsn = L.dvn = 0;
+      L.ainv = L.mf = L.kg = L.rq = L.rk = L.sc = L.vn = L.dsn = L.dvn = 0;
     }
     L.total = o;
     return L;
