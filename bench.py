@@ -1,0 +1,473 @@
+"""Benchmark of the chunked gated delta rule, forward + backward, on B200 (sm_100a).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 1|2|3|4] [--impl b200|reference]
+
+One step = the forward (o, S_T) and the backward (dq, dk, dv, dg, dbeta, ds0; chunk states recomputed) of one batch of
+the configuration through the library's C ABI (include/gated_delta_b200.h: gd_forward + gd_backward), captured once in
+a CUDA graph. The headline metric is BASELINE.json's: tokens/s (tokens = B * T) for forward + backward at config 1
+(B=4, T=1024, H=16, dk=dv=128, bf16, chunk 64, l2-normalised q/k). Inputs are seeded synthetic tensors with the
+distributions of BASELINE.json configs[0].
+
+Multi-GPU (torchrun, one process per GPU): weak scaling over independent (batch, head) slices. Every rank owns
+config 1's B batch rows of a global batch of N * B rows; there is no collective on the data path. The time is the
+maximum over ranks of the device time (CUDA events), taken with an NCCL all-reduce(max) after the timed region.
+
+Printed (rank 0), one JSON line:
+  value        whole-job tokens/s with inputs resident in HBM (sum of per-step device times; L2 flushed between steps)
+  e2e          the same metric with the inputs copied host->device from pinned memory and every output copied back,
+               inside the timed region (a CPU caller's view of the C ABI)
+  roofline     the dominant kernel's achieved rate against MEASURED_PEAKS.json (per-kernel CUDA-event timing pass)
+  cpu_baseline transformers' torch_chunk_gated_delta_rule (the reference torch implementation; oracle/transformers_ref.py)
+               forward + backward on a bounded sample on this host's cores (rank 0, N = 1 only)
+--impl reference runs only that CPU implementation (all host threads) and prints its line.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "mac-ai-engineering_b200"))
+sys.path.insert(0, ROOT)
+
+METRIC = "gated-delta fwd+bwd tokens/s (B4 T1024 H16 d128 bf16)"
+# the reference's own published number for this shape and pass (Apple M3 Max, Metal; not re-measurable
+# here): 10.210 ms fwd+bwd at B4 T1024 H16 -> 401,175 tokens/s (docs/series_layer.md:1679-1684 of the reference)
+PUBLISHED_TOKENS_S = 4 * 1024 / 10.210e-3
+CONFIGS = {
+    # name: (B, T, H value heads, HK key heads, D, with s0 / final state, forward only)
+    1: dict(B=4, T=1024, H=16, HK=16, D=128, s0=False, fwd_only=False, tag="c1: B4 T1024 H16 d128 fwd+bwd"),
+    2: dict(B=2, T=1024, H=32, HK=16, D=128, s0=True, fwd_only=False, tag="c2: B2 T1024 Hk16 Hv32 d128 fwd+bwd, s0"),
+    3: dict(B=1, T=32768, H=32, HK=32, D=128, s0=False, fwd_only=True, tag="c3: B1 T32768 H32 d128 forward"),
+    4: dict(B=64, T=4096, H=32, HK=32, D=128, s0=False, fwd_only=False, tag="c4: B64 T4096 H32 d128 fwd+bwd"),
+}
+# per token-head algorithmic work, D = 128, C = 64 (fixed formula; the backward's recompute is not credited)
+FLOP_FWD, FLOP_BWD = 181_589, 409_600
+BYTES_FWD, BYTES_BWD = 1_032, 1_808
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+def synthetic(cfg, device, seed):
+    """BASELINE.json configs[0] distributions: q, k, v ~ N(0,1) (bf16); beta = sigmoid(N(0,1));
+    g = -exp(U(log 1, log 16)) * softplus(N(0,1)); dO ~ N(0,1) (bf16); s0 ~ N(0, 0.02)."""
+    import torch
+    B, T, H, HK, D = cfg["B"], cfg["T"], cfg["H"], cfg["HK"], cfg["D"]
+    gen = torch.Generator(device=device).manual_seed(seed)
+    bf = torch.bfloat16
+    t = {}
+    t["q"] = torch.randn(B, T, HK, D, generator=gen, device=device).to(bf)
+    t["k"] = torch.randn(B, T, HK, D, generator=gen, device=device).to(bf)
+    t["v"] = torch.randn(B, T, H, D, generator=gen, device=device).to(bf)
+    t["beta"] = torch.sigmoid(torch.randn(B, T, H, generator=gen, device=device))
+    t["g"] = (-torch.exp(torch.rand(B, T, H, generator=gen, device=device) * math.log(16.0))
+              * torch.nn.functional.softplus(torch.randn(B, T, H, generator=gen, device=device)))
+    t["do"] = torch.randn(B, T, H, D, generator=gen, device=device).to(bf)
+    t["s0"] = (torch.randn(B, H, D, D, generator=gen, device=device) * 0.02) if cfg["s0"] else None
+    t["dsT"] = (torch.randn(B, H, D, D, generator=gen, device=device) * 0.02) if cfg["s0"] else None
+    return t
+
+
+class Clocks:
+    """nvidia-smi samples during the timed region (SM clock, power, throttle reasons)."""
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = os.path.join("/tmp", f"gd_clocks_{os.getpid()}.csv")
+
+    def __enter__(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"], stdout=self.f,
+                                         stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        smax = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def cpu_reference(cfg, steps, warmup, sample_batch=1, threads=None):
+    """transformers' torch_chunk_gated_delta_rule forward + backward on the CPU over a bounded sample of the workload
+    (sample_batch of its B batch rows, all T and H): tokens/s of that sample, median over `steps`."""
+    import torch
+    from oracle import transformers_ref
+    if threads:
+        torch.set_num_threads(threads)
+    scfg = dict(cfg, B=sample_batch)
+    t = synthetic(scfg, "cpu", 1234)
+    f = transformers_ref.rule()
+    rep = cfg["H"] // cfg["HK"]
+    times = []
+    for i in range(warmup + steps):
+        xs = [t[n].clone().requires_grad_(True) for n in ("q", "k", "v", "g", "beta")]
+        s0 = t["s0"].clone().requires_grad_(True) if t["s0"] is not None else None
+        t0 = time.perf_counter()
+        qx = xs[0].repeat_interleave(rep, 2) if rep > 1 else xs[0]
+        kx = xs[1].repeat_interleave(rep, 2) if rep > 1 else xs[1]
+        o, sT = f(qx, kx, xs[2], xs[3], xs[4], chunk_size=64, initial_state=s0, output_final_state=True,
+                  use_qk_l2norm_in_kernel=True)
+        if not cfg["fwd_only"]:
+            loss = (o.float() * t["do"].float()).sum()
+            if t["dsT"] is not None:
+                loss = loss + (sT * t["dsT"]).sum()
+            loss.backward()
+        dt = time.perf_counter() - t0
+        if i >= warmup:
+            times.append(dt)
+    med = statistics.median(times)
+    tokens = sample_batch * cfg["T"]
+    return {"value": tokens / med, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "reference",
+            "sample": f"transformers torch_chunk_gated_delta_rule {'fwd' if cfg['fwd_only'] else 'fwd+bwd'} "
+                      f"B={sample_batch} of {cfg['B']} (T={cfg['T']}, H={cfg['H']}), median of {steps} "
+                      f"after {warmup} warm-up, {med:.3f} s/step",
+            "seconds_per_sample": med}
+
+
+def run_reference(args, cfg):
+    import torch
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = os.cpu_count()
+    res = cpu_reference(cfg, steps=args.steps, warmup=max(1, min(args.warmup, 2)), threads=threads)
+    line = {"impl": "reference", "metric": METRIC if args.config == 1 else f"gated-delta tokens/s ({cfg['tag']})",
+            "value": res["value"], "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": res["seconds_per_sample"] * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (BASELINE configs[0] "
+            "distributions)", "config": {"workload": cfg["tag"], "sample": res["sample"]},
+            "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": res["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", type=int, default=1, choices=sorted(CONFIGS))
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-graph", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    cfg = CONFIGS[args.config]
+    if args.impl == "reference":
+        return run_reference(args, cfg)
+
+    import torch
+    import torch.distributed as dist
+    from macai_b200 import _lib
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+
+    lib = _lib.load()
+    B, T, H, HK, D = cfg["B"], cfg["T"], cfg["H"], cfg["HK"], cfg["D"]
+    t = synthetic(cfg, dev, 1000 + rank)
+    flags = _lib.GD_L2NORM | _lib.GD_SCALE_Q
+    nbytes = lib.gd_workspace_bytes(B, T, H, HK, D, D, 0 if cfg["fwd_only"] else 1)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    o = torch.empty(B, T, H, D, dtype=torch.bfloat16, device=dev)
+    sT = torch.empty(B, H, D, D, dtype=torch.float32, device=dev)
+    dq, dk = torch.empty_like(t["q"]), torch.empty_like(t["k"])
+    dv = torch.empty_like(t["v"])
+    dg = torch.empty(B, T, H, dtype=torch.float32, device=dev)
+    db = torch.empty_like(dg)
+    ds0 = torch.empty(B, H, D, D, dtype=torch.float32, device=dev)
+    P = lambda x: None if x is None else ctypes.c_void_p(x.data_ptr())
+    stream = torch.cuda.Stream(device=dev)
+    sp = ctypes.c_void_p(stream.cuda_stream)
+    BF = _lib.GD_BFLOAT16
+    kernels_per_step = 2 if cfg["fwd_only"] else 6
+
+    def step():
+        st = lib.gd_forward(P(t["q"]), P(t["k"]), P(t["v"]), P(t["g"]), P(t["beta"]), P(t["s0"]), P(o), P(sT), BF,
+                            B, T, H, HK, D, D, flags, P(ws), nbytes, sp)
+        _lib.check(st, "gd_forward")
+        if not cfg["fwd_only"]:
+            st = lib.gd_backward(P(t["q"]), P(t["k"]), P(t["v"]), P(t["g"]), P(t["beta"]), P(t["s0"]), P(t["do"]),
+                                 P(t["dsT"]), P(dq), P(dk), P(dv), P(dg), P(db), P(ds0), BF, B, T, H, HK, D, D, flags,
+                                 P(ws), nbytes, sp)
+            _lib.check(st, "gd_backward")
+
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            step()
+    stream.synchronize()
+    code = lib.gd_read_error(P(ws), sp, None)
+    if code != 0:
+        raise RuntimeError(f"device error word {code} after warm-up")
+
+    graph = None
+    if not args.no_graph:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            step()
+        run = graph.replay
+    else:
+        def run():
+            with torch.cuda.stream(stream):
+                step()
+
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)  # > 126 MB L2
+    for _ in range(args.warmup):
+        with torch.cuda.stream(stream):
+            flush.zero_()
+            run()
+    stream.synchronize()
+
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    with Clocks(local) as clocks:
+        with torch.cuda.stream(stream):
+            for i in range(args.steps):
+                flush.zero_()
+                starts[i].record(stream)
+                run()
+                ends[i].record(stream)
+        torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    per_step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    total_ms = torch.tensor([sum(per_step_ms)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(total_ms, op=dist.ReduceOp.MAX)
+    total_s = total_ms.item() / 1e3
+    tokens_per_step = B * T * world
+    value = tokens_per_step * args.steps / total_s
+
+    # ---- per-kernel timing pass (not the headline): each entry point between events on the stream
+    kern = kernel_times(lib, t, cfg, flags, ws, nbytes, o, sT, dq, dk, dv, dg, db, ds0, stream, flush)
+    hbm, tflops, peak_kind = peaks()
+    roof = roofline(kern, cfg, hbm, tflops, peak_kind)
+
+    # ---- end to end through the C ABI with host buffers
+    e2e = end_to_end(lib, t, cfg, flags, ws, nbytes, stream, args)
+    if world > 1:
+        e2 = torch.tensor([e2e["seconds"]], dtype=torch.float64, device=dev)
+        dist.all_reduce(e2, op=dist.ReduceOp.MAX)
+        e2e["seconds"] = e2.item()
+    e2e_value = tokens_per_step * e2e["steps"] / e2e["seconds"]
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_reference(cfg, steps=3, warmup=1, threads=os.cpu_count())
+        cpu = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
+
+    step_flops = (FLOP_FWD + (0 if cfg["fwd_only"] else FLOP_BWD)) * B * T * H
+    step_bytes = (BYTES_FWD + (0 if cfg["fwd_only"] else BYTES_BWD)) * B * T * H
+    step_s = total_s / args.steps
+    if rank == 0:
+        line = {
+            "metric": METRIC if args.config == 1 else f"gated-delta tokens/s ({cfg['tag']})",
+            "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": total_s * 1e3 / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": (value / PUBLISHED_TOKENS_S) if args.config == 1 else None,
+            "dtype": "bf16", "data": "synthetic (BASELINE configs[0] distributions, seeded per rank)",
+            "config": {"workload": cfg["tag"], "global_batch": B * world, "seq_len": T, "heads": H,
+                       "key_heads": HK, "head_dim": D, "chunk": 64, "parallelism": f"dp{world} over (batch, head)",
+                       "l2": "flushed between steps (256 MiB write, outside the per-step events)",
+                       "cuda_graph": graph is not None, "per_rank_batch": B,
+                       "vs_baseline_ref": "M3 Max Metal fwd+bwd 10.210 ms at B4 T1024 H16 (reference docs)"},
+            "step_roofline": {"achieved_tflops": step_flops / step_s / 1e12,
+                              "achieved_gbs": step_bytes / step_s / 1e9,
+                              "roofline_time_us": max(step_flops / (tflops * 1e12), step_bytes / (hbm * 1e9)) * 1e6,
+                              "frac": max(step_flops / (tflops * 1e12), step_bytes / (hbm * 1e9)) / step_s,
+                              "peak": f"{peak_kind} MEASURED_PEAKS.json"},
+            "roofline": roof,
+            "kernels": kern,
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": e2e["h2d"],
+                    "d2h_bytes_per_step": e2e["d2h"], "ms_per_step": e2e["seconds"] * 1e3 / e2e["steps"]},
+            "gpu_launches": kernels_per_step * args.steps,
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    del graph
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def kernel_times(lib, t, cfg, flags, ws, nbytes, o, sT, dq, dk, dv, dg, db, ds0, stream, flush, iters=5):
+    """Average device time of each kernel (entry point) of one step, CUDA events on the launching stream, L2 flushed
+    before each step's sequence."""
+    import torch
+    from macai_b200 import _lib
+    P = lambda x: None if x is None else ctypes.c_void_p(x.data_ptr())
+    sp = ctypes.c_void_p(stream.cuda_stream)
+    B, T, H, HK, D = cfg["B"], cfg["T"], cfg["H"], cfg["HK"], cfg["D"]
+    BF = _lib.GD_BFLOAT16
+    seq = [("prep", lambda: lib.gd_prep(P(t["q"]), P(t["k"]), P(t["v"]), P(t["g"]), P(t["beta"]), BF, B, T, H, HK, D, D,
+                                        flags, P(ws), nbytes, sp)),
+           ("fwd_state", lambda: lib.gd_fwd_state(P(t["s0"]), P(o), P(sT), BF, B, T, H, HK, D, D, flags, P(ws), nbytes,
+                                                  sp))]
+    if not cfg["fwd_only"]:
+        seq += [("prep(bwd)", seq[0][1]),
+                ("fwd_state(store)", lambda: lib.gd_fwd_state(P(t["s0"]), None, None, BF, B, T, H, HK, D, D,
+                                                              flags | _lib.GD_STORE_STATES, P(ws), nbytes, sp)),
+                ("bwd_state", lambda: lib.gd_bwd_state(P(t["do"]), P(t["dsT"]), P(ds0), BF, B, T, H, HK, D, D, flags,
+                                                       P(ws), nbytes, sp)),
+                ("bwd_chunk", lambda: lib.gd_bwd_chunk(P(t["q"]), P(t["k"]), P(t["v"]), P(t["beta"]), P(t["do"]),
+                                                       P(dq), P(dk), P(dv), P(dg), P(db), BF, B, T, H, HK, D, D, flags,
+                                                       P(ws), nbytes, sp))]
+    acc = {name: 0.0 for name, _ in seq}
+    with torch.cuda.stream(stream):
+        for it in range(iters + 1):
+            flush.zero_()
+            evs = [torch.cuda.Event(enable_timing=True) for _ in range(len(seq) + 1)]
+            evs[0].record(stream)
+            for i, (name, f) in enumerate(seq):
+                _lib.check(f(), name)
+                evs[i + 1].record(stream)
+            stream.synchronize()
+            if it > 0:
+                for i, (name, _) in enumerate(seq):
+                    acc[name] += evs[i].elapsed_time(evs[i + 1])
+    return {name: acc[name] / iters * 1e3 for name in acc}  # microseconds
+
+
+def roofline(kern, cfg, hbm, tflops, peak_kind):
+    """The dominant kernel against its bound. Algorithmic work per launch (per token-head unit, D = 128, C = 64),
+    derived from the same dense counts as the step's FLOP formula:
+      fwd_state        6 D^2 + 2 C D   = 114,688 FLOP   (W S, Q S, K^T Vn; M Vn)     bytes: q, k bf16 + o bf16
+      bwd_state        6 D^2 + 2 C D   = 114,688 FLOP   (K dS, Q^T dO, W^T dVn; M^T dO)
+      bwd_chunk        10 D^2 + 16 C D + 4 C^2 = 311,296 FLOP
+      prep             4 C D + ... (C x C products and W, U) = 4 C D * 2 + ... see DESIGN.md
+    and HBM bytes per token-head of the kernel's algorithmic inputs and outputs (bf16 q/k/v/do/o/grads 256 B each row
+    of 128, fp32 g/beta/dg/dbeta 4 B)."""
+    D, C = cfg["D"], 64
+    per = {
+        "prep": (4 * C * D * 2, 3 * 2 * D + 8),
+        "prep(bwd)": (4 * C * D * 2, 3 * 2 * D + 8),
+        "fwd_state": (6 * D * D + 2 * C * D, 2 * 2 * D + 2 * D),
+        "fwd_state(store)": (6 * D * D + 2 * C * D, 2 * 2 * D),
+        "bwd_state": (6 * D * D + 2 * C * D, 2 * 2 * D + 2 * D),
+        "bwd_chunk": (10 * D * D + 16 * C * D + 4 * C * C, 2 * D * 7 + 16),
+    }
+    name = max(kern, key=kern.get)
+    units = cfg["B"] * cfg["T"] * cfg["H"]
+    flop, byts = per[name]
+    dur = kern[name] * 1e-6
+    a_t = flop * units / dur / 1e12
+    a_b = byts * units / dur / 1e9
+    if a_t / tflops >= a_b / hbm:
+        return {"kernel": name, "bound": "tensor", "achieved": a_t, "peak": tflops, "unit": "TFLOP/s",
+                "frac": a_t / tflops, "traffic": None, "peak_source": peak_kind, "duration_us": kern[name],
+                "hbm_frac": a_b / hbm}
+    return {"kernel": name, "bound": "hbm", "achieved": a_b, "peak": hbm, "unit": "GB/s", "frac": a_b / hbm,
+            "traffic": None, "peak_source": peak_kind, "duration_us": kern[name], "tensor_frac": a_t / tflops}
+
+
+def end_to_end(lib, t, cfg, flags, ws, nbytes, stream, args):
+    """The step through the C ABI for a caller holding host buffers: pinned host inputs copied to the device, forward +
+    backward, every output copied back to pinned host memory, all inside the timed region."""
+    import torch
+    from macai_b200 import _lib
+    P = lambda x: None if x is None else ctypes.c_void_p(x.data_ptr())
+    sp = ctypes.c_void_p(stream.cuda_stream)
+    B, T, H, HK, D = cfg["B"], cfg["T"], cfg["H"], cfg["HK"], cfg["D"]
+    names_in = [n for n in ("q", "k", "v", "g", "beta", "s0", "do", "dsT") if t[n] is not None]
+    if cfg["fwd_only"]:
+        names_in = [n for n in names_in if n not in ("do", "dsT")]
+    host_in = {n: t[n].cpu().pin_memory() for n in names_in}
+    dev_in = {n: torch.empty_like(t[n]) for n in names_in}
+    outs = {"o": torch.empty(B, T, H, D, dtype=torch.bfloat16, device=t["q"].device),
+            "sT": torch.empty(B, H, D, D, dtype=torch.float32, device=t["q"].device)}
+    if not cfg["fwd_only"]:
+        outs.update(dq=torch.empty_like(t["q"]), dk=torch.empty_like(t["k"]), dv=torch.empty_like(t["v"]),
+                    dg=torch.empty_like(t["g"]), db=torch.empty_like(t["g"]),
+                    ds0=torch.empty(B, H, D, D, dtype=torch.float32, device=t["q"].device))
+    host_out = {n: torch.empty(x.shape, dtype=x.dtype, pin_memory=True) for n, x in outs.items()}
+    h2d = sum(x.numel() * x.element_size() for x in host_in.values())
+    d2h = sum(x.numel() * x.element_size() for x in host_out.values())
+    BF = _lib.GD_BFLOAT16
+    g = lambda n: dev_in.get(n)
+
+    def one():
+        for n in names_in:
+            dev_in[n].copy_(host_in[n], non_blocking=True)
+        st = lib.gd_forward(P(g("q")), P(g("k")), P(g("v")), P(g("g")), P(g("beta")), P(g("s0")), P(outs["o"]),
+                            P(outs["sT"]), BF, B, T, H, HK, D, D, flags, P(ws), nbytes, sp)
+        _lib.check(st, "gd_forward")
+        if not cfg["fwd_only"]:
+            st = lib.gd_backward(P(g("q")), P(g("k")), P(g("v")), P(g("g")), P(g("beta")), P(g("s0")), P(g("do")),
+                                 P(g("dsT")), P(outs["dq"]), P(outs["dk"]), P(outs["dv"]), P(outs["dg"]),
+                                 P(outs["db"]), P(outs["ds0"]), BF, B, T, H, HK, D, D, flags, P(ws), nbytes, sp)
+            _lib.check(st, "gd_backward")
+        for n, x in outs.items():
+            host_out[n].copy_(x, non_blocking=True)
+
+    steps = max(3, min(args.steps, 10))
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            one()
+        stream.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            one()
+        e1.record(stream)
+        stream.synchronize()
+    return {"seconds": e0.elapsed_time(e1) / 1e3, "steps": steps, "h2d": h2d, "d2h": d2h}
+
+
+if __name__ == "__main__":
+    main()

@@ -221,7 +221,8 @@ cudaError_t launch_bwd_state(const void* d_o, const float* dsT, float* ds0, cons
                              unsigned char* ws, cudaStream_t st) {
   using S = BwdStateSmem<DK, DV>;
   auto kern = bwd_state_kernel<T, DK, DV>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::total);
+  static bool attr_done[kMaxDevices] = {};  // once per device: no attribute call inside a graph capture
+  cudaError_t e = set_smem_once(kern, S::total, attr_done);
   if (e != cudaSuccess) return e;
   dim3 grid(lay.H, lay.B);
   kern<<<grid, 128, S::total, st>>>(static_cast<const T*>(d_o), dsT, ds0, lay, flags, ws);

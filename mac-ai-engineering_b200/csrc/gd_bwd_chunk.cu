@@ -546,7 +546,8 @@ cudaError_t launch_bwd_chunk(const void* q, const void* k, const void* v, const 
                              unsigned char* ws, cudaStream_t st) {
   using S = ChunkSmem<DK, DV>;
   auto kern = bwd_chunk_kernel<T, DK, DV>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::total);
+  static bool attr_done[kMaxDevices] = {};  // once per device: no attribute call inside a graph capture
+  cudaError_t e = set_smem_once(kern, S::total, attr_done);
   if (e != cudaSuccess) return e;
   dim3 grid(lay.NT, lay.HK, lay.B);
   kern<<<grid, 256, S::total, st>>>(static_cast<const T*>(q), static_cast<const T*>(k), static_cast<const T*>(v), beta,

@@ -41,6 +41,23 @@ __device__ __forceinline__ void report(ErrorWord* err, int code, int where) {
 }
 
 // ------------------------------------------------------------------------------------------------------------------
+// host: the dynamic shared-memory opt-in of a kernel, set once per device (the first call of an entry point on a
+// device must therefore come before any stream capture that records it)
+
+constexpr int kMaxDevices = 64;
+
+template <typename K>
+inline cudaError_t set_smem_once(K kern, size_t bytes, bool (&done)[kMaxDevices]) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev >= 0 && dev < kMaxDevices && done[dev]) return cudaSuccess;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  if (e == cudaSuccess && dev >= 0 && dev < kMaxDevices) done[dev] = true;
+  return e;
+}
+
+// ------------------------------------------------------------------------------------------------------------------
 // shared memory, fences, mbarriers, bulk copies
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

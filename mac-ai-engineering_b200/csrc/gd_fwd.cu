@@ -507,7 +507,8 @@ cudaError_t launch_prep(const void* q, const void* k, const void* v, const float
                         const Layout& lay, int flags, unsigned char* ws, cudaStream_t st) {
   using S = PrepSmem<DK, DV>;
   auto kern = prep_kernel<T, DK, DV>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::total);
+  static bool attr_done[kMaxDevices] = {};  // once per device: no attribute call inside a graph capture
+  cudaError_t e = set_smem_once(kern, S::total, attr_done);
   if (e != cudaSuccess) return e;
   dim3 grid(lay.NT, lay.H, lay.B);
   kern<<<grid, 128, S::total, st>>>(static_cast<const T*>(q), static_cast<const T*>(k), static_cast<const T*>(v), g,
@@ -520,7 +521,8 @@ cudaError_t launch_state(const float* s0, void* o, float* sT, const Layout& lay,
                          cudaStream_t st) {
   using S = StateSmem<DK, DV>;
   auto kern = state_kernel<T, DK, DV>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::total);
+  static bool attr_done[kMaxDevices] = {};  // once per device: no attribute call inside a graph capture
+  cudaError_t e = set_smem_once(kern, S::total, attr_done);
   if (e != cudaSuccess) return e;
   dim3 grid(lay.H, lay.B);
   kern<<<grid, 128, S::total, st>>>(s0, static_cast<T*>(o), sT, lay, flags, ws);
