@@ -180,8 +180,9 @@ __global__ void __launch_bounds__(256) bwd_chunk_kernel(const T* __restrict__ qr
     {
       const float4* s4 = reinterpret_cast<const float4*>(ws + lay.sc + cidx * lay.s_bytes());
       const float4* d4 = reinterpret_cast<const float4*>(ws + lay.dsn + cidx * lay.s_bytes());
+#pragma unroll 8
       for (int i = tid; i < DK * DV / 4; i += 256) {
-        const float4 x = s4[i], y = d4[i];
+        const float4 x = __ldg(s4 + i), y = __ldg(d4 + i);
         sdot = fmaf(x.x, y.x, fmaf(x.y, y.y, fmaf(x.z, y.z, fmaf(x.w, y.w, sdot))));
       }
       sdot = warp_sum(sdot);

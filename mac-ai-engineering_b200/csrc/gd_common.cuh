@@ -422,16 +422,32 @@ __device__ __forceinline__ void load_rows(const T* x, int b, int t0, int T_, int
 template <int R, int Cc, int NTHREADS>
 __device__ __forceinline__ void f32_to_tiles(const float* __restrict__ src, unsigned char* hi, unsigned char* lo) {
   constexpr int NCHUNK = R * Cc / 8;
-  for (int idx = threadIdx.x; idx < NCHUNK; idx += NTHREADS) {
-    const int rl = idx & 7, cb = (idx >> 3) % (Cc / 8), rb = idx / (8 * (Cc / 8));
-    const int r = 8 * rb + rl;
-    const float4* p = reinterpret_cast<const float4*>(src + (size_t)r * Cc + 8 * cb);
-    const float4 a = p[0], b4 = p[1];
-    float v[8] = {a.x, a.y, a.z, a.w, b4.x, b4.y, b4.z, b4.w};
-    if (lo != nullptr) {
-      store8_split(hi, lo, r, 8 * cb, Cc, v);
-    } else {
-      store8_bf16(hi, r, 8 * cb, Cc, v);
+  static_assert(NCHUNK % NTHREADS == 0, "whole passes only");
+  constexpr int PER = NCHUNK / NTHREADS;  // 8-float chunks per thread
+  constexpr int BATCH = PER < 4 ? PER : 4;
+  // loads of a batch are all issued before its stores (memory-level parallelism instead of one round trip each)
+#pragma unroll
+  for (int p0 = 0; p0 < PER; p0 += BATCH) {
+    float4 a[BATCH], b4[BATCH];
+#pragma unroll
+    for (int u = 0; u < BATCH; ++u) {
+      const int idx = threadIdx.x + (p0 + u) * NTHREADS;
+      const int rl = idx & 7, cb = (idx >> 3) % (Cc / 8), rb = idx / (8 * (Cc / 8));
+      const float4* p = reinterpret_cast<const float4*>(src + (size_t)(8 * rb + rl) * Cc + 8 * cb);
+      a[u] = __ldg(p);
+      b4[u] = __ldg(p + 1);
+    }
+#pragma unroll
+    for (int u = 0; u < BATCH; ++u) {
+      const int idx = threadIdx.x + (p0 + u) * NTHREADS;
+      const int rl = idx & 7, cb = (idx >> 3) % (Cc / 8), rb = idx / (8 * (Cc / 8));
+      const int r = 8 * rb + rl;
+      float v[8] = {a[u].x, a[u].y, a[u].z, a[u].w, b4[u].x, b4[u].y, b4[u].z, b4[u].w};
+      if (lo != nullptr) {
+        store8_split(hi, lo, r, 8 * cb, Cc, v);
+      } else {
+        store8_bf16(hi, r, 8 * cb, Cc, v);
+      }
     }
   }
 }

@@ -1,0 +1,68 @@
+"""The C ABI library without a GPU: it loads, exports every entry point include/gated_delta_b200.h declares, sizes
+workspaces, and refuses bad arguments with status codes before touching a device (no compute calls here)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from macai_b200 import _lib
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include", "gated_delta_b200.h")
+
+
+def declared():
+    src = open(HEADER).read()
+    return sorted(set(re.findall(r"^\s*(?:const char\*|size_t|int)\s+(gd_\w+)\s*\(", src, re.M)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    names = declared()
+    assert len(names) >= 9
+    missing = [n for n in names if not hasattr(lib, n)]
+    assert not missing, missing
+    assert sorted(_lib.EXPORTS) == names
+
+
+def test_status_strings():
+    lib = _lib.load()
+    for s in range(8):
+        assert lib.gd_status_string(s)
+    assert b"unknown" in lib.gd_status_string(99)
+
+
+def test_workspace_sizes():
+    lib = _lib.load()
+    f = lib.gd_workspace_bytes(4, 1024, 16, 16, 128, 128, 0)
+    b = lib.gd_workspace_bytes(4, 1024, 16, 16, 128, 128, 1)
+    assert 0 < f < b
+    assert lib.gd_workspace_bytes(8, 1024, 16, 16, 128, 128, 1) > b          # grows with the batch
+    assert lib.gd_workspace_bytes(4, 1000, 16, 16, 128, 128, 0) == f         # chunks of 64 tokens
+    assert lib.gd_workspace_bytes(4, 1024, 16, 16, 64, 128, 1) == 0          # head width not built
+    assert lib.gd_workspace_bytes(4, 1024, 15, 4, 128, 128, 1) == 0          # value heads not a multiple of key heads
+
+
+def test_refusals_before_any_device_call():
+    lib = _lib.load()
+    nul = ctypes.c_void_p(0)
+    one = ctypes.c_void_p(256)
+    st = lib.gd_prep(one, one, one, one, one, _lib.GD_BFLOAT16, 1, 64, 1, 1, 96, 128, 0, one, 1 << 30, nul)
+    assert st == _lib.GD_ERR_SHAPE
+    st = lib.gd_prep(nul, one, one, one, one, _lib.GD_BFLOAT16, 1, 64, 1, 1, 128, 128, 0, one, 1 << 30, nul)
+    assert st == _lib.GD_ERR_ARG
+    st = lib.gd_prep(one, one, one, one, one, 7, 1, 64, 1, 1, 128, 128, 0, one, 1 << 30, nul)
+    assert st == _lib.GD_ERR_ARG
+    st = lib.gd_prep(ctypes.c_void_p(257), one, one, one, one, _lib.GD_BFLOAT16, 1, 64, 1, 1, 128, 128, 0, one,
+                     1 << 30, nul)
+    assert st == _lib.GD_ERR_ALIGN
+    st = lib.gd_forward(one, one, one, one, one, nul, one, nul, _lib.GD_BFLOAT16, 0, 64, 1, 1, 128, 128, 0, one,
+                        1 << 30, nul)
+    assert st == _lib.GD_ERR_SHAPE
+
+
+def test_error_type_carries_status():
+    e = _lib.GatedDeltaError(_lib.GD_ERR_TIMEOUT, "gd_forward")
+    assert e.status == _lib.GD_ERR_TIMEOUT and "gd_forward" in str(e)
+    with pytest.raises(_lib.GatedDeltaError):
+        _lib.check(_lib.GD_ERR_SHAPE, "x")

@@ -1,0 +1,113 @@
+"""BASELINE.json's configurations on the B200 kernels, each against the float64 oracle with the north star's bar
+(max error <= 2x transformers' own error against float64, per tensor), at full size where the CPU references finish
+in seconds and on (batch, head) slices plus size-independent properties where they do not."""
+import math
+
+import pytest
+import torch
+
+from oracle import gated_delta_f64 as ref
+from oracle import parity, transformers_ref
+from test_gpu_backward import NAMES, run_grads
+from test_gpu_forward import inputs
+
+pytestmark = pytest.mark.gpu
+
+
+def ratios(rep):
+    return {k: round(v["ratio"], 3) for k, v in rep.items()}
+
+
+def parity_case(q, k, v, g, beta, s0, do, dsT):
+    got = run_grads(q, k, v, g, beta, s0, do, dsT)
+    truth = ref.dropin(q, k, v, g, beta, s0, do.double(), dsT)
+    theirs = transformers_ref.run(q, k, v, g, beta, s0, do=do, dsT=dsT)
+    return parity.check(got, theirs, truth, names=NAMES)
+
+
+def test_config1_full_size():
+    """B=4, T=1024, H=16, d=128, bf16, l2-normalised q/k, fwd+bwd (dO ~ N(0,1) bf16)."""
+    q, k, v, g, beta, _ = inputs(4, 1024, 16, seed=101, s0=False)
+    gen = torch.Generator().manual_seed(102)
+    do = torch.randn(4, 1024, 16, 128, generator=gen).to(torch.bfloat16)
+    rep = parity_case(q, k, v, g, beta, None, do, None)
+    assert not parity.failures(rep), ratios(rep)
+
+
+def test_config2_gqa_with_initial_state():
+    """B=2, T=1024, 16 key heads serving 32 value heads, initial state ~ N(0, 0.02) with its gradient, final state."""
+    q, k, v, g, beta, s0 = inputs(2, 1024, 32, seed=201, s0=True, HK=16)
+    gen = torch.Generator().manual_seed(202)
+    do = torch.randn(2, 1024, 32, 128, generator=gen).to(torch.bfloat16)
+    dsT = torch.randn(2, 32, 128, 128, generator=gen) * 0.02
+    rep = parity_case(q, k, v, g, beta, s0, do, dsT)
+    assert not parity.failures(rep), ratios(rep)
+
+
+def test_config3_long_prefill_heads():
+    """B=1, T=32768, H=32 forward with the final state on the GPU; heads 0 and 31 against the CPU references."""
+    from macai_b200.gated_delta import chunk_gated_delta_rule
+    q, k, v, g, beta, _ = inputs(1, 32768, 32, seed=301, s0=False)
+    dev = "cuda"
+    with torch.no_grad():
+        o, sT = chunk_gated_delta_rule(q.to(dev), k.to(dev), v.to(dev), g.to(dev), beta.to(dev),
+                                       output_final_state=True, use_qk_l2norm_in_kernel=True)
+    o, sT = o.cpu(), sT.cpu()
+    for h in (0, 31):
+        sl = lambda x: x[:, :, h:h + 1].contiguous()
+        truth = ref.dropin(sl(q), sl(k), sl(v), sl(g), sl(beta))
+        theirs = transformers_ref.run(sl(q), sl(k), sl(v), sl(g), sl(beta))
+        rep = parity.check([sl(o), sT[:, h:h + 1]], theirs, truth, names=("o", "sT"))
+        assert not parity.failures(rep), (h, ratios(rep))
+
+
+def test_config4_slices_and_shard_bit_identity():
+    """B=64, T=4096, H=32 fwd+bwd: (batch, head) slices against the references, and the rows a shard would own
+    computed alone are bit-identical to the same rows of the full batch (the sharded-vs-single-GPU property)."""
+    from macai_b200.gated_delta import chunk_gated_delta_rule
+    B, T, H, D = 64, 4096, 32, 128
+    dev = "cuda"
+    gen = torch.Generator(device=dev).manual_seed(401)
+    bf = torch.bfloat16
+    q = torch.randn(B, T, H, D, generator=gen, device=dev).to(bf)
+    k = torch.randn(B, T, H, D, generator=gen, device=dev).to(bf)
+    v = torch.randn(B, T, H, D, generator=gen, device=dev).to(bf)
+    beta = torch.sigmoid(torch.randn(B, T, H, generator=gen, device=dev))
+    g = -torch.exp(torch.rand(B, T, H, generator=gen, device=dev) * math.log(16.0)) * torch.nn.functional.softplus(
+        torch.randn(B, T, H, generator=gen, device=dev))
+    do = torch.randn(B, T, H, D, generator=gen, device=dev).to(bf)
+
+    def run(rows):
+        xs = [x[rows].contiguous().requires_grad_(True) for x in (q, k, v, g, beta)]
+        o, _ = chunk_gated_delta_rule(*xs, use_qk_l2norm_in_kernel=True)
+        (o.float() * do[rows].float()).sum().backward()
+        return [o.detach()] + [x.grad for x in xs]
+
+    full = run(slice(0, B))
+    part = run(slice(48, 56))                      # one rank's rows at 8 GPUs
+    for a, b in zip(full, part):
+        assert parity.identical(a[48:56], b)
+    del part
+    for (b, h) in ((0, 0), (63, 31)):
+        sl = lambda x: x[b:b + 1, :, h:h + 1].cpu().contiguous()
+        truth = ref.dropin(sl(q), sl(k), sl(v), sl(g), sl(beta), do=sl(do).double())
+        theirs = transformers_ref.run(sl(q), sl(k), sl(v), sl(g), sl(beta), do=sl(do))
+        got = [sl(full[0]), None] + [sl(x) for x in full[1:]] + [None]
+        rep = parity.check(got, theirs, truth, names=NAMES)
+        assert not parity.failures(rep), ((b, h), ratios(rep))
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.float32])
+def test_other_input_dtypes_run(dtype):
+    """fp16 and fp32 inputs run through the same bf16 tensor-core kernels; outputs come back in the input dtype and
+    stay within the reference's own drop-in bar for bf16 (2e-2 of the largest magnitude, tests/test_harness.py:
+    100-116 of the reference). An fp32-exact mode is not built."""
+    q, k, v, g, beta, s0 = inputs(2, 200, 2, seed=501, s0=True, dtype=dtype)
+    gen = torch.Generator().manual_seed(502)
+    do = torch.randn(2, 200, 2, 128, generator=gen).to(dtype)
+    got = run_grads(q, k, v, g, beta, s0, do, None)
+    truth = ref.dropin(q, k, v, g, beta, s0, do.double(), None)
+    assert got[0].dtype == dtype and got[2].dtype == dtype
+    for n, a, t in zip(NAMES, got, truth):
+        if a is not None:
+            assert parity.rel_err(a, t) < 2e-2, n
