@@ -1,212 +1,274 @@
-// Backward kernels of the chunked gated delta rule on B200 (sm_100a):
-//   bwd_state_kernel  one CTA per (value head, batch row): the reverse sequential pass carrying dS = dLoss/dS in fp32
-//                     registers, chunks last to first; keeps dS_{c+1} and dVn per chunk for the per-chunk kernel;
-//   bwd_chunk_kernel  one CTA per (chunk, key head, batch row): every gradient of the chunk, all independent, no atomics.
-// Equations (tools/check_chunk_equations.py:49-76 and src/macai/gated_delta/_chunked.py:20-34 of the reference):
-//   dVn = M^T dO + diag(e) K dS_{c+1}
+// Reverse state pass of the chunked gated delta rule on B200 (sm_100a).
+//
+// One CTA per (value head, batch row) walks the chunks last to first carrying dS = dLoss/dS (fp32, in registers):
+//   dVn = M^T dO + K~ dS_{c+1}                       (K~ = diag(e) K: the decay e of the state update)
 //   dS_c = exp(G_last) dS_{c+1} + (diag(gamma) Q)^T dO - W^T dVn
-//   dM = Gamma * (dO Vn^T) (lower), dQ = diag(gamma) dO S_c^T + dM K, dKs = diag(e) Vn dS_{c+1}^T
-//   dW = -dVn S_c^T, X = A^T dW, Y = A^T dVn, dV = diag(beta) Y
-//   dA = strict_lower(dW (diag(beta gamma) K)^T + dVn (diag(beta) V)^T), dL = -A^T dA A^T (strictly lower)
-//   P = dL * Gamma, dK = dM^T Q + dKs + diag(beta gamma) X + diag(beta) P K + P^T diag(beta) K
-//   dbeta = gamma (k . X) + (v . Y) + rowsum(P * (K K^T)); dg without cancellation (see dg_chunk below).
-// Precision (bf16 operands, fp32 accumulation): dS, gamma Q, dM, Vn (with dS), dVn (in A^T dVn) are split into bf16
-// hi + lo pairs; every other operand is one bf16. The choice keeps every gradient within the parity bar with margin.
+// (tools/check_chunk_equations.py:51-52 and src/macai/gated_delta/_chunked.py:20-24 of the reference). Only K~ dS and
+// W^T dVn are on the sequential chain; M^T dO and (gamma Q)^T dO do not depend on dS and are issued one chunk ahead.
+// It keeps, per chunk, the images the per-chunk gradient kernel reads: dS_{c+1}^T (hi, lo), dVn^T (hi, lo), dO, and
+// the 16 partial sums of <S_c, dS_{c+1}> (from the forward recompute's fp32 S_c^T).
+//
+// Warp specialisation as in the forward pass: 16 epilogue warps (warp w: TMEM lane quadrant w % 4 = value columns,
+// tokens 16 (w / 4) .. +15, key rows 32 (w / 4) .. +31 of dS held in registers) and one MMA / bulk-copy thread; all
+// hand-offs are mbarriers. Precision: dS and K~ split into bf16 hi + lo (three products), gamma Q split, the rest bf16.
 #include "gd_common.cuh"
 #include "gd_layout.cuh"
 
 namespace gd {
 
-// ------------------------------------------------------------------------------------------------------------------
-// reverse state pass
-
 template <int DK, int DV>
 struct BwdStateSmem {
-  static constexpr size_t dth = 0;                       // [DV x DK] dS^T hi (rows v, cols dk)
-  static constexpr size_t dtl = dth + DV * DK * 2;       //           lo
-  static constexpr size_t qk = dtl + DV * DK * 2;        // stage: [2][64 x DK] q, k images (hi)
-  static constexpr size_t qkl = qk + 2 * 64 * DK * 2;    // stage: [2][64 x DK] their low halves
-  static constexpr size_t wt = qkl + 2 * 64 * DK * 2;    // stage: [DK x 64] W^T image
-  static constexpr size_t m = wt + DK * 64 * 2;          // stage: [64 x 64] M image
-  static constexpr size_t g = m + 64 * 64 * 2;           // stage: [64] G
-  static constexpr size_t dO = g + 64 * 4;               // [64 x DV] dO tile
-  static constexpr size_t gqh = dO + 64 * DV * 2;        // [64 x DK] (gamma Q) hi
-  static constexpr size_t gql = gqh + 64 * DK * 2;       //                      lo
-  static constexpr size_t dvt = gql + 64 * DK * 2;       // [DV x 64] dVn^T
-  static constexpr size_t bar = dvt + DV * 64 * 2;       // 2 mbarriers: mma, inputs
-  static constexpr size_t tmem = bar + 2 * 8;
+  static constexpr size_t dsh = 0;                         // [DV x DK] dS^T hi (rows v, cols dk)
+  static constexpr size_t dsl = dsh + DV * DK * 2;         //            lo
+  static constexpr size_t dvh = dsl + DV * DK * 2;         // [DV x 64] dVn^T hi
+  static constexpr size_t crit0 = dvh + DV * 64 * 2;       // two stages of the sequential chain, each:
+  static constexpr size_t c_kt = 0;                        //   [2][64 x DK] K~ hi, lo
+  static constexpr size_t c_g = c_kt + 2 * 64 * DK * 2;    //   [64] G
+  static constexpr size_t crit_bytes = c_g + 64 * 4;
+  static constexpr size_t wt = crit0 + 2 * crit_bytes;     // [DK x 64] W^T (one buffer)
+  static constexpr size_t m = wt + DK * 64 * 2;            // [64 x 64] M        } inputs of the dS-independent
+  static constexpr size_t gq = m + 64 * 64 * 2;            // [2][64 x DK] gamma Q }  products, one chunk ahead
+  static constexpr size_t dO = gq + 2 * 64 * DK * 2;       // [64 x DV] dO       }
+  static constexpr size_t bar = dO + 64 * DV * 2;
+  static constexpr int NBAR = 12;
+  static constexpr size_t tmem = bar + NBAR * 8;
   static constexpr size_t total = tmem + 8;
-  static constexpr uint32_t stage_bytes = 4 * 64 * DK * 2 + DK * 64 * 2 + 64 * 64 * 2 + 64 * 4;
 };
 
-template <int DK, int DV, typename S>
-__device__ __forceinline__ void issue_bwd_stage(unsigned char* smem, const unsigned char* ws, const Layout& lay,
-                                                size_t cidx, uint64_t* bar) {
-  mbar_arrive_expect_tx(bar, S::stage_bytes);
-  bulk_g2s(smem + S::qk, ws + lay.qk + cidx * lay.qk_bytes(), (uint32_t)lay.qk_bytes(), bar);
-  bulk_g2s(smem + S::qkl, ws + lay.qkl + cidx * lay.qk_bytes(), (uint32_t)lay.qk_bytes(), bar);
-  bulk_g2s(smem + S::wt, ws + lay.wt + cidx * lay.wt_bytes(), (uint32_t)lay.wt_bytes(), bar);
-  bulk_g2s(smem + S::m, ws + lay.m + cidx * lay.m_bytes(), (uint32_t)lay.m_bytes(), bar);
-  bulk_g2s(smem + S::g, ws + lay.gc + cidx * lay.gc_bytes(), (uint32_t)lay.gc_bytes(), bar);
-}
-
 template <typename T, int DK, int DV>
-__global__ void __launch_bounds__(128) bwd_state_kernel(const T* __restrict__ d_o, const float* __restrict__ dsT,
+__global__ void __launch_bounds__(544) bwd_state_kernel(const T* __restrict__ d_o, const float* __restrict__ dsT,
                                                         float* __restrict__ ds0, Layout lay, int flags,
                                                         unsigned char* __restrict__ ws) {
-  static_assert(DV == 128, "the reverse pass maps one thread to each of 128 value columns");
+  static_assert(DV == 128 && DK == 128, "one TMEM lane per value column; four epilogue warps per lane quadrant");
   using S = BwdStateSmem<DK, DV>;
   extern __shared__ __align__(1024) unsigned char smem[];
   ErrorWord* err = reinterpret_cast<ErrorWord*>(ws + lay.err);
   const int h = blockIdx.x, b = blockIdx.y;
-  const int tid = threadIdx.x, warp = tid >> 5;
-  const int vcol = tid;
-  uint64_t* bar_mma = reinterpret_cast<uint64_t*>(smem + S::bar);
-  uint64_t* bar_in = bar_mma + 1;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::bar);
+  uint64_t* crit_full = bars + 0;   // [2] K~, G loaded
+  uint64_t* wt_full = bars + 2;
+  uint64_t* pre_full = bars + 3;    // M, gamma Q loaded
+  uint64_t* a_full = bars + 4;      // (M^T dO)^T and ((gamma Q)^T dO)^T done
+  uint64_t* b_full = bars + 5;      // (K~ dS)^T done
+  uint64_t* d_full = bars + 6;      // (W^T dVn)^T done
+  uint64_t* ds_ready = bars + 7;    // 16 warps: dS tiles written
+  uint64_t* do_full = bars + 8;     // 16 warps: dO tile written
+  uint64_t* dvn_full = bars + 9;    // 16 warps: dVn tile written, G read
   uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + S::tmem);
-  const float* sG = reinterpret_cast<const float*>(smem + S::g);
-  const size_t row0 = ((size_t)b * lay.H + h) * lay.NT;
+  const int NT = lay.NT;
+  const size_t row0 = ((size_t)b * lay.H + h) * NT;
 
   if (warp == 0) {
     tmem_alloc(tslot, 512);
     tmem_relinquish();
   }
   if (tid == 0) {
-    mbar_init(bar_mma, 1);
-    mbar_init(bar_in, 1);
+    for (int i = 0; i < 7; ++i) mbar_init(bars + i, 1);
+    for (int i = 7; i < 10; ++i) mbar_init(bars + i, 16);
     fence_mbar_init();
   }
-  __syncthreads();
-  if (tid == 0) issue_bwd_stage<DK, DV, S>(smem, ws, lay, row0 + lay.NT - 1, bar_in);
-
-  float dS[DK];  // column vcol of dLoss/dS (all key rows), fp32
-  {
-    const float* p = dsT ? dsT + ((size_t)b * lay.H + h) * DK * DV : nullptr;
-#pragma unroll
-    for (int d = 0; d < DK; ++d) dS[d] = p ? p[(size_t)d * DV + vcol] : 0.f;
-#pragma unroll
-    for (int d8 = 0; d8 < DK / 8; ++d8) store8_split(smem + S::dth, smem + S::dtl, vcol, 8 * d8, DK, dS + 8 * d8);
-  }
-  fence_async_smem();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tm = *tslot;
-  const uint32_t tA = tm + 0, tB = tm + 64, tC = tm + 128, tD = tm + 256;
-
-  uint32_t ph_mma = 0, ph_in = 0;
+  const uint32_t tA = tm, tB = tm + 64, tD = tm + 384;  // ((gamma Q)^T dO)^T at tm + 128 + 128 (n & 1)
   bool ok = true;
-  for (int c = lay.NT - 1; c >= 0 && ok; --c) {
-    const size_t cidx = row0 + c;
-    const int t0 = c * C;
-    // dS_{c+1} for the per-chunk kernel, then this chunk's dO tile
-    {
-      float* dsn = reinterpret_cast<float*>(ws + lay.dsn + cidx * lay.s_bytes());
-#pragma unroll
-      for (int d = 0; d < DK; ++d) dsn[(size_t)d * DV + vcol] = dS[d];
-    }
-    load_rows<T, DV>(d_o, b, t0, lay.T, lay.H, h, false, 1.f, smem + S::dO, nullptr);
-    ok = mbar_wait(bar_in, ph_in, err, 30);
-    ph_in ^= 1;
-    ok = __syncthreads_and(ok);
-    if (!ok) break;
-    // (gamma Q) hi / lo from the q image's hi + lo halves
-    for (int idx = tid; idx < 64 * DK / 8; idx += 128) {
-      const int rl = idx & 7, cb = (idx >> 3) % (DK / 8), rb = idx / (8 * (DK / 8));
-      const int r = 8 * rb + rl;
-      const uint4 u = *reinterpret_cast<const uint4*>(smem + S::qk + blk_off(r, 8 * cb, DK));
-      const uint4 ul = *reinterpret_cast<const uint4*>(smem + S::qkl + blk_off(r, 8 * cb, DK));
-      const __nv_bfloat162* hq = reinterpret_cast<const __nv_bfloat162*>(&u);
-      const __nv_bfloat162* lq = reinterpret_cast<const __nv_bfloat162*>(&ul);
-      const float gr = __expf(sG[r]);
-      float v[8];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 f = __bfloat1622float2(hq[e]);
-        const float2 fl = __bfloat1622float2(lq[e]);
-        v[2 * e] = gr * (f.x + fl.x);
-        v[2 * e + 1] = gr * (f.y + fl.y);
+
+  auto load_crit = [&](int c, int s) {
+    unsigned char* st = smem + S::crit0 + s * S::crit_bytes;
+    mbar_arrive_expect_tx(crit_full + s, (uint32_t)S::crit_bytes);
+    bulk_g2s(st + S::c_kt, ws + lay.kt + (row0 + c) * lay.qk_bytes(), (uint32_t)lay.qk_bytes(), crit_full + s);
+    bulk_g2s(st + S::c_g, ws + lay.gc + (row0 + c) * lay.gc_bytes(), (uint32_t)lay.gc_bytes(), crit_full + s);
+  };
+  auto load_wt = [&](int c) {
+    mbar_arrive_expect_tx(wt_full, (uint32_t)lay.wt_bytes());
+    bulk_g2s(smem + S::wt, ws + lay.wt + (row0 + c) * lay.wt_bytes(), (uint32_t)lay.wt_bytes(), wt_full);
+  };
+  auto load_pre = [&](int c) {
+    mbar_arrive_expect_tx(pre_full, (uint32_t)(lay.m_bytes() + lay.qk_bytes()));
+    bulk_g2s(smem + S::m, ws + lay.m + (row0 + c) * lay.m_bytes(), (uint32_t)lay.m_bytes(), pre_full);
+    bulk_g2s(smem + S::gq, ws + lay.gq + (row0 + c) * lay.qk_bytes(), (uint32_t)lay.qk_bytes(), pre_full);
+  };
+  const Tile tDO{smem_u32(smem + S::dO), DV};
+  // chunk c's dO image for the per-chunk kernel; its reads finish before the products that precede the tile's reuse
+  auto copy_do = [&](int c) {
+    bulk_s2g(ws + lay.doi + (row0 + c) * lay.vi_bytes(), smem + S::dO, (uint32_t)lay.vi_bytes());
+    bulk_commit();
+    bulk_wait_read0();
+  };
+  // (M^T dO)^T = dO^T M [DV x 64]; ((gamma Q)^T dO)^T = dO^T (gamma Q) [DV x DK], gamma Q split
+  auto issue_pre = [&](int n) {
+    mma_tiles(tA, DV, 64, 64, tDO, false, 0, 0, Tile{smem_u32(smem + S::m), 64}, true, 0, false);
+    const uint32_t tC = tm + 128 + 128 * (n & 1);
+    mma_tiles(tC, DV, DK, 64, tDO, false, 0, 0, Tile{smem_u32(smem + S::gq), DK}, true, 0, false);
+    mma_tiles(tC, DV, DK, 64, tDO, false, 0, 0, Tile{smem_u32(smem + S::gq + 64 * DK * 2), DK}, true, 0, true);
+    mma_commit(a_full);
+  };
+
+  if (warp == 16) {
+    // ---------------- MMA and bulk-copy issuer (one thread); iteration n handles chunk c = NT - 1 - n
+    if (lane == 0) {
+      load_crit(NT - 1, 0);
+      if (NT > 1) load_crit(NT - 2, 1);
+      load_wt(NT - 1);
+      load_pre(NT - 1);
+      ok = mbar_wait(pre_full, 0, err, 30) && mbar_wait(do_full, 0, err, 31);
+      if (ok) {
+        tc_fence_after();
+        copy_do(NT - 1);
+        issue_pre(0);
       }
-      store8_split(smem + S::gqh, smem + S::gql, r, 8 * cb, DK, v);
-    }
-    fence_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    if (tid == 0) {
-      tc_fence_after();
-      const Tile tdo{smem_u32(smem + S::dO), DV};
-      // (M^T dO)^T = dO^T M  [DV x 64]
-      mma_tiles(tA, DV, 64, 64, tdo, false, 0, 0, Tile{smem_u32(smem + S::m), 64}, true, 0, false);
-      // (K dS)^T = dS^T K^T  [DV x 64], dS and K split (hi hi + hi lo + lo hi)
-      const Tile tk{smem_u32(smem + S::qk + 64 * DK * 2), DK}, tkl{smem_u32(smem + S::qkl + 64 * DK * 2), DK};
-      mma_tiles(tB, DV, 64, DK, Tile{smem_u32(smem + S::dth), DK}, true, 0, 0, tk, false, 0, false);
-      mma_tiles(tB, DV, 64, DK, Tile{smem_u32(smem + S::dth), DK}, true, 0, 0, tkl, false, 0, true);
-      mma_tiles(tB, DV, 64, DK, Tile{smem_u32(smem + S::dtl), DK}, true, 0, 0, tk, false, 0, true);
-      // ((gamma Q)^T dO)^T = dO^T (gamma Q)  [DV x DK], gamma Q split
-      mma_tiles(tC, DV, DK, 64, tdo, false, 0, 0, Tile{smem_u32(smem + S::gqh), DK}, true, 0, false);
-      mma_tiles(tC, DV, DK, 64, tdo, false, 0, 0, Tile{smem_u32(smem + S::gql), DK}, true, 0, true);
-      mma_commit(bar_mma);
-    }
-    ok = mbar_wait(bar_mma, ph_mma, err, 31);
-    ph_mma ^= 1;
-    ok = __syncthreads_and(ok);
-    if (!ok) break;
-    tc_fence_after();
-    const float Glast = sG[63];
-    {
-      float a[32], bb[32], dvn[32];
-      float* dvn_out = reinterpret_cast<float*>(ws + lay.dvn + cidx * lay.u_bytes());
-#pragma unroll 1
-      for (int half = 0; half < 2; ++half) {
-        tmem_ld32(tmem_lane_addr(tA, warp, 32 * half), a);
-        tmem_ld32(tmem_lane_addr(tB, warp, 32 * half), bb);
-#pragma unroll
-        for (int jj = 0; jj < 32; ++jj) {
-          const int i = 32 * half + jj;
-          dvn[jj] = fmaf(__expf(Glast - sG[i]), bb[jj], a[jj]);
-          dvn_out[i * DV + vcol] = dvn[jj];
+      for (int n = 0; n < NT && ok; ++n) {
+        const int c = NT - 1 - n, s = n & 1;
+        const size_t cidx = row0 + c;
+        unsigned char* st = smem + S::crit0 + s * S::crit_bytes;
+        ok = mbar_wait(crit_full + s, (n >> 1) & 1, err, 32) && mbar_wait(ds_ready, n & 1, err, 33);
+        if (!ok) break;
+        tc_fence_after();
+        // dS_{c+1} images for the per-chunk kernel
+        bulk_s2g(ws + lay.dsi + cidx * 2 * lay.si_bytes(), smem + S::dsh, 2 * (uint32_t)lay.si_bytes());
+        bulk_commit();
+        // * (K~ dS)^T = dS^T K~^T [DV x 64]: hi hi + hi lo + lo hi
+        const Tile tKh{smem_u32(st + S::c_kt), DK}, tKl{smem_u32(st + S::c_kt + 64 * DK * 2), DK};
+        const Tile tDh{smem_u32(smem + S::dsh), DK}, tDl{smem_u32(smem + S::dsl), DK};
+        mma_tiles(tB, DV, 64, DK, tDh, true, 0, 0, tKh, false, 0, false);
+        mma_tiles(tB, DV, 64, DK, tDh, true, 0, 0, tKl, false, 0, true);
+        mma_tiles(tB, DV, 64, DK, tDl, true, 0, 0, tKh, false, 0, true);
+        mma_commit(b_full);
+        // the dS-independent inputs of the next chunk can replace this chunk's once its products are done
+        ok = mbar_wait(a_full, n & 1, err, 34);
+        if (!ok) break;
+        if (c > 0) load_pre(c - 1);
+        ok = mbar_wait(dvn_full, n & 1, err, 35) && mbar_wait(wt_full, n & 1, err, 36);
+        if (!ok) break;
+        tc_fence_after();
+        bulk_s2g(ws + lay.dvni + cidx * lay.vn_bytes(), smem + S::dvh, DV * 64 * 2);
+        bulk_commit();
+        bulk_wait_read0();  // the dS and dVn tiles may be rewritten once d_full fires
+        // * (W^T dVn)^T = dVn^T W [DV x DK]
+        mma_tiles(tD, DV, DK, 64, Tile{smem_u32(smem + S::dvh), 64}, true, 0, 0, Tile{smem_u32(smem + S::wt), 64},
+                  false, 0, false);
+        mma_commit(d_full);
+        if (c > 0) {
+          // refill this K~ stage with chunk c - 2 (its reader, (K~ dS)^T, is done: b_full precedes a_full... wait it)
+          ok = mbar_wait(b_full, n & 1, err, 37);
+          if (!ok) break;
+          if (c > 1) load_crit(c - 2, s);
+          ok = mbar_wait(d_full, n & 1, err, 38);
+          if (!ok) break;
+          load_wt(c - 1);
+          // next chunk's dS-independent products
+          ok = mbar_wait(pre_full, (n + 1) & 1, err, 39) && mbar_wait(do_full, (n + 1) & 1, err, 40);
+          if (!ok) break;
+          tc_fence_after();
+          copy_do(c - 1);
+          issue_pre(n + 1);
         }
-#pragma unroll
-        for (int q8 = 0; q8 < 4; ++q8) store8_bf16(smem + S::dvt, vcol, 32 * half + 8 * q8, 64, dvn + 8 * q8);
       }
+      bulk_wait0();
     }
-    fence_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    if (tid == 0) {
-      tc_fence_after();
-      // (W^T dVn)^T = dVn^T W  [DV x DK]
-      mma_tiles(tD, DV, DK, 64, Tile{smem_u32(smem + S::dvt), 64}, true, 0, 0, Tile{smem_u32(smem + S::wt), 64},
-                false, 0, false);
-      mma_commit(bar_mma);
-    }
-    ok = mbar_wait(bar_mma, ph_mma, err, 32);
-    ph_mma ^= 1;
-    ok = __syncthreads_and(ok);
-    if (!ok) break;
-    tc_fence_after();
+  } else {
+    // ---------------- epilogue warps
+    const int qd = warp & 3, quarter = warp >> 2;
+    const int v = 32 * qd + lane;
+    const int tk0 = 16 * quarter;
+    const int dk0 = 32 * quarter;
+    float Dr[32];  // dS[dk0 + j][v]
+    auto write_ds = [&]() {
+#pragma unroll
+      for (int q8 = 0; q8 < 4; ++q8) store8_split(smem + S::dsh, smem + S::dsl, v, dk0 + 8 * q8, DK, Dr + 8 * q8);
+      fence_async_smem();
+      mbar_arrive_warp(ds_ready);
+    };
+    // this chunk's dO tile: 1024 16-byte pieces, two per thread, eight consecutive threads per 128-byte core matrix
+    auto load_do = [&](int c) {
+      const int t0 = c * C;
+#pragma unroll
+      for (int p = 0; p < 2; ++p) {
+        const int idx = tid + 512 * p;
+        const int rl = idx & 7, cb = (idx >> 3) & 15, rb = idx >> 7;
+        const int r = 8 * rb + rl, t = t0 + r;
+        float x[8];
+        if (d_o != nullptr && t < lay.T) {
+          load8<T>(d_o + (((size_t)b * lay.T + t) * lay.H + h) * DV + 8 * cb, x);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) x[e] = 0.f;
+        }
+        store8_bf16(smem + S::dO, r, 8 * cb, DV, x);
+      }
+      fence_async_smem();
+      mbar_arrive_warp(do_full);
+    };
     {
-      const float gl = __expf(Glast);
-      float cc[32], dd[32];
+      const float* p = dsT ? dsT + ((size_t)b * lay.H + h) * DK * DV : nullptr;
 #pragma unroll
-      for (int q4 = 0; q4 < DK / 32; ++q4) {
-        tmem_ld32(tmem_lane_addr(tC, warp, 32 * q4), cc);
-        tmem_ld32(tmem_lane_addr(tD, warp, 32 * q4), dd);
-#pragma unroll
-        for (int jj = 0; jj < 32; ++jj) dS[32 * q4 + jj] = fmaf(gl, dS[32 * q4 + jj], cc[jj] - dd[jj]);
-      }
-#pragma unroll
-      for (int d8 = 0; d8 < DK / 8; ++d8) store8_split(smem + S::dth, smem + S::dtl, vcol, 8 * d8, DK, dS + 8 * d8);
+      for (int j = 0; j < 32; ++j) Dr[j] = p ? p[(size_t)(dk0 + j) * DV + v] : 0.f;
+      write_ds();
+      load_do(NT - 1);
     }
-    fence_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    if (tid == 0 && c > 0) issue_bwd_stage<DK, DV, S>(smem, ws, lay, cidx - 1, bar_in);
-  }
-  if (ok && ds0 != nullptr) {
-    float* p = ds0 + ((size_t)b * lay.H + h) * DK * DV;
+    for (int n = 0; n < NT; ++n) {
+      const int c = NT - 1 - n, s = n & 1;
+      const size_t cidx = row0 + c;
+      const float* sG = reinterpret_cast<const float*>(smem + S::crit0 + s * S::crit_bytes + S::c_g);
+      {  // partial <S_c, dS_{c+1}> of this thread's 32 entries (fp32 S_c^T from the forward recompute)
+        const float4* sc = reinterpret_cast<const float4*>(ws + lay.scf + cidx * lay.s_bytes() + ((size_t)v * DK + dk0) * 4);
+        float acc = 0.f;
 #pragma unroll
-    for (int d = 0; d < DK; ++d) p[(size_t)d * DV + vcol] = dS[d];
+        for (int q4 = 0; q4 < 8; ++q4) {
+          const float4 x = __ldg(sc + q4);
+          acc = fmaf(x.x, Dr[4 * q4], fmaf(x.y, Dr[4 * q4 + 1], fmaf(x.z, Dr[4 * q4 + 2], fmaf(x.w, Dr[4 * q4 + 3], acc))));
+        }
+        acc = warp_sum(acc);
+        if (lane == 0) reinterpret_cast<float*>(ws + lay.sl + cidx * 64)[warp] = acc;
+      }
+      // * dVn = M^T dO + K~ dS_{c+1}
+      if (!mbar_wait(b_full, n & 1, err, 41) || !mbar_wait(a_full, n & 1, err, 42)) { ok = false; break; }
+      tc_fence_after();
+      const float gl = __expf(sG[63]);
+      {
+        float a[16], bb[16];
+        tmem_ld16(tmem_lane_addr(tA, warp, tk0), a);
+        tmem_ld16(tmem_lane_addr(tB, warp, tk0), bb);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) a[j] += bb[j];
+        float hi[16], lo[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) split_bf16(a[j], hi[j], lo[j]);
+        store8_bf16(smem + S::dvh, v, tk0, 64, hi);
+        store8_bf16(smem + S::dvh, v, tk0 + 8, 64, hi + 8);
+        unsigned char* dlo = ws + lay.dvni + cidx * lay.vn_bytes() + DV * 64 * 2;  // the low half: straight to HBM
+        store8_bf16(dlo, v, tk0, 64, lo);
+        store8_bf16(dlo, v, tk0 + 8, 64, lo + 8);
+        tc_fence_before();
+        fence_async_smem();
+        mbar_arrive_warp(dvn_full);
+      }
+      // the next chunk's dO (this chunk's dO products are done: a_full; its image went out before they were issued)
+      if (c > 0) load_do(c - 1);
+      // * dS_c = exp(G_last) dS_{c+1} + (gamma Q)^T dO - W^T dVn
+      if (!mbar_wait(d_full, n & 1, err, 43)) { ok = false; break; }
+      tc_fence_after();
+      {
+        const uint32_t tC = tm + 128 + 128 * (n & 1);
+        float cc[16], dd[16];
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          tmem_ld16(tmem_lane_addr(tC, warp, dk0 + 16 * hh), cc);
+          tmem_ld16(tmem_lane_addr(tD, warp, dk0 + 16 * hh), dd);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) Dr[16 * hh + j] = fmaf(gl, Dr[16 * hh + j], cc[j] - dd[j]);
+        }
+        tc_fence_before();
+      }
+      if (c > 0) write_ds();
+    }
+    if (ok && ds0 != nullptr) {
+      float* p = ds0 + ((size_t)b * lay.H + h) * DK * DV;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) p[(size_t)(dk0 + j) * DV + v] = Dr[j];
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -221,16 +283,13 @@ cudaError_t launch_bwd_state(const void* d_o, const float* dsT, float* ds0, cons
                              unsigned char* ws, cudaStream_t st) {
   using S = BwdStateSmem<DK, DV>;
   auto kern = bwd_state_kernel<T, DK, DV>;
-  static bool attr_done[kMaxDevices] = {};  // once per device: no attribute call inside a graph capture
+  static bool attr_done[kMaxDevices] = {};
   cudaError_t e = set_smem_once(kern, S::total, attr_done);
   if (e != cudaSuccess) return e;
   dim3 grid(lay.H, lay.B);
-  kern<<<grid, 128, S::total, st>>>(static_cast<const T*>(d_o), dsT, ds0, lay, flags, ws);
+  kern<<<grid, 544, S::total, st>>>(static_cast<const T*>(d_o), dsT, ds0, lay, flags, ws);
   return cudaGetLastError();
 }
-
-// ------------------------------------------------------------------------------------------------------------------
-// per-chunk gradients (in gd_bwd_chunk.cu)
 
 #define INST(T)                                                                                                    \
   template cudaError_t launch_bwd_state<T, 128, 128>(const void*, const float*, float*, const Layout&, int,         \

@@ -1,12 +1,14 @@
 // Per-chunk gradients of the chunked gated delta rule on B200 (sm_100a): one CTA of 256 threads per (chunk, key head,
 // batch row), all CTAs independent, one writer per gradient element (no atomics; bitwise reproducible).
 //
-// Inputs per value head (from the workspace): the q / k images and G (prep), A = (I + L)^-1 (prep, fp32), the state
-// entering the chunk S_c and Vn (the forward state pass with GD_STORE_STATES), dS_{c+1} and dVn (the reverse pass);
-// from the caller: v, beta, dO and, for the l2 prologue's backward, q and k.
+// Inputs per value head, all bf16 images from the workspace copied whole by the bulk-copy engine: the q / k images,
+// A = (I + L)^-1 and V (prep), S_c^T and Vn^T (the forward state pass with GD_STORE_STATES), dS_{c+1}^T, dVn^T and dO
+// (the reverse pass); G, M and K K^T in fp32 (prep), the partial sums of <S_c, dS_{c+1}> (reverse pass); from the
+// caller: v, beta and, for the l2 prologue's backward, q and k.
 //
 // Products, all tcgen05 from blocked shared-memory tiles into TMEM (transposed "[D x 64]" accumulators put the head
-// dimension on TMEM lanes; C x C ones use M = 64):
+// dimension on TMEM lanes; C x C ones use M = 64; an image with rows along a product's K dimension is its MN-major
+// operand):
 //   group 1:  dO Vn^T, (dO S_c^T)^T, (dVn S_c^T)^T, (A^T dVn)^T, dVn V^T
 //   group 2:  (Vn dS^T)^T                      (Vn and dS split: three products)
 //   group 3:  (dM K)^T, (dM^T Q)^T, (A^T dW)^T, dW K^T      (dM, q and k split: three products each)
@@ -29,20 +31,20 @@ struct ChunkSmem {
   static constexpr size_t qkl = qk + 2 * 64 * DK * 2;    // [128 x DK]: their low halves
   static constexpr size_t a = qkl + 2 * 64 * DK * 2;     // [64 x 64] A
   static constexpr size_t big = a + 64 * 64 * 2;         // 64 KB, reused by phase (see the kernel)
-  static constexpr size_t sc = big;                      //   phase 1: [DK x DV] S_c
+  static constexpr size_t sc = big;                      //   phase 1: [DV x DK] S_c^T
   static constexpr size_t dO = big + DK * DV * 2;        //            [64 x DV] dO
   static constexpr size_t v = dO + 64 * DV * 2;          //            [64 x DV] V
-  static constexpr size_t dsh = big;                     //   phase 2: [DK x DV] dS hi
-  static constexpr size_t dsl = big + DK * DV * 2;       //            [DK x DV] dS lo
+  static constexpr size_t dsh = big;                     //   phase 2: [DV x DK] dS^T hi
+  static constexpr size_t dsl = big + DK * DV * 2;       //            [DV x DK] dS^T lo
   static constexpr size_t da = big;                      //   phase 3: [64 x 64] dA
   static constexpr size_t t1 = big + 8192;               //            [64 x 64] T1
   static constexpr size_t z = big + 16384;               //            [64 x 64] Z
-  static constexpr size_t vn = big + 65536;              // 32 KB: [64 x DV] Vn hi, lo; later fp32 [64][64] P_beta, R
-  static constexpr size_t vnl = vn + 64 * DV * 2;
+  static constexpr size_t vn = big + 65536;              // 32 KB: [DV x 64] Vn^T hi, lo; later fp32 [64][64] P_beta, R
+  static constexpr size_t vnl = vn + DV * 64 * 2;
   static constexpr size_t pb = vn;                       //   fp32 [64][64] P_beta (swizzled)
   static constexpr size_t r = vn + 16384;                //   fp32 [64][64] R (swizzled)
-  static constexpr size_t dvn = vn + 32768;              // 32 KB: [64 x DV] dVn hi, lo; later dM hi, lo and dW^T
-  static constexpr size_t dvnl = dvn + 64 * DV * 2;
+  static constexpr size_t dvn = vn + 32768;              // 32 KB: [DV x 64] dVn^T hi, lo; later dM hi, lo and dW^T
+  static constexpr size_t dvnl = dvn + DV * 64 * 2;
   static constexpr size_t dmh = dvn;                     //   [64 x 64] dM hi
   static constexpr size_t dml = dvn + 8192;              //   [64 x 64] dM lo
   static constexpr size_t dwt = dvn + 16384;             //   [DK x 64] dW^T
@@ -51,9 +53,9 @@ struct ChunkSmem {
   static constexpr size_t beta = g + 256;                // [64]
   static constexpr size_t part = beta + 256;             // [5][4][64] quadrant partial dots: a, kX, vY, E, xq/xk
   static constexpr size_t pk = part + 5 * 4 * 64 * 4;    // [2][64] row halves of sum_j P_ij KG_ij
-  static constexpr size_t red = pk + 2 * 64 * 4;         // [8] block reduction
-  static constexpr size_t bar = red + 64;                // 3 mbarriers: mma, q/k image, group 2
-  static constexpr size_t tmem = bar + 24;
+  static constexpr size_t red = pk + 2 * 64 * 4;         // [16] partial sums of <S_c, dS_{c+1}>
+  static constexpr size_t bar = red + 64;                // 5 mbarriers: mma, q/k images, group 2, phase-1 and dS images
+  static constexpr size_t tmem = bar + 40;
   static constexpr size_t total = tmem + 16;
 };
 
@@ -87,6 +89,8 @@ __global__ void __launch_bounds__(256) bwd_chunk_kernel(const T* __restrict__ qr
   uint64_t* bar_mma = reinterpret_cast<uint64_t*>(smem + S::bar);
   uint64_t* bar_qk = bar_mma + 1;
   uint64_t* bar_g2 = bar_mma + 2;  // group 2 completes on its own barrier: its wait follows group 3's commit
+  uint64_t* bar_in = bar_mma + 3;  // phase-1 images of one value head
+  uint64_t* bar_ds = bar_mma + 4;  // dS images of one value head
   uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + S::tmem);
   const bool norm = (flags & GD_L2NORM) != 0;
   const float qscale = (flags & GD_SCALE_Q) ? rsqrtf((float)DK) : 1.f;
@@ -99,6 +103,8 @@ __global__ void __launch_bounds__(256) bwd_chunk_kernel(const T* __restrict__ qr
     mbar_init(bar_mma, 1);
     mbar_init(bar_qk, 1);
     mbar_init(bar_g2, 1);
+    mbar_init(bar_in, 1);
+    mbar_init(bar_ds, 1);
     fence_mbar_init();
   }
   __syncthreads();
@@ -138,78 +144,71 @@ __global__ void __launch_bounds__(256) bwd_chunk_kernel(const T* __restrict__ qr
   for (int j = 0; j < 32; ++j) dQacc[j] = dKacc[j] = 0.f;
 
   uint32_t ph = 0;
+  GD_TRACE_AT(ws, lay, 0);
   bool ok = mbar_wait(bar_qk, 0, err, 40);
   block_sync_ok(ok);
 
   for (int r = 0; r < lay.rep && ok; ++r) {
     const int h = hk * lay.rep + r;
     const size_t cidx = ((size_t)b * lay.H + h) * lay.NT + c;
-    // ---------------- phase 1: operand tiles
+    // ---------------- phase 1: operand images (bulk copies; the previous value head's readers are done)
+    if (tid == 0) {
+      const uint32_t bytes = (uint32_t)(lay.m_bytes() + lay.si_bytes() + 2 * lay.vi_bytes() + 2 * lay.vn_bytes());
+      mbar_arrive_expect_tx(bar_in, bytes);
+      bulk_g2s(smem + S::a, ws + lay.ai + cidx * lay.m_bytes(), (uint32_t)lay.m_bytes(), bar_in);
+      bulk_g2s(smem + S::sc, ws + lay.sci + cidx * lay.si_bytes(), (uint32_t)lay.si_bytes(), bar_in);
+      bulk_g2s(smem + S::dO, ws + lay.doi + cidx * lay.vi_bytes(), (uint32_t)lay.vi_bytes(), bar_in);
+      bulk_g2s(smem + S::v, ws + lay.vi + cidx * lay.vi_bytes(), (uint32_t)lay.vi_bytes(), bar_in);
+      bulk_g2s(smem + S::vn, ws + lay.vni + cidx * lay.vn_bytes(), (uint32_t)lay.vn_bytes(), bar_in);
+      bulk_g2s(smem + S::dvn, ws + lay.dvni + cidx * lay.vn_bytes(), (uint32_t)lay.vn_bytes(), bar_in);
+    }
     if (tid < 64) {
       sG[tid] = reinterpret_cast<const float*>(ws + lay.gc + cidx * lay.gc_bytes())[tid];
       const int t = t0 + tid;
       sB[tid] = (t < lay.T) ? beta[((size_t)b * lay.T + t) * lay.H + h] : 0.f;
     }
-    f32_to_tiles<64, 64, 256>(reinterpret_cast<const float*>(ws + lay.ainv + cidx * lay.ainv_bytes()), smem + S::a,
-                              nullptr);
-    f32_to_tiles<DK, DV, 256>(reinterpret_cast<const float*>(ws + lay.sc + cidx * lay.s_bytes()), smem + S::sc,
-                              nullptr);
-    f32_to_tiles<64, DV, 256>(reinterpret_cast<const float*>(ws + lay.vn + cidx * lay.u_bytes()), smem + S::vn,
-                              smem + S::vnl);
-    f32_to_tiles<64, DV, 256>(reinterpret_cast<const float*>(ws + lay.dvn + cidx * lay.u_bytes()), smem + S::dvn,
-                              smem + S::dvnl);
-    load_rows<T, DV, 8>(d_o, b, t0, lay.T, lay.H, h, false, 1.f, smem + S::dO, nullptr);
-    load_rows<T, DV, 8>(vraw, b, t0, lay.T, lay.H, h, false, 1.f, smem + S::v, nullptr);
-    fence_async_smem();
-    tc_fence_before();
-    __syncthreads();
+    if (tid < 16) sRed[tid] = reinterpret_cast<const float*>(ws + lay.sl + cidx * 64)[tid];
+    ok = mbar_wait(bar_in, r & 1, err, 47);
+    block_sync_ok(ok);
+    if (!ok) break;
     if (tid == 0) {
       tc_fence_after();
-      const Tile tSc{smem_u32(smem + S::sc), DV}, tDO{smem_u32(smem + S::dO), DV}, tV{smem_u32(smem + S::v), DV};
-      const Tile tVn{smem_u32(smem + S::vn), DV}, tDVh{smem_u32(smem + S::dvn), DV}, tDVl{smem_u32(smem + S::dvnl), DV};
-      mma_tiles(T_DM, 64, 64, DV, tDO, true, 0, 0, tVn, false, 0, false);         // dO Vn^T
-      mma_tiles(T_DQA, DK, 64, DV, tSc, true, 0, 0, tDO, false, 0, false);        // S_c dO^T
-      mma_tiles(T_DW, DK, 64, DV, tSc, true, 0, 0, tDVh, false, 0, false);        // S_c dVn^T
-      mma_tiles(T_Y, DV, 64, 64, tDVh, false, 0, 0, tA, true, 0, false);          // dVn^T A (dVn split)
-      mma_tiles(T_Y, DV, 64, 64, tDVl, false, 0, 0, tA, true, 0, true);
-      mma_tiles(T_DAV, 64, 64, DV, tDVh, true, 0, 0, tV, false, 0, false);        // dVn V^T
+      const Tile tSc{smem_u32(smem + S::sc), DK}, tDO{smem_u32(smem + S::dO), DV}, tV{smem_u32(smem + S::v), DV};
+      const Tile tVn{smem_u32(smem + S::vn), 64}, tDVh{smem_u32(smem + S::dvn), 64}, tDVl{smem_u32(smem + S::dvnl), 64};
+      mma_tiles(T_DM, 64, 64, DV, tDO, true, 0, 0, tVn, true, 0, false);          // dO Vn^T
+      mma_tiles(T_DQA, DK, 64, DV, tSc, false, 0, 0, tDO, false, 0, false);       // S_c dO^T
+      mma_tiles(T_DW, DK, 64, DV, tSc, false, 0, 0, tDVh, true, 0, false);        // S_c dVn^T
+      mma_tiles(T_Y, DV, 64, 64, tDVh, true, 0, 0, tA, true, 0, false);           // dVn^T A (dVn split)
+      mma_tiles(T_Y, DV, 64, 64, tDVl, true, 0, 0, tA, true, 0, true);
+      mma_tiles(T_DAV, 64, 64, DV, tDVh, false, 0, 0, tV, false, 0, false);       // dVn V^T
       mma_commit(bar_mma);
     }
-    // gamma_last <S_c, dS_{c+1}> while the tensor core works (fp32 sources)
-    float sdot = 0.f;
-    {
-      const float4* s4 = reinterpret_cast<const float4*>(ws + lay.sc + cidx * lay.s_bytes());
-      const float4* d4 = reinterpret_cast<const float4*>(ws + lay.dsn + cidx * lay.s_bytes());
-#pragma unroll 8
-      for (int i = tid; i < DK * DV / 4; i += 256) {
-        const float4 x = __ldg(s4 + i), y = __ldg(d4 + i);
-        sdot = fmaf(x.x, y.x, fmaf(x.y, y.y, fmaf(x.z, y.z, fmaf(x.w, y.w, sdot))));
-      }
-      sdot = warp_sum(sdot);
-      if (lane == 0) sRed[warp] = sdot;
-    }
+    GD_TRACE_AT(ws, lay, 2);
     ok = mbar_wait(bar_mma, ph, err, 41);
     ph ^= 1;
     block_sync_ok(ok);
     if (!ok) break;
     tc_fence_after();
-    // ---------------- phase 2: dS tiles (over S_c / dO / V), then (Vn dS^T)^T
-    f32_to_tiles<DK, DV, 256>(reinterpret_cast<const float*>(ws + lay.dsn + cidx * lay.s_bytes()), smem + S::dsh,
-                              smem + S::dsl);
-    fence_async_smem();
-    tc_fence_before();
-    __syncthreads();
+    GD_TRACE_AT(ws, lay, 3);
+    // ---------------- phase 2: dS^T images (over S_c / dO / V, whose readers are done), then (Vn dS^T)^T
     if (tid == 0) {
-      tc_fence_after();
-      const Tile tDh{smem_u32(smem + S::dsh), DV}, tDl{smem_u32(smem + S::dsl), DV};
-      const Tile tVh{smem_u32(smem + S::vn), DV}, tVl{smem_u32(smem + S::vnl), DV};
-      mma_tiles(T_DKS, DK, 64, DV, tDh, true, 0, 0, tVh, false, 0, false);
-      mma_tiles(T_DKS, DK, 64, DV, tDh, true, 0, 0, tVl, false, 0, true);
-      mma_tiles(T_DKS, DK, 64, DV, tDl, true, 0, 0, tVh, false, 0, true);
-      mma_commit(bar_g2);
+      mbar_arrive_expect_tx(bar_ds, 2 * (uint32_t)lay.si_bytes());
+      bulk_g2s(smem + S::dsh, ws + lay.dsi + cidx * 2 * lay.si_bytes(), 2 * (uint32_t)lay.si_bytes(), bar_ds);
+      if (mbar_wait(bar_ds, r & 1, err, 48)) {
+        const Tile tDh{smem_u32(smem + S::dsh), DK}, tDl{smem_u32(smem + S::dsl), DK};
+        const Tile tVh{smem_u32(smem + S::vn), 64}, tVl{smem_u32(smem + S::vnl), 64};
+        mma_tiles(T_DKS, DK, 64, DV, tDh, false, 0, 0, tVh, true, 0, false);
+        mma_tiles(T_DKS, DK, 64, DV, tDh, false, 0, 0, tVl, true, 0, true);
+        mma_tiles(T_DKS, DK, 64, DV, tDl, false, 0, 0, tVh, true, 0, true);
+      }
+      mma_commit(bar_g2);  // completes after a failed wait too; the error word is already set
     }
+    GD_TRACE_AT(ws, lay, 4);
     // epilogue of group 1 while group 2 runs
-    const float s_last = __expf(sG[63]) * (sRed[0] + sRed[1] + sRed[2] + sRed[3] + sRed[4] + sRed[5] + sRed[6] + sRed[7]);
+    float s_last = 0.f;
+#pragma unroll
+    for (int w = 0; w < 16; ++w) s_last += sRed[w];
+    s_last *= __expf(sG[63]);
     {
       float acc[32];
       // dW^T tile (rows dk, cols tokens), dW = -(S_c dVn^T)^T
@@ -274,12 +273,14 @@ __global__ void __launch_bounds__(256) bwd_chunk_kernel(const T* __restrict__ qr
       mma_tiles(T_DAK, 64, 64, DK, tDW, false, 0, 0, tK, false, 0, false);      // dW K^T
       mma_commit(bar_mma);
     }
+    GD_TRACE_AT(ws, lay, 5);
     ok = mbar_wait(bar_g2, r & 1, err, 42);  // group 2 (one phase per value head)
     if (ok) ok = mbar_wait(bar_mma, ph, err, 43);  // group 3
     ph ^= 1;
     block_sync_ok(ok);
     if (!ok) break;
     tc_fence_after();
+    GD_TRACE_AT(ws, lay, 6);
     // ---------------- phase 3: E, k.X partials; dA
     {
       float acc[32], kx[32];
@@ -299,7 +300,7 @@ __global__ void __launch_bounds__(256) bwd_chunk_kernel(const T* __restrict__ qr
       tmem_ld32(tmem_lane_addr(T_DM, warp, tok0), acc);
       if (rowthr) {
         const int i = rrow;
-        const float* mrow = reinterpret_cast<const float*>(ws + lay.mf + cidx * lay.ainv_bytes()) + i * 64 + tok0;
+        const float* mrow = reinterpret_cast<const float*>(ws + lay.mf + cidx * lay.cc_bytes()) + i * 64 + tok0;
 #pragma unroll
         for (int jj = 0; jj < 32; ++jj) {
           const int j = tok0 + jj;
@@ -330,6 +331,7 @@ __global__ void __launch_bounds__(256) bwd_chunk_kernel(const T* __restrict__ qr
       mma_tiles(T_T1, 64, 64, 64, Tile{smem_u32(smem + S::da), 64}, true, 0, 0, tA, false, 0, false);  // dA A^T
       mma_commit(bar_mma);
     }
+    GD_TRACE_AT(ws, lay, 7);
     ok = mbar_wait(bar_mma, ph, err, 44);
     ph ^= 1;
     block_sync_ok(ok);
@@ -351,6 +353,7 @@ __global__ void __launch_bounds__(256) bwd_chunk_kernel(const T* __restrict__ qr
       mma_tiles(T_DL, 64, 64, 64, tA, false, 0, 0, Tile{smem_u32(smem + S::t1), 64}, true, 0, false);  // A^T T1
       mma_commit(bar_mma);
     }
+    GD_TRACE_AT(ws, lay, 8);
     ok = mbar_wait(bar_mma, ph, err, 45);
     ph ^= 1;
     block_sync_ok(ok);
@@ -364,7 +367,7 @@ __global__ void __launch_bounds__(256) bwd_chunk_kernel(const T* __restrict__ qr
       if (rowthr) {
         const int i = rrow;
         const float Gi = sG[i], bi = sB[i];
-        const float* kgrow = reinterpret_cast<const float*>(ws + lay.kg + cidx * lay.ainv_bytes()) + i * 64 + tok0;
+        const float* kgrow = reinterpret_cast<const float*>(ws + lay.kg + cidx * lay.cc_bytes()) + i * 64 + tok0;
         float pk = 0.f;
 #pragma unroll
         for (int jj = 0; jj < 32; ++jj) {
@@ -409,6 +412,7 @@ __global__ void __launch_bounds__(256) bwd_chunk_kernel(const T* __restrict__ qr
       mma_tiles(T_DKC, DK, 64, 64, tK, false, 0, 0, Tile{smem_u32(smem + S::z), 64}, false, 0, false);  // K^T Z^T
       mma_commit(bar_mma);
     }
+    GD_TRACE_AT(ws, lay, 9);
     // rect_t = sum_{i >= t} sum_{j < t} R_ij while the tensor core works: row prefixes in place, then column suffixes
     if (tid < 64) {
       const int i = tid;
@@ -425,6 +429,7 @@ __global__ void __launch_bounds__(256) bwd_chunk_kernel(const T* __restrict__ qr
     block_sync_ok(ok);
     if (!ok) break;
     tc_fence_after();
+    GD_TRACE_AT(ws, lay, 10);
     // ---------------- phase 4: dQ, dK of this value head; dg and dbeta
     {
       float a[32], bq[32];

@@ -33,6 +33,20 @@ struct ErrorWord {
   int pad[13];
 };
 
+// Phase tracing for builds with -DGD_TRACE (profiling only; a normal build compiles it away): thread 0 of each
+// 128-thread group of CTA (0, 0, 0) stores clock64() into the trace area of the workspace at (group, slot).
+#ifdef GD_TRACE
+#define GD_TRACE_AT(ws, lay, slot)                                                                        \
+  do {                                                                                                    \
+    if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && (threadIdx.x & 127) == 0 && (slot) < 4096) \
+      reinterpret_cast<long long*>((ws) + (lay).trace)[(threadIdx.x >> 7) * 4096 + (slot)] = clock64();   \
+  } while (0)
+#else
+#define GD_TRACE_AT(ws, lay, slot) \
+  do {                             \
+  } while (0)
+#endif
+
 __device__ __forceinline__ void report(ErrorWord* err, int code, int where) {
   if (err != nullptr && atomicCAS(&err->code, 0, code) == 0) {
     err->where = where;
@@ -96,6 +110,16 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, ErrorW
     }
   }
   return true;
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// One arrival per warp after the whole warp got here (lane 0 arrives; the barrier counts warps).
+__device__ __forceinline__ void mbar_arrive_warp(uint64_t* bar) {
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) mbar_arrive(bar);
 }
 
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
@@ -232,7 +256,21 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// TMEM address of column `col` in the lane quadrant of this warp (warps w and w+4 share a quadrant).
+// TMEM -> registers: this warp's 32 lanes, 16 consecutive fp32 columns each.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// TMEM address of column `col` in the lane quadrant of this warp (warps w, w+4, w+8, ... share a quadrant).
 __device__ __forceinline__ uint32_t tmem_lane_addr(uint32_t base, int warp, int col) {
   return base + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)col;
 }
@@ -467,6 +505,30 @@ __device__ __forceinline__ float warp_reduce_scatter32(float (&v)[32]) {
     }
   }
   return v[0];
+}
+
+// Reduce-scatter of 16 values across a warp whose two half-warps hold different partial terms of the same 16 sums:
+// returns, in lane l, the sum over all 32 lanes of v[l & 15] (31 shuffles).
+__device__ __forceinline__ float warp_reduce_scatter16(float (&v)[16]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int k = 0; k < 16; ++k) v[k] += __shfl_xor_sync(0xffffffffu, v[k], 16);
+#pragma unroll
+  for (int s = 8; s >= 1; s >>= 1) {
+    const bool upper = (lane & s) != 0;
+#pragma unroll
+    for (int k = 0; k < s; ++k) {
+      const float send = upper ? v[k] : v[k + s];
+      const float keep = upper ? v[k + s] : v[k];
+      v[k] = keep + __shfl_xor_sync(0xffffffffu, send, s);
+    }
+  }
+  return v[0];
+}
+
+// bf16 element (r, c) of a blocked tile, as float
+__device__ __forceinline__ float tile_at(const unsigned char* tile, int r, int c, int cols) {
+  return __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(tile + blk_off(r, c, cols)));
 }
 
 // [64][64] fp32 C x C scratch, columns XOR-swizzled by row so that both row-wise and column-wise thread patterns are

@@ -113,6 +113,7 @@ __global__ void __launch_bounds__(128) prep_kernel(const T* __restrict__ q, cons
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + S::bar);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + S::tmem);
 
+  GD_TRACE_AT(ws, lay, 0);
   if (warp == 0) {
     tmem_alloc(tslot, 256);
     tmem_relinquish();
@@ -131,6 +132,7 @@ __global__ void __launch_bounds__(128) prep_kernel(const T* __restrict__ q, cons
   load_rows<T, DK>(q, b, t0, lay.T, lay.HK, hk, norm, qscale, smem + S::q, rq, smem + S::ql);
   load_rows<T, DK>(k, b, t0, lay.T, lay.HK, hk, norm, 1.f, smem + S::k, rk, smem + S::kl);
   load_rows<T, DV>(v, b, t0, lay.T, lay.H, h, false, 1.f, smem + S::v, nullptr);
+  GD_TRACE_AT(ws, lay, 1);
 
   // cumulative log decay (padding rows: g = 0, beta = 0, which leaves G constant past the last token)
   if (tid < 64) {
@@ -167,12 +169,37 @@ __global__ void __launch_bounds__(128) prep_kernel(const T* __restrict__ q, cons
     mma_commit(bar);
   }
   __syncthreads();  // sG complete for everyone
+  GD_TRACE_AT(ws, lay, 2);
   {  // the low halves go out before L and A overwrite them
     const uint4* src = reinterpret_cast<const uint4*>(smem + S::ql);
     uint4* dst = reinterpret_cast<uint4*>(ws + lay.qkl + cidx * lay.qk_bytes());
     for (int idx = tid; idx < (int)(lay.qk_bytes() / 16); idx += 128) dst[idx] = src[idx];
   }
+  {  // K~ = diag(e) K (e_i = exp(G_last - G_i) <= 1) from k's hi + lo, split again: the state update's operand
+    unsigned char* kth = ws + lay.kt + cidx * lay.qk_bytes();
+    unsigned char* ktl = kth + 64 * DK * 2;
+    const float Glast = sG[63];
+    for (int idx = tid; idx < 64 * DK / 8; idx += 128) {
+      const int rl = idx & 7, cb = (idx >> 3) % (DK / 8), rb = idx / (8 * (DK / 8));
+      const int r = 8 * rb + rl;
+      const uint4 uh = *reinterpret_cast<const uint4*>(smem + S::k + blk_off(r, 8 * cb, DK));
+      const uint4 ul = *reinterpret_cast<const uint4*>(smem + S::kl + blk_off(r, 8 * cb, DK));
+      const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&uh);
+      const __nv_bfloat162* l2 = reinterpret_cast<const __nv_bfloat162*>(&ul);
+      const float er = __expf(Glast - sG[r]);
+      float x[8];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 fh = __bfloat1622float2(h2[e]), fl = __bfloat1622float2(l2[e]);
+        x[2 * e] = er * (fh.x + fl.x);
+        x[2 * e + 1] = er * (fh.y + fl.y);
+      }
+      store8_split(kth, ktl, r, 8 * cb, DK, x);
+    }
+  }
+  GD_TRACE_AT(ws, lay, 3);
   bool ok = mbar_wait(bar, 0, err, 10);
+  GD_TRACE_AT(ws, lay, 4);
   ok = __syncthreads_and(ok);
   tc_fence_after();
   if (ok) {
@@ -180,8 +207,8 @@ __global__ void __launch_bounds__(128) prep_kernel(const T* __restrict__ q, cons
     const float Gi = sG[i];
     float acc[32];
     unsigned char* mimg = ws + lay.m + cidx * lay.m_bytes();
-    float* mf = lay.backward() ? reinterpret_cast<float*>(ws + lay.mf + cidx * lay.ainv_bytes()) + i * 64 : nullptr;
-    float* kgf = lay.backward() ? reinterpret_cast<float*>(ws + lay.kg + cidx * lay.ainv_bytes()) + i * 64 : nullptr;
+    float* mf = lay.backward() ? reinterpret_cast<float*>(ws + lay.mf + cidx * lay.cc_bytes()) + i * 64 : nullptr;
+    float* kgf = lay.backward() ? reinterpret_cast<float*>(ws + lay.kg + cidx * lay.cc_bytes()) + i * 64 : nullptr;
 #pragma unroll 1
     for (int half = 0; half < 2; ++half) {
       tmem_ld32(tmem_lane_addr(tm, warp, 32 * half), acc);
@@ -213,30 +240,57 @@ __global__ void __launch_bounds__(128) prep_kernel(const T* __restrict__ q, cons
     }
   }
   __syncthreads();
+  GD_TRACE_AT(ws, lay, 5);
   if (ok) unit_lower_inverse(sL, sAi, reinterpret_cast<float*>(smem + S::T3));
+  GD_TRACE_AT(ws, lay, 6);
 
   if (ok) {
     // A diag(beta gamma) and the hi/lo split of A diag(beta) as K-major B operands (rows i, cols j)
     const int i = tid >> 1, j0 = 32 * (tid & 1);
+    unsigned char* aimg = lay.backward() ? ws + lay.ai + cidx * lay.m_bytes() : nullptr;
 #pragma unroll 1
     for (int q8 = 0; q8 < 4; ++q8) {
-      float a1[8], a2[8];
+      float a0[8], a1[8], a2[8];
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
         const int j = j0 + 8 * q8 + e;
-        const float a = sAi[i * 65 + j];
-        a1[e] = a * sB[j] * __expf(sG[j]);
-        a2[e] = a * sB[j];
+        a0[e] = sAi[i * 65 + j];
+        a1[e] = a0[e] * sB[j] * __expf(sG[j]);
+        a2[e] = a0[e] * sB[j];
       }
       store8_bf16(smem + S::a1, i, j0 + 8 * q8, 64, a1);
       store8_split(smem + S::a2h, smem + S::a2l, i, j0 + 8 * q8, 64, a2);
+      if (aimg != nullptr) store8_bf16(aimg, i, j0 + 8 * q8, 64, a0);  // the backward's A image
     }
     if (lay.backward()) {
-      float* ainv = reinterpret_cast<float*>(ws + lay.ainv + cidx * lay.ainv_bytes());
-      for (int idx = tid; idx < 64 * 64; idx += 128) ainv[idx] = sAi[(idx >> 6) * 65 + (idx & 63)];
+      // the backward's V image and diag(gamma) Q (hi + lo, from q's two halves)
+      const uint4* vs = reinterpret_cast<const uint4*>(smem + S::v);
+      uint4* vd = reinterpret_cast<uint4*>(ws + lay.vi + cidx * lay.vi_bytes());
+      for (int idx = tid; idx < (int)(lay.vi_bytes() / 16); idx += 128) vd[idx] = vs[idx];
+      unsigned char* gqh = ws + lay.gq + cidx * lay.qk_bytes();
+      unsigned char* gql = gqh + 64 * DK * 2;
+      const unsigned char* qlo = ws + lay.qkl + cidx * lay.qk_bytes();  // written above by this CTA
+      for (int idx = tid; idx < 64 * DK / 8; idx += 128) {
+        const int rl = idx & 7, cb = (idx >> 3) % (DK / 8), rb = idx / (8 * (DK / 8));
+        const int r = 8 * rb + rl;
+        const uint4 uh = *reinterpret_cast<const uint4*>(smem + S::q + blk_off(r, 8 * cb, DK));
+        const uint4 ul = *reinterpret_cast<const uint4*>(qlo + blk_off(r, 8 * cb, DK));
+        const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&uh);
+        const __nv_bfloat162* l2 = reinterpret_cast<const __nv_bfloat162*>(&ul);
+        const float gr = __expf(sG[r]);
+        float x[8];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 fh = __bfloat1622float2(h2[e]), fl = __bfloat1622float2(l2[e]);
+          x[2 * e] = gr * (fh.x + fl.x);
+          x[2 * e + 1] = gr * (fh.y + fl.y);
+        }
+        store8_split(gqh, gql, r, 8 * cb, DK, x);
+      }
     }
   }
   fence_async_smem();
+  GD_TRACE_AT(ws, lay, 7);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -258,6 +312,7 @@ __global__ void __launch_bounds__(128) prep_kernel(const T* __restrict__ q, cons
     if (tid < 64) reinterpret_cast<float*>(ws + lay.gc + cidx * lay.gc_bytes())[tid] = sG[tid];
   }
   if (ok) ok = mbar_wait(bar, 1, err, 11);
+  GD_TRACE_AT(ws, lay, 8);
   ok = __syncthreads_and(ok);
   tc_fence_after();
   if (ok) {
@@ -283,6 +338,7 @@ __global__ void __launch_bounds__(128) prep_kernel(const T* __restrict__ q, cons
       }
     }
   }
+  GD_TRACE_AT(ws, lay, 9);
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
@@ -292,204 +348,253 @@ __global__ void __launch_bounds__(128) prep_kernel(const T* __restrict__ q, cons
 }
 
 // ------------------------------------------------------------------------------------------------------------------
-// forward state pass
+// forward state pass (warp-specialised)
+//
+// One CTA per (value head, batch row): 16 epilogue warps + 1 MMA warp. Epilogue warp w reads TMEM lane quadrant w % 4
+// (value columns 32 (w % 4) .. +31, one per lane) and one quarter of each accumulator's columns: tokens
+// 16 (w / 4) .. +15 of the [DV x 64] products, key rows 32 (w / 4) .. +31 of the [DV x DK] state update; it holds the
+// fp32 state S[32 (w / 4) + j][v] in registers. One thread of warp 16 issues every MMA and bulk copy. Hand-offs are
+// mbarriers only: an MMA issue blocks its thread until the tensor pipe takes it, so the MMA thread never joins a
+// barrier with the epilogue warps (that would serialise MMA time with epilogue time). Per chunk c:
+//   MMA: wait stage c and the S tile -> (W S)^T -> ws_full; (Q S)^T -> qs_full[c & 1]
+//   EPI: wait ws_full -> Vn = U - W S (U prefetched into registers) -> Vn^T hi / lo tiles -> vn_full
+//   MMA: wait vn_full -> (K~^T Vn)^T, three products (K~ = diag(e) K and Vn split) -> ds_full (the commit also covers
+//        (Q S)^T, the last reader of the S tile); (M Vn)^T -> mv_full; stage_free[c & 1]
+//   EPI: wait ds_full -> S <- exp(G_last) S + K~^T Vn -> S tile -> st_full
+//   EPI: wait qs_full, mv_full -> O = diag(gamma) Q S + M Vn -> global
+//   MMA: wait stage_free[c & 1] -> refill the stage with chunk c + 2 (bulk copies, two stages in flight)
+// With GD_STORE_STATES (the backward's recompute) O is not formed; the pass keeps S_c^T (fp32 and a bf16 image) and
+// the Vn^T hi / lo images of every chunk for the backward kernels.
 
 template <int DK, int DV>
 struct StateSmem {
-  static constexpr size_t st = 0;                        // [DV x DK] bf16 blocked, S^T (rows v, cols dk)
-  static constexpr size_t vh = st + DV * DK * 2;         // [DV x 64] Vn^T hi
-  static constexpr size_t vl = vh + DV * 64 * 2;         //            lo
-  static constexpr size_t eh = vl + DV * 64 * 2;         // [DV x 64] (e Vn)^T hi
-  static constexpr size_t el = eh + DV * 64 * 2;         //               lo
-  static constexpr size_t qk = el + DV * 64 * 2;         // stage: [2][64 x DK] q, k images
-  static constexpr size_t kl = qk + 2 * 64 * DK * 2;     // stage: [64 x DK] low half of the k image
-  static constexpr size_t wt = kl + 64 * DK * 2;         // stage: [DK x 64] W^T image
-  static constexpr size_t m = wt + DK * 64 * 2;          // stage: [64 x 64] M image
-  static constexpr size_t g = m + 64 * 64 * 2;           // stage: [64] G
-  static constexpr size_t u = g + 64 * 4;                // [64][DV] fp32 U
-  static constexpr size_t bar = u + 64 * DV * 4;         // 3 mbarriers: mma, inputs, U
-  static constexpr size_t tmem = bar + 3 * 8;
+  static constexpr size_t st = 0;                          // [DV x DK] bf16 S^T (rows v, cols dk)
+  static constexpr size_t vh = st + DV * DK * 2;           // [DV x 64] Vn^T hi
+  static constexpr size_t vl = vh + DV * 64 * 2;           //            lo
+  static constexpr size_t stage0 = vl + DV * 64 * 2;       // two input stages, each:
+  static constexpr size_t s_wt = 0;                        //   [DK x 64] W^T image
+  static constexpr size_t s_q = s_wt + DK * 64 * 2;        //   [64 x DK] q image (hi)
+  static constexpr size_t s_kt = s_q + 64 * DK * 2;        //   [2][64 x DK] K~ hi, lo
+  static constexpr size_t s_m = s_kt + 2 * 64 * DK * 2;    //   [64 x 64] M image
+  static constexpr size_t s_g = s_m + 64 * 64 * 2;         //   [64] G
+  static constexpr size_t stage_bytes = s_g + 64 * 4;
+  static constexpr size_t bar = stage0 + 2 * stage_bytes;
+  static constexpr int NBAR = 13;
+  static constexpr size_t tmem = bar + NBAR * 8;
   static constexpr size_t total = tmem + 8;
-  static constexpr uint32_t stage_bytes = 3 * 64 * DK * 2 + DK * 64 * 2 + 64 * 64 * 2 + 64 * 4;
 };
 
 template <int DK, int DV>
-__device__ __forceinline__ void issue_stage(unsigned char* smem, const unsigned char* ws, const Layout& lay,
+__device__ __forceinline__ void issue_stage(unsigned char* stg, const unsigned char* ws, const Layout& lay,
                                             size_t cidx, uint64_t* bar) {
   using S = StateSmem<DK, DV>;
-  mbar_arrive_expect_tx(bar, S::stage_bytes);
-  bulk_g2s(smem + S::qk, ws + lay.qk + cidx * lay.qk_bytes(), (uint32_t)lay.qk_bytes(), bar);
-  bulk_g2s(smem + S::kl, ws + lay.qkl + cidx * lay.qk_bytes() + 64 * DK * 2, 64 * DK * 2, bar);
-  bulk_g2s(smem + S::wt, ws + lay.wt + cidx * lay.wt_bytes(), (uint32_t)lay.wt_bytes(), bar);
-  bulk_g2s(smem + S::m, ws + lay.m + cidx * lay.m_bytes(), (uint32_t)lay.m_bytes(), bar);
-  bulk_g2s(smem + S::g, ws + lay.gc + cidx * lay.gc_bytes(), (uint32_t)lay.gc_bytes(), bar);
+  mbar_arrive_expect_tx(bar, (uint32_t)S::stage_bytes);
+  bulk_g2s(stg + S::s_wt, ws + lay.wt + cidx * lay.wt_bytes(), (uint32_t)lay.wt_bytes(), bar);
+  bulk_g2s(stg + S::s_q, ws + lay.qk + cidx * lay.qk_bytes(), 64 * DK * 2, bar);
+  bulk_g2s(stg + S::s_kt, ws + lay.kt + cidx * lay.qk_bytes(), (uint32_t)lay.qk_bytes(), bar);
+  bulk_g2s(stg + S::s_m, ws + lay.m + cidx * lay.m_bytes(), (uint32_t)lay.m_bytes(), bar);
+  bulk_g2s(stg + S::s_g, ws + lay.gc + cidx * lay.gc_bytes(), (uint32_t)lay.gc_bytes(), bar);
 }
 
 template <typename T, int DK, int DV>
-__global__ void __launch_bounds__(128) state_kernel(const float* __restrict__ s0, T* __restrict__ o,
-                                                    float* __restrict__ sT, Layout lay, int flags,
-                                                    unsigned char* __restrict__ ws) {
-  static_assert(DV == 128, "the state pass maps one thread to each of 128 value columns");
+__global__ void __launch_bounds__(544) state_kernel(const float* __restrict__ s0, T* __restrict__ o,
+                                                       float* __restrict__ sT, Layout lay, int flags,
+                                                       unsigned char* __restrict__ ws) {
+  static_assert(DV == 128 && DK == 128, "one TMEM lane per value column; four epilogue warps per lane quadrant");
   using S = StateSmem<DK, DV>;
   extern __shared__ __align__(1024) unsigned char smem[];
   ErrorWord* err = reinterpret_cast<ErrorWord*>(ws + lay.err);
   const int h = blockIdx.x, b = blockIdx.y;
-  const int tid = threadIdx.x, warp = tid >> 5;
-  const int vcol = tid;  // this thread's value column (TMEM lane of every M = 128 accumulator)
-  uint64_t* bar_mma = reinterpret_cast<uint64_t*>(smem + S::bar);
-  uint64_t* bar_in = bar_mma + 1;
-  uint64_t* bar_u = bar_mma + 2;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::bar);
+  uint64_t* full = bars + 0;        // [2] stage loaded (bulk-copy bytes)
+  uint64_t* stage_free = bars + 2;  // [2] every MMA that reads the stage is done
+  uint64_t* ws_full = bars + 4;
+  uint64_t* qs_full = bars + 5;     // [2]
+  uint64_t* ds_full = bars + 7;
+  uint64_t* mv_full = bars + 8;
+  uint64_t* vn_full = bars + 9;     // 16 epilogue warps
+  uint64_t* st_full = bars + 10;    // 16 epilogue warps
+  uint64_t* stage_epi = bars + 11;  // [2] 16 epilogue warps: done reading the stage
   uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + S::tmem);
-  const float* sG = reinterpret_cast<const float*>(smem + S::g);
-  const float* sU = reinterpret_cast<const float*>(smem + S::u);
   const bool store = (flags & GD_STORE_STATES) != 0 && lay.backward();
-  const size_t row0 = ((size_t)b * lay.H + h) * lay.NT;  // chunk index of chunk 0
+  const bool out = o != nullptr && !store;
+  const int NT = lay.NT;
+  const size_t row0 = ((size_t)b * lay.H + h) * NT;
 
   if (warp == 0) {
     tmem_alloc(tslot, 512);
     tmem_relinquish();
   }
   if (tid == 0) {
-    mbar_init(bar_mma, 1);
-    mbar_init(bar_in, 1);
-    mbar_init(bar_u, 1);
+    for (int i = 0; i < 9; ++i) mbar_init(bars + i, 1);
+    mbar_init(vn_full, 16);
+    mbar_init(st_full, 16);
+    mbar_init(stage_epi, 16);
+    mbar_init(stage_epi + 1, 16);
     fence_mbar_init();
   }
-  __syncthreads();
-  if (tid == 0) {
-    issue_stage<DK, DV>(smem, ws, lay, row0, bar_in);
-    mbar_arrive_expect_tx(bar_u, (uint32_t)lay.u_bytes());
-    bulk_g2s(smem + S::u, ws + lay.u + row0 * lay.u_bytes(), (uint32_t)lay.u_bytes(), bar_u);
-  }
-
-  float Sreg[DK];  // column vcol of S (all key rows), fp32
-  {
-    const float* s0p = s0 ? s0 + ((size_t)b * lay.H + h) * DK * DV : nullptr;
-#pragma unroll
-    for (int d = 0; d < DK; ++d) Sreg[d] = s0p ? s0p[(size_t)d * DV + vcol] : 0.f;
-#pragma unroll
-    for (int d8 = 0; d8 < DK / 8; ++d8) store8_bf16(smem + S::st, vcol, 8 * d8, DK, Sreg + 8 * d8);
-  }
-  fence_async_smem();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tm = *tslot;
-  const uint32_t tWS = tm + 0, tQS = tm + 64, tMV = tm + 128, tDS = tm + 256;
-
-  uint32_t ph_mma = 0, ph_in = 0, ph_u = 0;
+  const uint32_t tWS = tm, tMV = tm + 192, tDS = tm + 256;  // (Q S)^T at tm + 64 + 64 (c & 1)
+  const Tile tSt{smem_u32(smem + S::st), DK};
+  const Tile tVh{smem_u32(smem + S::vh), 64}, tVl{smem_u32(smem + S::vl), 64};
   bool ok = true;
-  for (int c = 0; c < lay.NT && ok; ++c) {
-    const size_t cidx = row0 + c;
-    const int t0 = c * C;
-    ok = mbar_wait(bar_in, ph_in, err, 20);
-    ph_in ^= 1;
-    ok = __syncthreads_and(ok);
-    if (!ok) break;
-    if (tid == 0) {
-      tc_fence_after();
-      // (W S)^T = S^T W^T  and  (Q S)^T = S^T Q^T : [DV x 64]
-      mma_tiles(tWS, DV, 64, DK, Tile{smem_u32(smem + S::st), DK}, true, 0, 0, Tile{smem_u32(smem + S::wt), 64}, true,
-                0, false);
-      mma_tiles(tQS, DV, 64, DK, Tile{smem_u32(smem + S::st), DK}, true, 0, 0, Tile{smem_u32(smem + S::qk), DK},
-                false, 0, false);
-      mma_commit(bar_mma);
+
+  if (warp == 16) {
+    // ---------------- MMA and bulk-copy issuer (one thread)
+    if (lane == 0) {
+      issue_stage<DK, DV>(smem + S::stage0, ws, lay, row0, full);
+      if (NT > 1) issue_stage<DK, DV>(smem + S::stage0 + S::stage_bytes, ws, lay, row0 + 1, full + 1);
+      for (int c = 0; c < NT && ok; ++c) {
+        const int s = c & 1;
+        const uint32_t par2 = (c >> 1) & 1;
+        unsigned char* stg = smem + S::stage0 + s * S::stage_bytes;
+        ok = mbar_wait(full + s, par2, err, 20) && mbar_wait(st_full, c & 1, err, 21);
+        if (!ok) break;
+        tc_fence_after();
+        if (store) {  // S_c^T image for the backward (bulk copy out; its reads finish before the tile is rewritten)
+          bulk_s2g(ws + lay.sci + (row0 + c) * lay.si_bytes(), smem + S::st, (uint32_t)lay.si_bytes());
+          bulk_commit();
+        }
+        mma_tiles(tWS, DV, 64, DK, tSt, true, 0, 0, Tile{smem_u32(stg + S::s_wt), 64}, true, 0, false);
+        mma_commit(ws_full);
+        if (out) {
+          mma_tiles(tm + 64 + 64 * s, DV, 64, DK, tSt, true, 0, 0, Tile{smem_u32(stg + S::s_q), DK}, false, 0,
+                    false);
+          mma_commit(qs_full + s);
+        }
+        ok = mbar_wait(vn_full, c & 1, err, 22);
+        if (!ok) break;
+        tc_fence_after();
+        if (store) {
+          bulk_s2g(ws + lay.vni + (row0 + c) * lay.vn_bytes(), smem + S::vh, (uint32_t)lay.vn_bytes());
+          bulk_commit();
+          bulk_wait_read0();  // the S^T and Vn^T tiles may be rewritten once ds_full / mv_full fire
+        }
+        const Tile tKh{smem_u32(stg + S::s_kt), DK}, tKl{smem_u32(stg + S::s_kt + 64 * DK * 2), DK};
+        mma_tiles(tDS, DV, DK, 64, tVh, true, 0, 0, tKh, true, 0, false);
+        mma_tiles(tDS, DV, DK, 64, tVh, true, 0, 0, tKl, true, 0, true);
+        mma_tiles(tDS, DV, DK, 64, tVl, true, 0, 0, tKh, true, 0, true);
+        mma_commit(ds_full);
+        if (out) {
+          const Tile tM{smem_u32(stg + S::s_m), 64};
+          mma_tiles(tMV, DV, 64, 64, tVh, true, 0, 0, tM, false, 0, false);
+          mma_tiles(tMV, DV, 64, 64, tVl, true, 0, 0, tM, false, 0, true);
+          mma_commit(mv_full);
+        }
+        mma_commit(stage_free + s);
+        if (c + 2 < NT) {
+          ok = mbar_wait(stage_free + s, par2, err, 23) && mbar_wait(stage_epi + s, par2, err, 28);
+          if (!ok) break;
+          issue_stage<DK, DV>(stg, ws, lay, row0 + c + 2, full + s);
+        }
+      }
+      if (store) bulk_wait0();
     }
-    ok = mbar_wait(bar_mma, ph_mma, err, 21);
-    ph_mma ^= 1;
-    if (ok) ok = mbar_wait(bar_u, ph_u, err, 22);
-    ph_u ^= 1;
-    ok = __syncthreads_and(ok);
-    if (!ok) break;
-    tc_fence_after();
-    const float Glast = sG[63];
+  } else {
+    // ---------------- epilogue warps
+    const int qd = warp & 3, quarter = warp >> 2;
+    const int v = 32 * qd + lane;   // value column = TMEM lane
+    const int tk0 = 16 * quarter;   // tokens of the [DV x 64] accumulators
+    const int dk0 = 32 * quarter;   // key rows of the state held here
+    float Sr[32];                   // S[dk0 + j][v]
     {
-      float acc[32];
-      float* vn_out = store ? reinterpret_cast<float*>(ws + lay.vn + cidx * lay.u_bytes()) : nullptr;
-#pragma unroll 1
-      for (int half = 0; half < 2; ++half) {
-        tmem_ld32(tmem_lane_addr(tWS, warp, 32 * half), acc);
-        float vn[32], ev[32];
+      const float* p = s0 ? s0 + ((size_t)b * lay.H + h) * DK * DV : nullptr;
 #pragma unroll
-        for (int jj = 0; jj < 32; ++jj) {
-          const int i = 32 * half + jj;
-          vn[jj] = sU[i * DV + vcol] - acc[jj];
-          ev[jj] = vn[jj] * __expf(Glast - sG[i]);
-          if (store) vn_out[i * DV + vcol] = vn[jj];
-        }
+      for (int j = 0; j < 32; ++j) Sr[j] = p ? p[(size_t)(dk0 + j) * DV + v] : 0.f;
 #pragma unroll
-        for (int q8 = 0; q8 < 4; ++q8) {
-          store8_split(smem + S::vh, smem + S::vl, vcol, 32 * half + 8 * q8, 64, vn + 8 * q8);
-          store8_split(smem + S::eh, smem + S::el, vcol, 32 * half + 8 * q8, 64, ev + 8 * q8);
-        }
-      }
+      for (int q8 = 0; q8 < 4; ++q8) store8_bf16(smem + S::st, v, dk0 + 8 * q8, DK, Sr + 8 * q8);
+      fence_async_smem();
+      mbar_arrive_warp(st_full);
     }
-    fence_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    if (tid == 0) {
-      tc_fence_after();
-      if (c + 1 < lay.NT) {  // U is consumed: stream in the next chunk's
-        mbar_arrive_expect_tx(bar_u, (uint32_t)lay.u_bytes());
-        bulk_g2s(smem + S::u, ws + lay.u + (cidx + 1) * lay.u_bytes(), (uint32_t)lay.u_bytes(), bar_u);
-      }
-      // (M Vn)^T = Vn^T M^T  [DV x 64];  (K^T e Vn)^T = (e Vn)^T K  [DV x DK]
-      mma_tiles(tMV, DV, 64, 64, Tile{smem_u32(smem + S::vh), 64}, true, 0, 0, Tile{smem_u32(smem + S::m), 64}, false,
-                0, false);
-      mma_tiles(tMV, DV, 64, 64, Tile{smem_u32(smem + S::vl), 64}, true, 0, 0, Tile{smem_u32(smem + S::m), 64}, false,
-                0, true);
-      // e Vn and k both split: hi hi + hi lo + lo hi (the state carries the sequence: it gets the extra bits)
-      const Tile tkh{smem_u32(smem + S::qk + 64 * DK * 2), DK}, tkl{smem_u32(smem + S::kl), DK};
-      mma_tiles(tDS, DV, DK, 64, Tile{smem_u32(smem + S::eh), 64}, true, 0, 0, tkh, true, 0, false);
-      mma_tiles(tDS, DV, DK, 64, Tile{smem_u32(smem + S::eh), 64}, true, 0, 0, tkl, true, 0, true);
-      mma_tiles(tDS, DV, DK, 64, Tile{smem_u32(smem + S::el), 64}, true, 0, 0, tkh, true, 0, true);
-      mma_commit(bar_mma);
-    }
-    ok = mbar_wait(bar_mma, ph_mma, err, 23);
-    ph_mma ^= 1;
-    ok = __syncthreads_and(ok);
-    if (!ok) break;
-    tc_fence_after();
+    float Ur[16];
     {
-      float qs[32], mv[32];
-#pragma unroll 1
-      for (int half = 0; half < 2; ++half) {
-        tmem_ld32(tmem_lane_addr(tQS, warp, 32 * half), qs);
-        tmem_ld32(tmem_lane_addr(tMV, warp, 32 * half), mv);
-        if (o != nullptr) {
+      const float* u = reinterpret_cast<const float*>(ws + lay.u + row0 * lay.u_bytes());
 #pragma unroll
-          for (int jj = 0; jj < 32; ++jj) {
-            const int i = 32 * half + jj;
-            const int t = t0 + i;
-            if (t < lay.T) o[(((size_t)b * lay.T + t) * lay.H + h) * DV + vcol] = from_f32<T>(__expf(sG[i]) * qs[jj] + mv[jj]);
-          }
-        }
+      for (int j = 0; j < 16; ++j) Ur[j] = __ldg(u + (tk0 + j) * DV + v);
+    }
+    for (int c = 0; c < NT; ++c) {
+      const size_t cidx = row0 + c;
+      const int s = c & 1;
+      const float* sG = reinterpret_cast<const float*>(smem + S::stage0 + s * S::stage_bytes + S::s_g);
+      // * Vn = U - W S
+      GD_TRACE_AT(ws, lay, 8 * c + 0);
+      if (!mbar_wait(ws_full, c & 1, err, 24)) { ok = false; break; }
+      GD_TRACE_AT(ws, lay, 8 * c + 1);
+      tc_fence_after();
+      const float gl = __expf(sG[63]);
+      {
+        float acc[16], vn[16];
+        tmem_ld16(tmem_lane_addr(tWS, warp, tk0), acc);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) vn[j] = Ur[j] - acc[j];
+        store8_split(smem + S::vh, smem + S::vl, v, tk0, 64, vn);
+        store8_split(smem + S::vh, smem + S::vl, v, tk0 + 8, 64, vn + 8);
+        tc_fence_before();
+        fence_async_smem();
+        mbar_arrive_warp(vn_full);
       }
+      GD_TRACE_AT(ws, lay, 8 * c + 2);
+      if (c + 1 < NT) {  // next chunk's U into registers while the tensor core works
+        const float* u = reinterpret_cast<const float*>(ws + lay.u + (cidx + 1) * lay.u_bytes());
+#pragma unroll
+        for (int j = 0; j < 16; ++j) Ur[j] = __ldg(u + (tk0 + j) * DV + v);
+      }
+      // * S <- exp(G_last) S + K~^T Vn
+      if (!mbar_wait(ds_full, c & 1, err, 25)) { ok = false; break; }
+      GD_TRACE_AT(ws, lay, 8 * c + 3);
+      tc_fence_after();
       if (store) {
-        float* sc = reinterpret_cast<float*>(ws + lay.sc + cidx * lay.s_bytes());
+        float* sc = reinterpret_cast<float*>(ws + lay.scf + cidx * lay.s_bytes()) + (size_t)v * DK + dk0;
 #pragma unroll
-        for (int d = 0; d < DK; ++d) sc[(size_t)d * DV + vcol] = Sreg[d];
+        for (int q4 = 0; q4 < 8; ++q4)
+          reinterpret_cast<float4*>(sc)[q4] = make_float4(Sr[4 * q4], Sr[4 * q4 + 1], Sr[4 * q4 + 2], Sr[4 * q4 + 3]);
       }
-      const float gl = __expf(Glast);
-      float ds[32];
+      {
+        float d[16];
+        tmem_ld16(tmem_lane_addr(tDS, warp, dk0), d);
 #pragma unroll
-      for (int q4 = 0; q4 < DK / 32; ++q4) {
-        tmem_ld32(tmem_lane_addr(tDS, warp, 32 * q4), ds);
+        for (int j = 0; j < 16; ++j) Sr[j] = fmaf(gl, Sr[j], d[j]);
+        tmem_ld16(tmem_lane_addr(tDS, warp, dk0 + 16), d);
 #pragma unroll
-        for (int jj = 0; jj < 32; ++jj) Sreg[32 * q4 + jj] = fmaf(gl, Sreg[32 * q4 + jj], ds[jj]);
+        for (int j = 0; j < 16; ++j) Sr[16 + j] = fmaf(gl, Sr[16 + j], d[j]);
+#pragma unroll
+        for (int q8 = 0; q8 < 4; ++q8) store8_bf16(smem + S::st, v, dk0 + 8 * q8, DK, Sr + 8 * q8);
+        tc_fence_before();
+        fence_async_smem();
+        mbar_arrive_warp(st_full);
       }
+      GD_TRACE_AT(ws, lay, 8 * c + 4);
+      // O of chunk c (overlaps chunk c + 1's products)
+      if (out) {
+        if (!mbar_wait(qs_full + s, (c >> 1) & 1, err, 26) || !mbar_wait(mv_full, c & 1, err, 27)) {
+          ok = false;
+          break;
+        }
+        GD_TRACE_AT(ws, lay, 8 * c + 7);
+        tc_fence_after();
+        float qs[16], mv[16];
+        tmem_ld16(tmem_lane_addr(tm + 64 + 64 * s, warp, tk0), qs);
+        tmem_ld16(tmem_lane_addr(tMV, warp, tk0), mv);
+        const int t0 = c * C;
 #pragma unroll
-      for (int d8 = 0; d8 < DK / 8; ++d8) store8_bf16(smem + S::st, vcol, 8 * d8, DK, Sreg + 8 * d8);
+        for (int j = 0; j < 16; ++j) {
+          const int i = tk0 + j, t = t0 + i;
+          if (t < lay.T) o[(((size_t)b * lay.T + t) * lay.H + h) * DV + v] = from_f32<T>(fmaf(__expf(sG[i]), qs[j], mv[j]));
+        }
+        tc_fence_before();
+      }
+      mbar_arrive_warp(stage_epi + s);  // this warp is done reading chunk c's stage
+      GD_TRACE_AT(ws, lay, 8 * c + 5);
     }
-    fence_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    if (tid == 0 && c + 1 < lay.NT) issue_stage<DK, DV>(smem, ws, lay, cidx + 1, bar_in);
-  }
-  if (ok && sT != nullptr) {
-    float* sp = sT + ((size_t)b * lay.H + h) * DK * DV;
+    if (ok && sT != nullptr) {
+      float* sp = sT + ((size_t)b * lay.H + h) * DK * DV;
 #pragma unroll
-    for (int d = 0; d < DK; ++d) sp[(size_t)d * DV + vcol] = Sreg[d];
+      for (int j = 0; j < 32; ++j) sp[(size_t)(dk0 + j) * DV + v] = Sr[j];
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -498,7 +603,6 @@ __global__ void __launch_bounds__(128) state_kernel(const float* __restrict__ s0
     tmem_dealloc(tm, 512);
   }
 }
-
 // ------------------------------------------------------------------------------------------------------------------
 // launchers
 
@@ -525,7 +629,7 @@ cudaError_t launch_state(const float* s0, void* o, float* sT, const Layout& lay,
   cudaError_t e = set_smem_once(kern, S::total, attr_done);
   if (e != cudaSuccess) return e;
   dim3 grid(lay.H, lay.B);
-  kern<<<grid, 128, S::total, st>>>(s0, static_cast<T*>(o), sT, lay, flags, ws);
+  kern<<<grid, 544, S::total, st>>>(s0, static_cast<T*>(o), sT, lay, flags, ws);
   return cudaGetLastError();
 }
 

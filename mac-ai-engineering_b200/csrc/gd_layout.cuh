@@ -1,19 +1,30 @@
 // Workspace layout shared by the host entry points and the kernels.
 //
 // All intermediates of one call live in one caller-provided buffer. Per chunk (index cidx = (b * H + h) * NT + c, h a
-// value head) the prep kernel writes:
-//   qk   [2][64 x DK] bf16 blocked   normalised q (scaled DK^-1/2) then normalised k, the MMA-ready images
-//   wt   [DK x 64]    bf16 blocked   W^T, W = A diag(beta gamma) K
-//   m    [64 x 64]    bf16 blocked   M = (Q K^T) * exp(G_i - G_j), lower with the diagonal
-//   u    [64][DV]     fp32           U = A diag(beta) V
-//   gc   [64]         fp32           G, the in-chunk inclusive cumulative sum of g
-//   qkl  [2][64 x DK] bf16 blocked   the low halves of normalised q and k (q = hi + lo to ~16 significant bits)
+// value head), "image" = an MMA-ready bf16 tile in the blocked layout of gd_common.cuh, copied to and from shared
+// memory whole by the bulk-copy engine. The prep kernel writes:
+//   qk   [2][64 x DK] image   normalised q (scaled), then normalised k (bf16 high halves)
+//   qkl  [2][64 x DK] image   their low halves (q = hi + lo to ~16 significant bits)
+//   kt   [2][64 x DK] image   K~ = diag(e) K, e_i = exp(G_last - G_i): hi, then lo (the state updates' operand)
+//   wt   [DK x 64]    image   W^T, W = A diag(beta gamma) K
+//   m    [64 x 64]    image   M = (Q K^T) * exp(G_i - G_j), lower with the diagonal
+//   u    [64][DV]     fp32    U = A diag(beta) V
+//   gc   [64]         fp32    G, the in-chunk inclusive cumulative sum of g
 // and for the backward also
-//   ainv [64][64]     fp32           A = (I + L)^-1
-//   mf, kg [64][64]   fp32           M (with its decay mask) and K K^T
-//   rq, rk [B*T*HK]   fp32           the l2 prologue's rsqrt per raw q / k row
-// The state pass with GD_STORE_STATES writes sc [DK][DV] fp32 (the state entering the chunk) and vn [64][DV] fp32;
-// the reverse pass writes dsn [DK][DV] fp32 (dLoss/dS_{c+1}) and dvn [64][DV] fp32.
+//   gq   [2][64 x DK] image   diag(gamma) Q: hi, then lo
+//   ai   [64 x 64]    image   A = (I + L)^-1
+//   vi   [64 x DV]    image   V
+//   mf, kg [64][64]   fp32    M and K K^T
+//   rq, rk [B*T*HK]   fp32    the l2 prologue's rsqrt per raw q / k row
+// The state pass with GD_STORE_STATES writes per chunk
+//   scf  [DV][DK]     fp32    S_c^T, the state entering the chunk
+//   sci  [DV x DK]    image   S_c^T (bf16)
+//   vni  [2][DV x 64] image   Vn^T: hi, then lo
+// and the reverse pass
+//   dsi  [2][DV x DK] image   dS_{c+1}^T: hi, then lo
+//   dvni [2][DV x 64] image   dVn^T: hi, then lo
+//   doi  [64 x DV]    image   dO
+//   sl   [16]         fp32    partial sums of <S_c, dS_{c+1}> (one per epilogue warp)
 // Every array starts on a 256-byte boundary (bulk copies need 16).
 #pragma once
 
@@ -25,17 +36,21 @@ namespace gd {
 struct Layout {
   int B, T, H, HK, DK, DV, NT, rep;
   size_t nch;  // B * H * NT chunks
-  size_t err, qk, wt, m, u, gc, qkl, ainv, mf, kg, rq, rk, sc, vn, dsn, dvn, total;
+  size_t err, trace, qk, qkl, kt, wt, m, u, gc;
+  size_t gq, ai, vi, mf, kg, rq, rk, scf, sci, vni, dsi, dvni, doi, sl, total;
 
   __host__ __device__ static size_t up(size_t x) { return (x + 255) & ~size_t(255); }
 
-  __host__ __device__ size_t qk_bytes() const { return (size_t)2 * 64 * DK * 2; }
+  __host__ __device__ size_t qk_bytes() const { return (size_t)2 * 64 * DK * 2; }   // a [2][64 x DK] image pair
   __host__ __device__ size_t wt_bytes() const { return (size_t)DK * 64 * 2; }
   __host__ __device__ size_t m_bytes() const { return (size_t)64 * 64 * 2; }
   __host__ __device__ size_t u_bytes() const { return (size_t)64 * DV * 4; }
   __host__ __device__ size_t gc_bytes() const { return (size_t)64 * 4; }
-  __host__ __device__ size_t ainv_bytes() const { return (size_t)64 * 64 * 4; }
-  __host__ __device__ size_t s_bytes() const { return (size_t)DK * DV * 4; }
+  __host__ __device__ size_t cc_bytes() const { return (size_t)64 * 64 * 4; }      // fp32 C x C
+  __host__ __device__ size_t vi_bytes() const { return (size_t)64 * DV * 2; }
+  __host__ __device__ size_t s_bytes() const { return (size_t)DK * DV * 4; }       // fp32 state
+  __host__ __device__ size_t si_bytes() const { return (size_t)DK * DV * 2; }      // one state image
+  __host__ __device__ size_t vn_bytes() const { return (size_t)2 * DV * 64 * 2; }  // a [2][DV x 64] image pair
 
   __host__ static Layout make(int B, int T, int H, int HK, int DK, int DV, bool backward) {
     Layout L{};
@@ -44,30 +59,42 @@ struct Layout {
     L.rep = HK > 0 ? H / HK : 1;
     L.nch = (size_t)B * H * L.NT;
     size_t o = 0;
-    L.err = o; o = up(o + 64);
-    L.qk = o; o = up(o + L.nch * L.qk_bytes());
-    L.wt = o; o = up(o + L.nch * L.wt_bytes());
-    L.m = o; o = up(o + L.nch * L.m_bytes());
-    L.u = o; o = up(o + L.nch * L.u_bytes());
-    L.gc = o; o = up(o + L.nch * L.gc_bytes());
-    L.qkl = o; o = up(o + L.nch * L.qk_bytes());
+    auto take = [&](size_t bytes) { size_t at = o; o = up(o + bytes); return at; };
+    L.err = take(64);
+#ifdef GD_TRACE
+    L.trace = take(4 * 4096 * 8);  // phase timestamps (profiling builds only)
+#else
+    L.trace = 0;
+#endif
+    L.qk = take(L.nch * L.qk_bytes());
+    L.qkl = take(L.nch * L.qk_bytes());
+    L.kt = take(L.nch * L.qk_bytes());
+    L.wt = take(L.nch * L.wt_bytes());
+    L.m = take(L.nch * L.m_bytes());
+    L.u = take(L.nch * L.u_bytes());
+    L.gc = take(L.nch * L.gc_bytes());
     if (backward) {
-      L.ainv = o; o = up(o + L.nch * L.ainv_bytes());
-      L.mf = o; o = up(o + L.nch * L.ainv_bytes());
-      L.kg = o; o = up(o + L.nch * L.ainv_bytes());
-      L.rq = o; o = up(o + (size_t)B * T * HK * 4);
-      L.rk = o; o = up(o + (size_t)B * T * HK * 4);
-      L.sc = o; o = up(o + L.nch * L.s_bytes());
-      L.vn = o; o = up(o + L.nch * L.u_bytes());
-      L.dsn = o; o = up(o + L.nch * L.s_bytes());
-      L.dvn = o; o = up(o + L.nch * L.u_bytes());
+      L.gq = take(L.nch * L.qk_bytes());
+      L.ai = take(L.nch * L.m_bytes());
+      L.vi = take(L.nch * L.vi_bytes());
+      L.mf = take(L.nch * L.cc_bytes());
+      L.kg = take(L.nch * L.cc_bytes());
+      L.rq = take((size_t)B * T * HK * 4);
+      L.rk = take((size_t)B * T * HK * 4);
+      L.scf = take(L.nch * L.s_bytes());
+      L.sci = take(L.nch * L.si_bytes());
+      L.vni = take(L.nch * L.vn_bytes());
+      L.dsi = take(L.nch * 2 * L.si_bytes());
+      L.dvni = take(L.nch * L.vn_bytes());
+      L.doi = take(L.nch * L.vi_bytes());
+      L.sl = take(L.nch * 64);
     } else {
-      L.ainv = L.mf = L.kg = L.rq = L.rk = L.sc = L.vn = L.dsn = L.dvn = 0;
+      L.gq = L.ai = L.vi = L.mf = L.kg = L.rq = L.rk = L.scf = L.sci = L.vni = L.dsi = L.dvni = L.doi = L.sl = 0;
     }
     L.total = o;
     return L;
   }
-  __host__ __device__ bool backward() const { return sc != 0; }
+  __host__ __device__ bool backward() const { return scf != 0; }
 };
 
 }  // namespace gd
