@@ -4,8 +4,10 @@
  * torch.mps.compile_shader and dispatched as lib.<kernel>(...). Each entry point below replaces one of those dispatch
  * sites (cited as reference file:line), or one autograd step that sequences them. Every function:
  *   - takes raw device pointers, sizes and a CUDA stream (cudaStream_t passed as void*), no torch types;
- *   - allocates nothing: intermediates live in a caller-provided workspace of gd_workspace_bytes();
- *   - launches on the given stream and does not synchronise (graph-capturable), except gd_read_error;
+ *   - allocates nothing: intermediates live in a caller-provided workspace of gd_workspace_bytes() (for
+ *     gd_forward_noalloc, in a fixed array inside the library: see its comment);
+ *   - launches on the given stream and does not synchronise (graph-capturable), except gd_read_error and
+ *     gd_forward_noalloc, which are described on their own;
  *   - returns a status code (GD_OK or a GD_ERR_*) and never aborts or traps.
  *
  * Layouts (all contiguous, row-major):
@@ -35,6 +37,7 @@ extern "C" {
 #define GD_ERR_LAUNCH 5    /* the CUDA launch failed */
 #define GD_ERR_TIMEOUT 6   /* a bounded device-side wait gave up (recorded in the workspace's error word) */
 #define GD_ERR_DEVICE 7    /* the current device is not sm_100 */
+#define GD_ERR_SCRATCH 8   /* gd_forward_noalloc: the sizes need more than its fixed 64 MiB scratch array */
 
 /* dtypes of q / k / v / o / do and of dq / dk / dv */
 #define GD_FLOAT32 0
@@ -103,6 +106,24 @@ int gd_backward(const void* q, const void* k, const void* v, const float* g, con
 /* Synchronises the stream and returns the first device-side failure recorded in the workspace's error word (GD_OK if
  * none), with the kernel stage that recorded it in *where (may be NULL); then clears the word. */
 int gd_read_error(void* workspace, void* stream, int* where);
+
+/* gd_forward for callers that cannot allocate device memory: a program whose device memory all belongs to another
+ * allocator (a serving engine's reserved pool, a host framework that owns the GPU), or a caller that may not risk the
+ * device synchronisation cudaMalloc / cudaFree can cause. Same arguments and results as gd_forward, without the
+ * workspace: the intermediates go to one fixed 64 MiB device array inside the library (enough for
+ * gd_workspace_bytes(..., 0) <= 64 MiB, e.g. 16 value heads x 1,664 tokens); larger sizes return GD_ERR_SCRATCH
+ * before any device call. The library allocates nothing either: the array is static device memory, held until the
+ * process exits on each GPU where this code has been loaded.
+ *   - The first call on a device (that device current) looks the array's device address up with
+ *     cudaGetSymbolAddress and keeps it; make that first call before any stream capture.
+ *   - All calls on a device share the array. Each call clears the part that must start at zero (the error word) on
+ *     its stream; calls whose work overlaps on the GPU race on the array, so the caller serialises them.
+ *   - device_status NULL: asynchronous like gd_forward. Otherwise the call waits for its stream and stores the
+ *     kernels' own status (GD_OK, or GD_ERR_TIMEOUT) in *device_status.
+ * No counterpart in the reference: its Metal path allocates through torch. */
+int gd_forward_noalloc(const void* q, const void* k, const void* v, const float* g, const float* beta,
+                       const float* s0, void* o, float* sT, int dtype, int B, int T, int H, int HK, int DK, int DV,
+                       int flags, void* stream, int* device_status);
 
 #ifdef __cplusplus
 }

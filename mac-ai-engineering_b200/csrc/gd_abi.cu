@@ -107,6 +107,7 @@ const char* gd_status_string(int status) {
     case GD_ERR_LAUNCH: return "CUDA kernel launch failed";
     case GD_ERR_TIMEOUT: return "a device-side wait gave up (kernel stage recorded in the error word)";
     case GD_ERR_DEVICE: return "the current CUDA device is not sm_100 (B200)";
+    case GD_ERR_SCRATCH: return "sizes need more than gd_forward_noalloc's fixed 64 MiB scratch array";
     default: return "unknown status";
   }
 }

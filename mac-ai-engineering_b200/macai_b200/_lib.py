@@ -11,12 +11,13 @@ import os
 from . import build as _build
 
 GD_OK, GD_ERR_ARG, GD_ERR_SHAPE, GD_ERR_ALIGN, GD_ERR_WORKSPACE, GD_ERR_LAUNCH, GD_ERR_TIMEOUT, GD_ERR_DEVICE = range(8)
+GD_ERR_SCRATCH = 8
 GD_FLOAT32, GD_FLOAT16, GD_BFLOAT16 = 0, 1, 2
 GD_L2NORM, GD_STORE_STATES, GD_SCALE_Q = 1, 2, 4
 
 # every entry point declared in include/gated_delta_b200.h
 EXPORTS = ("gd_status_string", "gd_workspace_bytes", "gd_prep", "gd_fwd_state", "gd_bwd_state", "gd_bwd_chunk",
-           "gd_forward", "gd_backward", "gd_read_error")
+           "gd_forward", "gd_backward", "gd_read_error", "gd_forward_noalloc")
 
 _P = ctypes.c_void_p
 _I = ctypes.c_int
@@ -32,6 +33,7 @@ _SIGS = {
     "gd_forward": ([_P] * 8 + [_I] * 8 + [_P, _SZ, _P], _I),
     "gd_backward": ([_P] * 14 + [_I] * 8 + [_P, _SZ, _P], _I),
     "gd_read_error": ([_P, _P, ctypes.POINTER(_I)], _I),
+    "gd_forward_noalloc": ([_P] * 8 + [_I] * 8 + [_P, ctypes.POINTER(_I)], _I),
 }
 
 _lib = None
