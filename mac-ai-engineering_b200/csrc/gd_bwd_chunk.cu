@@ -128,14 +128,16 @@ __global__ void __launch_bounds__(256) bwd_chunk_kernel(const T* __restrict__ qr
   const uint32_t T_DKS = tm + 384;
   const uint32_t T_DQ = tm + 448;
 
-  const Tile tQ{smem_u32(smem + S::qk), DK};
-  const Tile tK{smem_u32(smem + S::qk + 64 * DK * 2), DK};
-  const Tile tQl{smem_u32(smem + S::qkl), DK};
-  const Tile tKl{smem_u32(smem + S::qkl + 64 * DK * 2), DK};
+  // q / k images are transposed ([DK x 64], rows d): the K-major operand wherever d is a product's M or N
+  const Tile tQ{smem_u32(smem + S::qk), 64};
+  const Tile tK{smem_u32(smem + S::qk + 64 * DK * 2), 64};
+  const Tile tQl{smem_u32(smem + S::qkl), 64};
+  const Tile tKl{smem_u32(smem + S::qkl + 64 * DK * 2), 64};
   // fp32 normalised q / k element (i, d) from the hi + lo images
   auto qhat = [&](int i, int d) {
-    return __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(smem + S::qk + blk_off(i, d, DK))) +
-           __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(smem + S::qkl + blk_off(i, d, DK)));
+    const int r = (i & 64) ? DK + d : d, cc = i & 63;  // token i of q (i < 64) or of k (i - 64)
+    return __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(smem + S::qk + blk_off(r, cc, 64))) +
+           __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(smem + S::qkl + blk_off(r, cc, 64)));
   };
   const Tile tA{smem_u32(smem + S::a), 64};
 
@@ -173,14 +175,14 @@ __global__ void __launch_bounds__(256) bwd_chunk_kernel(const T* __restrict__ qr
     if (!ok) break;
     if (tid == 0) {
       tc_fence_after();
-      const Tile tSc{smem_u32(smem + S::sc), DK}, tDO{smem_u32(smem + S::dO), DV}, tV{smem_u32(smem + S::v), DV};
+      const Tile tSc{smem_u32(smem + S::sc), DK}, tDO{smem_u32(smem + S::dO), DV}, tV{smem_u32(smem + S::v), 64};
       const Tile tVn{smem_u32(smem + S::vn), 64}, tDVh{smem_u32(smem + S::dvn), 64}, tDVl{smem_u32(smem + S::dvnl), 64};
       mma_tiles(T_DM, 64, 64, DV, tDO, true, 0, 0, tVn, true, 0, false);          // dO Vn^T
       mma_tiles(T_DQA, DK, 64, DV, tSc, false, 0, 0, tDO, false, 0, false);       // S_c dO^T
       mma_tiles(T_DW, DK, 64, DV, tSc, false, 0, 0, tDVh, true, 0, false);        // S_c dVn^T
       mma_tiles(T_Y, DV, 64, 64, tDVh, true, 0, 0, tA, true, 0, false);           // dVn^T A (dVn split)
       mma_tiles(T_Y, DV, 64, 64, tDVl, true, 0, 0, tA, true, 0, true);
-      mma_tiles(T_DAV, 64, 64, DV, tDVh, false, 0, 0, tV, false, 0, false);       // dVn V^T
+      mma_tiles(T_DAV, 64, 64, DV, tDVh, false, 0, 0, tV, true, 0, false);        // dVn V^T
       mma_commit(bar_mma);
     }
     GD_TRACE_AT(ws, lay, 2);
@@ -263,14 +265,14 @@ __global__ void __launch_bounds__(256) bwd_chunk_kernel(const T* __restrict__ qr
     if (tid == 0) {
       tc_fence_after();
       const Tile tDMh{smem_u32(smem + S::dmh), 64}, tDMl{smem_u32(smem + S::dml), 64}, tDW{smem_u32(smem + S::dwt), 64};
-      mma_tiles(T_DQ, DK, 64, 64, tK, false, 0, 0, tDMh, false, 0, false);      // (dM K)^T = K^T dM^T
-      mma_tiles(T_DQ, DK, 64, 64, tKl, false, 0, 0, tDMh, false, 0, true);
-      mma_tiles(T_DQ, DK, 64, 64, tK, false, 0, 0, tDMl, false, 0, true);
-      mma_tiles(T_DKA, DK, 64, 64, tQ, false, 0, 0, tDMh, true, 0, false);      // (dM^T Q)^T = Q^T dM
-      mma_tiles(T_DKA, DK, 64, 64, tQl, false, 0, 0, tDMh, true, 0, true);
-      mma_tiles(T_DKA, DK, 64, 64, tQ, false, 0, 0, tDMl, true, 0, true);
+      mma_tiles(T_DQ, DK, 64, 64, tK, true, 0, 0, tDMh, false, 0, false);       // (dM K)^T = K^T dM^T
+      mma_tiles(T_DQ, DK, 64, 64, tKl, true, 0, 0, tDMh, false, 0, true);
+      mma_tiles(T_DQ, DK, 64, 64, tK, true, 0, 0, tDMl, false, 0, true);
+      mma_tiles(T_DKA, DK, 64, 64, tQ, true, 0, 0, tDMh, true, 0, false);       // (dM^T Q)^T = Q^T dM
+      mma_tiles(T_DKA, DK, 64, 64, tQl, true, 0, 0, tDMh, true, 0, true);
+      mma_tiles(T_DKA, DK, 64, 64, tQ, true, 0, 0, tDMl, true, 0, true);
       mma_tiles(T_X, DK, 64, 64, tDW, true, 0, 0, tA, true, 0, false);          // (A^T dW)^T = dW^T A
-      mma_tiles(T_DAK, 64, 64, DK, tDW, false, 0, 0, tK, false, 0, false);      // dW K^T
+      mma_tiles(T_DAK, 64, 64, DK, tDW, false, 0, 0, tK, true, 0, false);       // dW K^T
       mma_commit(bar_mma);
     }
     GD_TRACE_AT(ws, lay, 5);
@@ -409,7 +411,7 @@ __global__ void __launch_bounds__(256) bwd_chunk_kernel(const T* __restrict__ qr
     __syncthreads();
     if (tid == 0) {
       tc_fence_after();
-      mma_tiles(T_DKC, DK, 64, 64, tK, false, 0, 0, Tile{smem_u32(smem + S::z), 64}, false, 0, false);  // K^T Z^T
+      mma_tiles(T_DKC, DK, 64, 64, tK, true, 0, 0, Tile{smem_u32(smem + S::z), 64}, false, 0, false);  // K^T Z^T
       mma_commit(bar_mma);
     }
     GD_TRACE_AT(ws, lay, 9);

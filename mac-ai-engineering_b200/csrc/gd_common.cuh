@@ -319,6 +319,28 @@ __device__ __forceinline__ void store8_split(unsigned char* hi_tile, unsigned ch
   store8_bf16(lo_tile, r, c0, cols, l);
 }
 
+// A blocked [R x Cc] bf16 tile in shared memory -> its transpose, a blocked [Cc x R] image in global memory. Each warp
+// moves four 8 x 8 core matrices per step: ldmatrix.trans hands lane l the transposed core's row l / 4, elements
+// 2 (l % 4) and 2 (l % 4) + 1, which is the 4-byte word l of that 128-byte core (so a warp's stores are contiguous).
+template <int R, int Cc, int NWARPS>
+__device__ __forceinline__ void store_tile_transposed(const unsigned char* src, unsigned char* dst) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr int NCORE = (R / 8) * (Cc / 8);
+  static_assert(NCORE % 4 == 0, "whole groups of four core matrices");
+  for (int gidx = warp; gidx < NCORE / 4; gidx += NWARPS) {
+    const uint32_t addr = smem_u32(src + (4 * gidx + (lane >> 3)) * 128 + (lane & 7) * 16);
+    uint32_t r[4];
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int cs = 4 * gidx + i, rb = cs / (Cc / 8), cb = cs % (Cc / 8);  // source core (rb, cb) -> (cb, rb)
+      reinterpret_cast<uint32_t*>(dst + ((size_t)cb * (R / 8) + rb) * 128)[lane] = r[i];
+    }
+  }
+}
+
 template <typename T>
 __device__ __forceinline__ float to_f32(T x);
 template <>

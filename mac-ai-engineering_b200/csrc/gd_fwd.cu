@@ -170,10 +170,31 @@ __global__ void __launch_bounds__(128) prep_kernel(const T* __restrict__ q, cons
   }
   __syncthreads();  // sG complete for everyone
   GD_TRACE_AT(ws, lay, 2);
-  {  // the low halves go out before L and A overwrite them
-    const uint4* src = reinterpret_cast<const uint4*>(smem + S::ql);
-    uint4* dst = reinterpret_cast<uint4*>(ws + lay.qkl + cidx * lay.qk_bytes());
-    for (int idx = tid; idx < (int)(lay.qk_bytes() / 16); idx += 128) dst[idx] = src[idx];
+  {  // the low halves go out (transposed images) before L and A overwrite them
+    unsigned char* dst = ws + lay.qkl + cidx * lay.qk_bytes();
+    store_tile_transposed<64, DK, 4>(smem + S::ql, dst);
+    store_tile_transposed<64, DK, 4>(smem + S::kl, dst + 64 * DK * 2);
+  }
+  if (lay.backward()) {  // diag(gamma) Q from q's hi + lo, split again: the reverse pass's operand
+    unsigned char* gqh = ws + lay.gq + cidx * lay.qk_bytes();
+    unsigned char* gql = gqh + 64 * DK * 2;
+    for (int idx = tid; idx < 64 * DK / 8; idx += 128) {
+      const int rl = idx & 7, cb = (idx >> 3) % (DK / 8), rb = idx / (8 * (DK / 8));
+      const int r = 8 * rb + rl;
+      const uint4 uh = *reinterpret_cast<const uint4*>(smem + S::q + blk_off(r, 8 * cb, DK));
+      const uint4 ul = *reinterpret_cast<const uint4*>(smem + S::ql + blk_off(r, 8 * cb, DK));
+      const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&uh);
+      const __nv_bfloat162* l2 = reinterpret_cast<const __nv_bfloat162*>(&ul);
+      const float gr = __expf(sG[r]);
+      float x[8];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 fh = __bfloat1622float2(h2[e]), fl = __bfloat1622float2(l2[e]);
+        x[2 * e] = gr * (fh.x + fl.x);
+        x[2 * e + 1] = gr * (fh.y + fl.y);
+      }
+      store8_split(gqh, gql, r, 8 * cb, DK, x);
+    }
   }
   {  // K~ = diag(e) K (e_i = exp(G_last - G_i) <= 1) from k's hi + lo, split again: the state update's operand
     unsigned char* kth = ws + lay.kt + cidx * lay.qk_bytes();
@@ -263,30 +284,8 @@ __global__ void __launch_bounds__(128) prep_kernel(const T* __restrict__ q, cons
       if (aimg != nullptr) store8_bf16(aimg, i, j0 + 8 * q8, 64, a0);  // the backward's A image
     }
     if (lay.backward()) {
-      // the backward's V image and diag(gamma) Q (hi + lo, from q's two halves)
-      const uint4* vs = reinterpret_cast<const uint4*>(smem + S::v);
-      uint4* vd = reinterpret_cast<uint4*>(ws + lay.vi + cidx * lay.vi_bytes());
-      for (int idx = tid; idx < (int)(lay.vi_bytes() / 16); idx += 128) vd[idx] = vs[idx];
-      unsigned char* gqh = ws + lay.gq + cidx * lay.qk_bytes();
-      unsigned char* gql = gqh + 64 * DK * 2;
-      const unsigned char* qlo = ws + lay.qkl + cidx * lay.qk_bytes();  // written above by this CTA
-      for (int idx = tid; idx < 64 * DK / 8; idx += 128) {
-        const int rl = idx & 7, cb = (idx >> 3) % (DK / 8), rb = idx / (8 * (DK / 8));
-        const int r = 8 * rb + rl;
-        const uint4 uh = *reinterpret_cast<const uint4*>(smem + S::q + blk_off(r, 8 * cb, DK));
-        const uint4 ul = *reinterpret_cast<const uint4*>(qlo + blk_off(r, 8 * cb, DK));
-        const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&uh);
-        const __nv_bfloat162* l2 = reinterpret_cast<const __nv_bfloat162*>(&ul);
-        const float gr = __expf(sG[r]);
-        float x[8];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 fh = __bfloat1622float2(h2[e]), fl = __bfloat1622float2(l2[e]);
-          x[2 * e] = gr * (fh.x + fl.x);
-          x[2 * e + 1] = gr * (fh.y + fl.y);
-        }
-        store8_split(gqh, gql, r, 8 * cb, DK, x);
-      }
+      // the backward's V image, transposed ([DV x 64], rows v)
+      store_tile_transposed<64, DV, 4>(smem + S::v, ws + lay.vi + cidx * lay.vi_bytes());
     }
   }
   fence_async_smem();
@@ -306,9 +305,9 @@ __global__ void __launch_bounds__(128) prep_kernel(const T* __restrict__ q, cons
   }
   // the q / k images and G go out while the MMAs run
   if (ok) {
-    const uint4* src = reinterpret_cast<const uint4*>(smem + S::q);
-    uint4* dst = reinterpret_cast<uint4*>(ws + lay.qk + cidx * lay.qk_bytes());
-    for (int idx = tid; idx < (int)(lay.qk_bytes() / 16); idx += 128) dst[idx] = src[idx];
+    unsigned char* dst = ws + lay.qk + cidx * lay.qk_bytes();  // transposed images ([DK x 64], rows d)
+    store_tile_transposed<64, DK, 4>(smem + S::q, dst);
+    store_tile_transposed<64, DK, 4>(smem + S::k, dst + 64 * DK * 2);
     if (tid < 64) reinterpret_cast<float*>(ws + lay.gc + cidx * lay.gc_bytes())[tid] = sG[tid];
   }
   if (ok) ok = mbar_wait(bar, 1, err, 11);
@@ -373,7 +372,7 @@ struct StateSmem {
   static constexpr size_t vl = vh + DV * 64 * 2;           //            lo
   static constexpr size_t stage0 = vl + DV * 64 * 2;       // two input stages, each:
   static constexpr size_t s_wt = 0;                        //   [DK x 64] W^T image
-  static constexpr size_t s_q = s_wt + DK * 64 * 2;        //   [64 x DK] q image (hi)
+  static constexpr size_t s_q = s_wt + DK * 64 * 2;        //   [DK x 64] q image (hi, transposed)
   static constexpr size_t s_kt = s_q + 64 * DK * 2;        //   [2][64 x DK] K~ hi, lo
   static constexpr size_t s_m = s_kt + 2 * 64 * DK * 2;    //   [64 x 64] M image
   static constexpr size_t s_g = s_m + 64 * 64 * 2;         //   [64] G
@@ -462,7 +461,7 @@ __global__ void __launch_bounds__(544) state_kernel(const float* __restrict__ s0
         mma_tiles(tWS, DV, 64, DK, tSt, true, 0, 0, Tile{smem_u32(stg + S::s_wt), 64}, true, 0, false);
         mma_commit(ws_full);
         if (out) {
-          mma_tiles(tm + 64 + 64 * s, DV, 64, DK, tSt, true, 0, 0, Tile{smem_u32(stg + S::s_q), DK}, false, 0,
+          mma_tiles(tm + 64 + 64 * s, DV, 64, DK, tSt, true, 0, 0, Tile{smem_u32(stg + S::s_q), 64}, true, 0,
                     false);
           mma_commit(qs_full + s);
         }

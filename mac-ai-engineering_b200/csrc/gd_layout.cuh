@@ -3,8 +3,8 @@
 // All intermediates of one call live in one caller-provided buffer. Per chunk (index cidx = (b * H + h) * NT + c, h a
 // value head), "image" = an MMA-ready bf16 tile in the blocked layout of gd_common.cuh, copied to and from shared
 // memory whole by the bulk-copy engine. The prep kernel writes:
-//   qk   [2][64 x DK] image   normalised q (scaled), then normalised k (bf16 high halves)
-//   qkl  [2][64 x DK] image   their low halves (q = hi + lo to ~16 significant bits)
+//   qk   [2][DK x 64] image   normalised q (scaled), then normalised k (bf16 high halves), transposed (rows d)
+//   qkl  [2][DK x 64] image   their low halves (q = hi + lo to ~16 significant bits)
 //   kt   [2][64 x DK] image   K~ = diag(e) K, e_i = exp(G_last - G_i): hi, then lo (the state updates' operand)
 //   wt   [DK x 64]    image   W^T, W = A diag(beta gamma) K
 //   m    [64 x 64]    image   M = (Q K^T) * exp(G_i - G_j), lower with the diagonal
@@ -13,7 +13,7 @@
 // and for the backward also
 //   gq   [2][64 x DK] image   diag(gamma) Q: hi, then lo
 //   ai   [64 x 64]    image   A = (I + L)^-1
-//   vi   [64 x DV]    image   V
+//   vi   [DV x 64]    image   V^T
 //   mf, kg [64][64]   fp32    M and K K^T
 //   rq, rk [B*T*HK]   fp32    the l2 prologue's rsqrt per raw q / k row
 // The state pass with GD_STORE_STATES writes per chunk
