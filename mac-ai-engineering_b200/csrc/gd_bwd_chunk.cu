@@ -1,24 +1,34 @@
-// Per-chunk gradients of the chunked gated delta rule on B200 (sm_100a): one CTA of 256 threads per (chunk, key head,
-// batch row), all CTAs independent, one writer per gradient element (no atomics; bitwise reproducible).
+// Per-chunk gradients of the chunked gated delta rule on B200 (sm_100a).
 //
-// Inputs per value head, all bf16 images from the workspace copied whole by the bulk-copy engine: the q / k images,
-// A = (I + L)^-1 and V (prep), S_c^T and Vn^T (the forward state pass with GD_STORE_STATES), dS_{c+1}^T, dVn^T and dO
-// (the reverse pass); G, M and K K^T in fp32 (prep), the partial sums of <S_c, dS_{c+1}> (reverse pass); from the
-// caller: v, beta and, for the l2 prologue's backward, q and k.
+// A persistent kernel: one CTA per SM walks work items (chunk c, key head hk, batch row b) in a fixed order; an item has
+// one sub-item per value head of the key head (GQA), and d(normalised q / k) are summed over the sub-items in registers
+// in a fixed order (one writer per gradient element: no atomics, bitwise reproducible).
 //
-// Products, all tcgen05 from blocked shared-memory tiles into TMEM (transposed "[D x 64]" accumulators put the head
-// dimension on TMEM lanes; C x C ones use M = 64; an image with rows along a product's K dimension is its MN-major
-// operand):
-//   group 1:  dO Vn^T, (dO S_c^T)^T, (dVn S_c^T)^T, (A^T dVn)^T, dVn V^T
-//   group 2:  (Vn dS^T)^T                      (Vn and dS split: three products)
-//   group 3:  (dM K)^T, (dM^T Q)^T, (A^T dW)^T, dW K^T      (dM, q and k split: three products each)
-// M (with its decay mask) and K K^T come in fp32 from the prep kernel; q and k as bf16 hi + lo images.
-//   group 4:  T1 = dA A^T;  group 5: dL = -A^T T1;  group 6: (K^T Z)^T with Z = P_beta + P_beta^T, P_beta = diag(beta) P
+// Inputs per sub-item, all bf16 images from the workspace copied whole by the bulk-copy engine: S_c^T and Vn^T (the
+// forward recompute), dS_{c+1}^T (hi, lo), dVn^T (hi, lo) and dO (the reverse pass), A, V^T and the transposed q / k
+// images (prep); G, M and K K^T in fp32 (prep), the partial sums of <S_c, dS_{c+1}> (reverse pass). From the caller:
+// beta and, for the l2 prologue's backward, q and k.
+//
+// Products, all tcgen05 from blocked shared-memory tiles into TMEM ("[D x 64]" accumulators put the head dimension on
+// the 128 TMEM lanes; C x C ones use M = 64). TMEM blocks of 64 columns B0..B7:
+//   G1:  B0 dO Vn^T, B1 (dO S^T)^T, B2 (dVn S^T)^T, B3 (A^T dVn)^T (dVn split), B4 dVn V^T
+//   G3:  B6 (dM K)^T, B7 (dM^T Q)^T (dM, q and k split), B2 (A^T dW)^T, B1 dW K^T        dW = -dVn S^T
+//   G2:  B5 (Vn dS^T)^T (Vn and dS split)
+//   tail: B6 T1 = dA A^T, B7 A^T T1 (dL = -A^T T1), B5 (K^T (P_beta + P_beta^T)) with P_beta = diag(beta) (dL * Gamma)
 // Equations: tools/check_chunk_equations.py:49-76 and src/macai/gated_delta/_chunked.py:20-34 of the reference; dg is
 // summed without cancellation (the regrouping of _chunked.py:1138-1142, extended to the decay-mask terms):
 //   dg_t = sum_{s>=t} (a_s + w_s) + gamma_last <S_c, dS_{c+1}> + sum_{r<t} E_r + sum_{i>=t>j} R_ij
 //   a_s = gamma_s q_s . (dO S_c^T)_s, w_s = beta_s gamma_s k_s . X_s, E_r = e_r k_r . (Vn dS^T)_r,
-//   R_ij = dM_ij (Q K^T)_ij + dL_ij L_ij.
+//   R_ij = dM_ij (Q K^T)_ij + dL_ij L_ij,  X = A^T dW.
+//
+// Roles (18 warps): warps 0-15 epilogue (warp w: TMEM lane quadrant w % 4, 16 columns from 16 (w / 4)); warp 16 one
+// thread issuing every MMA (in dependency order, whichever is ready first); warp 17 one thread issuing every bulk copy.
+// Shared memory holds one sub-item's tiles; each region is refilled for the next sub-item as soon as its last reader is
+// done (the TMEM block plan lets the next sub-item's G1 run under this one's tail):
+//   IN1 (S_c^T, dO, V^T; then dS^T)   free after G2        IN2 (dVn^T; then dM, dW^T)   free after G3
+//   IN3 (Vn^T)                        free after G2        A                            free after A^T T1
+//   QK (q^T, k^T hi + lo)             free after the last sub-item's P11 (the l2 backward reads q and k from HBM)
+// All hand-offs are mbarriers; every wait is bounded and reports GD_ERR_TIMEOUT.
 #include "gd_common.cuh"
 #include "gd_layout.cuh"
 
@@ -26,518 +36,666 @@ namespace gd {
 
 template <int DK, int DV>
 struct ChunkSmem {
-  // bf16 tiles
-  static constexpr size_t qk = 0;                        // [128 x DK]: q image (rows 0-63), k image (rows 64-127)
-  static constexpr size_t qkl = qk + 2 * 64 * DK * 2;    // [128 x DK]: their low halves
-  static constexpr size_t a = qkl + 2 * 64 * DK * 2;     // [64 x 64] A
-  static constexpr size_t big = a + 64 * 64 * 2;         // 64 KB, reused by phase (see the kernel)
-  static constexpr size_t sc = big;                      //   phase 1: [DV x DK] S_c^T
-  static constexpr size_t dO = big + DK * DV * 2;        //            [64 x DV] dO
-  static constexpr size_t v = dO + 64 * DV * 2;          //            [64 x DV] V
-  static constexpr size_t dsh = big;                     //   phase 2: [DV x DK] dS^T hi
-  static constexpr size_t dsl = big + DK * DV * 2;       //            [DV x DK] dS^T lo
-  static constexpr size_t da = big;                      //   phase 3: [64 x 64] dA
-  static constexpr size_t t1 = big + 8192;               //            [64 x 64] T1
-  static constexpr size_t z = big + 16384;               //            [64 x 64] Z
-  static constexpr size_t vn = big + 65536;              // 32 KB: [DV x 64] Vn^T hi, lo; later fp32 [64][64] P_beta, R
-  static constexpr size_t vnl = vn + DV * 64 * 2;
-  static constexpr size_t pb = vn;                       //   fp32 [64][64] P_beta (swizzled)
-  static constexpr size_t r = vn + 16384;                //   fp32 [64][64] R (swizzled)
-  static constexpr size_t dvn = vn + 32768;              // 32 KB: [DV x 64] dVn^T hi, lo; later dM hi, lo and dW^T
-  static constexpr size_t dvnl = dvn + DV * 64 * 2;
-  static constexpr size_t dmh = dvn;                     //   [64 x 64] dM hi
-  static constexpr size_t dml = dvn + 8192;              //   [64 x 64] dM lo
-  static constexpr size_t dwt = dvn + 16384;             //   [DK x 64] dW^T
-  // fp32
-  static constexpr size_t g = dvn + 32768;               // [64] G
-  static constexpr size_t beta = g + 256;                // [64]
-  static constexpr size_t part = beta + 256;             // [5][4][64] quadrant partial dots: a, kX, vY, E, xq/xk
-  static constexpr size_t pk = part + 5 * 4 * 64 * 4;    // [2][64] row halves of sum_j P_ij KG_ij
-  static constexpr size_t red = pk + 2 * 64 * 4;         // [16] partial sums of <S_c, dS_{c+1}>
-  static constexpr size_t bar = red + 64;                // 5 mbarriers: mma, q/k images, group 2, phase-1 and dS images
-  static constexpr size_t tmem = bar + 40;
+  static constexpr size_t qk = 0;                           // [2][DK x 64] q^T, k^T (hi)
+  static constexpr size_t qkl = qk + 2 * DK * 64 * 2;       //              their low halves
+  static constexpr size_t a = qkl + 2 * DK * 64 * 2;        // [64 x 64] A
+  static constexpr size_t in1 = a + 64 * 64 * 2;            // 64 KB
+  static constexpr size_t sc = in1;                         //   [DV x DK] S_c^T
+  static constexpr size_t dO = sc + DV * DK * 2;            //   [64 x DV] dO
+  static constexpr size_t vt = dO + 64 * DV * 2;            //   [DV x 64] V^T
+  static constexpr size_t dsh = in1;                        //   then [DV x DK] dS^T hi
+  static constexpr size_t dsl = in1 + DV * DK * 2;          //                     lo
+  static constexpr size_t in2 = in1 + 2 * DV * DK * 2;      // 32 KB
+  static constexpr size_t dvh = in2;                        //   [DV x 64] dVn^T hi
+  static constexpr size_t dvl = in2 + DV * 64 * 2;          //                   lo
+  static constexpr size_t dmh = in2;                        //   then [64 x 64] dM hi
+  static constexpr size_t dml = in2 + 64 * 64 * 2;          //                  lo
+  static constexpr size_t dwt = in2 + 2 * 64 * 64 * 2;      //        [DK x 64] dW^T
+  static constexpr size_t in3 = in2 + 2 * DV * 64 * 2;      // 32 KB: [DV x 64] Vn^T hi, lo
+  static constexpr size_t vnh = in3;
+  static constexpr size_t vnl = in3 + DV * 64 * 2;
+  static constexpr size_t tail = in3 + 2 * DV * 64 * 2;     // 16 KB
+  static constexpr size_t da = tail;                        //   [64 x 64] dA, then P_beta
+  static constexpr size_t t1 = tail + 64 * 64 * 2;          //   [64 x 64] T1
+  static constexpr size_t g = tail + 2 * 64 * 64 * 2;       // fp32 [2][64] G (by sub-item parity)
+  static constexpr size_t beta = g + 2 * 64 * 4;            // fp32 [64]
+  static constexpr size_t part = beta + 64 * 4;             // fp32 [6][4][64] per-token partial sums (see kernel)
+  static constexpr size_t scr = part + 6 * 4 * 64 * 4;      // fp32 [2][4][64] exchange scratch
+  static constexpr size_t bar = scr + 2 * 4 * 64 * 4;
+  static constexpr int NBAR = 18;
+  static constexpr size_t tmem = bar + NBAR * 8;
   static constexpr size_t total = tmem + 16;
+  static_assert(dwt + DK * 64 * 2 <= in3, "dM and dW^T fit in the dVn region");
 };
 
-__device__ __forceinline__ void block_sync_ok(bool& ok) { ok = __syncthreads_and(ok); }
+// partial-sum arrays (index into ChunkSmem::part): by TMEM lane quadrant [4][64] unless noted
+enum { P_A = 0, P_KX = 1, P_VY = 2, P_E = 3, P_RECT = 4, P_PK = 5 /* by column quarter */ };
+
+__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 512;" ::: "memory"); }
+
+// every epilogue thread gets the AND of all epilogue threads' flags (keeps the 16 warps on one path)
+__device__ __forceinline__ bool epi_all(bool ok) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, 1, 512, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}\n"
+      : "=r"(r)
+      : "r"(ok ? 1u : 0u)
+      : "memory");
+  return r != 0;
+}
+
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void unpack8(uint4 u, float* x) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    x[2 * e] = __uint_as_float(w[e] << 16);
+    x[2 * e + 1] = __uint_as_float(w[e] & 0xffff0000u);
+  }
+}
+
+// columns c0 .. c0 + 15 of row r of a blocked [R x 64] image (shared or global), as floats; plus the low-half image
+template <bool LO>
+__device__ __forceinline__ void row16(const unsigned char* hi, const unsigned char* lo, int r, int c0, float (&x)[16]) {
+  unpack8(*reinterpret_cast<const uint4*>(hi + blk_off(r, c0, 64)), x);
+  unpack8(*reinterpret_cast<const uint4*>(hi + blk_off(r, c0 + 8, 64)), x + 8);
+  if (LO) {
+    float y[16];
+    unpack8(*reinterpret_cast<const uint4*>(lo + blk_off(r, c0, 64)), y);
+    unpack8(*reinterpret_cast<const uint4*>(lo + blk_off(r, c0 + 8, 64)), y + 8);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) x[j] += y[j];
+  }
+}
+
+struct Item {
+  int b, hk, c, r, h;
+  size_t cidx;   // this sub-item's chunk (value head h)
+  size_t cidx0;  // the chunk of the key head's first value head (its q / k images)
+};
+
+__device__ __forceinline__ Item item_of(const Layout& lay, int n) {
+  const int kk = n / lay.rep;
+  const int g = blockIdx.x + kk * gridDim.x;
+  Item it;
+  it.c = g % lay.NT;
+  const int bh = g / lay.NT;
+  it.hk = bh % lay.HK;
+  it.b = bh / lay.HK;
+  it.r = n - kk * lay.rep;
+  it.h = it.hk * lay.rep + it.r;
+  it.cidx = ((size_t)it.b * lay.H + it.h) * lay.NT + it.c;
+  it.cidx0 = ((size_t)it.b * lay.H + (size_t)it.hk * lay.rep) * lay.NT + it.c;
+  return it;
+}
 
 template <typename T, int DK, int DV>
-__global__ void __launch_bounds__(256) bwd_chunk_kernel(const T* __restrict__ qraw, const T* __restrict__ kraw,
-                                                        const T* __restrict__ vraw, const float* __restrict__ beta,
-                                                        const T* __restrict__ d_o, T* __restrict__ dq,
-                                                        T* __restrict__ dk, T* __restrict__ dv,
-                                                        float* __restrict__ dg, float* __restrict__ dbeta, Layout lay,
-                                                        int flags, unsigned char* __restrict__ ws) {
-  static_assert(DK == 128 && DV == 128, "the per-chunk kernel maps the head dimension onto the 128 TMEM lanes");
+__global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__ qraw, const T* __restrict__ kraw,
+                                                           const float* __restrict__ beta, T* __restrict__ dq,
+                                                           T* __restrict__ dk, T* __restrict__ dv,
+                                                           float* __restrict__ dg, float* __restrict__ dbeta,
+                                                           Layout lay, int flags, unsigned char* __restrict__ ws) {
+  static_assert(DK == 128 && DV == 128, "the head dimension maps onto the 128 TMEM lanes");
   using S = ChunkSmem<DK, DV>;
   extern __shared__ __align__(1024) unsigned char smem[];
   ErrorWord* err = reinterpret_cast<ErrorWord*>(ws + lay.err);
-  const int c = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int qd = warp & 3, half = warp >> 2;
-  const int dcol = 32 * qd + lane;   // head-dimension index this thread owns in [D x 64] accumulators
-  const int tok0 = 32 * half;        // its 32 tokens
-  const int rrow = 16 * qd + lane;   // its row in M = 64 accumulators (lane < 16)
-  const bool rowthr = lane < 16;
-  const int t0 = c * C;
-  float* sR = reinterpret_cast<float*>(smem + S::r);
-  float* sG = reinterpret_cast<float*>(smem + S::g);
-  float* sB = reinterpret_cast<float*>(smem + S::beta);
-  float* sPart = reinterpret_cast<float*>(smem + S::part);
-  float* sPk = reinterpret_cast<float*>(smem + S::pk);
-  float* sRed = reinterpret_cast<float*>(smem + S::red);
-  uint64_t* bar_mma = reinterpret_cast<uint64_t*>(smem + S::bar);
-  uint64_t* bar_qk = bar_mma + 1;
-  uint64_t* bar_g2 = bar_mma + 2;  // group 2 completes on its own barrier: its wait follows group 3's commit
-  uint64_t* bar_in = bar_mma + 3;  // phase-1 images of one value head
-  uint64_t* bar_ds = bar_mma + 4;  // dS images of one value head
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::bar);
+  uint64_t* in_full = bars + 0;    // IN1 + IN2 + IN3 + G of a sub-item (bulk-copy bytes)
+  uint64_t* a_full = bars + 1;
+  uint64_t* qk_full = bars + 2;    // once per item
+  uint64_t* ds_full = bars + 3;
+  uint64_t* g1_full = bars + 4;    // MMA commits
+  uint64_t* g3_full = bars + 5;
+  uint64_t* g2_full = bars + 6;
+  uint64_t* t1_full = bars + 7;
+  uint64_t* dl_full = bars + 8;
+  uint64_t* p11_full = bars + 9;
+  uint64_t* e1_done = bars + 10;   // 16 epilogue warps each
+  uint64_t* e2_done = bars + 11;
+  uint64_t* e3_done = bars + 12;
+  uint64_t* e4_done = bars + 13;
+  uint64_t* b5_free = bars + 14;
+  uint64_t* epi_done = bars + 15;  // [2] by sub-item parity
+  uint64_t* drain = bars + 17;
   uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + S::tmem);
-  const bool norm = (flags & GD_L2NORM) != 0;
-  const float qscale = (flags & GD_SCALE_Q) ? rsqrtf((float)DK) : 1.f;
+
+  const int NG = lay.B * lay.HK * lay.NT;
+  const int nsub = ((NG - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x) * lay.rep;
 
   if (warp == 0) {
     tmem_alloc(tslot, 512);
     tmem_relinquish();
   }
   if (tid == 0) {
-    mbar_init(bar_mma, 1);
-    mbar_init(bar_qk, 1);
-    mbar_init(bar_g2, 1);
-    mbar_init(bar_in, 1);
-    mbar_init(bar_ds, 1);
+    for (int i = 0; i < 10; ++i) mbar_init(bars + i, 1);
+    for (int i = 10; i < 17; ++i) mbar_init(bars + i, 16);
+    mbar_init(drain, 1);
     fence_mbar_init();
-  }
-  __syncthreads();
-  const size_t cidx0 = ((size_t)b * lay.H + (size_t)hk * lay.rep) * lay.NT + c;
-  if (tid == 0) {  // the q / k images are the same for every value head of this key head
-    mbar_arrive_expect_tx(bar_qk, 2 * (uint32_t)lay.qk_bytes());
-    bulk_g2s(smem + S::qk, ws + lay.qk + cidx0 * lay.qk_bytes(), (uint32_t)lay.qk_bytes(), bar_qk);
-    bulk_g2s(smem + S::qkl, ws + lay.qkl + cidx0 * lay.qk_bytes(), (uint32_t)lay.qk_bytes(), bar_qk);
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tm = *tslot;
-  // TMEM columns (each block 64 wide; reused once its reader is done)
-  const uint32_t T_DAK = tm + 0, T_DL = tm + 0;
-  const uint32_t T_DM = tm + 64;
-  const uint32_t T_DQA = tm + 128;
-  const uint32_t T_DW = tm + 192, T_X = tm + 192;
-  const uint32_t T_Y = tm + 256, T_DKA = tm + 256;
-  const uint32_t T_DAV = tm + 320, T_T1 = tm + 320, T_DKC = tm + 320;
-  const uint32_t T_DKS = tm + 384;
-  const uint32_t T_DQ = tm + 448;
+  const uint32_t B0 = tm, B1 = tm + 64, B2 = tm + 128, B3 = tm + 192, B4 = tm + 256, B5 = tm + 320, B6 = tm + 384,
+                 B7 = tm + 448;
 
-  // q / k images are transposed ([DK x 64], rows d): the K-major operand wherever d is a product's M or N
-  const Tile tQ{smem_u32(smem + S::qk), 64};
-  const Tile tK{smem_u32(smem + S::qk + 64 * DK * 2), 64};
-  const Tile tQl{smem_u32(smem + S::qkl), 64};
-  const Tile tKl{smem_u32(smem + S::qkl + 64 * DK * 2), 64};
-  // fp32 normalised q / k element (i, d) from the hi + lo images
-  auto qhat = [&](int i, int d) {
-    const int r = (i & 64) ? DK + d : d, cc = i & 63;  // token i of q (i < 64) or of k (i - 64)
-    return __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(smem + S::qk + blk_off(r, cc, 64))) +
-           __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(smem + S::qkl + blk_off(r, cc, 64)));
-  };
+  const Tile tQ{smem_u32(smem + S::qk), 64}, tK{smem_u32(smem + S::qk + DK * 64 * 2), 64};
+  const Tile tQl{smem_u32(smem + S::qkl), 64}, tKl{smem_u32(smem + S::qkl + DK * 64 * 2), 64};
   const Tile tA{smem_u32(smem + S::a), 64};
 
-  float dQacc[32], dKacc[32];  // d(normalised q / k)[token tok0 + j][dcol], summed over the value heads
-#pragma unroll
-  for (int j = 0; j < 32; ++j) dQacc[j] = dKacc[j] = 0.f;
-
-  uint32_t ph = 0;
-  GD_TRACE_AT(ws, lay, 0);
-  bool ok = mbar_wait(bar_qk, 0, err, 40);
-  block_sync_ok(ok);
-
-  for (int r = 0; r < lay.rep && ok; ++r) {
-    const int h = hk * lay.rep + r;
-    const size_t cidx = ((size_t)b * lay.H + h) * lay.NT + c;
-    // ---------------- phase 1: operand images (bulk copies; the previous value head's readers are done)
-    if (tid == 0) {
-      const uint32_t bytes = (uint32_t)(lay.m_bytes() + lay.si_bytes() + 2 * lay.vi_bytes() + 2 * lay.vn_bytes());
-      mbar_arrive_expect_tx(bar_in, bytes);
-      bulk_g2s(smem + S::a, ws + lay.ai + cidx * lay.m_bytes(), (uint32_t)lay.m_bytes(), bar_in);
-      bulk_g2s(smem + S::sc, ws + lay.sci + cidx * lay.si_bytes(), (uint32_t)lay.si_bytes(), bar_in);
-      bulk_g2s(smem + S::dO, ws + lay.doi + cidx * lay.vi_bytes(), (uint32_t)lay.vi_bytes(), bar_in);
-      bulk_g2s(smem + S::v, ws + lay.vi + cidx * lay.vi_bytes(), (uint32_t)lay.vi_bytes(), bar_in);
-      bulk_g2s(smem + S::vn, ws + lay.vni + cidx * lay.vn_bytes(), (uint32_t)lay.vn_bytes(), bar_in);
-      bulk_g2s(smem + S::dvn, ws + lay.dvni + cidx * lay.vn_bytes(), (uint32_t)lay.vn_bytes(), bar_in);
-    }
-    if (tid < 64) {
-      sG[tid] = reinterpret_cast<const float*>(ws + lay.gc + cidx * lay.gc_bytes())[tid];
-      const int t = t0 + tid;
-      sB[tid] = (t < lay.T) ? beta[((size_t)b * lay.T + t) * lay.H + h] : 0.f;
-    }
-    if (tid < 16) sRed[tid] = reinterpret_cast<const float*>(ws + lay.sl + cidx * 64)[tid];
-    ok = mbar_wait(bar_in, r & 1, err, 47);
-    block_sync_ok(ok);
-    if (!ok) break;
-    if (tid == 0) {
-      tc_fence_after();
-      const Tile tSc{smem_u32(smem + S::sc), DK}, tDO{smem_u32(smem + S::dO), DV}, tV{smem_u32(smem + S::v), 64};
-      const Tile tVn{smem_u32(smem + S::vn), 64}, tDVh{smem_u32(smem + S::dvn), 64}, tDVl{smem_u32(smem + S::dvnl), 64};
-      mma_tiles(T_DM, 64, 64, DV, tDO, true, 0, 0, tVn, true, 0, false);          // dO Vn^T
-      mma_tiles(T_DQA, DK, 64, DV, tSc, false, 0, 0, tDO, false, 0, false);       // S_c dO^T
-      mma_tiles(T_DW, DK, 64, DV, tSc, false, 0, 0, tDVh, true, 0, false);        // S_c dVn^T
-      mma_tiles(T_Y, DV, 64, 64, tDVh, true, 0, 0, tA, true, 0, false);           // dVn^T A (dVn split)
-      mma_tiles(T_Y, DV, 64, 64, tDVl, true, 0, 0, tA, true, 0, true);
-      mma_tiles(T_DAV, 64, 64, DV, tDVh, false, 0, 0, tV, true, 0, false);        // dVn V^T
-      mma_commit(bar_mma);
-    }
-    GD_TRACE_AT(ws, lay, 2);
-    ok = mbar_wait(bar_mma, ph, err, 41);
-    ph ^= 1;
-    block_sync_ok(ok);
-    if (!ok) break;
-    tc_fence_after();
-    GD_TRACE_AT(ws, lay, 3);
-    // ---------------- phase 2: dS^T images (over S_c / dO / V, whose readers are done), then (Vn dS^T)^T
-    if (tid == 0) {
-      mbar_arrive_expect_tx(bar_ds, 2 * (uint32_t)lay.si_bytes());
-      bulk_g2s(smem + S::dsh, ws + lay.dsi + cidx * 2 * lay.si_bytes(), 2 * (uint32_t)lay.si_bytes(), bar_ds);
-      if (mbar_wait(bar_ds, r & 1, err, 48)) {
-        const Tile tDh{smem_u32(smem + S::dsh), DK}, tDl{smem_u32(smem + S::dsl), DK};
-        const Tile tVh{smem_u32(smem + S::vn), 64}, tVl{smem_u32(smem + S::vnl), 64};
-        mma_tiles(T_DKS, DK, 64, DV, tDh, false, 0, 0, tVh, true, 0, false);
-        mma_tiles(T_DKS, DK, 64, DV, tDh, false, 0, 0, tVl, true, 0, true);
-        mma_tiles(T_DKS, DK, 64, DV, tDl, false, 0, 0, tVh, true, 0, true);
-      }
-      mma_commit(bar_g2);  // completes after a failed wait too; the error word is already set
-    }
-    GD_TRACE_AT(ws, lay, 4);
-    // epilogue of group 1 while group 2 runs
-    float s_last = 0.f;
-#pragma unroll
-    for (int w = 0; w < 16; ++w) s_last += sRed[w];
-    s_last *= __expf(sG[63]);
-    {
-      float acc[32];
-      // dW^T tile (rows dk, cols tokens), dW = -(S_c dVn^T)^T
-      tmem_ld32(tmem_lane_addr(T_DW, warp, tok0), acc);
-#pragma unroll
-      for (int jj = 0; jj < 32; ++jj) acc[jj] = -acc[jj];
-#pragma unroll
-      for (int q8 = 0; q8 < 4; ++q8) store8_bf16(smem + S::dwt, dcol, tok0 + 8 * q8, 64, acc + 8 * q8);
-      // a_t partial: gamma_t q_t . (dO S_c^T)_t over this thread's dk
-      tmem_ld32(tmem_lane_addr(T_DQA, warp, tok0), acc);
-#pragma unroll
-      for (int jj = 0; jj < 32; ++jj) {
-        const int i = tok0 + jj;
-        acc[jj] *= qhat(i, dcol);
-      }
-      sPart[(0 * 4 + qd) * 64 + tok0 + lane] = warp_reduce_scatter32(acc);
-      // Y = A^T dVn: dV = beta Y (written now) and the (v . Y) partial
-      tmem_ld32(tmem_lane_addr(T_Y, warp, tok0), acc);
-#pragma unroll
-      for (int jj = 0; jj < 32; ++jj) {
-        const int i = tok0 + jj, t = t0 + i;
-        float vv = 0.f;
-        if (t < lay.T) {
-          const size_t o = (((size_t)b * lay.T + t) * lay.H + h) * DV + dcol;
-          vv = to_f32<T>(vraw[o]);
-          dv[o] = from_f32<T>(sB[i] * acc[jj]);
+  if (warp == 17) {
+    // ---------------- bulk-copy issuer
+    if (lane == 0) {
+      bool ok = true;
+      int last_in = -1, last_a = -1, last_qk = -1, last_ds = -1;
+      const uint32_t in_bytes = (uint32_t)(lay.si_bytes() + 2 * lay.vi_bytes() + 2 * lay.vn_bytes() + lay.gc_bytes());
+      for (int n = 0; n < nsub && ok; ++n) {
+        const Item it = item_of(lay, n);
+        if (n >= 1) ok = mbar_wait(g3_full, (n - 1) & 1, err, 60);  // dM / dW^T (the IN2 region) consumed
+        if (!ok) break;
+        mbar_arrive_expect_tx(in_full, in_bytes);
+        last_in = n;
+        bulk_g2s(smem + S::in2, ws + lay.dvni + it.cidx * lay.vn_bytes(), (uint32_t)lay.vn_bytes(), in_full);
+        if (n >= 1) ok = mbar_wait(g2_full, (n - 1) & 1, err, 61);                // dS^T and Vn^T consumed
+        if (ok && n >= 2) ok = mbar_wait(epi_done + (n & 1), ((n - 2) >> 1) & 1, err, 62);  // G buffer n & 1 read
+        if (!ok) break;
+        bulk_g2s(smem + S::sc, ws + lay.sci + it.cidx * lay.si_bytes(), (uint32_t)lay.si_bytes(), in_full);
+        bulk_g2s(smem + S::dO, ws + lay.doi + it.cidx * lay.vi_bytes(), (uint32_t)lay.vi_bytes(), in_full);
+        bulk_g2s(smem + S::vt, ws + lay.vi + it.cidx * lay.vi_bytes(), (uint32_t)lay.vi_bytes(), in_full);
+        bulk_g2s(smem + S::in3, ws + lay.vni + it.cidx * lay.vn_bytes(), (uint32_t)lay.vn_bytes(), in_full);
+        bulk_g2s(smem + S::g + (n & 1) * 256, ws + lay.gc + it.cidx * lay.gc_bytes(), (uint32_t)lay.gc_bytes(),
+                 in_full);
+        prefetch_l2(ws + lay.mf + it.cidx * lay.cc_bytes(), (uint32_t)lay.cc_bytes());
+        prefetch_l2(ws + lay.kg + it.cidx * lay.cc_bytes(), (uint32_t)lay.cc_bytes());
+        if (n >= 1) ok = mbar_wait(dl_full, (n - 1) & 1, err, 63);  // A consumed
+        if (!ok) break;
+        mbar_arrive_expect_tx(a_full, (uint32_t)lay.m_bytes());
+        last_a = n;
+        bulk_g2s(smem + S::a, ws + lay.ai + it.cidx * lay.m_bytes(), (uint32_t)lay.m_bytes(), a_full);
+        if (it.r == 0) {
+          if (n >= 1) ok = mbar_wait(p11_full, (n - 1) & 1, err, 64);  // the previous item's q / k consumed
+          if (!ok) break;
+          mbar_arrive_expect_tx(qk_full, 2 * (uint32_t)lay.qk_bytes());
+          last_qk = n / lay.rep;
+          bulk_g2s(smem + S::qk, ws + lay.qk + it.cidx0 * lay.qk_bytes(), (uint32_t)lay.qk_bytes(), qk_full);
+          bulk_g2s(smem + S::qkl, ws + lay.qkl + it.cidx0 * lay.qk_bytes(), (uint32_t)lay.qk_bytes(), qk_full);
         }
-        acc[jj] *= vv;
+        ok = mbar_wait(g1_full, n & 1, err, 65);  // S_c^T, dO, V^T consumed: dS^T goes over them
+        if (!ok) break;
+        mbar_arrive_expect_tx(ds_full, 2 * (uint32_t)lay.si_bytes());
+        last_ds = n;
+        bulk_g2s(smem + S::dsh, ws + lay.dsi + it.cidx * 2 * lay.si_bytes(), 2 * (uint32_t)lay.si_bytes(), ds_full);
       }
-      sPart[(2 * 4 + qd) * 64 + tok0 + lane] = warp_reduce_scatter32(acc);
-    }
-    {
-      // dM = Gamma * (dO Vn^T) (lower with the diagonal) -> hi / lo tiles
-      float acc[32];
-      tmem_ld32(tmem_lane_addr(T_DM, warp, tok0), acc);
-      if (rowthr) {
-        const int i = rrow;
-        const float Gi = sG[i];
-        float dm[32];
-#pragma unroll
-        for (int jj = 0; jj < 32; ++jj) {
-          const int j = tok0 + jj;
-          dm[jj] = (j <= i) ? acc[jj] * __expf(Gi - sG[j]) : 0.f;
-        }
-#pragma unroll
-        for (int q8 = 0; q8 < 4; ++q8) store8_split(smem + S::dmh, smem + S::dml, i, tok0 + 8 * q8, 64, dm + 8 * q8);
-      }
-    }
-    fence_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    if (tid == 0) {
-      tc_fence_after();
-      const Tile tDMh{smem_u32(smem + S::dmh), 64}, tDMl{smem_u32(smem + S::dml), 64}, tDW{smem_u32(smem + S::dwt), 64};
-      mma_tiles(T_DQ, DK, 64, 64, tK, true, 0, 0, tDMh, false, 0, false);       // (dM K)^T = K^T dM^T
-      mma_tiles(T_DQ, DK, 64, 64, tKl, true, 0, 0, tDMh, false, 0, true);
-      mma_tiles(T_DQ, DK, 64, 64, tK, true, 0, 0, tDMl, false, 0, true);
-      mma_tiles(T_DKA, DK, 64, 64, tQ, true, 0, 0, tDMh, true, 0, false);       // (dM^T Q)^T = Q^T dM
-      mma_tiles(T_DKA, DK, 64, 64, tQl, true, 0, 0, tDMh, true, 0, true);
-      mma_tiles(T_DKA, DK, 64, 64, tQ, true, 0, 0, tDMl, true, 0, true);
-      mma_tiles(T_X, DK, 64, 64, tDW, true, 0, 0, tA, true, 0, false);          // (A^T dW)^T = dW^T A
-      mma_tiles(T_DAK, 64, 64, DK, tDW, false, 0, 0, tK, true, 0, false);       // dW K^T
-      mma_commit(bar_mma);
-    }
-    GD_TRACE_AT(ws, lay, 5);
-    ok = mbar_wait(bar_g2, r & 1, err, 42);  // group 2 (one phase per value head)
-    if (ok) ok = mbar_wait(bar_mma, ph, err, 43);  // group 3
-    ph ^= 1;
-    block_sync_ok(ok);
-    if (!ok) break;
-    tc_fence_after();
-    GD_TRACE_AT(ws, lay, 6);
-    // ---------------- phase 3: E, k.X partials; dA
-    {
-      float acc[32], kx[32];
-      tmem_ld32(tmem_lane_addr(T_DKS, warp, tok0), acc);
-      tmem_ld32(tmem_lane_addr(T_X, warp, tok0), kx);
-      const float Glast = sG[63];
-#pragma unroll
-      for (int jj = 0; jj < 32; ++jj) {
-        const int i = tok0 + jj;
-        const float kv = qhat(64 + i, dcol);
-        acc[jj] *= __expf(Glast - sG[i]) * kv;
-        kx[jj] *= kv;
-      }
-      sPart[(3 * 4 + qd) * 64 + tok0 + lane] = warp_reduce_scatter32(acc);
-      sPart[(1 * 4 + qd) * 64 + tok0 + lane] = warp_reduce_scatter32(kx);
-      // R = dM * (Q K^T) = (dO Vn^T) * M, strictly lower (M from the prep kernel, fp32, mask included)
-      tmem_ld32(tmem_lane_addr(T_DM, warp, tok0), acc);
-      if (rowthr) {
-        const int i = rrow;
-        const float* mrow = reinterpret_cast<const float*>(ws + lay.mf + cidx * lay.cc_bytes()) + i * 64 + tok0;
-#pragma unroll
-        for (int jj = 0; jj < 32; ++jj) {
-          const int j = tok0 + jj;
-          sR[cc_idx(i, j)] = (j < i) ? acc[jj] * mrow[jj] : 0.f;
-        }
-      }
-      // dA = strict_lower(beta_j gamma_j (dW K^T) + beta_j (dVn V^T)) -> bf16 tile
-      float ak[32], av[32];
-      tmem_ld32(tmem_lane_addr(T_DAK, warp, tok0), ak);
-      tmem_ld32(tmem_lane_addr(T_DAV, warp, tok0), av);
-      if (rowthr) {
-        const int i = rrow;
-        float da[32];
-#pragma unroll
-        for (int jj = 0; jj < 32; ++jj) {
-          const int j = tok0 + jj;
-          da[jj] = (j < i) ? sB[j] * fmaf(__expf(sG[j]), ak[jj], av[jj]) : 0.f;
-        }
-#pragma unroll
-        for (int q8 = 0; q8 < 4; ++q8) store8_bf16(smem + S::da, i, tok0 + 8 * q8, 64, da + 8 * q8);
-      }
-    }
-    fence_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    if (tid == 0) {
-      tc_fence_after();
-      mma_tiles(T_T1, 64, 64, 64, Tile{smem_u32(smem + S::da), 64}, true, 0, 0, tA, false, 0, false);  // dA A^T
-      mma_commit(bar_mma);
-    }
-    GD_TRACE_AT(ws, lay, 7);
-    ok = mbar_wait(bar_mma, ph, err, 44);
-    ph ^= 1;
-    block_sync_ok(ok);
-    if (!ok) break;
-    tc_fence_after();
-    {
-      float acc[32];
-      tmem_ld32(tmem_lane_addr(T_T1, warp, tok0), acc);
-      if (rowthr) {
-#pragma unroll
-        for (int q8 = 0; q8 < 4; ++q8) store8_bf16(smem + S::t1, rrow, tok0 + 8 * q8, 64, acc + 8 * q8);
-      }
-    }
-    fence_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    if (tid == 0) {
-      tc_fence_after();
-      mma_tiles(T_DL, 64, 64, 64, tA, false, 0, 0, Tile{smem_u32(smem + S::t1), 64}, true, 0, false);  // A^T T1
-      mma_commit(bar_mma);
-    }
-    GD_TRACE_AT(ws, lay, 8);
-    ok = mbar_wait(bar_mma, ph, err, 45);
-    ph ^= 1;
-    block_sync_ok(ok);
-    if (!ok) break;
-    tc_fence_after();
-    {
-      // dL = -(A^T T1), strictly lower; L = beta_i KG_ij Gamma_ij; R += dL L; P = dL Gamma; P_beta = beta_i P
-      float acc[32];
-      float* sPB = reinterpret_cast<float*>(smem + S::pb);
-      tmem_ld32(tmem_lane_addr(T_DL, warp, tok0), acc);
-      if (rowthr) {
-        const int i = rrow;
-        const float Gi = sG[i], bi = sB[i];
-        const float* kgrow = reinterpret_cast<const float*>(ws + lay.kg + cidx * lay.cc_bytes()) + i * 64 + tok0;
-        float pk = 0.f;
-#pragma unroll
-        for (int jj = 0; jj < 32; ++jj) {
-          const int j = tok0 + jj;
-          const int ci = cc_idx(i, j);
-          float pb = 0.f;
-          if (j < i) {
-            const float dl = -acc[jj];
-            const float gam = __expf(Gi - sG[j]);
-            const float kg = kgrow[jj];
-            const float P = dl * gam;
-            sR[ci] += dl * bi * kg * gam;
-            pk = fmaf(P, kg, pk);
-            pb = bi * P;
+      if (!ok) {  // let copies already issued land before the CTA can exit (short bound, no second report)
+        const long long t0 = clock64();
+        auto settle = [&](uint64_t* bar, int phase) {
+          if (phase < 0) return;
+          while (!mbar_try_wait(bar, phase & 1) && clock64() - t0 < 20000000ll) {
           }
-          sPB[ci] = pb;
-        }
-        sPk[half * 64 + i] = pk;
+        };
+        settle(in_full, last_in);
+        settle(a_full, last_a);
+        settle(qk_full, last_qk);
+        settle(ds_full, last_ds);
       }
     }
-    __syncthreads();
-    {
-      // Z = P_beta + P_beta^T -> bf16 tile (rows i, cols j)
-      const float* sPB = reinterpret_cast<const float*>(smem + S::pb);
-      for (int idx = tid; idx < 64 * 8; idx += 256) {
-        const int rl = idx & 7, cb = (idx >> 3) & 7, rb = idx >> 6;
-        const int i = 8 * rb + rl;
-        float zz[8];
+    __syncwarp();
+  } else if (warp == 16) {
+    // ---------------- MMA issuer: per sub-item n, in dependency order, whichever is ready first
+    if (lane == 0) {
+      const Tile tSc{smem_u32(smem + S::sc), DK}, tDO{smem_u32(smem + S::dO), DV}, tVt{smem_u32(smem + S::vt), 64};
+      const Tile tDvh{smem_u32(smem + S::dvh), 64}, tDvl{smem_u32(smem + S::dvl), 64};
+      const Tile tVnh{smem_u32(smem + S::vnh), 64}, tVnl{smem_u32(smem + S::vnl), 64};
+      const Tile tDsh{smem_u32(smem + S::dsh), DK}, tDsl{smem_u32(smem + S::dsl), DK};
+      const Tile tDmh{smem_u32(smem + S::dmh), 64}, tDml{smem_u32(smem + S::dml), 64};
+      const Tile tDwt{smem_u32(smem + S::dwt), 64};
+      const Tile tDa{smem_u32(smem + S::da), 64}, tT1{smem_u32(smem + S::t1), 64};
+      auto issue_g1 = [&]() {
+        mma_tiles(B0, 64, 64, DV, tDO, true, 0, 0, tVnh, true, 0, false);    // dO Vn^T
+        mma_tiles(B1, DK, 64, DV, tSc, false, 0, 0, tDO, false, 0, false);   // S dO^T
+        mma_tiles(B2, DK, 64, DV, tSc, false, 0, 0, tDvh, true, 0, false);   // S dVn^T
+        mma_tiles(B3, DV, 64, 64, tDvh, true, 0, 0, tA, true, 0, false);     // dVn^T A
+        mma_tiles(B3, DV, 64, 64, tDvl, true, 0, 0, tA, true, 0, true);
+        mma_tiles(B4, 64, 64, DV, tDvh, false, 0, 0, tVt, true, 0, false);   // dVn V^T
+        mma_commit(g1_full);
+      };
+      bool ok = nsub > 0;
+      if (ok) ok = mbar_wait(in_full, 0, err, 70) && mbar_wait(a_full, 0, err, 71);
+      if (ok) {
+        tc_fence_after();
+        issue_g1();
+      }
+      for (int n = 0; n < nsub && ok; ++n) {
+        const uint32_t par = n & 1;
+        const uint32_t qpar = (n / lay.rep) & 1;
+        bool g3 = false, g2 = false, t1 = false, dl = false, p11 = false, g1n = (n + 1 >= nsub);
+        long long t0 = clock64();
+        while (!(g3 && g2 && t1 && dl && p11 && g1n)) {
+          bool progressed = false;
+          if (!g3 && mbar_try_wait(e1_done, par) && mbar_try_wait(qk_full, qpar)) {
+            tc_fence_after();
+            mma_tiles(B6, DK, 64, 64, tK, true, 0, 0, tDmh, false, 0, false);    // (dM K)^T = K^T dM^T
+            mma_tiles(B6, DK, 64, 64, tKl, true, 0, 0, tDmh, false, 0, true);
+            mma_tiles(B6, DK, 64, 64, tK, true, 0, 0, tDml, false, 0, true);
+            mma_tiles(B7, DK, 64, 64, tQ, true, 0, 0, tDmh, true, 0, false);     // (dM^T Q)^T = Q^T dM
+            mma_tiles(B7, DK, 64, 64, tQl, true, 0, 0, tDmh, true, 0, true);
+            mma_tiles(B7, DK, 64, 64, tQ, true, 0, 0, tDml, true, 0, true);
+            mma_tiles(B2, DK, 64, 64, tDwt, true, 0, 0, tA, true, 0, false);     // (A^T dW)^T = dW^T A
+            mma_tiles(B1, 64, 64, DK, tDwt, false, 0, 0, tK, true, 0, false);    // dW K^T
+            mma_commit(g3_full);
+            g3 = progressed = true;
+          }
+          if (!g2 && mbar_try_wait(ds_full, par) && (n == 0 || mbar_try_wait(b5_free, (n - 1) & 1))) {
+            tc_fence_after();
+            mma_tiles(B5, DK, 64, DV, tDsh, false, 0, 0, tVnh, true, 0, false);  // (Vn dS^T)^T = dS Vn^T
+            mma_tiles(B5, DK, 64, DV, tDsh, false, 0, 0, tVnl, true, 0, true);
+            mma_tiles(B5, DK, 64, DV, tDsl, false, 0, 0, tVnh, true, 0, true);
+            mma_commit(g2_full);
+            g2 = progressed = true;
+          }
+          if (g3 && !t1 && mbar_try_wait(e2_done, par)) {
+            tc_fence_after();
+            mma_tiles(B6, 64, 64, 64, tDa, true, 0, 0, tA, false, 0, false);     // T1 = dA A^T
+            mma_commit(t1_full);
+            t1 = progressed = true;
+          }
+          if (t1 && !dl && mbar_try_wait(e3_done, par)) {
+            tc_fence_after();
+            mma_tiles(B7, 64, 64, 64, tA, false, 0, 0, tT1, true, 0, false);     // A^T T1
+            mma_commit(dl_full);
+            dl = progressed = true;
+          }
+          if (t1 && !g1n && mbar_try_wait(in_full, par ^ 1) && mbar_try_wait(a_full, par ^ 1)) {
+            tc_fence_after();
+            issue_g1();  // the next sub-item's first products (B0-B4 were read before e2_done)
+            g1n = progressed = true;
+          }
+          if (dl && g2 && !p11 && mbar_try_wait(e4_done, par)) {
+            tc_fence_after();
+            mma_tiles(B5, DK, 64, 64, tK, true, 0, 0, tDa, true, 0, false);      // K^T P_beta
+            mma_tiles(B5, DK, 64, 64, tK, true, 0, 0, tDa, false, 0, true);      //  + K^T P_beta^T
+            mma_commit(p11_full);
+            p11 = progressed = true;
+          }
+          if (progressed) {
+            t0 = clock64();
+          } else if (clock64() - t0 > kWaitCycles) {
+            report(err, GD_ERR_TIMEOUT, 72 + (g3 ? 1 : 0) + (g2 ? 2 : 0) + (t1 ? 4 : 0) + (dl ? 8 : 0));
+            ok = false;
+            break;
+          }
+        }
+      }
+      // every MMA issued has completed before TMEM is freed
+      mma_commit(drain);
+      mbar_wait(drain, 0, err, 99);
+    }
+    __syncwarp();
+  } else {
+    // ---------------- epilogue warps
+    const int qd = warp & 3, quarter = warp >> 2;
+    const int dcol = 32 * qd + lane;  // head-dimension row of the [D x 64] accumulators
+    const int tok0 = 16 * quarter;    // their 16 token columns / the C x C columns of this warp
+    const int ri = 16 * qd + lane;    // C x C row (lanes 0-15)
+    const bool rowthr = lane < 16;
+    float* sB = reinterpret_cast<float*>(smem + S::beta);
+    float* part = reinterpret_cast<float*>(smem + S::part);
+    float* scr = reinterpret_cast<float*>(smem + S::scr);
+    auto P = [&](int which, int row, int t) -> float& { return part[(which * 4 + row) * 64 + t]; };
+    const bool norm = (flags & GD_L2NORM) != 0;
+    const float qscale = (flags & GD_SCALE_Q) ? rsqrtf((float)DK) : 1.f;
+    const unsigned char* qh = smem + S::qk;
+    const unsigned char* ql = smem + S::qkl;
+    const unsigned char* kh = smem + S::qk + DK * 64 * 2;
+    const unsigned char* kl = smem + S::qkl + DK * 64 * 2;
+
+    // rect_t += sum_{i >= t} sum_{j < t} R_ij for this warp's columns t, from R's row segments rv (row ri, columns
+    // tok0 .. tok0 + 15; zero off the rows): quarter row totals through scr, exclusive row prefixes, masked row sums
+    auto rect = [&](const float (&rv)[16], bool init) {
+      float tot = 0.f;
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const int j = 8 * cb + e;
-          zz[e] = sPB[cc_idx(i, j)] + sPB[cc_idx(j, i)];
-        }
-        store8_bf16(smem + S::z, i, 8 * cb, 64, zz);
-      }
-    }
-    fence_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    if (tid == 0) {
-      tc_fence_after();
-      mma_tiles(T_DKC, DK, 64, 64, tK, true, 0, 0, Tile{smem_u32(smem + S::z), 64}, false, 0, false);  // K^T Z^T
-      mma_commit(bar_mma);
-    }
-    GD_TRACE_AT(ws, lay, 9);
-    // rect_t = sum_{i >= t} sum_{j < t} R_ij while the tensor core works: row prefixes in place, then column suffixes
-    if (tid < 64) {
-      const int i = tid;
+      for (int j = 0; j < 16; ++j) tot += rv[j];
+      if (rowthr) scr[quarter * 64 + ri] = tot;
+      epi_sync();
       float run = 0.f;
-      for (int j = 0; j < 64; ++j) {
-        const int ci = cc_idx(i, j);
-        const float x = sR[ci];
-        sR[ci] = run;  // sum_{j' < j} R_ij'
-        run += x;
+      for (int q2 = 0; q2 < quarter; ++q2) run += rowthr ? scr[q2 * 64 + ri] : 0.f;
+      float v[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        v[j] = (rowthr && ri >= tok0 + j) ? run : 0.f;
+        run += rv[j];
       }
+      const float s = warp_reduce_scatter16(v);
+      if (lane < 16) P(P_RECT, qd, tok0 + lane) = init ? s : P(P_RECT, qd, tok0 + lane) + s;
+    };
+
+    float dQ[16], dK[16];  // d(normalised q / k)[token tok0 + j][dcol], summed over the item's value heads
+#pragma unroll
+    for (int j = 0; j < 16; ++j) dQ[j] = dK[j] = 0.f;
+    if (nsub > 0 && tid < 64) {
+      const Item it = item_of(lay, 0);
+      const int t = it.c * C + tid;
+      sB[tid] = (t < lay.T) ? beta[((size_t)it.b * lay.T + t) * lay.H + it.h] : 0.f;
     }
-    ok = mbar_wait(bar_mma, ph, err, 46);
-    ph ^= 1;
-    block_sync_ok(ok);
-    if (!ok) break;
-    tc_fence_after();
-    GD_TRACE_AT(ws, lay, 10);
-    // ---------------- phase 4: dQ, dK of this value head; dg and dbeta
-    {
-      float a[32], bq[32];
-      tmem_ld32(tmem_lane_addr(T_DQA, warp, tok0), a);
-      tmem_ld32(tmem_lane_addr(T_DQ, warp, tok0), bq);
+    epi_sync();
+    bool ok = true;
+    for (int n = 0; n < nsub; ++n) {
+      const Item it = item_of(lay, n);
+      const uint32_t par = n & 1;
+      const int t0 = it.c * C;
+      const float* sG = reinterpret_cast<const float*>(smem + S::g + (n & 1) * 256);
+      // ---- e1: dW^T and dM tiles, dQ's first term and the a partials
+      ok = mbar_wait(in_full, par, err, 80) && mbar_wait(g1_full, par, err, 81);
+      if (!(ok = epi_all(ok))) break;
+      tc_fence_after();
+      GD_TRACE_AT(ws, lay, 16 * n + 0);
+      float av[16];
+      {
+        float x[16];
+        tmem_ld16(tmem_lane_addr(B2, warp, tok0), x);
 #pragma unroll
-      for (int jj = 0; jj < 32; ++jj) dQacc[jj] += fmaf(__expf(sG[tok0 + jj]), a[jj], bq[jj]);
-      float ka[32], ks[32];
-      tmem_ld32(tmem_lane_addr(T_DKA, warp, tok0), ka);
-      tmem_ld32(tmem_lane_addr(T_DKS, warp, tok0), ks);
-      const float Glast = sG[63];
+        for (int j = 0; j < 16; ++j) x[j] = -x[j];
+        store8_bf16(smem + S::dwt, dcol, tok0, 64, x);
+        store8_bf16(smem + S::dwt, dcol, tok0 + 8, 64, x + 8);
+        tmem_ld16(tmem_lane_addr(B0, warp, tok0), x);
+        if (rowthr) {
+          const float Gi = sG[ri];
 #pragma unroll
-      for (int jj = 0; jj < 32; ++jj) dKacc[jj] += fmaf(__expf(Glast - sG[tok0 + jj]), ks[jj], ka[jj]);
-      tmem_ld32(tmem_lane_addr(T_X, warp, tok0), ka);
-      tmem_ld32(tmem_lane_addr(T_DKC, warp, tok0), ks);
-#pragma unroll
-      for (int jj = 0; jj < 32; ++jj) {
-        const int i = tok0 + jj;
-        dKacc[jj] += fmaf(sB[i] * __expf(sG[i]), ka[jj], ks[jj]);
-      }
-    }
-    if (tid < 64) {
-      const int t = tid;
-      float rect = 0.f;
-      for (int i = t; i < 64; ++i) rect += sR[cc_idx(i, t)];
-      const float a = __expf(sG[t]) * (sPart[(0 * 4 + 0) * 64 + t] + sPart[(0 * 4 + 1) * 64 + t] +
-                                        sPart[(0 * 4 + 2) * 64 + t] + sPart[(0 * 4 + 3) * 64 + t]);
-      const float kx = sPart[(1 * 4 + 0) * 64 + t] + sPart[(1 * 4 + 1) * 64 + t] + sPart[(1 * 4 + 2) * 64 + t] +
-                       sPart[(1 * 4 + 3) * 64 + t];
-      const float vy = sPart[(2 * 4 + 0) * 64 + t] + sPart[(2 * 4 + 1) * 64 + t] + sPart[(2 * 4 + 2) * 64 + t] +
-                       sPart[(2 * 4 + 3) * 64 + t];
-      const float E = sPart[(3 * 4 + 0) * 64 + t] + sPart[(3 * 4 + 1) * 64 + t] + sPart[(3 * 4 + 2) * 64 + t] +
-                      sPart[(3 * 4 + 3) * 64 + t];
-      const float gt = __expf(sG[t]);
-      const float w = sB[t] * gt * kx;
-      const float db = gt * kx + vy + sPk[t] + sPk[64 + t];
-      // suffix sum of (a + w) over the chunk (64 tokens in two warps), exclusive prefix of E
-      float aw = a + w;
-      float suf = aw, pre = E;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const float y = __shfl_down_sync(0xffffffffu, suf, o);
-        if (lane + o < 32) suf += y;
-        const float z = __shfl_up_sync(0xffffffffu, pre, o);
-        if (lane >= o) pre += z;
-      }
-      // combine the two warps: warp 0 adds warp 1's total suffix; warp 1 adds warp 0's total prefix. The exclusive
-      // prefix is the inclusive one shifted by a lane (never inclusive minus E: that would cancel)
-      if (lane == 0 && warp == 1) sPart[4 * 4 * 64 + 0] = suf;   // warp 1's full sum of (a + w)
-      if (lane == 31 && warp == 0) sPart[4 * 4 * 64 + 1] = pre;  // warp 0's full sum of E
-      float pre_excl = __shfl_up_sync(0xffffffffu, pre, 1);
-      if (lane == 0) pre_excl = 0.f;
-      asm volatile("bar.sync 1, 64;" ::: "memory");
-      if (warp == 0) suf += sPart[4 * 4 * 64 + 0];
-      if (warp == 1) pre_excl += sPart[4 * 4 * 64 + 1];
-      const float dgt = suf + s_last + pre_excl + rect;
-      const int tt = t0 + t;
-      if (tt < lay.T) {
-        dg[((size_t)b * lay.T + tt) * lay.H + h] = dgt;
-        dbeta[((size_t)b * lay.T + tt) * lay.H + h] = db;
-      }
-    }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-  }
-  if (ok) {
-    // l2 prologue backward (src/macai/gated_delta/_norm.py:6-9): dx = scale r (dy - x_hat (x_hat . dy))
-    float xq[32], xk[32], pq[32], pk_[32];
-    float rq[32], rk[32];
-#pragma unroll
-    for (int jj = 0; jj < 32; ++jj) {
-      const int t = t0 + tok0 + jj;
-      const bool valid = t < lay.T;
-      const size_t o = (((size_t)b * lay.T + (valid ? t : 0)) * lay.HK + hk) * DK + dcol;
-      const size_t ro = ((size_t)b * lay.T + (valid ? t : 0)) * lay.HK + hk;
-      rq[jj] = (norm && valid) ? reinterpret_cast<const float*>(ws + lay.rq)[ro] : 1.f;
-      rk[jj] = (norm && valid) ? reinterpret_cast<const float*>(ws + lay.rk)[ro] : 1.f;
-      xq[jj] = valid ? to_f32<T>(qraw[o]) * rq[jj] : 0.f;
-      xk[jj] = valid ? to_f32<T>(kraw[o]) * rk[jj] : 0.f;
-      pq[jj] = xq[jj] * dQacc[jj];
-      pk_[jj] = xk[jj] * dKacc[jj];
-    }
-    float* sDot = sPart;  // reuse: [2][4][64]
-    __syncthreads();
-    sDot[(0 * 4 + qd) * 64 + tok0 + lane] = warp_reduce_scatter32(pq);
-    sDot[(1 * 4 + qd) * 64 + tok0 + lane] = warp_reduce_scatter32(pk_);
-    __syncthreads();
-#pragma unroll
-    for (int jj = 0; jj < 32; ++jj) {
-      const int i = tok0 + jj, t = t0 + i;
-      if (t < lay.T) {
-        const size_t o = (((size_t)b * lay.T + t) * lay.HK + hk) * DK + dcol;
-        float gq, gk;
-        if (norm) {
-          const float dotq = sDot[0 * 64 + i] + sDot[1 * 64 + i] + sDot[2 * 64 + i] + sDot[3 * 64 + i];
-          const float dotk = sDot[4 * 64 + i] + sDot[5 * 64 + i] + sDot[6 * 64 + i] + sDot[7 * 64 + i];
-          gq = qscale * rq[jj] * (dQacc[jj] - xq[jj] * dotq);
-          gk = rk[jj] * (dKacc[jj] - xk[jj] * dotk);
-        } else {
-          gq = qscale * dQacc[jj];
-          gk = dKacc[jj];
+          for (int j = 0; j < 16; ++j) x[j] = (tok0 + j <= ri) ? x[j] * __expf(Gi - sG[tok0 + j]) : 0.f;
+          store8_split(smem + S::dmh, smem + S::dml, ri, tok0, 64, x);
+          store8_split(smem + S::dmh, smem + S::dml, ri, tok0 + 8, 64, x + 8);
         }
-        dq[o] = from_f32<T>(gq);
-        dk[o] = from_f32<T>(gk);
+        tmem_ld16(tmem_lane_addr(B1, warp, tok0), av);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          av[j] *= __expf(sG[tok0 + j]);  // gamma_t (dO S^T)_t
+          dQ[j] += av[j];
+        }
       }
+      tc_fence_before();
+      fence_async_smem();
+      mbar_arrive_warp(e1_done);
+      ok = mbar_wait(qk_full, (n / lay.rep) & 1, err, 82);
+      if (!(ok = epi_all(ok))) break;
+      {
+        float x[16];
+        row16<true>(qh, ql, dcol, tok0, x);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) av[j] *= x[j];
+        const float s = warp_reduce_scatter16(av);
+        if (lane < 16) P(P_A, qd, tok0 + lane) = s;
+      }
+      // ---- e2: dV, dQ / dK terms, dA (and R's first term)
+      ok = mbar_wait(g3_full, par, err, 83);
+      if (!(ok = epi_all(ok))) break;
+      tc_fence_after();
+      GD_TRACE_AT(ws, lay, 16 * n + 1);
+      float mrow[16];
+      if (rowthr) {
+        const float4* m4 = reinterpret_cast<const float4*>(ws + lay.mf + it.cidx * lay.cc_bytes()) + (ri * 64 + tok0) / 4;
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          const float4 u = __ldg(m4 + q4);
+          mrow[4 * q4] = u.x, mrow[4 * q4 + 1] = u.y, mrow[4 * q4 + 2] = u.z, mrow[4 * q4 + 3] = u.w;
+        }
+      }
+      {
+        float y[16], x[16];
+        tmem_ld16(tmem_lane_addr(B3, warp, tok0), y);  // Y^T: dV = diag(beta) Y, and v . Y
+        row16<false>(ws + lay.vi + it.cidx * lay.vi_bytes(), nullptr, dcol, tok0, x);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int t = t0 + tok0 + j;
+          if (t < lay.T) dv[(((size_t)it.b * lay.T + t) * lay.H + it.h) * DV + dcol] = from_f32<T>(sB[tok0 + j] * y[j]);
+          y[j] *= x[j];
+        }
+        float s = warp_reduce_scatter16(y);
+        if (lane < 16) P(P_VY, qd, tok0 + lane) = s;
+        tmem_ld16(tmem_lane_addr(B6, warp, tok0), x);  // (dM K)^T
+#pragma unroll
+        for (int j = 0; j < 16; ++j) dQ[j] += x[j];
+        tmem_ld16(tmem_lane_addr(B7, warp, tok0), x);  // (dM^T Q)^T
+#pragma unroll
+        for (int j = 0; j < 16; ++j) dK[j] += x[j];
+        tmem_ld16(tmem_lane_addr(B2, warp, tok0), x);  // X^T
+        row16<true>(kh, kl, dcol, tok0, y);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int i = tok0 + j;
+          dK[j] = fmaf(sB[i] * __expf(sG[i]), x[j], dK[j]);
+          y[j] *= x[j];
+        }
+        s = warp_reduce_scatter16(y);
+        if (lane < 16) P(P_KX, qd, tok0 + lane) = s;
+      }
+      float rv[16];
+      {
+        float a10[16], a5[16];
+        tmem_ld16(tmem_lane_addr(B1, warp, tok0), a10);  // dW K^T
+        tmem_ld16(tmem_lane_addr(B4, warp, tok0), a5);   // dVn V^T
+        if (rowthr) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int jj = tok0 + j;
+            a10[j] = (jj < ri) ? sB[jj] * fmaf(__expf(sG[jj]), a10[j], a5[j]) : 0.f;
+          }
+          store8_bf16(smem + S::da, ri, tok0, 64, a10);
+          store8_bf16(smem + S::da, ri, tok0 + 8, 64, a10 + 8);
+        }
+        tmem_ld16(tmem_lane_addr(B0, warp, tok0), a5);  // dO Vn^T again: R's first term (dO Vn^T) * M
+#pragma unroll
+        for (int j = 0; j < 16; ++j) rv[j] = (rowthr && tok0 + j < ri) ? a5[j] * mrow[j] : 0.f;
+      }
+      tc_fence_before();
+      fence_async_smem();
+      mbar_arrive_warp(e2_done);
+      rect(rv, true);
+      // ---- eg2: (Vn dS^T)^T -> dK's decay-path term and the E partials
+      ok = mbar_wait(g2_full, par, err, 84);
+      if (!(ok = epi_all(ok))) break;
+      tc_fence_after();
+      GD_TRACE_AT(ws, lay, 16 * n + 2);
+      {
+        float x[16], y[16];
+        tmem_ld16(tmem_lane_addr(B5, warp, tok0), x);
+        row16<true>(kh, kl, dcol, tok0, y);
+        const float Gl = sG[63];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          x[j] *= __expf(Gl - sG[tok0 + j]);
+          dK[j] += x[j];
+          y[j] *= x[j];
+        }
+        const float s = warp_reduce_scatter16(y);
+        if (lane < 16) P(P_E, qd, tok0 + lane) = s;
+      }
+      tc_fence_before();
+      // ---- e3: T1 tile
+      float kgrow[16];
+      if (rowthr) {
+        const float4* k4 = reinterpret_cast<const float4*>(ws + lay.kg + it.cidx * lay.cc_bytes()) + (ri * 64 + tok0) / 4;
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          const float4 u = __ldg(k4 + q4);
+          kgrow[4 * q4] = u.x, kgrow[4 * q4 + 1] = u.y, kgrow[4 * q4 + 2] = u.z, kgrow[4 * q4 + 3] = u.w;
+        }
+      }
+      ok = mbar_wait(t1_full, par, err, 85);
+      if (!(ok = epi_all(ok))) break;
+      tc_fence_after();
+      GD_TRACE_AT(ws, lay, 16 * n + 3);
+      {
+        float x[16];
+        tmem_ld16(tmem_lane_addr(B6, warp, tok0), x);
+        if (rowthr) {
+          store8_bf16(smem + S::t1, ri, tok0, 64, x);
+          store8_bf16(smem + S::t1, ri, tok0 + 8, 64, x + 8);
+        }
+      }
+      tc_fence_before();
+      fence_async_smem();
+      mbar_arrive_warp(e3_done);
+      // ---- e4: dL = -A^T T1 (strictly lower): R's second term, P_beta tile, the pk partials
+      ok = mbar_wait(dl_full, par, err, 86);
+      if (!(ok = epi_all(ok))) break;
+      tc_fence_after();
+      GD_TRACE_AT(ws, lay, 16 * n + 4);
+      {
+        float x[16];
+        tmem_ld16(tmem_lane_addr(B7, warp, tok0), x);
+        float pk = 0.f;
+        if (rowthr) {
+          const float Gi = sG[ri], bi = sB[ri];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int jj = tok0 + j;
+            float pb = 0.f;
+            rv[j] = 0.f;
+            if (jj < ri) {
+              const float dl = -x[j];
+              const float gam = __expf(Gi - sG[jj]);
+              const float p = dl * gam;
+              rv[j] = dl * bi * kgrow[j] * gam;
+              pk = fmaf(p, kgrow[j], pk);
+              pb = bi * p;
+            }
+            x[j] = pb;
+          }
+          store8_bf16(smem + S::da, ri, tok0, 64, x);
+          store8_bf16(smem + S::da, ri, tok0 + 8, 64, x + 8);
+          P(P_PK, quarter, ri) = pk;
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) rv[j] = 0.f;
+        }
+      }
+      tc_fence_before();
+      fence_async_smem();
+      mbar_arrive_warp(e4_done);
+      rect(rv, false);
+      // ---- final: dK's last term; dg and dbeta of this value head; dq / dk after the item's last value head
+      ok = mbar_wait(p11_full, par, err, 87);
+      if (!(ok = epi_all(ok))) break;
+      tc_fence_after();
+      GD_TRACE_AT(ws, lay, 16 * n + 5);
+      {
+        float x[16];
+        tmem_ld16(tmem_lane_addr(B5, warp, tok0), x);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) dK[j] += x[j];
+      }
+      tc_fence_before();
+      mbar_arrive_warp(b5_free);
+      epi_sync();  // every partial of this sub-item is in place
+      if (tid < 64) {
+        const int t = tid;
+        float a = 0.f, kx = 0.f, vy = 0.f, E = 0.f, rc = 0.f, pk = 0.f;
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+          a += P(P_A, w, t);
+          kx += P(P_KX, w, t);
+          vy += P(P_VY, w, t);
+          E += P(P_E, w, t);
+          rc += P(P_RECT, w, t);
+          pk += P(P_PK, w, t);
+        }
+        float sl = 0.f;
+        const float* slp = reinterpret_cast<const float*>(ws + lay.sl + it.cidx * 64);
+#pragma unroll
+        for (int w = 0; w < 16; ++w) sl += slp[w];
+        const float gt = __expf(sG[t]);
+        const float w_ = sB[t] * gt * kx;
+        const float db = fmaf(gt, kx, vy) + pk;
+        // suffix sum of (a + w) over the chunk and exclusive prefix of E (two warps), without subtraction
+        float suf = a + w_, pre = E;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const float y = __shfl_down_sync(0xffffffffu, suf, o);
+          if (lane + o < 32) suf += y;
+          const float z = __shfl_up_sync(0xffffffffu, pre, o);
+          if (lane >= o) pre += z;
+        }
+        float* xch = scr + 4 * 64;  // [2] cross-warp totals
+        if (lane == 0 && warp == 1) xch[0] = suf;
+        if (lane == 31 && warp == 0) xch[1] = pre;
+        float pre_excl = __shfl_up_sync(0xffffffffu, pre, 1);
+        if (lane == 0) pre_excl = 0.f;
+        asm volatile("bar.sync 2, 64;" ::: "memory");
+        if (warp == 0) suf += xch[0];
+        if (warp == 1) pre_excl += xch[1];
+        const float dgt = suf + __expf(sG[63]) * sl + pre_excl + rc;
+        const int tt = t0 + t;
+        if (tt < lay.T) {
+          dg[((size_t)it.b * lay.T + tt) * lay.H + it.h] = dgt;
+          dbeta[((size_t)it.b * lay.T + tt) * lay.H + it.h] = db;
+        }
+      }
+      if (it.r == lay.rep - 1) {
+        // l2 prologue backward (src/macai/gated_delta/_norm.py:6-9): dx = scale r (dy - x_hat (x_hat . dy)), from the
+        // raw rows and the prologue's rsqrt (q, k, v share a dtype)
+        const size_t row0 = (size_t)it.b * lay.T;
+        float x[16];
+        const float* rqp = reinterpret_cast<const float*>(ws + lay.rq);
+        const float* rkp = reinterpret_cast<const float*>(ws + lay.rk);
+        float* dotq = scr;
+        float* dotk = scr + 4 * 64;
+        epi_sync();  // the dg / dbeta threads are done with scr
+        if (norm) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int t = t0 + tok0 + j;
+            x[j] = (t < lay.T) ? to_f32<T>(qraw[((row0 + t) * lay.HK + it.hk) * DK + dcol]) *
+                                     rqp[(row0 + t) * lay.HK + it.hk] * dQ[j]
+                               : 0.f;
+          }
+          float s = warp_reduce_scatter16(x);
+          if (lane < 16) dotq[qd * 64 + tok0 + lane] = s;
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int t = t0 + tok0 + j;
+            x[j] = (t < lay.T) ? to_f32<T>(kraw[((row0 + t) * lay.HK + it.hk) * DK + dcol]) *
+                                     rkp[(row0 + t) * lay.HK + it.hk] * dK[j]
+                               : 0.f;
+          }
+          s = warp_reduce_scatter16(x);
+          if (lane < 16) dotk[qd * 64 + tok0 + lane] = s;
+        }
+        epi_sync();
+#pragma unroll 4
+        for (int j = 0; j < 16; ++j) {
+          const int i = tok0 + j, t = t0 + i;
+          if (t < lay.T) {
+            const size_t o = ((row0 + t) * lay.HK + it.hk) * DK + dcol;
+            float gq = qscale * dQ[j], gk = dK[j];
+            if (norm) {
+              const float r_q = rqp[(row0 + t) * lay.HK + it.hk], r_k = rkp[(row0 + t) * lay.HK + it.hk];
+              const float xq = to_f32<T>(qraw[o]) * r_q, xk = to_f32<T>(kraw[o]) * r_k;
+              const float dqt = dotq[i] + dotq[64 + i] + dotq[128 + i] + dotq[192 + i];
+              const float dkt = dotk[i] + dotk[64 + i] + dotk[128 + i] + dotk[192 + i];
+              gq = qscale * r_q * (dQ[j] - xq * dqt);
+              gk = r_k * (dK[j] - xk * dkt);
+            }
+            dq[o] = from_f32<T>(gq);
+            dk[o] = from_f32<T>(gk);
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < 16; ++j) dQ[j] = dK[j] = 0.f;
+      }
+      if (n + 1 < nsub && tid < 64) {  // the next sub-item's beta (thread t alone reads sB[t] above)
+        const Item nx = item_of(lay, n + 1);
+        const int t = nx.c * C + tid;
+        sB[tid] = (t < lay.T) ? beta[((size_t)nx.b * lay.T + t) * lay.H + nx.h] : 0.f;
+      }
+      epi_sync();  // partials and scratch read; next beta in place
+      mbar_arrive_warp(epi_done + (n & 1));
     }
   }
   tc_fence_before();
@@ -552,15 +710,23 @@ template <typename T, int DK, int DV>
 cudaError_t launch_bwd_chunk(const void* q, const void* k, const void* v, const float* beta, const void* d_o, void* dq,
                              void* dk, void* dv, float* dg, float* dbeta, const Layout& lay, int flags,
                              unsigned char* ws, cudaStream_t st) {
+  (void)v;
+  (void)d_o;  // dO and V reach this kernel as workspace images
   using S = ChunkSmem<DK, DV>;
   auto kern = bwd_chunk_kernel<T, DK, DV>;
   static bool attr_done[kMaxDevices] = {};  // once per device: no attribute call inside a graph capture
+  static int sms[kMaxDevices] = {};
   cudaError_t e = set_smem_once(kern, S::total, attr_done);
   if (e != cudaSuccess) return e;
-  dim3 grid(lay.NT, lay.HK, lay.B);
-  kern<<<grid, 256, S::total, st>>>(static_cast<const T*>(q), static_cast<const T*>(k), static_cast<const T*>(v), beta,
-                                    static_cast<const T*>(d_o), static_cast<T*>(dq), static_cast<T*>(dk),
-                                    static_cast<T*>(dv), dg, dbeta, lay, flags, ws);
+  int dev = 0;
+  if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  if (sms[dev] == 0 && (e = cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
+    return e;
+  const int ngroups = lay.B * lay.HK * lay.NT;
+  const int grid = ngroups < sms[dev] ? ngroups : sms[dev];
+  kern<<<grid, 576, S::total, st>>>(static_cast<const T*>(q), static_cast<const T*>(k), beta, static_cast<T*>(dq),
+                                    static_cast<T*>(dk), static_cast<T*>(dv), dg, dbeta, lay, flags, ws);
   return cudaGetLastError();
 }
 
