@@ -6,14 +6,15 @@
 //
 // Inputs per sub-item, all bf16 images from the workspace copied whole by the bulk-copy engine: S_c^T and Vn^T (the
 // forward recompute), dS_{c+1}^T (hi, lo), dVn^T (hi, lo) and dO (the reverse pass), A, V^T and the transposed q / k
-// images (prep); G, M and K K^T in fp32 (prep), the partial sums of <S_c, dS_{c+1}> (reverse pass). From the caller:
+// images (prep); G (prep) and the partial sums of <S_c, dS_{c+1}> (reverse pass) in fp32. From the caller:
 // beta and, for the l2 prologue's backward, q and k.
 //
 // Products, all tcgen05 from blocked shared-memory tiles into TMEM ("[D x 64]" accumulators put the head dimension on
 // the 128 TMEM lanes; C x C ones use M = 64). TMEM blocks of 64 columns B0..B7:
 //   G1:  B0 dO Vn^T, B1 (dO S^T)^T, B2 (dVn S^T)^T, B3 (A^T dVn)^T (dVn split), B4 dVn V^T
-//   G3:  B6 (dM K)^T, B7 (dM^T Q)^T (dM, q and k split), B2 (A^T dW)^T, B1 dW K^T        dW = -dVn S^T
-//   G2:  B5 (Vn dS^T)^T (Vn and dS split)
+//   G3:  B6 (dM K)^T, B7 (dM^T Q)^T (dM, q and k split), B2 (A^T dW)^T, B1 dW K^T,       dW = -dVn S^T
+//        B3 Q K^T (q and k split: M = Q K^T * Gamma in fp32 precision for R)
+//   G2:  B5 (Vn dS^T)^T (Vn and dS split), then B5 K K^T (k split, for L and the dbeta term)
 //   tail: B6 T1 = dA A^T, B7 A^T T1 (dL = -A^T T1), B5 (K^T (P_beta + P_beta^T)) with P_beta = diag(beta) (dL * Gamma)
 // Equations: tools/check_chunk_equations.py:49-76 and src/macai/gated_delta/_chunked.py:20-34 of the reference; dg is
 // summed without cancellation (the regrouping of _chunked.py:1138-1142, extended to the decay-mask terms):
@@ -27,7 +28,7 @@
 // done (the TMEM block plan lets the next sub-item's G1 run under this one's tail):
 //   IN1 (S_c^T, dO, V^T; then dS^T)   free after G2        IN2 (dVn^T; then dM, dW^T)   free after G3
 //   IN3 (Vn^T)                        free after G2        A                            free after A^T T1
-//   QK (q^T, k^T hi + lo)             free after the last sub-item's P11 (the l2 backward reads q and k from HBM)
+//   QK (q^T, k^T hi + lo, rsqrt)      free after the item's last sub-item (the l2 backward reads x_hat from it)
 // All hand-offs are mbarriers; every wait is bounded and reports GD_ERR_TIMEOUT.
 #include "gd_common.cuh"
 #include "gd_layout.cuh"
@@ -61,8 +62,10 @@ struct ChunkSmem {
   static constexpr size_t beta = g + 2 * 64 * 4;            // fp32 [64]
   static constexpr size_t part = beta + 64 * 4;             // fp32 [6][4][64] per-token partial sums (see kernel)
   static constexpr size_t scr = part + 6 * 4 * 64 * 4;      // fp32 [2][4][64] exchange scratch
-  static constexpr size_t bar = scr + 2 * 4 * 64 * 4;
-  static constexpr int NBAR = 18;
+  static constexpr size_t rqk = scr + 2 * 4 * 64 * 4;       // fp32 [2][64] the item's l2 rsqrt of q, k rows
+  static constexpr size_t sl = rqk + 2 * 64 * 4;            // fp32 [2][16] <S_c, dS_{c+1}> partials (by parity)
+  static constexpr size_t bar = sl + 2 * 16 * 4;
+  static constexpr int NBAR = 21;
   static constexpr size_t tmem = bar + NBAR * 8;
   static constexpr size_t total = tmem + 16;
   static_assert(dwt + DK * 64 * 2 <= in3, "dM and dW^T fit in the dVn region");
@@ -111,6 +114,36 @@ __device__ __forceinline__ void row16(const unsigned char* hi, const unsigned ch
     unpack8(*reinterpret_cast<const uint4*>(lo + blk_off(r, c0 + 8, 64)), y + 8);
 #pragma unroll
     for (int j = 0; j < 16; ++j) x[j] += y[j];
+  }
+}
+
+// v[16]: this lane's values at head-dimension index d0 + lane % 8 (d0: its 8-lane group's first index) for tokens
+// tok + 0 .. 15. An 8 x 8 transpose inside each 8-lane group (three shuffle rounds) leaves lane L with tokens tok + L
+// and tok + 8 + L at the group's 8 consecutive indices, each stored as one 8-element row segment (16 bytes for
+// 16-bit T) at out + t * tok_stride + d0; tokens t >= T_ are skipped.
+template <typename T>
+__device__ __forceinline__ void store_token_rows(float (&v)[16], T* out, size_t tok_stride, int tok, int T_, int d0) {
+  const int L = threadIdx.x & 7;
+#pragma unroll
+  for (int s = 4; s >= 1; s >>= 1) {
+    const bool upper = (L & s) != 0;
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      if ((e & s) == 0) {  // the pair (e, e + s) inside one 8-block
+        const float send = upper ? v[e] : v[e + s];
+        const float recv = __shfl_xor_sync(0xffffffffu, send, s);
+        if (upper) {
+          v[e] = recv;
+        } else {
+          v[e + s] = recv;
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int blk = 0; blk < 2; ++blk) {
+    const int t = tok + 8 * blk + L;
+    if (t < T_) store8<T>(out + (size_t)t * tok_stride + d0, v + 8 * blk);
   }
 }
 
@@ -164,6 +197,9 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
   uint64_t* b5_free = bars + 14;
   uint64_t* epi_done = bars + 15;  // [2] by sub-item parity
   uint64_t* drain = bars + 17;
+  uint64_t* qk_free = bars + 18;   // 16 epilogue warps, once per item
+  uint64_t* eg2_done = bars + 19;  // 16 epilogue warps: (Vn dS^T)^T read
+  uint64_t* kk_full = bars + 20;   // MMA commit: K K^T
   uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + S::tmem);
 
   const int NG = lay.B * lay.HK * lay.NT;
@@ -177,12 +213,16 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
     for (int i = 0; i < 10; ++i) mbar_init(bars + i, 1);
     for (int i = 10; i < 17; ++i) mbar_init(bars + i, 16);
     mbar_init(drain, 1);
+    mbar_init(qk_free, 16);
+    mbar_init(eg2_done, 16);
+    mbar_init(kk_full, 1);
     fence_mbar_init();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tm = *tslot;
+  if (warp < 16) GD_TRACE_AT(ws, lay, 4000);
   const uint32_t B0 = tm, B1 = tm + 64, B2 = tm + 128, B3 = tm + 192, B4 = tm + 256, B5 = tm + 320, B6 = tm + 384,
                  B7 = tm + 448;
 
@@ -195,7 +235,8 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
     if (lane == 0) {
       bool ok = true;
       int last_in = -1, last_a = -1, last_qk = -1, last_ds = -1;
-      const uint32_t in_bytes = (uint32_t)(lay.si_bytes() + 2 * lay.vi_bytes() + 2 * lay.vn_bytes() + lay.gc_bytes());
+      const uint32_t in_bytes =
+          (uint32_t)(lay.si_bytes() + 2 * lay.vi_bytes() + 2 * lay.vn_bytes() + lay.gc_bytes() + 64);
       for (int n = 0; n < nsub && ok; ++n) {
         const Item it = item_of(lay, n);
         if (n >= 1) ok = mbar_wait(g3_full, (n - 1) & 1, err, 60);  // dM / dW^T (the IN2 region) consumed
@@ -212,22 +253,25 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
         bulk_g2s(smem + S::in3, ws + lay.vni + it.cidx * lay.vn_bytes(), (uint32_t)lay.vn_bytes(), in_full);
         bulk_g2s(smem + S::g + (n & 1) * 256, ws + lay.gc + it.cidx * lay.gc_bytes(), (uint32_t)lay.gc_bytes(),
                  in_full);
-        prefetch_l2(ws + lay.mf + it.cidx * lay.cc_bytes(), (uint32_t)lay.cc_bytes());
-        prefetch_l2(ws + lay.kg + it.cidx * lay.cc_bytes(), (uint32_t)lay.cc_bytes());
+        bulk_g2s(smem + S::sl + (n & 1) * 64, ws + lay.sl + it.cidx * 64, 64, in_full);
         if (n >= 1) ok = mbar_wait(dl_full, (n - 1) & 1, err, 63);  // A consumed
         if (!ok) break;
         mbar_arrive_expect_tx(a_full, (uint32_t)lay.m_bytes());
         last_a = n;
         bulk_g2s(smem + S::a, ws + lay.ai + it.cidx * lay.m_bytes(), (uint32_t)lay.m_bytes(), a_full);
         if (it.r == 0) {
-          if (n >= 1) ok = mbar_wait(p11_full, (n - 1) & 1, err, 64);  // the previous item's q / k consumed
+          const int m = n / lay.rep;
+          if (m >= 1) ok = mbar_wait(qk_free, (m - 1) & 1, err, 64);  // the previous item's q / k consumed
           if (!ok) break;
-          mbar_arrive_expect_tx(qk_full, 2 * (uint32_t)lay.qk_bytes());
-          last_qk = n / lay.rep;
+          mbar_arrive_expect_tx(qk_full, 2 * (uint32_t)lay.qk_bytes() + 2 * 256);
+          last_qk = m;
           bulk_g2s(smem + S::qk, ws + lay.qk + it.cidx0 * lay.qk_bytes(), (uint32_t)lay.qk_bytes(), qk_full);
           bulk_g2s(smem + S::qkl, ws + lay.qkl + it.cidx0 * lay.qk_bytes(), (uint32_t)lay.qk_bytes(), qk_full);
+          const size_t rrow = (((size_t)it.b * lay.HK + it.hk) * lay.NT + it.c) * 64 * 4;
+          bulk_g2s(smem + S::rqk, ws + lay.rq + rrow, 256, qk_full);
+          bulk_g2s(smem + S::rqk + 256, ws + lay.rk + rrow, 256, qk_full);
         }
-        ok = mbar_wait(g1_full, n & 1, err, 65);  // S_c^T, dO, V^T consumed: dS^T goes over them
+        ok = mbar_wait(e1_done, n & 1, err, 65);  // S_c^T, dO, V^T consumed (G1 and e1): dS^T goes over them
         if (!ok) break;
         mbar_arrive_expect_tx(ds_full, 2 * (uint32_t)lay.si_bytes());
         last_ds = n;
@@ -275,9 +319,9 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
       for (int n = 0; n < nsub && ok; ++n) {
         const uint32_t par = n & 1;
         const uint32_t qpar = (n / lay.rep) & 1;
-        bool g3 = false, g2 = false, t1 = false, dl = false, p11 = false, g1n = (n + 1 >= nsub);
+        bool g3 = false, g2 = false, kk = false, t1 = false, dl = false, p11 = false, g1n = (n + 1 >= nsub);
         long long t0 = clock64();
-        while (!(g3 && g2 && t1 && dl && p11 && g1n)) {
+        while (!(g3 && g2 && kk && t1 && dl && p11 && g1n)) {
           bool progressed = false;
           if (!g3 && mbar_try_wait(e1_done, par) && mbar_try_wait(qk_full, qpar)) {
             tc_fence_after();
@@ -289,6 +333,9 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
             mma_tiles(B7, DK, 64, 64, tQ, true, 0, 0, tDml, true, 0, true);
             mma_tiles(B2, DK, 64, 64, tDwt, true, 0, 0, tA, true, 0, false);     // (A^T dW)^T = dW^T A
             mma_tiles(B1, 64, 64, DK, tDwt, false, 0, 0, tK, true, 0, false);    // dW K^T
+            mma_tiles(B3, 64, 64, DK, tQ, false, 0, 0, tK, true, 0, false);      // Q K^T
+            mma_tiles(B3, 64, 64, DK, tQ, false, 0, 0, tKl, true, 0, true);
+            mma_tiles(B3, 64, 64, DK, tQl, false, 0, 0, tK, true, 0, true);
             mma_commit(g3_full);
             g3 = progressed = true;
           }
@@ -299,6 +346,14 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
             mma_tiles(B5, DK, 64, DV, tDsl, false, 0, 0, tVnh, true, 0, true);
             mma_commit(g2_full);
             g2 = progressed = true;
+          }
+          if (g2 && g3 && !kk && mbar_try_wait(eg2_done, par)) {
+            tc_fence_after();
+            mma_tiles(B5, 64, 64, DK, tK, false, 0, 0, tK, true, 0, false);      // K K^T
+            mma_tiles(B5, 64, 64, DK, tK, false, 0, 0, tKl, true, 0, true);
+            mma_tiles(B5, 64, 64, DK, tKl, false, 0, 0, tK, true, 0, true);
+            mma_commit(kk_full);
+            kk = progressed = true;
           }
           if (g3 && !t1 && mbar_try_wait(e2_done, par)) {
             tc_fence_after();
@@ -317,7 +372,7 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
             issue_g1();  // the next sub-item's first products (B0-B4 were read before e2_done)
             g1n = progressed = true;
           }
-          if (dl && g2 && !p11 && mbar_try_wait(e4_done, par)) {
+          if (dl && kk && !p11 && mbar_try_wait(e4_done, par)) {
             tc_fence_after();
             mma_tiles(B5, DK, 64, 64, tK, true, 0, 0, tDa, true, 0, false);      // K^T P_beta
             mma_tiles(B5, DK, 64, 64, tK, true, 0, 0, tDa, false, 0, true);      //  + K^T P_beta^T
@@ -327,7 +382,7 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
           if (progressed) {
             t0 = clock64();
           } else if (clock64() - t0 > kWaitCycles) {
-            report(err, GD_ERR_TIMEOUT, 72 + (g3 ? 1 : 0) + (g2 ? 2 : 0) + (t1 ? 4 : 0) + (dl ? 8 : 0));
+            report(err, GD_ERR_TIMEOUT, 100 + (g3 ? 1 : 0) + (g2 ? 2 : 0) + (t1 ? 4 : 0) + (dl ? 8 : 0) + (kk ? 16 : 0));
             ok = false;
             break;
           }
@@ -391,12 +446,25 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
       const uint32_t par = n & 1;
       const int t0 = it.c * C;
       const float* sG = reinterpret_cast<const float*>(smem + S::g + (n & 1) * 256);
-      // ---- e1: dW^T and dM tiles, dQ's first term and the a partials
+      // ---- e1: dV and the vy partials, dW^T and dM tiles, dQ's first term and the a partials
       ok = mbar_wait(in_full, par, err, 80) && mbar_wait(g1_full, par, err, 81);
       if (!(ok = epi_all(ok))) break;
       tc_fence_after();
-      GD_TRACE_AT(ws, lay, 16 * n + 0);
-      float av[16];
+      GD_TRACE_AT(ws, lay, 32 * n + 0);
+      {
+        float y[16], x[16];
+        tmem_ld16(tmem_lane_addr(B3, warp, tok0), y);  // Y^T: v . Y, and dV = diag(beta) Y
+        row16<false>(smem + S::vt, nullptr, dcol, tok0, x);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          x[j] *= y[j];
+          y[j] *= sB[tok0 + j];
+        }
+        const float s = warp_reduce_scatter16(x);
+        if (lane < 16) P(P_VY, qd, tok0 + lane) = s;
+        store_token_rows<T>(y, dv + ((size_t)it.b * lay.T * lay.H + it.h) * DV, (size_t)lay.H * DV, t0 + tok0, lay.T,
+                            32 * qd + 8 * (lane >> 3));
+      }
       {
         float x[16];
         tmem_ld16(tmem_lane_addr(B2, warp, tok0), x);
@@ -412,52 +480,37 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
           store8_split(smem + S::dmh, smem + S::dml, ri, tok0, 64, x);
           store8_split(smem + S::dmh, smem + S::dml, ri, tok0 + 8, 64, x + 8);
         }
+      }
+      GD_TRACE_AT(ws, lay, 32 * n + 1);
+      ok = mbar_wait(qk_full, (n / lay.rep) & 1, err, 82);
+      if (!(ok = epi_all(ok))) break;
+      GD_TRACE_AT(ws, lay, 32 * n + 2);
+      {
+        float av[16], x[16];
         tmem_ld16(tmem_lane_addr(B1, warp, tok0), av);
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           av[j] *= __expf(sG[tok0 + j]);  // gamma_t (dO S^T)_t
           dQ[j] += av[j];
         }
-      }
-      tc_fence_before();
-      fence_async_smem();
-      mbar_arrive_warp(e1_done);
-      ok = mbar_wait(qk_full, (n / lay.rep) & 1, err, 82);
-      if (!(ok = epi_all(ok))) break;
-      {
-        float x[16];
+        tc_fence_before();
+        fence_async_smem();
+        mbar_arrive_warp(e1_done);
         row16<true>(qh, ql, dcol, tok0, x);
 #pragma unroll
         for (int j = 0; j < 16; ++j) av[j] *= x[j];
         const float s = warp_reduce_scatter16(av);
         if (lane < 16) P(P_A, qd, tok0 + lane) = s;
       }
+      GD_TRACE_AT(ws, lay, 32 * n + 3);
       // ---- e2: dV, dQ / dK terms, dA (and R's first term)
       ok = mbar_wait(g3_full, par, err, 83);
       if (!(ok = epi_all(ok))) break;
       tc_fence_after();
-      GD_TRACE_AT(ws, lay, 16 * n + 1);
-      float mrow[16];
-      if (rowthr) {
-        const float4* m4 = reinterpret_cast<const float4*>(ws + lay.mf + it.cidx * lay.cc_bytes()) + (ri * 64 + tok0) / 4;
-#pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
-          const float4 u = __ldg(m4 + q4);
-          mrow[4 * q4] = u.x, mrow[4 * q4 + 1] = u.y, mrow[4 * q4 + 2] = u.z, mrow[4 * q4 + 3] = u.w;
-        }
-      }
+      GD_TRACE_AT(ws, lay, 32 * n + 4);
       {
         float y[16], x[16];
-        tmem_ld16(tmem_lane_addr(B3, warp, tok0), y);  // Y^T: dV = diag(beta) Y, and v . Y
-        row16<false>(ws + lay.vi + it.cidx * lay.vi_bytes(), nullptr, dcol, tok0, x);
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int t = t0 + tok0 + j;
-          if (t < lay.T) dv[(((size_t)it.b * lay.T + t) * lay.H + it.h) * DV + dcol] = from_f32<T>(sB[tok0 + j] * y[j]);
-          y[j] *= x[j];
-        }
-        float s = warp_reduce_scatter16(y);
-        if (lane < 16) P(P_VY, qd, tok0 + lane) = s;
+        GD_TRACE_AT(ws, lay, 32 * n + 5);
         tmem_ld16(tmem_lane_addr(B6, warp, tok0), x);  // (dM K)^T
 #pragma unroll
         for (int j = 0; j < 16; ++j) dQ[j] += x[j];
@@ -472,8 +525,9 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
           dK[j] = fmaf(sB[i] * __expf(sG[i]), x[j], dK[j]);
           y[j] *= x[j];
         }
-        s = warp_reduce_scatter16(y);
+        const float s = warp_reduce_scatter16(y);
         if (lane < 16) P(P_KX, qd, tok0 + lane) = s;
+        GD_TRACE_AT(ws, lay, 32 * n + 6);
       }
       float rv[16];
       {
@@ -489,19 +543,25 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
           store8_bf16(smem + S::da, ri, tok0, 64, a10);
           store8_bf16(smem + S::da, ri, tok0 + 8, 64, a10 + 8);
         }
-        tmem_ld16(tmem_lane_addr(B0, warp, tok0), a5);  // dO Vn^T again: R's first term (dO Vn^T) * M
+        tmem_ld16(tmem_lane_addr(B0, warp, tok0), a5);   // dO Vn^T again and Q K^T: R's first term
+        tmem_ld16(tmem_lane_addr(B3, warp, tok0), a10);  //   dM * (Q K^T) = (dO Vn^T) * (Q K^T) * Gamma
+        const float Gi = rowthr ? sG[ri] : 0.f;
 #pragma unroll
-        for (int j = 0; j < 16; ++j) rv[j] = (rowthr && tok0 + j < ri) ? a5[j] * mrow[j] : 0.f;
+        for (int j = 0; j < 16; ++j)
+          rv[j] = (rowthr && tok0 + j < ri) ? a5[j] * a10[j] * __expf(Gi - sG[tok0 + j]) : 0.f;
       }
+      GD_TRACE_AT(ws, lay, 32 * n + 7);
       tc_fence_before();
       fence_async_smem();
       mbar_arrive_warp(e2_done);
+      GD_TRACE_AT(ws, lay, 32 * n + 8);
       rect(rv, true);
+      GD_TRACE_AT(ws, lay, 32 * n + 9);
       // ---- eg2: (Vn dS^T)^T -> dK's decay-path term and the E partials
       ok = mbar_wait(g2_full, par, err, 84);
       if (!(ok = epi_all(ok))) break;
       tc_fence_after();
-      GD_TRACE_AT(ws, lay, 16 * n + 2);
+      GD_TRACE_AT(ws, lay, 32 * n + 10);
       {
         float x[16], y[16];
         tmem_ld16(tmem_lane_addr(B5, warp, tok0), x);
@@ -513,24 +573,18 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
           dK[j] += x[j];
           y[j] *= x[j];
         }
+        tc_fence_before();
+        mbar_arrive_warp(eg2_done);  // B5 may take K K^T
         const float s = warp_reduce_scatter16(y);
         if (lane < 16) P(P_E, qd, tok0 + lane) = s;
       }
-      tc_fence_before();
+      GD_TRACE_AT(ws, lay, 32 * n + 11);
       // ---- e3: T1 tile
-      float kgrow[16];
-      if (rowthr) {
-        const float4* k4 = reinterpret_cast<const float4*>(ws + lay.kg + it.cidx * lay.cc_bytes()) + (ri * 64 + tok0) / 4;
-#pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
-          const float4 u = __ldg(k4 + q4);
-          kgrow[4 * q4] = u.x, kgrow[4 * q4 + 1] = u.y, kgrow[4 * q4 + 2] = u.z, kgrow[4 * q4 + 3] = u.w;
-        }
-      }
+      GD_TRACE_AT(ws, lay, 32 * n + 12);
       ok = mbar_wait(t1_full, par, err, 85);
       if (!(ok = epi_all(ok))) break;
       tc_fence_after();
-      GD_TRACE_AT(ws, lay, 16 * n + 3);
+      GD_TRACE_AT(ws, lay, 32 * n + 13);
       {
         float x[16];
         tmem_ld16(tmem_lane_addr(B6, warp, tok0), x);
@@ -542,14 +596,16 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
       tc_fence_before();
       fence_async_smem();
       mbar_arrive_warp(e3_done);
+      GD_TRACE_AT(ws, lay, 32 * n + 14);
       // ---- e4: dL = -A^T T1 (strictly lower): R's second term, P_beta tile, the pk partials
-      ok = mbar_wait(dl_full, par, err, 86);
+      ok = mbar_wait(dl_full, par, err, 86) && mbar_wait(kk_full, par, err, 88);
       if (!(ok = epi_all(ok))) break;
       tc_fence_after();
-      GD_TRACE_AT(ws, lay, 16 * n + 4);
+      GD_TRACE_AT(ws, lay, 32 * n + 15);
       {
-        float x[16];
+        float x[16], kgrow[16];
         tmem_ld16(tmem_lane_addr(B7, warp, tok0), x);
+        tmem_ld16(tmem_lane_addr(B5, warp, tok0), kgrow);  // K K^T
         float pk = 0.f;
         if (rowthr) {
           const float Gi = sG[ri], bi = sB[ri];
@@ -579,12 +635,20 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
       tc_fence_before();
       fence_async_smem();
       mbar_arrive_warp(e4_done);
+      GD_TRACE_AT(ws, lay, 32 * n + 16);
       rect(rv, false);
+      GD_TRACE_AT(ws, lay, 32 * n + 17);
       // ---- final: dK's last term; dg and dbeta of this value head; dq / dk after the item's last value head
+      float bnext = 0.f;  // the next sub-item's beta, fetched early (thread t alone reads and writes sB[t])
+      if (n + 1 < nsub && tid < 64) {
+        const Item nx = item_of(lay, n + 1);
+        const int t = nx.c * C + tid;
+        if (t < lay.T) bnext = beta[((size_t)nx.b * lay.T + t) * lay.H + nx.h];
+      }
       ok = mbar_wait(p11_full, par, err, 87);
       if (!(ok = epi_all(ok))) break;
       tc_fence_after();
-      GD_TRACE_AT(ws, lay, 16 * n + 5);
+      GD_TRACE_AT(ws, lay, 32 * n + 18);
       {
         float x[16];
         tmem_ld16(tmem_lane_addr(B5, warp, tok0), x);
@@ -594,6 +658,7 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
       tc_fence_before();
       mbar_arrive_warp(b5_free);
       epi_sync();  // every partial of this sub-item is in place
+      GD_TRACE_AT(ws, lay, 32 * n + 19);
       if (tid < 64) {
         const int t = tid;
         float a = 0.f, kx = 0.f, vy = 0.f, E = 0.f, rc = 0.f, pk = 0.f;
@@ -607,7 +672,7 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
           pk += P(P_PK, w, t);
         }
         float sl = 0.f;
-        const float* slp = reinterpret_cast<const float*>(ws + lay.sl + it.cidx * 64);
+        const float* slp = reinterpret_cast<const float*>(smem + S::sl + (n & 1) * 64);
 #pragma unroll
         for (int w = 0; w < 16; ++w) sl += slp[w];
         const float gt = __expf(sG[t]);
@@ -636,66 +701,70 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
           dg[((size_t)it.b * lay.T + tt) * lay.H + it.h] = dgt;
           dbeta[((size_t)it.b * lay.T + tt) * lay.H + it.h] = db;
         }
+        sB[t] = bnext;
       }
+      GD_TRACE_AT(ws, lay, 32 * n + 20);
       if (it.r == lay.rep - 1) {
-        // l2 prologue backward (src/macai/gated_delta/_norm.py:6-9): dx = scale r (dy - x_hat (x_hat . dy)), from the
-        // raw rows and the prologue's rsqrt (q, k, v share a dtype)
-        const size_t row0 = (size_t)it.b * lay.T;
-        float x[16];
-        const float* rqp = reinterpret_cast<const float*>(ws + lay.rq);
-        const float* rkp = reinterpret_cast<const float*>(ws + lay.rk);
+        // l2 prologue backward (src/macai/gated_delta/_norm.py:6-9): dx = scale r (dy - x_hat (x_hat . dy)), with
+        // x_hat from the q / k images (hi + lo) and the prologue's rsqrt r, both in shared memory
+        const float* sRq = reinterpret_cast<const float*>(smem + S::rqk);
+        const float* sRk = sRq + 64;
         float* dotq = scr;
         float* dotk = scr + 4 * 64;
+        const float inv_qscale = 1.f / qscale;
+        float x[16];
         epi_sync();  // the dg / dbeta threads are done with scr
         if (norm) {
+          row16<true>(qh, ql, dcol, tok0, x);
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int t = t0 + tok0 + j;
-            x[j] = (t < lay.T) ? to_f32<T>(qraw[((row0 + t) * lay.HK + it.hk) * DK + dcol]) *
-                                     rqp[(row0 + t) * lay.HK + it.hk] * dQ[j]
-                               : 0.f;
-          }
+          for (int j = 0; j < 16; ++j) x[j] *= inv_qscale * dQ[j];
           float s = warp_reduce_scatter16(x);
           if (lane < 16) dotq[qd * 64 + tok0 + lane] = s;
+          row16<true>(kh, kl, dcol, tok0, x);
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int t = t0 + tok0 + j;
-            x[j] = (t < lay.T) ? to_f32<T>(kraw[((row0 + t) * lay.HK + it.hk) * DK + dcol]) *
-                                     rkp[(row0 + t) * lay.HK + it.hk] * dK[j]
-                               : 0.f;
-          }
+          for (int j = 0; j < 16; ++j) x[j] *= dK[j];
           s = warp_reduce_scatter16(x);
           if (lane < 16) dotk[qd * 64 + tok0 + lane] = s;
         }
         epi_sync();
-#pragma unroll 4
-        for (int j = 0; j < 16; ++j) {
-          const int i = tok0 + j, t = t0 + i;
-          if (t < lay.T) {
-            const size_t o = ((row0 + t) * lay.HK + it.hk) * DK + dcol;
-            float gq = qscale * dQ[j], gk = dK[j];
-            if (norm) {
-              const float r_q = rqp[(row0 + t) * lay.HK + it.hk], r_k = rkp[(row0 + t) * lay.HK + it.hk];
-              const float xq = to_f32<T>(qraw[o]) * r_q, xk = to_f32<T>(kraw[o]) * r_k;
-              const float dqt = dotq[i] + dotq[64 + i] + dotq[128 + i] + dotq[192 + i];
-              const float dkt = dotk[i] + dotk[64 + i] + dotk[128 + i] + dotk[192 + i];
-              gq = qscale * r_q * (dQ[j] - xq * dqt);
-              gk = r_k * (dK[j] - xk * dkt);
-            }
-            dq[o] = from_f32<T>(gq);
-            dk[o] = from_f32<T>(gk);
+        GD_TRACE_AT(ws, lay, 32 * n + 21);
+        T* dq0 = dq + ((size_t)it.b * lay.T * lay.HK + it.hk) * DK;
+        T* dk0 = dk + ((size_t)it.b * lay.T * lay.HK + it.hk) * DK;
+        const int d0 = 32 * qd + 8 * (lane >> 3);
+        if (norm) {
+          row16<true>(qh, ql, dcol, tok0, x);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int i = tok0 + j;
+            const float dot = dotq[i] + dotq[64 + i] + dotq[128 + i] + dotq[192 + i];
+            x[j] = qscale * sRq[i] * (dQ[j] - x[j] * inv_qscale * dot);
           }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) x[j] = qscale * dQ[j];
         }
+        store_token_rows<T>(x, dq0, (size_t)lay.HK * DK, t0 + tok0, lay.T, d0);
+        if (norm) {
+          row16<true>(kh, kl, dcol, tok0, x);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int i = tok0 + j;
+            const float dot = dotk[i] + dotk[64 + i] + dotk[128 + i] + dotk[192 + i];
+            x[j] = sRk[i] * (dK[j] - x[j] * dot);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) x[j] = dK[j];
+        }
+        store_token_rows<T>(x, dk0, (size_t)lay.HK * DK, t0 + tok0, lay.T, d0);
+        mbar_arrive_warp(qk_free);  // the q / k images may be replaced by the next item's
 #pragma unroll
         for (int j = 0; j < 16; ++j) dQ[j] = dK[j] = 0.f;
       }
-      if (n + 1 < nsub && tid < 64) {  // the next sub-item's beta (thread t alone reads sB[t] above)
-        const Item nx = item_of(lay, n + 1);
-        const int t = nx.c * C + tid;
-        sB[tid] = (t < lay.T) ? beta[((size_t)nx.b * lay.T + t) * lay.H + nx.h] : 0.f;
-      }
+      GD_TRACE_AT(ws, lay, 32 * n + 22);
       epi_sync();  // partials and scratch read; next beta in place
       mbar_arrive_warp(epi_done + (n & 1));
+      GD_TRACE_AT(ws, lay, 32 * n + 23);
     }
   }
   tc_fence_before();

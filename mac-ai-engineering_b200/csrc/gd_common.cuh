@@ -462,7 +462,7 @@ __device__ __forceinline__ void load_rows(const T* x, int b, int t0, int T_, int
       ss += __shfl_xor_sync(0xffffffffu, ss, 16);
       const float rs = rsqrtf(ss + 1e-6f);
       f = rs * scale;
-      if (rsq_out != nullptr && valid && lane < 8) rsq_out[((size_t)b * T_ + t) * heads + hh] = rs;
+      if (rsq_out != nullptr && valid && lane < 8) rsq_out[t] = rs;  // the (b, hh) row of [B][heads][.]
     }
 #pragma unroll
     for (int j = 0; j < J; ++j) {

@@ -126,8 +126,9 @@ __global__ void __launch_bounds__(128) prep_kernel(const T* __restrict__ q, cons
   // l2 prologue and operand tiles
   const bool norm = (flags & GD_L2NORM) != 0;
   const bool bwd = lay.backward() && (h % lay.rep == 0);
-  float* rq = bwd ? reinterpret_cast<float*>(ws + lay.rq) : nullptr;
-  float* rk = bwd ? reinterpret_cast<float*>(ws + lay.rk) : nullptr;
+  const size_t rrow = ((size_t)b * lay.HK + hk) * lay.NT * 64;  // this (batch row, key head)'s rsqrt row
+  float* rq = bwd ? reinterpret_cast<float*>(ws + lay.rq) + rrow : nullptr;
+  float* rk = bwd ? reinterpret_cast<float*>(ws + lay.rk) + rrow : nullptr;
   const float qscale = (flags & GD_SCALE_Q) ? rsqrtf((float)DK) : 1.f;
   load_rows<T, DK>(q, b, t0, lay.T, lay.HK, hk, norm, qscale, smem + S::q, rq, smem + S::ql);
   load_rows<T, DK>(k, b, t0, lay.T, lay.HK, hk, norm, 1.f, smem + S::k, rk, smem + S::kl);
@@ -228,8 +229,6 @@ __global__ void __launch_bounds__(128) prep_kernel(const T* __restrict__ q, cons
     const float Gi = sG[i];
     float acc[32];
     unsigned char* mimg = ws + lay.m + cidx * lay.m_bytes();
-    float* mf = lay.backward() ? reinterpret_cast<float*>(ws + lay.mf + cidx * lay.cc_bytes()) + i * 64 : nullptr;
-    float* kgf = lay.backward() ? reinterpret_cast<float*>(ws + lay.kg + cidx * lay.cc_bytes()) + i * 64 : nullptr;
 #pragma unroll 1
     for (int half = 0; half < 2; ++half) {
       tmem_ld32(tmem_lane_addr(tm, warp, 32 * half), acc);
@@ -242,20 +241,12 @@ __global__ void __launch_bounds__(128) prep_kernel(const T* __restrict__ q, cons
         }
 #pragma unroll
         for (int q8 = 0; q8 < 4; ++q8) store8_bf16(mimg, i, 32 * half + 8 * q8, 64, mv + 8 * q8);
-        if (mf != nullptr) {
-#pragma unroll
-          for (int q8 = 0; q8 < 4; ++q8) store8<float>(mf + 32 * half + 8 * q8, mv + 8 * q8);
-        }
       } else {
         const float bi = sB[i];
 #pragma unroll
         for (int jj = 0; jj < 32; ++jj) {
           const int j = 32 * half + jj;
           sL[i * 65 + j] = (j < i) ? bi * acc[jj] * __expf(Gi - sG[j]) : 0.f;
-        }
-        if (kgf != nullptr) {
-#pragma unroll
-          for (int q8 = 0; q8 < 4; ++q8) store8<float>(kgf + 32 * half + 8 * q8, acc + 8 * q8);
         }
       }
     }

@@ -14,8 +14,7 @@
 //   gq   [2][64 x DK] image   diag(gamma) Q: hi, then lo
 //   ai   [64 x 64]    image   A = (I + L)^-1
 //   vi   [DV x 64]    image   V^T
-//   mf, kg [64][64]   fp32    M and K K^T
-//   rq, rk [B*T*HK]   fp32    the l2 prologue's rsqrt per raw q / k row
+//   rq, rk [B][HK][NT * 64] fp32  the l2 prologue's rsqrt per raw q / k row (a chunk's 64 rows contiguous)
 // The state pass with GD_STORE_STATES writes per chunk
 //   scf  [DV][DK]     fp32    S_c^T, the state entering the chunk
 //   sci  [DV x DK]    image   S_c^T (bf16)
@@ -37,7 +36,7 @@ struct Layout {
   int B, T, H, HK, DK, DV, NT, rep;
   size_t nch;  // B * H * NT chunks
   size_t err, trace, qk, qkl, kt, wt, m, u, gc;
-  size_t gq, ai, vi, mf, kg, rq, rk, scf, sci, vni, dsi, dvni, doi, sl, total;
+  size_t gq, ai, vi, rq, rk, scf, sci, vni, dsi, dvni, doi, sl, total;
 
   __host__ __device__ static size_t up(size_t x) { return (x + 255) & ~size_t(255); }
 
@@ -46,7 +45,6 @@ struct Layout {
   __host__ __device__ size_t m_bytes() const { return (size_t)64 * 64 * 2; }
   __host__ __device__ size_t u_bytes() const { return (size_t)64 * DV * 4; }
   __host__ __device__ size_t gc_bytes() const { return (size_t)64 * 4; }
-  __host__ __device__ size_t cc_bytes() const { return (size_t)64 * 64 * 4; }      // fp32 C x C
   __host__ __device__ size_t vi_bytes() const { return (size_t)64 * DV * 2; }
   __host__ __device__ size_t s_bytes() const { return (size_t)DK * DV * 4; }       // fp32 state
   __host__ __device__ size_t si_bytes() const { return (size_t)DK * DV * 2; }      // one state image
@@ -77,10 +75,8 @@ struct Layout {
       L.gq = take(L.nch * L.qk_bytes());
       L.ai = take(L.nch * L.m_bytes());
       L.vi = take(L.nch * L.vi_bytes());
-      L.mf = take(L.nch * L.cc_bytes());
-      L.kg = take(L.nch * L.cc_bytes());
-      L.rq = take((size_t)B * T * HK * 4);
-      L.rk = take((size_t)B * T * HK * 4);
+      L.rq = take((size_t)B * HK * L.NT * 64 * 4);
+      L.rk = take((size_t)B * HK * L.NT * 64 * 4);
       L.scf = take(L.nch * L.s_bytes());
       L.sci = take(L.nch * L.si_bytes());
       L.vni = take(L.nch * L.vn_bytes());
@@ -89,7 +85,7 @@ struct Layout {
       L.doi = take(L.nch * L.vi_bytes());
       L.sl = take(L.nch * 64);
     } else {
-      L.gq = L.ai = L.vi = L.mf = L.kg = L.rq = L.rk = L.scf = L.sci = L.vni = L.dsi = L.dvni = L.doi = L.sl = 0;
+      L.gq = L.ai = L.vi = L.rq = L.rk = L.scf = L.sci = L.vni = L.dsi = L.dvni = L.doi = L.sl = 0;
     }
     L.total = o;
     return L;
