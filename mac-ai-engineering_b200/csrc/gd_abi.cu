@@ -181,13 +181,17 @@ int gd_bwd_chunk(const void* q, const void* k, const void* v, const float* beta,
 int gd_forward(const void* q, const void* k, const void* v, const float* g, const float* beta, const float* s0,
                void* o, float* sT, int dtype, int B, int T, int H, int HK, int DK, int DV, int flags, void* workspace,
                size_t workspace_bytes, void* stream) {
-  int s = gd_prep(q, k, v, g, beta, dtype, B, T, H, HK, DK, DV, flags & (GD_L2NORM | GD_SCALE_Q), workspace,
-                  workspace_bytes, stream);
+  int s = check_dims(B, T, H, HK, DK, DV, dtype);
+  if (s) return s;
+  // the forward-only layout in any workspace at least that large: prep then skips the backward's extra images
+  const size_t fwd_bytes = Layout::make(B, T, H, HK, DK, DV, false).total;
+  if (workspace_bytes < fwd_bytes) return GD_ERR_WORKSPACE;
+  s = gd_prep(q, k, v, g, beta, dtype, B, T, H, HK, DK, DV, flags & (GD_L2NORM | GD_SCALE_Q), workspace, fwd_bytes,
+              stream);
   if (s) return s;
   if (!o) return GD_ERR_ARG;
   if (!aligned16(o)) return GD_ERR_ALIGN;
-  return gd_fwd_state(s0, o, sT, dtype, B, T, H, HK, DK, DV, flags & ~GD_STORE_STATES, workspace, workspace_bytes,
-                      stream);
+  return gd_fwd_state(s0, o, sT, dtype, B, T, H, HK, DK, DV, flags & ~GD_STORE_STATES, workspace, fwd_bytes, stream);
 }
 
 int gd_backward(const void* q, const void* k, const void* v, const float* g, const float* beta, const float* s0,

@@ -181,25 +181,37 @@ __global__ void __launch_bounds__(544) bwd_state_kernel(const T* __restrict__ d_
       fence_async_smem();
       mbar_arrive_warp(ds_ready);
     };
-    // this chunk's dO tile: 1024 16-byte pieces, two per thread, eight consecutive threads per 128-byte core matrix
-    auto load_do = [&](int c) {
+    // a chunk's dO tile: 1024 16-byte pieces, two per thread, eight consecutive threads per 128-byte core matrix;
+    // fetched into registers early (fetch_do) and written to the tile once the tile's readers are done (put_do)
+    float dox[2][8];
+    auto fetch_do = [&](int c) {
       const int t0 = c * C;
 #pragma unroll
       for (int p = 0; p < 2; ++p) {
         const int idx = tid + 512 * p;
         const int rl = idx & 7, cb = (idx >> 3) & 15, rb = idx >> 7;
-        const int r = 8 * rb + rl, t = t0 + r;
-        float x[8];
+        const int t = t0 + 8 * rb + rl;
         if (d_o != nullptr && t < lay.T) {
-          load8<T>(d_o + (((size_t)b * lay.T + t) * lay.H + h) * DV + 8 * cb, x);
+          load8<T>(d_o + (((size_t)b * lay.T + t) * lay.H + h) * DV + 8 * cb, dox[p]);
         } else {
 #pragma unroll
-          for (int e = 0; e < 8; ++e) x[e] = 0.f;
+          for (int e = 0; e < 8; ++e) dox[p][e] = 0.f;
         }
-        store8_bf16(smem + S::dO, r, 8 * cb, DV, x);
+      }
+    };
+    auto put_do = [&]() {
+#pragma unroll
+      for (int p = 0; p < 2; ++p) {
+        const int idx = tid + 512 * p;
+        const int rl = idx & 7, cb = (idx >> 3) & 15, rb = idx >> 7;
+        store8_bf16(smem + S::dO, 8 * rb + rl, 8 * cb, DV, dox[p]);
       }
       fence_async_smem();
       mbar_arrive_warp(do_full);
+    };
+    auto load_do = [&](int c) {
+      fetch_do(c);
+      put_do();
     };
     {
       const float* p = dsT ? dsT + ((size_t)b * lay.H + h) * DK * DV : nullptr;
@@ -212,25 +224,29 @@ __global__ void __launch_bounds__(544) bwd_state_kernel(const T* __restrict__ d_
       const int c = NT - 1 - n, s = n & 1;
       const size_t cidx = row0 + c;
       const float* sG = reinterpret_cast<const float*>(smem + S::crit0 + s * S::crit_bytes + S::c_g);
-      {  // partial <S_c, dS_{c+1}> of this thread's 32 entries (fp32 S_c^T from the forward recompute)
-        const float4* sc = reinterpret_cast<const float4*>(ws + lay.scf + cidx * lay.s_bytes() + ((size_t)v * DK + dk0) * 4);
+      if (c > 0) fetch_do(c - 1);  // the next chunk's dO, in flight during this chunk's waits
+      {  // partial <S_c, dS_{c+1}> of this thread's 32 entries (fp32 S_c from the forward recompute; the layout puts
+         // a warp's 16-byte pieces side by side)
+        const float4* sc =
+            reinterpret_cast<const float4*>(ws + lay.scf + cidx * lay.s_bytes()) + (size_t)quarter * 8 * DV + v;
         float acc = 0.f;
 #pragma unroll
         for (int q4 = 0; q4 < 8; ++q4) {
-          const float4 x = __ldg(sc + q4);
+          const float4 x = __ldg(sc + (size_t)q4 * DV);
           acc = fmaf(x.x, Dr[4 * q4], fmaf(x.y, Dr[4 * q4 + 1], fmaf(x.z, Dr[4 * q4 + 2], fmaf(x.w, Dr[4 * q4 + 3], acc))));
         }
         acc = warp_sum(acc);
         if (lane == 0) reinterpret_cast<float*>(ws + lay.sl + cidx * 64)[warp] = acc;
       }
       // * dVn = M^T dO + K~ dS_{c+1}
+      GD_TRACE_AT(ws, lay, 8 * n + 0);
       if (!mbar_wait(b_full, n & 1, err, 41) || !mbar_wait(a_full, n & 1, err, 42)) { ok = false; break; }
       tc_fence_after();
+      GD_TRACE_AT(ws, lay, 8 * n + 1);
       const float gl = __expf(sG[63]);
       {
         float a[16], bb[16];
-        tmem_ld16(tmem_lane_addr(tA, warp, tk0), a);
-        tmem_ld16(tmem_lane_addr(tB, warp, tk0), bb);
+        tmem_ld16x2(tmem_lane_addr(tA, warp, tk0), a, tmem_lane_addr(tB, warp, tk0), bb);
 #pragma unroll
         for (int j = 0; j < 16; ++j) a[j] += bb[j];
         float hi[16], lo[16];
@@ -245,24 +261,28 @@ __global__ void __launch_bounds__(544) bwd_state_kernel(const T* __restrict__ d_
         fence_async_smem();
         mbar_arrive_warp(dvn_full);
       }
-      // the next chunk's dO (this chunk's dO products are done: a_full; its image went out before they were issued)
-      if (c > 0) load_do(c - 1);
+      GD_TRACE_AT(ws, lay, 8 * n + 2);
+      // the next chunk's dO tile (this chunk's dO products are done: a_full; its image went out before they were
+      // issued)
+      if (c > 0) put_do();
       // * dS_c = exp(G_last) dS_{c+1} + (gamma Q)^T dO - W^T dVn
+      GD_TRACE_AT(ws, lay, 8 * n + 3);
       if (!mbar_wait(d_full, n & 1, err, 43)) { ok = false; break; }
       tc_fence_after();
+      GD_TRACE_AT(ws, lay, 8 * n + 4);
       {
         const uint32_t tC = tm + 128 + 128 * (n & 1);
         float cc[16], dd[16];
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
-          tmem_ld16(tmem_lane_addr(tC, warp, dk0 + 16 * hh), cc);
-          tmem_ld16(tmem_lane_addr(tD, warp, dk0 + 16 * hh), dd);
+          tmem_ld16x2(tmem_lane_addr(tC, warp, dk0 + 16 * hh), cc, tmem_lane_addr(tD, warp, dk0 + 16 * hh), dd);
 #pragma unroll
           for (int j = 0; j < 16; ++j) Dr[16 * hh + j] = fmaf(gl, Dr[16 * hh + j], cc[j] - dd[j]);
         }
         tc_fence_before();
       }
       if (c > 0) write_ds();
+      GD_TRACE_AT(ws, lay, 8 * n + 5);
     }
     if (ok && ds0 != nullptr) {
       float* p = ds0 + ((size_t)b * lay.H + h) * DK * DV;

@@ -12,8 +12,8 @@
 // Products, all tcgen05 from blocked shared-memory tiles into TMEM ("[D x 64]" accumulators put the head dimension on
 // the 128 TMEM lanes; C x C ones use M = 64). TMEM blocks of 64 columns B0..B7:
 //   G1:  B0 dO Vn^T, B1 (dO S^T)^T, B2 (dVn S^T)^T, B3 (A^T dVn)^T (dVn split), B4 dVn V^T
-//   G3:  B6 (dM K)^T, B7 (dM^T Q)^T (dM, q and k split), B2 (A^T dW)^T, B1 dW K^T,       dW = -dVn S^T
-//        B3 Q K^T (q and k split: M = Q K^T * Gamma in fp32 precision for R)
+//   G3:  B6 (dM K)^T, B7 (dM^T Q)^T (dM, q and k split), B2 (A^T dW)^T (one commit), B1 dW K^T,
+//        B3 Q K^T (q and k split: M = Q K^T * Gamma in fp32 precision for R);   dW = -dVn S^T
 //   G2:  B5 (Vn dS^T)^T (Vn and dS split), then B5 K K^T (k split, for L and the dbeta term)
 //   tail: B6 T1 = dA A^T, B7 A^T T1 (dL = -A^T T1), B5 (K^T (P_beta + P_beta^T)) with P_beta = diag(beta) (dL * Gamma)
 // Equations: tools/check_chunk_equations.py:49-76 and src/macai/gated_delta/_chunked.py:20-34 of the reference; dg is
@@ -65,7 +65,7 @@ struct ChunkSmem {
   static constexpr size_t rqk = scr + 2 * 4 * 64 * 4;       // fp32 [2][64] the item's l2 rsqrt of q, k rows
   static constexpr size_t sl = rqk + 2 * 64 * 4;            // fp32 [2][16] <S_c, dS_{c+1}> partials (by parity)
   static constexpr size_t bar = sl + 2 * 16 * 4;
-  static constexpr int NBAR = 21;
+  static constexpr int NBAR = 22;
   static constexpr size_t tmem = bar + NBAR * 8;
   static constexpr size_t total = tmem + 16;
   static_assert(dwt + DK * 64 * 2 <= in3, "dM and dW^T fit in the dVn region");
@@ -114,36 +114,6 @@ __device__ __forceinline__ void row16(const unsigned char* hi, const unsigned ch
     unpack8(*reinterpret_cast<const uint4*>(lo + blk_off(r, c0 + 8, 64)), y + 8);
 #pragma unroll
     for (int j = 0; j < 16; ++j) x[j] += y[j];
-  }
-}
-
-// v[16]: this lane's values at head-dimension index d0 + lane % 8 (d0: its 8-lane group's first index) for tokens
-// tok + 0 .. 15. An 8 x 8 transpose inside each 8-lane group (three shuffle rounds) leaves lane L with tokens tok + L
-// and tok + 8 + L at the group's 8 consecutive indices, each stored as one 8-element row segment (16 bytes for
-// 16-bit T) at out + t * tok_stride + d0; tokens t >= T_ are skipped.
-template <typename T>
-__device__ __forceinline__ void store_token_rows(float (&v)[16], T* out, size_t tok_stride, int tok, int T_, int d0) {
-  const int L = threadIdx.x & 7;
-#pragma unroll
-  for (int s = 4; s >= 1; s >>= 1) {
-    const bool upper = (L & s) != 0;
-#pragma unroll
-    for (int e = 0; e < 16; ++e) {
-      if ((e & s) == 0) {  // the pair (e, e + s) inside one 8-block
-        const float send = upper ? v[e] : v[e + s];
-        const float recv = __shfl_xor_sync(0xffffffffu, send, s);
-        if (upper) {
-          v[e] = recv;
-        } else {
-          v[e + s] = recv;
-        }
-      }
-    }
-  }
-#pragma unroll
-  for (int blk = 0; blk < 2; ++blk) {
-    const int t = tok + 8 * blk + L;
-    if (t < T_) store8<T>(out + (size_t)t * tok_stride + d0, v + 8 * blk);
   }
 }
 
@@ -200,6 +170,7 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
   uint64_t* qk_free = bars + 18;   // 16 epilogue warps, once per item
   uint64_t* eg2_done = bars + 19;  // 16 epilogue warps: (Vn dS^T)^T read
   uint64_t* kk_full = bars + 20;   // MMA commit: K K^T
+  uint64_t* g3a_full = bars + 21;  // MMA commit: the first part of G3 (B6, B7, B2)
   uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + S::tmem);
 
   const int NG = lay.B * lay.HK * lay.NT;
@@ -216,6 +187,7 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
     mbar_init(qk_free, 16);
     mbar_init(eg2_done, 16);
     mbar_init(kk_full, 1);
+    mbar_init(g3a_full, 1);
     fence_mbar_init();
   }
   tc_fence_before();
@@ -332,6 +304,7 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
             mma_tiles(B7, DK, 64, 64, tQl, true, 0, 0, tDmh, true, 0, true);
             mma_tiles(B7, DK, 64, 64, tQ, true, 0, 0, tDml, true, 0, true);
             mma_tiles(B2, DK, 64, 64, tDwt, true, 0, 0, tA, true, 0, false);     // (A^T dW)^T = dW^T A
+            mma_commit(g3a_full);
             mma_tiles(B1, 64, 64, DK, tDwt, false, 0, 0, tK, true, 0, false);    // dW K^T
             mma_tiles(B3, 64, 64, DK, tQ, false, 0, 0, tK, true, 0, false);      // Q K^T
             mma_tiles(B3, 64, 64, DK, tQ, false, 0, 0, tKl, true, 0, true);
@@ -339,7 +312,8 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
             mma_commit(g3_full);
             g3 = progressed = true;
           }
-          if (!g2 && mbar_try_wait(ds_full, par) && (n == 0 || mbar_try_wait(b5_free, (n - 1) & 1))) {
+          // G2 after G3: its result is read after G3's
+          if (g3 && !g2 && mbar_try_wait(ds_full, par) && (n == 0 || mbar_try_wait(b5_free, (n - 1) & 1))) {
             tc_fence_after();
             mma_tiles(B5, DK, 64, DV, tDsh, false, 0, 0, tVnh, true, 0, false);  // (Vn dS^T)^T = dS Vn^T
             mma_tiles(B5, DK, 64, DV, tDsh, false, 0, 0, tVnl, true, 0, true);
@@ -466,13 +440,12 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
                             32 * qd + 8 * (lane >> 3));
       }
       {
-        float x[16];
-        tmem_ld16(tmem_lane_addr(B2, warp, tok0), x);
+        float x[16], y[16];
+        tmem_ld16x2(tmem_lane_addr(B2, warp, tok0), y, tmem_lane_addr(B0, warp, tok0), x);  // dW^T, dO Vn^T
 #pragma unroll
-        for (int j = 0; j < 16; ++j) x[j] = -x[j];
-        store8_bf16(smem + S::dwt, dcol, tok0, 64, x);
-        store8_bf16(smem + S::dwt, dcol, tok0 + 8, 64, x + 8);
-        tmem_ld16(tmem_lane_addr(B0, warp, tok0), x);
+        for (int j = 0; j < 16; ++j) y[j] = -y[j];
+        store8_bf16(smem + S::dwt, dcol, tok0, 64, y);
+        store8_bf16(smem + S::dwt, dcol, tok0 + 8, 64, y + 8);
         if (rowthr) {
           const float Gi = sG[ri];
 #pragma unroll
@@ -503,20 +476,20 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
         if (lane < 16) P(P_A, qd, tok0 + lane) = s;
       }
       GD_TRACE_AT(ws, lay, 32 * n + 3);
-      // ---- e2: dV, dQ / dK terms, dA (and R's first term)
-      ok = mbar_wait(g3_full, par, err, 83);
+      // ---- e2: dQ / dK terms, dA (and R's first term)
+      ok = mbar_wait(g3a_full, par, err, 83);
       if (!(ok = epi_all(ok))) break;
       tc_fence_after();
       GD_TRACE_AT(ws, lay, 32 * n + 4);
       {
         float y[16], x[16];
         GD_TRACE_AT(ws, lay, 32 * n + 5);
-        tmem_ld16(tmem_lane_addr(B6, warp, tok0), x);  // (dM K)^T
+        tmem_ld16x2(tmem_lane_addr(B6, warp, tok0), x, tmem_lane_addr(B7, warp, tok0), y);  // (dM K)^T, (dM^T Q)^T
 #pragma unroll
-        for (int j = 0; j < 16; ++j) dQ[j] += x[j];
-        tmem_ld16(tmem_lane_addr(B7, warp, tok0), x);  // (dM^T Q)^T
-#pragma unroll
-        for (int j = 0; j < 16; ++j) dK[j] += x[j];
+        for (int j = 0; j < 16; ++j) {
+          dQ[j] += x[j];
+          dK[j] += y[j];
+        }
         tmem_ld16(tmem_lane_addr(B2, warp, tok0), x);  // X^T
         row16<true>(kh, kl, dcol, tok0, y);
 #pragma unroll
@@ -529,11 +502,13 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
         if (lane < 16) P(P_KX, qd, tok0 + lane) = s;
         GD_TRACE_AT(ws, lay, 32 * n + 6);
       }
+      ok = mbar_wait(g3_full, par, err, 89);
+      if (!(ok = epi_all(ok))) break;
+      tc_fence_after();
       float rv[16];
       {
         float a10[16], a5[16];
-        tmem_ld16(tmem_lane_addr(B1, warp, tok0), a10);  // dW K^T
-        tmem_ld16(tmem_lane_addr(B4, warp, tok0), a5);   // dVn V^T
+        tmem_ld16x2(tmem_lane_addr(B1, warp, tok0), a10, tmem_lane_addr(B4, warp, tok0), a5);  // dW K^T, dVn V^T
         if (rowthr) {
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
@@ -543,8 +518,8 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
           store8_bf16(smem + S::da, ri, tok0, 64, a10);
           store8_bf16(smem + S::da, ri, tok0 + 8, 64, a10 + 8);
         }
-        tmem_ld16(tmem_lane_addr(B0, warp, tok0), a5);   // dO Vn^T again and Q K^T: R's first term
-        tmem_ld16(tmem_lane_addr(B3, warp, tok0), a10);  //   dM * (Q K^T) = (dO Vn^T) * (Q K^T) * Gamma
+        // dO Vn^T again and Q K^T: R's first term dM * (Q K^T) = (dO Vn^T) * (Q K^T) * Gamma
+        tmem_ld16x2(tmem_lane_addr(B0, warp, tok0), a5, tmem_lane_addr(B3, warp, tok0), a10);
         const float Gi = rowthr ? sG[ri] : 0.f;
 #pragma unroll
         for (int j = 0; j < 16; ++j)
@@ -604,8 +579,7 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
       GD_TRACE_AT(ws, lay, 32 * n + 15);
       {
         float x[16], kgrow[16];
-        tmem_ld16(tmem_lane_addr(B7, warp, tok0), x);
-        tmem_ld16(tmem_lane_addr(B5, warp, tok0), kgrow);  // K K^T
+        tmem_ld16x2(tmem_lane_addr(B7, warp, tok0), x, tmem_lane_addr(B5, warp, tok0), kgrow);  // A^T T1, K K^T
         float pk = 0.f;
         if (rowthr) {
           const float Gi = sG[ri], bi = sB[ri];

@@ -240,18 +240,20 @@ __device__ __forceinline__ void mma_tiles(uint32_t d_tmem, int M, int N, int K, 
 }
 
 // TMEM -> registers: this warp's 32 lanes, 32 consecutive fp32 columns each (thread t gets lane (lane_base + t)).
+// The load and its wait are one asm statement, so no use of the registers can be scheduled before the wait.
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   uint32_t r[32];
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
       "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
         "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
         "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
         "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+      : "r"(taddr)
+      : "memory");
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
@@ -261,13 +263,36 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   uint32_t r[16];
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
         "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+      : "r"(taddr)
+      : "memory");
 #pragma unroll
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Two such loads in flight under one wait.
+__device__ __forceinline__ void tmem_ld16x2(uint32_t a0, float (&v0)[16], uint32_t a1, float (&v1)[16]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%32];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%33];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(a0), "r"(a1)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    v0[i] = __uint_as_float(r[i]);
+    v1[i] = __uint_as_float(r[16 + i]);
+  }
 }
 
 // TMEM address of column `col` in the lane quadrant of this warp (warps w, w+4, w+8, ... share a quadrant).
@@ -416,6 +441,36 @@ template <>
 __device__ __forceinline__ void store8<float>(float* p, const float* v) {
   reinterpret_cast<float4*>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
   reinterpret_cast<float4*>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
+}
+
+// v[16]: this lane's values at head-dimension index d0 + lane % 8 (d0: its 8-lane group's first index) for tokens
+// tok + 0 .. 15. An 8 x 8 transpose inside each 8-lane group (three shuffle rounds) leaves lane L with tokens tok + L
+// and tok + 8 + L at the group's 8 consecutive indices, each stored as one 8-element row segment (16 bytes for
+// 16-bit T) at out + t * tok_stride + d0; tokens t >= T_ are skipped.
+template <typename T>
+__device__ __forceinline__ void store_token_rows(float (&v)[16], T* out, size_t tok_stride, int tok, int T_, int d0) {
+  const int L = threadIdx.x & 7;
+#pragma unroll
+  for (int s = 4; s >= 1; s >>= 1) {
+    const bool upper = (L & s) != 0;
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      if ((e & s) == 0) {  // the pair (e, e + s) inside one 8-block
+        const float send = upper ? v[e] : v[e + s];
+        const float recv = __shfl_xor_sync(0xffffffffu, send, s);
+        if (upper) {
+          v[e] = recv;
+        } else {
+          v[e + s] = recv;
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int blk = 0; blk < 2; ++blk) {
+    const int t = tok + 8 * blk + L;
+    if (t < T_) store8<T>(out + (size_t)t * tok_stride + d0, v + 8 * blk);
+  }
 }
 
 __device__ __forceinline__ float warp_sum(float x) {

@@ -456,18 +456,27 @@ __global__ void __launch_bounds__(544) state_kernel(const float* __restrict__ s0
                     false);
           mma_commit(qs_full + s);
         }
+        // the stage of chunk c - 1 takes chunk c + 1 once its readers (chunk c - 1's MMAs and O) are done; chunk
+        // c's first products are already issued, so this wait (on O of chunk c - 1) delays nothing on the chain
+        if (c >= 1 && c + 1 < NT) {
+          const int sp = (c - 1) & 1;
+          const uint32_t pp = ((c - 1) >> 1) & 1;
+          ok = mbar_wait(stage_free + sp, pp, err, 23) && mbar_wait(stage_epi + sp, pp, err, 28);
+          if (!ok) break;
+          issue_stage<DK, DV>(smem + S::stage0 + sp * S::stage_bytes, ws, lay, row0 + c + 1, full + sp);
+        }
         ok = mbar_wait(vn_full, c & 1, err, 22);
         if (!ok) break;
         tc_fence_after();
         if (store) {
           bulk_s2g(ws + lay.vni + (row0 + c) * lay.vn_bytes(), smem + S::vh, (uint32_t)lay.vn_bytes());
           bulk_commit();
-          bulk_wait_read0();  // the S^T and Vn^T tiles may be rewritten once ds_full / mv_full fire
         }
         const Tile tKh{smem_u32(stg + S::s_kt), DK}, tKl{smem_u32(stg + S::s_kt + 64 * DK * 2), DK};
         mma_tiles(tDS, DV, DK, 64, tVh, true, 0, 0, tKh, true, 0, false);
         mma_tiles(tDS, DV, DK, 64, tVh, true, 0, 0, tKl, true, 0, true);
         mma_tiles(tDS, DV, DK, 64, tVl, true, 0, 0, tKh, true, 0, true);
+        if (store) bulk_wait_read0();  // the S^T and Vn^T tiles may be rewritten once ds_full fires
         mma_commit(ds_full);
         if (out) {
           const Tile tM{smem_u32(stg + S::s_m), 64};
@@ -476,11 +485,6 @@ __global__ void __launch_bounds__(544) state_kernel(const float* __restrict__ s0
           mma_commit(mv_full);
         }
         mma_commit(stage_free + s);
-        if (c + 2 < NT) {
-          ok = mbar_wait(stage_free + s, par2, err, 23) && mbar_wait(stage_epi + s, par2, err, 28);
-          if (!ok) break;
-          issue_stage<DK, DV>(stg, ws, lay, row0 + c + 2, full + s);
-        }
       }
       if (store) bulk_wait0();
     }
@@ -500,6 +504,14 @@ __global__ void __launch_bounds__(544) state_kernel(const float* __restrict__ s0
       fence_async_smem();
       mbar_arrive_warp(st_full);
     }
+    // the fp32 state entering chunk c, for the backward (coalesced: lanes write adjacent 16-byte pieces)
+    auto store_scf = [&](int c) {
+      float4* sc = reinterpret_cast<float4*>(ws + lay.scf + (row0 + c) * lay.s_bytes()) + (size_t)quarter * 8 * DV + v;
+#pragma unroll
+      for (int q4 = 0; q4 < 8; ++q4)
+        sc[(size_t)q4 * DV] = make_float4(Sr[4 * q4], Sr[4 * q4 + 1], Sr[4 * q4 + 2], Sr[4 * q4 + 3]);
+    };
+    if (store) store_scf(0);
     float Ur[16];
     {
       const float* u = reinterpret_cast<const float*>(ws + lay.u + row0 * lay.u_bytes());
@@ -537,12 +549,6 @@ __global__ void __launch_bounds__(544) state_kernel(const float* __restrict__ s0
       if (!mbar_wait(ds_full, c & 1, err, 25)) { ok = false; break; }
       GD_TRACE_AT(ws, lay, 8 * c + 3);
       tc_fence_after();
-      if (store) {
-        float* sc = reinterpret_cast<float*>(ws + lay.scf + cidx * lay.s_bytes()) + (size_t)v * DK + dk0;
-#pragma unroll
-        for (int q4 = 0; q4 < 8; ++q4)
-          reinterpret_cast<float4*>(sc)[q4] = make_float4(Sr[4 * q4], Sr[4 * q4 + 1], Sr[4 * q4 + 2], Sr[4 * q4 + 3]);
-      }
       {
         float d[16];
         tmem_ld16(tmem_lane_addr(tDS, warp, dk0), d);
@@ -557,6 +563,7 @@ __global__ void __launch_bounds__(544) state_kernel(const float* __restrict__ s0
         fence_async_smem();
         mbar_arrive_warp(st_full);
       }
+      if (store && c + 1 < NT) store_scf(c + 1);  // off the chain: the next MMAs are already unblocked
       GD_TRACE_AT(ws, lay, 8 * c + 4);
       // O of chunk c (overlaps chunk c + 1's products)
       if (out) {
@@ -571,10 +578,9 @@ __global__ void __launch_bounds__(544) state_kernel(const float* __restrict__ s0
         tmem_ld16(tmem_lane_addr(tMV, warp, tk0), mv);
         const int t0 = c * C;
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int i = tk0 + j, t = t0 + i;
-          if (t < lay.T) o[(((size_t)b * lay.T + t) * lay.H + h) * DV + v] = from_f32<T>(fmaf(__expf(sG[i]), qs[j], mv[j]));
-        }
+        for (int j = 0; j < 16; ++j) qs[j] = fmaf(__expf(sG[tk0 + j]), qs[j], mv[j]);
+        store_token_rows<T>(qs, o + ((size_t)b * lay.T * lay.H + h) * DV, (size_t)lay.H * DV, t0 + tk0, lay.T,
+                            32 * qd + 8 * (lane >> 3));
         tc_fence_before();
       }
       mbar_arrive_warp(stage_epi + s);  // this warp is done reading chunk c's stage

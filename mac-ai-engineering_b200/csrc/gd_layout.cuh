@@ -16,7 +16,8 @@
 //   vi   [DV x 64]    image   V^T
 //   rq, rk [B][HK][NT * 64] fp32  the l2 prologue's rsqrt per raw q / k row (a chunk's 64 rows contiguous)
 // The state pass with GD_STORE_STATES writes per chunk
-//   scf  [DV][DK]     fp32    S_c^T, the state entering the chunk
+//   scf  [DK/32][8][DV][4] fp32  S_c, the state entering the chunk: element (dk, v) at float
+//                               ((dk / 32 * 8 + dk % 32 / 4) * DV + v) * 4 + dk % 4 (a warp's 16-byte pieces adjacent)
 //   sci  [DV x DK]    image   S_c^T (bf16)
 //   vni  [2][DV x 64] image   Vn^T: hi, then lo
 // and the reverse pass
