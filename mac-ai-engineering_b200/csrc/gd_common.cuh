@@ -480,92 +480,115 @@ __device__ __forceinline__ float warp_sum(float x) {
 }
 
 
-// Loads 64 rows x D of a [B, T, heads, D] tensor into a blocked bf16 tile; with norm, each row is scaled by
-// rsqrt(sum x^2 + eps) * scale (the l2 prologue of src/macai/gated_delta/_norm.py:27-43), else by `scale`.
-// Rows past T, and every row when x is null, are zero. With lo_tile, the rounding remainder goes there (hi + lo).
-// NWARPS warps share the 64 rows; each warp stores 8 rows x 32 columns per instruction (512 contiguous bytes: no bank
-// conflict).
-template <typename T, int D, int NWARPS = 4>
-__device__ __forceinline__ void load_rows(const T* x, int b, int t0, int T_, int heads, int hh, bool norm, float scale,
-                                          unsigned char* tile, float* rsq_out, unsigned char* lo_tile = nullptr) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  constexpr int J = D / 32;              // 8-column groups per lane
-  constexpr int RB = 64 / (8 * NWARPS);  // row blocks per warp
-#pragma unroll 1
-  for (int rbi = 0; rbi < RB; ++rbi) {
-    const int r = 8 * (RB * warp + rbi) + (lane & 7);
-    const int t = t0 + r;
-    const bool valid = x != nullptr && t < T_;
-    const T* row = x + (((size_t)b * T_ + (valid ? t : 0)) * heads + hh) * D;
-    float vals[J][8];
-    float ss = 0.f;
+// 64 rows x D of a [B, T, heads, D] tensor -> a blocked bf16 tile, in two steps so that several tensors' loads are in
+// flight at once: rows_issue starts the global loads into registers, rows_finish (after any other work) converts.
+// With norm, each row is scaled by rsqrt(sum x^2 + eps) * scale (the l2 prologue of src/macai/gated_delta/_norm.py:27-43),
+// else by `scale`. Rows past T, and every row when x is null, are zero. With lo_tile, the rounding remainder goes
+// there (hi + lo). NWARPS warps share the 64 rows; each warp stores 8 rows x 32 columns per instruction (512
+// contiguous bytes: no bank conflict).
+template <typename T>
+struct Piece {  // 8 consecutive elements, raw
+  uint4 u;
+  __device__ __forceinline__ void load(const T* p) { u = __ldg(reinterpret_cast<const uint4*>(p)); }
+  __device__ __forceinline__ void zero() { u = make_uint4(0, 0, 0, 0); }
+  __device__ __forceinline__ void to_f32(float* v) const;
+};
+template <>
+__device__ __forceinline__ void Piece<__nv_bfloat16>::to_f32(float* v) const {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
 #pragma unroll
-    for (int j = 0; j < J; ++j) {
-      const int c0 = 8 * ((lane >> 3) + 4 * j);
-      if (valid) {
-        load8<T>(row + c0, vals[j]);
-      } else {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) vals[j][e] = 0.f;
-      }
-#pragma unroll
-      for (int e = 0; e < 8; ++e) ss = fmaf(vals[j][e], vals[j][e], ss);
-    }
-    float f = scale;
-    if (norm) {
-      ss += __shfl_xor_sync(0xffffffffu, ss, 8);
-      ss += __shfl_xor_sync(0xffffffffu, ss, 16);
-      const float rs = rsqrtf(ss + 1e-6f);
-      f = rs * scale;
-      if (rsq_out != nullptr && valid && lane < 8) rsq_out[t] = rs;  // the (b, hh) row of [B][heads][.]
-    }
-#pragma unroll
-    for (int j = 0; j < J; ++j) {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) vals[j][e] *= f;
-      if (lo_tile != nullptr) {
-        store8_split(tile, lo_tile, r, 8 * ((lane >> 3) + 4 * j), D, vals[j]);
-      } else {
-        store8_bf16(tile, r, 8 * ((lane >> 3) + 4 * j), D, vals[j]);
-      }
-    }
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
   }
 }
+template <>
+__device__ __forceinline__ void Piece<__half>::to_f32(float* v) const {
+  const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __half22float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+template <>
+struct Piece<float> {
+  float4 a, b;
+  __device__ __forceinline__ void load(const float* p) {
+    a = __ldg(reinterpret_cast<const float4*>(p));
+    b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+  }
+  __device__ __forceinline__ void zero() { a = b = make_float4(0.f, 0.f, 0.f, 0.f); }
+  __device__ __forceinline__ void to_f32(float* v) const {
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  }
+};
 
-// fp32 [R][Cc] row-major -> blocked bf16 tile(s): hi, and lo = x - hi when lo is not null. Eight consecutive threads
-// fill one 128-byte core matrix (no bank conflicts) and each reads one 32-byte sector.
-template <int R, int Cc, int NTHREADS>
-__device__ __forceinline__ void f32_to_tiles(const float* __restrict__ src, unsigned char* hi, unsigned char* lo) {
-  constexpr int NCHUNK = R * Cc / 8;
-  static_assert(NCHUNK % NTHREADS == 0, "whole passes only");
-  constexpr int PER = NCHUNK / NTHREADS;  // 8-float chunks per thread
-  constexpr int BATCH = PER < 4 ? PER : 4;
-  // loads of a batch are all issued before its stores (memory-level parallelism instead of one round trip each)
+template <typename T, int D, int NWARPS = 4>
+struct Rows {
+  static constexpr int J = D / 32;              // 8-column groups per lane
+  static constexpr int RB = 64 / (8 * NWARPS);  // row blocks per warp
+  Piece<T> p[RB][J];
+  __device__ __forceinline__ static int row(int rbi) {
+    return 8 * (RB * (int)(threadIdx.x >> 5) + rbi) + (int)(threadIdx.x & 7);
+  }
+  __device__ __forceinline__ static int col(int j) { return 8 * ((int)((threadIdx.x & 31) >> 3) + 4 * j); }
+
+  __device__ __forceinline__ void issue(const T* x, int b, int t0, int T_, int heads, int hh) {
 #pragma unroll
-  for (int p0 = 0; p0 < PER; p0 += BATCH) {
-    float4 a[BATCH], b4[BATCH];
+    for (int rbi = 0; rbi < RB; ++rbi) {
+      const int t = t0 + row(rbi);
+      const bool valid = x != nullptr && t < T_;
+      const T* rp = x + (((size_t)b * T_ + (valid ? t : 0)) * heads + hh) * D;
 #pragma unroll
-    for (int u = 0; u < BATCH; ++u) {
-      const int idx = threadIdx.x + (p0 + u) * NTHREADS;
-      const int rl = idx & 7, cb = (idx >> 3) % (Cc / 8), rb = idx / (8 * (Cc / 8));
-      const float4* p = reinterpret_cast<const float4*>(src + (size_t)(8 * rb + rl) * Cc + 8 * cb);
-      a[u] = __ldg(p);
-      b4[u] = __ldg(p + 1);
-    }
-#pragma unroll
-    for (int u = 0; u < BATCH; ++u) {
-      const int idx = threadIdx.x + (p0 + u) * NTHREADS;
-      const int rl = idx & 7, cb = (idx >> 3) % (Cc / 8), rb = idx / (8 * (Cc / 8));
-      const int r = 8 * rb + rl;
-      float v[8] = {a[u].x, a[u].y, a[u].z, a[u].w, b4[u].x, b4[u].y, b4[u].z, b4[u].w};
-      if (lo != nullptr) {
-        store8_split(hi, lo, r, 8 * cb, Cc, v);
-      } else {
-        store8_bf16(hi, r, 8 * cb, Cc, v);
+      for (int j = 0; j < J; ++j) {
+        if (valid) {
+          p[rbi][j].load(rp + col(j));
+        } else {
+          p[rbi][j].zero();
+        }
       }
     }
   }
-}
+
+  __device__ __forceinline__ void finish(int t0, int T_, bool norm, float scale, unsigned char* tile, float* rsq_out,
+                                         unsigned char* lo_tile) const {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int rbi = 0; rbi < RB; ++rbi) {
+      const int r = row(rbi), t = t0 + r;
+      float vals[J][8];
+      float ss = 0.f;
+#pragma unroll
+      for (int j = 0; j < J; ++j) {
+        p[rbi][j].to_f32(vals[j]);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) ss = fmaf(vals[j][e], vals[j][e], ss);
+      }
+      float f = scale;
+      if (norm) {
+        ss += __shfl_xor_sync(0xffffffffu, ss, 8);
+        ss += __shfl_xor_sync(0xffffffffu, ss, 16);
+        const float rs = rsqrtf(ss + 1e-6f);
+        f = rs * scale;
+        if (rsq_out != nullptr && t < T_ && lane < 8) rsq_out[t] = rs;  // the (b, hh) row of [B][heads][.]
+      }
+#pragma unroll
+      for (int j = 0; j < J; ++j) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) vals[j][e] *= f;
+        if (lo_tile != nullptr) {
+          store8_split(tile, lo_tile, r, col(j), D, vals[j]);
+        } else {
+          store8_bf16(tile, r, col(j), D, vals[j]);
+        }
+      }
+    }
+  }
+};
 
 // Reduce-scatter across a warp: each lane holds v[0..31]; returns, in lane l, the sum over the warp's lanes of v[l]
 // (31 shuffles instead of 32 x 5).

@@ -27,74 +27,65 @@ struct PrepSmem {
   static constexpr size_t a2h = a1 + 64 * 64 * 2;         // [64 x 64] A diag(beta), hi
   static constexpr size_t a2l = a2h + 64 * 64 * 2;        //                           lo
   static constexpr size_t L = a2l + 64 * 64 * 2;          // [64][65] fp32, L (strictly lower)
-  static constexpr size_t Ai = L + 64 * 65 * 4;           // [64][65] fp32, A
+  static constexpr size_t Ai = L + 64 * 65 * 4;           // [64][68] fp32, A (16-byte aligned rows)
   static constexpr size_t ql = L;                         // [64 x DK] low half of q, then k: live only until the
   static constexpr size_t kl = ql + 64 * DK * 2;          //   Q K^T / K K^T product is done (L and A reuse them)
-  static_assert(2 * 64 * DK * 2 <= 2 * 64 * 65 * 4, "the q / k low halves must fit in the L and A buffers");
-  static constexpr size_t T3 = Ai + 64 * 65 * 4;          // [3][16][17] fp32 block products of the inverse
-  static constexpr size_t G = T3 + 3 * 16 * 17 * 4;       // [64] cumulative log decay
+  static_assert(2 * 64 * DK * 2 <= 64 * 65 * 4 + 64 * 68 * 4, "the q / k low halves must fit in the L and A buffers");
+  static constexpr size_t G = Ai + 64 * 68 * 4;           // [64] cumulative log decay
   static constexpr size_t beta = G + 64 * 4;              // [64]
   static constexpr size_t scan = beta + 64 * 4;           // [2] warp totals of the scan
-  static constexpr size_t bar = (scan + 16 + 7) & ~size_t(7);
-  static constexpr size_t tmem = bar + 8;
+  static constexpr size_t bar = (scan + 16 + 7) & ~size_t(7);  // [5] MMA commits; row blocks of A published
+  static constexpr size_t tmem = bar + 5 * 8;
   static constexpr size_t total = tmem + 16;
 };
 
-// A = (I + L)^-1 for the 64 x 64 strictly lower L (fp32, row stride 65), by substitution inside the four 16 x 16
-// diagonal blocks and block merges below them, A_IJ = -A_II sum_{m=J}^{I-1} L_Im A_mJ (one block distance at a time),
-// as in the reference's gdc_prep (src/macai/gated_delta/_chunked.py:282-311) with 16-row blocks. 128 threads.
-__device__ __forceinline__ void unit_lower_inverse(const float* L, float* A, float* T3) {
-  const int tid = threadIdx.x;
-  // zero the strictly upper blocks (and everything, so the blocks below are written over a clean slate)
-  for (int idx = tid; idx < 64 * 64; idx += 128) {
-    const int i = idx >> 6, j = idx & 63;
-    if ((i >> 4) < (j >> 4)) A[i * 65 + j] = 0.f;
+// A = (I + L)^-1 for the 64 x 64 strictly lower L (fp32, row stride 65), by forward substitution
+// A[i, :] = e_i - sum_{m < i} L[i, m] A[m, :], rows held in registers: warp w owns rows 16 w .. 16 w + 15, lane l
+// columns 2 l and 2 l + 1. A warp folds in each row block above it as soon as that block's owner publishes it (a
+// 16 x 16 by 16 x 64 update), then solves its own block, publishes it to A (fp32, row stride 68) and arrives on its
+// block's barrier. 128 threads. (The reference's gdc_prep, src/macai/gated_delta/_chunked.py:282-311, also inverts by
+// substitution in blocks; this is a register-resident formulation of the same recurrence.)
+__device__ __forceinline__ bool unit_lower_inverse(const float* L, float* A, uint64_t* blk, ErrorWord* err) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r0 = 16 * warp, c0 = 2 * lane;
+  bool ok = true;
+  float a[16][2];
+#pragma unroll
+  for (int r = 0; r < 16; ++r) {
+    a[r][0] = (r0 + r == c0) ? 1.f : 0.f;
+    a[r][1] = (r0 + r == c0 + 1) ? 1.f : 0.f;
   }
-  if (tid < 64) {
-    const int blk = tid >> 4, col = tid & 15, o = 16 * blk;
-    float x[16];
+  for (int bb = 0; bb < warp; ++bb) {
+    ok = ok && mbar_wait(blk + bb, 0, err, 12);
+#pragma unroll 4
+    for (int m = 0; m < 16; ++m) {
+      const float2 am = *reinterpret_cast<const float2*>(A + (16 * bb + m) * 68 + c0);
 #pragma unroll
-    for (int r = 0; r < 16; ++r) {
-      float s = (r == col) ? 1.f : 0.f;
-      if (r > col) {
-#pragma unroll
-        for (int m = 0; m < 16; ++m)
-          if (m >= col && m < r) s = fmaf(-L[(o + r) * 65 + o + m], x[m], s);
+      for (int r = 0; r < 16; ++r) {
+        const float l = L[(r0 + r) * 65 + 16 * bb + m];
+        a[r][0] = fmaf(-l, am.x, a[r][0]);
+        a[r][1] = fmaf(-l, am.y, a[r][1]);
       }
-      x[r] = s;
     }
-#pragma unroll
-    for (int r = 0; r < 16; ++r) A[(o + r) * 65 + o + col] = x[r];
   }
-  __syncthreads();
-  for (int d = 1; d < 4; ++d) {
-    const int npairs = 4 - d;  // pairs (I, J) = (J + d, J), J = 0 .. npairs-1
-    // T_IJ = sum_{m=J}^{I-1} L_Im A_mJ
-    for (int idx = tid; idx < npairs * 256; idx += 128) {
-      const int p = idx >> 8, r = (idx >> 4) & 15, s = idx & 15;
-      const int J = p, I = p + d;
-      float acc = 0.f;
-      for (int m = J; m < I; ++m) {
 #pragma unroll
-        for (int u = 0; u < 16; ++u) acc = fmaf(L[(16 * I + r) * 65 + 16 * m + u], A[(16 * m + u) * 65 + 16 * J + s], acc);
-      }
-      T3[p * 16 * 17 + r * 17 + s] = acc;
+  for (int r = 1; r < 16; ++r) {
+#pragma unroll
+    for (int m = 0; m < r; ++m) {
+      const float l = L[(r0 + r) * 65 + r0 + m];
+      a[r][0] = fmaf(-l, a[m][0], a[r][0]);
+      a[r][1] = fmaf(-l, a[m][1], a[r][1]);
     }
-    __syncthreads();
-    // A_IJ = -A_II T_IJ (A_II unit lower)
-    for (int idx = tid; idx < npairs * 256; idx += 128) {
-      const int p = idx >> 8, r = (idx >> 4) & 15, s = idx & 15;
-      const int J = p, I = p + d;
-      float acc = T3[p * 16 * 17 + r * 17 + s];
-      for (int u = 0; u < r; ++u) acc = fmaf(A[(16 * I + r) * 65 + 16 * I + u], T3[p * 16 * 17 + u * 17 + s], acc);
-      A[(16 * I + r) * 65 + 16 * J + s] = -acc;
-    }
-    __syncthreads();
   }
+#pragma unroll
+  for (int r = 0; r < 16; ++r) *reinterpret_cast<float2*>(A + (r0 + r) * 68 + c0) = make_float2(a[r][0], a[r][1]);
+  __syncwarp();
+  if (lane == 0) mbar_arrive(blk + warp);
+  return ok;
 }
 
 template <typename T, int DK, int DV>
-__global__ void __launch_bounds__(128) prep_kernel(const T* __restrict__ q, const T* __restrict__ k,
+__global__ void __launch_bounds__(128, 2) prep_kernel(const T* __restrict__ q, const T* __restrict__ k,
                                                    const T* __restrict__ v, const float* __restrict__ g,
                                                    const float* __restrict__ beta, Layout lay, int flags,
                                                    unsigned char* __restrict__ ws) {
@@ -119,20 +110,26 @@ __global__ void __launch_bounds__(128) prep_kernel(const T* __restrict__ q, cons
     tmem_relinquish();
   }
   if (tid == 0) {
-    mbar_init(bar, 1);
+    for (int i = 0; i < 5; ++i) mbar_init(bar + i, 1);  // bar[0]: MMA commits; bar[1 + w]: row block w of A
     fence_mbar_init();
   }
 
-  // l2 prologue and operand tiles
+  // l2 prologue and operand tiles: every row load in flight before any is converted
   const bool norm = (flags & GD_L2NORM) != 0;
   const bool bwd = lay.backward() && (h % lay.rep == 0);
   const size_t rrow = ((size_t)b * lay.HK + hk) * lay.NT * 64;  // this (batch row, key head)'s rsqrt row
   float* rq = bwd ? reinterpret_cast<float*>(ws + lay.rq) + rrow : nullptr;
   float* rk = bwd ? reinterpret_cast<float*>(ws + lay.rk) + rrow : nullptr;
   const float qscale = (flags & GD_SCALE_Q) ? rsqrtf((float)DK) : 1.f;
-  load_rows<T, DK>(q, b, t0, lay.T, lay.HK, hk, norm, qscale, smem + S::q, rq, smem + S::ql);
-  load_rows<T, DK>(k, b, t0, lay.T, lay.HK, hk, norm, 1.f, smem + S::k, rk, smem + S::kl);
-  load_rows<T, DV>(v, b, t0, lay.T, lay.H, h, false, 1.f, smem + S::v, nullptr);
+  Rows<T, DK> rq_rows, rk_rows;
+  Rows<T, DV> rv_rows;
+  rq_rows.issue(q, b, t0, lay.T, lay.HK, hk);
+  rk_rows.issue(k, b, t0, lay.T, lay.HK, hk);
+  if (sizeof(T) == 2) rv_rows.issue(v, b, t0, lay.T, lay.H, h);
+  rq_rows.finish(t0, lay.T, norm, qscale, smem + S::q, rq, smem + S::ql);
+  rk_rows.finish(t0, lay.T, norm, 1.f, smem + S::k, rk, smem + S::kl);
+  if (sizeof(T) != 2) rv_rows.issue(v, b, t0, lay.T, lay.H, h);
+  rv_rows.finish(t0, lay.T, false, 1.f, smem + S::v, nullptr, nullptr);
   GD_TRACE_AT(ws, lay, 1);
 
   // cumulative log decay (padding rows: g = 0, beta = 0, which leaves G constant past the last token)
@@ -253,7 +250,8 @@ __global__ void __launch_bounds__(128) prep_kernel(const T* __restrict__ q, cons
   }
   __syncthreads();
   GD_TRACE_AT(ws, lay, 5);
-  if (ok) unit_lower_inverse(sL, sAi, reinterpret_cast<float*>(smem + S::T3));
+  if (ok) ok = unit_lower_inverse(sL, sAi, bar + 1, err);
+  ok = __syncthreads_and(ok);  // A complete for everyone
   GD_TRACE_AT(ws, lay, 6);
 
   if (ok) {
@@ -266,7 +264,7 @@ __global__ void __launch_bounds__(128) prep_kernel(const T* __restrict__ q, cons
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
         const int j = j0 + 8 * q8 + e;
-        a0[e] = sAi[i * 65 + j];
+        a0[e] = sAi[i * 68 + j];
         a1[e] = a0[e] * sB[j] * __expf(sG[j]);
         a2[e] = a0[e] * sB[j];
       }
