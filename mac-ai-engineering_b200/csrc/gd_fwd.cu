@@ -1,5 +1,5 @@
 // Forward kernels of the chunked gated delta rule on B200 (sm_100a):
-//   prep_kernel   one CTA per (chunk, value head, batch row): l2 prologue, cumulative decay, the chunk's C x C products
+//   prep_kernel   one CTA of 256 threads per (chunk, value head, batch row): l2 prologue, cumulative decay, the C x C products
 //                 on tcgen05, the unit-lower-triangular inverse, W and U;
 //   state_kernel  one CTA per (value head, batch row): the sequential chunk pass with the state in registers (fp32) and
 //                 every product on tcgen05 from shared memory, chunk inputs streamed in by the bulk-copy engine.
@@ -40,52 +40,42 @@ struct PrepSmem {
 };
 
 // A = (I + L)^-1 for the 64 x 64 strictly lower L (fp32, row stride 65), by forward substitution
-// A[i, :] = e_i - sum_{m < i} L[i, m] A[m, :], rows held in registers: warp w owns rows 16 w .. 16 w + 15, lane l
-// columns 2 l and 2 l + 1. A warp folds in each row block above it as soon as that block's owner publishes it (a
-// 16 x 16 by 16 x 64 update), then solves its own block, publishes it to A (fp32, row stride 68) and arrives on its
-// block's barrier. 128 threads. (The reference's gdc_prep, src/macai/gated_delta/_chunked.py:282-311, also inverts by
-// substitution in blocks; this is a register-resident formulation of the same recurrence.)
+// A[i, :] = e_i - sum_{m < i} L[i, m] A[m, :], rows held in registers: warps w and w + 4 own rows 16 w .. 16 w + 15,
+// one column per lane (warp w: columns 0-31, warp w + 4: 32-63). A warp folds in each row block above it as soon as
+// that block's two owners publish it (a 16 x 16 by 16 x 32 update), then solves its own block, publishes it to A (fp32,
+// row stride 68) and arrives on its block's barrier (two arrivals). 256 threads. (The reference's gdc_prep,
+// src/macai/gated_delta/_chunked.py:282-311, also inverts by substitution in blocks; this is a register-resident
+// formulation of the same recurrence.)
 __device__ __forceinline__ bool unit_lower_inverse(const float* L, float* A, uint64_t* blk, ErrorWord* err) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int r0 = 16 * warp, c0 = 2 * lane;
+  const int blkw = warp & 3, r0 = 16 * blkw, col = 32 * (warp >> 2) + lane;
   bool ok = true;
-  float a[16][2];
+  float a[16];
 #pragma unroll
-  for (int r = 0; r < 16; ++r) {
-    a[r][0] = (r0 + r == c0) ? 1.f : 0.f;
-    a[r][1] = (r0 + r == c0 + 1) ? 1.f : 0.f;
-  }
-  for (int bb = 0; bb < warp; ++bb) {
+  for (int r = 0; r < 16; ++r) a[r] = (r0 + r == col) ? 1.f : 0.f;
+  for (int bb = 0; bb < blkw; ++bb) {
     ok = ok && mbar_wait(blk + bb, 0, err, 12);
 #pragma unroll 4
     for (int m = 0; m < 16; ++m) {
-      const float2 am = *reinterpret_cast<const float2*>(A + (16 * bb + m) * 68 + c0);
+      const float am = A[(16 * bb + m) * 68 + col];
 #pragma unroll
-      for (int r = 0; r < 16; ++r) {
-        const float l = L[(r0 + r) * 65 + 16 * bb + m];
-        a[r][0] = fmaf(-l, am.x, a[r][0]);
-        a[r][1] = fmaf(-l, am.y, a[r][1]);
-      }
+      for (int r = 0; r < 16; ++r) a[r] = fmaf(-L[(r0 + r) * 65 + 16 * bb + m], am, a[r]);
     }
   }
 #pragma unroll
   for (int r = 1; r < 16; ++r) {
 #pragma unroll
-    for (int m = 0; m < r; ++m) {
-      const float l = L[(r0 + r) * 65 + r0 + m];
-      a[r][0] = fmaf(-l, a[m][0], a[r][0]);
-      a[r][1] = fmaf(-l, a[m][1], a[r][1]);
-    }
+    for (int m = 0; m < r; ++m) a[r] = fmaf(-L[(r0 + r) * 65 + r0 + m], a[m], a[r]);
   }
 #pragma unroll
-  for (int r = 0; r < 16; ++r) *reinterpret_cast<float2*>(A + (r0 + r) * 68 + c0) = make_float2(a[r][0], a[r][1]);
+  for (int r = 0; r < 16; ++r) A[(r0 + r) * 68 + col] = a[r];
   __syncwarp();
-  if (lane == 0) mbar_arrive(blk + warp);
+  if (lane == 0) mbar_arrive(blk + blkw);
   return ok;
 }
 
 template <typename T, int DK, int DV>
-__global__ void __launch_bounds__(128, 2) prep_kernel(const T* __restrict__ q, const T* __restrict__ k,
+__global__ void __launch_bounds__(256, 2) prep_kernel(const T* __restrict__ q, const T* __restrict__ k,
                                                    const T* __restrict__ v, const float* __restrict__ g,
                                                    const float* __restrict__ beta, Layout lay, int flags,
                                                    unsigned char* __restrict__ ws) {
@@ -110,7 +100,8 @@ __global__ void __launch_bounds__(128, 2) prep_kernel(const T* __restrict__ q, c
     tmem_relinquish();
   }
   if (tid == 0) {
-    for (int i = 0; i < 5; ++i) mbar_init(bar + i, 1);  // bar[0]: MMA commits; bar[1 + w]: row block w of A
+    mbar_init(bar, 1);  // MMA commits
+    for (int i = 1; i < 5; ++i) mbar_init(bar + i, 2);  // row block i - 1 of A published (its two warps)
     fence_mbar_init();
   }
 
@@ -121,8 +112,8 @@ __global__ void __launch_bounds__(128, 2) prep_kernel(const T* __restrict__ q, c
   float* rq = bwd ? reinterpret_cast<float*>(ws + lay.rq) + rrow : nullptr;
   float* rk = bwd ? reinterpret_cast<float*>(ws + lay.rk) + rrow : nullptr;
   const float qscale = (flags & GD_SCALE_Q) ? rsqrtf((float)DK) : 1.f;
-  Rows<T, DK> rq_rows, rk_rows;
-  Rows<T, DV> rv_rows;
+  Rows<T, DK, 8> rq_rows, rk_rows;
+  Rows<T, DV, 8> rv_rows;
   rq_rows.issue(q, b, t0, lay.T, lay.HK, hk);
   rk_rows.issue(k, b, t0, lay.T, lay.HK, hk);
   if (sizeof(T) == 2) rv_rows.issue(v, b, t0, lay.T, lay.H, h);
@@ -170,13 +161,13 @@ __global__ void __launch_bounds__(128, 2) prep_kernel(const T* __restrict__ q, c
   GD_TRACE_AT(ws, lay, 2);
   {  // the low halves go out (transposed images) before L and A overwrite them
     unsigned char* dst = ws + lay.qkl + cidx * lay.qk_bytes();
-    store_tile_transposed<64, DK, 4>(smem + S::ql, dst);
-    store_tile_transposed<64, DK, 4>(smem + S::kl, dst + 64 * DK * 2);
+    store_tile_transposed<64, DK, 8>(smem + S::ql, dst);
+    store_tile_transposed<64, DK, 8>(smem + S::kl, dst + 64 * DK * 2);
   }
   if (lay.backward()) {  // diag(gamma) Q from q's hi + lo, split again: the reverse pass's operand
     unsigned char* gqh = ws + lay.gq + cidx * lay.qk_bytes();
     unsigned char* gql = gqh + 64 * DK * 2;
-    for (int idx = tid; idx < 64 * DK / 8; idx += 128) {
+    for (int idx = tid; idx < 64 * DK / 8; idx += 256) {
       const int rl = idx & 7, cb = (idx >> 3) % (DK / 8), rb = idx / (8 * (DK / 8));
       const int r = 8 * rb + rl;
       const uint4 uh = *reinterpret_cast<const uint4*>(smem + S::q + blk_off(r, 8 * cb, DK));
@@ -198,7 +189,7 @@ __global__ void __launch_bounds__(128, 2) prep_kernel(const T* __restrict__ q, c
     unsigned char* kth = ws + lay.kt + cidx * lay.qk_bytes();
     unsigned char* ktl = kth + 64 * DK * 2;
     const float Glast = sG[63];
-    for (int idx = tid; idx < 64 * DK / 8; idx += 128) {
+    for (int idx = tid; idx < 64 * DK / 8; idx += 256) {
       const int rl = idx & 7, cb = (idx >> 3) % (DK / 8), rb = idx / (8 * (DK / 8));
       const int r = 8 * rb + rl;
       const uint4 uh = *reinterpret_cast<const uint4*>(smem + S::k + blk_off(r, 8 * cb, DK));
@@ -222,14 +213,15 @@ __global__ void __launch_bounds__(128, 2) prep_kernel(const T* __restrict__ q, c
   ok = __syncthreads_and(ok);
   tc_fence_after();
   if (ok) {
+    // warp w: accumulator rows 32 (w % 4) + lane (Q K^T for w % 4 < 2, K K^T otherwise), columns 32 (w / 4) .. + 31
     const int i = tid & 63;
     const float Gi = sG[i];
     float acc[32];
     unsigned char* mimg = ws + lay.m + cidx * lay.m_bytes();
-#pragma unroll 1
-    for (int half = 0; half < 2; ++half) {
+    {
+      const int half = warp >> 2;
       tmem_ld32(tmem_lane_addr(tm, warp, 32 * half), acc);
-      if (tid < 64) {
+      if ((warp & 3) < 2) {
         float mv[32];
 #pragma unroll
         for (int jj = 0; jj < 32; ++jj) {
@@ -256,10 +248,10 @@ __global__ void __launch_bounds__(128, 2) prep_kernel(const T* __restrict__ q, c
 
   if (ok) {
     // A diag(beta gamma) and the hi/lo split of A diag(beta) as K-major B operands (rows i, cols j)
-    const int i = tid >> 1, j0 = 32 * (tid & 1);
+    const int i = tid >> 2, j0 = 16 * (tid & 3);
     unsigned char* aimg = lay.backward() ? ws + lay.ai + cidx * lay.m_bytes() : nullptr;
-#pragma unroll 1
-    for (int q8 = 0; q8 < 4; ++q8) {
+#pragma unroll
+    for (int q8 = 0; q8 < 2; ++q8) {
       float a0[8], a1[8], a2[8];
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
@@ -274,7 +266,7 @@ __global__ void __launch_bounds__(128, 2) prep_kernel(const T* __restrict__ q, c
     }
     if (lay.backward()) {
       // the backward's V image, transposed ([DV x 64], rows v)
-      store_tile_transposed<64, DV, 4>(smem + S::v, ws + lay.vi + cidx * lay.vi_bytes());
+      store_tile_transposed<64, DV, 8>(smem + S::v, ws + lay.vi + cidx * lay.vi_bytes());
     }
   }
   fence_async_smem();
@@ -295,8 +287,8 @@ __global__ void __launch_bounds__(128, 2) prep_kernel(const T* __restrict__ q, c
   // the q / k images and G go out while the MMAs run
   if (ok) {
     unsigned char* dst = ws + lay.qk + cidx * lay.qk_bytes();  // transposed images ([DK x 64], rows d)
-    store_tile_transposed<64, DK, 4>(smem + S::q, dst);
-    store_tile_transposed<64, DK, 4>(smem + S::k, dst + 64 * DK * 2);
+    store_tile_transposed<64, DK, 8>(smem + S::q, dst);
+    store_tile_transposed<64, DK, 8>(smem + S::k, dst + 64 * DK * 2);
     if (tid < 64) reinterpret_cast<float*>(ws + lay.gc + cidx * lay.gc_bytes())[tid] = sG[tid];
   }
   if (ok) ok = mbar_wait(bar, 1, err, 11);
@@ -305,24 +297,22 @@ __global__ void __launch_bounds__(128, 2) prep_kernel(const T* __restrict__ q, c
   tc_fence_after();
   if (ok) {
     float acc[32];
-    // W^T row dk = tid -> blocked [DK x 64] image, 16-byte stores
-    unsigned char* wimg = ws + lay.wt + cidx * lay.wt_bytes();
-    if (tid < DK) {
+    const int row = tid & 127;
+    if (warp < 4) {  // W^T row dk = row -> blocked [DK x 64] image, 16-byte stores
+      unsigned char* wimg = ws + lay.wt + cidx * lay.wt_bytes();
 #pragma unroll 1
       for (int half = 0; half < 2; ++half) {
         tmem_ld32(tmem_lane_addr(tm, warp, 64 + 32 * half), acc);
 #pragma unroll
-        for (int q8 = 0; q8 < 4; ++q8) store8_bf16(wimg, tid, 32 * half + 8 * q8, 64, acc + 8 * q8);
+        for (int q8 = 0; q8 < 4; ++q8) store8_bf16(wimg, row, 32 * half + 8 * q8, 64, acc + 8 * q8);
       }
-    }
-    // U^T row v = tid -> U [64][DV] fp32
-    float* u = reinterpret_cast<float*>(ws + lay.u + cidx * lay.u_bytes());
-    if (tid < DV) {
+    } else {  // U^T row v = row -> U [64][DV] fp32
+      float* u = reinterpret_cast<float*>(ws + lay.u + cidx * lay.u_bytes());
 #pragma unroll 1
       for (int half = 0; half < 2; ++half) {
         tmem_ld32(tmem_lane_addr(tm, warp, 128 + 32 * half), acc);
 #pragma unroll
-        for (int jj = 0; jj < 32; ++jj) u[(32 * half + jj) * DV + tid] = acc[jj];
+        for (int jj = 0; jj < 32; ++jj) u[(32 * half + jj) * DV + row] = acc[jj];
       }
     }
   }
@@ -609,7 +599,7 @@ cudaError_t launch_prep(const void* q, const void* k, const void* v, const float
   cudaError_t e = set_smem_once(kern, S::total, attr_done);
   if (e != cudaSuccess) return e;
   dim3 grid(lay.NT, lay.H, lay.B);
-  kern<<<grid, 128, S::total, st>>>(static_cast<const T*>(q), static_cast<const T*>(k), static_cast<const T*>(v), g,
+  kern<<<grid, 256, S::total, st>>>(static_cast<const T*>(q), static_cast<const T*>(k), static_cast<const T*>(v), g,
                                     beta, lay, flags, ws);
   return cudaGetLastError();
 }
