@@ -129,6 +129,10 @@ __global__ void __launch_bounds__(544) bwd_state_kernel(const T* __restrict__ d_
         // dS_{c+1} images for the per-chunk kernel
         bulk_s2g(ws + lay.dsi + cidx * 2 * lay.si_bytes(), smem + S::dsh, 2 * (uint32_t)lay.si_bytes());
         bulk_commit();
+        if (c > 0)  // the next chunk's fp32 state, for the epilogue's <S, dS> partial sums
+          asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(ws + lay.scf + (cidx - 1) * lay.s_bytes()),
+                       "r"((uint32_t)lay.s_bytes())
+                       : "memory");
         // * (K~ dS)^T = dS^T K~^T [DV x 64]: hi hi + hi lo + lo hi
         const Tile tKh{smem_u32(st + S::c_kt), DK}, tKl{smem_u32(st + S::c_kt + 64 * DK * 2), DK};
         const Tile tDh{smem_u32(smem + S::dsh), DK}, tDl{smem_u32(smem + S::dsl), DK};
@@ -183,7 +187,7 @@ __global__ void __launch_bounds__(544) bwd_state_kernel(const T* __restrict__ d_
     };
     // a chunk's dO tile: 1024 16-byte pieces, two per thread, eight consecutive threads per 128-byte core matrix;
     // fetched into registers early (fetch_do) and written to the tile once the tile's readers are done (put_do)
-    float dox[2][8];
+    Piece<T> dox[2];  // raw until written, so the loads stay in flight through the waits
     auto fetch_do = [&](int c) {
       const int t0 = c * C;
 #pragma unroll
@@ -192,10 +196,9 @@ __global__ void __launch_bounds__(544) bwd_state_kernel(const T* __restrict__ d_
         const int rl = idx & 7, cb = (idx >> 3) & 15, rb = idx >> 7;
         const int t = t0 + 8 * rb + rl;
         if (d_o != nullptr && t < lay.T) {
-          load8<T>(d_o + (((size_t)b * lay.T + t) * lay.H + h) * DV + 8 * cb, dox[p]);
+          dox[p].load(d_o + (((size_t)b * lay.T + t) * lay.H + h) * DV + 8 * cb);
         } else {
-#pragma unroll
-          for (int e = 0; e < 8; ++e) dox[p][e] = 0.f;
+          dox[p].zero();
         }
       }
     };
@@ -204,7 +207,9 @@ __global__ void __launch_bounds__(544) bwd_state_kernel(const T* __restrict__ d_
       for (int p = 0; p < 2; ++p) {
         const int idx = tid + 512 * p;
         const int rl = idx & 7, cb = (idx >> 3) & 15, rb = idx >> 7;
-        store8_bf16(smem + S::dO, 8 * rb + rl, 8 * cb, DV, dox[p]);
+        float x[8];
+        dox[p].to_f32(x);
+        store8_bf16(smem + S::dO, 8 * rb + rl, 8 * cb, DV, x);
       }
       fence_async_smem();
       mbar_arrive_warp(do_full);
@@ -225,19 +230,6 @@ __global__ void __launch_bounds__(544) bwd_state_kernel(const T* __restrict__ d_
       const size_t cidx = row0 + c;
       const float* sG = reinterpret_cast<const float*>(smem + S::crit0 + s * S::crit_bytes + S::c_g);
       if (c > 0) fetch_do(c - 1);  // the next chunk's dO, in flight during this chunk's waits
-      {  // partial <S_c, dS_{c+1}> of this thread's 32 entries (fp32 S_c from the forward recompute; the layout puts
-         // a warp's 16-byte pieces side by side)
-        const float4* sc =
-            reinterpret_cast<const float4*>(ws + lay.scf + cidx * lay.s_bytes()) + (size_t)quarter * 8 * DV + v;
-        float acc = 0.f;
-#pragma unroll
-        for (int q4 = 0; q4 < 8; ++q4) {
-          const float4 x = __ldg(sc + (size_t)q4 * DV);
-          acc = fmaf(x.x, Dr[4 * q4], fmaf(x.y, Dr[4 * q4 + 1], fmaf(x.z, Dr[4 * q4 + 2], fmaf(x.w, Dr[4 * q4 + 3], acc))));
-        }
-        acc = warp_sum(acc);
-        if (lane == 0) reinterpret_cast<float*>(ws + lay.sl + cidx * 64)[warp] = acc;
-      }
       // * dVn = M^T dO + K~ dS_{c+1}
       GD_TRACE_AT(ws, lay, 8 * n + 0);
       if (!mbar_wait(b_full, n & 1, err, 41) || !mbar_wait(a_full, n & 1, err, 42)) { ok = false; break; }
@@ -246,22 +238,27 @@ __global__ void __launch_bounds__(544) bwd_state_kernel(const T* __restrict__ d_
       const float gl = __expf(sG[63]);
       {
         float a[16], bb[16];
-        tmem_ld16x2(tmem_lane_addr(tA, warp, tk0), a, tmem_lane_addr(tB, warp, tk0), bb);
+        tmem_ld16(tmem_lane_addr(tA, warp, tk0), a);
+        tmem_ld16(tmem_lane_addr(tB, warp, tk0), bb);
 #pragma unroll
-        for (int j = 0; j < 16; ++j) a[j] += bb[j];
-        float hi[16], lo[16];
-#pragma unroll
-        for (int j = 0; j < 16; ++j) split_bf16(a[j], hi[j], lo[j]);
-        store8_bf16(smem + S::dvh, v, tk0, 64, hi);
-        store8_bf16(smem + S::dvh, v, tk0 + 8, 64, hi + 8);
+        for (int j = 0; j < 16; ++j) split_bf16(a[j] + bb[j], a[j], bb[j]);  // in place: a = hi, bb = lo
+        store8_bf16(smem + S::dvh, v, tk0, 64, a);
+        store8_bf16(smem + S::dvh, v, tk0 + 8, 64, a + 8);
         unsigned char* dlo = ws + lay.dvni + cidx * lay.vn_bytes() + DV * 64 * 2;  // the low half: straight to HBM
-        store8_bf16(dlo, v, tk0, 64, lo);
-        store8_bf16(dlo, v, tk0 + 8, 64, lo + 8);
+        store8_bf16(dlo, v, tk0, 64, bb);
+        store8_bf16(dlo, v, tk0 + 8, 64, bb + 8);
         tc_fence_before();
         fence_async_smem();
         mbar_arrive_warp(dvn_full);
       }
       GD_TRACE_AT(ws, lay, 8 * n + 2);
+      // partial <S_c, dS_{c+1}> of this thread's 32 entries (fp32 S_c from the forward recompute, prefetched into L2 a
+      // chunk ahead; the layout puts a warp's 16-byte pieces side by side): loads in flight through the wait for
+      // (W^T dVn)^T, consumed before dS moves on
+      const float4* sc = reinterpret_cast<const float4*>(ws + lay.scf + cidx * lay.s_bytes()) + (size_t)quarter * 8 * DV + v;
+      float4 sx[8];
+#pragma unroll
+      for (int q4 = 0; q4 < 8; ++q4) sx[q4] = __ldg(sc + (size_t)q4 * DV);
       // the next chunk's dO tile (this chunk's dO products are done: a_full; its image went out before they were
       // issued)
       if (c > 0) put_do();
@@ -270,6 +267,13 @@ __global__ void __launch_bounds__(544) bwd_state_kernel(const T* __restrict__ d_
       if (!mbar_wait(d_full, n & 1, err, 43)) { ok = false; break; }
       tc_fence_after();
       GD_TRACE_AT(ws, lay, 8 * n + 4);
+      float sacc = 0.f;
+#pragma unroll
+      for (int q4 = 0; q4 < 8; ++q4)
+        sacc = fmaf(sx[q4].x, Dr[4 * q4], fmaf(sx[q4].y, Dr[4 * q4 + 1], fmaf(sx[q4].z, Dr[4 * q4 + 2],
+                                                                              fmaf(sx[q4].w, Dr[4 * q4 + 3], sacc))));
+      sacc = warp_sum(sacc);
+      if (lane == 0) reinterpret_cast<float*>(ws + lay.sl + cidx * 64)[warp] = sacc;
       {
         const uint32_t tC = tm + 128 + 128 * (n & 1);
         float cc[16], dd[16];
