@@ -372,8 +372,9 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
     const int qd = warp & 3, quarter = warp >> 2;
     const int dcol = 32 * qd + lane;  // head-dimension row of the [D x 64] accumulators
     const int tok0 = 16 * quarter;    // their 16 token columns / the C x C columns of this warp
-    const int ri = 16 * qd + lane;    // C x C row (lanes 0-15)
-    const bool rowthr = lane < 16;
+    // C x C (M = 64) accumulators are read whole-warp (tmem_ld8h): row ri, columns c8 .. c8 + 7
+    const int ri = 16 * qd + (lane & 15);
+    const int c8 = tok0 + 8 * (lane >> 4);
     float* sB = reinterpret_cast<float*>(smem + S::beta);
     float* part = reinterpret_cast<float*>(smem + S::part);
     float* scr = reinterpret_cast<float*>(smem + S::scr);
@@ -385,24 +386,29 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
     const unsigned char* kh = smem + S::qk + DK * 64 * 2;
     const unsigned char* kl = smem + S::qkl + DK * 64 * 2;
 
-    // rect_t += sum_{i >= t} sum_{j < t} R_ij for this warp's columns t, from R's row segments rv (row ri, columns
-    // tok0 .. tok0 + 15; zero off the rows): quarter row totals through scr, exclusive row prefixes, masked row sums
-    auto rect = [&](const float (&rv)[16], bool init) {
+    // rect_t += sum_{i >= t} sum_{j < t} R_ij for this thread's columns t, from R's row segment rv (row ri, columns
+    // c8 .. c8 + 7): row totals by 8-column group through scr, exclusive row prefixes, masked sums over the
+    // half-warp's 16 rows
+    auto rect = [&](const float (&rv)[8], bool init) {
+      const int grp = c8 >> 3;
       float tot = 0.f;
 #pragma unroll
-      for (int j = 0; j < 16; ++j) tot += rv[j];
-      if (rowthr) scr[quarter * 64 + ri] = tot;
+      for (int j = 0; j < 8; ++j) tot += rv[j];
+      scr[grp * 64 + ri] = tot;
       epi_sync();
       float run = 0.f;
-      for (int q2 = 0; q2 < quarter; ++q2) run += rowthr ? scr[q2 * 64 + ri] : 0.f;
-      float v[16];
+      for (int g2 = 0; g2 < grp; ++g2) run += scr[g2 * 64 + ri];
+      float v[8];
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        v[j] = (rowthr && ri >= tok0 + j) ? run : 0.f;
+      for (int j = 0; j < 8; ++j) {
+        v[j] = (ri >= c8 + j) ? run : 0.f;
         run += rv[j];
       }
-      const float s = warp_reduce_scatter16(v);
-      if (lane < 16) P(P_RECT, qd, tok0 + lane) = init ? s : P(P_RECT, qd, tok0 + lane) + s;
+      const float s = halfwarp_reduce_scatter8(v);
+      if ((lane & 8) == 0) {
+        float& dst = P(P_RECT, qd, c8 + (lane & 7));
+        dst = init ? s : dst + s;
+      }
     };
 
     float dQ[16], dK[16];  // d(normalised q / k)[token tok0 + j][dcol], summed over the item's value heads
@@ -440,19 +446,17 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
                             32 * qd + 8 * (lane >> 3));
       }
       {
-        float x[16], y[16];
-        tmem_ld16x2(tmem_lane_addr(B2, warp, tok0), y, tmem_lane_addr(B0, warp, tok0), x);  // dW^T, dO Vn^T
+        float y[16], x[8];
+        tmem_ld16(tmem_lane_addr(B2, warp, tok0), y);  // dW^T
 #pragma unroll
         for (int j = 0; j < 16; ++j) y[j] = -y[j];
         store8_bf16(smem + S::dwt, dcol, tok0, 64, y);
         store8_bf16(smem + S::dwt, dcol, tok0 + 8, 64, y + 8);
-        if (rowthr) {
-          const float Gi = sG[ri];
+        tmem_ld8h(tmem_lane_addr(B0, warp, tok0), x);  // dO Vn^T -> dM
+        const float Gi = sG[ri];
 #pragma unroll
-          for (int j = 0; j < 16; ++j) x[j] = (tok0 + j <= ri) ? x[j] * __expf(Gi - sG[tok0 + j]) : 0.f;
-          store8_split(smem + S::dmh, smem + S::dml, ri, tok0, 64, x);
-          store8_split(smem + S::dmh, smem + S::dml, ri, tok0 + 8, 64, x + 8);
-        }
+        for (int j = 0; j < 8; ++j) x[j] = (c8 + j <= ri) ? x[j] * __expf(Gi - sG[c8 + j]) : 0.f;
+        store8_split(smem + S::dmh, smem + S::dml, ri, c8, 64, x);
       }
       GD_TRACE_AT(ws, lay, 32 * n + 1);
       ok = mbar_wait(qk_full, (n / lay.rep) & 1, err, 82);
@@ -505,25 +509,21 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
       ok = mbar_wait(g3_full, par, err, 89);
       if (!(ok = epi_all(ok))) break;
       tc_fence_after();
-      float rv[16];
+      float rv[8];
       {
-        float a10[16], a5[16];
-        tmem_ld16x2(tmem_lane_addr(B1, warp, tok0), a10, tmem_lane_addr(B4, warp, tok0), a5);  // dW K^T, dVn V^T
-        if (rowthr) {
+        float a10[8], a5[8];
+        tmem_ld8hx2(tmem_lane_addr(B1, warp, tok0), a10, tmem_lane_addr(B4, warp, tok0), a5);  // dW K^T, dVn V^T
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int jj = tok0 + j;
-            a10[j] = (jj < ri) ? sB[jj] * fmaf(__expf(sG[jj]), a10[j], a5[j]) : 0.f;
-          }
-          store8_bf16(smem + S::da, ri, tok0, 64, a10);
-          store8_bf16(smem + S::da, ri, tok0 + 8, 64, a10 + 8);
+        for (int j = 0; j < 8; ++j) {
+          const int jj = c8 + j;
+          a10[j] = (jj < ri) ? sB[jj] * fmaf(__expf(sG[jj]), a10[j], a5[j]) : 0.f;
         }
+        store8_bf16(smem + S::da, ri, c8, 64, a10);
         // dO Vn^T again and Q K^T: R's first term dM * (Q K^T) = (dO Vn^T) * (Q K^T) * Gamma
-        tmem_ld16x2(tmem_lane_addr(B0, warp, tok0), a5, tmem_lane_addr(B3, warp, tok0), a10);
-        const float Gi = rowthr ? sG[ri] : 0.f;
+        tmem_ld8hx2(tmem_lane_addr(B0, warp, tok0), a5, tmem_lane_addr(B3, warp, tok0), a10);
+        const float Gi = sG[ri];
 #pragma unroll
-        for (int j = 0; j < 16; ++j)
-          rv[j] = (rowthr && tok0 + j < ri) ? a5[j] * a10[j] * __expf(Gi - sG[tok0 + j]) : 0.f;
+        for (int j = 0; j < 8; ++j) rv[j] = (c8 + j < ri) ? a5[j] * a10[j] * __expf(Gi - sG[c8 + j]) : 0.f;
       }
       GD_TRACE_AT(ws, lay, 32 * n + 7);
       tc_fence_before();
@@ -561,12 +561,9 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
       tc_fence_after();
       GD_TRACE_AT(ws, lay, 32 * n + 13);
       {
-        float x[16];
-        tmem_ld16(tmem_lane_addr(B6, warp, tok0), x);
-        if (rowthr) {
-          store8_bf16(smem + S::t1, ri, tok0, 64, x);
-          store8_bf16(smem + S::t1, ri, tok0 + 8, 64, x + 8);
-        }
+        float x[8];
+        tmem_ld8h(tmem_lane_addr(B6, warp, tok0), x);
+        store8_bf16(smem + S::t1, ri, c8, 64, x);
       }
       tc_fence_before();
       fence_async_smem();
@@ -578,33 +575,28 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
       tc_fence_after();
       GD_TRACE_AT(ws, lay, 32 * n + 15);
       {
-        float x[16], kgrow[16];
-        tmem_ld16x2(tmem_lane_addr(B7, warp, tok0), x, tmem_lane_addr(B5, warp, tok0), kgrow);  // A^T T1, K K^T
+        float x[8], kgrow[8];
+        tmem_ld8hx2(tmem_lane_addr(B7, warp, tok0), x, tmem_lane_addr(B5, warp, tok0), kgrow);  // A^T T1, K K^T
         float pk = 0.f;
-        if (rowthr) {
-          const float Gi = sG[ri], bi = sB[ri];
+        const float Gi = sG[ri], bi = sB[ri];
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int jj = tok0 + j;
-            float pb = 0.f;
-            rv[j] = 0.f;
-            if (jj < ri) {
-              const float dl = -x[j];
-              const float gam = __expf(Gi - sG[jj]);
-              const float p = dl * gam;
-              rv[j] = dl * bi * kgrow[j] * gam;
-              pk = fmaf(p, kgrow[j], pk);
-              pb = bi * p;
-            }
-            x[j] = pb;
+        for (int j = 0; j < 8; ++j) {
+          const int jj = c8 + j;
+          float pb = 0.f;
+          rv[j] = 0.f;
+          if (jj < ri) {
+            const float dl = -x[j];
+            const float gam = __expf(Gi - sG[jj]);
+            const float p = dl * gam;
+            rv[j] = dl * bi * kgrow[j] * gam;
+            pk = fmaf(p, kgrow[j], pk);
+            pb = bi * p;
           }
-          store8_bf16(smem + S::da, ri, tok0, 64, x);
-          store8_bf16(smem + S::da, ri, tok0 + 8, 64, x + 8);
-          P(P_PK, quarter, ri) = pk;
-        } else {
-#pragma unroll
-          for (int j = 0; j < 16; ++j) rv[j] = 0.f;
+          x[j] = pb;
         }
+        store8_bf16(smem + S::da, ri, c8, 64, x);
+        pk += __shfl_xor_sync(0xffffffffu, pk, 16);  // the row's other 8 columns of this quarter
+        if (lane < 16) P(P_PK, quarter, ri) = pk;
       }
       tc_fence_before();
       fence_async_smem();

@@ -295,6 +295,56 @@ __device__ __forceinline__ void tmem_ld16x2(uint32_t a0, float (&v0)[16], uint32
   }
 }
 
+// An M = 64 accumulator (rows in lanes 0-15 of each 32-lane quadrant) read by a whole warp: shape 16x32bx2, thread
+// t < 16 gets row (quadrant base + t), columns [col, col + 8); thread t >= 16 the same row t - 16, columns
+// [col + 8, col + 16). taddr carries the quadrant's lane base and col.
+__device__ __forceinline__ void tmem_ld8h(uint32_t taddr, float (&v)[8]) {
+  uint32_t r[8];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.16x32bx2.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8], 8;\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Two such loads under one wait.
+__device__ __forceinline__ void tmem_ld8hx2(uint32_t a0, float (&v0)[8], uint32_t a1, float (&v1)[8]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.16x32bx2.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%16], 8;\n\t"
+      "tcgen05.ld.sync.aligned.16x32bx2.x8.b32 {%8,%9,%10,%11,%12,%13,%14,%15}, [%17], 8;\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(a0), "r"(a1)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    v0[i] = __uint_as_float(r[i]);
+    v1[i] = __uint_as_float(r[8 + i]);
+  }
+}
+
+// Reduce-scatter inside each 16-lane half of a warp: lane l gets the sum over its half's 16 lanes of v[l % 8]
+// (lanes l and l ^ 8 hold the same sum).
+__device__ __forceinline__ float halfwarp_reduce_scatter8(float (&v)[8]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int s = 4; s >= 1; s >>= 1) {
+    const bool upper = (lane & s) != 0;
+#pragma unroll
+    for (int k = 0; k < s; ++k) {
+      const float send = upper ? v[k] : v[k + s];
+      const float keep = upper ? v[k + s] : v[k];
+      v[k] = keep + __shfl_xor_sync(0xffffffffu, send, s);
+    }
+  }
+  return v[0] + __shfl_xor_sync(0xffffffffu, v[0], 8);
+}
+
 // TMEM address of column `col` in the lane quadrant of this warp (warps w, w+4, w+8, ... share a quadrant).
 __device__ __forceinline__ uint32_t tmem_lane_addr(uint32_t base, int warp, int col) {
   return base + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)col;
