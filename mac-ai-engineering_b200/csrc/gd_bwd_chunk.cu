@@ -295,7 +295,7 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
         long long t0 = clock64();
         while (!(g3 && g2 && kk && t1 && dl && p11 && g1n)) {
           bool progressed = false;
-          if (!g3 && mbar_try_wait(e1_done, par) && mbar_try_wait(qk_full, qpar)) {
+          if (!g3 && mbar_test(e1_done, par) && mbar_test(qk_full, qpar)) {
             tc_fence_after();
             mma_tiles(B6, DK, 64, 64, tK, true, 0, 0, tDmh, false, 0, false);    // (dM K)^T = K^T dM^T
             mma_tiles(B6, DK, 64, 64, tKl, true, 0, 0, tDmh, false, 0, true);
@@ -313,7 +313,7 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
             g3 = progressed = true;
           }
           // G2 after G3: its result is read after G3's
-          if (g3 && !g2 && mbar_try_wait(ds_full, par) && (n == 0 || mbar_try_wait(b5_free, (n - 1) & 1))) {
+          if (g3 && !g2 && mbar_test(ds_full, par) && (n == 0 || mbar_test(b5_free, (n - 1) & 1))) {
             tc_fence_after();
             mma_tiles(B5, DK, 64, DV, tDsh, false, 0, 0, tVnh, true, 0, false);  // (Vn dS^T)^T = dS Vn^T
             mma_tiles(B5, DK, 64, DV, tDsh, false, 0, 0, tVnl, true, 0, true);
@@ -321,7 +321,7 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
             mma_commit(g2_full);
             g2 = progressed = true;
           }
-          if (g2 && g3 && !kk && mbar_try_wait(eg2_done, par)) {
+          if (g2 && g3 && !kk && mbar_test(eg2_done, par)) {
             tc_fence_after();
             mma_tiles(B5, 64, 64, DK, tK, false, 0, 0, tK, true, 0, false);      // K K^T
             mma_tiles(B5, 64, 64, DK, tK, false, 0, 0, tKl, true, 0, true);
@@ -329,24 +329,25 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
             mma_commit(kk_full);
             kk = progressed = true;
           }
-          if (g3 && !t1 && mbar_try_wait(e2_done, par)) {
+          if (g3 && !t1 && mbar_test(e2_done, par)) {
             tc_fence_after();
             mma_tiles(B6, 64, 64, 64, tDa, true, 0, 0, tA, false, 0, false);     // T1 = dA A^T
             mma_commit(t1_full);
             t1 = progressed = true;
           }
-          if (t1 && !dl && mbar_try_wait(e3_done, par)) {
+          if (t1 && !dl && mbar_test(e3_done, par)) {
             tc_fence_after();
             mma_tiles(B7, 64, 64, 64, tA, false, 0, 0, tT1, true, 0, false);     // A^T T1
             mma_commit(dl_full);
             dl = progressed = true;
           }
-          if (t1 && !g1n && mbar_try_wait(in_full, par ^ 1) && mbar_try_wait(a_full, par ^ 1)) {
+          // the next sub-item's G1 after P11 (P11 is on the chain; G1 has the whole final phase to run)
+          if (p11 && !g1n && mbar_test(in_full, par ^ 1) && mbar_test(a_full, par ^ 1)) {
             tc_fence_after();
             issue_g1();  // the next sub-item's first products (B0-B4 were read before e2_done)
             g1n = progressed = true;
           }
-          if (dl && kk && !p11 && mbar_try_wait(e4_done, par)) {
+          if (dl && kk && !p11 && mbar_test(e4_done, par)) {
             tc_fence_after();
             mma_tiles(B5, DK, 64, 64, tK, true, 0, 0, tDa, true, 0, false);      // K^T P_beta
             mma_tiles(B5, DK, 64, 64, tK, true, 0, 0, tDa, false, 0, true);      //  + K^T P_beta^T
@@ -355,7 +356,10 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
           }
           if (progressed) {
             t0 = clock64();
-          } else if (clock64() - t0 > kWaitCycles) {
+          } else {
+            __nanosleep(32);  // leave the sub-partition's issue slots to the epilogue warps
+          }
+          if (!progressed && clock64() - t0 > kWaitCycles) {
             report(err, GD_ERR_TIMEOUT, 100 + (g3 ? 1 : 0) + (g2 ? 2 : 0) + (t1 ? 4 : 0) + (dl ? 8 : 0) + (kk ? 16 : 0));
             ok = false;
             break;

@@ -98,6 +98,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking test of the phase with this parity (for threads that poll several barriers in turn: try_wait may
+// suspend the thread on one barrier while another becomes ready).
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Waits for the phase with this parity to complete. Returns false (and records a timeout) if it does not within the
 // poll limit; callers then skip their remaining work and go to clean-up.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, ErrorWord* err, int where) {
