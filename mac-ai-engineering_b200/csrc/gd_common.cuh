@@ -342,6 +342,21 @@ __device__ __forceinline__ void tmem_ld8hx2(uint32_t a0, float (&v0)[8], uint32_
   }
 }
 
+// The same shape with 16 columns per half: thread t < 16 gets row (base + t), columns [col, col + 16); thread t >= 16
+// row t - 16, columns [col + 16, col + 32).
+__device__ __forceinline__ void tmem_ld16h(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.16x32bx2.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16], 16;\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 // Reduce-scatter inside each 16-lane half of a warp: lane l gets the sum over its half's 16 lanes of v[l % 8]
 // (lanes l and l ^ 8 hold the same sum).
 __device__ __forceinline__ float halfwarp_reduce_scatter8(float (&v)[8]) {
@@ -535,6 +550,31 @@ __device__ __forceinline__ void store_token_rows(float (&v)[16], T* out, size_t 
     const int t = tok + 8 * blk + L;
     if (t < T_) store8<T>(out + (size_t)t * tok_stride + d0, v + 8 * blk);
   }
+}
+
+// One 8 x 8 block of the above: v[8] at head-dimension index d0 + lane % 8 for tokens tok .. tok + 7; after the
+// transpose lane L stores token tok + L (if below T_) at d0 .. d0 + 7.
+template <typename T>
+__device__ __forceinline__ void store_token_rows8(float (&v)[8], T* out, size_t tok_stride, int tok, int T_, int d0) {
+  const int L = threadIdx.x & 7;
+#pragma unroll
+  for (int s = 4; s >= 1; s >>= 1) {
+    const bool upper = (L & s) != 0;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      if ((e & s) == 0) {
+        const float send = upper ? v[e] : v[e + s];
+        const float recv = __shfl_xor_sync(0xffffffffu, send, s);
+        if (upper) {
+          v[e] = recv;
+        } else {
+          v[e + s] = recv;
+        }
+      }
+    }
+  }
+  const int t = tok + L;
+  if (t < T_) store8<T>(out + (size_t)t * tok_stride + d0, v);
 }
 
 __device__ __forceinline__ float warp_sum(float x) {

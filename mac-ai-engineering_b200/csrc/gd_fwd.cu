@@ -326,30 +326,34 @@ __global__ void __launch_bounds__(256, 2) prep_kernel(const T* __restrict__ q, c
 }
 
 // ------------------------------------------------------------------------------------------------------------------
-// forward state pass (warp-specialised)
+// forward state pass (warp-specialised, value-split)
 //
-// One CTA per (value head, batch row): 16 epilogue warps + 1 MMA warp. Epilogue warp w reads TMEM lane quadrant w % 4
-// (value columns 32 (w % 4) .. +31, one per lane) and one quarter of each accumulator's columns: tokens
-// 16 (w / 4) .. +15 of the [DV x 64] products, key rows 32 (w / 4) .. +31 of the [DV x DK] state update; it holds the
-// fp32 state S[32 (w / 4) + j][v] in registers. One thread of warp 16 issues every MMA and bulk copy. Hand-offs are
-// mbarriers only: an MMA issue blocks its thread until the tensor pipe takes it, so the MMA thread never joins a
-// barrier with the epilogue warps (that would serialise MMA time with epilogue time). Per chunk c:
+// Two CTAs per (value head, batch row), each owning 64 of the 128 value columns (the recurrence never mixes value
+// columns: Vn = U - W S, S <- e S + K~^T Vn and O = gamma Q S + M Vn act on each column of S alone), so the pass runs
+// on twice the SMs with half the work per chunk step. 16 epilogue warps + 1 MMA warp. Every product is M = 64 (the
+// CTA's value columns on TMEM lanes 0-15 of each quadrant) and is read whole-warp (16x32bx2): warp w (quadrant w % 4,
+// quarter w / 4) thread t holds value column 16 (w % 4) + t % 16 and tokens 16 (w / 4) + 8 (t / 16) .. + 7 of the
+// [64 x 64] products, key rows 32 (w / 4) + 16 (t / 16) .. + 15 of the [64 x DK] state update; it keeps the fp32
+// state S[those key rows][its column] in registers. One thread of warp 16 issues every MMA and bulk copy; hand-offs
+// are mbarriers only. Per chunk c:
 //   MMA: wait stage c and the S tile -> (W S)^T -> ws_full; (Q S)^T -> qs_full[c & 1]
 //   EPI: wait ws_full -> Vn = U - W S (U prefetched into registers) -> Vn^T hi / lo tiles -> vn_full
-//   MMA: wait vn_full -> (K~^T Vn)^T, three products (K~ = diag(e) K and Vn split) -> ds_full (the commit also covers
-//        (Q S)^T, the last reader of the S tile); (M Vn)^T -> mv_full; stage_free[c & 1]
+//   MMA: refill the stage of chunk c - 1 with chunk c + 1 once chunk c - 1's readers are done; wait vn_full ->
+//        (K~^T Vn)^T, three products (K~ = diag(e) K and Vn split) -> ds_full; (M Vn)^T -> mv_full; stage_free[c & 1]
 //   EPI: wait ds_full -> S <- exp(G_last) S + K~^T Vn -> S tile -> st_full
-//   EPI: wait qs_full, mv_full -> O = diag(gamma) Q S + M Vn -> global
-//   MMA: wait stage_free[c & 1] -> refill the stage with chunk c + 2 (bulk copies, two stages in flight)
-// With GD_STORE_STATES (the backward's recompute) O is not formed; the pass keeps S_c^T (fp32 and a bf16 image) and
-// the Vn^T hi / lo images of every chunk for the backward kernels.
+//   EPI: wait qs_full, mv_full -> O = diag(gamma) Q S + M Vn -> global (16-byte rows after an 8 x 8 transpose)
+// With GD_STORE_STATES (the backward's recompute) O is not formed; the pass keeps S_c (fp32 and a bf16 S_c^T image) and
+// the Vn^T hi / lo images of every chunk for the backward kernels (each CTA its 64 rows of them).
+
+constexpr int kVsplit = 2;  // CTAs per (value head, batch row)
 
 template <int DK, int DV>
 struct StateSmem {
-  static constexpr size_t st = 0;                          // [DV x DK] bf16 S^T (rows v, cols dk)
-  static constexpr size_t vh = st + DV * DK * 2;           // [DV x 64] Vn^T hi
-  static constexpr size_t vl = vh + DV * 64 * 2;           //            lo
-  static constexpr size_t stage0 = vl + DV * 64 * 2;       // two input stages, each:
+  static constexpr int DVH = DV / kVsplit;                 // value columns per CTA
+  static constexpr size_t st = 0;                          // [DVH x DK] bf16 S^T (rows v, cols dk)
+  static constexpr size_t vh = st + DVH * DK * 2;          // [DVH x 64] Vn^T hi
+  static constexpr size_t vl = vh + DVH * 64 * 2;          //             lo
+  static constexpr size_t stage0 = vl + DVH * 64 * 2;      // two input stages, each:
   static constexpr size_t s_wt = 0;                        //   [DK x 64] W^T image
   static constexpr size_t s_q = s_wt + DK * 64 * 2;        //   [DK x 64] q image (hi, transposed)
   static constexpr size_t s_kt = s_q + 64 * DK * 2;        //   [2][64 x DK] K~ hi, lo
@@ -378,11 +382,13 @@ template <typename T, int DK, int DV>
 __global__ void __launch_bounds__(544) state_kernel(const float* __restrict__ s0, T* __restrict__ o,
                                                        float* __restrict__ sT, Layout lay, int flags,
                                                        unsigned char* __restrict__ ws) {
-  static_assert(DV == 128 && DK == 128, "one TMEM lane per value column; four epilogue warps per lane quadrant");
+  static_assert(DV == 128 && DK == 128, "64 value columns per CTA on TMEM lanes 0-15 of each quadrant");
   using S = StateSmem<DK, DV>;
+  constexpr int DVH = S::DVH;
   extern __shared__ __align__(1024) unsigned char smem[];
   ErrorWord* err = reinterpret_cast<ErrorWord*>(ws + lay.err);
-  const int h = blockIdx.x, b = blockIdx.y;
+  const int half = blockIdx.x % kVsplit, h = blockIdx.x / kVsplit, b = blockIdx.y;
+  const int vbase = DVH * half;  // this CTA's first value column
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::bar);
   uint64_t* full = bars + 0;        // [2] stage loaded (bulk-copy bytes)
@@ -416,7 +422,7 @@ __global__ void __launch_bounds__(544) state_kernel(const float* __restrict__ s0
   __syncthreads();
   tc_fence_after();
   const uint32_t tm = *tslot;
-  const uint32_t tWS = tm, tMV = tm + 192, tDS = tm + 256;  // (Q S)^T at tm + 64 + 64 (c & 1)
+  const uint32_t tWS = tm, tMV = tm + 192, tDS = tm + 256;  // (Q S)^T at tm + 64 + 64 (c & 1); (K~^T Vn)^T 128 wide
   const Tile tSt{smem_u32(smem + S::st), DK};
   const Tile tVh{smem_u32(smem + S::vh), 64}, tVl{smem_u32(smem + S::vl), 64};
   bool ok = true;
@@ -433,14 +439,14 @@ __global__ void __launch_bounds__(544) state_kernel(const float* __restrict__ s0
         ok = mbar_wait(full + s, par2, err, 20) && mbar_wait(st_full, c & 1, err, 21);
         if (!ok) break;
         tc_fence_after();
-        if (store) {  // S_c^T image for the backward (bulk copy out; its reads finish before the tile is rewritten)
-          bulk_s2g(ws + lay.sci + (row0 + c) * lay.si_bytes(), smem + S::st, (uint32_t)lay.si_bytes());
+        if (store) {  // this CTA's rows of the S_c^T image (bulk copy out; done reading before the tile is rewritten)
+          bulk_s2g(ws + lay.sci + (row0 + c) * lay.si_bytes() + (size_t)vbase * DK * 2, smem + S::st, DVH * DK * 2);
           bulk_commit();
         }
-        mma_tiles(tWS, DV, 64, DK, tSt, true, 0, 0, Tile{smem_u32(stg + S::s_wt), 64}, true, 0, false);
+        mma_tiles(tWS, DVH, 64, DK, tSt, true, 0, 0, Tile{smem_u32(stg + S::s_wt), 64}, true, 0, false);
         mma_commit(ws_full);
         if (out) {
-          mma_tiles(tm + 64 + 64 * s, DV, 64, DK, tSt, true, 0, 0, Tile{smem_u32(stg + S::s_q), 64}, true, 0,
+          mma_tiles(tm + 64 + 64 * s, DVH, 64, DK, tSt, true, 0, 0, Tile{smem_u32(stg + S::s_q), 64}, true, 0,
                     false);
           mma_commit(qs_full + s);
         }
@@ -456,56 +462,62 @@ __global__ void __launch_bounds__(544) state_kernel(const float* __restrict__ s0
         ok = mbar_wait(vn_full, c & 1, err, 22);
         if (!ok) break;
         tc_fence_after();
-        if (store) {
-          bulk_s2g(ws + lay.vni + (row0 + c) * lay.vn_bytes(), smem + S::vh, (uint32_t)lay.vn_bytes());
+        if (store) {  // this CTA's rows of the Vn^T hi and lo images
+          unsigned char* vn = ws + lay.vni + (row0 + c) * lay.vn_bytes() + (size_t)vbase * 64 * 2;
+          bulk_s2g(vn, smem + S::vh, DVH * 64 * 2);
+          bulk_s2g(vn + DV * 64 * 2, smem + S::vl, DVH * 64 * 2);
           bulk_commit();
         }
         const Tile tKh{smem_u32(stg + S::s_kt), DK}, tKl{smem_u32(stg + S::s_kt + 64 * DK * 2), DK};
-        mma_tiles(tDS, DV, DK, 64, tVh, true, 0, 0, tKh, true, 0, false);
-        mma_tiles(tDS, DV, DK, 64, tVh, true, 0, 0, tKl, true, 0, true);
-        mma_tiles(tDS, DV, DK, 64, tVl, true, 0, 0, tKh, true, 0, true);
+        mma_tiles(tDS, DVH, DK, 64, tVh, true, 0, 0, tKh, true, 0, false);
+        mma_tiles(tDS, DVH, DK, 64, tVh, true, 0, 0, tKl, true, 0, true);
+        mma_tiles(tDS, DVH, DK, 64, tVl, true, 0, 0, tKh, true, 0, true);
         if (store) bulk_wait_read0();  // the S^T and Vn^T tiles may be rewritten once ds_full fires
         mma_commit(ds_full);
         if (out) {
           const Tile tM{smem_u32(stg + S::s_m), 64};
-          mma_tiles(tMV, DV, 64, 64, tVh, true, 0, 0, tM, false, 0, false);
-          mma_tiles(tMV, DV, 64, 64, tVl, true, 0, 0, tM, false, 0, true);
+          mma_tiles(tMV, DVH, 64, 64, tVh, true, 0, 0, tM, false, 0, false);
+          mma_tiles(tMV, DVH, 64, 64, tVl, true, 0, 0, tM, false, 0, true);
           mma_commit(mv_full);
         }
         mma_commit(stage_free + s);
       }
       if (store) bulk_wait0();
     }
+    __syncwarp();
   } else {
     // ---------------- epilogue warps
     const int qd = warp & 3, quarter = warp >> 2;
-    const int v = 32 * qd + lane;   // value column = TMEM lane
-    const int tk0 = 16 * quarter;   // tokens of the [DV x 64] accumulators
-    const int dk0 = 32 * quarter;   // key rows of the state held here
-    float Sr[32];                   // S[dk0 + j][v]
+    const int vl_ = 16 * qd + (lane & 15);               // local value column (TMEM lane within the quadrant)
+    const int v = vbase + vl_;                           // value column
+    const int tk = 16 * quarter + 8 * (lane >> 4);       // tokens tk .. tk + 7 of the [64 x 64] products
+    const int dk0 = 32 * quarter + 16 * (lane >> 4);     // key rows dk0 .. dk0 + 15 of the state held here
+    float Sr[16];                                        // S[dk0 + j][v]
     {
       const float* p = s0 ? s0 + ((size_t)b * lay.H + h) * DK * DV : nullptr;
 #pragma unroll
-      for (int j = 0; j < 32; ++j) Sr[j] = p ? p[(size_t)(dk0 + j) * DV + v] : 0.f;
+      for (int j = 0; j < 16; ++j) Sr[j] = p ? p[(size_t)(dk0 + j) * DV + v] : 0.f;
 #pragma unroll
-      for (int q8 = 0; q8 < 4; ++q8) store8_bf16(smem + S::st, v, dk0 + 8 * q8, DK, Sr + 8 * q8);
+      for (int q8 = 0; q8 < 2; ++q8) store8_bf16(smem + S::st, vl_, dk0 + 8 * q8, DK, Sr + 8 * q8);
       fence_async_smem();
       mbar_arrive_warp(st_full);
     }
-    // the fp32 state entering chunk c, for the backward (coalesced: lanes write adjacent 16-byte pieces)
+    // the fp32 state entering chunk c, for the backward (lanes 0-15 / 16-31 write adjacent 16-byte pieces)
     auto store_scf = [&](int c) {
-      float4* sc = reinterpret_cast<float4*>(ws + lay.scf + (row0 + c) * lay.s_bytes()) + (size_t)quarter * 8 * DV + v;
+      float4* sc = reinterpret_cast<float4*>(ws + lay.scf + (row0 + c) * lay.s_bytes()) +
+                   (size_t)(quarter * 8 + 4 * (lane >> 4)) * DV + v;
 #pragma unroll
-      for (int q4 = 0; q4 < 8; ++q4)
+      for (int q4 = 0; q4 < 4; ++q4)
         sc[(size_t)q4 * DV] = make_float4(Sr[4 * q4], Sr[4 * q4 + 1], Sr[4 * q4 + 2], Sr[4 * q4 + 3]);
     };
     if (store) store_scf(0);
-    float Ur[16];
-    {
-      const float* u = reinterpret_cast<const float*>(ws + lay.u + row0 * lay.u_bytes());
+    float Ur[8];
+    auto load_u = [&](size_t cidx) {
+      const float* u = reinterpret_cast<const float*>(ws + lay.u + cidx * lay.u_bytes());
 #pragma unroll
-      for (int j = 0; j < 16; ++j) Ur[j] = __ldg(u + (tk0 + j) * DV + v);
-    }
+      for (int j = 0; j < 8; ++j) Ur[j] = __ldg(u + (tk + j) * DV + v);
+    };
+    load_u(row0);
     for (int c = 0; c < NT; ++c) {
       const size_t cidx = row0 + c;
       const int s = c & 1;
@@ -517,36 +529,28 @@ __global__ void __launch_bounds__(544) state_kernel(const float* __restrict__ s0
       tc_fence_after();
       const float gl = __expf(sG[63]);
       {
-        float acc[16], vn[16];
-        tmem_ld16(tmem_lane_addr(tWS, warp, tk0), acc);
+        float acc[8];
+        tmem_ld8h(tmem_lane_addr(tWS, warp, 16 * quarter), acc);
 #pragma unroll
-        for (int j = 0; j < 16; ++j) vn[j] = Ur[j] - acc[j];
-        store8_split(smem + S::vh, smem + S::vl, v, tk0, 64, vn);
-        store8_split(smem + S::vh, smem + S::vl, v, tk0 + 8, 64, vn + 8);
+        for (int j = 0; j < 8; ++j) acc[j] = Ur[j] - acc[j];
+        store8_split(smem + S::vh, smem + S::vl, vl_, tk, 64, acc);
         tc_fence_before();
         fence_async_smem();
         mbar_arrive_warp(vn_full);
       }
       GD_TRACE_AT(ws, lay, 8 * c + 2);
-      if (c + 1 < NT) {  // next chunk's U into registers while the tensor core works
-        const float* u = reinterpret_cast<const float*>(ws + lay.u + (cidx + 1) * lay.u_bytes());
-#pragma unroll
-        for (int j = 0; j < 16; ++j) Ur[j] = __ldg(u + (tk0 + j) * DV + v);
-      }
+      if (c + 1 < NT) load_u(cidx + 1);  // next chunk's U into registers while the tensor core works
       // * S <- exp(G_last) S + K~^T Vn
       if (!mbar_wait(ds_full, c & 1, err, 25)) { ok = false; break; }
       GD_TRACE_AT(ws, lay, 8 * c + 3);
       tc_fence_after();
       {
         float d[16];
-        tmem_ld16(tmem_lane_addr(tDS, warp, dk0), d);
+        tmem_ld16h(tmem_lane_addr(tDS, warp, 32 * quarter), d);
 #pragma unroll
         for (int j = 0; j < 16; ++j) Sr[j] = fmaf(gl, Sr[j], d[j]);
-        tmem_ld16(tmem_lane_addr(tDS, warp, dk0 + 16), d);
 #pragma unroll
-        for (int j = 0; j < 16; ++j) Sr[16 + j] = fmaf(gl, Sr[16 + j], d[j]);
-#pragma unroll
-        for (int q8 = 0; q8 < 4; ++q8) store8_bf16(smem + S::st, v, dk0 + 8 * q8, DK, Sr + 8 * q8);
+        for (int q8 = 0; q8 < 2; ++q8) store8_bf16(smem + S::st, vl_, dk0 + 8 * q8, DK, Sr + 8 * q8);
         tc_fence_before();
         fence_async_smem();
         mbar_arrive_warp(st_full);
@@ -561,14 +565,12 @@ __global__ void __launch_bounds__(544) state_kernel(const float* __restrict__ s0
         }
         GD_TRACE_AT(ws, lay, 8 * c + 7);
         tc_fence_after();
-        float qs[16], mv[16];
-        tmem_ld16(tmem_lane_addr(tm + 64 + 64 * s, warp, tk0), qs);
-        tmem_ld16(tmem_lane_addr(tMV, warp, tk0), mv);
-        const int t0 = c * C;
+        float qs[8], mv[8];
+        tmem_ld8hx2(tmem_lane_addr(tm + 64 + 64 * s, warp, 16 * quarter), qs, tmem_lane_addr(tMV, warp, 16 * quarter), mv);
 #pragma unroll
-        for (int j = 0; j < 16; ++j) qs[j] = fmaf(__expf(sG[tk0 + j]), qs[j], mv[j]);
-        store_token_rows<T>(qs, o + ((size_t)b * lay.T * lay.H + h) * DV, (size_t)lay.H * DV, t0 + tk0, lay.T,
-                            32 * qd + 8 * (lane >> 3));
+        for (int j = 0; j < 8; ++j) qs[j] = fmaf(__expf(sG[tk + j]), qs[j], mv[j]);
+        store_token_rows8<T>(qs, o + ((size_t)b * lay.T * lay.H + h) * DV, (size_t)lay.H * DV, c * C + tk, lay.T,
+                             vbase + 16 * qd + 8 * ((lane >> 3) & 1));
         tc_fence_before();
       }
       mbar_arrive_warp(stage_epi + s);  // this warp is done reading chunk c's stage
@@ -577,7 +579,7 @@ __global__ void __launch_bounds__(544) state_kernel(const float* __restrict__ s0
     if (ok && sT != nullptr) {
       float* sp = sT + ((size_t)b * lay.H + h) * DK * DV;
 #pragma unroll
-      for (int j = 0; j < 32; ++j) sp[(size_t)(dk0 + j) * DV + v] = Sr[j];
+      for (int j = 0; j < 16; ++j) sp[(size_t)(dk0 + j) * DV + v] = Sr[j];
     }
   }
   tc_fence_before();
@@ -612,7 +614,7 @@ cudaError_t launch_state(const float* s0, void* o, float* sT, const Layout& lay,
   static bool attr_done[kMaxDevices] = {};  // once per device: no attribute call inside a graph capture
   cudaError_t e = set_smem_once(kern, S::total, attr_done);
   if (e != cudaSuccess) return e;
-  dim3 grid(lay.H, lay.B);
+  dim3 grid(lay.H * kVsplit, lay.B);
   kern<<<grid, 544, S::total, st>>>(s0, static_cast<T*>(o), sT, lay, flags, ws);
   return cudaGetLastError();
 }
