@@ -1,6 +1,7 @@
 // Reverse state pass of the chunked gated delta rule on B200 (sm_100a).
 //
-// One CTA per (value head, batch row) walks the chunks last to first carrying dS = dLoss/dS (fp32, in registers):
+// Two CTAs per (value head, batch row), each owning 64 value columns (column v of dVn and dS depends on column v of dO
+// and dS alone), walk the chunks last to first carrying dS = dLoss/dS (fp32, in registers):
 //   dVn = M^T dO + K~ dS_{c+1}                       (K~ = diag(e) K: the decay e of the state update)
 //   dS_c = exp(G_last) dS_{c+1} + (diag(gamma) Q)^T dO - W^T dVn
 // (tools/check_chunk_equations.py:51-52 and src/macai/gated_delta/_chunked.py:20-24 of the reference). Only K~ dS and
@@ -8,9 +9,9 @@
 // It keeps, per chunk, the images the per-chunk gradient kernel reads: dS_{c+1}^T (hi, lo), dVn^T (hi, lo), dO, and
 // the 16 partial sums of <S_c, dS_{c+1}> (from the forward recompute's fp32 S_c^T).
 //
-// Warp specialisation as in the forward pass: 16 epilogue warps (warp w: TMEM lane quadrant w % 4 = value columns,
-// tokens 16 (w / 4) .. +15, key rows 32 (w / 4) .. +31 of dS held in registers) and one MMA / bulk-copy thread; all
-// hand-offs are mbarriers. Precision: dS and K~ split into bf16 hi + lo (three products), gamma Q split, the rest bf16.
+// Warp specialisation as in the forward pass: 16 epilogue warps reading the M = 64 products whole-warp (thread t of
+// warp w: local value column 16 (w % 4) + t % 16, 8 tokens and 16 key rows of dS held in registers) and one MMA /
+// bulk-copy thread; all hand-offs are mbarriers. Precision: dS and K~ split into bf16 hi + lo (three products), gamma Q split, the rest bf16.
 #include "gd_common.cuh"
 #include "gd_layout.cuh"
 
@@ -18,18 +19,19 @@ namespace gd {
 
 template <int DK, int DV>
 struct BwdStateSmem {
-  static constexpr size_t dsh = 0;                         // [DV x DK] dS^T hi (rows v, cols dk)
-  static constexpr size_t dsl = dsh + DV * DK * 2;         //            lo
-  static constexpr size_t dvh = dsl + DV * DK * 2;         // [DV x 64] dVn^T hi
-  static constexpr size_t crit0 = dvh + DV * 64 * 2;       // two stages of the sequential chain, each:
+  static constexpr int DVH = DV / 2;                       // value columns per CTA (two CTAs per head and row)
+  static constexpr size_t dsh = 0;                         // [DVH x DK] dS^T hi (rows v, cols dk)
+  static constexpr size_t dsl = dsh + DVH * DK * 2;        //             lo
+  static constexpr size_t dvh = dsl + DVH * DK * 2;        // [DVH x 64] dVn^T hi
+  static constexpr size_t crit0 = dvh + DVH * 64 * 2;      // two stages of the sequential chain, each:
   static constexpr size_t c_kt = 0;                        //   [2][64 x DK] K~ hi, lo
   static constexpr size_t c_g = c_kt + 2 * 64 * DK * 2;    //   [64] G
   static constexpr size_t crit_bytes = c_g + 64 * 4;
   static constexpr size_t wt = crit0 + 2 * crit_bytes;     // [DK x 64] W^T (one buffer)
   static constexpr size_t m = wt + DK * 64 * 2;            // [64 x 64] M        } inputs of the dS-independent
   static constexpr size_t gq = m + 64 * 64 * 2;            // [2][64 x DK] gamma Q }  products, one chunk ahead
-  static constexpr size_t dO = gq + 2 * 64 * DK * 2;       // [64 x DV] dO       }
-  static constexpr size_t bar = dO + 64 * DV * 2;
+  static constexpr size_t dO = gq + 2 * 64 * DK * 2;       // [64 x DVH] dO      }
+  static constexpr size_t bar = dO + 64 * DVH * 2;
   static constexpr int NBAR = 12;
   static constexpr size_t tmem = bar + NBAR * 8;
   static constexpr size_t total = tmem + 8;
@@ -39,11 +41,13 @@ template <typename T, int DK, int DV>
 __global__ void __launch_bounds__(544) bwd_state_kernel(const T* __restrict__ d_o, const float* __restrict__ dsT,
                                                         float* __restrict__ ds0, Layout lay, int flags,
                                                         unsigned char* __restrict__ ws) {
-  static_assert(DV == 128 && DK == 128, "one TMEM lane per value column; four epilogue warps per lane quadrant");
+  static_assert(DV == 128 && DK == 128, "64 value columns per CTA on TMEM lanes 0-15 of each quadrant");
   using S = BwdStateSmem<DK, DV>;
+  constexpr int DVH = S::DVH;
   extern __shared__ __align__(1024) unsigned char smem[];
   ErrorWord* err = reinterpret_cast<ErrorWord*>(ws + lay.err);
-  const int h = blockIdx.x, b = blockIdx.y;
+  const int half = blockIdx.x & 1, h = blockIdx.x >> 1, b = blockIdx.y;
+  const int vbase = DVH * half;  // this CTA's first value column
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::bar);
   uint64_t* crit_full = bars + 0;   // [2] K~, G loaded
@@ -72,7 +76,8 @@ __global__ void __launch_bounds__(544) bwd_state_kernel(const T* __restrict__ d_
   __syncthreads();
   tc_fence_after();
   const uint32_t tm = *tslot;
-  const uint32_t tA = tm, tB = tm + 64, tD = tm + 384;  // ((gamma Q)^T dO)^T at tm + 128 + 128 (n & 1)
+  // TMEM: (M^T dO)^T at tm, (K~ dS)^T at tm + 64, ((gamma Q)^T dO)^T at tm + 128 + 128 (n & 1), (W^T dVn)^T at tm + 384
+  const uint32_t tA = tm, tB = tm + 64, tD = tm + 384;
   bool ok = true;
 
   auto load_crit = [&](int c, int s) {
@@ -90,19 +95,23 @@ __global__ void __launch_bounds__(544) bwd_state_kernel(const T* __restrict__ d_
     bulk_g2s(smem + S::m, ws + lay.m + (row0 + c) * lay.m_bytes(), (uint32_t)lay.m_bytes(), pre_full);
     bulk_g2s(smem + S::gq, ws + lay.gq + (row0 + c) * lay.qk_bytes(), (uint32_t)lay.qk_bytes(), pre_full);
   };
-  const Tile tDO{smem_u32(smem + S::dO), DV};
-  // chunk c's dO image for the per-chunk kernel; its reads finish before the products that precede the tile's reuse
+  const Tile tDO{smem_u32(smem + S::dO), DVH};
+  // chunk c's dO image for the per-chunk kernel: this CTA's columns of each 8-row block (1 KB pieces of the
+  // [64 x DV] image); its reads finish before the products that precede the tile's reuse
   auto copy_do = [&](int c) {
-    bulk_s2g(ws + lay.doi + (row0 + c) * lay.vi_bytes(), smem + S::dO, (uint32_t)lay.vi_bytes());
+    unsigned char* dst = ws + lay.doi + (row0 + c) * lay.vi_bytes();
+#pragma unroll 1
+    for (int rb = 0; rb < 8; ++rb)
+      bulk_s2g(dst + ((size_t)rb * (DV / 8) + vbase / 8) * 128, smem + S::dO + rb * (DVH / 8) * 128, DVH / 8 * 128);
     bulk_commit();
     bulk_wait_read0();
   };
-  // (M^T dO)^T = dO^T M [DV x 64]; ((gamma Q)^T dO)^T = dO^T (gamma Q) [DV x DK], gamma Q split
+  // (M^T dO)^T = dO^T M [DVH x 64]; ((gamma Q)^T dO)^T = dO^T (gamma Q) [DVH x DK], gamma Q split
   auto issue_pre = [&](int n) {
-    mma_tiles(tA, DV, 64, 64, tDO, false, 0, 0, Tile{smem_u32(smem + S::m), 64}, true, 0, false);
+    mma_tiles(tA, DVH, 64, 64, tDO, false, 0, 0, Tile{smem_u32(smem + S::m), 64}, true, 0, false);
     const uint32_t tC = tm + 128 + 128 * (n & 1);
-    mma_tiles(tC, DV, DK, 64, tDO, false, 0, 0, Tile{smem_u32(smem + S::gq), DK}, true, 0, false);
-    mma_tiles(tC, DV, DK, 64, tDO, false, 0, 0, Tile{smem_u32(smem + S::gq + 64 * DK * 2), DK}, true, 0, true);
+    mma_tiles(tC, DVH, DK, 64, tDO, false, 0, 0, Tile{smem_u32(smem + S::gq), DK}, true, 0, false);
+    mma_tiles(tC, DVH, DK, 64, tDO, false, 0, 0, Tile{smem_u32(smem + S::gq + 64 * DK * 2), DK}, true, 0, true);
     mma_commit(a_full);
   };
 
@@ -126,19 +135,21 @@ __global__ void __launch_bounds__(544) bwd_state_kernel(const T* __restrict__ d_
         ok = mbar_wait(crit_full + s, (n >> 1) & 1, err, 32) && mbar_wait(ds_ready, n & 1, err, 33);
         if (!ok) break;
         tc_fence_after();
-        // dS_{c+1} images for the per-chunk kernel
-        bulk_s2g(ws + lay.dsi + cidx * 2 * lay.si_bytes(), smem + S::dsh, 2 * (uint32_t)lay.si_bytes());
+        // this CTA's rows of the dS_{c+1}^T images (hi, lo) for the per-chunk kernel
+        unsigned char* dsi = ws + lay.dsi + cidx * 2 * lay.si_bytes() + (size_t)vbase * DK * 2;
+        bulk_s2g(dsi, smem + S::dsh, DVH * DK * 2);
+        bulk_s2g(dsi + lay.si_bytes(), smem + S::dsl, DVH * DK * 2);
         bulk_commit();
         if (c > 0)  // the next chunk's fp32 state, for the epilogue's <S, dS> partial sums
           asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(ws + lay.scf + (cidx - 1) * lay.s_bytes()),
                        "r"((uint32_t)lay.s_bytes())
                        : "memory");
-        // * (K~ dS)^T = dS^T K~^T [DV x 64]: hi hi + hi lo + lo hi
+        // * (K~ dS)^T = dS^T K~^T [DVH x 64]: hi hi + hi lo + lo hi
         const Tile tKh{smem_u32(st + S::c_kt), DK}, tKl{smem_u32(st + S::c_kt + 64 * DK * 2), DK};
         const Tile tDh{smem_u32(smem + S::dsh), DK}, tDl{smem_u32(smem + S::dsl), DK};
-        mma_tiles(tB, DV, 64, DK, tDh, true, 0, 0, tKh, false, 0, false);
-        mma_tiles(tB, DV, 64, DK, tDh, true, 0, 0, tKl, false, 0, true);
-        mma_tiles(tB, DV, 64, DK, tDl, true, 0, 0, tKh, false, 0, true);
+        mma_tiles(tB, DVH, 64, DK, tDh, true, 0, 0, tKh, false, 0, false);
+        mma_tiles(tB, DVH, 64, DK, tDh, true, 0, 0, tKl, false, 0, true);
+        mma_tiles(tB, DVH, 64, DK, tDl, true, 0, 0, tKh, false, 0, true);
         mma_commit(b_full);
         // the dS-independent inputs of the next chunk can replace this chunk's once its products are done
         ok = mbar_wait(a_full, n & 1, err, 34);
@@ -147,15 +158,15 @@ __global__ void __launch_bounds__(544) bwd_state_kernel(const T* __restrict__ d_
         ok = mbar_wait(dvn_full, n & 1, err, 35) && mbar_wait(wt_full, n & 1, err, 36);
         if (!ok) break;
         tc_fence_after();
-        bulk_s2g(ws + lay.dvni + cidx * lay.vn_bytes(), smem + S::dvh, DV * 64 * 2);
+        bulk_s2g(ws + lay.dvni + cidx * lay.vn_bytes() + (size_t)vbase * 64 * 2, smem + S::dvh, DVH * 64 * 2);
         bulk_commit();
         bulk_wait_read0();  // the dS and dVn tiles may be rewritten once d_full fires
-        // * (W^T dVn)^T = dVn^T W [DV x DK]
-        mma_tiles(tD, DV, DK, 64, Tile{smem_u32(smem + S::dvh), 64}, true, 0, 0, Tile{smem_u32(smem + S::wt), 64},
+        // * (W^T dVn)^T = dVn^T W [DVH x DK]
+        mma_tiles(tD, DVH, DK, 64, Tile{smem_u32(smem + S::dvh), 64}, true, 0, 0, Tile{smem_u32(smem + S::wt), 64},
                   false, 0, false);
         mma_commit(d_full);
         if (c > 0) {
-          // refill this K~ stage with chunk c - 2 (its reader, (K~ dS)^T, is done: b_full precedes a_full... wait it)
+          // refill this K~ stage with chunk c - 2 once (K~ dS)^T, its reader, is done
           ok = mbar_wait(b_full, n & 1, err, 37);
           if (!ok) break;
           if (c > 1) load_crit(c - 2, s);
@@ -172,58 +183,47 @@ __global__ void __launch_bounds__(544) bwd_state_kernel(const T* __restrict__ d_
       }
       bulk_wait0();
     }
+    __syncwarp();
   } else {
-    // ---------------- epilogue warps
+    // ---------------- epilogue warps: thread t of warp w holds local value column 16 (w % 4) + t % 16, tokens
+    // 16 (w / 4) + 8 (t / 16) .. + 7 of the [64 x 64] products and key rows 32 (w / 4) + 16 (t / 16) .. + 15 of dS
     const int qd = warp & 3, quarter = warp >> 2;
-    const int v = 32 * qd + lane;
-    const int tk0 = 16 * quarter;
-    const int dk0 = 32 * quarter;
-    float Dr[32];  // dS[dk0 + j][v]
+    const int vl_ = 16 * qd + (lane & 15), v = vbase + vl_;
+    const int tk = 16 * quarter + 8 * (lane >> 4);
+    const int dk0 = 32 * quarter + 16 * (lane >> 4);
+    float Dr[16];  // dS[dk0 + j][v]
     auto write_ds = [&]() {
 #pragma unroll
-      for (int q8 = 0; q8 < 4; ++q8) store8_split(smem + S::dsh, smem + S::dsl, v, dk0 + 8 * q8, DK, Dr + 8 * q8);
+      for (int q8 = 0; q8 < 2; ++q8) store8_split(smem + S::dsh, smem + S::dsl, vl_, dk0 + 8 * q8, DK, Dr + 8 * q8);
       fence_async_smem();
       mbar_arrive_warp(ds_ready);
     };
-    // a chunk's dO tile: 1024 16-byte pieces, two per thread, eight consecutive threads per 128-byte core matrix;
-    // fetched into registers early (fetch_do) and written to the tile once the tile's readers are done (put_do)
-    Piece<T> dox[2];  // raw until written, so the loads stay in flight through the waits
+    // a chunk's dO tile (this CTA's 64 columns): 512 16-byte pieces, one per thread, eight consecutive threads per
+    // 128-byte core matrix; fetched raw into registers early, written to the tile once the tile's readers are done
+    Piece<T> dox;
+    const int prl = tid & 7, pcb = (tid >> 3) & 7, prb = tid >> 6;
     auto fetch_do = [&](int c) {
-      const int t0 = c * C;
-#pragma unroll
-      for (int p = 0; p < 2; ++p) {
-        const int idx = tid + 512 * p;
-        const int rl = idx & 7, cb = (idx >> 3) & 15, rb = idx >> 7;
-        const int t = t0 + 8 * rb + rl;
-        if (d_o != nullptr && t < lay.T) {
-          dox[p].load(d_o + (((size_t)b * lay.T + t) * lay.H + h) * DV + 8 * cb);
-        } else {
-          dox[p].zero();
-        }
+      const int t = c * C + 8 * prb + prl;
+      if (d_o != nullptr && t < lay.T) {
+        dox.load(d_o + (((size_t)b * lay.T + t) * lay.H + h) * DV + vbase + 8 * pcb);
+      } else {
+        dox.zero();
       }
     };
     auto put_do = [&]() {
-#pragma unroll
-      for (int p = 0; p < 2; ++p) {
-        const int idx = tid + 512 * p;
-        const int rl = idx & 7, cb = (idx >> 3) & 15, rb = idx >> 7;
-        float x[8];
-        dox[p].to_f32(x);
-        store8_bf16(smem + S::dO, 8 * rb + rl, 8 * cb, DV, x);
-      }
+      float x[8];
+      dox.to_f32(x);
+      store8_bf16(smem + S::dO, 8 * prb + prl, 8 * pcb, DVH, x);
       fence_async_smem();
       mbar_arrive_warp(do_full);
-    };
-    auto load_do = [&](int c) {
-      fetch_do(c);
-      put_do();
     };
     {
       const float* p = dsT ? dsT + ((size_t)b * lay.H + h) * DK * DV : nullptr;
 #pragma unroll
-      for (int j = 0; j < 32; ++j) Dr[j] = p ? p[(size_t)(dk0 + j) * DV + v] : 0.f;
+      for (int j = 0; j < 16; ++j) Dr[j] = p ? p[(size_t)(dk0 + j) * DV + v] : 0.f;
       write_ds();
-      load_do(NT - 1);
+      fetch_do(NT - 1);
+      put_do();
     }
     for (int n = 0; n < NT; ++n) {
       const int c = NT - 1 - n, s = n & 1;
@@ -237,28 +237,24 @@ __global__ void __launch_bounds__(544) bwd_state_kernel(const T* __restrict__ d_
       GD_TRACE_AT(ws, lay, 8 * n + 1);
       const float gl = __expf(sG[63]);
       {
-        float a[16], bb[16];
-        tmem_ld16(tmem_lane_addr(tA, warp, tk0), a);
-        tmem_ld16(tmem_lane_addr(tB, warp, tk0), bb);
+        float a[8], bb[8];
+        tmem_ld8hx2(tmem_lane_addr(tA, warp, 16 * quarter), a, tmem_lane_addr(tB, warp, 16 * quarter), bb);
 #pragma unroll
-        for (int j = 0; j < 16; ++j) split_bf16(a[j] + bb[j], a[j], bb[j]);  // in place: a = hi, bb = lo
-        store8_bf16(smem + S::dvh, v, tk0, 64, a);
-        store8_bf16(smem + S::dvh, v, tk0 + 8, 64, a + 8);
-        unsigned char* dlo = ws + lay.dvni + cidx * lay.vn_bytes() + DV * 64 * 2;  // the low half: straight to HBM
-        store8_bf16(dlo, v, tk0, 64, bb);
-        store8_bf16(dlo, v, tk0 + 8, 64, bb + 8);
+        for (int j = 0; j < 8; ++j) split_bf16(a[j] + bb[j], a[j], bb[j]);  // in place: a = hi, bb = lo
+        store8_bf16(smem + S::dvh, vl_, tk, 64, a);
+        store8_bf16(ws + lay.dvni + cidx * lay.vn_bytes() + DV * 64 * 2, v, tk, 64, bb);  // low half: straight to HBM
         tc_fence_before();
         fence_async_smem();
         mbar_arrive_warp(dvn_full);
       }
       GD_TRACE_AT(ws, lay, 8 * n + 2);
-      // partial <S_c, dS_{c+1}> of this thread's 32 entries (fp32 S_c from the forward recompute, prefetched into L2 a
-      // chunk ahead; the layout puts a warp's 16-byte pieces side by side): loads in flight through the wait for
-      // (W^T dVn)^T, consumed before dS moves on
-      const float4* sc = reinterpret_cast<const float4*>(ws + lay.scf + cidx * lay.s_bytes()) + (size_t)quarter * 8 * DV + v;
-      float4 sx[8];
+      // partial <S_c, dS_{c+1}> of this thread's 16 entries (fp32 S_c from the forward recompute, prefetched into L2 a
+      // chunk ahead; lanes read adjacent 16-byte pieces): loads in flight through the wait for (W^T dVn)^T
+      const float4* sc = reinterpret_cast<const float4*>(ws + lay.scf + cidx * lay.s_bytes()) +
+                         (size_t)(quarter * 8 + 4 * (lane >> 4)) * DV + v;
+      float4 sx[4];
 #pragma unroll
-      for (int q4 = 0; q4 < 8; ++q4) sx[q4] = __ldg(sc + (size_t)q4 * DV);
+      for (int q4 = 0; q4 < 4; ++q4) sx[q4] = __ldg(sc + (size_t)q4 * DV);
       // the next chunk's dO tile (this chunk's dO products are done: a_full; its image went out before they were
       // issued)
       if (c > 0) put_do();
@@ -269,20 +265,18 @@ __global__ void __launch_bounds__(544) bwd_state_kernel(const T* __restrict__ d_
       GD_TRACE_AT(ws, lay, 8 * n + 4);
       float sacc = 0.f;
 #pragma unroll
-      for (int q4 = 0; q4 < 8; ++q4)
+      for (int q4 = 0; q4 < 4; ++q4)
         sacc = fmaf(sx[q4].x, Dr[4 * q4], fmaf(sx[q4].y, Dr[4 * q4 + 1], fmaf(sx[q4].z, Dr[4 * q4 + 2],
                                                                               fmaf(sx[q4].w, Dr[4 * q4 + 3], sacc))));
       sacc = warp_sum(sacc);
-      if (lane == 0) reinterpret_cast<float*>(ws + lay.sl + cidx * 64)[warp] = sacc;
+      if (lane == 0) reinterpret_cast<float*>(ws + lay.sl + cidx * lay.sl_bytes())[16 * half + warp] = sacc;
       {
         const uint32_t tC = tm + 128 + 128 * (n & 1);
         float cc[16], dd[16];
+        tmem_ld16h(tmem_lane_addr(tC, warp, 32 * quarter), cc);
+        tmem_ld16h(tmem_lane_addr(tD, warp, 32 * quarter), dd);
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          tmem_ld16x2(tmem_lane_addr(tC, warp, dk0 + 16 * hh), cc, tmem_lane_addr(tD, warp, dk0 + 16 * hh), dd);
-#pragma unroll
-          for (int j = 0; j < 16; ++j) Dr[16 * hh + j] = fmaf(gl, Dr[16 * hh + j], cc[j] - dd[j]);
-        }
+        for (int j = 0; j < 16; ++j) Dr[j] = fmaf(gl, Dr[j], cc[j] - dd[j]);
         tc_fence_before();
       }
       if (c > 0) write_ds();
@@ -291,7 +285,7 @@ __global__ void __launch_bounds__(544) bwd_state_kernel(const T* __restrict__ d_
     if (ok && ds0 != nullptr) {
       float* p = ds0 + ((size_t)b * lay.H + h) * DK * DV;
 #pragma unroll
-      for (int j = 0; j < 32; ++j) p[(size_t)(dk0 + j) * DV + v] = Dr[j];
+      for (int j = 0; j < 16; ++j) p[(size_t)(dk0 + j) * DV + v] = Dr[j];
     }
   }
   tc_fence_before();
@@ -310,7 +304,7 @@ cudaError_t launch_bwd_state(const void* d_o, const float* dsT, float* ds0, cons
   static bool attr_done[kMaxDevices] = {};
   cudaError_t e = set_smem_once(kern, S::total, attr_done);
   if (e != cudaSuccess) return e;
-  dim3 grid(lay.H, lay.B);
+  dim3 grid(lay.H * 2, lay.B);
   kern<<<grid, 544, S::total, st>>>(static_cast<const T*>(d_o), dsT, ds0, lay, flags, ws);
   return cudaGetLastError();
 }

@@ -63,8 +63,8 @@ struct ChunkSmem {
   static constexpr size_t part = beta + 64 * 4;             // fp32 [6][4][64] per-token partial sums (see kernel)
   static constexpr size_t scr = part + 6 * 4 * 64 * 4;      // fp32 [2][4][64] exchange scratch
   static constexpr size_t rqk = scr + 2 * 4 * 64 * 4;       // fp32 [2][64] the item's l2 rsqrt of q, k rows
-  static constexpr size_t sl = rqk + 2 * 64 * 4;            // fp32 [2][16] <S_c, dS_{c+1}> partials (by parity)
-  static constexpr size_t bar = sl + 2 * 16 * 4;
+  static constexpr size_t sl = rqk + 2 * 64 * 4;            // fp32 [2][32] <S_c, dS_{c+1}> partials (by parity)
+  static constexpr size_t bar = sl + 2 * 32 * 4;
   static constexpr int NBAR = 22;
   static constexpr size_t tmem = bar + NBAR * 8;
   static constexpr size_t total = tmem + 16;
@@ -208,7 +208,7 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
       bool ok = true;
       int last_in = -1, last_a = -1, last_qk = -1, last_ds = -1;
       const uint32_t in_bytes =
-          (uint32_t)(lay.si_bytes() + 2 * lay.vi_bytes() + 2 * lay.vn_bytes() + lay.gc_bytes() + 64);
+          (uint32_t)(lay.si_bytes() + 2 * lay.vi_bytes() + 2 * lay.vn_bytes() + lay.gc_bytes() + lay.sl_bytes());
       for (int n = 0; n < nsub && ok; ++n) {
         const Item it = item_of(lay, n);
         if (n >= 1) ok = mbar_wait(g3_full, (n - 1) & 1, err, 60);  // dM / dW^T (the IN2 region) consumed
@@ -225,7 +225,7 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
         bulk_g2s(smem + S::in3, ws + lay.vni + it.cidx * lay.vn_bytes(), (uint32_t)lay.vn_bytes(), in_full);
         bulk_g2s(smem + S::g + (n & 1) * 256, ws + lay.gc + it.cidx * lay.gc_bytes(), (uint32_t)lay.gc_bytes(),
                  in_full);
-        bulk_g2s(smem + S::sl + (n & 1) * 64, ws + lay.sl + it.cidx * 64, 64, in_full);
+        bulk_g2s(smem + S::sl + (n & 1) * 128, ws + lay.sl + it.cidx * lay.sl_bytes(), (uint32_t)lay.sl_bytes(), in_full);
         if (n >= 1) ok = mbar_wait(dl_full, (n - 1) & 1, err, 63);  // A consumed
         if (!ok) break;
         mbar_arrive_expect_tx(a_full, (uint32_t)lay.m_bytes());
@@ -642,9 +642,9 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
           pk += P(P_PK, w, t);
         }
         float sl = 0.f;
-        const float* slp = reinterpret_cast<const float*>(smem + S::sl + (n & 1) * 64);
+        const float* slp = reinterpret_cast<const float*>(smem + S::sl + (n & 1) * 128);
 #pragma unroll
-        for (int w = 0; w < 16; ++w) sl += slp[w];
+        for (int w = 0; w < 32; ++w) sl += slp[w];
         const float gt = __expf(sG[t]);
         const float w_ = sB[t] * gt * kx;
         const float db = fmaf(gt, kx, vy) + pk;

@@ -24,7 +24,7 @@
 //   dsi  [2][DV x DK] image   dS_{c+1}^T: hi, then lo
 //   dvni [2][DV x 64] image   dVn^T: hi, then lo
 //   doi  [64 x DV]    image   dO
-//   sl   [16]         fp32    partial sums of <S_c, dS_{c+1}> (one per epilogue warp)
+//   sl   [32]         fp32    partial sums of <S_c, dS_{c+1}> (one per epilogue warp of the chunk's two CTAs)
 // Every array starts on a 256-byte boundary (bulk copies need 16).
 #pragma once
 
@@ -50,6 +50,7 @@ struct Layout {
   __host__ __device__ size_t s_bytes() const { return (size_t)DK * DV * 4; }       // fp32 state
   __host__ __device__ size_t si_bytes() const { return (size_t)DK * DV * 2; }      // one state image
   __host__ __device__ size_t vn_bytes() const { return (size_t)2 * DV * 64 * 2; }  // a [2][DV x 64] image pair
+  __host__ __device__ size_t sl_bytes() const { return (size_t)32 * 4; }           // <S, dS> partial sums
 
   __host__ static Layout make(int B, int T, int H, int HK, int DK, int DV, bool backward) {
     Layout L{};
@@ -84,7 +85,7 @@ struct Layout {
       L.dsi = take(L.nch * 2 * L.si_bytes());
       L.dvni = take(L.nch * L.vn_bytes());
       L.doi = take(L.nch * L.vi_bytes());
-      L.sl = take(L.nch * 64);
+      L.sl = take(L.nch * L.sl_bytes());
     } else {
       L.gq = L.ai = L.vi = L.rq = L.rk = L.scf = L.sci = L.vni = L.dsi = L.dvni = L.doi = L.sl = 0;
     }
