@@ -196,6 +196,10 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--profile", action="store_true",
+                    help="profiling case for ncu: --steps plain forward+backward calls through the C ABI (no graph, "
+                         "no timing, no CPU baseline), then exit; launch order per step: prep, state, prep, state "
+                         "(store), bwd_state, bwd_chunk")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     cfg = CONFIGS[args.config]
@@ -245,12 +249,15 @@ def main():
             _lib.check(st, "gd_backward")
 
     with torch.cuda.stream(stream):
-        for _ in range(2):
+        for _ in range(args.steps if args.profile else 2):
             step()
     stream.synchronize()
     code = lib.gd_read_error(P(ws), sp, None)
     if code != 0:
         raise RuntimeError(f"device error word {code} after warm-up")
+    if args.profile:
+        print(json.dumps({"profile": cfg["tag"], "steps": args.steps, "device_status": code}), flush=True)
+        return
 
     graph = None
     if not args.no_graph:
@@ -408,12 +415,34 @@ def roofline(kern, cfg, hbm, tflops, peak_kind):
     dur = kern[name] * 1e-6
     a_t = flop * units / dur / 1e12
     a_b = byts * units / dur / 1e9
+    traffic = measured_traffic(name, cfg)
+    extra = {"traffic_unit": "DRAM bytes per launch (ncu dram__bytes_read.sum + dram__bytes_write.sum, cold cache)",
+             "traffic_source": TRAFFIC_FILE if traffic is not None else None,
+             "algorithmic_bytes": byts * units, "algorithmic_flop": flop * units}
     if a_t / tflops >= a_b / hbm:
         return {"kernel": name, "bound": "tensor", "achieved": a_t, "peak": tflops, "unit": "TFLOP/s",
-                "frac": a_t / tflops, "traffic": None, "peak_source": peak_kind, "duration_us": kern[name],
-                "hbm_frac": a_b / hbm}
+                "frac": a_t / tflops, "traffic": traffic, "peak_source": peak_kind, "duration_us": kern[name],
+                "hbm_frac": a_b / hbm, **extra}
     return {"kernel": name, "bound": "hbm", "achieved": a_b, "peak": hbm, "unit": "GB/s", "frac": a_b / hbm,
-            "traffic": None, "peak_source": peak_kind, "duration_us": kern[name], "tensor_frac": a_t / tflops}
+            "traffic": traffic, "peak_source": peak_kind, "duration_us": kern[name], "tensor_frac": a_t / tflops,
+            **extra}
+
+
+TRAFFIC_FILE = "profiles/bwd_chunk_c1_dram.json"
+
+
+def measured_traffic(kernel, cfg):
+    """DRAM bytes per launch of the dominant kernel from the committed ncu capture summary, when it covers this
+    kernel and workload (the capture cannot run inside the timed bench); None otherwise."""
+    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), TRAFFIC_FILE)
+    try:
+        with open(path) as f:
+            rec = json.load(f)
+    except (OSError, ValueError):
+        return None
+    if rec.get("kernel") != kernel or not rec.get("workload", "").startswith(cfg["tag"].split(":")[0] + ":"):
+        return None
+    return rec["dram_bytes_read"] + rec["dram_bytes_write"]
 
 
 def end_to_end(lib, t, cfg, flags, ws, nbytes, stream, args):
