@@ -26,51 +26,85 @@ struct PrepSmem {
   static constexpr size_t a1 = v + 64 * DV * 2;           // [64 x 64] A diag(beta gamma)
   static constexpr size_t a2h = a1 + 64 * 64 * 2;         // [64 x 64] A diag(beta), hi
   static constexpr size_t a2l = a2h + 64 * 64 * 2;        //                           lo
-  static constexpr size_t L = a2l + 64 * 64 * 2;          // [64][65] fp32, L (strictly lower)
-  static constexpr size_t Ai = L + 64 * 65 * 4;           // [64][68] fp32, A (16-byte aligned rows)
+  static constexpr size_t L = a2l + 64 * 64 * 2;          // [64][68] fp32, L (strictly lower; 16-byte aligned rows)
+  static constexpr size_t Ai = L + 64 * 68 * 4;           // [64][68] fp32, A
   static constexpr size_t ql = L;                         // [64 x DK] low half of q, then k: live only until the
   static constexpr size_t kl = ql + 64 * DK * 2;          //   Q K^T / K K^T product is done (L and A reuse them)
-  static_assert(2 * 64 * DK * 2 <= 64 * 65 * 4 + 64 * 68 * 4, "the q / k low halves must fit in the L and A buffers");
+  static_assert(2 * 64 * DK * 2 <= 2 * 64 * 68 * 4, "the q / k low halves must fit in the L and A buffers");
   static constexpr size_t G = Ai + 64 * 68 * 4;           // [64] cumulative log decay
   static constexpr size_t beta = G + 64 * 4;              // [64]
-  static constexpr size_t scan = beta + 64 * 4;           // [2] warp totals of the scan
+  static constexpr size_t gam = beta + 64 * 4;            // [64] gamma = exp(G)
+  static constexpr size_t bgam = gam + 64 * 4;            // [64] beta gamma
+  static constexpr size_t scan = bgam + 64 * 4;           // [2] warp totals of the scan
   static constexpr size_t bar = (scan + 16 + 7) & ~size_t(7);  // [5] MMA commits; row blocks of A published
   static constexpr size_t tmem = bar + 5 * 8;
   static constexpr size_t total = tmem + 16;
 };
 
-// A = (I + L)^-1 for the 64 x 64 strictly lower L (fp32, row stride 65), by forward substitution
-// A[i, :] = e_i - sum_{m < i} L[i, m] A[m, :], rows held in registers: warps w and w + 4 own rows 16 w .. 16 w + 15,
-// one column per lane (warp w: columns 0-31, warp w + 4: 32-63). A warp folds in each row block above it as soon as
+// A = (I + L)^-1 for the 64 x 64 strictly lower L (fp32, row stride 68), by forward substitution
+// A[i, :] = e_i - sum_{m < i} L[i, m] A[m, :], rows held in registers: warps 2 b and 2 b + 1 own rows 16 b .. 16 b + 15,
+// one column per lane (warp 2 b: columns 0-31, warp 2 b + 1: 32-63). A warp folds in each row block above it as soon as
 // that block's two owners publish it (a 16 x 16 by 16 x 32 update), then solves its own block, publishes it to A (fp32,
 // row stride 68) and arrives on its block's barrier (two arrivals). 256 threads. (The reference's gdc_prep,
 // src/macai/gated_delta/_chunked.py:282-311, also inverts by substitution in blocks; this is a register-resident
 // formulation of the same recurrence.)
-__device__ __forceinline__ bool unit_lower_inverse(const float* L, float* A, uint64_t* blk, ErrorWord* err) {
+__device__ __forceinline__ bool unit_lower_inverse(const float* L, float* A, uint64_t* blk, ErrorWord* err,
+                                                   long long* trace = nullptr) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int blkw = warp & 3, r0 = 16 * blkw, col = 32 * (warp >> 2) + lane;
+#ifdef GD_TRACE
+  int tslot = 0;
+  auto tr = [&]() {
+    if (trace != nullptr && lane == 0 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0)
+      trace[3 * 4096 + 1024 + warp * 16 + tslot] = clock64();
+    ++tslot;
+  };
+#else
+  auto tr = [&]() {};
+#endif
+  tr();
+  // a block's two warps sit on different SM sub-partitions (warp % 4), so its work does not share one issue port
+  const int blkw = warp >> 1, r0 = 16 * blkw, col = 32 * (warp & 1) + lane;
   bool ok = true;
   float a[16];
 #pragma unroll
   for (int r = 0; r < 16; ++r) a[r] = (r0 + r == col) ? 1.f : 0.f;
   for (int bb = 0; bb < blkw; ++bb) {
     ok = ok && mbar_wait(blk + bb, 0, err, 12);
-#pragma unroll 4
-    for (int m = 0; m < 16; ++m) {
-      const float am = A[(16 * bb + m) * 68 + col];
+    tr();
+#pragma unroll 1
+    for (int m4 = 0; m4 < 4; ++m4) {  // four rows of the published block at a time; L read as float4 (broadcast)
+      float am[4];
 #pragma unroll
-      for (int r = 0; r < 16; ++r) a[r] = fmaf(-L[(r0 + r) * 65 + 16 * bb + m], am, a[r]);
+      for (int u = 0; u < 4; ++u) am[u] = A[(16 * bb + 4 * m4 + u) * 68 + col];
+#pragma unroll
+      for (int r = 0; r < 16; ++r) {
+        const float4 l4 = *reinterpret_cast<const float4*>(L + (r0 + r) * 68 + 16 * bb + 4 * m4);
+        a[r] = fmaf(-l4.x, am[0], a[r]);
+        a[r] = fmaf(-l4.y, am[1], a[r]);
+        a[r] = fmaf(-l4.z, am[2], a[r]);
+        a[r] = fmaf(-l4.w, am[3], a[r]);
+      }
     }
   }
+  tr();
 #pragma unroll
   for (int r = 1; r < 16; ++r) {
 #pragma unroll
-    for (int m = 0; m < r; ++m) a[r] = fmaf(-L[(r0 + r) * 65 + r0 + m], a[m], a[r]);
+    for (int m4 = 0; m4 < 4; ++m4) {
+      if (4 * m4 < r) {
+        const float4 l4 = *reinterpret_cast<const float4*>(L + (r0 + r) * 68 + r0 + 4 * m4);
+        const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (4 * m4 + u < r) a[r] = fmaf(-lv[u], a[4 * m4 + u], a[r]);
+      }
+    }
   }
 #pragma unroll
   for (int r = 0; r < 16; ++r) A[(r0 + r) * 68 + col] = a[r];
   __syncwarp();
   if (lane == 0) mbar_arrive(blk + blkw);
+  tr();
   return ok;
 }
 
@@ -144,11 +178,19 @@ __global__ void __launch_bounds__(256, 2) prep_kernel(const T* __restrict__ q, c
   fence_async_smem();
   tc_fence_before();
   __syncthreads();
-  if (tid >= 32 && tid < 64) sG[tid] += reinterpret_cast<float*>(smem + S::scan)[0];
+  float* sGam = reinterpret_cast<float*>(smem + S::gam);
+  float* sBG = reinterpret_cast<float*>(smem + S::bgam);
+  if (tid < 64) {  // each thread finishes its own token: G, gamma, beta gamma
+    if (tid >= 32) sG[tid] += reinterpret_cast<float*>(smem + S::scan)[0];
+    sGam[tid] = __expf(sG[tid]);
+    sBG[tid] = sB[tid] * sGam[tid];
+  }
   tc_fence_after();
   const uint32_t tm = *tslot;
+  __syncthreads();  // G, gamma complete for everyone
 
-  // [Q; K] K^T with q and k carried as bf16 hi + lo (three products): lanes 0-63 hold Q K^T rows, 64-127 K K^T rows
+  // [Q; K] K^T with q and k carried as bf16 hi + lo (three products): lanes 0-63 hold Q K^T rows, 64-127 K K^T rows.
+  // Issued after the barrier: the issue blocks thread 0 while the other warps write the images below.
   if (tid == 0) {
     const Tile qkh{smem_u32(smem + S::q), DK}, qkl{smem_u32(smem + S::ql), DK};
     const Tile kh{smem_u32(smem + S::k), DK}, kl{smem_u32(smem + S::kl), DK};
@@ -157,7 +199,6 @@ __global__ void __launch_bounds__(256, 2) prep_kernel(const T* __restrict__ q, c
     mma_tiles(tm, 128, 64, DK, qkl, true, 0, 0, kh, false, 0, true);
     mma_commit(bar);
   }
-  __syncthreads();  // sG complete for everyone
   GD_TRACE_AT(ws, lay, 2);
   {  // the low halves go out (transposed images) before L and A overwrite them
     unsigned char* dst = ws + lay.qkl + cidx * lay.qk_bytes();
@@ -174,7 +215,7 @@ __global__ void __launch_bounds__(256, 2) prep_kernel(const T* __restrict__ q, c
       const uint4 ul = *reinterpret_cast<const uint4*>(smem + S::ql + blk_off(r, 8 * cb, DK));
       const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&uh);
       const __nv_bfloat162* l2 = reinterpret_cast<const __nv_bfloat162*>(&ul);
-      const float gr = __expf(sG[r]);
+      const float gr = sGam[r];
       float x[8];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
@@ -235,14 +276,22 @@ __global__ void __launch_bounds__(256, 2) prep_kernel(const T* __restrict__ q, c
 #pragma unroll
         for (int jj = 0; jj < 32; ++jj) {
           const int j = 32 * half + jj;
-          sL[i * 65 + j] = (j < i) ? bi * acc[jj] * __expf(Gi - sG[j]) : 0.f;
+          acc[jj] = (j < i) ? bi * acc[jj] * __expf(Gi - sG[j]) : 0.f;
         }
+        float4* lrow = reinterpret_cast<float4*>(sL + i * 68 + 32 * half);
+#pragma unroll
+        for (int q4 = 0; q4 < 8; ++q4)
+          lrow[q4] = make_float4(acc[4 * q4], acc[4 * q4 + 1], acc[4 * q4 + 2], acc[4 * q4 + 3]);
       }
     }
   }
   __syncthreads();
   GD_TRACE_AT(ws, lay, 5);
+#ifdef GD_TRACE
+  if (ok) ok = unit_lower_inverse(sL, sAi, bar + 1, err, reinterpret_cast<long long*>(ws + lay.trace));
+#else
   if (ok) ok = unit_lower_inverse(sL, sAi, bar + 1, err);
+#endif
   ok = __syncthreads_and(ok);  // A complete for everyone
   GD_TRACE_AT(ws, lay, 6);
 
@@ -257,7 +306,7 @@ __global__ void __launch_bounds__(256, 2) prep_kernel(const T* __restrict__ q, c
       for (int e = 0; e < 8; ++e) {
         const int j = j0 + 8 * q8 + e;
         a0[e] = sAi[i * 68 + j];
-        a1[e] = a0[e] * sB[j] * __expf(sG[j]);
+        a1[e] = a0[e] * sBG[j];
         a2[e] = a0[e] * sB[j];
       }
       store8_bf16(smem + S::a1, i, j0 + 8 * q8, 64, a1);
