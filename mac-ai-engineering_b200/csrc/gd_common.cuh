@@ -41,9 +41,35 @@ struct ErrorWord {
     if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && (threadIdx.x & 127) == 0 && (slot) < 4096) \
       reinterpret_cast<long long*>((ws) + (lay).trace)[(threadIdx.x >> 7) * 4096 + (slot)] = clock64();   \
   } while (0)
+// the same from a single calling thread (an issuer lane), into group 0's row
+#define GD_TRACE_ONE(ws, lay, slot)                                                              \
+  do {                                                                                           \
+    if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && (slot) < 4096)                  \
+      reinterpret_cast<long long*>((ws) + (lay).trace)[(slot)] = clock64();                      \
+  } while (0)
+// per CTA (up to 4096 of them): SM id, then globaltimer (ns) at entry (which 0) and exit (which 1), in rows 1-3
+#define GD_TRACE_CTA(ws, lay, which)                                                                    \
+  do {                                                                                                  \
+    const unsigned int cta_ = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);           \
+    if (threadIdx.x == 0 && cta_ < 4096) {                                                              \
+      unsigned long long t_;                                                                            \
+      unsigned int sm_;                                                                                 \
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                                            \
+      asm volatile("mov.u32 %0, %%smid;" : "=r"(sm_));                                                  \
+      long long* tr_ = reinterpret_cast<long long*>((ws) + (lay).trace);                                \
+      tr_[4096 + cta_] = sm_;                                                                           \
+      tr_[4096 * (2 + (which)) + cta_] = (long long)t_;                                                 \
+    }                                                                                                   \
+  } while (0)
 #else
+#define GD_TRACE_CTA(ws, lay, which) \
+  do {                               \
+  } while (0)
 #define GD_TRACE_AT(ws, lay, slot) \
   do {                             \
+  } while (0)
+#define GD_TRACE_ONE(ws, lay, slot) \
+  do {                              \
   } while (0)
 #endif
 

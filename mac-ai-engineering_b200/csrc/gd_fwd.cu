@@ -36,76 +36,91 @@ struct PrepSmem {
   static constexpr size_t gam = beta + 64 * 4;            // [64] gamma = exp(G)
   static constexpr size_t bgam = gam + 64 * 4;            // [64] beta gamma
   static constexpr size_t scan = bgam + 64 * 4;           // [2] warp totals of the scan
-  static constexpr size_t bar = (scan + 16 + 7) & ~size_t(7);  // [5] MMA commits; row blocks of A published
-  static constexpr size_t tmem = bar + 5 * 8;
+  static constexpr size_t bar = (scan + 16 + 7) & ~size_t(7);  // MMA commits
+  static constexpr size_t tmem = bar + 8;
   static constexpr size_t total = tmem + 16;
 };
 
-// A = (I + L)^-1 for the 64 x 64 strictly lower L (fp32, row stride 68), by forward substitution
-// A[i, :] = e_i - sum_{m < i} L[i, m] A[m, :], rows held in registers: warps 2 b and 2 b + 1 own rows 16 b .. 16 b + 15,
-// one column per lane (warp 2 b: columns 0-31, warp 2 b + 1: 32-63). A warp folds in each row block above it as soon as
-// that block's two owners publish it (a 16 x 16 by 16 x 32 update), then solves its own block, publishes it to A (fp32,
-// row stride 68) and arrives on its block's barrier (two arrivals). 256 threads. (The reference's gdc_prep,
-// src/macai/gated_delta/_chunked.py:282-311, also inverts by substitution in blocks; this is a register-resident
-// formulation of the same recurrence.)
-__device__ __forceinline__ bool unit_lower_inverse(const float* L, float* A, uint64_t* blk, ErrorWord* err,
-                                                   long long* trace = nullptr) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-#ifdef GD_TRACE
-  int tslot = 0;
-  auto tr = [&]() {
-    if (trace != nullptr && lane == 0 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0)
-      trace[3 * 4096 + 1024 + warp * 16 + tslot] = clock64();
-    ++tslot;
-  };
-#else
-  auto tr = [&]() {};
-#endif
-  tr();
-  // a block's two warps sit on different SM sub-partitions (warp % 4), so its work does not share one issue port
-  const int blkw = warp >> 1, r0 = 16 * blkw, col = 32 * (warp & 1) + lane;
-  bool ok = true;
-  float a[16];
+// A = (I + L)^-1 for the 64 x 64 strictly lower L (fp32, row stride 68) by divide and conquer, all 256 threads:
+//   1. the four diagonal 16 x 16 blocks T_b = (I + L_bb)^-1 at once, one column per thread (64 threads: forward
+//      substitution x_i = [i == j] - sum_{m < i} L_im x_m, unrolled; the other warps zero A's upper blocks meanwhile);
+//   2. the 32 x 32 halves: A_21 = -T_2 (L_21 T_1) for block pairs (0, 1) and (2, 3);
+//   3. the whole: A_21 = -A_22 (L_21 A_11) with 32 x 32 blocks.
+// Each product is a 4-column strip per thread over float4 rows; Y (32 x 36 floats, 16-byte rows) is scratch. The
+// reference's gdc_prep (src/macai/gated_delta/_chunked.py:282-311) inverts by blocked substitution; the blocks are the
+// same unit-lower inverse, combined here by the block formula instead of row by row.
+// out[i][j0 .. j0 + 3] = sign * sum_{m < N} X[i][m] Z[m][j0 .. j0 + 3] (row strides xs, zs, os floats; 16-byte rows),
+// unrolled so that the shared-memory loads run ahead of the four accumulation chains
+template <int N>
+__device__ __forceinline__ void strip(const float* X, int xs, const float* Z, int zs, float* out, int os, float sign,
+                                      int i, int j0) {
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-  for (int r = 0; r < 16; ++r) a[r] = (r0 + r == col) ? 1.f : 0.f;
-  for (int bb = 0; bb < blkw; ++bb) {
-    ok = ok && mbar_wait(blk + bb, 0, err, 12);
-    tr();
-#pragma unroll 1
-    for (int m4 = 0; m4 < 4; ++m4) {  // four rows of the published block at a time; L read as float4 (broadcast)
-      float am[4];
+  for (int m4 = 0; m4 < N; m4 += 4) {
+    const float4 x4 = *reinterpret_cast<const float4*>(X + i * xs + m4);
+    const float xv[4] = {x4.x, x4.y, x4.z, x4.w};
 #pragma unroll
-      for (int u = 0; u < 4; ++u) am[u] = A[(16 * bb + 4 * m4 + u) * 68 + col];
-#pragma unroll
-      for (int r = 0; r < 16; ++r) {
-        const float4 l4 = *reinterpret_cast<const float4*>(L + (r0 + r) * 68 + 16 * bb + 4 * m4);
-        a[r] = fmaf(-l4.x, am[0], a[r]);
-        a[r] = fmaf(-l4.y, am[1], a[r]);
-        a[r] = fmaf(-l4.z, am[2], a[r]);
-        a[r] = fmaf(-l4.w, am[3], a[r]);
-      }
+    for (int u = 0; u < 4; ++u) {
+      const float4 z = *reinterpret_cast<const float4*>(Z + (m4 + u) * zs + j0);
+      acc.x = fmaf(xv[u], z.x, acc.x);
+      acc.y = fmaf(xv[u], z.y, acc.y);
+      acc.z = fmaf(xv[u], z.z, acc.z);
+      acc.w = fmaf(xv[u], z.w, acc.w);
     }
   }
-  tr();
+  *reinterpret_cast<float4*>(out + i * os + j0) = make_float4(sign * acc.x, sign * acc.y, sign * acc.z, sign * acc.w);
+}
+
+__device__ __forceinline__ void unit_lower_inverse(const float* L, float* A, float* Y, unsigned char* ws,
+                                                   const Layout& lay) {
+  const int tid = threadIdx.x;
+  if (tid < 64) {
+    const int b = tid >> 4, j = tid & 15, r0 = 16 * b;
+    float x[16];
 #pragma unroll
-  for (int r = 1; r < 16; ++r) {
+    for (int i = 0; i < 16; ++i) {
+      float acc = (i == j) ? 1.f : 0.f;
 #pragma unroll
-    for (int m4 = 0; m4 < 4; ++m4) {
-      if (4 * m4 < r) {
-        const float4 l4 = *reinterpret_cast<const float4*>(L + (r0 + r) * 68 + r0 + 4 * m4);
+      for (int m4 = 0; m4 < i; m4 += 4) {
+        const float4 l4 = *reinterpret_cast<const float4*>(L + (r0 + i) * 68 + r0 + m4);
         const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
 #pragma unroll
         for (int u = 0; u < 4; ++u)
-          if (4 * m4 + u < r) a[r] = fmaf(-lv[u], a[4 * m4 + u], a[r]);
+          if (m4 + u < i) acc = fmaf(-lv[u], x[m4 + u], acc);
       }
+      x[i] = acc;
+    }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) A[(r0 + i) * 68 + r0 + j] = x[i];
+  } else {
+    // upper blocks (block row bi < block column bj) are zero: 6 blocks x 16 rows x 4 float4
+    for (int idx = tid - 64; idx < 6 * 64; idx += 192) {
+      const int blk = idx >> 6, r = (idx >> 2) & 15, c4 = idx & 3;
+      const int bi = blk < 3 ? 0 : (blk < 5 ? 1 : 2);
+      const int bj = blk < 3 ? blk + 1 : (blk < 5 ? blk - 1 : 3);
+      *reinterpret_cast<float4*>(A + (16 * bi + r) * 68 + 16 * bj + 4 * c4) = make_float4(0.f, 0.f, 0.f, 0.f);
     }
   }
-#pragma unroll
-  for (int r = 0; r < 16; ++r) A[(r0 + r) * 68 + col] = a[r];
-  __syncwarp();
-  if (lane == 0) mbar_arrive(blk + blkw);
-  tr();
-  return ok;
+  GD_TRACE_AT(ws, lay, 16);
+  __syncthreads();
+  GD_TRACE_AT(ws, lay, 17);
+  // 2. pairs p = 0, 1: blocks lo = 2p, hi = 2p + 1 (rows / columns 16 lo .., 16 hi ..)
+  const int p = tid >> 6, i16 = (tid >> 2) & 15, j4 = 4 * (tid & 3);
+  if (tid < 128)  // Y_p = L[hi][lo] T_lo
+    strip<16>(L + (32 * p + 16) * 68 + 32 * p, 68, A + (32 * p) * 68 + 32 * p, 68, Y + 16 * p * 36, 36, 1.f, i16, j4);
+  __syncthreads();
+  if (tid < 128)  // A[hi][lo] = -T_hi Y_p
+    strip<16>(A + (32 * p + 16) * 68 + 32 * p + 16, 68, Y + 16 * p * 36, 36, A + (32 * p + 16) * 68 + 32 * p, 68, -1.f,
+              i16, j4);
+  __syncthreads();
+  GD_TRACE_AT(ws, lay, 18);
+  // 3. Y = L[32:64][0:32] A_11 ; A[32:64][0:32] = -A_22 Y
+  const int i32 = tid >> 3, j8 = 4 * (tid & 7);
+  strip<32>(L + 32 * 68, 68, A, 68, Y, 36, 1.f, i32, j8);
+  __syncthreads();
+  GD_TRACE_AT(ws, lay, 19);
+  strip<32>(A + 32 * 68 + 32, 68, Y, 36, A + 32 * 68, 68, -1.f, i32, j8);
+  GD_TRACE_AT(ws, lay, 20);
 }
 
 template <typename T, int DK, int DV>
@@ -129,13 +144,13 @@ __global__ void __launch_bounds__(256, 2) prep_kernel(const T* __restrict__ q, c
   uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + S::tmem);
 
   GD_TRACE_AT(ws, lay, 0);
+  GD_TRACE_CTA(ws, lay, 0);
   if (warp == 0) {
     tmem_alloc(tslot, 256);
     tmem_relinquish();
   }
   if (tid == 0) {
     mbar_init(bar, 1);  // MMA commits
-    for (int i = 1; i < 5; ++i) mbar_init(bar + i, 2);  // row block i - 1 of A published (its two warps)
     fence_mbar_init();
   }
 
@@ -200,7 +215,7 @@ __global__ void __launch_bounds__(256, 2) prep_kernel(const T* __restrict__ q, c
     mma_commit(bar);
   }
   GD_TRACE_AT(ws, lay, 2);
-  {  // the low halves go out (transposed images) before L and A overwrite them
+  if (lay.backward()) {  // the low halves go out (transposed images) before L and A overwrite them
     unsigned char* dst = ws + lay.qkl + cidx * lay.qk_bytes();
     store_tile_transposed<64, DK, 8>(smem + S::ql, dst);
     store_tile_transposed<64, DK, 8>(smem + S::kl, dst + 64 * DK * 2);
@@ -287,12 +302,9 @@ __global__ void __launch_bounds__(256, 2) prep_kernel(const T* __restrict__ q, c
   }
   __syncthreads();
   GD_TRACE_AT(ws, lay, 5);
-#ifdef GD_TRACE
-  if (ok) ok = unit_lower_inverse(sL, sAi, bar + 1, err, reinterpret_cast<long long*>(ws + lay.trace));
-#else
-  if (ok) ok = unit_lower_inverse(sL, sAi, bar + 1, err);
-#endif
-  ok = __syncthreads_and(ok);  // A complete for everyone
+  // (ok is the same in every thread: the barriers inside are reached by all or none)
+  if (ok) unit_lower_inverse(sL, sAi, reinterpret_cast<float*>(smem + S::a1), ws, lay);
+  __syncthreads();  // A complete for everyone
   GD_TRACE_AT(ws, lay, 6);
 
   if (ok) {
@@ -333,11 +345,11 @@ __global__ void __launch_bounds__(256, 2) prep_kernel(const T* __restrict__ q, c
               false, 0, true);
     mma_commit(bar);
   }
-  // the q / k images and G go out while the MMAs run
+  // the q / k images and G go out while the MMAs run (the k image only for the backward)
   if (ok) {
     unsigned char* dst = ws + lay.qk + cidx * lay.qk_bytes();  // transposed images ([DK x 64], rows d)
     store_tile_transposed<64, DK, 8>(smem + S::q, dst);
-    store_tile_transposed<64, DK, 8>(smem + S::k, dst + 64 * DK * 2);
+    if (lay.backward()) store_tile_transposed<64, DK, 8>(smem + S::k, dst + 64 * DK * 2);
     if (tid < 64) reinterpret_cast<float*>(ws + lay.gc + cidx * lay.gc_bytes())[tid] = sG[tid];
   }
   if (ok) ok = mbar_wait(bar, 1, err, 11);
@@ -372,6 +384,7 @@ __global__ void __launch_bounds__(256, 2) prep_kernel(const T* __restrict__ q, c
     tc_fence_after();
     tmem_dealloc(tm, 256);
   }
+  GD_TRACE_CTA(ws, lay, 1);
 }
 
 // ------------------------------------------------------------------------------------------------------------------
@@ -379,18 +392,23 @@ __global__ void __launch_bounds__(256, 2) prep_kernel(const T* __restrict__ q, c
 //
 // Two CTAs per (value head, batch row), each owning 64 of the 128 value columns (the recurrence never mixes value
 // columns: Vn = U - W S, S <- e S + K~^T Vn and O = gamma Q S + M Vn act on each column of S alone), so the pass runs
-// on twice the SMs with half the work per chunk step. 16 epilogue warps + 1 MMA warp. Every product is M = 64 (the
+// on twice the SMs with half the work per chunk step. 16 epilogue warps, 1 MMA warp, 1 loader warp. Every product is
+// M = 64 (the
 // CTA's value columns on TMEM lanes 0-15 of each quadrant) and is read whole-warp (16x32bx2): warp w (quadrant w % 4,
 // quarter w / 4) thread t holds value column 16 (w % 4) + t % 16 and tokens 16 (w / 4) + 8 (t / 16) .. + 7 of the
 // [64 x 64] products, key rows 32 (w / 4) + 16 (t / 16) .. + 15 of the [64 x DK] state update; it keeps the fp32
-// state S[those key rows][its column] in registers. One thread of warp 16 issues every MMA and bulk copy; hand-offs
-// are mbarriers only. Per chunk c:
+// state S[those key rows][its column] in registers. One thread of warp 16 issues every MMA (and, with
+// GD_STORE_STATES, the bulk copies out); one thread of warp 17 loads the two input stages, so that a refill (whose
+// bulk copies queue behind running products) never delays the MMA thread's next hand-off. Hand-offs are mbarriers
+// only. Per chunk c:
+//   LOAD: wait stage_free of chunk c - 2 -> stage c & 1 <- W^T, q^T, K~ hi / lo, M images of chunk c
 //   MMA: wait stage c and the S tile -> (W S)^T -> ws_full; (Q S)^T -> qs_full[c & 1]
-//   EPI: wait ws_full -> Vn = U - W S (U prefetched into registers) -> Vn^T hi / lo tiles -> vn_full
-//   MMA: refill the stage of chunk c - 1 with chunk c + 1 once chunk c - 1's readers are done; wait vn_full ->
-//        (K~^T Vn)^T, three products (K~ = diag(e) K and Vn split) -> ds_full; (M Vn)^T -> mv_full; stage_free[c & 1]
+//   EPI: wait ws_full -> Vn = U - W S (U and G prefetched into registers) -> Vn^T hi / lo tiles -> vn_full
+//   MMA: wait vn_full -> (K~^T Vn)^T, three products (K~ = diag(e) K and Vn split) -> ds_full; (M Vn)^T ->
+//        mv_full[c & 1]; stage_free[c & 1]
+//   EPI: (after handing Vn of chunk c to the tensor core) O of chunk c - 1 = diag(gamma) Q S + M Vn -> global (16-byte
+//        rows after an 8 x 8 transpose): it runs under chunk c's state-update product, off the chain
 //   EPI: wait ds_full -> S <- exp(G_last) S + K~^T Vn -> S tile -> st_full
-//   EPI: wait qs_full, mv_full -> O = diag(gamma) Q S + M Vn -> global (16-byte rows after an 8 x 8 transpose)
 // With GD_STORE_STATES (the backward's recompute) O is not formed; the pass keeps S_c (fp32 and a bf16 S_c^T image) and
 // the Vn^T hi / lo images of every chunk for the backward kernels (each CTA its 64 rows of them).
 
@@ -407,8 +425,7 @@ struct StateSmem {
   static constexpr size_t s_q = s_wt + DK * 64 * 2;        //   [DK x 64] q image (hi, transposed)
   static constexpr size_t s_kt = s_q + 64 * DK * 2;        //   [2][64 x DK] K~ hi, lo
   static constexpr size_t s_m = s_kt + 2 * 64 * DK * 2;    //   [64 x 64] M image
-  static constexpr size_t s_g = s_m + 64 * 64 * 2;         //   [64] G
-  static constexpr size_t stage_bytes = s_g + 64 * 4;
+  static constexpr size_t stage_bytes = s_m + 64 * 64 * 2;
   static constexpr size_t bar = stage0 + 2 * stage_bytes;
   static constexpr int NBAR = 13;
   static constexpr size_t tmem = bar + NBAR * 8;
@@ -424,11 +441,10 @@ __device__ __forceinline__ void issue_stage(unsigned char* stg, const unsigned c
   bulk_g2s(stg + S::s_q, ws + lay.qk + cidx * lay.qk_bytes(), 64 * DK * 2, bar);
   bulk_g2s(stg + S::s_kt, ws + lay.kt + cidx * lay.qk_bytes(), (uint32_t)lay.qk_bytes(), bar);
   bulk_g2s(stg + S::s_m, ws + lay.m + cidx * lay.m_bytes(), (uint32_t)lay.m_bytes(), bar);
-  bulk_g2s(stg + S::s_g, ws + lay.gc + cidx * lay.gc_bytes(), (uint32_t)lay.gc_bytes(), bar);
 }
 
 template <typename T, int DK, int DV>
-__global__ void __launch_bounds__(544) state_kernel(const float* __restrict__ s0, T* __restrict__ o,
+__global__ void __launch_bounds__(576) state_kernel(const float* __restrict__ s0, T* __restrict__ o,
                                                        float* __restrict__ sT, Layout lay, int flags,
                                                        unsigned char* __restrict__ ws) {
   static_assert(DV == 128 && DK == 128, "64 value columns per CTA on TMEM lanes 0-15 of each quadrant");
@@ -436,6 +452,7 @@ __global__ void __launch_bounds__(544) state_kernel(const float* __restrict__ s0
   constexpr int DVH = S::DVH;
   extern __shared__ __align__(1024) unsigned char smem[];
   ErrorWord* err = reinterpret_cast<ErrorWord*>(ws + lay.err);
+  GD_TRACE_AT(ws, lay, 4000);
   const int half = blockIdx.x % kVsplit, h = blockIdx.x / kVsplit, b = blockIdx.y;
   const int vbase = DVH * half;  // this CTA's first value column
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -445,10 +462,9 @@ __global__ void __launch_bounds__(544) state_kernel(const float* __restrict__ s0
   uint64_t* ws_full = bars + 4;
   uint64_t* qs_full = bars + 5;     // [2]
   uint64_t* ds_full = bars + 7;
-  uint64_t* mv_full = bars + 8;
-  uint64_t* vn_full = bars + 9;     // 16 epilogue warps
-  uint64_t* st_full = bars + 10;    // 16 epilogue warps
-  uint64_t* stage_epi = bars + 11;  // [2] 16 epilogue warps: done reading the stage
+  uint64_t* mv_full = bars + 8;     // [2]
+  uint64_t* vn_full = bars + 10;    // 16 epilogue warps
+  uint64_t* st_full = bars + 11;    // 16 epilogue warps
   uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + S::tmem);
   const bool store = (flags & GD_STORE_STATES) != 0 && lay.backward();
   const bool out = o != nullptr && !store;
@@ -460,18 +476,18 @@ __global__ void __launch_bounds__(544) state_kernel(const float* __restrict__ s0
     tmem_relinquish();
   }
   if (tid == 0) {
-    for (int i = 0; i < 9; ++i) mbar_init(bars + i, 1);
+    for (int i = 0; i < 10; ++i) mbar_init(bars + i, 1);
     mbar_init(vn_full, 16);
     mbar_init(st_full, 16);
-    mbar_init(stage_epi, 16);
-    mbar_init(stage_epi + 1, 16);
     fence_mbar_init();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tm = *tslot;
-  const uint32_t tWS = tm, tMV = tm + 192, tDS = tm + 256;  // (Q S)^T at tm + 64 + 64 (c & 1); (K~^T Vn)^T 128 wide
+  GD_TRACE_AT(ws, lay, 4001);
+  // TMEM: (W S)^T at tm, (Q S)^T at tm + 64 + 64 (c & 1), (M Vn)^T at tm + 192 + 64 (c & 1), (K~^T Vn)^T (128 wide)
+  const uint32_t tWS = tm, tDS = tm + 320;
   const Tile tSt{smem_u32(smem + S::st), DK};
   const Tile tVh{smem_u32(smem + S::vh), 64}, tVl{smem_u32(smem + S::vl), 64};
   bool ok = true;
@@ -479,14 +495,13 @@ __global__ void __launch_bounds__(544) state_kernel(const float* __restrict__ s0
   if (warp == 16) {
     // ---------------- MMA and bulk-copy issuer (one thread)
     if (lane == 0) {
-      issue_stage<DK, DV>(smem + S::stage0, ws, lay, row0, full);
-      if (NT > 1) issue_stage<DK, DV>(smem + S::stage0 + S::stage_bytes, ws, lay, row0 + 1, full + 1);
       for (int c = 0; c < NT && ok; ++c) {
         const int s = c & 1;
         const uint32_t par2 = (c >> 1) & 1;
         unsigned char* stg = smem + S::stage0 + s * S::stage_bytes;
         ok = mbar_wait(full + s, par2, err, 20) && mbar_wait(st_full, c & 1, err, 21);
         if (!ok) break;
+        GD_TRACE_ONE(ws, lay, 1024 + 8 * c + 0);
         tc_fence_after();
         if (store) {  // this CTA's rows of the S_c^T image (bulk copy out; done reading before the tile is rewritten)
           bulk_s2g(ws + lay.sci + (row0 + c) * lay.si_bytes() + (size_t)vbase * DK * 2, smem + S::st, DVH * DK * 2);
@@ -494,22 +509,17 @@ __global__ void __launch_bounds__(544) state_kernel(const float* __restrict__ s0
         }
         mma_tiles(tWS, DVH, 64, DK, tSt, true, 0, 0, Tile{smem_u32(stg + S::s_wt), 64}, true, 0, false);
         mma_commit(ws_full);
+        GD_TRACE_ONE(ws, lay, 1024 + 8 * c + 1);
         if (out) {
           mma_tiles(tm + 64 + 64 * s, DVH, 64, DK, tSt, true, 0, 0, Tile{smem_u32(stg + S::s_q), 64}, true, 0,
                     false);
           mma_commit(qs_full + s);
         }
-        // the stage of chunk c - 1 takes chunk c + 1 once its readers (chunk c - 1's MMAs and O) are done; chunk
-        // c's first products are already issued, so this wait (on O of chunk c - 1) delays nothing on the chain
-        if (c >= 1 && c + 1 < NT) {
-          const int sp = (c - 1) & 1;
-          const uint32_t pp = ((c - 1) >> 1) & 1;
-          ok = mbar_wait(stage_free + sp, pp, err, 23) && mbar_wait(stage_epi + sp, pp, err, 28);
-          if (!ok) break;
-          issue_stage<DK, DV>(smem + S::stage0 + sp * S::stage_bytes, ws, lay, row0 + c + 1, full + sp);
-        }
+        GD_TRACE_ONE(ws, lay, 1024 + 8 * c + 2);
+        GD_TRACE_ONE(ws, lay, 1024 + 8 * c + 3);
         ok = mbar_wait(vn_full, c & 1, err, 22);
         if (!ok) break;
+        GD_TRACE_ONE(ws, lay, 1024 + 8 * c + 4);
         tc_fence_after();
         if (store) {  // this CTA's rows of the Vn^T hi and lo images
           unsigned char* vn = ws + lay.vni + (row0 + c) * lay.vn_bytes() + (size_t)vbase * 64 * 2;
@@ -523,15 +533,30 @@ __global__ void __launch_bounds__(544) state_kernel(const float* __restrict__ s0
         mma_tiles(tDS, DVH, DK, 64, tVl, true, 0, 0, tKh, true, 0, true);
         if (store) bulk_wait_read0();  // the S^T and Vn^T tiles may be rewritten once ds_full fires
         mma_commit(ds_full);
+        GD_TRACE_ONE(ws, lay, 1024 + 8 * c + 5);
         if (out) {
           const Tile tM{smem_u32(stg + S::s_m), 64};
-          mma_tiles(tMV, DVH, 64, 64, tVh, true, 0, 0, tM, false, 0, false);
-          mma_tiles(tMV, DVH, 64, 64, tVl, true, 0, 0, tM, false, 0, true);
-          mma_commit(mv_full);
+          mma_tiles(tm + 192 + 64 * s, DVH, 64, 64, tVh, true, 0, 0, tM, false, 0, false);
+          mma_tiles(tm + 192 + 64 * s, DVH, 64, 64, tVl, true, 0, 0, tM, false, 0, true);
+          mma_commit(mv_full + s);
         }
         mma_commit(stage_free + s);
+        GD_TRACE_ONE(ws, lay, 1024 + 8 * c + 6);
       }
       if (store) bulk_wait0();
+    }
+    __syncwarp();
+  } else if (warp == 17) {
+    // ---------------- stage loader (one thread)
+    if (lane == 0) {
+      int c = 0;
+      for (; c < NT; ++c) {
+        const int s = c & 1;
+        if (c >= 2 && !mbar_wait(stage_free + s, ((c - 2) >> 1) & 1, err, 23)) break;
+        issue_stage<DK, DV>(smem + S::stage0 + s * S::stage_bytes, ws, lay, row0 + c, full + s);
+      }
+      // every copy issued here lands before the CTA may exit, also after a failed wait
+      for (int l = c >= 2 ? c - 2 : 0; l < c; ++l) mbar_wait(full + (l & 1), (l >> 1) & 1, err, 29);
     }
     __syncwarp();
   } else {
@@ -560,35 +585,67 @@ __global__ void __launch_bounds__(544) state_kernel(const float* __restrict__ s0
         sc[(size_t)q4 * DV] = make_float4(Sr[4 * q4], Sr[4 * q4 + 1], Sr[4 * q4 + 2], Sr[4 * q4 + 3]);
     };
     if (store) store_scf(0);
-    float Ur[8];
+    // U of the next chunk, and G (cumulative log gates) at tokens tk .. tk + 7 and the chunk's last token: read from L2
+    // one pass ahead so that no stage holds G for the late O product
+    float Ur[8], gcur[8], gcur_last, gprev[8];
     auto load_u = [&](size_t cidx) {
       const float* u = reinterpret_cast<const float*>(ws + lay.u + cidx * lay.u_bytes());
 #pragma unroll
       for (int j = 0; j < 8; ++j) Ur[j] = __ldg(u + (tk + j) * DV + v);
+      const float* gp = reinterpret_cast<const float*>(ws + lay.gc + cidx * lay.gc_bytes());
+      const float4 g0 = __ldg(reinterpret_cast<const float4*>(gp + tk)), g1 = __ldg(reinterpret_cast<const float4*>(gp + tk + 4));
+      gcur[0] = g0.x; gcur[1] = g0.y; gcur[2] = g0.z; gcur[3] = g0.w;
+      gcur[4] = g1.x; gcur[5] = g1.y; gcur[6] = g1.z; gcur[7] = g1.w;
+      gcur_last = __ldg(gp + 63);
     };
     load_u(row0);
-    for (int c = 0; c < NT; ++c) {
+    // pass c computes Vn and the state update of chunk c (c < NT) and, between them, O of chunk c - 1 (c >= 1)
+    for (int c = 0; c <= NT; ++c) {
       const size_t cidx = row0 + c;
-      const int s = c & 1;
-      const float* sG = reinterpret_cast<const float*>(smem + S::stage0 + s * S::stage_bytes + S::s_g);
-      // * Vn = U - W S
-      GD_TRACE_AT(ws, lay, 8 * c + 0);
-      if (!mbar_wait(ws_full, c & 1, err, 24)) { ok = false; break; }
-      GD_TRACE_AT(ws, lay, 8 * c + 1);
-      tc_fence_after();
-      const float gl = __expf(sG[63]);
-      {
+      if (c < NT) {
+        // * Vn = U - W S
+        GD_TRACE_AT(ws, lay, 8 * c + 0);
+        if (!mbar_wait(ws_full, c & 1, err, 24)) { ok = false; break; }
+        GD_TRACE_AT(ws, lay, 8 * c + 1);
+        tc_fence_after();
         float acc[8];
         tmem_ld8h(tmem_lane_addr(tWS, warp, 16 * quarter), acc);
+        GD_TRACE_AT(ws, lay, 2048 + 8 * c + 0);
 #pragma unroll
         for (int j = 0; j < 8; ++j) acc[j] = Ur[j] - acc[j];
         store8_split(smem + S::vh, smem + S::vl, vl_, tk, 64, acc);
+        GD_TRACE_AT(ws, lay, 2048 + 8 * c + 1);
         tc_fence_before();
         fence_async_smem();
+        GD_TRACE_AT(ws, lay, 2048 + 8 * c + 2);
         mbar_arrive_warp(vn_full);
+        GD_TRACE_AT(ws, lay, 8 * c + 2);
       }
-      GD_TRACE_AT(ws, lay, 8 * c + 2);
-      if (c + 1 < NT) load_u(cidx + 1);  // next chunk's U into registers while the tensor core works
+      if (out && c >= 1) {
+        // * O of chunk c - 1 = diag(gamma) Q S + M Vn, under this chunk's state-update product
+        const int p = c - 1, s = p & 1;
+        if (!mbar_wait(qs_full + s, (p >> 1) & 1, err, 26) || !mbar_wait(mv_full + s, (p >> 1) & 1, err, 27)) {
+          ok = false;
+          break;
+        }
+        GD_TRACE_AT(ws, lay, 8 * c + 5);
+        tc_fence_after();
+        float qs[8], mv[8];
+        tmem_ld8hx2(tmem_lane_addr(tm + 64 + 64 * s, warp, 16 * quarter), qs,
+                    tmem_lane_addr(tm + 192 + 64 * s, warp, 16 * quarter), mv);
+        GD_TRACE_AT(ws, lay, 8 * c + 6);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) qs[j] = fmaf(__expf(gprev[j]), qs[j], mv[j]);
+        store_token_rows8<T>(qs, o + ((size_t)b * lay.T * lay.H + h) * DV, (size_t)lay.H * DV, p * C + tk, lay.T,
+                             vbase + 16 * qd + 8 * ((lane >> 3) & 1));
+        tc_fence_before();
+      }
+      if (c == NT) break;
+      GD_TRACE_AT(ws, lay, 8 * c + 7);
+      const float gl = __expf(gcur_last);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) gprev[j] = gcur[j];
+      if (c + 1 < NT) load_u(cidx + 1);  // next chunk's U and G into registers while the tensor core works
       // * S <- exp(G_last) S + K~^T Vn
       if (!mbar_wait(ds_full, c & 1, err, 25)) { ok = false; break; }
       GD_TRACE_AT(ws, lay, 8 * c + 3);
@@ -596,35 +653,21 @@ __global__ void __launch_bounds__(544) state_kernel(const float* __restrict__ s0
       {
         float d[16];
         tmem_ld16h(tmem_lane_addr(tDS, warp, 32 * quarter), d);
+        GD_TRACE_AT(ws, lay, 2048 + 8 * c + 3);
 #pragma unroll
         for (int j = 0; j < 16; ++j) Sr[j] = fmaf(gl, Sr[j], d[j]);
 #pragma unroll
         for (int q8 = 0; q8 < 2; ++q8) store8_bf16(smem + S::st, vl_, dk0 + 8 * q8, DK, Sr + 8 * q8);
+        GD_TRACE_AT(ws, lay, 2048 + 8 * c + 4);
         tc_fence_before();
         fence_async_smem();
+        GD_TRACE_AT(ws, lay, 2048 + 8 * c + 5);
         mbar_arrive_warp(st_full);
       }
       if (store && c + 1 < NT) store_scf(c + 1);  // off the chain: the next MMAs are already unblocked
       GD_TRACE_AT(ws, lay, 8 * c + 4);
-      // O of chunk c (overlaps chunk c + 1's products)
-      if (out) {
-        if (!mbar_wait(qs_full + s, (c >> 1) & 1, err, 26) || !mbar_wait(mv_full, c & 1, err, 27)) {
-          ok = false;
-          break;
-        }
-        GD_TRACE_AT(ws, lay, 8 * c + 7);
-        tc_fence_after();
-        float qs[8], mv[8];
-        tmem_ld8hx2(tmem_lane_addr(tm + 64 + 64 * s, warp, 16 * quarter), qs, tmem_lane_addr(tMV, warp, 16 * quarter), mv);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) qs[j] = fmaf(__expf(sG[tk + j]), qs[j], mv[j]);
-        store_token_rows8<T>(qs, o + ((size_t)b * lay.T * lay.H + h) * DV, (size_t)lay.H * DV, c * C + tk, lay.T,
-                             vbase + 16 * qd + 8 * ((lane >> 3) & 1));
-        tc_fence_before();
-      }
-      mbar_arrive_warp(stage_epi + s);  // this warp is done reading chunk c's stage
-      GD_TRACE_AT(ws, lay, 8 * c + 5);
     }
+    GD_TRACE_AT(ws, lay, 4002);
     if (ok && sT != nullptr) {
       float* sp = sT + ((size_t)b * lay.H + h) * DK * DV;
 #pragma unroll
@@ -637,6 +680,7 @@ __global__ void __launch_bounds__(544) state_kernel(const float* __restrict__ s0
     tc_fence_after();
     tmem_dealloc(tm, 512);
   }
+  GD_TRACE_AT(ws, lay, 4003);
 }
 // ------------------------------------------------------------------------------------------------------------------
 // launchers
@@ -664,7 +708,7 @@ cudaError_t launch_state(const float* s0, void* o, float* sT, const Layout& lay,
   cudaError_t e = set_smem_once(kern, S::total, attr_done);
   if (e != cudaSuccess) return e;
   dim3 grid(lay.H * kVsplit, lay.B);
-  kern<<<grid, 544, S::total, st>>>(s0, static_cast<T*>(o), sT, lay, flags, ws);
+  kern<<<grid, 576, S::total, st>>>(s0, static_cast<T*>(o), sT, lay, flags, ws);
   return cudaGetLastError();
 }
 

@@ -3,14 +3,15 @@
 // All intermediates of one call live in one caller-provided buffer. Per chunk (index cidx = (b * H + h) * NT + c, h a
 // value head), "image" = an MMA-ready bf16 tile in the blocked layout of gd_common.cuh, copied to and from shared
 // memory whole by the bulk-copy engine. The prep kernel writes:
-//   qk   [2][DK x 64] image   normalised q (scaled), then normalised k (bf16 high halves), transposed (rows d)
-//   qkl  [2][DK x 64] image   their low halves (q = hi + lo to ~16 significant bits)
+//   qk   [2][DK x 64] image   normalised q (scaled), then normalised k (bf16 high halves), transposed (rows d); the
+//                             k half only for the backward
 //   kt   [2][64 x DK] image   K~ = diag(e) K, e_i = exp(G_last - G_i): hi, then lo (the state updates' operand)
 //   wt   [DK x 64]    image   W^T, W = A diag(beta gamma) K
 //   m    [64 x 64]    image   M = (Q K^T) * exp(G_i - G_j), lower with the diagonal
 //   u    [64][DV]     fp32    U = A diag(beta) V
 //   gc   [64]         fp32    G, the in-chunk inclusive cumulative sum of g
 // and for the backward also
+//   qkl  [2][DK x 64] image   the low halves of qk (q = hi + lo to ~16 significant bits)
 //   gq   [2][64 x DK] image   diag(gamma) Q: hi, then lo
 //   ai   [64 x 64]    image   A = (I + L)^-1
 //   vi   [DV x 64]    image   V^T
@@ -67,13 +68,13 @@ struct Layout {
     L.trace = 0;
 #endif
     L.qk = take(L.nch * L.qk_bytes());
-    L.qkl = take(L.nch * L.qk_bytes());
     L.kt = take(L.nch * L.qk_bytes());
     L.wt = take(L.nch * L.wt_bytes());
     L.m = take(L.nch * L.m_bytes());
     L.u = take(L.nch * L.u_bytes());
     L.gc = take(L.nch * L.gc_bytes());
     if (backward) {
+      L.qkl = take(L.nch * L.qk_bytes());
       L.gq = take(L.nch * L.qk_bytes());
       L.ai = take(L.nch * L.m_bytes());
       L.vi = take(L.nch * L.vi_bytes());
@@ -87,7 +88,7 @@ struct Layout {
       L.doi = take(L.nch * L.vi_bytes());
       L.sl = take(L.nch * L.sl_bytes());
     } else {
-      L.gq = L.ai = L.vi = L.rq = L.rk = L.scf = L.sci = L.vni = L.dsi = L.dvni = L.doi = L.sl = 0;
+      L.qkl = L.gq = L.ai = L.vi = L.rq = L.rk = L.scf = L.sci = L.vni = L.dsi = L.dvni = L.doi = L.sl = 0;
     }
     L.total = o;
     return L;

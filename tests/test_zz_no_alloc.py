@@ -68,7 +68,7 @@ def test_noalloc_matches_gd_forward_on_two_calls_in_a_row():
 
 def test_noalloc_refuses_sizes_beyond_its_array_before_any_device_call():
     lib = _lib.load()
-    # 16 value heads x 4,096 tokens need ~152 MiB of workspace; null pointers: nothing may be touched
+    # 16 value heads x 4,096 tokens need ~120 MiB of workspace; null pointers: nothing may be touched
     assert lib.gd_workspace_bytes(1, 4096, 16, 16, 128, 128, 0) > 64 << 20
     status = lib.gd_forward_noalloc(None, None, None, None, None, None, None, None, _lib.GD_BFLOAT16, 1, 4096, 16,
                                     16, 128, 128, FLAGS, None, None)
