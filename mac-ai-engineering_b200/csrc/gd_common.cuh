@@ -12,6 +12,7 @@
 #pragma once
 
 #include <cstdint>
+#include <cuda.h>  // CUtensorMap (the descriptor type only; the encoder is fetched at run time)
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -172,6 +173,17 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
   asm volatile(
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
       "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// A 4-D tiled tensor copy global -> shared (TMA engine, no multicast) completing on an mbarrier (transaction bytes =
+// the whole box; out-of-range elements arrive as zeros). c0 is the innermost coordinate.
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
+      "[%6];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
       : "memory");
 }
 
@@ -620,6 +632,7 @@ template <typename T>
 struct Piece {  // 8 consecutive elements, raw
   uint4 u;
   __device__ __forceinline__ void load(const T* p) { u = __ldg(reinterpret_cast<const uint4*>(p)); }
+  __device__ __forceinline__ void load_shared(const unsigned char* p) { u = *reinterpret_cast<const uint4*>(p); }
   __device__ __forceinline__ void zero() { u = make_uint4(0, 0, 0, 0); }
   __device__ __forceinline__ void to_f32(float* v) const;
 };
@@ -657,15 +670,39 @@ struct Piece<float> {
   }
 };
 
-template <typename T, int D, int NWARPS = 4>
+// ROT: lane (r = lane % 8, g = lane / 8) holds the 8-column groups (r + 4 g + j) mod 16 of its row instead of g + 4 j,
+// so that 8 rows 256 bytes apart in shared memory (a row-major staging of 16-bit rows, D = 128) are read by a
+// quarter warp without bank conflicts.
+template <typename T, int D, int NWARPS = 4, bool ROT = false>
 struct Rows {
   static constexpr int J = D / 32;              // 8-column groups per lane
   static constexpr int RB = 64 / (8 * NWARPS);  // row blocks per warp
+  static_assert(!ROT || (D == 128 && sizeof(T) == 2), "the rotated mapping covers 16 groups of 16 bytes a row");
   Piece<T> p[RB][J];
   __device__ __forceinline__ static int row(int rbi) {
     return 8 * (RB * (int)(threadIdx.x >> 5) + rbi) + (int)(threadIdx.x & 7);
   }
-  __device__ __forceinline__ static int col(int j) { return 8 * ((int)((threadIdx.x & 31) >> 3) + 4 * j); }
+  __device__ __forceinline__ static int col(int j) {
+    const int g = (int)((threadIdx.x & 31) >> 3);
+    return ROT ? 8 * (((int)(threadIdx.x & 7) + 4 * g + j) & 15) : 8 * (g + 4 * j);
+  }
+
+  // the same pieces from row-major rows already in shared memory (row r at raw + r * D * sizeof(T)); rows past T_ zero
+  __device__ __forceinline__ void issue_staged(const unsigned char* raw, int t0, int T_) {
+#pragma unroll
+    for (int rbi = 0; rbi < RB; ++rbi) {
+      const int r = row(rbi);
+      const bool valid = t0 + r < T_;
+#pragma unroll
+      for (int j = 0; j < J; ++j) {
+        if (valid) {
+          p[rbi][j].load_shared(raw + ((size_t)r * D + col(j)) * sizeof(T));
+        } else {
+          p[rbi][j].zero();
+        }
+      }
+    }
+  }
 
   __device__ __forceinline__ void issue(const T* x, int b, int t0, int T_, int heads, int hh) {
 #pragma unroll

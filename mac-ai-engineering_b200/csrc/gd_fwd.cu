@@ -10,6 +10,8 @@
 //   Vn = U - W S,  O = diag(gamma) Q S + M Vn,  S <- exp(G_last) S + K^T diag(e) Vn
 // Precision: bf16 operands with fp32 accumulation; A diag(beta) (in U), Vn (in M Vn) and e * Vn (in the state update)
 // are split into bf16 hi + lo pairs (two MMAs into one accumulator), the state is carried in fp32.
+#include <type_traits>
+
 #include "gd_common.cuh"
 #include "gd_layout.cuh"
 
@@ -36,8 +38,8 @@ struct PrepSmem {
   static constexpr size_t gam = beta + 64 * 4;            // [64] gamma = exp(G)
   static constexpr size_t bgam = gam + 64 * 4;            // [64] beta gamma
   static constexpr size_t scan = bgam + 64 * 4;           // [2] warp totals of the scan
-  static constexpr size_t bar = (scan + 16 + 7) & ~size_t(7);  // MMA commits
-  static constexpr size_t tmem = bar + 8;
+  static constexpr size_t bar = (scan + 16 + 7) & ~size_t(7);  // [2] MMA commits; raw rows landed (16-bit types)
+  static constexpr size_t tmem = bar + 2 * 8;
   static constexpr size_t total = tmem + 16;
 };
 
@@ -127,7 +129,10 @@ template <typename T, int DK, int DV>
 __global__ void __launch_bounds__(256, 2) prep_kernel(const T* __restrict__ q, const T* __restrict__ k,
                                                    const T* __restrict__ v, const float* __restrict__ g,
                                                    const float* __restrict__ beta, Layout lay, int flags,
-                                                   unsigned char* __restrict__ ws) {
+                                                   unsigned char* __restrict__ ws,
+                                                   const __grid_constant__ CUtensorMap tm_q,
+                                                   const __grid_constant__ CUtensorMap tm_k,
+                                                   const __grid_constant__ CUtensorMap tm_v) {
   using S = PrepSmem<DK, DV>;
   extern __shared__ __align__(1024) unsigned char smem[];
   ErrorWord* err = reinterpret_cast<ErrorWord*>(ws + lay.err);
@@ -145,13 +150,26 @@ __global__ void __launch_bounds__(256, 2) prep_kernel(const T* __restrict__ q, c
 
   GD_TRACE_AT(ws, lay, 0);
   GD_TRACE_CTA(ws, lay, 0);
+  if (tid == 0) {
+    mbar_init(bar, 1);      // MMA commits
+    mbar_init(bar + 1, 1);  // raw q / k / v rows landed
+    fence_mbar_init();
+  }
+  constexpr bool staged = sizeof(T) == 2;
+  if constexpr (staged) {
+    // 16-bit inputs: the chunk's raw q, k, v rows land row-major ([64][D], 256-byte rows) in the q, k, v tile buffers,
+    // one tensor-map copy each; rows past T arrive as zeros
+    if (tid == 0) {
+      mbar_arrive_expect_tx(bar + 1, (uint32_t)(64 * (2 * DK + DV) * 2));
+      tma_load_4d(smem + S::q, &tm_q, 0, hk, t0, b, bar + 1);
+      tma_load_4d(smem + S::k, &tm_k, 0, hk, t0, b, bar + 1);
+      tma_load_4d(smem + S::v, &tm_v, 0, h, t0, b, bar + 1);
+    }
+    __syncthreads();  // the barrier is initialised before anyone waits on it
+  }
   if (warp == 0) {
     tmem_alloc(tslot, 256);
     tmem_relinquish();
-  }
-  if (tid == 0) {
-    mbar_init(bar, 1);  // MMA commits
-    fence_mbar_init();
   }
 
   // l2 prologue and operand tiles: every row load in flight before any is converted
@@ -161,14 +179,27 @@ __global__ void __launch_bounds__(256, 2) prep_kernel(const T* __restrict__ q, c
   float* rq = bwd ? reinterpret_cast<float*>(ws + lay.rq) + rrow : nullptr;
   float* rk = bwd ? reinterpret_cast<float*>(ws + lay.rk) + rrow : nullptr;
   const float qscale = (flags & GD_SCALE_Q) ? rsqrtf((float)DK) : 1.f;
-  Rows<T, DK, 8> rq_rows, rk_rows;
-  Rows<T, DV, 8> rv_rows;
-  rq_rows.issue(q, b, t0, lay.T, lay.HK, hk);
-  rk_rows.issue(k, b, t0, lay.T, lay.HK, hk);
-  if (sizeof(T) == 2) rv_rows.issue(v, b, t0, lay.T, lay.H, h);
+  Rows<T, DK, 8, staged> rq_rows, rk_rows;
+  Rows<T, DV, 8, staged> rv_rows;
+  GD_TRACE_AT(ws, lay, 21);
+  bool landed = true;
+  if constexpr (staged) {
+    // each warp converts its own 8 rows in place: raw rows 8 w .. 8 w + 7 and tile row block w are the same 2 KB
+    landed = mbar_wait(bar + 1, 0, err, 13);
+    rq_rows.issue_staged(smem + S::q, t0, lay.T);
+    rk_rows.issue_staged(smem + S::k, t0, lay.T);
+    rv_rows.issue_staged(smem + S::v, t0, lay.T);
+    __syncwarp();
+  } else {
+    rq_rows.issue(q, b, t0, lay.T, lay.HK, hk);
+    rk_rows.issue(k, b, t0, lay.T, lay.HK, hk);
+  }
+  GD_TRACE_AT(ws, lay, 22);
   rq_rows.finish(t0, lay.T, norm, qscale, smem + S::q, rq, smem + S::ql);
+  GD_TRACE_AT(ws, lay, 23);
   rk_rows.finish(t0, lay.T, norm, 1.f, smem + S::k, rk, smem + S::kl);
-  if (sizeof(T) != 2) rv_rows.issue(v, b, t0, lay.T, lay.H, h);
+  GD_TRACE_AT(ws, lay, 24);
+  if (!staged) rv_rows.issue(v, b, t0, lay.T, lay.H, h);
   rv_rows.finish(t0, lay.T, false, 1.f, smem + S::v, nullptr, nullptr);
   GD_TRACE_AT(ws, lay, 1);
 
@@ -264,7 +295,7 @@ __global__ void __launch_bounds__(256, 2) prep_kernel(const T* __restrict__ q, c
     }
   }
   GD_TRACE_AT(ws, lay, 3);
-  bool ok = mbar_wait(bar, 0, err, 10);
+  bool ok = mbar_wait(bar, 0, err, 10) && landed;
   GD_TRACE_AT(ws, lay, 4);
   ok = __syncthreads_and(ok);
   tc_fence_after();
@@ -685,6 +716,40 @@ __global__ void __launch_bounds__(576) state_kernel(const float* __restrict__ s0
 // ------------------------------------------------------------------------------------------------------------------
 // launchers
 
+namespace {
+
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// cuTensorMapEncodeTiled from the driver (a host-only function: no device work, usable during stream capture)
+EncodeTiled encode_tiled() {
+  static EncodeTiled fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult res{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &res) != cudaSuccess ||
+        res != cudaDriverEntryPointSuccess)
+      p = nullptr;
+    return reinterpret_cast<EncodeTiled>(p);
+  }();
+  return fn;
+}
+
+// [B, T, heads, D] 16-bit rows as a 4-D tensor (D innermost); box = one head's D columns x 64 tokens
+bool rows_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int B, int T, int heads, int D) {
+  EncodeTiled enc = encode_tiled();
+  if (enc == nullptr) return false;
+  const cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)heads, (cuuint64_t)T, (cuuint64_t)B};
+  const cuuint64_t strides[3] = {(cuuint64_t)D * 2, (cuuint64_t)heads * D * 2, (cuuint64_t)T * heads * D * 2};
+  const cuuint32_t box[4] = {(cuuint32_t)D, 1, 64, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  return enc(m, dt, 4, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
 template <typename T, int DK, int DV>
 cudaError_t launch_prep(const void* q, const void* k, const void* v, const float* g, const float* beta,
                         const Layout& lay, int flags, unsigned char* ws, cudaStream_t st) {
@@ -693,9 +758,17 @@ cudaError_t launch_prep(const void* q, const void* k, const void* v, const float
   static bool attr_done[kMaxDevices] = {};  // once per device: no attribute call inside a graph capture
   cudaError_t e = set_smem_once(kern, S::total, attr_done);
   if (e != cudaSuccess) return e;
+  CUtensorMap mq{}, mk{}, mv{};  // 16-bit inputs only (fp32 rows are read by plain loads)
+  if (sizeof(T) == 2) {
+    const CUtensorMapDataType dt =
+        std::is_same<T, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    if (!rows_map(&mq, q, dt, lay.B, lay.T, lay.HK, DK) || !rows_map(&mk, k, dt, lay.B, lay.T, lay.HK, DK) ||
+        !rows_map(&mv, v, dt, lay.B, lay.T, lay.H, DV))
+      return cudaErrorInvalidValue;
+  }
   dim3 grid(lay.NT, lay.H, lay.B);
   kern<<<grid, 256, S::total, st>>>(static_cast<const T*>(q), static_cast<const T*>(k), static_cast<const T*>(v), g,
-                                    beta, lay, flags, ws);
+                                    beta, lay, flags, ws, mq, mk, mv);
   return cudaGetLastError();
 }
 
