@@ -300,6 +300,20 @@ def main():
     tokens_per_step = B * T * world
     value = tokens_per_step * args.steps / total_s
 
+    # ---- the stored-states mode (not the headline): same step with the states kept from the forward
+    stored = None
+    if not cfg["fwd_only"]:
+        stored_ms = stored_mode_ms(lib, t, cfg, flags, ws, nbytes, o, sT, dq, dk, dv, dg, db, ds0, stream, flush,
+                                   args.steps, args.warmup)
+        if world > 1:
+            sm = torch.tensor([stored_ms], dtype=torch.float64, device=dev)
+            dist.all_reduce(sm, op=dist.ReduceOp.MAX)
+            stored_ms = sm.item()
+        stored = {"ms_per_step": stored_ms, "value": tokens_per_step / (stored_ms / 1e3), "unit": "tokens/s",
+                  "mode": "RECOMPUTE_STATES=False (the reference's stored mode): the training forward keeps the chunk "
+                          "matrices, states and Vn, the backward skips the recompute; same bits as the headline's "
+                          "recompute mode"}
+
     # ---- per-kernel timing pass (not the headline): each entry point between events on the stream
     kern = kernel_times(lib, t, cfg, flags, ws, nbytes, o, sT, dq, dk, dv, dg, db, ds0, stream, flush)
     hbm, tflops, peak_kind = peaks()
@@ -340,6 +354,7 @@ def main():
                               "peak": f"{peak_kind} MEASURED_PEAKS.json"},
             "roofline": roof,
             "kernels": kern,
+            "stored_states": stored,
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": e2e["h2d"],
                     "d2h_bytes_per_step": e2e["d2h"], "ms_per_step": e2e["seconds"] * 1e3 / e2e["steps"]},
@@ -351,6 +366,49 @@ def main():
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def stored_mode_ms(lib, t, cfg, flags, ws, nbytes, o, sT, dq, dk, dv, dg, db, ds0, stream, flush, steps, warmup):
+    """Device ms per forward + backward step in the stored-states mode (gd_forward with GD_STORE_STATES, then
+    gd_backward with GD_STATES_STORED on the same workspace), CUDA graph, L2 flushed between steps as the headline."""
+    import torch
+    from macai_b200 import _lib
+    P = lambda x: None if x is None else ctypes.c_void_p(x.data_ptr())
+    sp = ctypes.c_void_p(stream.cuda_stream)
+    B, T, H, HK, D = cfg["B"], cfg["T"], cfg["H"], cfg["HK"], cfg["D"]
+    BF = _lib.GD_BFLOAT16
+
+    def step():
+        _lib.check(lib.gd_forward(P(t["q"]), P(t["k"]), P(t["v"]), P(t["g"]), P(t["beta"]), P(t["s0"]), P(o), P(sT),
+                                  BF, B, T, H, HK, D, D, flags | _lib.GD_STORE_STATES, P(ws), nbytes, sp), "gd_forward")
+        _lib.check(lib.gd_backward(P(t["q"]), P(t["k"]), P(t["v"]), None, P(t["beta"]), None, P(t["do"]), P(t["dsT"]),
+                                   P(dq), P(dk), P(dv), P(dg), P(db), P(ds0), BF, B, T, H, HK, D, D,
+                                   flags | _lib.GD_STATES_STORED, P(ws), nbytes, sp), "gd_backward")
+
+    with torch.cuda.stream(stream):
+        step()
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step()
+    with torch.cuda.stream(stream):
+        for _ in range(warmup):
+            flush.zero_()
+            graph.replay()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    with torch.cuda.stream(stream):
+        for i in range(steps):
+            flush.zero_()
+            starts[i].record(stream)
+            graph.replay()
+            ends[i].record(stream)
+    stream.synchronize()
+    code = lib.gd_read_error(P(ws), sp, None)
+    if code != 0:
+        raise RuntimeError(f"device error word {code} in the stored-states pass")
+    del graph
+    return sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / steps
 
 
 def kernel_times(lib, t, cfg, flags, ws, nbytes, o, sT, dq, dk, dv, dg, db, ds0, stream, flush, iters=5):

@@ -48,6 +48,7 @@ extern "C" {
 #define GD_L2NORM 1        /* use_qk_l2norm_in_kernel: q and k rows are l2-normalised (eps 1e-6) in the prep kernel */
 #define GD_STORE_STATES 2  /* the state pass keeps each chunk's entering state S_c and Vn for the backward */
 #define GD_SCALE_Q 4       /* q is multiplied by DK^-1/2 (after the l2 norm): the drop-in's query scaling */
+#define GD_STATES_STORED 8 /* gd_backward: the workspace already holds the states (gd_forward with GD_STORE_STATES) */
 
 /* Text for a status code. */
 const char* gd_status_string(int status);
@@ -66,8 +67,8 @@ int gd_prep(const void* q, const void* k, const void* v, const float* g, const f
 
 /* The sequential state pass, one CTA per (batch row, value head): for each chunk in order,
  * Vn = U - W S, O = diag(gamma) Q S + M Vn, S <- exp(G_last) S + K^T diag(e) Vn; writes o (q's dtype) and, when sT is
- * not NULL, the final state. s0 NULL = zero initial state. flags & GD_STORE_STATES: keeps S_c and Vn per chunk in
- * the workspace (the backward's recompute; o and sT may then be NULL).
+ * not NULL, the final state. s0 NULL = zero initial state. flags & GD_STORE_STATES: also keeps S_c and Vn per chunk in
+ * the workspace (the backward's recompute, o and sT then may be NULL; or the stored-states forward, with o).
  * Replaces: lib.gdc_fwd (src/macai/gated_delta/op.py:159 and :217, kernel _chunked.py:315-659). Requires gd_prep. */
 int gd_fwd_state(const float* s0, void* o, float* sT, int dtype, int B, int T, int H, int HK, int DK, int DV,
                  int flags, void* workspace, size_t workspace_bytes, void* stream);
@@ -89,15 +90,21 @@ int gd_bwd_chunk(const void* q, const void* k, const void* v, const float* beta,
                  void* dv, float* dg, float* dbeta, int dtype, int B, int T, int H, int HK, int DK, int DV, int flags,
                  void* workspace, size_t workspace_bytes, void* stream);
 
-/* The forward of the autograd function: gd_prep then gd_fwd_state.
+/* The forward of the autograd function: gd_prep then gd_fwd_state. flags & GD_STORE_STATES: the training forward of
+ * the stored-states mode (the reference's op.RECOMPUTE_STATES = False, op.py:27-33, :142, :151-155, :165-167): the
+ * workspace must hold gd_workspace_bytes(..., 1), and afterwards holds every chunk matrix, state and Vn the backward
+ * reads; keep it unchanged for gd_backward(GD_STATES_STORED). Outputs are the same bits in both modes.
  * Replaces: GatedDeltaRule.forward (src/macai/gated_delta/op.py:119-185) as called by the drop-in (op.py:296). */
 int gd_forward(const void* q, const void* k, const void* v, const float* g, const float* beta, const float* s0,
                void* o, float* sT, int dtype, int B, int T, int H, int HK, int DK, int DV, int flags, void* workspace,
                size_t workspace_bytes, void* stream);
 
 /* The backward with the chunk states recomputed from the inputs: gd_prep, gd_fwd_state(GD_STORE_STATES),
- * gd_bwd_state, gd_bwd_chunk. d_o / dsT NULL = zero cotangents; ds0 may be NULL.
- * Replaces: GatedDeltaRule.backward in its recompute mode (src/macai/gated_delta/op.py:187-243, :207-218). */
+ * gd_bwd_state, gd_bwd_chunk. d_o / dsT NULL = zero cotangents; ds0 may be NULL. flags & GD_STATES_STORED: the
+ * workspace comes from gd_forward(GD_STORE_STATES) on the same inputs and the recompute is skipped (g and s0 are then
+ * not read); the gradients are the same bits in both modes.
+ * Replaces: GatedDeltaRule.backward in its recompute mode (src/macai/gated_delta/op.py:187-243, :207-218) and its
+ * stored mode (ctx.mode "chunked", op.py:204-206). */
 int gd_backward(const void* q, const void* k, const void* v, const float* g, const float* beta, const float* s0,
                 const void* d_o, const float* dsT, void* dq, void* dk, void* dv, float* dg, float* dbeta, float* ds0,
                 int dtype, int B, int T, int H, int HK, int DK, int DV, int flags, void* workspace,

@@ -183,15 +183,18 @@ int gd_forward(const void* q, const void* k, const void* v, const float* g, cons
                size_t workspace_bytes, void* stream) {
   int s = check_dims(B, T, H, HK, DK, DV, dtype);
   if (s) return s;
-  // the forward-only layout in any workspace at least that large: prep then skips the backward's extra images
-  const size_t fwd_bytes = Layout::make(B, T, H, HK, DK, DV, false).total;
-  if (workspace_bytes < fwd_bytes) return GD_ERR_WORKSPACE;
-  s = gd_prep(q, k, v, g, beta, dtype, B, T, H, HK, DK, DV, flags & (GD_L2NORM | GD_SCALE_Q), workspace, fwd_bytes,
-              stream);
-  if (s) return s;
+  // GD_STORE_STATES: the backward layout, every image the backward reads written here (the stored-states training
+  // forward); otherwise the forward-only layout in any workspace at least that large (prep skips the extra images)
+  const bool keep = (flags & GD_STORE_STATES) != 0;
+  const size_t bytes = Layout::make(B, T, H, HK, DK, DV, keep).total;
+  if (workspace_bytes < bytes) return GD_ERR_WORKSPACE;
   if (!o) return GD_ERR_ARG;
   if (!aligned16(o)) return GD_ERR_ALIGN;
-  return gd_fwd_state(s0, o, sT, dtype, B, T, H, HK, DK, DV, flags & ~GD_STORE_STATES, workspace, fwd_bytes, stream);
+  const int f = flags & (GD_L2NORM | GD_SCALE_Q);
+  s = gd_prep(q, k, v, g, beta, dtype, B, T, H, HK, DK, DV, f, workspace, bytes, stream);
+  if (s) return s;
+  return gd_fwd_state(s0, o, sT, dtype, B, T, H, HK, DK, DV, f | (keep ? GD_STORE_STATES : 0), workspace, bytes,
+                      stream);
 }
 
 int gd_backward(const void* q, const void* k, const void* v, const float* g, const float* beta, const float* s0,
@@ -200,12 +203,22 @@ int gd_backward(const void* q, const void* k, const void* v, const float* g, con
                 size_t workspace_bytes, void* stream) {
   int s = check_dims(B, T, H, HK, DK, DV, dtype);
   if (s) return s;
+  if (!workspace) return GD_ERR_ARG;
+  if (!aligned16(workspace)) return GD_ERR_ALIGN;
   if (workspace_bytes < Layout::make(B, T, H, HK, DK, DV, true).total) return GD_ERR_WORKSPACE;
   const int f = flags & (GD_L2NORM | GD_SCALE_Q);
-  if ((s = gd_prep(q, k, v, g, beta, dtype, B, T, H, HK, DK, DV, f, workspace, workspace_bytes, stream))) return s;
-  if ((s = gd_fwd_state(s0, nullptr, nullptr, dtype, B, T, H, HK, DK, DV, f | GD_STORE_STATES, workspace,
-                        workspace_bytes, stream)))
-    return s;
+  if (flags & GD_STATES_STORED) {
+    // the workspace holds what gd_forward(GD_STORE_STATES) wrote for these inputs: no recompute; the error word is
+    // cleared here as gd_prep would
+    if ((s = check_device())) return s;
+    if (cudaMemsetAsync(workspace, 0, sizeof(gd::ErrorWord), static_cast<cudaStream_t>(stream)) != cudaSuccess)
+      return GD_ERR_LAUNCH;
+  } else {
+    if ((s = gd_prep(q, k, v, g, beta, dtype, B, T, H, HK, DK, DV, f, workspace, workspace_bytes, stream))) return s;
+    if ((s = gd_fwd_state(s0, nullptr, nullptr, dtype, B, T, H, HK, DK, DV, f | GD_STORE_STATES, workspace,
+                          workspace_bytes, stream)))
+      return s;
+  }
   if ((s = gd_bwd_state(d_o, dsT, ds0, dtype, B, T, H, HK, DK, DV, f, workspace, workspace_bytes, stream))) return s;
   return gd_bwd_chunk(q, k, v, beta, d_o, dq, dk, dv, dg, dbeta, dtype, B, T, H, HK, DK, DV, f, workspace,
                       workspace_bytes, stream);

@@ -69,6 +69,7 @@ struct ChunkSmem {
   static constexpr size_t tmem = bar + NBAR * 8;
   static constexpr size_t total = tmem + 16;
   static_assert(dwt + DK * 64 * 2 <= in3, "dM and dW^T fit in the dVn region");
+  static_assert(scr % 16 == 0, "scr is read as float4");
 };
 
 // partial-sum arrays (index into ChunkSmem::part): by TMEM lane quadrant [4][64] unless noted
@@ -679,7 +680,7 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
         // x_hat from the q / k images (hi + lo) and the prologue's rsqrt r, both in shared memory
         const float* sRq = reinterpret_cast<const float*>(smem + S::rqk);
         const float* sRk = sRq + 64;
-        float* dotq = scr;
+        float* dotq = scr;  // [64 tokens][4 head-dimension quarters]: one 16-byte read per token below
         float* dotk = scr + 4 * 64;
         const float inv_qscale = 1.f / qscale;
         float x[16];
@@ -689,12 +690,12 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
 #pragma unroll
           for (int j = 0; j < 16; ++j) x[j] *= inv_qscale * dQ[j];
           float s = warp_reduce_scatter16(x);
-          if (lane < 16) dotq[qd * 64 + tok0 + lane] = s;
+          if (lane < 16) dotq[(tok0 + lane) * 4 + qd] = s;
           row16<true>(kh, kl, dcol, tok0, x);
 #pragma unroll
           for (int j = 0; j < 16; ++j) x[j] *= dK[j];
           s = warp_reduce_scatter16(x);
-          if (lane < 16) dotk[qd * 64 + tok0 + lane] = s;
+          if (lane < 16) dotk[(tok0 + lane) * 4 + qd] = s;
         }
         epi_sync();
         GD_TRACE_AT(ws, lay, 32 * n + 21);
@@ -706,7 +707,8 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             const int i = tok0 + j;
-            const float dot = dotq[i] + dotq[64 + i] + dotq[128 + i] + dotq[192 + i];
+            const float4 d4 = *reinterpret_cast<const float4*>(dotq + 4 * i);
+            const float dot = d4.x + d4.y + d4.z + d4.w;
             x[j] = qscale * sRq[i] * (dQ[j] - x[j] * inv_qscale * dot);
           }
         } else {
@@ -719,7 +721,8 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             const int i = tok0 + j;
-            const float dot = dotk[i] + dotk[64 + i] + dotk[128 + i] + dotk[192 + i];
+            const float4 d4 = *reinterpret_cast<const float4*>(dotk + 4 * i);
+            const float dot = d4.x + d4.y + d4.z + d4.w;
             x[j] = sRk[i] * (dK[j] - x[j] * dot);
           }
         } else {

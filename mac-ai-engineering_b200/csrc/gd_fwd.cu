@@ -440,8 +440,9 @@ __global__ void __launch_bounds__(256, 2) prep_kernel(const T* __restrict__ q, c
 //   EPI: (after handing Vn of chunk c to the tensor core) O of chunk c - 1 = diag(gamma) Q S + M Vn -> global (16-byte
 //        rows after an 8 x 8 transpose): it runs under chunk c's state-update product, off the chain
 //   EPI: wait ds_full -> S <- exp(G_last) S + K~^T Vn -> S tile -> st_full
-// With GD_STORE_STATES (the backward's recompute) O is not formed; the pass keeps S_c (fp32 and a bf16 S_c^T image) and
-// the Vn^T hi / lo images of every chunk for the backward kernels (each CTA its 64 rows of them).
+// With GD_STORE_STATES (the backward's recompute, or a training forward that keeps its states) the pass also keeps S_c
+// (fp32 and a bf16 S_c^T image) and the Vn^T hi / lo images of every chunk for the backward kernels (each CTA its 64
+// rows of them); O is formed when o is not null.
 
 constexpr int kVsplit = 2;  // CTAs per (value head, batch row)
 
@@ -498,7 +499,7 @@ __global__ void __launch_bounds__(576) state_kernel(const float* __restrict__ s0
   uint64_t* st_full = bars + 11;    // 16 epilogue warps
   uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + S::tmem);
   const bool store = (flags & GD_STORE_STATES) != 0 && lay.backward();
-  const bool out = o != nullptr && !store;
+  const bool out = o != nullptr;  // both at once: the stored-states training forward
   const int NT = lay.NT;
   const size_t row0 = ((size_t)b * lay.H + h) * NT;
 

@@ -21,8 +21,13 @@ from .. import _lib
 CHUNK = 64
 # Head widths the kernels are built for (the Qwen3.5 / Qwen3-Next linear-attention shapes).
 HEAD_DIMS = (128,)
-# What each call ran, as the reference's op.CALLS (op.py:44-46): "fwd", "bwd", by (B, T, H, HK) shape class.
+# What each call ran, as the reference's op.CALLS (op.py:44-46): "fwd", "fwd stored", "bwd", "bwd stored".
 CALLS: collections.Counter = collections.Counter()
+# RECOMPUTE_STATES, as the reference's setting (op.py:27-33), read at each call: True (the default) = a training forward
+# keeps only its inputs and the backward recomputes the chunk matrices, states and Vn; False = the training forward
+# writes them into a workspace the autograd context keeps until the backward (gd_workspace_bytes(..., 1) of device
+# memory per call), and the backward skips the recompute. Outputs and gradients are the same bits either way.
+RECOMPUTE_STATES = True
 
 _DTYPES = {torch.float32: _lib.GD_FLOAT32, torch.float16: _lib.GD_FLOAT16, torch.bfloat16: _lib.GD_BFLOAT16}
 
@@ -98,6 +103,34 @@ def _(q, k, v, g, beta, s0, flags):
     return q.new_empty(B, T, H, DV), q.new_empty(B, H, DK, DV, dtype=torch.float32)
 
 
+@torch.library.custom_op("macai_b200::gated_delta_fwd_stored", mutates_args=(), device_types="cuda")
+def gated_delta_fwd_stored(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Tensor, beta: torch.Tensor,
+                           s0: Optional[torch.Tensor], flags: int) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """The stored-states training forward (RECOMPUTE_STATES = False; the reference's op.py:141-155, :165-167): o and
+    S_T as gated_delta_fwd, plus the workspace (uint8) holding every chunk matrix, state and Vn the backward reads."""
+    B, T, H, HK, DK, DV = _dims(q, v)
+    lib = _lib.load()
+    dev = q.device
+    o = torch.empty(B, T, H, DV, dtype=q.dtype, device=dev)
+    sT = torch.empty(B, H, DK, DV, dtype=torch.float32, device=dev)
+    nbytes = workspace_bytes(B, T, H, HK, DK, DV, True)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        st = lib.gd_forward(_p(q), _p(k), _p(v), _p(g), _p(beta), _p(s0), _p(o), _p(sT), _DTYPES[q.dtype], B, T, H, HK,
+                            DK, DV, flags | _lib.GD_STORE_STATES, _p(ws), nbytes, _stream(dev))
+    _lib.check(st, "gd_forward")
+    CALLS["fwd stored"] += 1
+    return o, sT, ws
+
+
+@gated_delta_fwd_stored.register_fake
+def _(q, k, v, g, beta, s0, flags):
+    B, T, H, HK, DK, DV = _dims(q, v)
+    nbytes = workspace_bytes(B, T, H, HK, DK, DV, True)
+    return (q.new_empty(B, T, H, DV), q.new_empty(B, H, DK, DV, dtype=torch.float32),
+            q.new_empty(nbytes, dtype=torch.uint8))
+
+
 @torch.library.custom_op("macai_b200::gated_delta_bwd", mutates_args=(), device_types="cuda")
 def gated_delta_bwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Tensor, beta: torch.Tensor,
                     s0: Optional[torch.Tensor], do: torch.Tensor, dsT: Optional[torch.Tensor],
@@ -131,6 +164,41 @@ def _(q, k, v, g, beta, s0, do, dsT, flags):
             q.new_empty(B, T, H, **f32), q.new_empty(B, H, DK, DV, **f32))
 
 
+# ws is declared unmutated: the backward rewrites only the workspace's backward scratch area (the reverse pass's dS,
+# dVn and dO images and partial sums), which holds nothing between calls and is always written before it is read; the
+# kept states are only read. (Declaring it mutated would bump the saved tensor's version and refuse a second
+# backward over a retained graph.)
+@torch.library.custom_op("macai_b200::gated_delta_bwd_stored", mutates_args=(), device_types="cuda")
+def gated_delta_bwd_stored(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, beta: torch.Tensor, do: torch.Tensor,
+                           dsT: Optional[torch.Tensor], ws: torch.Tensor,
+                           flags: int) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor,
+                                                torch.Tensor]:
+    """(dq, dk, dv, dg, dbeta, ds0) from the states gated_delta_fwd_stored kept in ws (the reference's stored mode,
+    op.py:204-206): the reverse state pass and the per-chunk gradients only."""
+    B, T, H, HK, DK, DV = _dims(q, v)
+    lib = _lib.load()
+    dev = q.device
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    dg = torch.empty(B, T, H, dtype=torch.float32, device=dev)
+    dbeta = torch.empty(B, T, H, dtype=torch.float32, device=dev)
+    ds0 = torch.empty(B, H, DK, DV, dtype=torch.float32, device=dev)
+    with torch.cuda.device(dev):
+        st = lib.gd_backward(_p(q), _p(k), _p(v), None, _p(beta), None, _p(do), _p(dsT), _p(dq), _p(dk), _p(dv),
+                             _p(dg), _p(dbeta), _p(ds0), _DTYPES[q.dtype], B, T, H, HK, DK, DV,
+                             flags | _lib.GD_STATES_STORED, _p(ws), ws.numel(), _stream(dev))
+    _lib.check(st, "gd_backward")
+    CALLS["bwd stored"] += 1
+    return dq, dk, dv, dg, dbeta, ds0
+
+
+@gated_delta_bwd_stored.register_fake
+def _(q, k, v, beta, do, dsT, ws, flags):
+    B, T, H, HK, DK, DV = _dims(q, v)
+    f32 = dict(dtype=torch.float32)
+    return (torch.empty_like(q), torch.empty_like(k), torch.empty_like(v), q.new_empty(B, T, H, **f32),
+            q.new_empty(B, T, H, **f32), q.new_empty(B, H, DK, DV, **f32))
+
+
 def _setup_context(ctx, inputs, output):
     q, k, v, g, beta, s0, flags = inputs
     ctx.save_for_backward(q, k, v, g, beta, s0)
@@ -151,22 +219,52 @@ def _backward(ctx, do, dsT):
 gated_delta_fwd.register_autograd(_backward, setup_context=_setup_context)
 
 
+def _setup_context_stored(ctx, inputs, output):
+    q, k, v, g, beta, s0, flags = inputs
+    ctx.save_for_backward(q, k, v, beta, output[2])
+    ctx.flags = flags
+    ctx.has_s0 = s0 is not None
+
+
+def _backward_stored(ctx, do, dsT, _dws):
+    q, k, v, beta, ws = ctx.saved_tensors
+    if do is None:
+        do = torch.zeros(*v.shape, dtype=q.dtype, device=q.device)
+    do = do.to(q.dtype).contiguous()
+    dsT = None if dsT is None else dsT.to(torch.float32).contiguous()
+    dq, dk, dv, dg, dbeta, ds0 = gated_delta_bwd_stored(q, k, v, beta, do, dsT, ws, ctx.flags)
+    return dq, dk, dv, dg, dbeta, (ds0 if ctx.has_s0 else None), None
+
+
+gated_delta_fwd_stored.register_autograd(_backward_stored, setup_context=_setup_context_stored)
+
+
+def _forward(q, k, v, g, beta, s0, flags):
+    """The forward op for this call: the stored-states one when RECOMPUTE_STATES is False and autograd will record
+    the call (the reference keeps states only for a backward, op.py:108, :141-142), else the plain one."""
+    if not RECOMPUTE_STATES and torch.is_grad_enabled() and any(
+            t is not None and t.requires_grad for t in (q, k, v, g, beta, s0)):
+        o, sT, _ = gated_delta_fwd_stored(q, k, v, g, beta, s0, flags)
+        return o, sT
+    return gated_delta_fwd(q, k, v, g, beta, s0, flags)
+
+
 # ------------------------------------------------------------------------------------------------------------------
 # the reference's Python surface
 
 class GatedDeltaRule:
     """o, S_T = recurrence(q, k, v, g, beta, S_0) on [B, T, H, D] tensors with q already normalised and scaled, as the
     reference's autograd function (op.py:116-257): `GatedDeltaRule.apply(q, k, v, g, beta, s0, save)`. `save` is
-    accepted for signature compatibility; autograd records the op whenever an input requires grad. The backward always
-    recomputes the chunk states (the reference's default, op.py:27-33)."""
+    accepted for signature compatibility; autograd records the op whenever an input requires grad. The backward
+    recomputes the chunk states unless RECOMPUTE_STATES is False (the reference's setting, op.py:27-33)."""
 
     @staticmethod
     def apply(q, k, v, g, beta, s0, save: bool = True):
         dt = q.dtype
         k, v = k.to(dt), v.to(dt)
         check_shapes(q, k, v, g, beta, s0)
-        return gated_delta_fwd(q.contiguous(), k.contiguous(), v.contiguous(), g.float().contiguous(),
-                               beta.float().contiguous(), None if s0 is None else s0.float().contiguous(), 0)
+        return _forward(q.contiguous(), k.contiguous(), v.contiguous(), g.float().contiguous(),
+                        beta.float().contiguous(), None if s0 is None else s0.float().contiguous(), 0)
 
 
 def l2norm(x: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
@@ -195,8 +293,8 @@ def chunk_gated_delta_rule(query, key, value, g, beta, chunk_size: int = 64, ini
     check_shapes(query, k, v, g, beta, initial_state)
     flags = _lib.GD_SCALE_Q | (_lib.GD_L2NORM if use_qk_l2norm_in_kernel else 0)
     s0 = None if initial_state is None else initial_state.to(torch.float32).contiguous()
-    o, sT = gated_delta_fwd(query.contiguous(), k.contiguous(), v.contiguous(), g.to(torch.float32).contiguous(),
-                            beta.to(torch.float32).contiguous(), s0, flags)
+    o, sT = _forward(query.contiguous(), k.contiguous(), v.contiguous(), g.to(torch.float32).contiguous(),
+                     beta.to(torch.float32).contiguous(), s0, flags)
     return o, (sT if output_final_state else None)
 
 
