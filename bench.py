@@ -316,6 +316,7 @@ def main():
 
     # ---- per-kernel timing pass (not the headline): each entry point between events on the stream
     kern = kernel_times(lib, t, cfg, flags, ws, nbytes, o, sT, dq, dk, dv, dg, db, ds0, stream, flush)
+    gates = gates_times(lib, dev, stream, flush) if rank == 0 else None
     hbm, tflops, peak_kind = peaks()
     roof = roofline(kern, cfg, hbm, tflops, peak_kind)
 
@@ -355,6 +356,7 @@ def main():
             "roofline": roof,
             "kernels": kern,
             "stored_states": stored,
+            "gates": gates,
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": e2e["h2d"],
                     "d2h_bytes_per_step": e2e["d2h"], "ms_per_step": e2e["seconds"] * 1e3 / e2e["steps"]},
@@ -409,6 +411,56 @@ def stored_mode_ms(lib, t, cfg, flags, ws, nbytes, o, sT, dq, dk, dv, dg, db, ds
         raise RuntimeError(f"device error word {code} in the stored-states pass")
     del graph
     return sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / steps
+
+
+def gates_times(lib, dev, stream, flush, iters=10):
+    """The layer's gates (gd_gates_fwd / gd_gates_bwd, bf16 b and a, fp32 A_log and dt_bias, frozen gate weights as in
+    LoRA training: no per-head sums) at config 1's [B, T, H] and at config 4's [64, 4096, 32]: device microseconds per
+    call (CUDA events, L2 flushed before each) and HBM bandwidth from the algorithmic bytes (forward: b, a read, beta, g
+    written = 12 B per element; backward: b, a, dbeta, dg read, db, da written = 16 B per element)."""
+    import torch
+    from macai_b200 import _lib
+    P = lambda x: None if x is None else ctypes.c_void_p(x.data_ptr())
+    sp = ctypes.c_void_p(stream.cuda_stream)
+    hbm, _, _ = peaks()
+    out = {}
+    for tag, shape in (("c1", (4, 1024, 16)), ("c4", (64, 4096, 32))):
+        n, H = shape[0] * shape[1] * shape[2], shape[2]
+        gen = torch.Generator(device=dev).manual_seed(7)
+        b = torch.randn(shape, generator=gen, device=dev).to(torch.bfloat16)
+        a = torch.randn(shape, generator=gen, device=dev).to(torch.bfloat16)
+        A_log = torch.rand(H, generator=gen, device=dev) * 2.7
+        dt_bias = torch.randn(H, generator=gen, device=dev)
+        beta = torch.empty(shape, device=dev)
+        g = torch.empty(shape, device=dev)
+        dbeta, dg = torch.randn_like(beta), torch.randn_like(g)
+        db, da = torch.empty_like(b), torch.empty_like(a)
+        BF, F32 = _lib.GD_BFLOAT16, _lib.GD_FLOAT32
+
+        def fwd():
+            _lib.check(lib.gd_gates_fwd(P(b), P(a), P(A_log), P(dt_bias), P(beta), P(g), BF, F32, n, H, sp), "gates")
+
+        def bwd():
+            _lib.check(lib.gd_gates_bwd(P(b), P(a), P(A_log), P(dt_bias), P(dbeta), P(dg), P(db), P(da), None, None,
+                                        BF, F32, n, H, None, 0, sp), "gates")
+        res = {"elements": n}
+        for name, f, per in (("fwd", fwd, 12), ("bwd", bwd, 16)):
+            with torch.cuda.stream(stream):
+                f()
+                tot = 0.0
+                for _ in range(iters):
+                    flush.zero_()
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record(stream)
+                    f()
+                    e1.record(stream)
+                    e1.synchronize()
+                    tot += e0.elapsed_time(e1)
+            us = tot / iters * 1e3
+            gbs = per * n / (us * 1e-6) / 1e9
+            res[name] = {"us": us, "gbs": gbs, "frac_hbm": gbs / hbm}
+        out[tag] = res
+    return out
 
 
 def kernel_times(lib, t, cfg, flags, ws, nbytes, o, sT, dq, dk, dv, dg, db, ds0, stream, flush, iters=5):

@@ -132,6 +132,28 @@ int gd_forward_noalloc(const void* q, const void* k, const void* v, const float*
                        const float* s0, void* o, float* sT, int dtype, int B, int T, int H, int HK, int DK, int DV,
                        int flags, void* stream, int* device_status);
 
+/* ---- the layer's gates (the step before the rule) ----
+ * beta = sigmoid(b), g = -exp(A_log) * softplus(a + dt_bias) (softplus with PyTorch's threshold of 20), both float32,
+ * from b, a [n = rows * H] in `dtype` and A_log, dt_bias [H] in `wdtype` (GD_FLOAT32 / GD_FLOAT16 / GD_BFLOAT16);
+ * element i belongs to head i % H. n < 2^31. No allocation, asynchronous on `stream`.
+ * Replaces: the reference's one-pass gates kernels gates_fwd_* (src/macai/layer/_gates.py:27-35, :51-56, dispatched at
+ * :91-92) and their autograd function's forward (:84-95). */
+int gd_gates_fwd(const void* b, const void* a, const void* A_log, const void* dt_bias, float* beta, float* g,
+                 int dtype, int wdtype, long long n, int H, void* stream);
+
+/* Bytes of workspace gd_gates_bwd needs when it forms dA_log or ddt_bias (0 for invalid sizes). */
+size_t gd_gates_workspace_bytes(long long n, int H);
+
+/* db = dbeta * beta * (1 - beta), da = dg * (-exp(A_log)) * sigmoid(a + dt_bias) (1 above the threshold), in `dtype`;
+ * dbeta / dg NULL = zero cotangents. dA_log = sum over rows of dg * g and ddt_bias = sum over rows of da (before its
+ * cast), in `wdtype`, when not NULL (then `workspace` holds gd_gates_workspace_bytes(n, H)); the sums are taken in a
+ * fixed order (no atomics: the same bits every run).
+ * Replaces: gates_bwd_* (src/macai/layer/_gates.py:38-48, :57-63, dispatched at :105-106) and the autograd
+ * function's reductions for trained gates (:108-116). */
+int gd_gates_bwd(const void* b, const void* a, const void* A_log, const void* dt_bias, const float* dbeta,
+                 const float* dg, void* db, void* da, void* dA_log, void* ddt_bias, int dtype, int wdtype, long long n,
+                 int H, void* workspace, size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

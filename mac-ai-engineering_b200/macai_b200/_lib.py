@@ -17,7 +17,8 @@ GD_L2NORM, GD_STORE_STATES, GD_SCALE_Q, GD_STATES_STORED = 1, 2, 4, 8
 
 # every entry point declared in include/gated_delta_b200.h
 EXPORTS = ("gd_status_string", "gd_workspace_bytes", "gd_prep", "gd_fwd_state", "gd_bwd_state", "gd_bwd_chunk",
-           "gd_forward", "gd_backward", "gd_read_error", "gd_forward_noalloc")
+           "gd_forward", "gd_backward", "gd_read_error", "gd_forward_noalloc", "gd_gates_fwd",
+           "gd_gates_workspace_bytes", "gd_gates_bwd")
 
 _P = ctypes.c_void_p
 _I = ctypes.c_int
@@ -34,6 +35,9 @@ _SIGS = {
     "gd_backward": ([_P] * 14 + [_I] * 8 + [_P, _SZ, _P], _I),
     "gd_read_error": ([_P, _P, ctypes.POINTER(_I)], _I),
     "gd_forward_noalloc": ([_P] * 8 + [_I] * 8 + [_P, ctypes.POINTER(_I)], _I),
+    "gd_gates_fwd": ([_P] * 6 + [_I, _I, ctypes.c_longlong, _I, _P], _I),
+    "gd_gates_workspace_bytes": ([ctypes.c_longlong, _I], _SZ),
+    "gd_gates_bwd": ([_P] * 10 + [_I, _I, ctypes.c_longlong, _I, _P, _SZ, _P], _I),
 }
 
 _lib = None

@@ -66,3 +66,19 @@ def test_error_type_carries_status():
     assert e.status == _lib.GD_ERR_TIMEOUT and "gd_forward" in str(e)
     with pytest.raises(_lib.GatedDeltaError):
         _lib.check(_lib.GD_ERR_SHAPE, "x")
+
+
+def test_gates_refusals_before_any_device_call():
+    lib = _lib.load()
+    nul = ctypes.c_void_p(0)
+    one = ctypes.c_void_p(256)
+    # n not a multiple of H, unknown dtype, null outputs: status codes, nothing launched
+    assert lib.gd_gates_fwd(one, one, one, one, one, one, 2, 0, 100, 16, nul) == _lib.GD_ERR_SHAPE
+    assert lib.gd_gates_fwd(one, one, one, one, one, one, 7, 0, 64, 16, nul) == _lib.GD_ERR_ARG
+    assert lib.gd_gates_fwd(one, one, one, one, nul, one, 2, 0, 64, 16, nul) == _lib.GD_ERR_ARG
+    assert lib.gd_gates_fwd(nul, nul, nul, nul, nul, nul, 2, 0, 0, 16, nul) == _lib.GD_OK  # no elements
+    # per-head sums without a workspace
+    ws = lib.gd_gates_workspace_bytes(64 * 1024, 16)
+    assert ws >= 2 * 16 * 4 and lib.gd_gates_workspace_bytes(100, 16) == 0
+    assert lib.gd_gates_bwd(one, one, one, one, one, one, one, one, one, nul, 2, 0, 64 * 1024, 16, nul, 0,
+                            nul) == _lib.GD_ERR_WORKSPACE
