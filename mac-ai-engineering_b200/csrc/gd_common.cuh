@@ -285,10 +285,13 @@ __device__ __forceinline__ void mma_tiles(uint32_t d_tmem, int M, int N, int K, 
     y_sbo = y.rowblk_bytes();
     y_step = 256;
   }
-  for (int kk = 0; kk < K / 16; ++kk) {
-    mma_bf16(d_tmem, sdesc(xa + kk * x_step, x_lbo, x_sbo), sdesc(ya + kk * y_step, y_lbo, y_sbo), idesc,
-             (accumulate || kk > 0) ? 1u : 0u);
-  }
+  // the descriptors once; each K step moves only the 14-bit start-address field (shared addresses < 2^18, so the
+  // field never carries into the strides)
+  const uint64_t dx = sdesc(xa, x_lbo, x_sbo), dy = sdesc(ya, y_lbo, y_sbo);
+  const uint64_t sx = x_step >> 4, sy = y_step >> 4;
+  mma_bf16(d_tmem, dx, dy, idesc, accumulate ? 1u : 0u);
+#pragma unroll 8
+  for (int kk = 1; kk < K / 16; ++kk) mma_bf16(d_tmem, dx + kk * sx, dy + kk * sy, idesc, 1u);
 }
 
 // TMEM -> registers: this warp's 32 lanes, 32 consecutive fp32 columns each (thread t gets lane (lane_base + t)).

@@ -631,6 +631,12 @@ __global__ void __launch_bounds__(576) state_kernel(const float* __restrict__ s0
       gcur_last = __ldg(gp + 63);
     };
     load_u(row0);
+    // O of one chunk: 16-byte token rows after an 8 x 8 transpose in 8-lane groups
+    float o8[8];
+    auto store_o = [&](int p) {
+      store_token_rows8<T>(o8, o + ((size_t)b * lay.T * lay.H + h) * DV, (size_t)lay.H * DV, p * C + tk, lay.T,
+                           vbase + 16 * qd + 8 * ((lane >> 3) & 1));
+    };
     // pass c computes Vn and the state update of chunk c (c < NT) and, between them, O of chunk c - 1 (c >= 1)
     for (int c = 0; c <= NT; ++c) {
       const size_t cidx = row0 + c;
@@ -654,25 +660,29 @@ __global__ void __launch_bounds__(576) state_kernel(const float* __restrict__ s0
         GD_TRACE_AT(ws, lay, 8 * c + 2);
       }
       if (out && c >= 1) {
-        // * O of chunk c - 1 = diag(gamma) Q S + M Vn, under this chunk's state-update product
+        // * O of chunk c - 1 = diag(gamma) Q S + M Vn, formed under this chunk's state-update product and stored after
+        // the update (under the next W S). Its (Q S)^T and (M Vn)^T are complete: ws_full of chunk c, waited above,
+        // tracks every earlier product; after the last chunk they are waited for here.
         const int p = c - 1, s = p & 1;
-        if (!mbar_wait(qs_full + s, (p >> 1) & 1, err, 26) || !mbar_wait(mv_full + s, (p >> 1) & 1, err, 27)) {
+        if (c == NT &&
+            (!mbar_wait(qs_full + s, (p >> 1) & 1, err, 26) || !mbar_wait(mv_full + s, (p >> 1) & 1, err, 27))) {
           ok = false;
           break;
         }
         GD_TRACE_AT(ws, lay, 8 * c + 5);
         tc_fence_after();
-        float qs[8], mv[8];
-        tmem_ld8hx2(tmem_lane_addr(tm + 64 + 64 * s, warp, 16 * quarter), qs,
+        float mv[8];
+        tmem_ld8hx2(tmem_lane_addr(tm + 64 + 64 * s, warp, 16 * quarter), o8,
                     tmem_lane_addr(tm + 192 + 64 * s, warp, 16 * quarter), mv);
         GD_TRACE_AT(ws, lay, 8 * c + 6);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) qs[j] = fmaf(__expf(gprev[j]), qs[j], mv[j]);
-        store_token_rows8<T>(qs, o + ((size_t)b * lay.T * lay.H + h) * DV, (size_t)lay.H * DV, p * C + tk, lay.T,
-                             vbase + 16 * qd + 8 * ((lane >> 3) & 1));
+        for (int j = 0; j < 8; ++j) o8[j] = fmaf(__expf(gprev[j]), o8[j], mv[j]);
         tc_fence_before();
       }
-      if (c == NT) break;
+      if (c == NT) {
+        if (out) store_o(NT - 1);
+        break;
+      }
       GD_TRACE_AT(ws, lay, 8 * c + 7);
       const float gl = __expf(gcur_last);
 #pragma unroll
@@ -697,6 +707,7 @@ __global__ void __launch_bounds__(576) state_kernel(const float* __restrict__ s0
         mbar_arrive_warp(st_full);
       }
       if (store && c + 1 < NT) store_scf(c + 1);  // off the chain: the next MMAs are already unblocked
+      if (out && c >= 1) store_o(c - 1);          // likewise
       GD_TRACE_AT(ws, lay, 8 * c + 4);
     }
     GD_TRACE_AT(ws, lay, 4002);

@@ -42,6 +42,57 @@ __device__ __forceinline__ __half cvt<__half>(float x) { return __float2half_rn(
 template <>
 __device__ __forceinline__ __nv_bfloat16 cvt<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
 
+// 8 consecutive elements (16-byte aligned start) to / from float
+__device__ __forceinline__ float2 unpack2(uint32_t w, const __nv_bfloat16*) {
+  return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w));
+}
+__device__ __forceinline__ float2 unpack2(uint32_t w, const __half*) {
+  return __half22float2(*reinterpret_cast<const __half2*>(&w));
+}
+__device__ __forceinline__ uint32_t pack2(float x, float y, const __nv_bfloat16*) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(x, y);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+__device__ __forceinline__ uint32_t pack2(float x, float y, const __half*) {
+  const __half2 v = __floats2half2_rn(x, y);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+template <typename T>
+__device__ __forceinline__ void ld8(const T* p, float (&v)[8]) {
+  if constexpr (sizeof(T) == 4) {
+    const float4 x = __ldg(reinterpret_cast<const float4*>(p)), y = __ldg(reinterpret_cast<const float4*>(p) + 1);
+    v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w; v[4] = y.x; v[5] = y.y; v[6] = y.z; v[7] = y.w;
+  } else {
+    const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = unpack2(w[j], p);
+      v[2 * j] = f.x;
+      v[2 * j + 1] = f.y;
+    }
+  }
+}
+template <typename T>
+__device__ __forceinline__ void st8(T* p, const float (&v)[8]) {
+  if constexpr (sizeof(T) == 4) {
+    reinterpret_cast<float4*>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
+    reinterpret_cast<float4*>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
+  } else {
+    *reinterpret_cast<uint4*>(p) = make_uint4(pack2(v[0], v[1], p), pack2(v[2], v[3], p), pack2(v[4], v[5], p),
+                                              pack2(v[6], v[7], p));
+  }
+}
+__device__ __forceinline__ void ld8f(const float* p, float (&v)[8]) {
+  if (p == nullptr) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = 0.f;
+    return;
+  }
+  const float4 x = __ldg(reinterpret_cast<const float4*>(p)), y = __ldg(reinterpret_cast<const float4*>(p) + 1);
+  v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w; v[4] = y.x; v[5] = y.y; v[6] = y.z; v[7] = y.w;
+}
+
 __device__ __forceinline__ float sigmoid(float x) { return 1.f / (1.f + expf(-x)); }
 __device__ __forceinline__ float softplus(float x) { return x > kThreshold ? x : log1pf(expf(x)); }
 
@@ -68,20 +119,42 @@ __device__ __forceinline__ void head_consts(const TW* alog, const TW* dtb, const
   }
 }
 
+// Each thread takes groups of 8 consecutive elements; vec: every pointer 16-byte aligned, so whole groups move as
+// 16-byte pieces (the tail group, and every group when vec is false, element by element).
 template <typename T, typename TW>
 __global__ void __launch_bounds__(kThreads) gates_fwd_kernel(const T* __restrict__ b, const T* __restrict__ a,
                                                              const TW* __restrict__ alog, const TW* __restrict__ dtb,
                                                              float* __restrict__ beta, float* __restrict__ g,
-                                                             long long n, int H) {
+                                                             int n, int H, bool vec) {
   __shared__ float s_na[kSmemHeads], s_dt[kSmemHeads];
   stage_heads(alog, dtb, H, s_na, s_dt);
-  const long long stride = (long long)gridDim.x * blockDim.x;
-  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
-    const int h = (int)(i % H);
-    float na, dt;
-    head_consts(alog, dtb, s_na, s_dt, h, na, dt);
-    beta[i] = sigmoid(ld(b, i));
-    g[i] = na * softplus(ld(a, i) + dt);
+  const int groups = (n + 7) / 8, stride = gridDim.x * blockDim.x;
+  for (int gi = blockIdx.x * blockDim.x + threadIdx.x; gi < groups; gi += stride) {
+    const int i0 = 8 * gi;
+    int h = i0 % H;
+    if (vec && i0 + 8 <= n) {
+      float vb[8], va[8], ob[8], og[8];
+      ld8(b + i0, vb);
+      ld8(a + i0, va);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float na, dt;
+        head_consts(alog, dtb, s_na, s_dt, h, na, dt);
+        ob[j] = sigmoid(vb[j]);
+        og[j] = na * softplus(va[j] + dt);
+        h = h + 1 == H ? 0 : h + 1;
+      }
+      st8(beta + i0, ob);
+      st8(g + i0, og);
+    } else {
+      for (int i = i0; i < n && i < i0 + 8; ++i) {
+        float na, dt;
+        head_consts(alog, dtb, s_na, s_dt, h, na, dt);
+        beta[i] = sigmoid(ld(b, i));
+        g[i] = na * softplus(ld(a, i) + dt);
+        h = h + 1 == H ? 0 : h + 1;
+      }
+    }
   }
 }
 
@@ -95,22 +168,46 @@ __global__ void __launch_bounds__(kThreads) gates_bwd_kernel(const T* __restrict
                                                              const float* __restrict__ dbeta,
                                                              const float* __restrict__ dg, T* __restrict__ db,
                                                              T* __restrict__ da, long long rows, int H, long long rpb,
-                                                             float* __restrict__ pa, float* __restrict__ pd) {
+                                                             float* __restrict__ pa, float* __restrict__ pd, bool vec) {
   __shared__ float s_na[kSmemHeads], s_dt[kSmemHeads];
   __shared__ float s_sa[kThreads], s_sd[kThreads];
   stage_heads(alog, dtb, H, s_na, s_dt);
   const bool sums = pa != nullptr;
-  if (!sums) {  // plain grid-stride elementwise pass
-    const long long n = rows * H, stride = (long long)gridDim.x * blockDim.x;
-    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
-      const int h = (int)(i % H);
-      float na, dt;
-      head_consts(alog, dtb, s_na, s_dt, h, na, dt);
-      const float sb = sigmoid(ld(b, i));
-      db[i] = cvt<T>((dbeta ? dbeta[i] : 0.f) * sb * (1.f - sb));
-      const float x = ld(a, i) + dt;
-      const float sx = x > kThreshold ? 1.f : sigmoid(x);
-      da[i] = cvt<T>((dg ? dg[i] : 0.f) * na * sx);
+  if (!sums) {  // plain elementwise pass in groups of 8 (as the forward)
+    const int n = (int)(rows * H), groups = (n + 7) / 8, stride = gridDim.x * blockDim.x;
+    for (int gi = blockIdx.x * blockDim.x + threadIdx.x; gi < groups; gi += stride) {
+      const int i0 = 8 * gi;
+      int h = i0 % H;
+      if (vec && i0 + 8 <= n) {
+        float vb[8], va[8], vdb[8], vdg[8], ob[8], oa[8];
+        ld8(b + i0, vb);
+        ld8(a + i0, va);
+        ld8f(dbeta ? dbeta + i0 : nullptr, vdb);
+        ld8f(dg ? dg + i0 : nullptr, vdg);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          float na, dt;
+          head_consts(alog, dtb, s_na, s_dt, h, na, dt);
+          const float sb = sigmoid(vb[j]);
+          ob[j] = vdb[j] * sb * (1.f - sb);
+          const float x = va[j] + dt;
+          oa[j] = vdg[j] * na * (x > kThreshold ? 1.f : sigmoid(x));
+          h = h + 1 == H ? 0 : h + 1;
+        }
+        st8(db + i0, ob);
+        st8(da + i0, oa);
+      } else {
+        for (int i = i0; i < n && i < i0 + 8; ++i) {
+          float na, dt;
+          head_consts(alog, dtb, s_na, s_dt, h, na, dt);
+          const float sb = sigmoid(ld(b, i));
+          db[i] = cvt<T>((dbeta ? dbeta[i] : 0.f) * sb * (1.f - sb));
+          const float x = ld(a, i) + dt;
+          const float sx = x > kThreshold ? 1.f : sigmoid(x);
+          da[i] = cvt<T>((dg ? dg[i] : 0.f) * na * sx);
+          h = h + 1 == H ? 0 : h + 1;
+        }
+      }
     }
     return;
   }
@@ -169,7 +266,7 @@ __global__ void __launch_bounds__(kThreads) gates_sum_kernel(const float* __rest
   if (ddtb) ddtb[h] = cvt<TW>(td);
 }
 
-int blocks_for(long long n) {
+int blocks_for(long long n) {  // n = work items (groups of 8 elements)
   int sms = 148;
   int dev = 0;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -187,15 +284,17 @@ void partition(long long rows, long long& rpb, int& P) {
 }
 
 bool aligned4(const void* p) { return p == nullptr || (reinterpret_cast<uintptr_t>(p) & 3u) == 0; }
+bool aligned16(const void* p) { return p == nullptr || (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 int status_of(cudaError_t e) { return e == cudaSuccess ? GD_OK : GD_ERR_LAUNCH; }
 
 template <typename T, typename TW>
 int fwd_t(const void* b, const void* a, const void* alog, const void* dtb, float* beta, float* g, long long n, int H,
           cudaStream_t st) {
-  gates_fwd_kernel<T, TW><<<blocks_for(n), kThreads, 0, st>>>(
+  const bool vec = aligned16(b) && aligned16(a) && aligned16(beta) && aligned16(g);
+  gates_fwd_kernel<T, TW><<<blocks_for((n + 7) / 8), kThreads, 0, st>>>(
       static_cast<const T*>(b), static_cast<const T*>(a), static_cast<const TW*>(alog), static_cast<const TW*>(dtb),
-      beta, g, n, H);
+      beta, g, (int)n, H, vec);
   return status_of(cudaGetLastError());
 }
 
@@ -204,9 +303,11 @@ int bwd_t(const void* b, const void* a, const void* alog, const void* dtb, const
           void* db, void* da, void* dalog, void* ddtb, long long n, int H, void* ws, cudaStream_t st) {
   const long long rows = n / H;
   if (dalog == nullptr && ddtb == nullptr) {
-    gates_bwd_kernel<T, TW><<<blocks_for(n), kThreads, 0, st>>>(
+    const bool vec = aligned16(b) && aligned16(a) && aligned16(dbeta) && aligned16(dg) && aligned16(db) &&
+                     aligned16(da);
+    gates_bwd_kernel<T, TW><<<blocks_for((n + 7) / 8), kThreads, 0, st>>>(
         static_cast<const T*>(b), static_cast<const T*>(a), static_cast<const TW*>(alog), static_cast<const TW*>(dtb),
-        dbeta, dg, static_cast<T*>(db), static_cast<T*>(da), rows, H, 0, nullptr, nullptr);
+        dbeta, dg, static_cast<T*>(db), static_cast<T*>(da), rows, H, 0, nullptr, nullptr, vec);
     return status_of(cudaGetLastError());
   }
   long long rpb;
@@ -216,7 +317,7 @@ int bwd_t(const void* b, const void* a, const void* alog, const void* dtb, const
   float* pd = pa + (size_t)P * H;
   gates_bwd_kernel<T, TW><<<P, kThreads, 0, st>>>(
       static_cast<const T*>(b), static_cast<const T*>(a), static_cast<const TW*>(alog), static_cast<const TW*>(dtb),
-      dbeta, dg, static_cast<T*>(db), static_cast<T*>(da), rows, H, rpb, pa, pd);
+      dbeta, dg, static_cast<T*>(db), static_cast<T*>(da), rows, H, rpb, pa, pd, false);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return GD_ERR_LAUNCH;
   gates_sum_kernel<TW><<<(H + kThreads - 1) / kThreads, kThreads, 0, st>>>(pa, pd, P, H, static_cast<TW*>(dalog),
