@@ -10,8 +10,12 @@
 // the 16 partial sums of <S_c, dS_{c+1}> (from the forward recompute's fp32 S_c^T).
 //
 // Warp specialisation as in the forward pass: 16 epilogue warps reading the M = 64 products whole-warp (thread t of
-// warp w: local value column 16 (w % 4) + t % 16, 8 tokens and 16 key rows of dS held in registers) and one MMA /
-// bulk-copy thread; all hand-offs are mbarriers. Precision: dS and K~ split into bf16 hi + lo (three products), gamma Q split, the rest bf16.
+// warp w: local value column 16 (w % 4) + t % 16, 8 tokens and 16 key rows of dS held in registers; they also write
+// the per-chunk images to global memory straight from registers), one MMA thread and one loader thread (every refill
+// waits on the product that frees its buffer, which is also the product whose next phase needs that refill); all
+// hand-offs are mbarriers. Per chunk the MMA thread issues only: K~ dS (chain) -> -W^T dVn (chain, added onto the
+// chunk's (gamma Q)^T dO) -> the next chunk's dS-independent products. Precision: dS and K~ split into bf16 hi + lo
+// (three products), gamma Q split, the rest bf16.
 #include "gd_common.cuh"
 #include "gd_layout.cuh"
 
@@ -38,7 +42,7 @@ struct BwdStateSmem {
 };
 
 template <typename T, int DK, int DV>
-__global__ void __launch_bounds__(544) bwd_state_kernel(const T* __restrict__ d_o, const float* __restrict__ dsT,
+__global__ void __launch_bounds__(576) bwd_state_kernel(const T* __restrict__ d_o, const float* __restrict__ dsT,
                                                         float* __restrict__ ds0, Layout lay, int flags,
                                                         unsigned char* __restrict__ ws) {
   static_assert(DV == 128 && DK == 128, "64 value columns per CTA on TMEM lanes 0-15 of each quadrant");
@@ -55,7 +59,7 @@ __global__ void __launch_bounds__(544) bwd_state_kernel(const T* __restrict__ d_
   uint64_t* pre_full = bars + 3;    // M, gamma Q loaded
   uint64_t* a_full = bars + 4;      // (M^T dO)^T and ((gamma Q)^T dO)^T done
   uint64_t* b_full = bars + 5;      // (K~ dS)^T done
-  uint64_t* d_full = bars + 6;      // (W^T dVn)^T done
+  uint64_t* d_full = bars + 6;      // -(W^T dVn)^T added to ((gamma Q)^T dO)^T
   uint64_t* ds_ready = bars + 7;    // 16 warps: dS tiles written
   uint64_t* do_full = bars + 8;     // 16 warps: dO tile written
   uint64_t* dvn_full = bars + 9;    // 16 warps: dVn tile written, G read
@@ -76,8 +80,9 @@ __global__ void __launch_bounds__(544) bwd_state_kernel(const T* __restrict__ d_
   __syncthreads();
   tc_fence_after();
   const uint32_t tm = *tslot;
-  // TMEM: (M^T dO)^T at tm, (K~ dS)^T at tm + 64, ((gamma Q)^T dO)^T at tm + 128 + 128 (n & 1), (W^T dVn)^T at tm + 384
-  const uint32_t tA = tm, tB = tm + 64, tD = tm + 384;
+  // TMEM: (M^T dO)^T at tm; (K~ dS)^T at tm + 64 as two 64-column halves (dS hi K~ hi + dS lo K~ hi | dS hi K~ lo)
+  // whose sum is the product; ((gamma Q)^T dO - W^T dVn)^T at tm + 192 + 128 (n & 1)
+  const uint32_t tA = tm, tB = tm + 64;
   bool ok = true;
 
   auto load_crit = [&](int c, int s) {
@@ -96,92 +101,98 @@ __global__ void __launch_bounds__(544) bwd_state_kernel(const T* __restrict__ d_
     bulk_g2s(smem + S::gq, ws + lay.gq + (row0 + c) * lay.qk_bytes(), (uint32_t)lay.qk_bytes(), pre_full);
   };
   const Tile tDO{smem_u32(smem + S::dO), DVH};
-  // chunk c's dO image for the per-chunk kernel: this CTA's columns of each 8-row block (1 KB pieces of the
-  // [64 x DV] image); its reads finish before the products that precede the tile's reuse
-  auto copy_do = [&](int c) {
-    unsigned char* dst = ws + lay.doi + (row0 + c) * lay.vi_bytes();
-#pragma unroll 1
-    for (int rb = 0; rb < 8; ++rb)
-      bulk_s2g(dst + ((size_t)rb * (DV / 8) + vbase / 8) * 128, smem + S::dO + rb * (DVH / 8) * 128, DVH / 8 * 128);
-    bulk_commit();
-    bulk_wait_read0();
-  };
   // (M^T dO)^T = dO^T M [DVH x 64]; ((gamma Q)^T dO)^T = dO^T (gamma Q) [DVH x DK], gamma Q split
   auto issue_pre = [&](int n) {
     mma_tiles(tA, DVH, 64, 64, tDO, false, 0, 0, Tile{smem_u32(smem + S::m), 64}, true, 0, false);
-    const uint32_t tC = tm + 128 + 128 * (n & 1);
+    const uint32_t tC = tm + 192 + 128 * (n & 1);
     mma_tiles(tC, DVH, DK, 64, tDO, false, 0, 0, Tile{smem_u32(smem + S::gq), DK}, true, 0, false);
     mma_tiles(tC, DVH, DK, 64, tDO, false, 0, 0, Tile{smem_u32(smem + S::gq + 64 * DK * 2), DK}, true, 0, true);
     mma_commit(a_full);
   };
 
   if (warp == 16) {
-    // ---------------- MMA and bulk-copy issuer (one thread); iteration n handles chunk c = NT - 1 - n
+    // ---------------- MMA issuer (one thread); iteration n handles chunk c = NT - 1 - n
     if (lane == 0) {
-      load_crit(NT - 1, 0);
-      if (NT > 1) load_crit(NT - 2, 1);
-      load_wt(NT - 1);
-      load_pre(NT - 1);
       ok = mbar_wait(pre_full, 0, err, 30) && mbar_wait(do_full, 0, err, 31);
       if (ok) {
         tc_fence_after();
-        copy_do(NT - 1);
         issue_pre(0);
       }
       for (int n = 0; n < NT && ok; ++n) {
         const int c = NT - 1 - n, s = n & 1;
-        const size_t cidx = row0 + c;
         unsigned char* st = smem + S::crit0 + s * S::crit_bytes;
         ok = mbar_wait(crit_full + s, (n >> 1) & 1, err, 32) && mbar_wait(ds_ready, n & 1, err, 33);
         if (!ok) break;
+        GD_TRACE_ONE(ws, lay, 1024 + 8 * n + 0);
         tc_fence_after();
-        // this CTA's rows of the dS_{c+1}^T images (hi, lo) for the per-chunk kernel
-        unsigned char* dsi = ws + lay.dsi + cidx * 2 * lay.si_bytes() + (size_t)vbase * DK * 2;
-        bulk_s2g(dsi, smem + S::dsh, DVH * DK * 2);
-        bulk_s2g(dsi + lay.si_bytes(), smem + S::dsl, DVH * DK * 2);
-        bulk_commit();
-        if (c > 0)  // the next chunk's fp32 state, for the epilogue's <S, dS> partial sums
-          asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(ws + lay.scf + (cidx - 1) * lay.s_bytes()),
-                       "r"((uint32_t)lay.s_bytes())
-                       : "memory");
-        // * (K~ dS)^T = dS^T K~^T [DVH x 64]: hi hi + hi lo + lo hi
-        const Tile tKh{smem_u32(st + S::c_kt), DK}, tKl{smem_u32(st + S::c_kt + 64 * DK * 2), DK};
+        // * (K~ dS)^T = dS^T K~^T [DVH x 64]: dS hi against [K~ hi; K~ lo] (the two images are adjacent: one N = 128
+        // operand) into both halves, then dS lo K~ hi onto the first half
+        const Tile tKh{smem_u32(st + S::c_kt), DK};
         const Tile tDh{smem_u32(smem + S::dsh), DK}, tDl{smem_u32(smem + S::dsl), DK};
-        mma_tiles(tB, DVH, 64, DK, tDh, true, 0, 0, tKh, false, 0, false);
-        mma_tiles(tB, DVH, 64, DK, tDh, true, 0, 0, tKl, false, 0, true);
+        mma_tiles(tB, DVH, 128, DK, tDh, true, 0, 0, tKh, false, 0, false);
         mma_tiles(tB, DVH, 64, DK, tDl, true, 0, 0, tKh, false, 0, true);
         mma_commit(b_full);
-        // the dS-independent inputs of the next chunk can replace this chunk's once its products are done
-        ok = mbar_wait(a_full, n & 1, err, 34);
-        if (!ok) break;
-        if (c > 0) load_pre(c - 1);
+        GD_TRACE_ONE(ws, lay, 1024 + 8 * n + 1);
         ok = mbar_wait(dvn_full, n & 1, err, 35) && mbar_wait(wt_full, n & 1, err, 36);
         if (!ok) break;
+        GD_TRACE_ONE(ws, lay, 1024 + 8 * n + 3);
         tc_fence_after();
-        bulk_s2g(ws + lay.dvni + cidx * lay.vn_bytes() + (size_t)vbase * 64 * 2, smem + S::dvh, DVH * 64 * 2);
-        bulk_commit();
-        bulk_wait_read0();  // the dS and dVn tiles may be rewritten once d_full fires
-        // * (W^T dVn)^T = dVn^T W [DVH x DK]
-        mma_tiles(tD, DVH, DK, 64, Tile{smem_u32(smem + S::dvh), 64}, true, 0, 0, Tile{smem_u32(smem + S::wt), 64},
-                  false, 0, false);
+        // * -(W^T dVn)^T = -dVn^T W [DVH x DK], onto this chunk's ((gamma Q)^T dO)^T
+        mma_tiles(tm + 192 + 128 * (n & 1), DVH, DK, 64, Tile{smem_u32(smem + S::dvh), 64}, true, 0, 0,
+                  Tile{smem_u32(smem + S::wt), 64}, false, 0, true, true);
         mma_commit(d_full);
-        if (c > 0) {
-          // refill this K~ stage with chunk c - 2 once (K~ dS)^T, its reader, is done
-          ok = mbar_wait(b_full, n & 1, err, 37);
-          if (!ok) break;
-          if (c > 1) load_crit(c - 2, s);
-          ok = mbar_wait(d_full, n & 1, err, 38);
-          if (!ok) break;
-          load_wt(c - 1);
-          // next chunk's dS-independent products
+        GD_TRACE_ONE(ws, lay, 1024 + 8 * n + 4);
+        if (c > 0) {  // the next chunk's dS-independent products, under this chunk's dS update
           ok = mbar_wait(pre_full, (n + 1) & 1, err, 39) && mbar_wait(do_full, (n + 1) & 1, err, 40);
           if (!ok) break;
           tc_fence_after();
-          copy_do(c - 1);
           issue_pre(n + 1);
         }
+        GD_TRACE_ONE(ws, lay, 1024 + 8 * n + 5);
       }
-      bulk_wait0();
+    }
+    __syncwarp();
+  } else if (warp == 17) {
+    // ---------------- loader (one thread). Each refill waits for the product that frees its buffer; that product's
+    // barrier cannot move on a further phase before this refill (its next phase needs the refilled data).
+    if (lane == 0) {
+      int nl = 0, nw = 0, np = 0;  // crit stages, W^T and pre loads issued
+      load_crit(NT - 1, 0);
+      ++nl;
+      if (NT > 1) {
+        load_crit(NT - 2, 1);
+        ++nl;
+      }
+      load_wt(NT - 1);
+      load_pre(NT - 1);
+      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(ws + lay.scf + (row0 + NT - 1) * lay.s_bytes()),
+                   "r"((uint32_t)lay.s_bytes())
+                   : "memory");
+      ++nw;
+      ++np;
+      for (int n = 0; n + 1 < NT && ok; ++n) {
+        const int c = NT - 1 - n;
+        ok = mbar_wait(a_full, n & 1, err, 34);  // chunk c's dS-independent products have read M and gamma Q
+        if (!ok) break;
+        // the next chunk's fp32 state into L2, for the epilogue's <S, dS> partial sums
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(ws + lay.scf + (row0 + c - 1) * lay.s_bytes()),
+                     "r"((uint32_t)lay.s_bytes())
+                     : "memory");
+        load_pre(c - 1);
+        ++np;
+        ok = mbar_wait(d_full, n & 1, err, 38);  // -W^T dVn of chunk c has read W^T; K~ dS read stage n & 1
+        if (!ok) break;
+        load_wt(c - 1);
+        ++nw;
+        if (c > 1) {
+          load_crit(c - 2, n & 1);
+          ++nl;
+        }
+      }
+      // every copy issued here lands before the CTA may exit, also after a failed wait
+      for (int l = nl > 2 ? nl - 2 : 0; l < nl; ++l) mbar_wait(crit_full + (l & 1), (l >> 1) & 1, err, 44);
+      mbar_wait(wt_full, (nw - 1) & 1, err, 45);
+      mbar_wait(pre_full, (np - 1) & 1, err, 46);
     }
     __syncwarp();
   } else {
@@ -192,11 +203,16 @@ __global__ void __launch_bounds__(544) bwd_state_kernel(const T* __restrict__ d_
     const int tk = 16 * quarter + 8 * (lane >> 4);
     const int dk0 = 32 * quarter + 16 * (lane >> 4);
     float Dr[16];  // dS[dk0 + j][v]
-    auto write_ds = [&]() {
+    // the dS tiles for the next K~ dS, then (after the hand-off: the proxy fence would wait for global stores in
+    // flight) this CTA's rows of chunk ci's dS_{ci+1}^T images (hi, lo) for the per-chunk kernel, from registers
+    auto write_ds = [&](int ci) {
 #pragma unroll
       for (int q8 = 0; q8 < 2; ++q8) store8_split(smem + S::dsh, smem + S::dsl, vl_, dk0 + 8 * q8, DK, Dr + 8 * q8);
       fence_async_smem();
       mbar_arrive_warp(ds_ready);
+      unsigned char* gh = ws + lay.dsi + (row0 + ci) * 2 * lay.si_bytes() + (size_t)vbase * DK * 2;
+#pragma unroll
+      for (int q8 = 0; q8 < 2; ++q8) store8_split(gh, gh + lay.si_bytes(), vl_, dk0 + 8 * q8, DK, Dr + 8 * q8);
     };
     // a chunk's dO tile (this CTA's 64 columns): 512 16-byte pieces, one per thread, eight consecutive threads per
     // 128-byte core matrix; fetched raw into registers early, written to the tile once the tile's readers are done
@@ -210,20 +226,21 @@ __global__ void __launch_bounds__(544) bwd_state_kernel(const T* __restrict__ d_
         dox.zero();
       }
     };
-    auto put_do = [&]() {
+    auto put_do = [&](int c) {  // chunk c's dO: the tile, then this CTA's columns of the [64 x DV] image
       float x[8];
       dox.to_f32(x);
       store8_bf16(smem + S::dO, 8 * prb + prl, 8 * pcb, DVH, x);
       fence_async_smem();
       mbar_arrive_warp(do_full);
+      store8_bf16(ws + lay.doi + (row0 + c) * lay.vi_bytes(), 8 * prb + prl, vbase + 8 * pcb, DV, x);
     };
     {
       const float* p = dsT ? dsT + ((size_t)b * lay.H + h) * DK * DV : nullptr;
 #pragma unroll
       for (int j = 0; j < 16; ++j) Dr[j] = p ? p[(size_t)(dk0 + j) * DV + v] : 0.f;
-      write_ds();
+      write_ds(NT - 1);
       fetch_do(NT - 1);
-      put_do();
+      put_do(NT - 1);
     }
     for (int n = 0; n < NT; ++n) {
       const int c = NT - 1 - n, s = n & 1;
@@ -237,27 +254,29 @@ __global__ void __launch_bounds__(544) bwd_state_kernel(const T* __restrict__ d_
       GD_TRACE_AT(ws, lay, 8 * n + 1);
       const float gl = __expf(sG[63]);
       {
-        float a[8], bb[8];
-        tmem_ld8hx2(tmem_lane_addr(tA, warp, 16 * quarter), a, tmem_lane_addr(tB, warp, 16 * quarter), bb);
+        float a[8], bb[8], b2[8];
+        tmem_ld8hx3(tmem_lane_addr(tA, warp, 16 * quarter), a, tmem_lane_addr(tB, warp, 16 * quarter), bb,
+                    tmem_lane_addr(tB + 64, warp, 16 * quarter), b2);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) split_bf16(a[j] + bb[j], a[j], bb[j]);  // in place: a = hi, bb = lo
+        for (int j = 0; j < 8; ++j) split_bf16(a[j] + (bb[j] + b2[j]), a[j], bb[j]);  // in place: a = hi, bb = lo
         store8_bf16(smem + S::dvh, vl_, tk, 64, a);
-        store8_bf16(ws + lay.dvni + cidx * lay.vn_bytes() + DV * 64 * 2, v, tk, 64, bb);  // low half: straight to HBM
         tc_fence_before();
         fence_async_smem();
         mbar_arrive_warp(dvn_full);
+        store8_bf16(ws + lay.dvni + cidx * lay.vn_bytes(), v, tk, 64, a);  // the image's halves straight from registers
+        store8_bf16(ws + lay.dvni + cidx * lay.vn_bytes() + DV * 64 * 2, v, tk, 64, bb);
       }
       GD_TRACE_AT(ws, lay, 8 * n + 2);
+      // the next chunk's dO tile (this chunk's dO products are done: a_full), published before any new load is in
+      // flight
+      if (c > 0) put_do(c - 1);
       // partial <S_c, dS_{c+1}> of this thread's 16 entries (fp32 S_c from the forward recompute, prefetched into L2 a
-      // chunk ahead; lanes read adjacent 16-byte pieces): loads in flight through the wait for (W^T dVn)^T
+      // chunk ahead; lanes read adjacent 16-byte pieces): loads in flight through the wait for -(W^T dVn)^T
       const float4* sc = reinterpret_cast<const float4*>(ws + lay.scf + cidx * lay.s_bytes()) +
                          (size_t)(quarter * 8 + 4 * (lane >> 4)) * DV + v;
       float4 sx[4];
 #pragma unroll
       for (int q4 = 0; q4 < 4; ++q4) sx[q4] = __ldg(sc + (size_t)q4 * DV);
-      // the next chunk's dO tile (this chunk's dO products are done: a_full; its image went out before they were
-      // issued)
-      if (c > 0) put_do();
       // * dS_c = exp(G_last) dS_{c+1} + (gamma Q)^T dO - W^T dVn
       GD_TRACE_AT(ws, lay, 8 * n + 3);
       if (!mbar_wait(d_full, n & 1, err, 43)) { ok = false; break; }
@@ -268,18 +287,17 @@ __global__ void __launch_bounds__(544) bwd_state_kernel(const T* __restrict__ d_
       for (int q4 = 0; q4 < 4; ++q4)
         sacc = fmaf(sx[q4].x, Dr[4 * q4], fmaf(sx[q4].y, Dr[4 * q4 + 1], fmaf(sx[q4].z, Dr[4 * q4 + 2],
                                                                               fmaf(sx[q4].w, Dr[4 * q4 + 3], sacc))));
-      sacc = warp_sum(sacc);
-      if (lane == 0) reinterpret_cast<float*>(ws + lay.sl + cidx * lay.sl_bytes())[16 * half + warp] = sacc;
       {
-        const uint32_t tC = tm + 128 + 128 * (n & 1);
-        float cc[16], dd[16];
-        tmem_ld16h(tmem_lane_addr(tC, warp, 32 * quarter), cc);
-        tmem_ld16h(tmem_lane_addr(tD, warp, 32 * quarter), dd);
+        float cc[16];
+        tmem_ld16h(tmem_lane_addr(tm + 192 + 128 * (n & 1), warp, 32 * quarter), cc);
 #pragma unroll
-        for (int j = 0; j < 16; ++j) Dr[j] = fmaf(gl, Dr[j], cc[j] - dd[j]);
+        for (int j = 0; j < 16; ++j) Dr[j] = fmaf(gl, Dr[j], cc[j]);
         tc_fence_before();
       }
-      if (c > 0) write_ds();
+      if (c > 0) write_ds(c - 1);
+      // the warp's partial sum goes out after the hand-off (the proxy fence there would wait for the store)
+      sacc = warp_sum(sacc);
+      if (lane == 0) reinterpret_cast<float*>(ws + lay.sl + cidx * lay.sl_bytes())[16 * half + warp] = sacc;
       GD_TRACE_AT(ws, lay, 8 * n + 5);
     }
     if (ok && ds0 != nullptr) {
@@ -305,7 +323,7 @@ cudaError_t launch_bwd_state(const void* d_o, const float* dsT, float* ds0, cons
   cudaError_t e = set_smem_once(kern, S::total, attr_done);
   if (e != cudaSuccess) return e;
   dim3 grid(lay.H * 2, lay.B);
-  kern<<<grid, 544, S::total, st>>>(static_cast<const T*>(d_o), dsT, ds0, lay, flags, ws);
+  kern<<<grid, 576, S::total, st>>>(static_cast<const T*>(d_o), dsT, ds0, lay, flags, ws);
   return cudaGetLastError();
 }
 

@@ -259,9 +259,10 @@ struct Tile {
 //   x_rows_m: X's tile rows index M (K-major A); otherwise the tile is X^T (rows index K: MN-major A).
 //   y_rows_k: Y's tile rows index K (MN-major B); otherwise the tile is Y^T (rows index N: K-major B).
 // (m0, n0, k0) select a sub-block of the tiles (multiples of 8, 8, 16). Issued by one thread.
+// negate_x: D (+)= -X . Y (the instruction descriptor's negate-A bit).
 __device__ __forceinline__ void mma_tiles(uint32_t d_tmem, int M, int N, int K, Tile x, bool x_rows_m, int m0, int k0,
-                                          Tile y, bool y_rows_k, int n0, bool accumulate) {
-  const uint32_t idesc = idesc_bf16(M, N, !x_rows_m, y_rows_k);
+                                          Tile y, bool y_rows_k, int n0, bool accumulate, bool negate_x = false) {
+  const uint32_t idesc = idesc_bf16(M, N, !x_rows_m, y_rows_k) | (negate_x ? (1u << 13) : 0u);
   uint32_t xa, x_lbo, x_sbo, x_step, ya, y_lbo, y_sbo, y_step;
   if (x_rows_m) {  // K-major: K groups adjacent (128 B), M groups one row block apart
     xa = x.addr + (m0 / 8) * x.rowblk_bytes() + (k0 / 8) * 128;
@@ -380,6 +381,28 @@ __device__ __forceinline__ void tmem_ld8hx2(uint32_t a0, float (&v0)[8], uint32_
   for (int i = 0; i < 8; ++i) {
     v0[i] = __uint_as_float(r[i]);
     v1[i] = __uint_as_float(r[8 + i]);
+  }
+}
+
+// Three such loads under one wait.
+__device__ __forceinline__ void tmem_ld8hx3(uint32_t a0, float (&v0)[8], uint32_t a1, float (&v1)[8], uint32_t a2,
+                                            float (&v2)[8]) {
+  uint32_t r[24];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.16x32bx2.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%24], 8;\n\t"
+      "tcgen05.ld.sync.aligned.16x32bx2.x8.b32 {%8,%9,%10,%11,%12,%13,%14,%15}, [%25], 8;\n\t"
+      "tcgen05.ld.sync.aligned.16x32bx2.x8.b32 {%16,%17,%18,%19,%20,%21,%22,%23}, [%26], 8;\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23])
+      : "r"(a0), "r"(a1), "r"(a2)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    v0[i] = __uint_as_float(r[i]);
+    v1[i] = __uint_as_float(r[8 + i]);
+    v2[i] = __uint_as_float(r[16 + i]);
   }
 }
 
