@@ -144,7 +144,9 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
                                                            const float* __restrict__ beta, T* __restrict__ dq,
                                                            T* __restrict__ dk, T* __restrict__ dv,
                                                            float* __restrict__ dg, float* __restrict__ dbeta,
-                                                           Layout lay, int flags, unsigned char* __restrict__ ws) {
+                                                           Layout lay, int flags, unsigned char* __restrict__ ws,
+                                                           const __grid_constant__ CUtensorMap tm_dq,
+                                                           const __grid_constant__ CUtensorMap tm_dk) {
   static_assert(DK == 128 && DV == 128, "the head dimension maps onto the 128 TMEM lanes");
   using S = ChunkSmem<DK, DV>;
   extern __shared__ __align__(1024) unsigned char smem[];
@@ -436,19 +438,18 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
       if (!(ok = epi_all(ok))) break;
       tc_fence_after();
       GD_TRACE_AT(ws, lay, 32 * n + 0);
+      float dvr[16];  // dV rows, stored after the e1 hand-off (its proxy fence would wait for global stores in flight)
       {
-        float y[16], x[16];
-        tmem_ld16(tmem_lane_addr(B3, warp, tok0), y);  // Y^T: v . Y, and dV = diag(beta) Y
+        float x[16];
+        tmem_ld16(tmem_lane_addr(B3, warp, tok0), dvr);  // Y^T: v . Y, and dV = diag(beta) Y
         row16<false>(smem + S::vt, nullptr, dcol, tok0, x);
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
-          x[j] *= y[j];
-          y[j] *= sB[tok0 + j];
+          x[j] *= dvr[j];
+          dvr[j] *= sB[tok0 + j];
         }
         const float s = warp_reduce_scatter16(x);
         if (lane < 16) P(P_VY, qd, tok0 + lane) = s;
-        store_token_rows<T>(y, dv + ((size_t)it.b * lay.T * lay.H + it.h) * DV, (size_t)lay.H * DV, t0 + tok0, lay.T,
-                            32 * qd + 8 * (lane >> 3));
       }
       {
         float y[16], x[8];
@@ -478,6 +479,8 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
         tc_fence_before();
         fence_async_smem();
         mbar_arrive_warp(e1_done);
+        store_token_rows<T>(dvr, dv + ((size_t)it.b * lay.T * lay.H + it.h) * DV, (size_t)lay.H * DV, t0 + tok0,
+                            lay.T, 32 * qd + 8 * (lane >> 3));
         row16<true>(qh, ql, dcol, tok0, x);
 #pragma unroll
         for (int j = 0; j < 16; ++j) av[j] *= x[j];
@@ -702,6 +705,7 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
         T* dq0 = dq + ((size_t)it.b * lay.T * lay.HK + it.hk) * DK;
         T* dk0 = dk + ((size_t)it.b * lay.T * lay.HK + it.hk) * DK;
         const int d0 = 32 * qd + 8 * (lane >> 3);
+        float xk[16];
         if (norm) {
           row16<true>(qh, ql, dcol, tok0, x);
 #pragma unroll
@@ -711,25 +715,45 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
             const float dot = d4.x + d4.y + d4.z + d4.w;
             x[j] = qscale * sRq[i] * (dQ[j] - x[j] * inv_qscale * dot);
           }
-        } else {
-#pragma unroll
-          for (int j = 0; j < 16; ++j) x[j] = qscale * dQ[j];
-        }
-        store_token_rows<T>(x, dq0, (size_t)lay.HK * DK, t0 + tok0, lay.T, d0);
-        if (norm) {
-          row16<true>(kh, kl, dcol, tok0, x);
+          row16<true>(kh, kl, dcol, tok0, xk);
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             const int i = tok0 + j;
             const float4 d4 = *reinterpret_cast<const float4*>(dotk + 4 * i);
             const float dot = d4.x + d4.y + d4.z + d4.w;
-            x[j] = sRk[i] * (dK[j] - x[j] * dot);
+            xk[j] = sRk[i] * (dK[j] - xk[j] * dot);
           }
         } else {
 #pragma unroll
-          for (int j = 0; j < 16; ++j) x[j] = dK[j];
+          for (int j = 0; j < 16; ++j) {
+            x[j] = qscale * dQ[j];
+            xk[j] = dK[j];
+          }
         }
-        store_token_rows<T>(x, dk0, (size_t)lay.HK * DK, t0 + tok0, lay.T, d0);
+        if constexpr (sizeof(T) == 2) {
+          // dq, dk tiles as row-major [64 tokens][DK] in the q^T / k^T image buffers (every thread is done reading
+          // them), then one tensor store each (rows past T are not written); the images' next fill waits for the
+          // stores' reads (qk_free: warp 0 arrives after them)
+          epi_sync();
+          T* sq = reinterpret_cast<T*>(smem + S::qk);
+          T* sk = reinterpret_cast<T*>(smem + S::qk + DK * 64 * 2);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            sq[(tok0 + j) * DK + dcol] = cvt_out<T>(x[j]);
+            sk[(tok0 + j) * DK + dcol] = cvt_out<T>(xk[j]);
+          }
+          fence_async_smem();
+          epi_sync();
+          if (tid == 0) {
+            tma_store_4d(&tm_dq, 0, it.hk, t0, it.b, sq);
+            tma_store_4d(&tm_dk, 0, it.hk, t0, it.b, sk);
+            bulk_commit();
+            bulk_wait_read0();
+          }
+        } else {
+          store_token_rows<T>(x, dq0, (size_t)lay.HK * DK, t0 + tok0, lay.T, d0);
+          store_token_rows<T>(xk, dk0, (size_t)lay.HK * DK, t0 + tok0, lay.T, d0);
+        }
         mbar_arrive_warp(qk_free);  // the q / k images may be replaced by the next item's
 #pragma unroll
         for (int j = 0; j < 16; ++j) dQ[j] = dK[j] = 0.f;
@@ -739,6 +763,7 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
       mbar_arrive_warp(epi_done + (n & 1));
       GD_TRACE_AT(ws, lay, 32 * n + 23);
     }
+    if (tid == 0) bulk_wait0();  // the tensor stores of dq / dk complete before the CTA ends
   }
   tc_fence_before();
   __syncthreads();
@@ -767,8 +792,12 @@ cudaError_t launch_bwd_chunk(const void* q, const void* k, const void* v, const 
     return e;
   const int ngroups = lay.B * lay.HK * lay.NT;
   const int grid = ngroups < sms[dev] ? ngroups : sms[dev];
+  CUtensorMap mdq{}, mdk{};  // 16-bit outputs: dq / dk tiles leave by tensor store (fp32 rows by plain stores)
+  if (sizeof(T) == 2 && (!rows_map(&mdq, dq, map_dtype<T>(), lay.B, lay.T, lay.HK, DK) ||
+                         !rows_map(&mdk, dk, map_dtype<T>(), lay.B, lay.T, lay.HK, DK)))
+    return cudaErrorInvalidValue;
   kern<<<grid, 576, S::total, st>>>(static_cast<const T*>(q), static_cast<const T*>(k), beta, static_cast<T*>(dq),
-                                    static_cast<T*>(dk), static_cast<T*>(dv), dg, dbeta, lay, flags, ws);
+                                    static_cast<T*>(dk), static_cast<T*>(dv), dg, dbeta, lay, flags, ws, mdq, mdk);
   return cudaGetLastError();
 }
 

@@ -728,39 +728,6 @@ __global__ void __launch_bounds__(576) state_kernel(const float* __restrict__ s0
 // ------------------------------------------------------------------------------------------------------------------
 // launchers
 
-namespace {
-
-using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-// cuTensorMapEncodeTiled from the driver (a host-only function: no device work, usable during stream capture)
-EncodeTiled encode_tiled() {
-  static EncodeTiled fn = [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult res{};
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &res) != cudaSuccess ||
-        res != cudaDriverEntryPointSuccess)
-      p = nullptr;
-    return reinterpret_cast<EncodeTiled>(p);
-  }();
-  return fn;
-}
-
-// [B, T, heads, D] 16-bit rows as a 4-D tensor (D innermost); box = one head's D columns x 64 tokens
-bool rows_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int B, int T, int heads, int D) {
-  EncodeTiled enc = encode_tiled();
-  if (enc == nullptr) return false;
-  const cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)heads, (cuuint64_t)T, (cuuint64_t)B};
-  const cuuint64_t strides[3] = {(cuuint64_t)D * 2, (cuuint64_t)heads * D * 2, (cuuint64_t)T * heads * D * 2};
-  const cuuint32_t box[4] = {(cuuint32_t)D, 1, 64, 1};
-  const cuuint32_t estr[4] = {1, 1, 1, 1};
-  return enc(m, dt, 4, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-             CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
-}  // namespace
 
 template <typename T, int DK, int DV>
 cudaError_t launch_prep(const void* q, const void* k, const void* v, const float* g, const float* beta,
@@ -772,8 +739,7 @@ cudaError_t launch_prep(const void* q, const void* k, const void* v, const float
   if (e != cudaSuccess) return e;
   CUtensorMap mq{}, mk{}, mv{};  // 16-bit inputs only (fp32 rows are read by plain loads)
   if (sizeof(T) == 2) {
-    const CUtensorMapDataType dt =
-        std::is_same<T, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    const CUtensorMapDataType dt = map_dtype<T>();
     if (!rows_map(&mq, q, dt, lay.B, lay.T, lay.HK, DK) || !rows_map(&mk, k, dt, lay.B, lay.T, lay.HK, DK) ||
         !rows_map(&mv, v, dt, lay.B, lay.T, lay.H, DV))
       return cudaErrorInvalidValue;
