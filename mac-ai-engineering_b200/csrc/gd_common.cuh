@@ -195,13 +195,14 @@ inline EncodeTiled encode_tiled() {
   return fn;
 }
 
-// loads past T read zeros; stores past T are not written
-inline bool rows_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int B, int T, int heads, int D) {
+// loads past T read zeros; stores past T are not written. box_d: the box's columns (default all D)
+inline bool rows_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int B, int T, int heads, int D,
+                     int box_d = 0) {
   EncodeTiled enc = encode_tiled();
   if (enc == nullptr) return false;
   const cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)heads, (cuuint64_t)T, (cuuint64_t)B};
   const cuuint64_t strides[3] = {(cuuint64_t)D * 2, (cuuint64_t)heads * D * 2, (cuuint64_t)T * heads * D * 2};
-  const cuuint32_t box[4] = {(cuuint32_t)D, 1, 64, 1};
+  const cuuint32_t box[4] = {(cuuint32_t)(box_d > 0 ? box_d : D), 1, 64, 1};
   const cuuint32_t estr[4] = {1, 1, 1, 1};
   return enc(m, dt, 4, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
              CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,

@@ -458,8 +458,9 @@ struct StateSmem {
   static constexpr size_t s_kt = s_q + 64 * DK * 2;        //   [2][64 x DK] K~ hi, lo
   static constexpr size_t s_m = s_kt + 2 * 64 * DK * 2;    //   [64 x 64] M image
   static constexpr size_t stage_bytes = s_m + 64 * 64 * 2;
-  static constexpr size_t bar = stage0 + 2 * stage_bytes;
-  static constexpr int NBAR = 13;
+  static constexpr size_t ost = stage0 + 2 * stage_bytes;   // [2][64 x DVH] O staging (row-major, 16-bit outputs)
+  static constexpr size_t bar = ost + 2 * 64 * DVH * 2;
+  static constexpr int NBAR = 16;
   static constexpr size_t tmem = bar + NBAR * 8;
   static constexpr size_t total = tmem + 8;
 };
@@ -478,7 +479,8 @@ __device__ __forceinline__ void issue_stage(unsigned char* stg, const unsigned c
 template <typename T, int DK, int DV>
 __global__ void __launch_bounds__(576) state_kernel(const float* __restrict__ s0, T* __restrict__ o,
                                                        float* __restrict__ sT, Layout lay, int flags,
-                                                       unsigned char* __restrict__ ws) {
+                                                       unsigned char* __restrict__ ws,
+                                                       const __grid_constant__ CUtensorMap tm_o) {
   static_assert(DV == 128 && DK == 128, "64 value columns per CTA on TMEM lanes 0-15 of each quadrant");
   using S = StateSmem<DK, DV>;
   constexpr int DVH = S::DVH;
@@ -497,6 +499,8 @@ __global__ void __launch_bounds__(576) state_kernel(const float* __restrict__ s0
   uint64_t* mv_full = bars + 8;     // [2]
   uint64_t* vn_full = bars + 10;    // 16 epilogue warps
   uint64_t* st_full = bars + 11;    // 16 epilogue warps
+  uint64_t* o_full = bars + 12;     // [2] 16 epilogue warps: O staging buffer written
+  uint64_t* o_free = bars + 14;     // [2] thread 0: the tensor store has read the buffer
   uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + S::tmem);
   const bool store = (flags & GD_STORE_STATES) != 0 && lay.backward();
   const bool out = o != nullptr;  // both at once: the stored-states training forward
@@ -511,6 +515,10 @@ __global__ void __launch_bounds__(576) state_kernel(const float* __restrict__ s0
     for (int i = 0; i < 10; ++i) mbar_init(bars + i, 1);
     mbar_init(vn_full, 16);
     mbar_init(st_full, 16);
+    mbar_init(o_full, 16);
+    mbar_init(o_full + 1, 16);
+    mbar_init(o_free, 1);
+    mbar_init(o_free + 1, 1);
     fence_mbar_init();
   }
   tc_fence_before();
@@ -631,11 +639,34 @@ __global__ void __launch_bounds__(576) state_kernel(const float* __restrict__ s0
       gcur_last = __ldg(gp + 63);
     };
     load_u(row0);
-    // O of one chunk: 16-byte token rows after an 8 x 8 transpose in 8-lane groups
+    // O of one chunk. 16-bit outputs: row-major into staging buffer p & 1 (every warp arrives on o_full), then one
+    // tensor store (rows past T are not written) issued by thread 0 once all have; thread 0 marks a buffer free
+    // (o_free) when the next chunk's O begins and the store has read it, and writers wait for that before reusing
+    // the buffer two chunks later. All waits bounded. fp32 outputs: 16-byte token rows after an 8 x 8 transpose.
     float o8[8];
-    auto store_o = [&](int p) {
-      store_token_rows8<T>(o8, o + ((size_t)b * lay.T * lay.H + h) * DV, (size_t)lay.H * DV, p * C + tk, lay.T,
-                           vbase + 16 * qd + 8 * ((lane >> 3) & 1));
+    auto store_o = [&](int p) -> bool {
+      if constexpr (sizeof(T) == 2) {
+        const int bi = p & 1;
+        T* stg = reinterpret_cast<T*>(smem + S::ost + bi * 64 * DVH * 2);
+        if (tid == 0 && p >= 1) {
+          bulk_wait_read0();
+          mbar_arrive(o_free + ((p - 1) & 1));
+        }
+        if (p >= 2 && !mbar_wait(o_free + bi, ((p - 2) >> 1) & 1, err, 50)) return false;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) stg[(tk + j) * DVH + vl_] = cvt_out<T>(o8[j]);
+        fence_async_smem();
+        mbar_arrive_warp(o_full + bi);
+        if (tid == 0) {
+          if (!mbar_wait(o_full + bi, (p >> 1) & 1, err, 51)) return false;
+          tma_store_4d(&tm_o, vbase, h, p * C, b, stg);
+          bulk_commit();
+        }
+      } else {
+        store_token_rows8<T>(o8, o + ((size_t)b * lay.T * lay.H + h) * DV, (size_t)lay.H * DV, p * C + tk, lay.T,
+                             vbase + 16 * qd + 8 * ((lane >> 3) & 1));
+      }
+      return true;
     };
     // pass c computes Vn and the state update of chunk c (c < NT) and, between them, O of chunk c - 1 (c >= 1)
     for (int c = 0; c <= NT; ++c) {
@@ -680,7 +711,7 @@ __global__ void __launch_bounds__(576) state_kernel(const float* __restrict__ s0
         tc_fence_before();
       }
       if (c == NT) {
-        if (out) store_o(NT - 1);
+        if (out && !store_o(NT - 1)) ok = false;
         break;
       }
       GD_TRACE_AT(ws, lay, 8 * c + 7);
@@ -707,10 +738,14 @@ __global__ void __launch_bounds__(576) state_kernel(const float* __restrict__ s0
         mbar_arrive_warp(st_full);
       }
       if (store && c + 1 < NT) store_scf(c + 1);  // off the chain: the next MMAs are already unblocked
-      if (out && c >= 1) store_o(c - 1);          // likewise
+      if (out && c >= 1 && !store_o(c - 1)) {  // likewise
+        ok = false;
+        break;
+      }
       GD_TRACE_AT(ws, lay, 8 * c + 4);
     }
     GD_TRACE_AT(ws, lay, 4002);
+    if (sizeof(T) == 2 && out && tid == 0) bulk_wait0();  // the O tensor stores complete before the CTA ends
     if (ok && sT != nullptr) {
       float* sp = sT + ((size_t)b * lay.H + h) * DK * DV;
 #pragma unroll
@@ -759,7 +794,10 @@ cudaError_t launch_state(const float* s0, void* o, float* sT, const Layout& lay,
   cudaError_t e = set_smem_once(kern, S::total, attr_done);
   if (e != cudaSuccess) return e;
   dim3 grid(lay.H * kVsplit, lay.B);
-  kern<<<grid, 576, S::total, st>>>(s0, static_cast<T*>(o), sT, lay, flags, ws);
+  CUtensorMap mo{};  // 16-bit O: chunk tiles of one CTA's 64 value columns leave by tensor store
+  if (sizeof(T) == 2 && o != nullptr && !rows_map(&mo, o, map_dtype<T>(), lay.B, lay.T, lay.H, DV, DV / kVsplit))
+    return cudaErrorInvalidValue;
+  kern<<<grid, 576, S::total, st>>>(s0, static_cast<T*>(o), sT, lay, flags, ws, mo);
   return cudaGetLastError();
 }
 
