@@ -461,7 +461,7 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
         tmem_ld8h(tmem_lane_addr(B0, warp, tok0), x);  // dO Vn^T -> dM
         const float Gi = sG[ri];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) x[j] = (c8 + j <= ri) ? x[j] * __expf(Gi - sG[c8 + j]) : 0.f;
+        for (int j = 0; j < 8; ++j) x[j] = keep_if(x[j] * __expf(Gi - sG[c8 + j]), c8 + j <= ri);
         store8_split(smem + S::dmh, smem + S::dml, ri, c8, 64, x);
       }
       GD_TRACE_AT(ws, lay, 32 * n + 1);
@@ -524,14 +524,14 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const int jj = c8 + j;
-          a10[j] = (jj < ri) ? sB[jj] * fmaf(__expf(sG[jj]), a10[j], a5[j]) : 0.f;
+          a10[j] = keep_if(sB[jj] * fmaf(__expf(sG[jj]), a10[j], a5[j]), jj < ri);
         }
         store8_bf16(smem + S::da, ri, c8, 64, a10);
         // dO Vn^T again and Q K^T: R's first term dM * (Q K^T) = (dO Vn^T) * (Q K^T) * Gamma
         tmem_ld8hx2(tmem_lane_addr(B0, warp, tok0), a5, tmem_lane_addr(B3, warp, tok0), a10);
         const float Gi = sG[ri];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) rv[j] = (c8 + j < ri) ? a5[j] * a10[j] * __expf(Gi - sG[c8 + j]) : 0.f;
+        for (int j = 0; j < 8; ++j) rv[j] = keep_if(a5[j] * a10[j] * __expf(Gi - sG[c8 + j]), c8 + j < ri);
       }
       GD_TRACE_AT(ws, lay, 32 * n + 7);
       tc_fence_before();
@@ -589,18 +589,13 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
         const float Gi = sG[ri], bi = sB[ri];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          const int jj = c8 + j;
-          float pb = 0.f;
-          rv[j] = 0.f;
-          if (jj < ri) {
-            const float dl = -x[j];
-            const float gam = __expf(Gi - sG[jj]);
-            const float p = dl * gam;
-            rv[j] = dl * bi * kgrow[j] * gam;
-            pk = fmaf(p, kgrow[j], pk);
-            pb = bi * p;
-          }
-          x[j] = pb;
+          const bool in = c8 + j < ri;
+          const float dl = -x[j];
+          const float gam = __expf(Gi - sG[c8 + j]);
+          const float p = keep_if(dl * gam, in);
+          rv[j] = keep_if(dl * bi * kgrow[j] * gam, in);
+          pk = fmaf(p, kgrow[j], pk);
+          x[j] = bi * p;
         }
         store8_bf16(smem + S::da, ri, c8, 64, x);
         pk += __shfl_xor_sync(0xffffffffu, pk, 16);  // the row's other 8 columns of this quarter

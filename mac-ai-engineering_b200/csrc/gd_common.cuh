@@ -49,6 +49,13 @@ struct ErrorWord {
     if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && (slot) < 4096)                  \
       reinterpret_cast<long long*>((ws) + (lay).trace)[(slot)] = clock64();                      \
   } while (0)
+// lane 0 of every warp of CTA (0, 0, 0): slot (< 16) of its warp in row 3 from index 2048
+#define GD_TRACE_WARP(ws, lay, slot)                                                                    \
+  do {                                                                                                  \
+    if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && (threadIdx.x & 31) == 0 && (slot) < 16)  \
+      reinterpret_cast<long long*>((ws) + (lay).trace)[3 * 4096 + 2048 + (threadIdx.x >> 5) * 16 + (slot)] = \
+          clock64();                                                                                    \
+  } while (0)
 // per CTA (up to 4096 of them): SM id, then globaltimer (ns) at entry (which 0) and exit (which 1), in rows 1-3
 #define GD_TRACE_CTA(ws, lay, which)                                                                    \
   do {                                                                                                  \
@@ -72,6 +79,9 @@ struct ErrorWord {
   } while (0)
 #define GD_TRACE_ONE(ws, lay, slot) \
   do {                              \
+  } while (0)
+#define GD_TRACE_WARP(ws, lay, slot) \
+  do {                               \
   } while (0)
 #endif
 
@@ -605,6 +615,12 @@ __device__ __forceinline__ void load8<float>(const float* p, float* v) {
   float4 b = __ldg(reinterpret_cast<const float4*>(p) + 1);
   v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
   v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
+// x where c holds, else +0, as a bit AND (x may be inf or NaN where c fails). A select of an expensive expression
+// (x * exp(..)) is compiled into per-element branches that serialise otherwise independent chains.
+__device__ __forceinline__ float keep_if(float x, bool c) {
+  return __uint_as_float(__float_as_uint(x) & (0u - (unsigned)c));
 }
 
 // one output element, rounded as store8 rounds

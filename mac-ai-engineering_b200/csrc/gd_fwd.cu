@@ -307,23 +307,29 @@ __global__ void __launch_bounds__(256, 2) prep_kernel(const T* __restrict__ q, c
     unsigned char* mimg = ws + lay.m + cidx * lay.m_bytes();
     {
       const int half = warp >> 2;
+      GD_TRACE_WARP(ws, lay, 0);
       tmem_ld32(tmem_lane_addr(tm, warp, 32 * half), acc);
-      if ((warp & 3) < 2) {
-        float mv[32];
+      GD_TRACE_AT(ws, lay, 25);
+      GD_TRACE_WARP(ws, lay, 1);
+      // the decay exp(G_i - G_j), computed for every column and then masked by keep_if (no branches)
+      const bool is_m = (warp & 3) < 2;
+      const int jmax = is_m ? i : i - 1;  // M keeps j <= i, L keeps j < i
+      const float bi = is_m ? 1.f : sB[i];
 #pragma unroll
-        for (int jj = 0; jj < 32; ++jj) {
-          const int j = 32 * half + jj;
-          mv[jj] = (j <= i) ? acc[jj] * __expf(Gi - sG[j]) : 0.f;
+      for (int q4 = 0; q4 < 8; ++q4) {
+        const float4 g4 = *reinterpret_cast<const float4*>(sG + 32 * half + 4 * q4);
+        const float gv[4] = {g4.x, g4.y, g4.z, g4.w};
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int jj = 4 * q4 + u;
+          acc[jj] = keep_if(bi * acc[jj] * __expf(Gi - gv[u]), 32 * half + jj <= jmax);
         }
+      }
+      GD_TRACE_WARP(ws, lay, 2);
+      if (is_m) {
 #pragma unroll
-        for (int q8 = 0; q8 < 4; ++q8) store8_bf16(mimg, i, 32 * half + 8 * q8, 64, mv + 8 * q8);
+        for (int q8 = 0; q8 < 4; ++q8) store8_bf16(mimg, i, 32 * half + 8 * q8, 64, acc + 8 * q8);
       } else {
-        const float bi = sB[i];
-#pragma unroll
-        for (int jj = 0; jj < 32; ++jj) {
-          const int j = 32 * half + jj;
-          acc[jj] = (j < i) ? bi * acc[jj] * __expf(Gi - sG[j]) : 0.f;
-        }
         float4* lrow = reinterpret_cast<float4*>(sL + i * 68 + 32 * half);
 #pragma unroll
         for (int q4 = 0; q4 < 8; ++q4)
@@ -331,6 +337,8 @@ __global__ void __launch_bounds__(256, 2) prep_kernel(const T* __restrict__ q, c
       }
     }
   }
+  GD_TRACE_AT(ws, lay, 26);
+  GD_TRACE_WARP(ws, lay, 3);
   __syncthreads();
   GD_TRACE_AT(ws, lay, 5);
   // (ok is the same in every thread: the barriers inside are reached by all or none)
@@ -341,7 +349,6 @@ __global__ void __launch_bounds__(256, 2) prep_kernel(const T* __restrict__ q, c
   if (ok) {
     // A diag(beta gamma) and the hi/lo split of A diag(beta) as K-major B operands (rows i, cols j)
     const int i = tid >> 2, j0 = 16 * (tid & 3);
-    unsigned char* aimg = lay.backward() ? ws + lay.ai + cidx * lay.m_bytes() : nullptr;
 #pragma unroll
     for (int q8 = 0; q8 < 2; ++q8) {
       float a0[8], a1[8], a2[8];
@@ -354,13 +361,10 @@ __global__ void __launch_bounds__(256, 2) prep_kernel(const T* __restrict__ q, c
       }
       store8_bf16(smem + S::a1, i, j0 + 8 * q8, 64, a1);
       store8_split(smem + S::a2h, smem + S::a2l, i, j0 + 8 * q8, 64, a2);
-      if (aimg != nullptr) store8_bf16(aimg, i, j0 + 8 * q8, 64, a0);  // the backward's A image
-    }
-    if (lay.backward()) {
-      // the backward's V image, transposed ([DV x 64], rows v)
-      store_tile_transposed<64, DV, 8>(smem + S::v, ws + lay.vi + cidx * lay.vi_bytes());
     }
   }
+  // (the backward's A and V^T images go out after the MMAs are issued: global stores ahead of this proxy fence would
+  // hold it until they complete)
   fence_async_smem();
   GD_TRACE_AT(ws, lay, 7);
   tc_fence_before();
@@ -376,11 +380,19 @@ __global__ void __launch_bounds__(256, 2) prep_kernel(const T* __restrict__ q, c
               false, 0, true);
     mma_commit(bar);
   }
-  // the q / k images and G go out while the MMAs run (the k image only for the backward)
+  // the q / k images and G go out while the MMAs run (the k image only for the backward), and for the backward the
+  // A image and the transposed V image ([DV x 64], rows v)
   if (ok) {
     unsigned char* dst = ws + lay.qk + cidx * lay.qk_bytes();  // transposed images ([DK x 64], rows d)
     store_tile_transposed<64, DK, 8>(smem + S::q, dst);
-    if (lay.backward()) store_tile_transposed<64, DK, 8>(smem + S::k, dst + 64 * DK * 2);
+    if (lay.backward()) {
+      store_tile_transposed<64, DK, 8>(smem + S::k, dst + 64 * DK * 2);
+      store_tile_transposed<64, DV, 8>(smem + S::v, ws + lay.vi + cidx * lay.vi_bytes());
+      unsigned char* aimg = ws + lay.ai + cidx * lay.m_bytes();
+      const int i = tid >> 2, j0 = 16 * (tid & 3);
+#pragma unroll
+      for (int q8 = 0; q8 < 2; ++q8) store8_bf16(aimg, i, j0 + 8 * q8, 64, sAi + i * 68 + j0 + 8 * q8);
+    }
     if (tid < 64) reinterpret_cast<float*>(ws + lay.gc + cidx * lay.gc_bytes())[tid] = sG[tid];
   }
   if (ok) ok = mbar_wait(bar, 1, err, 11);
