@@ -146,7 +146,8 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
                                                            float* __restrict__ dg, float* __restrict__ dbeta,
                                                            Layout lay, int flags, unsigned char* __restrict__ ws,
                                                            const __grid_constant__ CUtensorMap tm_dq,
-                                                           const __grid_constant__ CUtensorMap tm_dk) {
+                                                           const __grid_constant__ CUtensorMap tm_dk,
+                                                           const __grid_constant__ CUtensorMap tm_dv) {
   static_assert(DK == 128 && DV == 128, "the head dimension maps onto the 128 TMEM lanes");
   using S = ChunkSmem<DK, DV>;
   extern __shared__ __align__(1024) unsigned char smem[];
@@ -438,7 +439,10 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
       if (!(ok = epi_all(ok))) break;
       tc_fence_after();
       GD_TRACE_AT(ws, lay, 32 * n + 0);
-      float dvr[16];  // dV rows, stored after the e1 hand-off (its proxy fence would wait for global stores in flight)
+      // dV rows: 16-bit outputs are staged row-major ([64 tokens][DV]) in the tail buffer (free until e2 writes dA)
+      // and leave by one tensor store after the next barrier; fp32 rows are stored after the e1 hand-off (its proxy
+      // fence would wait for global stores in flight)
+      float dvr[16];
       {
         float x[16];
         tmem_ld16(tmem_lane_addr(B3, warp, tok0), dvr);  // Y^T: v . Y, and dV = diag(beta) Y
@@ -450,6 +454,12 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
         }
         const float s = warp_reduce_scatter16(x);
         if (lane < 16) P(P_VY, qd, tok0 + lane) = s;
+        if constexpr (sizeof(T) == 2) {
+          T* sv = reinterpret_cast<T*>(smem + S::tail);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) sv[(tok0 + j) * DV + dcol] = cvt_out<T>(dvr[j]);
+          fence_async_smem();
+        }
       }
       {
         float y[16], x[8];
@@ -467,6 +477,10 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
       GD_TRACE_AT(ws, lay, 32 * n + 1);
       ok = mbar_wait(qk_full, (n / lay.rep) & 1, err, 82);
       if (!(ok = epi_all(ok))) break;
+      if (sizeof(T) == 2 && tid == 0) {  // every warp's dV rows are staged
+        tma_store_4d(&tm_dv, 0, it.h, t0, it.b, smem + S::tail);
+        bulk_commit();
+      }
       GD_TRACE_AT(ws, lay, 32 * n + 2);
       {
         float av[16], x[16];
@@ -479,8 +493,9 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
         tc_fence_before();
         fence_async_smem();
         mbar_arrive_warp(e1_done);
-        store_token_rows<T>(dvr, dv + ((size_t)it.b * lay.T * lay.H + it.h) * DV, (size_t)lay.H * DV, t0 + tok0,
-                            lay.T, 32 * qd + 8 * (lane >> 3));
+        if constexpr (sizeof(T) != 2)
+          store_token_rows<T>(dvr, dv + ((size_t)it.b * lay.T * lay.H + it.h) * DV, (size_t)lay.H * DV, t0 + tok0,
+                              lay.T, 32 * qd + 8 * (lane >> 3));
         row16<true>(qh, ql, dcol, tok0, x);
 #pragma unroll
         for (int j = 0; j < 16; ++j) av[j] *= x[j];
@@ -490,6 +505,7 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
       GD_TRACE_AT(ws, lay, 32 * n + 3);
       // ---- e2: dQ / dK terms, dA (and R's first term)
       ok = mbar_wait(g3a_full, par, err, 83);
+      if (sizeof(T) == 2 && tid == 0) bulk_wait_read0();  // the dV store has read the tail buffer before dA goes in
       if (!(ok = epi_all(ok))) break;
       tc_fence_after();
       GD_TRACE_AT(ws, lay, 32 * n + 4);
@@ -787,12 +803,13 @@ cudaError_t launch_bwd_chunk(const void* q, const void* k, const void* v, const 
     return e;
   const int ngroups = lay.B * lay.HK * lay.NT;
   const int grid = ngroups < sms[dev] ? ngroups : sms[dev];
-  CUtensorMap mdq{}, mdk{};  // 16-bit outputs: dq / dk tiles leave by tensor store (fp32 rows by plain stores)
+  CUtensorMap mdq{}, mdk{}, mdv{};  // 16-bit outputs: dq / dk / dv tiles leave by tensor store (fp32 by plain stores)
   if (sizeof(T) == 2 && (!rows_map(&mdq, dq, map_dtype<T>(), lay.B, lay.T, lay.HK, DK) ||
-                         !rows_map(&mdk, dk, map_dtype<T>(), lay.B, lay.T, lay.HK, DK)))
+                         !rows_map(&mdk, dk, map_dtype<T>(), lay.B, lay.T, lay.HK, DK) ||
+                         !rows_map(&mdv, dv, map_dtype<T>(), lay.B, lay.T, lay.H, DV)))
     return cudaErrorInvalidValue;
   kern<<<grid, 576, S::total, st>>>(static_cast<const T*>(q), static_cast<const T*>(k), beta, static_cast<T*>(dq),
-                                    static_cast<T*>(dk), static_cast<T*>(dv), dg, dbeta, lay, flags, ws, mdq, mdk);
+                                    static_cast<T*>(dk), static_cast<T*>(dv), dg, dbeta, lay, flags, ws, mdq, mdk, mdv);
   return cudaGetLastError();
 }
 

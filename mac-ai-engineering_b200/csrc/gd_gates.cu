@@ -94,7 +94,17 @@ __device__ __forceinline__ void ld8f(const float* p, float (&v)[8]) {
 }
 
 __device__ __forceinline__ float sigmoid(float x) { return 1.f / (1.f + expf(-x)); }
-__device__ __forceinline__ float softplus(float x) { return x > kThreshold ? x : log1pf(expf(x)); }
+// Both arms are computed before the select (the expensive one on x clamped at the threshold, so it stays finite; a NaN
+// still propagates): a select with an expensive arm is compiled into per-element branches that serialise the chains
+// of a vector group.
+__device__ __forceinline__ float softplus(float x) {
+  const float s = log1pf(expf(x > kThreshold ? kThreshold : x));
+  return x > kThreshold ? x : s;
+}
+__device__ __forceinline__ float dsoftplus(float x) {  // PyTorch's softplus backward: 1 above the threshold
+  const float s = sigmoid(x > kThreshold ? kThreshold : x);
+  return x > kThreshold ? 1.f : s;
+}
 
 // per-head constants -exp(A_log) and dt_bias, staged once per CTA (heads beyond kSmemHeads read from global)
 template <typename TW>
@@ -191,7 +201,7 @@ __global__ void __launch_bounds__(kThreads) gates_bwd_kernel(const T* __restrict
           const float sb = sigmoid(vb[j]);
           ob[j] = vdb[j] * sb * (1.f - sb);
           const float x = va[j] + dt;
-          oa[j] = vdg[j] * na * (x > kThreshold ? 1.f : sigmoid(x));
+          oa[j] = vdg[j] * na * dsoftplus(x);
           h = h + 1 == H ? 0 : h + 1;
         }
         st8(db + i0, ob);
@@ -203,7 +213,7 @@ __global__ void __launch_bounds__(kThreads) gates_bwd_kernel(const T* __restrict
           const float sb = sigmoid(ld(b, i));
           db[i] = cvt<T>((dbeta ? dbeta[i] : 0.f) * sb * (1.f - sb));
           const float x = ld(a, i) + dt;
-          const float sx = x > kThreshold ? 1.f : sigmoid(x);
+          const float sx = dsoftplus(x);
           da[i] = cvt<T>((dg ? dg[i] : 0.f) * na * sx);
           h = h + 1 == H ? 0 : h + 1;
         }
@@ -226,7 +236,7 @@ __global__ void __launch_bounds__(kThreads) gates_bwd_kernel(const T* __restrict
         const float sb = sigmoid(ld(b, i));
         db[i] = cvt<T>((dbeta ? dbeta[i] : 0.f) * sb * (1.f - sb));
         const float x = ld(a, i) + dt;
-        const float sx = x > kThreshold ? 1.f : sigmoid(x);
+        const float sx = dsoftplus(x);
         const float dgi = dg ? dg[i] : 0.f;
         const float dai = dgi * na * sx;
         da[i] = cvt<T>(dai);
