@@ -14,8 +14,9 @@ maximum over ranks of the device time (CUDA events), taken with an NCCL all-redu
 
 Printed (rank 0), one JSON line:
   value        whole-job tokens/s with inputs resident in HBM (sum of per-step device times; L2 flushed between steps)
-  e2e          the same metric with the inputs copied host->device from pinned memory and every output copied back,
-               inside the timed region (a CPU caller's view of the C ABI)
+  e2e          the same metric with every step's inputs copied host->device from pinned memory and every output copied
+               back, inside the timed region (a CPU caller's view of the C ABI); steps overlap as in an input pipeline
+               (next inputs in and previous outputs out on two copy streams while a step computes)
   roofline     the dominant kernel's achieved rate against MEASURED_PEAKS.json (per-kernel CUDA-event timing pass)
   cpu_baseline transformers' torch_chunk_gated_delta_rule (the reference torch implementation; oracle/transformers_ref.py)
                forward + backward on a bounded sample on this host's cores (rank 0, N = 1 only)
@@ -556,55 +557,82 @@ def measured_traffic(kernel, cfg):
 
 
 def end_to_end(lib, t, cfg, flags, ws, nbytes, stream, args):
-    """The step through the C ABI for a caller holding host buffers: pinned host inputs copied to the device, forward +
-    backward, every output copied back to pinned host memory, all inside the timed region."""
+    """The step through the C ABI for a caller holding host buffers: every step copies its inputs from pinned host
+    memory to the device, runs forward + backward, and copies every output back to pinned host memory, all inside the
+    timed region. As an input pipeline would, the steps overlap: step i's inputs go in on one copy stream while step
+    i - 1 computes and step i - 2's outputs come back on another (two buffer sets, ordered by events; host-to-device
+    and device-to-host copies use separate engines)."""
     import torch
     from macai_b200 import _lib
     P = lambda x: None if x is None else ctypes.c_void_p(x.data_ptr())
     sp = ctypes.c_void_p(stream.cuda_stream)
+    dev = t["q"].device
     B, T, H, HK, D = cfg["B"], cfg["T"], cfg["H"], cfg["HK"], cfg["D"]
     names_in = [n for n in ("q", "k", "v", "g", "beta", "s0", "do", "dsT") if t[n] is not None]
     if cfg["fwd_only"]:
         names_in = [n for n in names_in if n not in ("do", "dsT")]
     host_in = {n: t[n].cpu().pin_memory() for n in names_in}
-    dev_in = {n: torch.empty_like(t[n]) for n in names_in}
-    outs = {"o": torch.empty(B, T, H, D, dtype=torch.bfloat16, device=t["q"].device),
-            "sT": torch.empty(B, H, D, D, dtype=torch.float32, device=t["q"].device)}
-    if not cfg["fwd_only"]:
-        outs.update(dq=torch.empty_like(t["q"]), dk=torch.empty_like(t["k"]), dv=torch.empty_like(t["v"]),
-                    dg=torch.empty_like(t["g"]), db=torch.empty_like(t["g"]),
-                    ds0=torch.empty(B, H, D, D, dtype=torch.float32, device=t["q"].device))
-    host_out = {n: torch.empty(x.shape, dtype=x.dtype, pin_memory=True) for n, x in outs.items()}
-    h2d = sum(x.numel() * x.element_size() for x in host_in.values())
-    d2h = sum(x.numel() * x.element_size() for x in host_out.values())
-    BF = _lib.GD_BFLOAT16
-    g = lambda n: dev_in.get(n)
+    dev_in = [{n: torch.empty_like(t[n]) for n in names_in} for _ in range(2)]
 
-    def one():
-        for n in names_in:
-            dev_in[n].copy_(host_in[n], non_blocking=True)
-        st = lib.gd_forward(P(g("q")), P(g("k")), P(g("v")), P(g("g")), P(g("beta")), P(g("s0")), P(outs["o"]),
-                            P(outs["sT"]), BF, B, T, H, HK, D, D, flags, P(ws), nbytes, sp)
+    def out_set():
+        o = {"o": torch.empty(B, T, H, D, dtype=torch.bfloat16, device=dev),
+             "sT": torch.empty(B, H, D, D, dtype=torch.float32, device=dev)}
+        if not cfg["fwd_only"]:
+            o.update(dq=torch.empty_like(t["q"]), dk=torch.empty_like(t["k"]), dv=torch.empty_like(t["v"]),
+                     dg=torch.empty_like(t["g"]), db=torch.empty_like(t["g"]),
+                     ds0=torch.empty(B, H, D, D, dtype=torch.float32, device=dev))
+        return o
+    outs = [out_set() for _ in range(2)]
+    host_out = [{n: torch.empty(x.shape, dtype=x.dtype, pin_memory=True) for n, x in outs[0].items()}
+                for _ in range(2)]
+    h2d = sum(x.numel() * x.element_size() for x in host_in.values())
+    d2h = sum(x.numel() * x.element_size() for x in host_out[0].values())
+    BF = _lib.GD_BFLOAT16
+    s_in, s_out = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+    ev = lambda: torch.cuda.Event()
+    in_ready, comp_done, out_done = [ev(), ev()], [ev(), ev()], [ev(), ev()]
+    used = [False, False]
+
+    def one(i):
+        b = i & 1
+        d, o = dev_in[b], outs[b]
+        with torch.cuda.stream(s_in):
+            if used[b]:
+                s_in.wait_event(comp_done[b])  # step i - 2 has finished reading these inputs
+            for n in names_in:
+                d[n].copy_(host_in[n], non_blocking=True)
+            in_ready[b].record(s_in)
+        stream.wait_event(in_ready[b])
+        if used[b]:
+            stream.wait_event(out_done[b])  # step i - 2's outputs have been copied out
+        st = lib.gd_forward(P(d["q"]), P(d["k"]), P(d["v"]), P(d["g"]), P(d["beta"]), P(d.get("s0")), P(o["o"]),
+                            P(o["sT"]), BF, B, T, H, HK, D, D, flags, P(ws), nbytes, sp)
         _lib.check(st, "gd_forward")
         if not cfg["fwd_only"]:
-            st = lib.gd_backward(P(g("q")), P(g("k")), P(g("v")), P(g("g")), P(g("beta")), P(g("s0")), P(g("do")),
-                                 P(g("dsT")), P(outs["dq"]), P(outs["dk"]), P(outs["dv"]), P(outs["dg"]),
-                                 P(outs["db"]), P(outs["ds0"]), BF, B, T, H, HK, D, D, flags, P(ws), nbytes, sp)
+            st = lib.gd_backward(P(d["q"]), P(d["k"]), P(d["v"]), P(d["g"]), P(d["beta"]), P(d.get("s0")),
+                                 P(d["do"]), P(d.get("dsT")), P(o["dq"]), P(o["dk"]), P(o["dv"]), P(o["dg"]),
+                                 P(o["db"]), P(o["ds0"]), BF, B, T, H, HK, D, D, flags, P(ws), nbytes, sp)
             _lib.check(st, "gd_backward")
-        for n, x in outs.items():
-            host_out[n].copy_(x, non_blocking=True)
+        comp_done[b].record(stream)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(comp_done[b])
+            for n, x in o.items():
+                host_out[b][n].copy_(x, non_blocking=True)
+            out_done[b].record(s_out)
+        used[b] = True
 
     steps = max(3, min(args.steps, 10))
-    with torch.cuda.stream(stream):
-        for _ in range(2):
-            one()
-        stream.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(steps):
-            one()
-        e1.record(stream)
-        stream.synchronize()
+    for i in range(2):
+        one(i)
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s_in)
+    for i in range(steps):
+        one(i)
+    s_out.wait_stream(s_in)
+    s_out.wait_stream(stream)
+    e1.record(s_out)
+    torch.cuda.synchronize(dev)
     return {"seconds": e0.elapsed_time(e1) / 1e3, "steps": steps, "h2d": h2d, "d2h": d2h}
 
 
