@@ -156,6 +156,13 @@ __global__ void __launch_bounds__(256, 2) prep_kernel(const T* __restrict__ q, c
     fence_mbar_init();
   }
   constexpr bool staged = sizeof(T) == 2;
+  // this chunk's g and beta (threads 0-63, one token each; padding rows: g = 0, beta = 0, which leaves G constant
+  // past the last token), loaded now so that their latency hides under the row loads
+  float gi = 0.f, bi = 0.f;
+  if (tid < 64 && t0 + tid < lay.T) {
+    gi = __ldg(g + ((size_t)b * lay.T + t0 + tid) * lay.H + h);
+    bi = __ldg(beta + ((size_t)b * lay.T + t0 + tid) * lay.H + h);
+  }
   if constexpr (staged) {
     // 16-bit inputs: the chunk's raw q, k, v rows land row-major ([64][D], 256-byte rows) in the q, k, v tile buffers,
     // one tensor-map copy each; rows past T arrive as zeros
@@ -203,14 +210,8 @@ __global__ void __launch_bounds__(256, 2) prep_kernel(const T* __restrict__ q, c
   rv_rows.finish(t0, lay.T, false, 1.f, smem + S::v, nullptr, nullptr);
   GD_TRACE_AT(ws, lay, 1);
 
-  // cumulative log decay (padding rows: g = 0, beta = 0, which leaves G constant past the last token)
+  // cumulative log decay
   if (tid < 64) {
-    const int t = t0 + tid;
-    float gi = 0.f, bi = 0.f;
-    if (t < lay.T) {
-      gi = g[((size_t)b * lay.T + t) * lay.H + h];
-      bi = beta[((size_t)b * lay.T + t) * lay.H + h];
-    }
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       const float y = __shfl_up_sync(0xffffffffu, gi, o);
