@@ -318,6 +318,8 @@ def main():
     # ---- per-kernel timing pass (not the headline): each entry point between events on the stream
     kern = kernel_times(lib, t, cfg, flags, ws, nbytes, o, sT, dq, dk, dv, dg, db, ds0, stream, flush)
     gates = gates_times(lib, dev, stream, flush) if rank == 0 else None
+    gnorm = gnorm_times(lib, dev, stream, flush) if rank == 0 else None
+    conv = conv_times(lib, dev, stream, flush) if rank == 0 else None
     hbm, tflops, peak_kind = peaks()
     roof = roofline(kern, cfg, hbm, tflops, peak_kind)
 
@@ -358,6 +360,8 @@ def main():
             "kernels": kern,
             "stored_states": stored,
             "gates": gates,
+            "gated_norm": gnorm,
+            "conv": conv,
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": e2e["h2d"],
                     "d2h_bytes_per_step": e2e["d2h"], "ms_per_step": e2e["seconds"] * 1e3 / e2e["steps"]},
@@ -461,6 +465,110 @@ def gates_times(lib, dev, stream, flush, iters=10):
             gbs = per * n / (us * 1e-6) / 1e9
             res[name] = {"us": us, "gbs": gbs, "frac_hbm": gbs / hbm}
         out[tag] = res
+    return out
+
+
+def gnorm_times(lib, dev, stream, flush, iters=10):
+    """The gated RMSNorm on the rule's output (gd_gnorm_fwd / gd_gnorm_bwd, bf16 x and z, bf16 weight frozen as in
+    LoRA training: no weight gradient) over config 1's and config 4's [B * T * H, 128] rows: device microseconds per
+    call (CUDA events, L2 flushed before each) and HBM bandwidth from the algorithmic bytes (forward: x, z read, o
+    written = 6 B per element; backward: x, z, dout read, dx, dz written = 10 B per element)."""
+    import torch
+    from macai_b200 import _lib
+    P = lambda x: None if x is None else ctypes.c_void_p(x.data_ptr())
+    sp = ctypes.c_void_p(stream.cuda_stream)
+    hbm, _, _ = peaks()
+    BF = _lib.GD_BFLOAT16
+    out = {}
+    for tag, rows in (("c1", 4 * 1024 * 16), ("c4", 64 * 4096 * 32)):
+        D = 128
+        gen = torch.Generator(device=dev).manual_seed(9)
+        x = torch.randn(rows, D, generator=gen, device=dev, dtype=torch.bfloat16)
+        z = torch.randn(rows, D, generator=gen, device=dev, dtype=torch.bfloat16)
+        do = torch.randn(rows, D, generator=gen, device=dev, dtype=torch.bfloat16)
+        w = (torch.randn(D, generator=gen, device=dev) * 0.1 + 1).to(torch.bfloat16)
+        o, dx, dz = torch.empty_like(x), torch.empty_like(x), torch.empty_like(z)
+
+        def fwd():
+            _lib.check(lib.gd_gnorm_fwd(P(x), P(z), P(w), P(o), BF, BF, rows, D, 1e-6, sp), "gnorm")
+
+        def bwd():
+            _lib.check(lib.gd_gnorm_bwd(P(x), P(z), P(w), P(do), P(dx), P(dz), None, BF, BF, rows, D, 1e-6, None, 0,
+                                        sp), "gnorm")
+        res = {"rows": rows, "width": D}
+        for name, f, per in (("fwd", fwd, 6), ("bwd", bwd, 10)):
+            with torch.cuda.stream(stream):
+                f()
+                tot = 0.0
+                for _ in range(iters):
+                    flush.zero_()
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record(stream)
+                    f()
+                    e1.record(stream)
+                    e1.synchronize()
+                    tot += e0.elapsed_time(e1)
+            us = tot / iters * 1e3
+            gbs = per * rows * D / (us * 1e-6) / 1e9
+            res[name] = {"us": us, "gbs": gbs, "frac_hbm": gbs / hbm}
+        out[tag] = res
+        del x, z, do, o, dx, dz
+    return out
+
+
+def conv_times(lib, dev, stream, flush, iters=5):
+    """The convolution path (gd_conv_fwd / gd_conv_bwd, bf16 x and weight, the weight frozen as in LoRA training) at
+    config 1's tokens with Qwen3.5-0.8B's widths (C = 6144: 16 key heads and 16 value heads of 128) and at config 4's
+    tokens with 9B's (C = 8192: 16 key heads serving 32 value heads): device microseconds per call (CUDA events, L2
+    flushed before each) and HBM bandwidth from the algorithmic bytes (forward: x read, q and k written in bf16 with
+    the key heads repeated, v written in fp32; backward: x, dq, dk, dv read, dx written)."""
+    import torch
+    from macai_b200 import _lib
+    P = lambda x: None if x is None else ctypes.c_void_p(x.data_ptr())
+    sp = ctypes.c_void_p(stream.cuda_stream)
+    hbm, _, _ = peaks()
+    BF = _lib.GD_BFLOAT16
+    out = {}
+    for tag, (B, T, kd, rep) in (("c1", (4, 1024, 2048, 1)), ("c4", (64, 4096, 2048, 2))):
+        dk = dv = 128
+        vd = kd * rep
+        C = 2 * kd + vd
+        hv = kd // dk * rep
+        gen = torch.Generator(device=dev).manual_seed(11)
+        x = torch.randn(B, T, C, generator=gen, device=dev, dtype=torch.bfloat16)
+        w = (torch.randn(C, 4, generator=gen, device=dev) * 0.3).to(torch.bfloat16)
+        q = torch.empty(B, T, hv, dk, device=dev, dtype=torch.bfloat16)
+        k = torch.empty_like(q)
+        v = torch.empty(B, T, hv, dv, device=dev)
+        dx = torch.empty_like(x)
+
+        def fwd():
+            _lib.check(lib.gd_conv_fwd(P(x), P(w), P(q), P(k), P(v), BF, BF, B, T, C, kd, dk, rep, dv, sp), "conv")
+
+        def bwd():  # the forward's outputs stand in for the cotangents (same shapes and dtypes)
+            _lib.check(lib.gd_conv_bwd(P(x), P(w), P(q), P(k), P(v), P(dx), None, BF, BF, B, T, C, kd, dk, rep, dv,
+                                       None, 0, sp), "conv")
+        tokens = B * T
+        per_fwd = tokens * (2 * C + 2 * 2 * hv * dk + 4 * hv * dv)
+        per_bwd = tokens * (2 * C + 2 * 2 * hv * dk + 4 * hv * dv + 2 * C)
+        res = {"tokens": tokens, "channels": C, "rep": rep}
+        for name, f, nbytes in (("fwd", fwd, per_fwd), ("bwd", bwd, per_bwd)):
+            with torch.cuda.stream(stream):
+                f()
+                tot = 0.0
+                for _ in range(iters):
+                    flush.zero_()
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record(stream)
+                    f()
+                    e1.record(stream)
+                    e1.synchronize()
+                    tot += e0.elapsed_time(e1)
+            us = tot / iters * 1e3
+            gbs = nbytes / (us * 1e-6) / 1e9
+            res[name] = {"us": us, "gbs": gbs, "frac_hbm": gbs / hbm}
+        out[tag] = res
+        del x, q, k, v, dx
     return out
 
 

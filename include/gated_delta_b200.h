@@ -154,6 +154,53 @@ int gd_gates_bwd(const void* b, const void* a, const void* A_log, const void* dt
                  const float* dg, void* db, void* da, void* dA_log, void* ddt_bias, int dtype, int wdtype, long long n,
                  int H, void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- the gated RMSNorm on the rule's output (the step after the rule) ----
+ * o = (w * (x * rsqrt(mean(x^2) + eps)).to(dtype) * silu(z)).to(dtype) over `rows` rows of width D (one value head
+ * each), with transformers' rounding points: the product with w is rounded to `dtype` again when `wdtype` == `dtype`.
+ * x, z, o: [rows, D] in `dtype`; w: [D] in `dtype` or GD_FLOAT32. D % 4 == 0, 0 < D <= 1024; every pointer 16-byte
+ * aligned. No allocation, asynchronous on `stream`.
+ * Replaces: the reference's gnorm_fwd_* kernels (src/macai/layer/_gated_norm.py:28-53, :107-114, dispatched at
+ * :166-167) and their autograd function's forward (:157-171). */
+int gd_gnorm_fwd(const void* x, const void* z, const void* w, void* o, int dtype, int wdtype, long long rows, int D,
+                 float eps, void* stream);
+
+/* Bytes of workspace gd_gnorm_bwd needs when it forms dw (0 for invalid sizes). */
+size_t gd_gnorm_workspace_bytes(long long rows, int D);
+
+/* dx, dz [rows, D] in `dtype` from dout (fp32 math, one rounding each; r recomputed from x). dw = the sum over rows of
+ * dout * silu(z) * x_hat.to(dtype), in `wdtype`, when not NULL (then `workspace` holds gd_gnorm_workspace_bytes(rows,
+ * D)); the sum is taken in a fixed order (no atomics: the same bits every run).
+ * Replaces: gnorm_bwd_* (src/macai/layer/_gated_norm.py:55-104, :115-124, dispatched at :188-190), the weight
+ * gradient's column sum col_sum (:127-137, :192-196) and the autograd function's backward (:172-197). */
+int gd_gnorm_bwd(const void* x, const void* z, const void* w, const void* dout, void* dx, void* dz, void* dw,
+                 int dtype, int wdtype, long long rows, int D, float eps, void* workspace, size_t workspace_bytes,
+                 void* stream);
+
+/* ---- the convolution path (the step that produces the rule's q, k, v) ----
+ * u[t, c] = sum_j w[c, j] x[t - 3 + j, c] (depthwise causal, kernel 4, no bias, zero before each row's start) and
+ * y = silu(u) on the fp32 u, over x [B, T, C] in `dtype` (the input projection's output read in place), written as the
+ * rule's inputs: q, k [B, T, H_v, DK] in `dtype` from channels [0, KD) and [KD, 2 KD), each of the KD / DK key heads
+ * written REP times (value head h REP + r); v [B, T, H_v, DV] in fp32 from channels [2 KD, C).
+ * w: [C, 4] in `dtype` or GD_FLOAT32. Requires C = 2 KD + VD, KD % DK == 0, VD % DV == 0, (KD / DK) REP == VD / DV,
+ * and C, KD, DK, DV multiples of 8 (16-bit) or 4 (fp32); x, q, k, v 16-byte aligned. No allocation, asynchronous.
+ * Replaces: the reference's conv_fwd_* kernels (src/macai/layer/_conv.py:52-83, :139-146, dispatched at :201-203) and
+ * their autograd function's forward (:191-207). */
+int gd_conv_fwd(const void* x, const void* w, void* q, void* k, float* v, int dtype, int wdtype, int B, int T, int C,
+                int KD, int DK, int REP, int DV, void* stream);
+
+/* Bytes of workspace gd_conv_bwd needs when it forms dw (0 for invalid sizes). */
+size_t gd_conv_workspace_bytes(int B, int T, int C);
+
+/* dx [B, T, C] in `dtype` from dq, dk (in `dtype`, summed over the REP value heads of each key head) and dv (fp32);
+ * any of the three NULL = a zero cotangent. u is recomputed from x. dw [C, 4] = the sum over rows and steps of
+ * du[t, c] x[t - 3 + j, c], in `wdtype`, when not NULL (then `workspace` holds gd_conv_workspace_bytes(B, T, C)); the
+ * sum is taken in a fixed order (no atomics: the same bits every run).
+ * Replaces: conv_bwd_* (src/macai/layer/_conv.py:84-137, :147-156, dispatched at :228-230), the weight gradient's
+ * sum dw_sum (:158-167, :232-236) and the autograd function's backward (:208-237). */
+int gd_conv_bwd(const void* x, const void* w, const void* dq, const void* dk, const float* dv, void* dx, void* dw,
+                int dtype, int wdtype, int B, int T, int C, int KD, int DK, int REP, int DV, void* workspace,
+                size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

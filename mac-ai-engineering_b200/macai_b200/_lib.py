@@ -18,7 +18,8 @@ GD_L2NORM, GD_STORE_STATES, GD_SCALE_Q, GD_STATES_STORED = 1, 2, 4, 8
 # every entry point declared in include/gated_delta_b200.h
 EXPORTS = ("gd_status_string", "gd_workspace_bytes", "gd_prep", "gd_fwd_state", "gd_bwd_state", "gd_bwd_chunk",
            "gd_forward", "gd_backward", "gd_read_error", "gd_forward_noalloc", "gd_gates_fwd",
-           "gd_gates_workspace_bytes", "gd_gates_bwd")
+           "gd_gates_workspace_bytes", "gd_gates_bwd", "gd_gnorm_fwd", "gd_gnorm_workspace_bytes", "gd_gnorm_bwd",
+           "gd_conv_fwd", "gd_conv_workspace_bytes", "gd_conv_bwd")
 
 _P = ctypes.c_void_p
 _I = ctypes.c_int
@@ -38,6 +39,12 @@ _SIGS = {
     "gd_gates_fwd": ([_P] * 6 + [_I, _I, ctypes.c_longlong, _I, _P], _I),
     "gd_gates_workspace_bytes": ([ctypes.c_longlong, _I], _SZ),
     "gd_gates_bwd": ([_P] * 10 + [_I, _I, ctypes.c_longlong, _I, _P, _SZ, _P], _I),
+    "gd_gnorm_fwd": ([_P] * 4 + [_I, _I, ctypes.c_longlong, _I, ctypes.c_float, _P], _I),
+    "gd_gnorm_workspace_bytes": ([ctypes.c_longlong, _I], _SZ),
+    "gd_gnorm_bwd": ([_P] * 7 + [_I, _I, ctypes.c_longlong, _I, ctypes.c_float, _P, _SZ, _P], _I),
+    "gd_conv_fwd": ([_P] * 5 + [_I] * 9 + [_P], _I),
+    "gd_conv_workspace_bytes": ([_I, _I, _I], _SZ),
+    "gd_conv_bwd": ([_P] * 7 + [_I] * 9 + [_P, _SZ, _P], _I),
 }
 
 _lib = None

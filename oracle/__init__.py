@@ -11,4 +11,7 @@ Modules:
   pinned 5.22.1 by the reference's requirements.txt:4, 5.5.0 installed here) run on the CPU, used for the parity bar
   (2x its own error against float64) and as the timed CPU baseline.
 - `parity`: the error metrics and the bar.
+- `gates_f64`, `gated_norm_f64`: float64 restatements of the layer steps either side of the rule (the gates before
+  it, src/macai/layer/_gates.py; the gated RMSNorm after it, src/macai/layer/_gated_norm.py), pinned on the CPU
+  against float64 autograd of the PyTorch expressions they replace.
 """

@@ -82,3 +82,45 @@ def test_gates_refusals_before_any_device_call():
     assert ws >= 2 * 16 * 4 and lib.gd_gates_workspace_bytes(100, 16) == 0
     assert lib.gd_gates_bwd(one, one, one, one, one, one, one, one, one, nul, 2, 0, 64 * 1024, 16, nul, 0,
                             nul) == _lib.GD_ERR_WORKSPACE
+
+
+def test_gated_norm_refusals_before_any_device_call():
+    lib = _lib.load()
+    nul = ctypes.c_void_p(0)
+    one = ctypes.c_void_p(256)
+    odd = ctypes.c_void_p(258)
+    BF, F16, F32 = _lib.GD_BFLOAT16, _lib.GD_FLOAT16, _lib.GD_FLOAT32
+    # widths: D % 4, D > 1024; weight dtype neither x's nor float32; unknown dtype; null and misaligned pointers
+    assert lib.gd_gnorm_fwd(one, one, one, one, BF, BF, 10, 126, 1e-6, nul) == _lib.GD_ERR_SHAPE
+    assert lib.gd_gnorm_fwd(one, one, one, one, BF, BF, 10, 2048, 1e-6, nul) == _lib.GD_ERR_SHAPE
+    assert lib.gd_gnorm_fwd(one, one, one, one, BF, F16, 10, 128, 1e-6, nul) == _lib.GD_ERR_ARG
+    assert lib.gd_gnorm_fwd(one, one, one, one, 9, F32, 10, 128, 1e-6, nul) == _lib.GD_ERR_ARG
+    assert lib.gd_gnorm_fwd(one, one, one, nul, BF, F32, 10, 128, 1e-6, nul) == _lib.GD_ERR_ARG
+    assert lib.gd_gnorm_fwd(one, odd, one, one, BF, F32, 10, 128, 1e-6, nul) == _lib.GD_ERR_ALIGN
+    assert lib.gd_gnorm_fwd(nul, nul, nul, nul, BF, BF, 0, 128, 1e-6, nul) == _lib.GD_OK  # no rows
+    # the weight's gradient without a workspace
+    assert lib.gd_gnorm_workspace_bytes(65536, 128) >= 128 * 4 and lib.gd_gnorm_workspace_bytes(10, 0) == 0
+    assert lib.gd_gnorm_bwd(one, one, one, one, one, one, one, BF, BF, 65536, 128, 1e-6, nul, 0,
+                            nul) == _lib.GD_ERR_WORKSPACE
+
+
+def test_conv_refusals_before_any_device_call():
+    lib = _lib.load()
+    nul = ctypes.c_void_p(0)
+    one = ctypes.c_void_p(256)
+    odd = ctypes.c_void_p(264)  # 8-byte aligned only
+    BF, F16, F32 = _lib.GD_BFLOAT16, _lib.GD_FLOAT16, _lib.GD_FLOAT32
+    # (B, T, C, KD, DK, REP, DV) of the 9B layer, then broken ones
+    ok = (2, 33, 8192, 2048, 128, 2, 128)
+    bad_shapes = [(2, 33, 8192, 2048, 128, 1, 128),   # value heads != key heads x rep
+                  (2, 33, 8196, 2048, 128, 2, 128),   # VD not a multiple of DV
+                  (2, 33, 4096, 2048, 128, 2, 128),   # no value channels
+                  (2, 33, 8192, 2048, 100, 2, 128)]   # DK does not divide KD / not a multiple of 8
+    for shp in bad_shapes:
+        assert lib.gd_conv_fwd(one, one, one, one, one, BF, BF, *shp, nul) == _lib.GD_ERR_SHAPE, shp
+    assert lib.gd_conv_fwd(one, one, one, one, one, BF, F16, *ok, nul) == _lib.GD_ERR_ARG
+    assert lib.gd_conv_fwd(one, one, nul, one, one, BF, BF, *ok, nul) == _lib.GD_ERR_ARG
+    assert lib.gd_conv_fwd(odd, one, one, one, one, BF, BF, *ok, nul) == _lib.GD_ERR_ALIGN
+    assert lib.gd_conv_fwd(nul, nul, nul, nul, nul, BF, BF, 0, 33, 8192, 2048, 128, 2, 128, nul) == _lib.GD_OK
+    assert lib.gd_conv_workspace_bytes(2, 33, 8192) >= 8192 * 4 * 4 and lib.gd_conv_workspace_bytes(2, 33, 0) == 0
+    assert lib.gd_conv_bwd(one, one, one, one, one, one, one, BF, BF, *ok, nul, 0, nul) == _lib.GD_ERR_WORKSPACE
