@@ -25,8 +25,9 @@
 namespace {
 
 constexpr int kThreads = 256;
-constexpr int kTile = 32;        // time steps a thread walks (L)
-constexpr int kBatch = 8;        // forward: x rows loaded before any is used
+constexpr int kTileF = 32;       // time steps a forward thread walks (L)
+constexpr int kTileB = 64;       // time steps a backward thread walks (its halo of 3 + 3 rows costs less per step)
+constexpr int kBatch = 4;        // forward: x rows loaded before any is used
 constexpr int kBatchB = 4;       // backward: x and cotangent rows loaded before any is used
 constexpr int kMaxPartials = 256;  // partial rows of dw: tiles are grouped into at most this many row blocks
 constexpr int kMaxGridY = 65535;
@@ -107,6 +108,10 @@ __device__ __forceinline__ __half cvt<__half>(float x) { return __float2half_rn(
 template <>
 __device__ __forceinline__ __nv_bfloat16 cvt<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
 
+// silu(u) = u / (1 + exp(-u)) and sigmoid(u) with the fast divide (2 ulp; a denominator past 2^126, u < -87, gives 0)
+__device__ __forceinline__ float silu(float u) { return __fdividef(u, 1.f + expf(-u)); }
+__device__ __forceinline__ float sigmoid(float u) { return __fdividef(1.f, 1.f + expf(-u)); }
+
 // where channel c's outputs go: q (c < KD) or k (KD <= c < 2 KD), key head h, column d (the REP copies at
 // h REP DK + r DK + d of a [H_v DK] row); or v (c >= 2 KD), column cc of a [VD] row
 struct Route {
@@ -135,14 +140,14 @@ __device__ __forceinline__ void load_taps(const TW* w, int c, float (&tp)[4][V])
 
 // grid (channel groups / 256, tiles of L steps, batch rows)
 template <typename T, typename TW>
-__global__ void __launch_bounds__(kThreads, 2) conv_fwd_kernel(const T* __restrict__ x, const TW* __restrict__ w,
+__global__ void __launch_bounds__(kThreads, 4) conv_fwd_kernel(const T* __restrict__ x, const TW* __restrict__ w,
                                                             T* __restrict__ qo, T* __restrict__ ko,
                                                             float* __restrict__ vo, int Tn, int C, int KD, int DK,
                                                             int REP) {
   constexpr int V = Vec<T>::V;
   const int c = (blockIdx.x * kThreads + threadIdx.x) * V;
   if (c >= C) return;
-  const int t0 = blockIdx.y * kTile, b = blockIdx.z;
+  const int t0 = blockIdx.y * kTileF, b = blockIdx.z;
   float tp[4][V];
   load_taps<TW, V>(w, c, tp);
   const T* xb = x + (size_t)b * Tn * C + c;
@@ -153,45 +158,52 @@ __global__ void __launch_bounds__(kThreads, 2) conv_fwd_kernel(const T* __restri
   if (t0 >= 2) ld(xb + (size_t)(t0 - 2) * C, xm2);
   if (t0 >= 1) ld(xb + (size_t)(t0 - 1) * C, xm1);
   const Route rt = route(c, KD, DK, REP);
-  T* qk = rt.isk ? ko : qo;
   const long long qrow = (long long)KD * REP, vrow = C - 2 * KD;
-  const int te = t0 + kTile < Tn ? t0 + kTile : Tn;
+  const long long bt0 = (long long)b * Tn + t0;
+  // running pointers at row t0, advanced a row at a time
+  const T* xp = xb + (size_t)t0 * C;
+  T* qkp = rt.isv ? nullptr : (rt.isk ? ko : qo) + bt0 * qrow + rt.qcol;
+  float* vp = rt.isv ? vo + bt0 * vrow + rt.cc : nullptr;
+  const int te = t0 + kTileF < Tn ? t0 + kTileF : Tn;
   // kBatch rows of x in flight before any is used
   for (int tb = t0; tb < te; tb += kBatch) {
+    const int n = te - tb;
     float xr[kBatch][V];
 #pragma unroll
     for (int s = 0; s < kBatch; ++s) {
 #pragma unroll
       for (int i = 0; i < V; ++i) xr[s][i] = 0.f;
-      if (tb + s < te) ld(xb + (size_t)(tb + s) * C, xr[s]);
+      if (s < n) ld(xp + (size_t)s * C, xr[s]);
     }
+    xp += (size_t)kBatch * C;
 #pragma unroll
     for (int s = 0; s < kBatch; ++s) {
-      const int t = tb + s;
-      if (t >= te) break;
+      if (s >= n) break;
       float y[V];
 #pragma unroll
       for (int i = 0; i < V; ++i) {
         const float u =
             fmaf(tp[3][i], xr[s][i], fmaf(tp[2][i], xm1[i], fmaf(tp[1][i], xm2[i], tp[0][i] * xm3[i])));
-        y[i] = u / (1.f + expf(-u));
+        y[i] = silu(u);
         xm3[i] = xm2[i];
         xm2[i] = xm1[i];
         xm1[i] = xr[s][i];
       }
-      const long long bt = (long long)b * Tn + t;
       if (rt.isv) {
-        stf<V>(vo + bt * vrow + rt.cc, y);
+        stf<V>(vp, y);
+        vp += vrow;
       } else {
-        for (int r = 0; r < REP; ++r) st(qk + bt * qrow + rt.qcol + (long long)r * DK, y);
+        for (int r = 0; r < REP; ++r) st(qkp + (long long)r * DK, y);
+        qkp += qrow;
       }
     }
   }
 }
 
 // grid (channel groups / 256, row blocks): row block p walks tiles [p tpb, (p + 1) tpb) of the (batch row, tile)
-// order; with DW its fp32 sums of du x go to partial row p ([P, C, 4]).
-template <typename T, typename TW, bool DW>
+// order; with DW its fp32 sums of du x go to partial row p ([P, C, 4]). RP: REP known at compile time (1 or 2: every
+// cotangent load of a batch in flight at once), or 0 (REP read at run time).
+template <typename T, typename TW, bool DW, int RP>
 __global__ void __launch_bounds__(kThreads, 2) conv_bwd_kernel(const T* __restrict__ x, const TW* __restrict__ w,
                                                             const T* __restrict__ dq, const T* __restrict__ dk,
                                                             const float* __restrict__ dv, T* __restrict__ dx,
@@ -205,7 +217,7 @@ __global__ void __launch_bounds__(kThreads, 2) conv_bwd_kernel(const T* __restri
   const Route rt = route(c, KD, DK, REP);
   const T* dqk = rt.isk ? dk : dq;
   const long long qrow = (long long)KD * REP, vrow = C - 2 * KD;
-  const int ntiles = (Tn + kTile - 1) / kTile;
+  const int ntiles = (Tn + kTileB - 1) / kTileB;
   const long long total = (long long)B * ntiles;
   float acc[4][V];
 #pragma unroll
@@ -216,8 +228,8 @@ __global__ void __launch_bounds__(kThreads, 2) conv_bwd_kernel(const T* __restri
   const long long q1 = q0 + tpb < total ? q0 + tpb : total;
   for (long long qt = q0; qt < q1; ++qt) {
     const int b = (int)(qt / ntiles);
-    const int t0 = (int)(qt % ntiles) * kTile;
-    const int tl = t0 + kTile < Tn ? t0 + kTile : Tn;  // this tile's outputs: [t0, tl)
+    const int t0 = (int)(qt % ntiles) * kTileB;
+    const int tl = t0 + kTileB < Tn ? t0 + kTileB : Tn;  // this tile's outputs: [t0, tl)
     const T* xb = x + (size_t)b * Tn * C + c;
     T* dxb = dx + (size_t)b * Tn * C + c;
     float xm3[V], xm2[V], xm1[V], dm1[V], dm2[V], dm3[V];
@@ -227,35 +239,54 @@ __global__ void __launch_bounds__(kThreads, 2) conv_bwd_kernel(const T* __restri
     if (t0 >= 2) ld(xb + (size_t)(t0 - 2) * C, xm2);
     if (t0 >= 1) ld(xb + (size_t)(t0 - 1) * C, xm1);
     // du[t] needs x[t - 3 .. t]; dx[t - 3] is complete once du[t] is known: walk t0 .. tl + 2, kBatchB steps' rows
-    // of x and of the cotangents in flight before any is used
+    // of x and of the cotangents in flight before any is used; running pointers at row t0
+    const long long bt0 = (long long)b * Tn + t0;
+    const T* xp = xb + (size_t)t0 * C;
+    const T* gp = (rt.isv || dqk == nullptr) ? nullptr : dqk + bt0 * qrow + rt.qcol;
+    const float* gvp = (rt.isv && dv != nullptr) ? dv + bt0 * vrow + rt.cc : nullptr;
+    T* dxp = dxb + (size_t)t0 * C;
     for (int tb = t0; tb < tl + 3; tb += kBatchB) {
+      const int n = Tn - tb;  // rows of this batch inside the sequence
       float xr[kBatchB][V], g[kBatchB][V];
 #pragma unroll
       for (int s = 0; s < kBatchB; ++s) {
 #pragma unroll
         for (int i = 0; i < V; ++i) xr[s][i] = g[s][i] = 0.f;
-        if (tb + s < Tn) ld(xb + (size_t)(tb + s) * C, xr[s]);
+        if (s < n) ld(xp + (size_t)s * C, xr[s]);
       }
-      const long long bt0 = (long long)b * Tn + tb;
-      if (rt.isv) {
-        if (dv) {
+      if (gvp) {
 #pragma unroll
-          for (int s = 0; s < kBatchB; ++s)
-            if (tb + s < Tn) ldf<V>(dv + (bt0 + s) * vrow + rt.cc, g[s]);
-        }
-      } else if (dqk) {
-        for (int r = 0; r < REP; ++r) {  // the REP value heads' gradients, in order
+        for (int s = 0; s < kBatchB; ++s)
+          if (s < n) ldf<V>(gvp + (long long)s * vrow, g[s]);
+      } else if (gp) {
+        const int nrep = RP > 0 ? RP : REP;
+#pragma unroll
+        for (int r = 0; r < (RP > 0 ? RP : 1); ++r) {  // the value heads' gradients, in order
 #pragma unroll
           for (int s = 0; s < kBatchB; ++s) {
-            if (tb + s < Tn) {
+            if (s < n) {
               float gr[V];
-              ld(dqk + (bt0 + s) * qrow + rt.qcol + (long long)r * DK, gr);
+              ld(gp + (long long)s * qrow + (long long)r * DK, gr);
+#pragma unroll
+              for (int i = 0; i < V; ++i) g[s][i] += gr[i];
+            }
+          }
+        }
+        for (int r = 1; RP == 0 && r < nrep; ++r) {
+#pragma unroll
+          for (int s = 0; s < kBatchB; ++s) {
+            if (s < n) {
+              float gr[V];
+              ld(gp + (long long)s * qrow + (long long)r * DK, gr);
 #pragma unroll
               for (int i = 0; i < V; ++i) g[s][i] += gr[i];
             }
           }
         }
       }
+      xp += (size_t)kBatchB * C;
+      if (gp) gp += (long long)kBatchB * qrow;
+      if (gvp) gvp += (long long)kBatchB * vrow;
 #pragma unroll
       for (int s = 0; s < kBatchB; ++s) {
         const int t = tb + s;
@@ -265,7 +296,7 @@ __global__ void __launch_bounds__(kThreads, 2) conv_bwd_kernel(const T* __restri
         for (int i = 0; i < V; ++i) {  // rows past Tn hold zeros: du = 0 there
           const float u =
               fmaf(tp[3][i], xr[s][i], fmaf(tp[2][i], xm1[i], fmaf(tp[1][i], xm2[i], tp[0][i] * xm3[i])));
-          const float sg = 1.f / (1.f + expf(-u));
+          const float sg = sigmoid(u);
           du[i] = g[s][i] * sg * (1.f + u * (1.f - sg));
         }
         if (DW && t < tl) {
@@ -282,7 +313,8 @@ __global__ void __launch_bounds__(kThreads, 2) conv_bwd_kernel(const T* __restri
 #pragma unroll
           for (int i = 0; i < V; ++i)
             o[i] = fmaf(tp[0][i], du[i], fmaf(tp[1][i], dm1[i], fmaf(tp[2][i], dm2[i], tp[3][i] * dm3[i])));
-          st(dxb + (size_t)(t - 3) * C, o);
+          st(dxp, o);  // row t - 3
+          dxp += C;
         }
 #pragma unroll
         for (int i = 0; i < V; ++i) {
@@ -327,7 +359,7 @@ __global__ void __launch_bounds__(1024) conv_dw_sum_kernel(const float* __restri
 
 // tiles per row block and the number of row blocks (at most kMaxPartials with dw, else at most the grid's y limit)
 void plan(int B, int Tn, bool dw, int& tpb, int& P) {
-  const long long total = (long long)B * ((Tn + kTile - 1) / kTile);
+  const long long total = (long long)B * ((Tn + kTileB - 1) / kTileB);
   const long long cap = dw ? kMaxPartials : kMaxGridY;
   tpb = (int)((total + cap - 1) / cap);
   if (tpb < 1) tpb = 1;
@@ -342,7 +374,7 @@ int fwd_t(const void* x, const void* w, void* q, void* k, float* v, int B, int T
           cudaStream_t st) {
   constexpr int V = Vec<T>::V;
   const int groups = C / V;
-  dim3 grid((groups + kThreads - 1) / kThreads, (Tn + kTile - 1) / kTile, B);
+  dim3 grid((groups + kThreads - 1) / kThreads, (Tn + kTileF - 1) / kTileF, B);
   conv_fwd_kernel<T, TW><<<grid, kThreads, 0, st>>>(static_cast<const T*>(x), static_cast<const TW*>(w),
                                                     static_cast<T*>(q), static_cast<T*>(k), v, Tn, C, KD, DK, REP);
   return status_of(cudaGetLastError());
@@ -357,14 +389,20 @@ int bwd_t(const void* x, const void* w, const void* dq, const void* dk, const fl
   plan(B, Tn, dw != nullptr, tpb, P);
   dim3 grid((groups + kThreads - 1) / kThreads, P);
   float* part = static_cast<float*>(ws);
-  if (dw == nullptr)
-    conv_bwd_kernel<T, TW, false><<<grid, kThreads, 0, st>>>(
-        static_cast<const T*>(x), static_cast<const TW*>(w), static_cast<const T*>(dq), static_cast<const T*>(dk), dv,
-        static_cast<T*>(dx), nullptr, B, Tn, C, KD, DK, REP, tpb);
-  else
-    conv_bwd_kernel<T, TW, true><<<grid, kThreads, 0, st>>>(
-        static_cast<const T*>(x), static_cast<const TW*>(w), static_cast<const T*>(dq), static_cast<const T*>(dk), dv,
-        static_cast<T*>(dx), part, B, Tn, C, KD, DK, REP, tpb);
+  auto launch = [&](auto kern) {
+    kern<<<grid, kThreads, 0, st>>>(static_cast<const T*>(x), static_cast<const TW*>(w), static_cast<const T*>(dq),
+                                    static_cast<const T*>(dk), dv, static_cast<T*>(dx), part, B, Tn, C, KD, DK, REP,
+                                    tpb);
+  };
+  if (dw == nullptr) {
+    if (REP == 1) launch(conv_bwd_kernel<T, TW, false, 1>);
+    else if (REP == 2) launch(conv_bwd_kernel<T, TW, false, 2>);
+    else launch(conv_bwd_kernel<T, TW, false, 0>);
+  } else {
+    if (REP == 1) launch(conv_bwd_kernel<T, TW, true, 1>);
+    else if (REP == 2) launch(conv_bwd_kernel<T, TW, true, 2>);
+    else launch(conv_bwd_kernel<T, TW, true, 0>);
+  }
   if (cudaGetLastError() != cudaSuccess) return GD_ERR_LAUNCH;
   if (dw == nullptr) return GD_OK;
   const int N = 4 * C;
@@ -378,7 +416,7 @@ int check_args(int dtype, int wdtype, int B, int Tn, int C, int KD, int DK, int 
   if (dtype < GD_FLOAT32 || dtype > GD_BFLOAT16 || wdtype < GD_FLOAT32 || wdtype > GD_BFLOAT16) return GD_ERR_ARG;
   if (wdtype != dtype && wdtype != GD_FLOAT32) return GD_ERR_ARG;
   const int V = dtype == GD_FLOAT32 ? 4 : 8;
-  if (B < 0 || Tn < 0 || B > kMaxGridY || (Tn + kTile - 1) / kTile > kMaxGridY) return GD_ERR_SHAPE;
+  if (B < 0 || Tn < 0 || B > kMaxGridY || (Tn + kTileF - 1) / kTileF > kMaxGridY) return GD_ERR_SHAPE;
   if (KD <= 0 || DK <= 0 || REP <= 0 || DV <= 0) return GD_ERR_SHAPE;
   const int VD = C - 2 * KD;
   if (VD <= 0 || KD % DK != 0 || VD % DV != 0 || (KD / DK) * REP != VD / DV) return GD_ERR_SHAPE;

@@ -84,8 +84,8 @@ def test_conv_path_trained_weight(model, dtype):
 
 
 def test_many_tiles_weight_gradient():
-    """More (row, tile) pairs than partial rows (256): each row block walks several tiles."""
-    check("0.8b", 8, 1100, torch.bfloat16, True, seed=21)
+    """More (row, 64-step tile) pairs than partial rows (256): each row block walks several tiles."""
+    check("0.8b", 8, 2100, torch.bfloat16, True, seed=21)
 
 
 def test_output_dtypes_and_zero_cotangents():
