@@ -132,6 +132,32 @@ int gd_forward_noalloc(const void* q, const void* k, const void* v, const float*
                        const float* s0, void* o, float* sT, int dtype, int B, int T, int H, int HK, int DK, int DV,
                        int flags, void* stream, int* device_status);
 
+/* ---- packed rows (cu_seqlens) ----
+ * N sequences concatenated along the token axis: q, k [T, HK, DK], v, o, do [T, H, DV], g, beta, dg, dbeta [T, H]
+ * (one batch row of T rows in all), sequence n at rows cu_seqlens[n] .. cu_seqlens[n + 1] - 1 (cu_seqlens: N + 1
+ * device int32, cu_seqlens[0] = 0, non-decreasing, cu_seqlens[N] = T; the kernels clamp any other input into range
+ * rather than read out of bounds, but its results are then undefined). Every sequence runs as its own row: states
+ * restart at its first token, s0 / sT / dsT / ds0 are [N, H, DK, DV] (s0, dsT NULL = zero), a sequence without tokens
+ * passes its state through. Each sequence starts a new chunk; the results equal N separate calls. The chunk table is
+ * built on the device from cu_seqlens (no host synchronisation: graph-capturable); o, dq, dk, dv are formed
+ * chunk-aligned in the workspace and copied to the packed rows at the end.
+ * Replaces: the drop-in's cu_seqlens argument, which the reference refuses (src/macai/gated_delta/op.py:270-273;
+ * design note docs/prior_art_gated_delta.md:310-312), with fla's packed-sequence semantics (transformers' call site
+ * passes cu_seqlens= to fla's kernel, layer/_qwen3_5.py:163-165). */
+size_t gd_workspace_bytes_packed(int N, int T, int H, int HK, int DK, int DV, int for_backward);
+
+/* gd_forward over packed rows (flags as gd_forward's, GD_STORE_STATES included). */
+int gd_forward_packed(const void* q, const void* k, const void* v, const float* g, const float* beta,
+                      const float* s0, void* o, float* sT, const int* cu_seqlens, int N, int dtype, int T, int H,
+                      int HK, int DK, int DV, int flags, void* workspace, size_t workspace_bytes, void* stream);
+
+/* gd_backward over packed rows (flags as gd_backward's, GD_STATES_STORED included: the workspace then comes from
+ * gd_forward_packed with GD_STORE_STATES on the same inputs and cu_seqlens). */
+int gd_backward_packed(const void* q, const void* k, const void* v, const float* g, const float* beta,
+                       const float* s0, const void* d_o, const float* dsT, void* dq, void* dk, void* dv, float* dg,
+                       float* dbeta, float* ds0, const int* cu_seqlens, int N, int dtype, int T, int H, int HK, int DK,
+                       int DV, int flags, void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---- the layer's gates (the step before the rule) ----
  * beta = sigmoid(b), g = -exp(A_log) * softplus(a + dt_bias) (softplus with PyTorch's threshold of 20), both float32,
  * from b, a [n = rows * H] in `dtype` and A_log, dt_bias [H] in `wdtype` (GD_FLOAT32 / GD_FLOAT16 / GD_BFLOAT16);

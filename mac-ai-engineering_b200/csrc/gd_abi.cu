@@ -17,6 +17,8 @@ cudaError_t launch_bwd_state(const void*, const float*, float*, const Layout&, i
 template <typename T, int DK, int DV>
 cudaError_t launch_bwd_chunk(const void*, const void*, const void*, const float*, const void*, void*, void*, void*,
                              float*, float*, const Layout&, int, unsigned char*, cudaStream_t);
+cudaError_t launch_chunk_table(const int*, const Layout&, unsigned char*, cudaStream_t);
+cudaError_t launch_scatter(const void*, void*, int, const Layout&, const unsigned char*, cudaStream_t);
 }  // namespace gd
 
 namespace {
@@ -47,6 +49,17 @@ int check_device() {
 }
 
 int launched(cudaError_t e) { return e == cudaSuccess ? GD_OK : GD_ERR_LAUNCH; }
+
+// packed rows: N sequences, T rows in all (one batch row); the state passes' grid rows are the sequences
+int check_packed(int N, int T, int H, int HK, int DK, int DV, int dtype) {
+  if (N <= 0 || N > 65535) return GD_ERR_SHAPE;
+  int s = check_dims(1, T, H, HK, DK, DV, dtype);
+  if (s) return s;
+  if ((long long)H * (T / 64 + N) > (1ll << 31) - 1) return GD_ERR_SHAPE;
+  return GD_OK;
+}
+
+int elem_bytes(int dtype) { return dtype == GD_FLOAT32 ? 4 : 2; }
 
 int prep(const void* q, const void* k, const void* v, const float* g, const float* beta, int dtype, const Layout& L,
          int flags, void* ws, cudaStream_t st) {
@@ -222,6 +235,65 @@ int gd_backward(const void* q, const void* k, const void* v, const float* g, con
   if ((s = gd_bwd_state(d_o, dsT, ds0, dtype, B, T, H, HK, DK, DV, f, workspace, workspace_bytes, stream))) return s;
   return gd_bwd_chunk(q, k, v, beta, d_o, dq, dk, dv, dg, dbeta, dtype, B, T, H, HK, DK, DV, f, workspace,
                       workspace_bytes, stream);
+}
+
+size_t gd_workspace_bytes_packed(int N, int T, int H, int HK, int DK, int DV, int for_backward) {
+  if (check_packed(N, T, H, HK, DK, DV, GD_BFLOAT16) != GD_OK) return 0;
+  return Layout::make(1, T, H, HK, DK, DV, for_backward != 0, N).total;
+}
+
+int gd_forward_packed(const void* q, const void* k, const void* v, const float* g, const float* beta,
+                      const float* s0, void* o, float* sT, const int* cu_seqlens, int N, int dtype, int T, int H,
+                      int HK, int DK, int DV, int flags, void* workspace, size_t workspace_bytes, void* stream) {
+  int s = check_packed(N, T, H, HK, DK, DV, dtype);
+  if (s) return s;
+  const bool keep = (flags & GD_STORE_STATES) != 0;
+  const Layout L = Layout::make(1, T, H, HK, DK, DV, keep, N);
+  if (!q || !k || !v || !g || !beta || !o || !cu_seqlens || !workspace) return GD_ERR_ARG;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o) || !aligned16(workspace)) return GD_ERR_ALIGN;
+  if (workspace_bytes < L.total) return GD_ERR_WORKSPACE;
+  if ((s = check_device())) return s;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  auto ws = static_cast<unsigned char*>(workspace);
+  if (cudaMemsetAsync(workspace, 0, sizeof(gd::ErrorWord), st) != cudaSuccess) return GD_ERR_LAUNCH;
+  if ((s = launched(gd::launch_chunk_table(cu_seqlens, L, ws, st)))) return s;
+  const int f = flags & (GD_L2NORM | GD_SCALE_Q);
+  if ((s = prep(q, k, v, g, beta, dtype, L, f, workspace, st))) return s;
+  if ((s = fwd_state(s0, ws + L.opad, sT, dtype, L, f | (keep ? GD_STORE_STATES : 0), workspace, st))) return s;
+  return launched(gd::launch_scatter(ws + L.opad, o, H * DV * elem_bytes(dtype), L, ws, st));
+}
+
+int gd_backward_packed(const void* q, const void* k, const void* v, const float* g, const float* beta,
+                       const float* s0, const void* d_o, const float* dsT, void* dq, void* dk, void* dv, float* dg,
+                       float* dbeta, float* ds0, const int* cu_seqlens, int N, int dtype, int T, int H, int HK, int DK,
+                       int DV, int flags, void* workspace, size_t workspace_bytes, void* stream) {
+  int s = check_packed(N, T, H, HK, DK, DV, dtype);
+  if (s) return s;
+  const Layout L = Layout::make(1, T, H, HK, DK, DV, true, N);
+  if (!q || !k || !v || !beta || !dq || !dk || !dv || !dg || !dbeta || !cu_seqlens || !workspace) return GD_ERR_ARG;
+  if (!(flags & GD_STATES_STORED) && !g) return GD_ERR_ARG;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(d_o) || !aligned16(dq) || !aligned16(dk) ||
+      !aligned16(dv) || !aligned16(workspace))
+    return GD_ERR_ALIGN;
+  if (workspace_bytes < L.total) return GD_ERR_WORKSPACE;
+  if ((s = check_device())) return s;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  auto ws = static_cast<unsigned char*>(workspace);
+  if (cudaMemsetAsync(workspace, 0, sizeof(gd::ErrorWord), st) != cudaSuccess) return GD_ERR_LAUNCH;
+  if ((s = launched(gd::launch_chunk_table(cu_seqlens, L, ws, st)))) return s;
+  const int f = flags & (GD_L2NORM | GD_SCALE_Q);
+  if (!(flags & GD_STATES_STORED)) {  // recompute the chunk states from the inputs
+    if ((s = prep(q, k, v, g, beta, dtype, L, f, workspace, st))) return s;
+    if ((s = fwd_state(s0, nullptr, nullptr, dtype, L, f | GD_STORE_STATES, workspace, st))) return s;
+  }
+  if ((s = bwd_state(d_o, dsT, ds0, dtype, L, f, workspace, st))) return s;
+  if ((s = bwd_chunk(q, k, v, beta, d_o, ws + L.dqpad, ws + L.dkpad, ws + L.dvpad, dg, dbeta, dtype, L, f, workspace,
+                     st)))
+    return s;
+  const int eb = elem_bytes(dtype);
+  if ((s = launched(gd::launch_scatter(ws + L.dqpad, dq, HK * DK * eb, L, ws, st)))) return s;
+  if ((s = launched(gd::launch_scatter(ws + L.dkpad, dk, HK * DK * eb, L, ws, st)))) return s;
+  return launched(gd::launch_scatter(ws + L.dvpad, dv, H * DV * eb, L, ws, st));
 }
 
 int gd_read_error(void* workspace, void* stream, int* where) {

@@ -50,9 +50,20 @@ __global__ void __launch_bounds__(576) bwd_state_kernel(const T* __restrict__ d_
   constexpr int DVH = S::DVH;
   extern __shared__ __align__(1024) unsigned char smem[];
   ErrorWord* err = reinterpret_cast<ErrorWord*>(ws + lay.err);
-  const int half = blockIdx.x & 1, h = blockIdx.x >> 1, b = blockIdx.y;
+  const int half = blockIdx.x & 1, h = blockIdx.x >> 1;
+  const int z = blockIdx.y;  // batch row, or sequence (packed rows): dsT and ds0 are indexed by it
+  int b, cfirst, clast;      // the workspace's batch row and the chunks [cfirst, clast) walked here
+  lay.chunks_of(ws, z, b, cfirst, clast);
   const int vbase = DVH * half;  // this CTA's first value column
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (clast <= cfirst) {  // a sequence without tokens: the state's gradient passes through
+    if (ds0 != nullptr)
+      for (int i = tid; i < DK * DVH; i += blockDim.x) {
+        const size_t at = ((size_t)z * lay.H + h) * DK * DV + (size_t)(i / DVH) * DV + vbase + i % DVH;
+        ds0[at] = dsT ? dsT[at] : 0.f;
+      }
+    return;
+  }
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::bar);
   uint64_t* crit_full = bars + 0;   // [2] K~, G loaded
   uint64_t* wt_full = bars + 2;
@@ -64,8 +75,8 @@ __global__ void __launch_bounds__(576) bwd_state_kernel(const T* __restrict__ d_
   uint64_t* do_full = bars + 8;     // 16 warps: dO tile written
   uint64_t* dvn_full = bars + 9;    // 16 warps: dVn tile written, G read
   uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + S::tmem);
-  const int NT = lay.NT;
-  const size_t row0 = ((size_t)b * lay.H + h) * NT;
+  const int NT = clast - cfirst;                                   // chunks this CTA pair walks
+  const size_t row0 = ((size_t)b * lay.H + h) * lay.NT + cfirst;  // the first one's workspace index
 
   if (warp == 0) {
     tmem_alloc(tslot, 512);
@@ -218,10 +229,11 @@ __global__ void __launch_bounds__(576) bwd_state_kernel(const T* __restrict__ d_
     // 128-byte core matrix; fetched raw into registers early, written to the tile once the tile's readers are done
     Piece<T> dox;
     const int prl = tid & 7, pcb = (tid >> 3) & 7, prb = tid >> 6;
-    auto fetch_do = [&](int c) {
-      const int t = c * C + 8 * prb + prl;
-      if (d_o != nullptr && t < lay.T) {
-        dox.load(d_o + (((size_t)b * lay.T + t) * lay.H + h) * DV + vbase + 8 * pcb);
+    auto fetch_do = [&](int c) {  // rows of the chunk's span in the caller's dO (zero past the sequence's end)
+      const ChunkSpan sp = lay.span(ws, cfirst + c);
+      const int t = sp.t0 + 8 * prb + prl;
+      if (d_o != nullptr && t < sp.end) {
+        dox.load(d_o + (((size_t)b * lay.Tin + t) * lay.H + h) * DV + vbase + 8 * pcb);
       } else {
         dox.zero();
       }
@@ -235,7 +247,7 @@ __global__ void __launch_bounds__(576) bwd_state_kernel(const T* __restrict__ d_
       store8_bf16(ws + lay.doi + (row0 + c) * lay.vi_bytes(), 8 * prb + prl, vbase + 8 * pcb, DV, x);
     };
     {
-      const float* p = dsT ? dsT + ((size_t)b * lay.H + h) * DK * DV : nullptr;
+      const float* p = dsT ? dsT + ((size_t)z * lay.H + h) * DK * DV : nullptr;
 #pragma unroll
       for (int j = 0; j < 16; ++j) Dr[j] = p ? p[(size_t)(dk0 + j) * DV + v] : 0.f;
       write_ds(NT - 1);
@@ -301,7 +313,7 @@ __global__ void __launch_bounds__(576) bwd_state_kernel(const T* __restrict__ d_
       GD_TRACE_AT(ws, lay, 8 * n + 5);
     }
     if (ok && ds0 != nullptr) {
-      float* p = ds0 + ((size_t)b * lay.H + h) * DK * DV;
+      float* p = ds0 + ((size_t)z * lay.H + h) * DK * DV;
 #pragma unroll
       for (int j = 0; j < 16; ++j) p[(size_t)(dk0 + j) * DV + v] = Dr[j];
     }
@@ -322,7 +334,7 @@ cudaError_t launch_bwd_state(const void* d_o, const float* dsT, float* ds0, cons
   static bool attr_done[kMaxDevices] = {};
   cudaError_t e = set_smem_once(kern, S::total, attr_done);
   if (e != cudaSuccess) return e;
-  dim3 grid(lay.H * 2, lay.B);
+  dim3 grid(lay.H * 2, lay.packed() ? lay.N : lay.B);  // one CTA pair per (head, batch row or sequence)
   kern<<<grid, 576, S::total, st>>>(static_cast<const T*>(d_o), dsT, ds0, lay, flags, ws);
   return cudaGetLastError();
 }

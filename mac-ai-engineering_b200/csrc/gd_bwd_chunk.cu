@@ -424,15 +424,17 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
     for (int j = 0; j < 16; ++j) dQ[j] = dK[j] = 0.f;
     if (nsub > 0 && tid < 64) {
       const Item it = item_of(lay, 0);
-      const int t = it.c * C + tid;
-      sB[tid] = (t < lay.T) ? beta[((size_t)it.b * lay.T + t) * lay.H + it.h] : 0.f;
+      const ChunkSpan sp = lay.span(ws, it.c);
+      const int t = sp.t0 + tid;
+      sB[tid] = (t < sp.end) ? beta[((size_t)it.b * lay.Tin + t) * lay.H + it.h] : 0.f;
     }
     epi_sync();
     bool ok = true;
     for (int n = 0; n < nsub; ++n) {
       const Item it = item_of(lay, n);
       const uint32_t par = n & 1;
-      const int t0 = it.c * C;
+      const int t0 = it.c * C;                    // the chunk's first row of dq, dk, dv (chunk-aligned)
+      const ChunkSpan sp = lay.span(ws, it.c);  // its rows of beta, dg, dbeta (the caller's rows)
       const float* sG = reinterpret_cast<const float*>(smem + S::g + (n & 1) * 256);
       // ---- e1: dV and the vy partials, dW^T and dM tiles, dQ's first term and the a partials
       ok = mbar_wait(in_full, par, err, 80) && mbar_wait(g1_full, par, err, 81);
@@ -627,8 +629,9 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
       float bnext = 0.f;  // the next sub-item's beta, fetched early (thread t alone reads and writes sB[t])
       if (n + 1 < nsub && tid < 64) {
         const Item nx = item_of(lay, n + 1);
-        const int t = nx.c * C + tid;
-        if (t < lay.T) bnext = beta[((size_t)nx.b * lay.T + t) * lay.H + nx.h];
+        const ChunkSpan nsp = lay.span(ws, nx.c);
+        const int t = nsp.t0 + tid;
+        if (t < nsp.end) bnext = beta[((size_t)nx.b * lay.Tin + t) * lay.H + nx.h];
       }
       ok = mbar_wait(p11_full, par, err, 87);
       if (!(ok = epi_all(ok))) break;
@@ -681,10 +684,10 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
         if (warp == 0) suf += xch[0];
         if (warp == 1) pre_excl += xch[1];
         const float dgt = suf + __expf(sG[63]) * sl + pre_excl + rc;
-        const int tt = t0 + t;
-        if (tt < lay.T) {
-          dg[((size_t)it.b * lay.T + tt) * lay.H + it.h] = dgt;
-          dbeta[((size_t)it.b * lay.T + tt) * lay.H + it.h] = db;
+        const int tt = sp.t0 + t;
+        if (tt < sp.end) {
+          dg[((size_t)it.b * lay.Tin + tt) * lay.H + it.h] = dgt;
+          dbeta[((size_t)it.b * lay.Tin + tt) * lay.H + it.h] = db;
         }
         sB[t] = bnext;
       }

@@ -803,12 +803,13 @@ struct Rows {
     }
   }
 
-  __device__ __forceinline__ void issue(const T* x, int b, int t0, int T_, int heads, int hh) {
+  // rows t0 + r of batch row b of x [B][rows][heads][D]; rows at or past `end` zero
+  __device__ __forceinline__ void issue(const T* x, int b, int t0, int rows, int end, int heads, int hh) {
 #pragma unroll
     for (int rbi = 0; rbi < RB; ++rbi) {
       const int t = t0 + row(rbi);
-      const bool valid = x != nullptr && t < T_;
-      const T* rp = x + (((size_t)b * T_ + (valid ? t : 0)) * heads + hh) * D;
+      const bool valid = x != nullptr && t < end;
+      const T* rp = x + (((size_t)b * rows + (valid ? t : 0)) * heads + hh) * D;
 #pragma unroll
       for (int j = 0; j < J; ++j) {
         if (valid) {
@@ -840,7 +841,7 @@ struct Rows {
         ss += __shfl_xor_sync(0xffffffffu, ss, 16);
         const float rs = rsqrtf(ss + 1e-6f);
         f = rs * scale;
-        if (rsq_out != nullptr && t < T_ && lane < 8) rsq_out[t] = rs;  // the (b, hh) row of [B][heads][.]
+        if (rsq_out != nullptr && t < T_ && lane < 8) rsq_out[r] = rs;  // the chunk's 64 slots
       }
 #pragma unroll
       for (int j = 0; j < J; ++j) {

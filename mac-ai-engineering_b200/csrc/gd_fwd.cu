@@ -139,7 +139,9 @@ __global__ void __launch_bounds__(256, 2) prep_kernel(const T* __restrict__ q, c
   const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int hk = h / lay.rep;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int t0 = c * C;
+  // the chunk's rows in the caller's arrays: t0 .. t0 + 63, those below tend valid (the sequence's end)
+  const ChunkSpan span = lay.span(ws, c);
+  const int t0 = span.t0, tend = span.end;
   const size_t cidx = ((size_t)b * lay.H + h) * lay.NT + c;
   float* sL = reinterpret_cast<float*>(smem + S::L);
   float* sAi = reinterpret_cast<float*>(smem + S::Ai);
@@ -159,9 +161,9 @@ __global__ void __launch_bounds__(256, 2) prep_kernel(const T* __restrict__ q, c
   // this chunk's g and beta (threads 0-63, one token each; padding rows: g = 0, beta = 0, which leaves G constant
   // past the last token), loaded now so that their latency hides under the row loads
   float gi = 0.f, bi = 0.f;
-  if (tid < 64 && t0 + tid < lay.T) {
-    gi = __ldg(g + ((size_t)b * lay.T + t0 + tid) * lay.H + h);
-    bi = __ldg(beta + ((size_t)b * lay.T + t0 + tid) * lay.H + h);
+  if (tid < 64 && t0 + tid < tend) {
+    gi = __ldg(g + ((size_t)b * lay.Tin + t0 + tid) * lay.H + h);
+    bi = __ldg(beta + ((size_t)b * lay.Tin + t0 + tid) * lay.H + h);
   }
   if constexpr (staged) {
     // 16-bit inputs: the chunk's raw q, k, v rows land row-major ([64][D], 256-byte rows) in the q, k, v tile buffers,
@@ -182,7 +184,7 @@ __global__ void __launch_bounds__(256, 2) prep_kernel(const T* __restrict__ q, c
   // l2 prologue and operand tiles: every row load in flight before any is converted
   const bool norm = (flags & GD_L2NORM) != 0;
   const bool bwd = lay.backward() && (h % lay.rep == 0);
-  const size_t rrow = ((size_t)b * lay.HK + hk) * lay.NT * 64;  // this (batch row, key head)'s rsqrt row
+  const size_t rrow = (((size_t)b * lay.HK + hk) * lay.NT + c) * 64;  // this chunk's 64 rsqrt slots
   float* rq = bwd ? reinterpret_cast<float*>(ws + lay.rq) + rrow : nullptr;
   float* rk = bwd ? reinterpret_cast<float*>(ws + lay.rk) + rrow : nullptr;
   const float qscale = (flags & GD_SCALE_Q) ? rsqrtf((float)DK) : 1.f;
@@ -193,21 +195,21 @@ __global__ void __launch_bounds__(256, 2) prep_kernel(const T* __restrict__ q, c
   if constexpr (staged) {
     // each warp converts its own 8 rows in place: raw rows 8 w .. 8 w + 7 and tile row block w are the same 2 KB
     landed = mbar_wait(bar + 1, 0, err, 13);
-    rq_rows.issue_staged(smem + S::q, t0, lay.T);
-    rk_rows.issue_staged(smem + S::k, t0, lay.T);
-    rv_rows.issue_staged(smem + S::v, t0, lay.T);
+    rq_rows.issue_staged(smem + S::q, t0, tend);
+    rk_rows.issue_staged(smem + S::k, t0, tend);
+    rv_rows.issue_staged(smem + S::v, t0, tend);
     __syncwarp();
   } else {
-    rq_rows.issue(q, b, t0, lay.T, lay.HK, hk);
-    rk_rows.issue(k, b, t0, lay.T, lay.HK, hk);
+    rq_rows.issue(q, b, t0, lay.Tin, tend, lay.HK, hk);
+    rk_rows.issue(k, b, t0, lay.Tin, tend, lay.HK, hk);
   }
   GD_TRACE_AT(ws, lay, 22);
-  rq_rows.finish(t0, lay.T, norm, qscale, smem + S::q, rq, smem + S::ql);
+  rq_rows.finish(t0, tend, norm, qscale, smem + S::q, rq, smem + S::ql);
   GD_TRACE_AT(ws, lay, 23);
-  rk_rows.finish(t0, lay.T, norm, 1.f, smem + S::k, rk, smem + S::kl);
+  rk_rows.finish(t0, tend, norm, 1.f, smem + S::k, rk, smem + S::kl);
   GD_TRACE_AT(ws, lay, 24);
-  if (!staged) rv_rows.issue(v, b, t0, lay.T, lay.H, h);
-  rv_rows.finish(t0, lay.T, false, 1.f, smem + S::v, nullptr, nullptr);
+  if (!staged) rv_rows.issue(v, b, t0, lay.Tin, tend, lay.H, h);
+  rv_rows.finish(t0, tend, false, 1.f, smem + S::v, nullptr, nullptr);
   GD_TRACE_AT(ws, lay, 1);
 
   // cumulative log decay
@@ -500,9 +502,20 @@ __global__ void __launch_bounds__(576) state_kernel(const float* __restrict__ s0
   extern __shared__ __align__(1024) unsigned char smem[];
   ErrorWord* err = reinterpret_cast<ErrorWord*>(ws + lay.err);
   GD_TRACE_AT(ws, lay, 4000);
-  const int half = blockIdx.x % kVsplit, h = blockIdx.x / kVsplit, b = blockIdx.y;
+  const int half = blockIdx.x % kVsplit, h = blockIdx.x / kVsplit;
+  const int z = blockIdx.y;  // batch row, or sequence (packed rows): s0 and sT are indexed by it
+  int b, cfirst, clast;      // the workspace's batch row and the chunks [cfirst, clast) walked here
+  lay.chunks_of(ws, z, b, cfirst, clast);
   const int vbase = DVH * half;  // this CTA's first value column
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (clast <= cfirst) {  // a sequence without tokens: the state passes through
+    if (sT != nullptr)
+      for (int i = tid; i < DK * DVH; i += blockDim.x) {
+        const size_t at = ((size_t)z * lay.H + h) * DK * DV + (size_t)(i / DVH) * DV + vbase + i % DVH;
+        sT[at] = s0 ? s0[at] : 0.f;
+      }
+    return;
+  }
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::bar);
   uint64_t* full = bars + 0;        // [2] stage loaded (bulk-copy bytes)
   uint64_t* stage_free = bars + 2;  // [2] every MMA that reads the stage is done
@@ -517,8 +530,9 @@ __global__ void __launch_bounds__(576) state_kernel(const float* __restrict__ s0
   uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + S::tmem);
   const bool store = (flags & GD_STORE_STATES) != 0 && lay.backward();
   const bool out = o != nullptr;  // both at once: the stored-states training forward
-  const int NT = lay.NT;
-  const size_t row0 = ((size_t)b * lay.H + h) * NT;
+  const int NT = clast - cfirst;                                     // chunks this CTA pair walks
+  const size_t row0 = ((size_t)b * lay.H + h) * lay.NT + cfirst;    // the first one's workspace index
+  const int trow0 = cfirst * C;                                      // its first row of o
 
   if (warp == 0) {
     tmem_alloc(tslot, 512);
@@ -621,7 +635,7 @@ __global__ void __launch_bounds__(576) state_kernel(const float* __restrict__ s0
     const int dk0 = 32 * quarter + 16 * (lane >> 4);     // key rows dk0 .. dk0 + 15 of the state held here
     float Sr[16];                                        // S[dk0 + j][v]
     {
-      const float* p = s0 ? s0 + ((size_t)b * lay.H + h) * DK * DV : nullptr;
+      const float* p = s0 ? s0 + ((size_t)z * lay.H + h) * DK * DV : nullptr;
 #pragma unroll
       for (int j = 0; j < 16; ++j) Sr[j] = p ? p[(size_t)(dk0 + j) * DV + v] : 0.f;
 #pragma unroll
@@ -672,11 +686,12 @@ __global__ void __launch_bounds__(576) state_kernel(const float* __restrict__ s0
         mbar_arrive_warp(o_full + bi);
         if (tid == 0) {
           if (!mbar_wait(o_full + bi, (p >> 1) & 1, err, 51)) return false;
-          tma_store_4d(&tm_o, vbase, h, p * C, b, stg);
+          tma_store_4d(&tm_o, vbase, h, trow0 + p * C, b, stg);
           bulk_commit();
         }
       } else {
-        store_token_rows8<T>(o8, o + ((size_t)b * lay.T * lay.H + h) * DV, (size_t)lay.H * DV, p * C + tk, lay.T,
+        store_token_rows8<T>(o8, o + ((size_t)b * lay.T * lay.H + h) * DV, (size_t)lay.H * DV, trow0 + p * C + tk,
+                             lay.T,
                              vbase + 16 * qd + 8 * ((lane >> 3) & 1));
       }
       return true;
@@ -760,7 +775,7 @@ __global__ void __launch_bounds__(576) state_kernel(const float* __restrict__ s0
     GD_TRACE_AT(ws, lay, 4002);
     if (sizeof(T) == 2 && out && tid == 0) bulk_wait0();  // the O tensor stores complete before the CTA ends
     if (ok && sT != nullptr) {
-      float* sp = sT + ((size_t)b * lay.H + h) * DK * DV;
+      float* sp = sT + ((size_t)z * lay.H + h) * DK * DV;
 #pragma unroll
       for (int j = 0; j < 16; ++j) sp[(size_t)(dk0 + j) * DV + v] = Sr[j];
     }
@@ -788,8 +803,8 @@ cudaError_t launch_prep(const void* q, const void* k, const void* v, const float
   CUtensorMap mq{}, mk{}, mv{};  // 16-bit inputs only (fp32 rows are read by plain loads)
   if (sizeof(T) == 2) {
     const CUtensorMapDataType dt = map_dtype<T>();
-    if (!rows_map(&mq, q, dt, lay.B, lay.T, lay.HK, DK) || !rows_map(&mk, k, dt, lay.B, lay.T, lay.HK, DK) ||
-        !rows_map(&mv, v, dt, lay.B, lay.T, lay.H, DV))
+    if (!rows_map(&mq, q, dt, lay.B, lay.Tin, lay.HK, DK) || !rows_map(&mk, k, dt, lay.B, lay.Tin, lay.HK, DK) ||
+        !rows_map(&mv, v, dt, lay.B, lay.Tin, lay.H, DV))
       return cudaErrorInvalidValue;
   }
   dim3 grid(lay.NT, lay.H, lay.B);
@@ -806,7 +821,7 @@ cudaError_t launch_state(const float* s0, void* o, float* sT, const Layout& lay,
   static bool attr_done[kMaxDevices] = {};  // once per device: no attribute call inside a graph capture
   cudaError_t e = set_smem_once(kern, S::total, attr_done);
   if (e != cudaSuccess) return e;
-  dim3 grid(lay.H * kVsplit, lay.B);
+  dim3 grid(lay.H * kVsplit, lay.packed() ? lay.N : lay.B);  // one CTA pair per (head, batch row or sequence)
   CUtensorMap mo{};  // 16-bit O: chunk tiles of one CTA's 64 value columns leave by tensor store
   if (sizeof(T) == 2 && o != nullptr && !rows_map(&mo, o, map_dtype<T>(), lay.B, lay.T, lay.H, DV, DV / kVsplit))
     return cudaErrorInvalidValue;

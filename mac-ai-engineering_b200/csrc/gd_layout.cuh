@@ -26,6 +26,14 @@
 //   dvni [2][DV x 64] image   dVn^T: hi, then lo
 //   doi  [64 x DV]    image   dO
 //   sl   [32]         fp32    partial sums of <S_c, dS_{c+1}> (one per epilogue warp of the chunk's two CTAs)
+// Packed rows (N > 0 sequences of lengths from cu_seqlens, concatenated in the caller's arrays as one batch row of Tin
+// rows): B = 1, each sequence starts a new chunk, NT = Tin / 64 + N bounds the chunk count (every sequence adds at most
+// one partial chunk) and T = NT * 64 is the chunk-aligned row count. Then also
+//   ctab [NT]   int2     chunk c's first row in the caller's arrays and its sequence's end row (rows t with
+//                        t0 <= t < end are the chunk's; (0, 0) for chunks past the last sequence's)
+//   seg  [N+1]  int      each sequence's first chunk; seg[N] = the chunks in use
+//   opad / dqpad / dkpad / dvpad  [T][heads][D] in the caller's dtype (4 bytes an element reserved): the chunk-aligned
+//                        o, dq, dk, dv the kernels write, scattered to the caller's packed rows afterwards
 // Every array starts on a 256-byte boundary (bulk copies need 16).
 #pragma once
 
@@ -34,10 +42,17 @@
 
 namespace gd {
 
+// chunk c's rows in the caller's token arrays: rows t0 .. t0 + 63, those below `end` valid
+struct ChunkSpan {
+  int t0, end;
+};
+
 struct Layout {
   int B, T, H, HK, DK, DV, NT, rep;
+  int N;    // packed rows: the number of sequences (0: a [B, T] batch)
+  int Tin;  // rows a batch row has in the caller's token arrays (T, or the packed total)
   size_t nch;  // B * H * NT chunks
-  size_t err, trace, qk, qkl, kt, wt, m, u, gc;
+  size_t err, trace, ctab, seg, opad, dqpad, dkpad, dvpad, qk, qkl, kt, wt, m, u, gc;
   size_t gq, ai, vi, rq, rk, scf, sci, vni, dsi, dvni, doi, sl, total;
 
   __host__ __device__ static size_t up(size_t x) { return (x + 255) & ~size_t(255); }
@@ -53,10 +68,14 @@ struct Layout {
   __host__ __device__ size_t vn_bytes() const { return (size_t)2 * DV * 64 * 2; }  // a [2][DV x 64] image pair
   __host__ __device__ size_t sl_bytes() const { return (size_t)32 * 4; }           // <S, dS> partial sums
 
-  __host__ static Layout make(int B, int T, int H, int HK, int DK, int DV, bool backward) {
+  // N > 0: packed rows, T = the packed total (B must be 1)
+  __host__ static Layout make(int B, int T, int H, int HK, int DK, int DV, bool backward, int N = 0) {
     Layout L{};
-    L.B = B; L.T = T; L.H = H; L.HK = HK; L.DK = DK; L.DV = DV;
-    L.NT = (T + 63) / 64;
+    L.B = B; L.H = H; L.HK = HK; L.DK = DK; L.DV = DV;
+    L.N = N;
+    L.Tin = T;
+    L.NT = N > 0 ? T / 64 + N : (T + 63) / 64;
+    L.T = N > 0 ? L.NT * 64 : T;
     L.rep = HK > 0 ? H / HK : 1;
     L.nch = (size_t)B * H * L.NT;
     size_t o = 0;
@@ -67,6 +86,17 @@ struct Layout {
 #else
     L.trace = 0;
 #endif
+    L.ctab = L.seg = L.opad = L.dqpad = L.dkpad = L.dvpad = 0;
+    if (N > 0) {
+      L.ctab = take((size_t)L.NT * 8);
+      L.seg = take((size_t)(N + 1) * 4);
+      L.opad = take((size_t)L.T * H * DV * 4);
+      if (backward) {
+        L.dqpad = take((size_t)L.T * HK * DK * 4);
+        L.dkpad = take((size_t)L.T * HK * DK * 4);
+        L.dvpad = take((size_t)L.T * H * DV * 4);
+      }
+    }
     L.qk = take(L.nch * L.qk_bytes());
     L.kt = take(L.nch * L.qk_bytes());
     L.wt = take(L.nch * L.wt_bytes());
@@ -94,6 +124,27 @@ struct Layout {
     return L;
   }
   __host__ __device__ bool backward() const { return scf != 0; }
+  __host__ __device__ bool packed() const { return N > 0; }
+
+  // chunk c's rows (regular batches: c * 64 up to T; packed rows: from the chunk table)
+  __device__ ChunkSpan span(const unsigned char* ws, int c) const {
+    if (N == 0) return ChunkSpan{c * 64, T};
+    const int2 e = reinterpret_cast<const int2*>(ws + ctab)[c];
+    return ChunkSpan{e.x, e.y};
+  }
+  // the chunks a state pass walks for grid row z: [first, last) of batch row z, or of sequence z
+  __device__ void chunks_of(const unsigned char* ws, int z, int& b, int& first, int& last) const {
+    if (N == 0) {
+      b = z;
+      first = 0;
+      last = NT;
+    } else {
+      const int* sg = reinterpret_cast<const int*>(ws + seg);
+      b = 0;
+      first = sg[z];
+      last = sg[z + 1];
+    }
+  }
 };
 
 }  // namespace gd

@@ -19,7 +19,8 @@ GD_L2NORM, GD_STORE_STATES, GD_SCALE_Q, GD_STATES_STORED = 1, 2, 4, 8
 EXPORTS = ("gd_status_string", "gd_workspace_bytes", "gd_prep", "gd_fwd_state", "gd_bwd_state", "gd_bwd_chunk",
            "gd_forward", "gd_backward", "gd_read_error", "gd_forward_noalloc", "gd_gates_fwd",
            "gd_gates_workspace_bytes", "gd_gates_bwd", "gd_gnorm_fwd", "gd_gnorm_workspace_bytes", "gd_gnorm_bwd",
-           "gd_conv_fwd", "gd_conv_workspace_bytes", "gd_conv_bwd")
+           "gd_conv_fwd", "gd_conv_workspace_bytes", "gd_conv_bwd", "gd_workspace_bytes_packed", "gd_forward_packed",
+           "gd_backward_packed")
 
 _P = ctypes.c_void_p
 _I = ctypes.c_int
@@ -45,6 +46,9 @@ _SIGS = {
     "gd_conv_fwd": ([_P] * 5 + [_I] * 9 + [_P], _I),
     "gd_conv_workspace_bytes": ([_I, _I, _I], _SZ),
     "gd_conv_bwd": ([_P] * 7 + [_I] * 9 + [_P, _SZ, _P], _I),
+    "gd_workspace_bytes_packed": ([_I] * 7, _SZ),
+    "gd_forward_packed": ([_P] * 9 + [_I] * 8 + [_P, _SZ, _P], _I),
+    "gd_backward_packed": ([_P] * 15 + [_I] * 8 + [_P, _SZ, _P], _I),
 }
 
 _lib = None

@@ -239,6 +239,191 @@ def _backward_stored(ctx, do, dsT, _dws):
 gated_delta_fwd_stored.register_autograd(_backward_stored, setup_context=_setup_context_stored)
 
 
+# ------------------------------------------------------------------------------------------------------------------
+# packed rows (cu_seqlens): q, k, v, g, beta carry one batch row of T tokens holding N sequences; s0 / S_T are
+# [N, H, DK, DV]; every sequence runs as its own row (the C ABI's gd_forward_packed / gd_backward_packed)
+
+def packed_workspace_bytes(N, T, H, HK, DK, DV, backward: bool) -> int:
+    n = _lib.load().gd_workspace_bytes_packed(N, T, H, HK, DK, DV, int(backward))
+    if n == 0:
+        raise NotImplementedError(f"unsupported packed sizes N={N} T={T} H={H} HK={HK} DK={DK} DV={DV}")
+    return n
+
+
+def _pdims(q, v, cu):
+    _, T, HK, DK = q.shape
+    return cu.numel() - 1, T, v.shape[2], HK, DK, v.shape[3]
+
+
+@torch.library.custom_op("macai_b200::gated_delta_fwd_packed", mutates_args=(), device_types="cuda")
+def gated_delta_fwd_packed(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Tensor, beta: torch.Tensor,
+                           s0: Optional[torch.Tensor], cu: torch.Tensor,
+                           flags: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """o [1, T, H, DV] and S_T [N, H, DK, DV] over packed rows; cu: int32 [N + 1] on the device."""
+    N, T, H, HK, DK, DV = _pdims(q, v, cu)
+    lib = _lib.load()
+    dev = q.device
+    o = torch.empty(1, T, H, DV, dtype=q.dtype, device=dev)
+    sT = torch.empty(N, H, DK, DV, dtype=torch.float32, device=dev)
+    nbytes = packed_workspace_bytes(N, T, H, HK, DK, DV, False)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        st = lib.gd_forward_packed(_p(q), _p(k), _p(v), _p(g), _p(beta), _p(s0), _p(o), _p(sT), _p(cu), N,
+                                   _DTYPES[q.dtype], T, H, HK, DK, DV, flags, _p(ws), nbytes, _stream(dev))
+    _lib.check(st, "gd_forward_packed")
+    CALLS["fwd packed"] += 1
+    return o, sT
+
+
+@gated_delta_fwd_packed.register_fake
+def _(q, k, v, g, beta, s0, cu, flags):
+    N, T, H, HK, DK, DV = _pdims(q, v, cu)
+    return q.new_empty(1, T, H, DV), q.new_empty(N, H, DK, DV, dtype=torch.float32)
+
+
+@torch.library.custom_op("macai_b200::gated_delta_fwd_packed_stored", mutates_args=(), device_types="cuda")
+def gated_delta_fwd_packed_stored(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Tensor,
+                                  beta: torch.Tensor, s0: Optional[torch.Tensor], cu: torch.Tensor,
+                                  flags: int) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """The stored-states training forward over packed rows: o, S_T and the workspace the backward reads."""
+    N, T, H, HK, DK, DV = _pdims(q, v, cu)
+    lib = _lib.load()
+    dev = q.device
+    o = torch.empty(1, T, H, DV, dtype=q.dtype, device=dev)
+    sT = torch.empty(N, H, DK, DV, dtype=torch.float32, device=dev)
+    nbytes = packed_workspace_bytes(N, T, H, HK, DK, DV, True)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        st = lib.gd_forward_packed(_p(q), _p(k), _p(v), _p(g), _p(beta), _p(s0), _p(o), _p(sT), _p(cu), N,
+                                   _DTYPES[q.dtype], T, H, HK, DK, DV, flags | _lib.GD_STORE_STATES, _p(ws), nbytes,
+                                   _stream(dev))
+    _lib.check(st, "gd_forward_packed")
+    CALLS["fwd packed stored"] += 1
+    return o, sT, ws
+
+
+@gated_delta_fwd_packed_stored.register_fake
+def _(q, k, v, g, beta, s0, cu, flags):
+    N, T, H, HK, DK, DV = _pdims(q, v, cu)
+    nbytes = packed_workspace_bytes(N, T, H, HK, DK, DV, True)
+    return (q.new_empty(1, T, H, DV), q.new_empty(N, H, DK, DV, dtype=torch.float32),
+            q.new_empty(nbytes, dtype=torch.uint8))
+
+
+def _packed_grads(q, k, v, cu):
+    N, T, H, HK, DK, DV = _pdims(q, v, cu)
+    dev = q.device
+    f32 = dict(dtype=torch.float32, device=dev)
+    return (torch.empty_like(q), torch.empty_like(k), torch.empty_like(v), torch.empty(1, T, H, **f32),
+            torch.empty(1, T, H, **f32), torch.empty(N, H, DK, DV, **f32))
+
+
+@torch.library.custom_op("macai_b200::gated_delta_bwd_packed", mutates_args=(), device_types="cuda")
+def gated_delta_bwd_packed(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Tensor, beta: torch.Tensor,
+                           s0: Optional[torch.Tensor], cu: torch.Tensor, do: torch.Tensor, dsT: Optional[torch.Tensor],
+                           flags: int) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor,
+                                                torch.Tensor]:
+    """(dq, dk, dv, dg, dbeta, ds0) over packed rows, the chunk states recomputed from the inputs."""
+    N, T, H, HK, DK, DV = _pdims(q, v, cu)
+    lib = _lib.load()
+    dev = q.device
+    dq, dk, dv, dg, dbeta, ds0 = _packed_grads(q, k, v, cu)
+    nbytes = packed_workspace_bytes(N, T, H, HK, DK, DV, True)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        st = lib.gd_backward_packed(_p(q), _p(k), _p(v), _p(g), _p(beta), _p(s0), _p(do), _p(dsT), _p(dq), _p(dk),
+                                    _p(dv), _p(dg), _p(dbeta), _p(ds0), _p(cu), N, _DTYPES[q.dtype], T, H, HK, DK, DV,
+                                    flags, _p(ws), nbytes, _stream(dev))
+    _lib.check(st, "gd_backward_packed")
+    CALLS["bwd packed"] += 1
+    return dq, dk, dv, dg, dbeta, ds0
+
+
+@gated_delta_bwd_packed.register_fake
+def _(q, k, v, g, beta, s0, cu, do, dsT, flags):
+    return _packed_grads(q, k, v, cu)
+
+
+# ws is declared unmutated for the reason given at gated_delta_bwd_stored
+@torch.library.custom_op("macai_b200::gated_delta_bwd_packed_stored", mutates_args=(), device_types="cuda")
+def gated_delta_bwd_packed_stored(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, beta: torch.Tensor,
+                                  cu: torch.Tensor, do: torch.Tensor, dsT: Optional[torch.Tensor], ws: torch.Tensor,
+                                  flags: int) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor,
+                                                       torch.Tensor, torch.Tensor]:
+    """(dq, dk, dv, dg, dbeta, ds0) over packed rows from the states gated_delta_fwd_packed_stored kept in ws."""
+    N, T, H, HK, DK, DV = _pdims(q, v, cu)
+    lib = _lib.load()
+    dev = q.device
+    dq, dk, dv, dg, dbeta, ds0 = _packed_grads(q, k, v, cu)
+    with torch.cuda.device(dev):
+        st = lib.gd_backward_packed(_p(q), _p(k), _p(v), None, _p(beta), None, _p(do), _p(dsT), _p(dq), _p(dk),
+                                    _p(dv), _p(dg), _p(dbeta), _p(ds0), _p(cu), N, _DTYPES[q.dtype], T, H, HK, DK, DV,
+                                    flags | _lib.GD_STATES_STORED, _p(ws), ws.numel(), _stream(dev))
+    _lib.check(st, "gd_backward_packed")
+    CALLS["bwd packed stored"] += 1
+    return dq, dk, dv, dg, dbeta, ds0
+
+
+@gated_delta_bwd_packed_stored.register_fake
+def _(q, k, v, beta, cu, do, dsT, ws, flags):
+    return _packed_grads(q, k, v, cu)
+
+
+def _setup_context_packed(ctx, inputs, output):
+    q, k, v, g, beta, s0, cu, flags = inputs
+    ctx.save_for_backward(q, k, v, g, beta, s0, cu)
+    ctx.flags = flags
+    ctx.has_s0 = s0 is not None
+
+
+def _backward_packed(ctx, do, dsT):
+    q, k, v, g, beta, s0, cu = ctx.saved_tensors
+    if do is None:
+        do = torch.zeros(*v.shape, dtype=q.dtype, device=q.device)
+    do = do.to(q.dtype).contiguous()
+    dsT = None if dsT is None else dsT.to(torch.float32).contiguous()
+    dq, dk, dv, dg, dbeta, ds0 = gated_delta_bwd_packed(q, k, v, g, beta, s0, cu, do, dsT, ctx.flags)
+    return dq, dk, dv, dg, dbeta, (ds0 if ctx.has_s0 else None), None, None
+
+
+gated_delta_fwd_packed.register_autograd(_backward_packed, setup_context=_setup_context_packed)
+
+
+def _setup_context_packed_stored(ctx, inputs, output):
+    q, k, v, g, beta, s0, cu, flags = inputs
+    ctx.save_for_backward(q, k, v, beta, cu, output[2])
+    ctx.flags = flags
+    ctx.has_s0 = s0 is not None
+
+
+def _backward_packed_stored(ctx, do, dsT, _dws):
+    q, k, v, beta, cu, ws = ctx.saved_tensors
+    if do is None:
+        do = torch.zeros(*v.shape, dtype=q.dtype, device=q.device)
+    do = do.to(q.dtype).contiguous()
+    dsT = None if dsT is None else dsT.to(torch.float32).contiguous()
+    dq, dk, dv, dg, dbeta, ds0 = gated_delta_bwd_packed_stored(q, k, v, beta, cu, do, dsT, ws, ctx.flags)
+    return dq, dk, dv, dg, dbeta, (ds0 if ctx.has_s0 else None), None, None
+
+
+gated_delta_fwd_packed_stored.register_autograd(_backward_packed_stored, setup_context=_setup_context_packed_stored)
+
+
+def check_cu_seqlens(cu_seqlens, T: int, device) -> torch.Tensor:
+    """cu_seqlens as the kernels take it (int32 on q's device), after the checks a wrong boundary list needs: 1-D with
+    N + 1 >= 2 entries, starting at 0, non-decreasing, ending at T (one host synchronisation for a device tensor)."""
+    cu = torch.as_tensor(cu_seqlens)
+    if cu.dim() != 1 or cu.numel() < 2:
+        raise ValueError(f"cu_seqlens must be 1-D with N + 1 >= 2 entries; got shape {tuple(cu.shape)}")
+    if cu.dtype.is_floating_point or cu.dtype == torch.bool:
+        raise TypeError(f"cu_seqlens must be an integer tensor; got {cu.dtype}")
+    c = cu.to(device=device, dtype=torch.int64)
+    ok = torch.stack([c[0] == 0, c[-1] == T, (c[1:] >= c[:-1]).all()]).all()
+    if not bool(ok):
+        raise ValueError(f"cu_seqlens must start at 0, not decrease and end at the token count T={T}")
+    return c.to(torch.int32).contiguous()
+
+
 def _forward(q, k, v, g, beta, s0, flags):
     """The forward op for this call: the stored-states one when RECOMPUTE_STATES is False and autograd will record
     the call (the reference keeps states only for a backward, op.py:108, :141-142), else the plain one."""
@@ -247,6 +432,15 @@ def _forward(q, k, v, g, beta, s0, flags):
         o, sT, _ = gated_delta_fwd_stored(q, k, v, g, beta, s0, flags)
         return o, sT
     return gated_delta_fwd(q, k, v, g, beta, s0, flags)
+
+
+def _forward_packed(q, k, v, g, beta, s0, cu, flags):
+    """_forward over packed rows."""
+    if not RECOMPUTE_STATES and torch.is_grad_enabled() and any(
+            t is not None and t.requires_grad for t in (q, k, v, g, beta, s0)):
+        o, sT, _ = gated_delta_fwd_packed_stored(q, k, v, g, beta, s0, cu, flags)
+        return o, sT
+    return gated_delta_fwd_packed(q, k, v, g, beta, s0, cu, flags)
 
 
 # ------------------------------------------------------------------------------------------------------------------
@@ -278,20 +472,34 @@ def chunk_gated_delta_rule(query, key, value, g, beta, chunk_size: int = 64, ini
     (H = HK, or a multiple of it: each key head then serves H / HK consecutive value heads); g (log decay, <= 0) and
     beta [B, T, H]; initial_state [B, H, DK, DV] or None. Returns the output [B, T, H, DV] in the query's dtype and the
     final state (float32) when output_final_state, else None. chunk_size is accepted and not used (the kernels chunk by
-    64 tokens), as in the reference (op.py:264-269). Raises NotImplementedError for packed rows (cu_seqlens), as the
-    reference does (op.py:270-273)."""
-    if kwargs.get("cu_seqlens") is not None:
-        # packed rows: the state must restart at each boundary; running without it would silently carry state
-        # across sequences
-        raise NotImplementedError("macai_b200's gated delta rule does not take packed rows (cu_seqlens) yet")
+    64 tokens), as in the reference (op.py:264-269). cu_seqlens (packed rows: batch size 1, N sequences along the
+    tokens, initial_state and the final state [N, H, DK, DV]) runs every sequence as its own row, with fla's
+    semantics; the reference refuses it (op.py:270-273)."""
+    cu_seqlens = kwargs.get("cu_seqlens")
     dt = query.dtype
     if dt not in _DTYPES:
         raise TypeError(f"query dtype {dt} is not supported (float32, float16, bfloat16)")
     # the kernels read q, k, v in one dtype: key and value follow the query's (differentiably, so their gradients
     # come back in their own dtypes)
     k, v = key.to(dt), value.to(dt)
-    check_shapes(query, k, v, g, beta, initial_state)
     flags = _lib.GD_SCALE_Q | (_lib.GD_L2NORM if use_qk_l2norm_in_kernel else 0)
+    if cu_seqlens is not None:
+        # packed rows: one batch row holding N sequences, each with its own state (initial_state [N, H, DK, DV])
+        if query.dim() != 4 or query.shape[0] != 1:
+            raise ValueError(f"with cu_seqlens the batch size must be 1 (sequences packed along the tokens); got "
+                             f"query {tuple(query.shape)}")
+        cu = check_cu_seqlens(cu_seqlens, query.shape[1], query.device)
+        N = cu.numel() - 1
+        B, T, H, HK, DK, DV = _dims(query, v)
+        if initial_state is not None and initial_state.shape != (N, H, DK, DV):
+            raise ValueError(f"with cu_seqlens initial_state must be [N, H, DK, DV] = {(N, H, DK, DV)}; got "
+                             f"{tuple(initial_state.shape)}")
+        check_shapes(query, k, v, g, beta, None)
+        s0 = None if initial_state is None else initial_state.to(torch.float32).contiguous()
+        o, sT = _forward_packed(query.contiguous(), k.contiguous(), v.contiguous(), g.to(torch.float32).contiguous(),
+                                beta.to(torch.float32).contiguous(), s0, cu, flags)
+        return o, (sT if output_final_state else None)
+    check_shapes(query, k, v, g, beta, initial_state)
     s0 = None if initial_state is None else initial_state.to(torch.float32).contiguous()
     o, sT = _forward(query.contiguous(), k.contiguous(), v.contiguous(), g.to(torch.float32).contiguous(),
                      beta.to(torch.float32).contiguous(), s0, flags)

@@ -195,3 +195,60 @@ def dropin(query, key, value, g, beta, initial_state=None, do=None, dsT=None, us
     else:
         dquery, dkey = dqn * scale, dkn
     return o, sT, dquery, dkey, dv, dg_, db_, ds0
+
+
+def dropin_packed(query, key, value, g, beta, cu_seqlens, initial_state=None, do=None, dsT=None,
+                  use_qk_l2norm_in_kernel=True, chunk: int | None = 64):
+    """Float64 truth of the drop-in over packed rows (cu_seqlens): batch size 1, sequence n at rows
+    cu_seqlens[n] .. cu_seqlens[n + 1] - 1, each run as its own row by `dropin` (its own initial state
+    initial_state[n], its own final state), the outputs and gradients concatenated back along the tokens and the
+    states stacked [N, H, DK, DV]. A sequence without tokens passes its state (and the state's gradient) through.
+    The reference refuses cu_seqlens (src/macai/gated_delta/op.py:270-273); these are the packed-sequence semantics of
+    fla's kernels, which transformers' Qwen3.5 layer calls with cu_seqlens (layer/_qwen3_5.py:163-165)."""
+    cu = [int(x) for x in cu_seqlens]
+    N = len(cu) - 1
+    Hv, DK, DV = value.shape[2], query.shape[3], value.shape[3]
+    s0 = torch.zeros(N, Hv, DK, DV, dtype=F64) if initial_state is None else initial_state.to(F64)
+    outs = []
+    for n in range(N):
+        a, b = cu[n], cu[n + 1]
+        if b == a:
+            empty = [torch.zeros(1, 0, *x.shape[2:], dtype=F64) for x in (query, key, value)]
+            e3 = torch.zeros(1, 0, Hv, dtype=F64)
+            if do is None:
+                outs.append((empty[2], s0[n:n + 1]))
+            else:
+                d = torch.zeros_like(s0[n:n + 1]) if dsT is None else dsT[n:n + 1].to(F64)
+                outs.append((empty[2], s0[n:n + 1], empty[0], empty[1], empty[2], e3, e3, d))
+            continue
+        sl = slice(a, b)
+        r = dropin(query[:, sl], key[:, sl], value[:, sl], g[:, sl], beta[:, sl], s0[n:n + 1],
+                   None if do is None else do[:, sl], None if dsT is None else dsT[n:n + 1],
+                   use_qk_l2norm_in_kernel, chunk)
+        outs.append(r)
+    cat = lambda i: torch.cat([o[i] for o in outs], dim=1)
+    stack = lambda i: torch.cat([o[i] for o in outs], dim=0)
+    if do is None:
+        return cat(0), stack(1)
+    return cat(0), stack(1), cat(2), cat(3), cat(4), cat(5), cat(6), stack(7)
+
+
+def recurrence_packed(q, k, v, g, beta, s0, cu_seqlens):
+    """The token recurrence over a packed stream [1, T, H, D] (q, k already normalised and scaled, GQA expanded) with
+    the state set to s0[n] at each sequence's first token and recorded after its last: an independent restatement of
+    the packed semantics, against which `dropin_packed` is pinned. Returns (o [1, T, H, DV], S_T [N, H, DK, DV])."""
+    cu = [int(x) for x in cu_seqlens]
+    N = len(cu) - 1
+    H, DK, DV = q.shape[2], q.shape[3], v.shape[3]
+    o = torch.zeros(1, q.shape[1], H, DV, dtype=F64)
+    sT = torch.zeros(N, H, DK, DV, dtype=F64)
+    for n in range(N):
+        S = s0[n].to(F64).clone()
+        for t in range(cu[n], cu[n + 1]):
+            S = S * torch.exp(g[0, t].to(F64))[:, None, None]
+            kt, vt = k[0, t].to(F64), v[0, t].to(F64)
+            pred = torch.einsum("hk,hkv->hv", kt, S)
+            S = S + torch.einsum("hk,hv->hkv", kt, beta[0, t].to(F64)[:, None] * (vt - pred))
+            o[0, t] = torch.einsum("hk,hkv->hv", q[0, t].to(F64), S)
+        sT[n] = S
+    return o, sT

@@ -124,3 +124,25 @@ def test_conv_refusals_before_any_device_call():
     assert lib.gd_conv_fwd(nul, nul, nul, nul, nul, BF, BF, 0, 33, 8192, 2048, 128, 2, 128, nul) == _lib.GD_OK
     assert lib.gd_conv_workspace_bytes(2, 33, 8192) >= 8192 * 4 * 4 and lib.gd_conv_workspace_bytes(2, 33, 0) == 0
     assert lib.gd_conv_bwd(one, one, one, one, one, one, one, BF, BF, *ok, nul, 0, nul) == _lib.GD_ERR_WORKSPACE
+
+
+def test_packed_refusals_before_any_device_call():
+    lib = _lib.load()
+    nul = ctypes.c_void_p(0)
+    one = ctypes.c_void_p(256)
+    BF = _lib.GD_BFLOAT16
+    # (N, dtype, T, H, HK, DK, DV, flags)
+    assert lib.gd_workspace_bytes_packed(0, 100, 16, 16, 128, 128, 1) == 0          # no sequences
+    assert lib.gd_workspace_bytes_packed(3, 100, 16, 16, 64, 128, 1) == 0           # head width
+    n1 = lib.gd_workspace_bytes_packed(3, 100, 16, 16, 128, 128, 1)
+    n0 = lib.gd_workspace_bytes_packed(3, 100, 16, 16, 128, 128, 0)
+    assert n1 > n0 > 0
+    # more sequences add chunks (each starts a new one): a larger workspace
+    assert lib.gd_workspace_bytes_packed(50, 100, 16, 16, 128, 128, 0) > n0
+    args = [one] * 8
+    assert lib.gd_forward_packed(*args, nul, 3, BF, 100, 16, 16, 128, 128, 5, one, n0, nul) == _lib.GD_ERR_ARG
+    assert lib.gd_forward_packed(*args, one, 0, BF, 100, 16, 16, 128, 128, 5, one, n0, nul) == _lib.GD_ERR_SHAPE
+    assert lib.gd_forward_packed(*args, one, 3, BF, 100, 16, 16, 128, 128, 5, one, n0 - 256,
+                                 nul) == _lib.GD_ERR_WORKSPACE
+    grads = [one] * 14
+    assert lib.gd_backward_packed(*grads, one, 3, BF, 100, 16, 16, 128, 128, 5, one, n0, nul) == _lib.GD_ERR_WORKSPACE

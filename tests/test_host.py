@@ -10,9 +10,21 @@ from macai_b200 import patch
 from macai_b200.gated_delta import chunk_gated_delta_rule, l2norm, op, recurrent_reference
 
 
-def test_packed_rows_refused():
+def test_packed_rows_checked_before_any_launch():
+    """cu_seqlens (which the reference refuses, op.py:270-273) is taken with fla's semantics; wrong boundary lists,
+    a batch size other than 1 and a per-sequence initial state of the wrong shape are refused on the host, and there
+    is still no CPU path."""
     x = torch.zeros(1, 4, 1, 128)
-    with pytest.raises(NotImplementedError):
+    for bad in ([0, 2, 3], [1, 2, 4], [0, 3, 2, 4], [4], [[0, 4]]):
+        with pytest.raises(ValueError):
+            chunk_gated_delta_rule(x, x, x, x[..., 0], x[..., 0], cu_seqlens=torch.tensor(bad))
+    x2 = torch.zeros(2, 4, 1, 128)
+    with pytest.raises(ValueError, match="batch size must be 1"):
+        chunk_gated_delta_rule(x2, x2, x2, x2[..., 0], x2[..., 0], cu_seqlens=torch.tensor([0, 2, 4]))
+    with pytest.raises(ValueError, match="initial_state"):
+        chunk_gated_delta_rule(x, x, x, x[..., 0], x[..., 0], cu_seqlens=torch.tensor([0, 2, 4]),
+                               initial_state=torch.zeros(1, 1, 128, 128))
+    with pytest.raises(RuntimeError, match="CUDA"):
         chunk_gated_delta_rule(x, x, x, x[..., 0], x[..., 0], cu_seqlens=torch.tensor([0, 2, 4]))
 
 

@@ -100,3 +100,21 @@ def test_identical_comparator():
     assert parity.identical(a, a.clone())
     assert not parity.identical(a, torch.tensor([-0.0, float("nan"), 1.0]))
     assert not parity.identical(a, a.double())
+
+
+def test_packed_oracle_matches_the_recurrence_with_state_resets():
+    """dropin_packed (each sequence run as its own row) against an independent restatement: one token recurrence over
+    the whole packed stream that resets the state to s0[n] at each sequence's first token. Boundaries cover a
+    one-token sequence, a chunk-exact one, an empty one and ragged tails."""
+    gen = torch.Generator().manual_seed(7)
+    T, H, D = 150, 2, 128
+    cu = [0, 1, 65, 65, 129, 150]
+    q, k, v = (torch.randn(1, T, H, D, generator=gen, dtype=torch.float64) for _ in range(3))
+    g = -torch.rand(1, T, H, generator=gen, dtype=torch.float64) * 2
+    beta = torch.rand(1, T, H, generator=gen, dtype=torch.float64)
+    s0 = torch.randn(5, H, D, D, generator=gen, dtype=torch.float64) * 0.02
+    o, sT = ref.dropin_packed(q, k, v, g, beta, cu, s0)
+    qn, kn = ref.l2norm(q) * D ** -0.5, ref.l2norm(k)
+    o2, sT2 = ref.recurrence_packed(qn, kn, v, g, beta, s0, cu)
+    assert (o - o2).abs().max().item() < 1e-12 and (sT - sT2).abs().max().item() < 1e-12
+    assert torch.equal(sT[2], s0[2])  # the empty sequence passes its state through
