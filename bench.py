@@ -315,6 +315,11 @@ def main():
                           "matrices, states and Vn, the backward skips the recompute; same bits as the headline's "
                           "recompute mode"}
 
+    # ---- packed rows (not the headline): the same tokens as N sequences of random lengths in one batch row
+    packed = None
+    if not cfg["fwd_only"] and rank == 0:
+        packed = packed_mode(lib, t, cfg, flags, stream, flush, args.steps, args.warmup)
+
     # ---- per-kernel timing pass (not the headline): each entry point between events on the stream
     kern = kernel_times(lib, t, cfg, flags, ws, nbytes, o, sT, dq, dk, dv, dg, db, ds0, stream, flush)
     gates = gates_times(lib, dev, stream, flush) if rank == 0 else None
@@ -359,6 +364,7 @@ def main():
             "roofline": roof,
             "kernels": kern,
             "stored_states": stored,
+            "packed": packed,
             "gates": gates,
             "gated_norm": gnorm,
             "conv": conv,
@@ -416,6 +422,74 @@ def stored_mode_ms(lib, t, cfg, flags, ws, nbytes, o, sT, dq, dk, dv, dg, db, ds
         raise RuntimeError(f"device error word {code} in the stored-states pass")
     del graph
     return sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / steps
+
+
+def packed_mode(lib, t, cfg, flags, stream, flush, steps, warmup, nseq=12, seed=5):
+    """Forward + backward over packed rows (gd_forward_packed then gd_backward_packed, recompute mode): the config's
+    B * T tokens (the same q, k, v, g, beta, dO viewed as one batch row) split into `nseq` sequences of seeded random
+    lengths (at least 1 token each, boundaries uniform over the tokens), with per-sequence initial states and state
+    gradients; CUDA graph, L2 flushed between steps as the headline. Reports ms per step and tokens/s; every sequence
+    starts a new chunk, so the chunk count grows by up to one per sequence over the headline's."""
+    import torch
+    from macai_b200 import _lib
+    P = lambda x: None if x is None else ctypes.c_void_p(x.data_ptr())
+    sp = ctypes.c_void_p(stream.cuda_stream)
+    B, T, H, HK, D = cfg["B"], cfg["T"], cfg["H"], cfg["HK"], cfg["D"]
+    dev = t["q"].device
+    Ttot = B * T
+    gen = torch.Generator().manual_seed(seed)
+    cuts = torch.randperm(Ttot - 1, generator=gen)[:nseq - 1].sort().values + 1
+    cu_host = torch.cat([torch.tensor([0]), cuts, torch.tensor([Ttot])]).to(torch.int32)
+    cu = cu_host.to(dev)
+    view = lambda x: x.reshape(1, Ttot, *x.shape[2:])
+    q, k, v, g, beta, do = (view(t[n]) for n in ("q", "k", "v", "g", "beta", "do"))
+    s0 = torch.randn(nseq, H, D, D, device=dev) * 0.02
+    dsT = torch.randn(nseq, H, D, D, device=dev) * 0.02
+    o = torch.empty_like(v)
+    sT = torch.empty_like(s0)
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    dg, db = torch.empty_like(g), torch.empty_like(beta)
+    ds0 = torch.empty_like(s0)
+    nb = lib.gd_workspace_bytes_packed(nseq, Ttot, H, HK, D, D, 1)
+    ws = torch.empty(nb, dtype=torch.uint8, device=dev)
+    BF = _lib.GD_BFLOAT16
+
+    def step():
+        _lib.check(lib.gd_forward_packed(P(q), P(k), P(v), P(g), P(beta), P(s0), P(o), P(sT), P(cu), nseq, BF, Ttot, H,
+                                         HK, D, D, flags, P(ws), nb, sp), "gd_forward_packed")
+        _lib.check(lib.gd_backward_packed(P(q), P(k), P(v), P(g), P(beta), P(s0), P(do), P(dsT), P(dq), P(dk), P(dv),
+                                          P(dg), P(db), P(ds0), P(cu), nseq, BF, Ttot, H, HK, D, D, flags, P(ws), nb,
+                                          sp), "gd_backward_packed")
+
+    with torch.cuda.stream(stream):
+        step()
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step()
+    with torch.cuda.stream(stream):
+        for _ in range(warmup):
+            flush.zero_()
+            graph.replay()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    with torch.cuda.stream(stream):
+        for i in range(steps):
+            flush.zero_()
+            starts[i].record(stream)
+            graph.replay()
+            ends[i].record(stream)
+    stream.synchronize()
+    code = lib.gd_read_error(P(ws), sp, None)
+    if code != 0:
+        raise RuntimeError(f"device error word {code} in the packed-rows pass")
+    del graph
+    ms = sum(s_.elapsed_time(e_) for s_, e_ in zip(starts, ends)) / steps
+    lengths = (cu_host[1:] - cu_host[:-1]).tolist()
+    return {"ms_per_step": ms, "value": Ttot / (ms / 1e3), "unit": "tokens/s", "sequences": nseq,
+            "lengths": lengths, "chunks": int(sum((n + 63) // 64 for n in lengths)),
+            "mode": "cu_seqlens: the config's tokens as one batch row of sequences with random boundaries (seeded), "
+                    "per-sequence states; fwd + bwd, recompute mode"}
 
 
 def gates_times(lib, dev, stream, flush, iters=10):

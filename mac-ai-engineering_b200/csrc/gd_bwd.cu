@@ -51,9 +51,9 @@ __global__ void __launch_bounds__(576) bwd_state_kernel(const T* __restrict__ d_
   extern __shared__ __align__(1024) unsigned char smem[];
   ErrorWord* err = reinterpret_cast<ErrorWord*>(ws + lay.err);
   const int half = blockIdx.x & 1, h = blockIdx.x >> 1;
-  const int z = blockIdx.y;  // batch row, or sequence (packed rows): dsT and ds0 are indexed by it
-  int b, cfirst, clast;      // the workspace's batch row and the chunks [cfirst, clast) walked here
-  lay.chunks_of(ws, z, b, cfirst, clast);
+  int z, b, cfirst, clast;  // z: batch row or sequence (dsT and ds0 are indexed by it); b: the workspace's batch
+                            // row; the chunks [cfirst, clast) walked here
+  lay.chunks_of(ws, blockIdx.y, z, b, cfirst, clast);
   const int vbase = DVH * half;  // this CTA's first value column
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (clast <= cfirst) {  // a sequence without tokens: the state's gradient passes through

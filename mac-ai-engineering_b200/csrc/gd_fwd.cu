@@ -503,9 +503,9 @@ __global__ void __launch_bounds__(576) state_kernel(const float* __restrict__ s0
   ErrorWord* err = reinterpret_cast<ErrorWord*>(ws + lay.err);
   GD_TRACE_AT(ws, lay, 4000);
   const int half = blockIdx.x % kVsplit, h = blockIdx.x / kVsplit;
-  const int z = blockIdx.y;  // batch row, or sequence (packed rows): s0 and sT are indexed by it
-  int b, cfirst, clast;      // the workspace's batch row and the chunks [cfirst, clast) walked here
-  lay.chunks_of(ws, z, b, cfirst, clast);
+  int z, b, cfirst, clast;  // z: batch row or sequence (s0 and sT are indexed by it); b: the workspace's batch row;
+                            // the chunks [cfirst, clast) walked here
+  lay.chunks_of(ws, blockIdx.y, z, b, cfirst, clast);
   const int vbase = DVH * half;  // this CTA's first value column
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (clast <= cfirst) {  // a sequence without tokens: the state passes through

@@ -32,6 +32,8 @@
 //   ctab [NT]   int2     chunk c's first row in the caller's arrays and its sequence's end row (rows t with
 //                        t0 <= t < end are the chunk's; (0, 0) for chunks past the last sequence's)
 //   seg  [N+1]  int      each sequence's first chunk; seg[N] = the chunks in use
+//   ord  [N]    int      the sequences by descending chunk count: the state passes' grid row z walks sequence
+//                        ord[z], so the longest chains start first (the block scheduler dispatches rows in order)
 //   opad / dqpad / dkpad / dvpad  [T][heads][D] in the caller's dtype (4 bytes an element reserved): the chunk-aligned
 //                        o, dq, dk, dv the kernels write, scattered to the caller's packed rows afterwards
 // Every array starts on a 256-byte boundary (bulk copies need 16).
@@ -52,7 +54,7 @@ struct Layout {
   int N;    // packed rows: the number of sequences (0: a [B, T] batch)
   int Tin;  // rows a batch row has in the caller's token arrays (T, or the packed total)
   size_t nch;  // B * H * NT chunks
-  size_t err, trace, ctab, seg, opad, dqpad, dkpad, dvpad, qk, qkl, kt, wt, m, u, gc;
+  size_t err, trace, ctab, seg, ord, opad, dqpad, dkpad, dvpad, qk, qkl, kt, wt, m, u, gc;
   size_t gq, ai, vi, rq, rk, scf, sci, vni, dsi, dvni, doi, sl, total;
 
   __host__ __device__ static size_t up(size_t x) { return (x + 255) & ~size_t(255); }
@@ -86,10 +88,11 @@ struct Layout {
 #else
     L.trace = 0;
 #endif
-    L.ctab = L.seg = L.opad = L.dqpad = L.dkpad = L.dvpad = 0;
+    L.ctab = L.seg = L.ord = L.opad = L.dqpad = L.dkpad = L.dvpad = 0;
     if (N > 0) {
       L.ctab = take((size_t)L.NT * 8);
       L.seg = take((size_t)(N + 1) * 4);
+      L.ord = take((size_t)N * 4);
       L.opad = take((size_t)L.T * H * DV * 4);
       if (backward) {
         L.dqpad = take((size_t)L.T * HK * DK * 4);
@@ -132,14 +135,16 @@ struct Layout {
     const int2 e = reinterpret_cast<const int2*>(ws + ctab)[c];
     return ChunkSpan{e.x, e.y};
   }
-  // the chunks a state pass walks for grid row z: [first, last) of batch row z, or of sequence z
-  __device__ void chunks_of(const unsigned char* ws, int z, int& b, int& first, int& last) const {
+  // the chunks a state pass walks for grid row y: [first, last) of batch row y, or of sequence ord[y] (returned in
+  // z: the index of the row's states)
+  __device__ void chunks_of(const unsigned char* ws, int y, int& z, int& b, int& first, int& last) const {
     if (N == 0) {
-      b = z;
+      z = b = y;
       first = 0;
       last = NT;
     } else {
       const int* sg = reinterpret_cast<const int*>(ws + seg);
+      z = reinterpret_cast<const int*>(ws + ord)[y];
       b = 0;
       first = sg[z];
       last = sg[z + 1];
