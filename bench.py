@@ -201,11 +201,17 @@ def main():
                     help="profiling case for ncu: --steps plain forward+backward calls through the C ABI (no graph, "
                          "no timing, no CPU baseline), then exit; launch order per step: prep, state, prep, state "
                          "(store), bwd_state, bwd_chunk")
+    ap.add_argument("--profile-layer", action="store_true",
+                    help="profiling case for ncu: --steps rounds of the layer steps' kernels through the C ABI "
+                         "(gates, gated norm, convolution path; forward then backward each) at sizes above L2, no "
+                         "timing, then exit")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     cfg = CONFIGS[args.config]
     if args.impl == "reference":
         return run_reference(args, cfg)
+    if args.profile_layer:
+        return profile_layer(args.steps)
 
     import torch
     import torch.distributed as dist
@@ -422,6 +428,59 @@ def stored_mode_ms(lib, t, cfg, flags, ws, nbytes, o, sT, dq, dk, dv, dg, db, ds
         raise RuntimeError(f"device error word {code} in the stored-states pass")
     del graph
     return sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / steps
+
+
+def profile_layer(steps):
+    """The layer steps' kernels for an ncu capture: gates over [16, 4096, 32] (bf16 b, a; fp32 A_log, dt_bias),
+    the gated norm over 1 M rows of 128 (bf16, frozen weight), the convolution path over [4, 4096, 8192] with the 9B
+    widths (bf16, frozen weight); each round runs every forward, then every backward, once. Inputs of 128-512 MB
+    each (above the 126 MB L2), about 3 GB in all."""
+    import torch
+    from macai_b200 import _lib
+    lib = _lib.load()
+    dev = torch.device("cuda", 0)
+    P = lambda x: None if x is None else ctypes.c_void_p(x.data_ptr())
+    stream = torch.cuda.Stream(device=dev)
+    sp = ctypes.c_void_p(stream.cuda_stream)
+    BF, F32 = _lib.GD_BFLOAT16, _lib.GD_FLOAT32
+    gen = torch.Generator(device=dev).manual_seed(3)
+    bf = torch.bfloat16
+    # gates
+    shape, H = (16, 4096, 32), 32
+    n = 16 * 4096 * 32
+    gb, ga = (torch.randn(shape, generator=gen, device=dev).to(bf) for _ in range(2))
+    A_log, dt_bias = torch.rand(H, generator=gen, device=dev) * 2.7, torch.randn(H, generator=gen, device=dev)
+    beta, g = torch.empty(shape, device=dev), torch.empty(shape, device=dev)
+    dbeta, dg = torch.randn_like(beta), torch.randn_like(g)
+    db, da = torch.empty_like(gb), torch.empty_like(ga)
+    # gated norm
+    rows, D = 1 << 20, 128
+    x, z, do = (torch.randn(rows, D, generator=gen, device=dev).to(bf) for _ in range(3))
+    w = torch.ones(D, device=dev, dtype=bf)
+    o, dx, dz = torch.empty_like(x), torch.empty_like(x), torch.empty_like(x)
+    # convolution path
+    B, T, kd, rep = 4, 4096, 2048, 2
+    C, hv = 2 * kd + kd * rep, kd // 128 * rep
+    cx = torch.randn(B, T, C, generator=gen, device=dev).to(bf)
+    cw = (torch.randn(C, 4, generator=gen, device=dev) * 0.3).to(bf)
+    cq, ck = (torch.empty(B, T, hv, 128, device=dev, dtype=bf) for _ in range(2))
+    cv = torch.empty(B, T, hv, 128, device=dev)
+    cdx = torch.empty_like(cx)
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        for _ in range(steps):
+            _lib.check(lib.gd_gates_fwd(P(gb), P(ga), P(A_log), P(dt_bias), P(beta), P(g), BF, F32, n, H, sp), "gates")
+            _lib.check(lib.gd_gnorm_fwd(P(x), P(z), P(w), P(o), BF, BF, rows, D, 1e-6, sp), "gnorm")
+            _lib.check(lib.gd_conv_fwd(P(cx), P(cw), P(cq), P(ck), P(cv), BF, BF, B, T, C, kd, 128, rep, 128, sp),
+                       "conv")
+            _lib.check(lib.gd_gates_bwd(P(gb), P(ga), P(A_log), P(dt_bias), P(dbeta), P(dg), P(db), P(da), None, None,
+                                        BF, F32, n, H, None, 0, sp), "gates")
+            _lib.check(lib.gd_gnorm_bwd(P(x), P(z), P(w), P(do), P(dx), P(dz), None, BF, BF, rows, D, 1e-6, None, 0,
+                                        sp), "gnorm")
+            _lib.check(lib.gd_conv_bwd(P(cx), P(cw), P(cq), P(ck), P(cv), P(cdx), None, BF, BF, B, T, C, kd, 128, rep,
+                                       128, None, 0, sp), "conv")
+    stream.synchronize()
+    print(json.dumps({"profile": "layer steps", "steps": steps}), flush=True)
 
 
 def packed_mode(lib, t, cfg, flags, stream, flush, steps, warmup, nseq=12, seed=5):
