@@ -93,7 +93,8 @@ __device__ __forceinline__ void ld8f(const float* p, float (&v)[8]) {
   v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w; v[4] = y.x; v[5] = y.y; v[6] = y.z; v[7] = y.w;
 }
 
-__device__ __forceinline__ float sigmoid(float x) { return 1.f / (1.f + expf(-x)); }
+// the fast divide (2 ulp; a denominator past 2^126, x < -87, gives 0)
+__device__ __forceinline__ float sigmoid(float x) { return __fdividef(1.f, 1.f + expf(-x)); }
 // Both arms are computed before the select (the expensive one on x clamped at the threshold, so it stays finite; a NaN
 // still propagates): a select with an expensive arm is compiled into per-element branches that serialise the chains
 // of a vector group.

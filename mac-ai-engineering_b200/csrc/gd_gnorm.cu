@@ -87,7 +87,9 @@ __device__ __forceinline__ float warp_sum(float v) {
 __device__ __forceinline__ float dot4(float4 a, float4 b) { return a.x * b.x + a.y * b.y + a.z * b.z + a.w * b.w; }
 __device__ __forceinline__ float4 mul4(float4 a, float4 b) { return make_float4(a.x * b.x, a.y * b.y, a.z * b.z, a.w * b.w); }
 __device__ __forceinline__ float4 scale4(float4 a, float s) { return make_float4(a.x * s, a.y * s, a.z * s, a.w * s); }
-__device__ __forceinline__ float sigmoid(float z) { return 1.f / (1.f + expf(-z)); }
+// sigmoid with the fast divide (2 ulp; a denominator past 2^126, z < -87, gives 0): the division's full-precision
+// sequence made the kernels instruction-bound
+__device__ __forceinline__ float sigmoid(float z) { return __fdividef(1.f, 1.f + expf(-z)); }
 
 // 1 / sqrt(mean + eps) from a correctly rounded square root and division (PyTorch's rsqrt on the CPU rounds the same
 // way to within an ulp)
