@@ -26,7 +26,7 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kTileF = 32;       // time steps a forward thread walks (L)
-constexpr int kTileB = 64;       // time steps a backward thread walks (its halo of 3 + 3 rows costs less per step)
+constexpr int kFillCTAs = 2 * 2 * 148;  // backward: two waves of 2 CTAs an SM on 148 SMs (see tile_for)
 constexpr int kBatch = 4;        // forward: x rows loaded before any is used
 constexpr int kBatchB = 4;       // backward: x and cotangent rows loaded before any is used
 constexpr int kMaxPartials = 256;  // partial rows of dw: tiles are grouped into at most this many row blocks
@@ -208,7 +208,7 @@ __global__ void __launch_bounds__(kThreads, 2) conv_bwd_kernel(const T* __restri
                                                             const T* __restrict__ dq, const T* __restrict__ dk,
                                                             const float* __restrict__ dv, T* __restrict__ dx,
                                                             float* __restrict__ part, int B, int Tn, int C, int KD,
-                                                            int DK, int REP, int tpb) {
+                                                            int DK, int REP, int tile, int tpb) {
   constexpr int V = Vec<T>::V;
   const int c = (blockIdx.x * kThreads + threadIdx.x) * V;
   if (c >= C) return;
@@ -217,7 +217,7 @@ __global__ void __launch_bounds__(kThreads, 2) conv_bwd_kernel(const T* __restri
   const Route rt = route(c, KD, DK, REP);
   const T* dqk = rt.isk ? dk : dq;
   const long long qrow = (long long)KD * REP, vrow = C - 2 * KD;
-  const int ntiles = (Tn + kTileB - 1) / kTileB;
+  const int ntiles = (Tn + tile - 1) / tile;
   const long long total = (long long)B * ntiles;
   float acc[4][V];
 #pragma unroll
@@ -228,8 +228,8 @@ __global__ void __launch_bounds__(kThreads, 2) conv_bwd_kernel(const T* __restri
   const long long q1 = q0 + tpb < total ? q0 + tpb : total;
   for (long long qt = q0; qt < q1; ++qt) {
     const int b = (int)(qt / ntiles);
-    const int t0 = (int)(qt % ntiles) * kTileB;
-    const int tl = t0 + kTileB < Tn ? t0 + kTileB : Tn;  // this tile's outputs: [t0, tl)
+    const int t0 = (int)(qt % ntiles) * tile;
+    const int tl = t0 + tile < Tn ? t0 + tile : Tn;  // this tile's outputs: [t0, tl)
     const T* xb = x + (size_t)b * Tn * C + c;
     T* dxb = dx + (size_t)b * Tn * C + c;
     float xm3[V], xm2[V], xm1[V], dm1[V], dm2[V], dm3[V];
@@ -357,9 +357,18 @@ __global__ void __launch_bounds__(1024) conv_dw_sum_kernel(const float* __restri
   if (ty == 0 && n < N) dw[n] = cvt<TW>(red[0][tx]);
 }
 
+// the backward's time steps a thread walks: 64 (its halo of 3 + 3 rows costs less per step) when that still gives two
+// full waves of CTAs, else 32 or 16 (short sequences and few batch rows: more CTAs in flight)
+int tile_for(int B, int Tn, int C) {
+  const long long groups = (C / Vec<float>::V + kThreads - 1) / kThreads;
+  for (int L = 64; L > 16; L /= 2)
+    if (groups * B * ((Tn + L - 1) / L) >= kFillCTAs) return L;
+  return 16;
+}
+
 // tiles per row block and the number of row blocks (at most kMaxPartials with dw, else at most the grid's y limit)
-void plan(int B, int Tn, bool dw, int& tpb, int& P) {
-  const long long total = (long long)B * ((Tn + kTileB - 1) / kTileB);
+void plan(int B, int Tn, int tile, bool dw, int& tpb, int& P) {
+  const long long total = (long long)B * ((Tn + tile - 1) / tile);
   const long long cap = dw ? kMaxPartials : kMaxGridY;
   tpb = (int)((total + cap - 1) / cap);
   if (tpb < 1) tpb = 1;
@@ -386,13 +395,14 @@ int bwd_t(const void* x, const void* w, const void* dq, const void* dk, const fl
   constexpr int V = Vec<T>::V;
   const int groups = C / V;
   int tpb, P;
-  plan(B, Tn, dw != nullptr, tpb, P);
+  const int tile = tile_for(B, Tn, C);
+  plan(B, Tn, tile, dw != nullptr, tpb, P);
   dim3 grid((groups + kThreads - 1) / kThreads, P);
   float* part = static_cast<float*>(ws);
   auto launch = [&](auto kern) {
     kern<<<grid, kThreads, 0, st>>>(static_cast<const T*>(x), static_cast<const TW*>(w), static_cast<const T*>(dq),
                                     static_cast<const T*>(dk), dv, static_cast<T*>(dx), part, B, Tn, C, KD, DK, REP,
-                                    tpb);
+                                    tile, tpb);
   };
   if (dw == nullptr) {
     if (REP == 1) launch(conv_bwd_kernel<T, TW, false, 1>);
@@ -432,7 +442,7 @@ extern "C" {
 size_t gd_conv_workspace_bytes(int B, int T, int C) {
   if (B < 0 || T < 0 || C <= 0) return 0;
   int tpb, P;
-  plan(B, T, true, tpb, P);
+  plan(B, T, tile_for(B, T, C), true, tpb, P);
   return (size_t)P * C * 4 * sizeof(float);
 }
 

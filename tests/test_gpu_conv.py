@@ -84,7 +84,8 @@ def test_conv_path_trained_weight(model, dtype):
 
 
 def test_many_tiles_weight_gradient():
-    """More (row, 64-step tile) pairs than partial rows (256): each row block walks several tiles."""
+    """More (row, time tile) pairs than partial rows (256; 64-step tiles at this size): each row block walks several
+    tiles. The short cases above run 16-step tiles."""
     check("0.8b", 8, 2100, torch.bfloat16, True, seed=21)
 
 
