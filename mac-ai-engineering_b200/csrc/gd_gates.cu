@@ -140,30 +140,52 @@ __global__ void __launch_bounds__(kThreads) gates_fwd_kernel(const T* __restrict
   __shared__ float s_na[kSmemHeads], s_dt[kSmemHeads];
   stage_heads(alog, dtb, H, s_na, s_dt);
   const int groups = (n + 7) / 8, stride = gridDim.x * blockDim.x;
-  for (int gi = blockIdx.x * blockDim.x + threadIdx.x; gi < groups; gi += stride) {
-    const int i0 = 8 * gi;
+  // group i0 .. i0 + 7 from its loaded b, a
+  auto out8 = [&](int i0, const float (&vb)[8], const float (&va)[8]) {
+    float ob[8], og[8];
     int h = i0 % H;
-    if (vec && i0 + 8 <= n) {
-      float vb[8], va[8], ob[8], og[8];
-      ld8(b + i0, vb);
-      ld8(a + i0, va);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        float na, dt;
-        head_consts(alog, dtb, s_na, s_dt, h, na, dt);
-        ob[j] = sigmoid(vb[j]);
-        og[j] = na * softplus(va[j] + dt);
-        h = h + 1 == H ? 0 : h + 1;
-      }
-      st8(beta + i0, ob);
-      st8(g + i0, og);
+    for (int j = 0; j < 8; ++j) {
+      float na, dt;
+      head_consts(alog, dtb, s_na, s_dt, h, na, dt);
+      ob[j] = sigmoid(vb[j]);
+      og[j] = na * softplus(va[j] + dt);
+      h = h + 1 == H ? 0 : h + 1;
+    }
+    st8(beta + i0, ob);
+    st8(g + i0, og);
+  };
+  auto scalar = [&](int i0) {  // the tail group, or any group when the pointers are not 16-byte aligned
+    int h = i0 % H;
+    for (int i = i0; i < n && i < i0 + 8; ++i) {
+      float na, dt;
+      head_consts(alog, dtb, s_na, s_dt, h, na, dt);
+      beta[i] = sigmoid(ld(b, i));
+      g[i] = na * softplus(ld(a, i) + dt);
+      h = h + 1 == H ? 0 : h + 1;
+    }
+  };
+  // two groups a step (gi and gi + stride), their four 16-byte loads in flight before either is computed
+  for (int gi = blockIdx.x * blockDim.x + threadIdx.x; gi < groups; gi += 2 * stride) {
+    const int gj = gi + stride;
+    if (vec && 8 * gj + 8 <= n) {
+      float vb0[8], va0[8], vb1[8], va1[8];
+      ld8(b + 8 * gi, vb0);
+      ld8(a + 8 * gi, va0);
+      ld8(b + 8 * gj, vb1);
+      ld8(a + 8 * gj, va1);
+      out8(8 * gi, vb0, va0);
+      out8(8 * gj, vb1, va1);
     } else {
-      for (int i = i0; i < n && i < i0 + 8; ++i) {
-        float na, dt;
-        head_consts(alog, dtb, s_na, s_dt, h, na, dt);
-        beta[i] = sigmoid(ld(b, i));
-        g[i] = na * softplus(ld(a, i) + dt);
-        h = h + 1 == H ? 0 : h + 1;
+      for (int gk = gi; gk < groups && gk <= gj; gk += stride) {
+        if (vec && 8 * gk + 8 <= n) {
+          float vb[8], va[8];
+          ld8(b + 8 * gk, vb);
+          ld8(a + 8 * gk, va);
+          out8(8 * gk, vb, va);
+        } else {
+          scalar(8 * gk);
+        }
       }
     }
   }
