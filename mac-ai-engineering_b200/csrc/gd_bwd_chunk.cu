@@ -702,12 +702,14 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
         const float inv_qscale = 1.f / qscale;
         float x[16];
         epi_sync();  // the dg / dbeta threads are done with scr
+        GD_TRACE_AT(ws, lay, 32 * n + 24);
         if (norm) {
           row16<true>(qh, ql, dcol, tok0, x);
 #pragma unroll
           for (int j = 0; j < 16; ++j) x[j] *= inv_qscale * dQ[j];
           float s = warp_reduce_scatter16(x);
           if (lane < 16) dotq[(tok0 + lane) * 4 + qd] = s;
+          GD_TRACE_AT(ws, lay, 32 * n + 25);
           row16<true>(kh, kl, dcol, tok0, x);
 #pragma unroll
           for (int j = 0; j < 16; ++j) x[j] *= dK[j];
@@ -744,11 +746,13 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
             xk[j] = dK[j];
           }
         }
+        GD_TRACE_AT(ws, lay, 32 * n + 26);
         if constexpr (sizeof(T) == 2) {
           // dq, dk tiles as row-major [64 tokens][DK] in the q^T / k^T image buffers (every thread is done reading
           // them), then one tensor store each (rows past T are not written); the images' next fill waits for the
           // stores' reads (qk_free: warp 0 arrives after them)
           epi_sync();
+          GD_TRACE_AT(ws, lay, 32 * n + 27);
           T* sq = reinterpret_cast<T*>(smem + S::qk);
           T* sk = reinterpret_cast<T*>(smem + S::qk + DK * 64 * 2);
 #pragma unroll
@@ -757,7 +761,9 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
             sk[(tok0 + j) * DK + dcol] = cvt_out<T>(xk[j]);
           }
           fence_async_smem();
+          GD_TRACE_AT(ws, lay, 32 * n + 28);
           epi_sync();
+          GD_TRACE_AT(ws, lay, 32 * n + 29);
           if (tid == 0) {
             tma_store_4d(&tm_dq, 0, it.hk, t0, it.b, sq);
             tma_store_4d(&tm_dk, 0, it.hk, t0, it.b, sk);
