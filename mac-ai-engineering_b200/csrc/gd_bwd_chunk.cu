@@ -718,6 +718,19 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
         }
         epi_sync();
         GD_TRACE_AT(ws, lay, 32 * n + 21);
+        // per token, once: dx = a dy - b img with a = scale r, b = r <x_hat, dy> (img = scale x_hat, the q / k image):
+        // threads 0-63 the q tokens, 64-127 the k tokens, into the partial-sum area (read by the dg threads already)
+        float2* coef = reinterpret_cast<float2*>(part);  // [2][64]: q, then k
+        if (norm) {
+          if (tid < 128) {
+            const int t = tid & 63;
+            const bool isk = tid >= 64;
+            const float4 d4 = *reinterpret_cast<const float4*>((isk ? dotk : dotq) + 4 * t);
+            const float r = isk ? sRk[t] : sRq[t];
+            coef[tid] = make_float2(isk ? r : qscale * r, r * (d4.x + d4.y + d4.z + d4.w));
+          }
+          epi_sync();
+        }
         T* dq0 = dq + ((size_t)it.b * lay.T * lay.HK + it.hk) * DK;
         T* dk0 = dk + ((size_t)it.b * lay.T * lay.HK + it.hk) * DK;
         const int d0 = 32 * qd + 8 * (lane >> 3);
@@ -726,18 +739,14 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
           row16<true>(qh, ql, dcol, tok0, x);
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
-            const int i = tok0 + j;
-            const float4 d4 = *reinterpret_cast<const float4*>(dotq + 4 * i);
-            const float dot = d4.x + d4.y + d4.z + d4.w;
-            x[j] = qscale * sRq[i] * (dQ[j] - x[j] * inv_qscale * dot);
+            const float2 ab = coef[tok0 + j];
+            x[j] = fmaf(ab.x, dQ[j], -ab.y * x[j]);
           }
           row16<true>(kh, kl, dcol, tok0, xk);
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
-            const int i = tok0 + j;
-            const float4 d4 = *reinterpret_cast<const float4*>(dotk + 4 * i);
-            const float dot = d4.x + d4.y + d4.z + d4.w;
-            xk[j] = sRk[i] * (dK[j] - xk[j] * dot);
+            const float2 ab = coef[64 + tok0 + j];
+            xk[j] = fmaf(ab.x, dK[j], -ab.y * xk[j]);
           }
         } else {
 #pragma unroll
