@@ -64,12 +64,14 @@ struct ChunkSmem {
   static constexpr size_t scr = part + 6 * 4 * 64 * 4;      // fp32 [2][4][64] exchange scratch
   static constexpr size_t rqk = scr + 2 * 4 * 64 * 4;       // fp32 [2][64] the item's l2 rsqrt of q, k rows
   static constexpr size_t sl = rqk + 2 * 64 * 4;            // fp32 [2][32] <S_c, dS_{c+1}> partials (by parity)
-  static constexpr size_t bar = sl + 2 * 32 * 4;
+  static constexpr size_t tok = sl + 2 * 32 * 4;            // fp32 [3][64] the sub-item's gamma_t, e_t, beta_t gamma_t
+  static constexpr size_t bar = tok + 3 * 64 * 4;
   static constexpr int NBAR = 22;
   static constexpr size_t tmem = bar + NBAR * 8;
   static constexpr size_t total = tmem + 16;
   static_assert(dwt + DK * 64 * 2 <= in3, "dM and dW^T fit in the dVn region");
   static_assert(scr % 16 == 0, "scr is read as float4");
+  static_assert(total <= 232448, "within the 227 KB a CTA can have");
 };
 
 // partial-sum arrays (index into ChunkSmem::part): by TMEM lane quadrant [4][64] unless noted
@@ -441,6 +443,15 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
       if (!(ok = epi_all(ok))) break;
       tc_fence_after();
       GD_TRACE_AT(ws, lay, 32 * n + 0);
+      // the sub-item's per-token factors gamma_t = exp(G_t), e_t = exp(G_last - G_t), beta_t gamma_t, once (the
+      // phases read them after the next epilogue barrier)
+      float* sGam = reinterpret_cast<float*>(smem + S::tok);
+      if (tid < 64) {
+        const float gt = __expf(sG[tid]);
+        sGam[tid] = gt;
+        sGam[64 + tid] = __expf(sG[63] - sG[tid]);
+        sGam[128 + tid] = sB[tid] * gt;
+      }
       // dV rows: 16-bit outputs are staged row-major ([64 tokens][DV]) in the tail buffer (free until e2 writes dA)
       // and leave by one tensor store after the next barrier; fp32 rows are stored after the e1 hand-off (its proxy
       // fence would wait for global stores in flight)
@@ -489,7 +500,7 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
         tmem_ld16(tmem_lane_addr(B1, warp, tok0), av);
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
-          av[j] *= __expf(sG[tok0 + j]);  // gamma_t (dO S^T)_t
+          av[j] *= sGam[tok0 + j];  // gamma_t (dO S^T)_t
           dQ[j] += av[j];
         }
         tc_fence_before();
@@ -525,7 +536,7 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           const int i = tok0 + j;
-          dK[j] = fmaf(sB[i] * __expf(sG[i]), x[j], dK[j]);
+          dK[j] = fmaf(sGam[128 + i], x[j], dK[j]);  // beta_i gamma_i
           y[j] *= x[j];
         }
         const float s = warp_reduce_scatter16(y);
@@ -542,7 +553,7 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const int jj = c8 + j;
-          a10[j] = keep_if(sB[jj] * fmaf(__expf(sG[jj]), a10[j], a5[j]), jj < ri);
+          a10[j] = keep_if(sB[jj] * fmaf(sGam[jj], a10[j], a5[j]), jj < ri);
         }
         store8_bf16(smem + S::da, ri, c8, 64, a10);
         // dO Vn^T again and Q K^T: R's first term dM * (Q K^T) = (dO Vn^T) * (Q K^T) * Gamma
@@ -567,10 +578,9 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
         float x[16], y[16];
         tmem_ld16(tmem_lane_addr(B5, warp, tok0), x);
         row16<true>(kh, kl, dcol, tok0, y);
-        const float Gl = sG[63];
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
-          x[j] *= __expf(Gl - sG[tok0 + j]);
+          x[j] *= sGam[64 + tok0 + j];  // e_t
           dK[j] += x[j];
           y[j] *= x[j];
         }
@@ -663,7 +673,7 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
         const float* slp = reinterpret_cast<const float*>(smem + S::sl + (n & 1) * 128);
 #pragma unroll
         for (int w = 0; w < 32; ++w) sl += slp[w];
-        const float gt = __expf(sG[t]);
+        const float gt = sGam[t];
         const float w_ = sB[t] * gt * kx;
         const float db = fmaf(gt, kx, vy) + pk;
         // suffix sum of (a + w) over the chunk and exclusive prefix of E (two warps), without subtraction
@@ -683,7 +693,7 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
         asm volatile("bar.sync 2, 64;" ::: "memory");
         if (warp == 0) suf += xch[0];
         if (warp == 1) pre_excl += xch[1];
-        const float dgt = suf + __expf(sG[63]) * sl + pre_excl + rc;
+        const float dgt = suf + sGam[63] * sl + pre_excl + rc;
         const int tt = sp.t0 + t;
         if (tt < sp.end) {
           dg[((size_t)it.b * lay.Tin + tt) * lay.H + it.h] = dgt;
