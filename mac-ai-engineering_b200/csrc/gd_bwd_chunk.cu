@@ -456,6 +456,7 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
       // and leave by one tensor store after the next barrier; fp32 rows are stored after the e1 hand-off (its proxy
       // fence would wait for global stores in flight)
       float dvr[16];
+      float dec[8];  // exp(G_ri - G_j) for this thread's row ri, columns c8 .. c8 + 7: dM, R and dL all use it
       {
         float x[16];
         tmem_ld16(tmem_lane_addr(B3, warp, tok0), dvr);  // Y^T: v . Y, and dV = diag(beta) Y
@@ -484,7 +485,10 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
         tmem_ld8h(tmem_lane_addr(B0, warp, tok0), x);  // dO Vn^T -> dM
         const float Gi = sG[ri];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) x[j] = keep_if(x[j] * __expf(Gi - sG[c8 + j]), c8 + j <= ri);
+        for (int j = 0; j < 8; ++j) {
+          dec[j] = __expf(Gi - sG[c8 + j]);
+          x[j] = keep_if(x[j] * dec[j], c8 + j <= ri);
+        }
         store8_split(smem + S::dmh, smem + S::dml, ri, c8, 64, x);
       }
       GD_TRACE_AT(ws, lay, 32 * n + 1);
@@ -558,9 +562,8 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
         store8_bf16(smem + S::da, ri, c8, 64, a10);
         // dO Vn^T again and Q K^T: R's first term dM * (Q K^T) = (dO Vn^T) * (Q K^T) * Gamma
         tmem_ld8hx2(tmem_lane_addr(B0, warp, tok0), a5, tmem_lane_addr(B3, warp, tok0), a10);
-        const float Gi = sG[ri];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) rv[j] = keep_if(a5[j] * a10[j] * __expf(Gi - sG[c8 + j]), c8 + j < ri);
+        for (int j = 0; j < 8; ++j) rv[j] = keep_if(a5[j] * a10[j] * dec[j], c8 + j < ri);
       }
       GD_TRACE_AT(ws, lay, 32 * n + 7);
       tc_fence_before();
@@ -614,12 +617,12 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
         float x[8], kgrow[8];
         tmem_ld8hx2(tmem_lane_addr(B7, warp, tok0), x, tmem_lane_addr(B5, warp, tok0), kgrow);  // A^T T1, K K^T
         float pk = 0.f;
-        const float Gi = sG[ri], bi = sB[ri];
+        const float bi = sB[ri];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const bool in = c8 + j < ri;
           const float dl = -x[j];
-          const float gam = __expf(Gi - sG[c8 + j]);
+          const float gam = dec[j];
           const float p = keep_if(dl * gam, in);
           rv[j] = keep_if(dl * bi * kgrow[j] * gam, in);
           pk = fmaf(p, kgrow[j], pk);
