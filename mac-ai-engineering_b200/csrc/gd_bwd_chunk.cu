@@ -350,7 +350,7 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
           // the next sub-item's G1 after P11 (P11 is on the chain; G1 has the whole final phase to run)
           if (p11 && !g1n && mbar_test(in_full, par ^ 1) && mbar_test(a_full, par ^ 1)) {
             tc_fence_after();
-            issue_g1();  // the next sub-item's first products (B0-B4 were read before e2_done)
+            issue_g1();  // the next sub-item's first products (B1, B2, B4 were read before e2_done, B0, B3 before e4_done)
             g1n = progressed = true;
           }
           if (dl && kk && !p11 && mbar_test(e4_done, par)) {
@@ -550,7 +550,6 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
       ok = mbar_wait(g3_full, par, err, 89);
       if (!(ok = epi_all(ok))) break;
       tc_fence_after();
-      float rv[8];
       {
         float a10[8], a5[8];
         tmem_ld8hx2(tmem_lane_addr(B1, warp, tok0), a10, tmem_lane_addr(B4, warp, tok0), a5);  // dW K^T, dVn V^T
@@ -560,17 +559,12 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
           a10[j] = keep_if(sB[jj] * fmaf(sGam[jj], a10[j], a5[j]), jj < ri);
         }
         store8_bf16(smem + S::da, ri, c8, 64, a10);
-        // dO Vn^T again and Q K^T: R's first term dM * (Q K^T) = (dO Vn^T) * (Q K^T) * Gamma
-        tmem_ld8hx2(tmem_lane_addr(B0, warp, tok0), a5, tmem_lane_addr(B3, warp, tok0), a10);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) rv[j] = keep_if(a5[j] * a10[j] * dec[j], c8 + j < ri);
       }
       GD_TRACE_AT(ws, lay, 32 * n + 7);
       tc_fence_before();
       fence_async_smem();
       mbar_arrive_warp(e2_done);
       GD_TRACE_AT(ws, lay, 32 * n + 8);
-      rect(rv, true);
       GD_TRACE_AT(ws, lay, 32 * n + 9);
       // ---- eg2: (Vn dS^T)^T -> dK's decay-path term and the E partials
       ok = mbar_wait(g2_full, par, err, 84);
@@ -613,8 +607,14 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
       if (!(ok = epi_all(ok))) break;
       tc_fence_after();
       GD_TRACE_AT(ws, lay, 32 * n + 15);
+      // R = dM * (Q K^T) + dL * L (strictly lower), both terms summed here for one rect pass: R's first term from
+      // dO Vn^T and Q K^T (still in TMEM: the next sub-item's G1 overwrites them only after e4_done)
+      float rv[8];
       {
         float x[8], kgrow[8];
+        tmem_ld8hx2(tmem_lane_addr(B0, warp, tok0), x, tmem_lane_addr(B3, warp, tok0), kgrow);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) rv[j] = x[j] * kgrow[j] * dec[j];  // masked with the dL term below
         tmem_ld8hx2(tmem_lane_addr(B7, warp, tok0), x, tmem_lane_addr(B5, warp, tok0), kgrow);  // A^T T1, K K^T
         float pk = 0.f;
         const float bi = sB[ri];
@@ -624,7 +624,7 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
           const float dl = -x[j];
           const float gam = dec[j];
           const float p = keep_if(dl * gam, in);
-          rv[j] = keep_if(dl * bi * kgrow[j] * gam, in);
+          rv[j] = keep_if(fmaf(dl * bi, kgrow[j] * gam, rv[j]), in);
           pk = fmaf(p, kgrow[j], pk);
           x[j] = bi * p;
         }
@@ -636,7 +636,7 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
       fence_async_smem();
       mbar_arrive_warp(e4_done);
       GD_TRACE_AT(ws, lay, 32 * n + 16);
-      rect(rv, false);
+      rect(rv, true);
       GD_TRACE_AT(ws, lay, 32 * n + 17);
       // ---- final: dK's last term; dg and dbeta of this value head; dq / dk after the item's last value head
       float bnext = 0.f;  // the next sub-item's beta, fetched early (thread t alone reads and writes sB[t])
