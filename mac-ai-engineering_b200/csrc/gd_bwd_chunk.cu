@@ -14,7 +14,7 @@
 //   G1:  B0 dO Vn^T, B1 (dO S^T)^T, B2 (dVn S^T)^T, B3 (A^T dVn)^T (dVn split), B4 dVn V^T
 //   G3:  B6 (dM K)^T, B7 (dM^T Q)^T (dM, q and k split), B2 (A^T dW)^T (one commit), B1 dW K^T,
 //        B3 Q K^T (q and k split: M = Q K^T * Gamma in fp32 precision for R);   dW = -dVn S^T
-//   G2:  B5 (Vn dS^T)^T (Vn and dS split), then B5 K K^T (k split, for L and the dbeta term)
+//   G2:  B5 (Vn dS^T)^T (Vn and dS split); after e2: B1 K K^T (k split, for L and the dbeta term)
 //   tail: B6 T1 = dA A^T, B7 A^T T1 (dL = -A^T T1), B5 (K^T (P_beta + P_beta^T)) with P_beta = diag(beta) (dL * Gamma)
 // Equations: tools/check_chunk_equations.py:49-76 and src/macai/gated_delta/_chunked.py:20-34 of the reference; dg is
 // summed without cancellation (the regrouping of _chunked.py:1138-1142, extended to the decay-mask terms):
@@ -141,6 +141,39 @@ __device__ __forceinline__ Item item_of(const Layout& lay, int n) {
   return it;
 }
 
+// The sub-item after `it` without divisions (item_of's runtime divides, redone by every epilogue warp per sub-item,
+// cost hundreds of issue cycles): the grid stride gridDim.x as (chunk, key head, batch) digits, added with carries.
+struct ItemStep {
+  int dc, dhk, db;
+  __device__ explicit ItemStep(const Layout& lay) {
+    const int G = gridDim.x;
+    dc = G % lay.NT;
+    const int q = G / lay.NT;
+    dhk = q % lay.HK;
+    db = q / lay.HK;
+  }
+  __device__ __forceinline__ Item next(const Layout& lay, Item it) const {
+    if (it.r + 1 < lay.rep) {  // the key head's next value head
+      ++it.r;
+      ++it.h;
+      it.cidx += lay.NT;
+      return it;
+    }
+    it.r = 0;
+    it.c += dc;  // c, dc < NT and hk, dhk < HK: one carry each at most
+    int carry = it.c >= lay.NT;
+    if (carry) it.c -= lay.NT;
+    it.hk += dhk + carry;
+    carry = it.hk >= lay.HK;
+    if (carry) it.hk -= lay.HK;
+    it.b += db + carry;
+    it.h = it.hk * lay.rep;
+    it.cidx0 = ((size_t)it.b * lay.H + it.h) * lay.NT + it.c;
+    it.cidx = it.cidx0;
+    return it;
+  }
+};
+
 template <typename T, int DK, int DV>
 __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__ qraw, const T* __restrict__ kraw,
                                                            const float* __restrict__ beta, T* __restrict__ dq,
@@ -174,7 +207,6 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
   uint64_t* epi_done = bars + 15;  // [2] by sub-item parity
   uint64_t* drain = bars + 17;
   uint64_t* qk_free = bars + 18;   // 16 epilogue warps, once per item
-  uint64_t* eg2_done = bars + 19;  // 16 epilogue warps: (Vn dS^T)^T read
   uint64_t* kk_full = bars + 20;   // MMA commit: K K^T
   uint64_t* g3a_full = bars + 21;  // MMA commit: the first part of G3 (B6, B7, B2)
   uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + S::tmem);
@@ -182,6 +214,7 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
   const int NG = lay.B * lay.HK * lay.NT;
   const int nsub = ((NG - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x) * lay.rep;
 
+  GD_TRACE_CTA(ws, lay, 0);
   if (warp == 0) {
     tmem_alloc(tslot, 512);
     tmem_relinquish();
@@ -191,7 +224,6 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
     for (int i = 10; i < 17; ++i) mbar_init(bars + i, 16);
     mbar_init(drain, 1);
     mbar_init(qk_free, 16);
-    mbar_init(eg2_done, 16);
     mbar_init(kk_full, 1);
     mbar_init(g3a_full, 1);
     fence_mbar_init();
@@ -220,11 +252,13 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
         if (n >= 1) ok = mbar_wait(g3_full, (n - 1) & 1, err, 60);  // dM / dW^T (the IN2 region) consumed
         if (!ok) break;
         mbar_arrive_expect_tx(in_full, in_bytes);
+        GD_TRACE_ONE(ws, lay, 3500 + 4 * n + 0);
         last_in = n;
         bulk_g2s(smem + S::in2, ws + lay.dvni + it.cidx * lay.vn_bytes(), (uint32_t)lay.vn_bytes(), in_full);
         if (n >= 1) ok = mbar_wait(g2_full, (n - 1) & 1, err, 61);                // dS^T and Vn^T consumed
         if (ok && n >= 2) ok = mbar_wait(epi_done + (n & 1), ((n - 2) >> 1) & 1, err, 62);  // G buffer n & 1 read
         if (!ok) break;
+        GD_TRACE_ONE(ws, lay, 3500 + 4 * n + 1);
         bulk_g2s(smem + S::sc, ws + lay.sci + it.cidx * lay.si_bytes(), (uint32_t)lay.si_bytes(), in_full);
         bulk_g2s(smem + S::dO, ws + lay.doi + it.cidx * lay.vi_bytes(), (uint32_t)lay.vi_bytes(), in_full);
         bulk_g2s(smem + S::vt, ws + lay.vi + it.cidx * lay.vi_bytes(), (uint32_t)lay.vi_bytes(), in_full);
@@ -235,6 +269,7 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
         if (n >= 1) ok = mbar_wait(dl_full, (n - 1) & 1, err, 63);  // A consumed
         if (!ok) break;
         mbar_arrive_expect_tx(a_full, (uint32_t)lay.m_bytes());
+        GD_TRACE_ONE(ws, lay, 3500 + 4 * n + 2);
         last_a = n;
         bulk_g2s(smem + S::a, ws + lay.ai + it.cidx * lay.m_bytes(), (uint32_t)lay.m_bytes(), a_full);
         if (it.r == 0) {
@@ -242,6 +277,7 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
           if (m >= 1) ok = mbar_wait(qk_free, (m - 1) & 1, err, 64);  // the previous item's q / k consumed
           if (!ok) break;
           mbar_arrive_expect_tx(qk_full, 2 * (uint32_t)lay.qk_bytes() + 2 * 256);
+          GD_TRACE_ONE(ws, lay, 3500 + 4 * n + 3);
           last_qk = m;
           bulk_g2s(smem + S::qk, ws + lay.qk + it.cidx0 * lay.qk_bytes(), (uint32_t)lay.qk_bytes(), qk_full);
           bulk_g2s(smem + S::qkl, ws + lay.qkl + it.cidx0 * lay.qk_bytes(), (uint32_t)lay.qk_bytes(), qk_full);
@@ -252,6 +288,7 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
         ok = mbar_wait(e1_done, n & 1, err, 65);  // S_c^T, dO, V^T consumed (G1 and e1): dS^T goes over them
         if (!ok) break;
         mbar_arrive_expect_tx(ds_full, 2 * (uint32_t)lay.si_bytes());
+        GD_TRACE_ONE(ws, lay, 3900 + n);
         last_ds = n;
         bulk_g2s(smem + S::dsh, ws + lay.dsi + it.cidx * 2 * lay.si_bytes(), 2 * (uint32_t)lay.si_bytes(), ds_full);
       }
@@ -292,7 +329,9 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
       if (ok) ok = mbar_wait(in_full, 0, err, 70) && mbar_wait(a_full, 0, err, 71);
       if (ok) {
         tc_fence_after();
+        GD_TRACE_ONE(ws, lay, 3000);
         issue_g1();
+        GD_TRACE_ONE(ws, lay, 3000 + 7);
       }
       for (int n = 0; n < nsub && ok; ++n) {
         const uint32_t par = n & 1;
@@ -303,6 +342,7 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
           bool progressed = false;
           if (!g3 && mbar_test(e1_done, par) && mbar_test(qk_full, qpar)) {
             tc_fence_after();
+            GD_TRACE_ONE(ws, lay, 3000 + 8 * n + 1);
             mma_tiles(B6, DK, 64, 64, tK, true, 0, 0, tDmh, false, 0, false);    // (dM K)^T = K^T dM^T
             mma_tiles(B6, DK, 64, 64, tKl, true, 0, 0, tDmh, false, 0, true);
             mma_tiles(B6, DK, 64, 64, tK, true, 0, 0, tDml, false, 0, true);
@@ -316,33 +356,41 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
             mma_tiles(B3, 64, 64, DK, tQ, false, 0, 0, tKl, true, 0, true);
             mma_tiles(B3, 64, 64, DK, tQl, false, 0, 0, tK, true, 0, true);
             mma_commit(g3_full);
+            GD_TRACE_ONE(ws, lay, 3300 + 8 * n + 1);
             g3 = progressed = true;
           }
           // G2 after G3: its result is read after G3's
           if (g3 && !g2 && mbar_test(ds_full, par) && (n == 0 || mbar_test(b5_free, (n - 1) & 1))) {
             tc_fence_after();
+            GD_TRACE_ONE(ws, lay, 3000 + 8 * n + 2);
             mma_tiles(B5, DK, 64, DV, tDsh, false, 0, 0, tVnh, true, 0, false);  // (Vn dS^T)^T = dS Vn^T
             mma_tiles(B5, DK, 64, DV, tDsh, false, 0, 0, tVnl, true, 0, true);
             mma_tiles(B5, DK, 64, DV, tDsl, false, 0, 0, tVnh, true, 0, true);
             mma_commit(g2_full);
+            GD_TRACE_ONE(ws, lay, 3300 + 8 * n + 2);
             g2 = progressed = true;
-          }
-          if (g2 && g3 && !kk && mbar_test(eg2_done, par)) {
-            tc_fence_after();
-            mma_tiles(B5, 64, 64, DK, tK, false, 0, 0, tK, true, 0, false);      // K K^T
-            mma_tiles(B5, 64, 64, DK, tK, false, 0, 0, tKl, true, 0, true);
-            mma_tiles(B5, 64, 64, DK, tKl, false, 0, 0, tK, true, 0, true);
-            mma_commit(kk_full);
-            kk = progressed = true;
           }
           if (g3 && !t1 && mbar_test(e2_done, par)) {
             tc_fence_after();
+            GD_TRACE_ONE(ws, lay, 3000 + 8 * n + 4);
             mma_tiles(B6, 64, 64, 64, tDa, true, 0, 0, tA, false, 0, false);     // T1 = dA A^T
             mma_commit(t1_full);
             t1 = progressed = true;
           }
+          // K K^T into B1 (free from e2_done until the next sub-item's G1) right behind T1, so that dL, on the chain
+          // to e4, is issued as soon as e3 is done
+          if (t1 && !kk) {
+            tc_fence_after();
+            GD_TRACE_ONE(ws, lay, 3000 + 8 * n + 3);
+            mma_tiles(B1, 64, 64, DK, tK, false, 0, 0, tK, true, 0, false);      // K K^T
+            mma_tiles(B1, 64, 64, DK, tK, false, 0, 0, tKl, true, 0, true);
+            mma_tiles(B1, 64, 64, DK, tKl, false, 0, 0, tK, true, 0, true);
+            mma_commit(kk_full);
+            kk = progressed = true;
+          }
           if (t1 && !dl && mbar_test(e3_done, par)) {
             tc_fence_after();
+            GD_TRACE_ONE(ws, lay, 3000 + 8 * n + 5);
             mma_tiles(B7, 64, 64, 64, tA, false, 0, 0, tT1, true, 0, false);     // A^T T1
             mma_commit(dl_full);
             dl = progressed = true;
@@ -350,11 +398,14 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
           // the next sub-item's G1 after P11 (P11 is on the chain; G1 has the whole final phase to run)
           if (p11 && !g1n && mbar_test(in_full, par ^ 1) && mbar_test(a_full, par ^ 1)) {
             tc_fence_after();
-            issue_g1();  // the next sub-item's first products (B1, B2, B4 were read before e2_done, B0, B3 before e4_done)
+            GD_TRACE_ONE(ws, lay, 3000 + 8 * (n + 1));
+            issue_g1();  // the next sub-item's first products (B2, B4 were read before e2_done, B0, B1, B3 before e4_done)
+            GD_TRACE_ONE(ws, lay, 3000 + 8 * (n + 1) + 7);
             g1n = progressed = true;
           }
           if (dl && kk && !p11 && mbar_test(e4_done, par)) {
             tc_fence_after();
+            GD_TRACE_ONE(ws, lay, 3000 + 8 * n + 6);
             mma_tiles(B5, DK, 64, 64, tK, true, 0, 0, tDa, true, 0, false);      // K^T P_beta
             mma_tiles(B5, DK, 64, 64, tK, true, 0, 0, tDa, false, 0, true);      //  + K^T P_beta^T
             mma_commit(p11_full);
@@ -432,14 +483,19 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
     }
     epi_sync();
     bool ok = true;
+    const ItemStep istep(lay);
+    Item nx = item_of(lay, 0);
     for (int n = 0; n < nsub; ++n) {
-      const Item it = item_of(lay, n);
+      const Item it = nx;
+      nx = istep.next(lay, it);  // read only while n + 1 < nsub
       const uint32_t par = n & 1;
       const int t0 = it.c * C;                    // the chunk's first row of dq, dk, dv (chunk-aligned)
       const ChunkSpan sp = lay.span(ws, it.c);  // its rows of beta, dg, dbeta (the caller's rows)
       const float* sG = reinterpret_cast<const float*>(smem + S::g + (n & 1) * 256);
       // ---- e1: dV and the vy partials, dW^T and dM tiles, dQ's first term and the a partials
-      ok = mbar_wait(in_full, par, err, 80) && mbar_wait(g1_full, par, err, 81);
+      ok = mbar_wait(in_full, par, err, 80);
+      GD_TRACE_AT(ws, lay, 32 * n + 30);
+      ok = ok && mbar_wait(g1_full, par, err, 81);
       if (!(ok = epi_all(ok))) break;
       tc_fence_after();
       GD_TRACE_AT(ws, lay, 32 * n + 0);
@@ -581,8 +637,6 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
           dK[j] += x[j];
           y[j] *= x[j];
         }
-        tc_fence_before();
-        mbar_arrive_warp(eg2_done);  // B5 may take K K^T
         const float s = warp_reduce_scatter16(y);
         if (lane < 16) P(P_E, qd, tok0 + lane) = s;
       }
@@ -615,7 +669,7 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
         tmem_ld8hx2(tmem_lane_addr(B0, warp, tok0), x, tmem_lane_addr(B3, warp, tok0), kgrow);
 #pragma unroll
         for (int j = 0; j < 8; ++j) rv[j] = x[j] * kgrow[j] * dec[j];  // masked with the dL term below
-        tmem_ld8hx2(tmem_lane_addr(B7, warp, tok0), x, tmem_lane_addr(B5, warp, tok0), kgrow);  // A^T T1, K K^T
+        tmem_ld8hx2(tmem_lane_addr(B7, warp, tok0), x, tmem_lane_addr(B1, warp, tok0), kgrow);  // A^T T1, K K^T
         float pk = 0.f;
         const float bi = sB[ri];
 #pragma unroll
@@ -641,7 +695,6 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
       // ---- final: dK's last term; dg and dbeta of this value head; dq / dk after the item's last value head
       float bnext = 0.f;  // the next sub-item's beta, fetched early (thread t alone reads and writes sB[t])
       if (n + 1 < nsub && tid < 64) {
-        const Item nx = item_of(lay, n + 1);
         const ChunkSpan nsp = lay.span(ws, nx.c);
         const int t = nsp.t0 + tid;
         if (t < nsp.end) bnext = beta[((size_t)nx.b * lay.Tin + t) * lay.H + nx.h];
@@ -813,6 +866,7 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
     tc_fence_after();
     tmem_dealloc(tm, 512);
   }
+  GD_TRACE_CTA(ws, lay, 1);
 }
 
 template <typename T, int DK, int DV>
