@@ -4,13 +4,19 @@
 
 One step = the forward (o, S_T) and the backward (dq, dk, dv, dg, dbeta, ds0; chunk states recomputed) of one batch of
 the configuration through the library's C ABI (include/gated_delta_b200.h: gd_forward + gd_backward), captured once in
-a CUDA graph. The headline metric is BASELINE.json's: tokens/s (tokens = B * T) for forward + backward at config 1
-(B=4, T=1024, H=16, dk=dv=128, bf16, chunk 64, l2-normalised q/k). Inputs are seeded synthetic tensors with the
-distributions of BASELINE.json configs[0].
+a CUDA graph. The headline metric: tokens/s (tokens = B * T) for forward + backward at config 1 (B=4, T=1024, H=16,
+dk=dv=128, bf16, chunk 64, l2-normalised q/k). Inputs are seeded synthetic tensors: q, k, v ~ N(0, 1),
+beta = sigmoid(N(0, 1)), g = -exp(U(log 1, log 16)) * softplus(N(0, 1)), dO ~ N(0, 1).
 
-Multi-GPU (torchrun, one process per GPU): weak scaling over independent (batch, head) slices. Every rank owns
-config 1's B batch rows of a global batch of N * B rows; there is no collective on the data path. The time is the
-maximum over ranks of the device time (CUDA events), taken with an NCCL all-reduce(max) after the timed region.
+Multi-GPU (torchrun, one process per GPU): the headline is weak scaling over independent (batch, head) slices. Every
+rank owns config 1's B batch rows of a global batch of N * B rows; there is no collective on the data path. The time
+is the maximum over ranks of the device time (CUDA events), taken with an NCCL all-reduce(max) after the timed region.
+Two sharded legs ride along (keys "c3" and "c4"; also at N = 1, as their one-GPU points):
+  c4  B=64, T=4096, H=32 forward + backward, batch rows split over the ranks (64 / N each; strong scaling), plus a
+      bit-identity check: one row of every rank's gradients, gathered (NCCL), against the same rows computed in one
+      call on rank 0's GPU;
+  c3  B=1, T=32768, H=32 forward, heads split over the ranks (32 / N each; strong scaling), the final states gathered
+      by NCCL all_gather_into_tensor inside the timed region.
 
 Printed (rank 0), one JSON line:
   value        whole-job tokens/s with inputs resident in HBM (sum of per-step device times; L2 flushed between steps)
@@ -39,8 +45,7 @@ sys.path.insert(0, os.path.join(ROOT, "mac-ai-engineering_b200"))
 sys.path.insert(0, ROOT)
 
 METRIC = "gated-delta fwd+bwd tokens/s (B4 T1024 H16 d128 bf16)"
-# the reference's own published number for this shape and pass (Apple M3 Max, Metal; not re-measurable
-# here): 10.210 ms fwd+bwd at B4 T1024 H16 -> 401,175 tokens/s (docs/series_layer.md:1679-1684 of the reference)
+# the reference's own published number for this shape and pass (Apple M3 Max, Metal; not re-measurable here): 10.210 ms fwd+bwd at B4 T1024 H16 -> 401,175 tokens/s (docs/series_layer.md:1679-1684 of the reference)
 PUBLISHED_TOKENS_S = 4 * 1024 / 10.210e-3
 CONFIGS = {
     # name: (B, T, H value heads, HK key heads, D, with s0 / final state, forward only)
@@ -65,7 +70,7 @@ def peaks():
 
 
 def synthetic(cfg, device, seed):
-    """BASELINE.json configs[0] distributions: q, k, v ~ N(0,1) (bf16); beta = sigmoid(N(0,1));
+    """The configurations' input distributions: q, k, v ~ N(0,1) (bf16); beta = sigmoid(N(0,1));
     g = -exp(U(log 1, log 16)) * softplus(N(0,1)); dO ~ N(0,1) (bf16); s0 ~ N(0, 0.02)."""
     import torch
     B, T, H, HK, D = cfg["B"], cfg["T"], cfg["H"], cfg["HK"], cfg["D"]
@@ -171,19 +176,56 @@ def cpu_reference(cfg, steps, warmup, sample_batch=1, threads=None):
             "seconds_per_sample": med}
 
 
+def cpu_config0(steps=5, warmup=1, threads=None):
+    """Config 0, the reference's CPU run: transformers' torch_chunk_gated_delta_rule forward only, fp32, B=1, T=256,
+    H=4, dk=dv=64, chunk 64, l2-normalised q/k, no initial state, on this host's cores. (The B200 kernels are built for
+    head width 128, so this configuration is a CPU-side timing only.)"""
+    import torch
+    from oracle import transformers_ref
+    if threads:
+        torch.set_num_threads(threads)
+    gen = torch.Generator().manual_seed(0)
+    B, T, H, D = 1, 256, 4, 64
+    q, k, v = (torch.randn(B, T, H, D, generator=gen) for _ in range(3))
+    beta = torch.sigmoid(torch.randn(B, T, H, generator=gen))
+    g = -torch.exp(torch.rand(B, T, H, generator=gen) * math.log(16.0)) * torch.nn.functional.softplus(
+        torch.randn(B, T, H, generator=gen))
+    f = transformers_ref.rule()
+    times = []
+    with torch.no_grad():
+        for i in range(warmup + steps):
+            t0 = time.perf_counter()
+            f(q, k, v, g, beta, chunk_size=64, initial_state=None, output_final_state=False,
+              use_qk_l2norm_in_kernel=True)
+            if i >= warmup:
+                times.append(time.perf_counter() - t0)
+    med = statistics.median(times)
+    return {"workload": "c0: B1 T256 H4 d64 fp32 forward (CPU only)", "ms": med * 1e3,
+            "tokens_per_s": B * T / med, "cores": torch.get_num_threads(),
+            "kind": "reference (transformers torch_chunk_gated_delta_rule)", "steps": steps}
+
+
 def run_reference(args, cfg):
+    """The reference arm: transformers' torch_chunk_gated_delta_rule (the reference torch implementation the drop-in
+    replaces) on this host's cores with every thread, on the full configuration (all B batch rows: the same workload
+    as the B200 arm), each step one forward + backward; plus config 0's CPU forward as an extra key. Under torchrun
+    rank 0 alone runs and prints; the other ranks exit without work."""
     import torch
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     threads = os.cpu_count()
-    res = cpu_reference(cfg, steps=args.steps, warmup=max(1, min(args.warmup, 2)), threads=threads)
+    res = cpu_reference(cfg, steps=args.steps, warmup=max(1, min(args.warmup, 2)), sample_batch=cfg["B"],
+                        threads=threads)
+    c0 = cpu_config0(threads=threads)
     line = {"impl": "reference", "metric": METRIC if args.config == 1 else f"gated-delta tokens/s ({cfg['tag']})",
             "value": res["value"], "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": res["seconds_per_sample"] * 1e3, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (BASELINE configs[0] "
-            "distributions)", "config": {"workload": cfg["tag"], "sample": res["sample"]},
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (the configurations' seeded "
+            "input distributions)", "config": {"workload": cfg["tag"], "sample": res["sample"],
+                                               "same_config": True},
             "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "cpu_config0": c0,
             "e2e": {"value": res["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -197,6 +239,7 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--no-shard", action="store_true", help="skip the sharded config 3 / config 4 legs")
     ap.add_argument("--profile", action="store_true",
                     help="profiling case for ncu: --steps plain forward+backward calls through the C ABI (no graph, "
                          "no timing, no CPU baseline), then exit; launch order per step: prep, state, prep, state "
@@ -341,11 +384,19 @@ def main():
         dist.all_reduce(e2, op=dist.ReduceOp.MAX)
         e2e["seconds"] = e2.item()
     e2e_value = tokens_per_step * e2e["steps"] / e2e["seconds"]
+    floor_s = _max_over_ranks(e2e["copy_floor_seconds"], dev, world)
 
-    cpu = None
+    # ---- the sharded configurations (strong scaling over the ranks; their one-GPU points at N = 1)
+    c3 = c4 = None
+    if not args.no_shard and args.config == 1:
+        c4 = sharded_c4(lib, dev, rank, world, steps=min(args.steps, 5), warmup=3, flush=flush)
+        c3 = sharded_c3(lib, dev, rank, world, steps=min(args.steps, 10), warmup=3, flush=flush)
+
+    cpu = cpu0 = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_reference(cfg, steps=3, warmup=1, threads=os.cpu_count())
+        cpu = cpu_reference(cfg, steps=3, warmup=1, sample_batch=cfg["B"], threads=os.cpu_count())
         cpu = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        cpu0 = cpu_config0(threads=os.cpu_count())
 
     step_flops = (FLOP_FWD + (0 if cfg["fwd_only"] else FLOP_BWD)) * B * T * H
     step_bytes = (BYTES_FWD + (0 if cfg["fwd_only"] else BYTES_BWD)) * B * T * H
@@ -356,7 +407,8 @@ def main():
             "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": total_s * 1e3 / args.steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": (value / PUBLISHED_TOKENS_S) if args.config == 1 else None,
-            "dtype": "bf16", "data": "synthetic (BASELINE configs[0] distributions, seeded per rank)",
+            "dtype": "bf16", "data": "synthetic (seeded per rank: q, k, v, dO ~ N(0,1); beta = sigmoid(N(0,1)); "
+                                                 "g = -exp(U(0, log 16)) softplus(N(0,1)))",
             "config": {"workload": cfg["tag"], "global_batch": B * world, "seq_len": T, "heads": H,
                        "key_heads": HK, "head_dim": D, "chunk": 64, "parallelism": f"dp{world} over (batch, head)",
                        "l2": "flushed between steps (256 MiB write, outside the per-step events)",
@@ -375,8 +427,14 @@ def main():
             "gated_norm": gnorm,
             "conv": conv,
             "cpu_baseline": cpu,
+            "cpu_config0": cpu0,
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": e2e["h2d"],
-                    "d2h_bytes_per_step": e2e["d2h"], "ms_per_step": e2e["seconds"] * 1e3 / e2e["steps"]},
+                    "d2h_bytes_per_step": e2e["d2h"], "ms_per_step": e2e["seconds"] * 1e3 / e2e["steps"],
+                    "copy_floor_ms": floor_s * 1e3 / e2e["steps"],
+                    "copy_floor": "the same pipelined host<->device copies with no compute (both directions at once, "
+                                  "max over ranks)", "numa_node": e2e["numa"]},
+            "c3": c3,
+            "c4": c4,
             "gpu_launches": kernels_per_step * args.steps,
             "clocks": clocks.summary(),
         }
@@ -385,6 +443,229 @@ def main():
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def slice_inputs(cfg, dev, sl, seed, fwd_only):
+    """Inputs of one rank's slice (shard.Slice) of a configuration, each (batch row, key head) unit seeded on its own
+    (seed + 1000 b + hk), so that every rank, and a one-GPU run of any subset of rows, builds the same values. A unit
+    holds its key head's q, k and the rep value heads it serves (v, g, beta, dO), with the distributions of
+    `synthetic`."""
+    import torch
+    T, H, HK, D = cfg["T"], cfg["H"], cfg["HK"], cfg["D"]
+    rep = H // HK
+    return unit_inputs(T, D, rep, range(sl.b0, sl.b1), range(sl.hk0, sl.hk1), dev, seed, fwd_only)
+
+
+def unit_inputs(T, D, rep, rows, key_heads, dev, seed, fwd_only):
+    """q, k [len(rows), T, len(key_heads), D] bf16, v / dO [.., rep * len(key_heads), D] bf16, g / beta fp32 for the
+    listed global batch rows and key heads (the unit seeding of slice_inputs)."""
+    import torch
+    nb, nk = len(rows), len(key_heads)
+    bf = torch.bfloat16
+    t = {"q": torch.empty(nb, T, nk, D, dtype=bf, device=dev), "k": torch.empty(nb, T, nk, D, dtype=bf, device=dev),
+         "v": torch.empty(nb, T, nk * rep, D, dtype=bf, device=dev),
+         "g": torch.empty(nb, T, nk * rep, device=dev), "beta": torch.empty(nb, T, nk * rep, device=dev),
+         "do": None if fwd_only else torch.empty(nb, T, nk * rep, D, dtype=bf, device=dev)}
+    for i, b in enumerate(rows):
+        for j, hk in enumerate(key_heads):
+            gen = torch.Generator(device=dev).manual_seed(seed + 1000 * b + hk)
+            hs = slice(j * rep, (j + 1) * rep)
+            t["q"][i, :, j] = torch.randn(T, D, generator=gen, device=dev).to(bf)
+            t["k"][i, :, j] = torch.randn(T, D, generator=gen, device=dev).to(bf)
+            t["v"][i, :, hs] = torch.randn(T, rep, D, generator=gen, device=dev).to(bf)
+            t["beta"][i, :, hs] = torch.sigmoid(torch.randn(T, rep, generator=gen, device=dev))
+            t["g"][i, :, hs] = (-torch.exp(torch.rand(T, rep, generator=gen, device=dev) * math.log(16.0))
+                                * torch.nn.functional.softplus(torch.randn(T, rep, generator=gen, device=dev)))
+            if not fwd_only:
+                t["do"][i, :, hs] = torch.randn(T, rep, D, generator=gen, device=dev).to(bf)
+    return t
+
+
+def _same_bits(a, b):
+    """Bitwise equality of two tensors of one dtype and shape (NaNs included)."""
+    import torch
+    ints = {torch.float32: torch.int32, torch.bfloat16: torch.int16, torch.float16: torch.int16}
+    return a.shape == b.shape and a.dtype == b.dtype and bool(torch.equal(a.view(ints[a.dtype]),
+                                                                           b.view(ints[b.dtype])))
+
+
+def _max_over_ranks(x, dev, world):
+    import torch
+    import torch.distributed as dist
+    v = torch.tensor([float(x)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(v, op=dist.ReduceOp.MAX)
+    return v.item()
+
+
+def sharded_c4(lib, dev, rank, world, steps, warmup, flush):
+    """Config 4 (B=64, T=4096, H=32, forward + backward) with its batch rows split over the ranks (strong scaling:
+    the job's 262,144 tokens are fixed, each rank computes 64 / N rows through the C ABI, no collective on the data
+    path). Timed as the headline: CUDA graph, L2 flushed between steps, barrier + synchronise around the timed region,
+    device time maximum over ranks. Then the bit-identity check: every rank's first row of dq, dk, dv, dg, dbeta is
+    gathered (NCCL all_gather_into_tensor) and rank 0 computes the same rows (built from the same unit seeds) in one
+    call of its own; they must be the same bits."""
+    import torch
+    import torch.distributed as dist
+    from macai_b200 import _lib
+    from macai_b200.gated_delta import shard
+    cfg = CONFIGS[4]
+    B, T, H, HK, D = cfg["B"], cfg["T"], cfg["H"], cfg["HK"], cfg["D"]
+    sl = shard.partition(B, H, HK, world, rank)
+    assert sl.dim == 0, "config 4 splits batch rows"
+    P = lambda x: None if x is None else ctypes.c_void_p(x.data_ptr())
+    BF, flags = _lib.GD_BFLOAT16, _lib.GD_L2NORM | _lib.GD_SCALE_Q
+    stream = torch.cuda.Stream(device=dev)
+    sp = ctypes.c_void_p(stream.cuda_stream)
+
+    def buffers(t, nb):
+        o = torch.empty(nb, T, H, D, dtype=torch.bfloat16, device=dev)
+        grads = [torch.empty_like(t["q"]), torch.empty_like(t["k"]), torch.empty_like(t["v"]),
+                 torch.empty(nb, T, H, device=dev), torch.empty(nb, T, H, device=dev)]
+        nbytes = lib.gd_workspace_bytes(nb, T, H, HK, D, D, 1)
+        return o, grads, torch.empty(nbytes, dtype=torch.uint8, device=dev), nbytes
+
+    def step_fn(t, nb, o, grads, ws, nbytes):
+        def step():
+            _lib.check(lib.gd_forward(P(t["q"]), P(t["k"]), P(t["v"]), P(t["g"]), P(t["beta"]), None, P(o), None, BF,
+                                      nb, T, H, HK, D, D, flags, P(ws), nbytes, sp), "gd_forward")
+            _lib.check(lib.gd_backward(P(t["q"]), P(t["k"]), P(t["v"]), P(t["g"]), P(t["beta"]), None, P(t["do"]),
+                                       None, *[P(x) for x in grads], None, BF, nb, T, H, HK, D, D, flags, P(ws),
+                                       nbytes, sp), "gd_backward")
+        return step
+
+    nb = sl.b1 - sl.b0
+    t = slice_inputs(cfg, dev, sl, 4000, False)
+    o, grads, ws, nbytes = buffers(t, nb)
+    step = step_fn(t, nb, o, grads, ws, nbytes)
+    with torch.cuda.stream(stream):
+        step()
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step()
+    with torch.cuda.stream(stream):
+        for _ in range(warmup):
+            flush.zero_()
+            graph.replay()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    with torch.cuda.stream(stream):
+        for e0, e1 in evs:
+            flush.zero_()
+            e0.record(stream)
+            graph.replay()
+            e1.record(stream)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    ms = _max_over_ranks(sum(a.elapsed_time(b) for a, b in evs) / steps, dev, world)
+    code = lib.gd_read_error(P(ws), sp, None)
+    del graph
+    # bit identity of the sharded gradients against one call over the same rows
+    firsts = [shard.partition(B, H, HK, world, r).b0 for r in range(world)]
+    mine = [x[0:1].contiguous() for x in grads]
+    gathered = []
+    for x in mine:
+        buf = torch.empty((world,) + tuple(x.shape[1:]), dtype=x.dtype, device=dev)
+        if world > 1:
+            dist.all_gather_into_tensor(buf, x)
+        else:
+            buf.copy_(x)
+        gathered.append(buf)
+    torch.cuda.synchronize(dev)
+    del t, o, grads, ws
+    identical = None
+    if rank == 0:
+        t1 = unit_inputs(T, D, H // HK, firsts, range(HK), dev, 4000, False)
+        o1, g1, ws1, nb1 = buffers(t1, world)
+        with torch.cuda.stream(stream):
+            step_fn(t1, world, o1, g1, ws1, nb1)()
+        stream.synchronize()
+        identical = all(_same_bits(a, b) for a, b in zip(gathered, g1))
+        del t1, o1, g1, ws1
+    torch.cuda.empty_cache()
+    tokens = B * T
+    return {"workload": "c4: B64 T4096 H32 d128 fwd+bwd, batch rows split over the ranks (strong scaling)",
+            "rows_per_rank": nb, "ms_per_step": ms, "tokens_per_s": tokens / (ms / 1e3), "steps": steps,
+            "l2": "inputs above L2 and flushed between steps", "device_status": code,
+            "bit_identical_vs_one_gpu": identical,
+            "identity_rows": firsts, "collective": "none on the data path; the identity check gathers one row of "
+                                                   "dq/dk/dv/dg/dbeta per rank after timing"}
+
+
+def sharded_c3(lib, dev, rank, world, steps, warmup, flush):
+    """Config 3 (B=1, T=32768, H=32, forward with the final state) with its heads split over the ranks (strong
+    scaling: 32 / N heads each), the final states [1, 32, 128, 128] fp32 gathered into every rank by NCCL
+    all_gather_into_tensor inside the timed region. Per step (L2 flushed before): the forward through the C ABI,
+    then the gather; device time (CUDA events on the launching stream, which the collective joins) maximum over
+    ranks, also split into the forward and the gather, so the curve's limit can be named."""
+    import torch
+    import torch.distributed as dist
+    from macai_b200 import _lib
+    from macai_b200.gated_delta import shard
+    cfg = CONFIGS[3]
+    B, T, H, HK, D = cfg["B"], cfg["T"], cfg["H"], cfg["HK"], cfg["D"]
+    sl = shard.partition(B, H, HK, world, rank)
+    P = lambda x: None if x is None else ctypes.c_void_p(x.data_ptr())
+    BF, flags = _lib.GD_BFLOAT16, _lib.GD_L2NORM | _lib.GD_SCALE_Q
+    stream = torch.cuda.Stream(device=dev)
+    sp = ctypes.c_void_p(stream.cuda_stream)
+    t = slice_inputs(cfg, dev, sl, 3000, True)
+    Hl, HKl = sl.h1 - sl.h0, sl.hk1 - sl.hk0
+    o = torch.empty(B, T, Hl, D, dtype=torch.bfloat16, device=dev)
+    sT = torch.empty(B, Hl, D, D, device=dev)
+    sT_all = torch.empty(world * B * Hl * D * D, device=dev)
+    nbytes = lib.gd_workspace_bytes(B, T, Hl, HKl, D, D, 0)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+
+    def fwd():
+        _lib.check(lib.gd_forward(P(t["q"]), P(t["k"]), P(t["v"]), P(t["g"]), P(t["beta"]), None, P(o), P(sT), BF, B,
+                                  T, Hl, HKl, D, D, flags, P(ws), nbytes, sp), "gd_forward")
+
+    def gather():
+        if world > 1:
+            dist.all_gather_into_tensor(sT_all, sT.reshape(-1))
+        else:
+            sT_all.copy_(sT.reshape(-1))
+
+    with torch.cuda.stream(stream):
+        for _ in range(warmup):
+            flush.zero_()
+            fwd()
+            gather()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    with torch.cuda.stream(stream):
+        for e in evs:
+            flush.zero_()
+            e[0].record(stream)
+            fwd()
+            e[1].record(stream)
+            gather()
+            e[2].record(stream)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    ms = _max_over_ranks(sum(e[0].elapsed_time(e[2]) for e in evs) / steps, dev, world)
+    fwd_ms = _max_over_ranks(sum(e[0].elapsed_time(e[1]) for e in evs) / steps, dev, world)
+    gat_ms = _max_over_ranks(sum(e[1].elapsed_time(e[2]) for e in evs) / steps, dev, world)
+    code = lib.gd_read_error(P(ws), sp, None)
+    # the gathered states hold every rank's heads in rank order: this rank's part is its own
+    mine = sT_all.view(world, -1)[rank].view_as(sT)
+    gathered_ok = bool(torch.equal(mine, sT))
+    del t, o, sT, sT_all, ws
+    torch.cuda.empty_cache()
+    return {"workload": "c3: B1 T32768 H32 d128 forward + final states, heads split over the ranks (strong scaling)",
+            "heads_per_rank": Hl, "ms_per_step": ms, "tokens_per_s": B * T / (ms / 1e3), "forward_ms": fwd_ms,
+            "gather_ms": gat_ms, "gather_bytes": world * B * Hl * D * D * 4, "steps": steps,
+            "l2": "inputs above L2 and flushed between steps", "device_status": code, "gather_ok": gathered_ok,
+            "limit": ("the gather" if gat_ms > fwd_ms else
+                      f"the forward's sequential chunk chain ({T // 64} chunks per head in order)")}
 
 
 def stored_mode_ms(lib, t, cfg, flags, ws, nbytes, o, sT, dq, dk, dv, dg, db, ds0, stream, flush, steps, warmup):
@@ -749,7 +1030,7 @@ def roofline(kern, cfg, hbm, tflops, peak_kind):
       fwd_state        6 D^2 + 2 C D   = 114,688 FLOP   (W S, Q S, K^T Vn; M Vn)     bytes: q, k bf16 + o bf16
       bwd_state        6 D^2 + 2 C D   = 114,688 FLOP   (K dS, Q^T dO, W^T dVn; M^T dO)
       bwd_chunk        10 D^2 + 16 C D + 4 C^2 = 311,296 FLOP
-      prep             4 C D + ... (C x C products and W, U) = 4 C D * 2 + ... see DESIGN.md
+      prep             8 C D           =  65,536 FLOP   (Q K^T, K K^T, W, U: four C x C x D products)
     and HBM bytes per token-head of the kernel's algorithmic inputs and outputs (bf16 q/k/v/do/o/grads 256 B each row
     of 128, fp32 g/beta/dg/dbeta 4 B)."""
     D, C = cfg["D"], 64
@@ -797,6 +1078,33 @@ def measured_traffic(kernel, cfg):
     return rec["dram_bytes_read"] + rec["dram_bytes_write"]
 
 
+def bind_to_gpu_numa(index):
+    """On a host with more than one NUMA node, restrict this process to the CPUs of the node its GPU hangs off (so its
+    pinned host buffers, touched after this, land in that node's memory). Returns the node, or None when the host has
+    one node or the topology cannot be read (then nothing changes)."""
+    import glob
+    nodes = glob.glob("/sys/devices/system/node/node[0-9]*")
+    if len(nodes) < 2:
+        return None
+    try:
+        out = subprocess.run(["nvidia-smi", f"--id={index}", "--query-gpu=pci.bus_id", "--format=csv,noheader"],
+                             capture_output=True, text=True, timeout=20).stdout.strip().lower()
+        bus = out[-12:] if len(out) >= 12 else out  # "0000:xx:yy.z"
+        with open(f"/sys/bus/pci/devices/{bus}/numa_node") as f:
+            node = int(f.read().strip())
+        if node < 0:
+            return None
+        with open(f"/sys/devices/system/node/node{node}/cpulist") as f:
+            cpus = set()
+            for part in f.read().strip().split(","):
+                lo, _, hi = part.partition("-")
+                cpus.update(range(int(lo), int(hi or lo) + 1))
+        os.sched_setaffinity(0, cpus)
+        return node
+    except Exception:
+        return None
+
+
 def end_to_end(lib, t, cfg, flags, ws, nbytes, stream, args):
     """The step through the C ABI for a caller holding host buffers: every step copies its inputs from pinned host
     memory to the device, runs forward + backward, and copies every output back to pinned host memory, all inside the
@@ -835,6 +1143,7 @@ def end_to_end(lib, t, cfg, flags, ws, nbytes, stream, args):
             views[name] = buf[off:off + n].view(dt).view(shape)
         return buf, views
 
+    numa = bind_to_gpu_numa(dev.index)  # before the pinned buffers are touched: their pages land on that node
     host_in_buf, host_in = packed_set(specs_in, pin_memory=True)
     for n in names_in:
         host_in[n].copy_(t[n].cpu())
@@ -890,7 +1199,22 @@ def end_to_end(lib, t, cfg, flags, ws, nbytes, stream, args):
     s_out.wait_stream(stream)
     e1.record(s_out)
     torch.cuda.synchronize(dev)
-    return {"seconds": e0.elapsed_time(e1) / 1e3, "steps": steps, "h2d": h2d, "d2h": d2h}
+    # the copy floor of the same run: the same pipelined copies (each step's inputs in on s_in, outputs out on s_out,
+    # both directions at once, two buffer sets) with no compute between them
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(s_in)
+    s_out.wait_stream(s_in)
+    for i in range(steps):
+        b = i & 1
+        with torch.cuda.stream(s_in):
+            dev_in[b][0].copy_(host_in_buf, non_blocking=True)
+        with torch.cuda.stream(s_out):
+            host_out[b][0].copy_(outs[b][0], non_blocking=True)
+    s_out.wait_stream(s_in)
+    f1.record(s_out)
+    torch.cuda.synchronize(dev)
+    return {"seconds": e0.elapsed_time(e1) / 1e3, "steps": steps, "h2d": h2d, "d2h": d2h,
+            "copy_floor_seconds": f0.elapsed_time(f1) / 1e3, "numa": numa}
 
 
 if __name__ == "__main__":

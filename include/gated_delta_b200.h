@@ -49,6 +49,12 @@ extern "C" {
 #define GD_STORE_STATES 2  /* the state pass keeps each chunk's entering state S_c and Vn for the backward */
 #define GD_SCALE_Q 4       /* q is multiplied by DK^-1/2 (after the l2 norm): the drop-in's query scaling */
 #define GD_STATES_STORED 8 /* gd_backward: the workspace already holds the states (gd_forward with GD_STORE_STATES) */
+/* Test only (never set in production): gd_fwd_state's MMA-issuing thread first waits on a barrier that nothing
+ * signals, with a ~1 ms budget. The wait expires, the kernel records GD_ERR_TIMEOUT at stage 28 in the error word,
+ * every role of the CTA gives up in its own bounded wait (~2 s) with no product or copy left in flight, and the CTA
+ * frees its TMEM and returns: gd_read_error then reports (GD_ERR_TIMEOUT, 28), and the context stays usable. The
+ * high-level entry points (gd_forward, gd_backward, ...) do not pass it on. */
+#define GD_TEST_WAIT_EXPIRES 0x40000000
 
 /* Text for a status code. */
 const char* gd_status_string(int status);
@@ -122,7 +128,11 @@ int gd_read_error(void* workspace, void* stream, int* where);
  * before any device call. The library allocates nothing either: the array is static device memory, held until the
  * process exits on each GPU where this code has been loaded.
  *   - The first call on a device (that device current) looks the array's device address up with
- *     cudaGetSymbolAddress and keeps it; make that first call before any stream capture.
+ *     cudaGetSymbolAddress and keeps it; make that first call before any stream capture. The address belongs to the
+ *     device's current context: after cudaDeviceReset the next call finds a new context and looks it up again (make
+ *     that call before any capture, too).
+ *   - flags as gd_forward's, except GD_STORE_STATES (GD_ERR_ARG): the stored-states forward's workspace must be kept
+ *     until the backward, which the shared array cannot promise.
  *   - All calls on a device share the array. Each call clears the part that must start at zero (the error word) on
  *     its stream; calls whose work overlaps on the GPU race on the array, so the caller serialises them.
  *   - device_status NULL: asynchronous like gd_forward. Otherwise the call waits for its stream and stores the

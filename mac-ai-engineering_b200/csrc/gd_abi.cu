@@ -1,5 +1,6 @@
 // The C ABI (include/gated_delta_b200.h): argument checks, dispatch on dtype and head widths, kernel sequencing.
 // No entry point allocates, synchronises (except gd_read_error) or aborts.
+#include <atomic>
 #include <cstdint>
 #include <cuda_runtime.h>
 
@@ -37,15 +38,24 @@ int check_dims(int B, int T, int H, int HK, int DK, int DV, int dtype) {
   return GD_OK;
 }
 
+// The current device must be sm_100 (the kernels are built for sm_100a only). The answer is kept per device index
+// (-1 = not yet asked), so a process that drives several GPUs gets each device's own answer; concurrent first calls
+// on one device store the same value.
+std::atomic<int> g_device_ok[gd::kMaxDevices];  // zero-initialised: 0 = not asked, 1 = sm_100, 2 = other
+
 int check_device() {
-  static int cached = -1;  // per process; the library serves sm_100 devices only
-  if (cached >= 0) return cached;
   int dev = 0, major = 0, minor = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return GD_ERR_DEVICE;
+  const bool cacheable = dev >= 0 && dev < gd::kMaxDevices;
+  if (cacheable) {
+    const int known = g_device_ok[dev].load(std::memory_order_relaxed);
+    if (known != 0) return known == 1 ? GD_OK : GD_ERR_DEVICE;
+  }
   if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return GD_ERR_DEVICE;
   if (cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess) return GD_ERR_DEVICE;
-  cached = (major == 10 && minor == 0) ? GD_OK : GD_ERR_DEVICE;
-  return cached;
+  const bool ok = major == 10 && minor == 0;
+  if (cacheable) g_device_ok[dev].store(ok ? 1 : 2, std::memory_order_relaxed);
+  return ok ? GD_OK : GD_ERR_DEVICE;
 }
 
 int launched(cudaError_t e) { return e == cudaSuccess ? GD_OK : GD_ERR_LAUNCH; }

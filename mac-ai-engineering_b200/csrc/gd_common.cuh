@@ -164,6 +164,23 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, ErrorW
   return true;
 }
 
+// The same with a caller-chosen budget (SM clocks).
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, ErrorWord* err, int where,
+                                              long long budget) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (clock64() - t0 > budget) {
+      report(err, GD_ERR_TIMEOUT, where);
+      return false;
+    }
+  }
+  return true;
+}
+
+// Budget of the test-only wait that GD_TEST_WAIT_EXPIRES adds (~1 ms at 1.9 GHz).
+constexpr long long kTestWaitCycles = 2000000ll;
+
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }

@@ -475,7 +475,7 @@ struct StateSmem {
   static constexpr size_t stage_bytes = s_m + 64 * 64 * 2;
   static constexpr size_t ost = stage0 + 2 * stage_bytes;   // [2][64 x DVH] O staging (row-major, 16-bit outputs)
   static constexpr size_t bar = ost + 2 * 64 * DVH * 2;
-  static constexpr int NBAR = 16;
+  static constexpr int NBAR = 17;
   static constexpr size_t tmem = bar + NBAR * 8;
   static constexpr size_t total = tmem + 8;
 };
@@ -527,6 +527,7 @@ __global__ void __launch_bounds__(576) state_kernel(const float* __restrict__ s0
   uint64_t* st_full = bars + 11;    // 16 epilogue warps
   uint64_t* o_full = bars + 12;     // [2] 16 epilogue warps: O staging buffer written
   uint64_t* o_free = bars + 14;     // [2] thread 0: the tensor store has read the buffer
+  uint64_t* never = bars + 16;      // GD_TEST_WAIT_EXPIRES: a barrier nothing signals
   uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + S::tmem);
   const bool store = (flags & GD_STORE_STATES) != 0 && lay.backward();
   const bool out = o != nullptr;  // both at once: the stored-states training forward
@@ -546,6 +547,7 @@ __global__ void __launch_bounds__(576) state_kernel(const float* __restrict__ s0
     mbar_init(o_full + 1, 16);
     mbar_init(o_free, 1);
     mbar_init(o_free + 1, 1);
+    mbar_init(never, 1);
     fence_mbar_init();
   }
   tc_fence_before();
@@ -562,6 +564,9 @@ __global__ void __launch_bounds__(576) state_kernel(const float* __restrict__ s0
   if (warp == 16) {
     // ---------------- MMA and bulk-copy issuer (one thread)
     if (lane == 0) {
+      // test only: a wait that expires before any product is issued (the failure path, with nothing in flight on
+      // the tensor core); the other roles then give up in their own bounded waits and the CTA frees its TMEM
+      if (flags & GD_TEST_WAIT_EXPIRES) ok = mbar_wait_for(never, 0, err, 28, kTestWaitCycles);
       for (int c = 0; c < NT && ok; ++c) {
         const int s = c & 1;
         const uint32_t par2 = (c >> 1) & 1;

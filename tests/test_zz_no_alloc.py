@@ -6,7 +6,8 @@ device, are not allowed where they run. gd_forward_noalloc takes the same inputs
 its intermediates in one fixed 64 MiB device array inside the library. These tests call both entry points through the
 C ABI on the same inputs and require identical results (the same kernels on the same inputs, so the tolerance is
 zero), on two calls in a row of different sizes, so that the second call also shows that what the first left in the
-shared array does not leak into it; and they check that sizes beyond the array are refused before any device call.
+shared array does not leak into it; and they check that sizes beyond the array, and the stored-states flag (whose
+workspace must outlive the call), are refused before any device call.
 
 The file name makes pytest collect it last."""
 import ctypes
@@ -74,3 +75,7 @@ def test_noalloc_refuses_sizes_beyond_its_array_before_any_device_call():
                                     16, 128, 128, FLAGS, None, None)
     assert status == _lib.GD_ERR_SCRATCH
     assert "64 MiB" in _lib.status_string(status)
+    # the stored-states forward (its workspace must outlive the call) is refused up front
+    status = lib.gd_forward_noalloc(None, None, None, None, None, None, None, None, _lib.GD_BFLOAT16, 1, 64, 1, 1,
+                                    128, 128, FLAGS | _lib.GD_STORE_STATES, None, None)
+    assert status == _lib.GD_ERR_ARG
