@@ -124,7 +124,7 @@ int gd_read_error(void* workspace, void* stream, int* where);
  * allocator (a serving engine's reserved pool, a host framework that owns the GPU), or a caller that may not risk the
  * device synchronisation cudaMalloc / cudaFree can cause. Same arguments and results as gd_forward, without the
  * workspace: the intermediates go to one fixed 64 MiB device array inside the library (enough for
- * gd_workspace_bytes(..., 0) <= 64 MiB, e.g. 16 value heads x 2,176 tokens); larger sizes return GD_ERR_SCRATCH
+ * gd_workspace_bytes(..., 0) <= 64 MiB, e.g. 16 value heads x 1,984 tokens); larger sizes return GD_ERR_SCRATCH
  * before any device call. The library allocates nothing either: the array is static device memory, held until the
  * process exits on each GPU where this code has been loaded.
  *   - The first call on a device (that device current) looks the array's device address up with

@@ -15,7 +15,7 @@
 // waits on the product that frees its buffer, which is also the product whose next phase needs that refill); all
 // hand-offs are mbarriers. Per chunk the MMA thread issues only: K~ dS (chain) -> -W^T dVn (chain, added onto the
 // chunk's (gamma Q)^T dO) -> the next chunk's dS-independent products. Precision: dS and K~ split into bf16 hi + lo
-// (three products), gamma Q split, the rest bf16.
+// (three products), gamma Q and M split, the rest bf16.
 #include "gd_common.cuh"
 #include "gd_layout.cuh"
 
@@ -32,8 +32,8 @@ struct BwdStateSmem {
   static constexpr size_t c_g = c_kt + 2 * 64 * DK * 2;    //   [64] G
   static constexpr size_t crit_bytes = c_g + 64 * 4;
   static constexpr size_t wt = crit0 + 2 * crit_bytes;     // [DK x 64] W^T (one buffer)
-  static constexpr size_t m = wt + DK * 64 * 2;            // [64 x 64] M        } inputs of the dS-independent
-  static constexpr size_t gq = m + 64 * 64 * 2;            // [2][64 x DK] gamma Q }  products, one chunk ahead
+  static constexpr size_t m = wt + DK * 64 * 2;            // [2][64 x 64] M hi, lo } inputs of the dS-independent
+  static constexpr size_t gq = m + 2 * 64 * 64 * 2;        // [2][64 x DK] gamma Q }  products, one chunk ahead
   static constexpr size_t dO = gq + 2 * 64 * DK * 2;       // [64 x DVH] dO      }
   static constexpr size_t bar = dO + 64 * DVH * 2;
   static constexpr int NBAR = 12;
@@ -107,14 +107,15 @@ __global__ void __launch_bounds__(576) bwd_state_kernel(const T* __restrict__ d_
     bulk_g2s(smem + S::wt, ws + lay.wt + (row0 + c) * lay.wt_bytes(), (uint32_t)lay.wt_bytes(), wt_full);
   };
   auto load_pre = [&](int c) {
-    mbar_arrive_expect_tx(pre_full, (uint32_t)(lay.m_bytes() + lay.qk_bytes()));
-    bulk_g2s(smem + S::m, ws + lay.m + (row0 + c) * lay.m_bytes(), (uint32_t)lay.m_bytes(), pre_full);
+    mbar_arrive_expect_tx(pre_full, (uint32_t)(lay.mm_bytes() + lay.qk_bytes()));
+    bulk_g2s(smem + S::m, ws + lay.m + (row0 + c) * lay.mm_bytes(), (uint32_t)lay.mm_bytes(), pre_full);
     bulk_g2s(smem + S::gq, ws + lay.gq + (row0 + c) * lay.qk_bytes(), (uint32_t)lay.qk_bytes(), pre_full);
   };
   const Tile tDO{smem_u32(smem + S::dO), DVH};
-  // (M^T dO)^T = dO^T M [DVH x 64]; ((gamma Q)^T dO)^T = dO^T (gamma Q) [DVH x DK], gamma Q split
+  // (M^T dO)^T = dO^T M [DVH x 64] (M hi + lo); ((gamma Q)^T dO)^T = dO^T (gamma Q) [DVH x DK], gamma Q split
   auto issue_pre = [&](int n) {
     mma_tiles(tA, DVH, 64, 64, tDO, false, 0, 0, Tile{smem_u32(smem + S::m), 64}, true, 0, false);
+    mma_tiles(tA, DVH, 64, 64, tDO, false, 0, 0, Tile{smem_u32(smem + S::m + 64 * 64 * 2), 64}, true, 0, true);
     const uint32_t tC = tm + 192 + 128 * (n & 1);
     mma_tiles(tC, DVH, DK, 64, tDO, false, 0, 0, Tile{smem_u32(smem + S::gq), DK}, true, 0, false);
     mma_tiles(tC, DVH, DK, 64, tDO, false, 0, 0, Tile{smem_u32(smem + S::gq + 64 * DK * 2), DK}, true, 0, true);

@@ -15,7 +15,8 @@
 //   G3:  B6 (dM K)^T, B7 (dM^T Q)^T (dM, q and k split), B2 (A^T dW)^T (one commit), B1 dW K^T,
 //        B3 Q K^T (q and k split: M = Q K^T * Gamma in fp32 precision for R);   dW = -dVn S^T
 //   G2:  B5 (Vn dS^T)^T (Vn and dS split); after e2: B1 K K^T (k split, for L and the dbeta term)
-//   tail: B6 T1 = dA A^T, B7 A^T T1 (dL = -A^T T1), B5 (K^T (P_beta + P_beta^T)) with P_beta = diag(beta) (dL * Gamma)
+//   tail: B6 T1 = dA A^T, B7 A^T T1 (dL = -A^T T1; T1 split, its low half in the dA tile), B5 (K^T (P_beta + P_beta^T))
+//         with P_beta = diag(beta) (dL * Gamma)
 // Equations: tools/check_chunk_equations.py:49-76 and src/macai/gated_delta/_chunked.py:20-34 of the reference; dg is
 // summed without cancellation (the regrouping of _chunked.py:1138-1142, extended to the decay-mask terms):
 //   dg_t = sum_{s>=t} (a_s + w_s) + gamma_last <S_c, dS_{c+1}> + sum_{r<t} E_r + sum_{i>=t>j} R_ij
@@ -391,7 +392,8 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
           if (t1 && !dl && mbar_test(e3_done, par)) {
             tc_fence_after();
             GD_TRACE_ONE(ws, lay, 3000 + 8 * n + 5);
-            mma_tiles(B7, 64, 64, 64, tA, false, 0, 0, tT1, true, 0, false);     // A^T T1
+            mma_tiles(B7, 64, 64, 64, tA, false, 0, 0, tT1, true, 0, false);     // A^T T1 (T1 hi + lo: with
+            mma_tiles(B7, 64, 64, 64, tA, false, 0, 0, tDa, true, 0, true);      //  nearly parallel keys)
             mma_commit(dl_full);
             dl = progressed = true;
           }
@@ -647,10 +649,11 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
       if (!(ok = epi_all(ok))) break;
       tc_fence_after();
       GD_TRACE_AT(ws, lay, 32 * n + 13);
-      {
+      {  // T1 hi, and its lo in the dA tile (dA's last reader, the T1 product, is complete; P_beta overwrites the lo
+         // half only after dl_full, when the dL product has read it)
         float x[8];
         tmem_ld8h(tmem_lane_addr(B6, warp, tok0), x);
-        store8_bf16(smem + S::t1, ri, c8, 64, x);
+        store8_split(smem + S::t1, smem + S::da, ri, c8, 64, x);
       }
       tc_fence_before();
       fence_async_smem();

@@ -30,6 +30,7 @@ struct PrepSmem {
   static constexpr size_t a2l = a2h + 64 * 64 * 2;        //                           lo
   static constexpr size_t L = a2l + 64 * 64 * 2;          // [64][68] fp32, L (strictly lower; 16-byte aligned rows)
   static constexpr size_t Ai = L + 64 * 68 * 4;           // [64][68] fp32, A
+  static constexpr size_t a1l = L;                        // [64 x 64] A diag(beta gamma), lo (L is dead by then)
   static constexpr size_t ql = L;                         // [64 x DK] low half of q, then k: live only until the
   static constexpr size_t kl = ql + 64 * DK * 2;          //   Q K^T / K K^T product is done (L and A reuse them)
   static_assert(2 * 64 * DK * 2 <= 2 * 64 * 68 * 4, "the q / k low halves must fit in the L and A buffers");
@@ -307,7 +308,7 @@ __global__ void __launch_bounds__(256, 2) prep_kernel(const T* __restrict__ q, c
     const int i = tid & 63;
     const float Gi = sG[i];
     float acc[32];
-    unsigned char* mimg = ws + lay.m + cidx * lay.m_bytes();
+    unsigned char* mimg = ws + lay.m + cidx * lay.mm_bytes();
     {
       const int half = warp >> 2;
       GD_TRACE_WARP(ws, lay, 0);
@@ -331,7 +332,8 @@ __global__ void __launch_bounds__(256, 2) prep_kernel(const T* __restrict__ q, c
       GD_TRACE_WARP(ws, lay, 2);
       if (is_m) {
 #pragma unroll
-        for (int q8 = 0; q8 < 4; ++q8) store8_bf16(mimg, i, 32 * half + 8 * q8, 64, acc + 8 * q8);
+        for (int q8 = 0; q8 < 4; ++q8)
+          store8_split(mimg, mimg + lay.m_bytes(), i, 32 * half + 8 * q8, 64, acc + 8 * q8);
       } else {
         float4* lrow = reinterpret_cast<float4*>(sL + i * 68 + 32 * half);
 #pragma unroll
@@ -362,7 +364,7 @@ __global__ void __launch_bounds__(256, 2) prep_kernel(const T* __restrict__ q, c
         a1[e] = a0[e] * sBG[j];
         a2[e] = a0[e] * sB[j];
       }
-      store8_bf16(smem + S::a1, i, j0 + 8 * q8, 64, a1);
+      store8_split(smem + S::a1, smem + S::a1l, i, j0 + 8 * q8, 64, a1);
       store8_split(smem + S::a2h, smem + S::a2l, i, j0 + 8 * q8, 64, a2);
     }
   }
@@ -374,9 +376,12 @@ __global__ void __launch_bounds__(256, 2) prep_kernel(const T* __restrict__ q, c
   __syncthreads();
   tc_fence_after();
   if (ok && tid == 0) {
-    // W^T [DK x 64] = K^T (A diag(beta gamma))^T ; U^T [DV x 64] = V^T (A diag(beta))^T (hi + lo)
+    // W^T [DK x 64] = K^T (A diag(beta gamma))^T ; U^T [DV x 64] = V^T (A diag(beta))^T (both A factors hi + lo:
+    // with nearly parallel keys W is a difference of nearly equal rows, which a one-bf16 A diag(beta gamma) loses)
     mma_tiles(tm + 64, DK, 64, 64, Tile{smem_u32(smem + S::k), DK}, false, 0, 0, Tile{smem_u32(smem + S::a1), 64},
               false, 0, false);
+    mma_tiles(tm + 64, DK, 64, 64, Tile{smem_u32(smem + S::k), DK}, false, 0, 0, Tile{smem_u32(smem + S::a1l), 64},
+              false, 0, true);
     mma_tiles(tm + 128, DV, 64, 64, Tile{smem_u32(smem + S::v), DV}, false, 0, 0, Tile{smem_u32(smem + S::a2h), 64},
               false, 0, false);
     mma_tiles(tm + 128, DV, 64, 64, Tile{smem_u32(smem + S::v), DV}, false, 0, 0, Tile{smem_u32(smem + S::a2l), 64},
@@ -471,8 +476,8 @@ struct StateSmem {
   static constexpr size_t s_wt = 0;                        //   [DK x 64] W^T image
   static constexpr size_t s_q = s_wt + DK * 64 * 2;        //   [DK x 64] q image (hi, transposed)
   static constexpr size_t s_kt = s_q + 64 * DK * 2;        //   [2][64 x DK] K~ hi, lo
-  static constexpr size_t s_m = s_kt + 2 * 64 * DK * 2;    //   [64 x 64] M image
-  static constexpr size_t stage_bytes = s_m + 64 * 64 * 2;
+  static constexpr size_t s_m = s_kt + 2 * 64 * DK * 2;    //   [2][64 x 64] M image: hi, lo
+  static constexpr size_t stage_bytes = s_m + 2 * 64 * 64 * 2;
   static constexpr size_t ost = stage0 + 2 * stage_bytes;   // [2][64 x DVH] O staging (row-major, 16-bit outputs)
   static constexpr size_t bar = ost + 2 * 64 * DVH * 2;
   static constexpr int NBAR = 17;
@@ -488,7 +493,7 @@ __device__ __forceinline__ void issue_stage(unsigned char* stg, const unsigned c
   bulk_g2s(stg + S::s_wt, ws + lay.wt + cidx * lay.wt_bytes(), (uint32_t)lay.wt_bytes(), bar);
   bulk_g2s(stg + S::s_q, ws + lay.qk + cidx * lay.qk_bytes(), 64 * DK * 2, bar);
   bulk_g2s(stg + S::s_kt, ws + lay.kt + cidx * lay.qk_bytes(), (uint32_t)lay.qk_bytes(), bar);
-  bulk_g2s(stg + S::s_m, ws + lay.m + cidx * lay.m_bytes(), (uint32_t)lay.m_bytes(), bar);
+  bulk_g2s(stg + S::s_m, ws + lay.m + cidx * lay.mm_bytes(), (uint32_t)lay.mm_bytes(), bar);
 }
 
 template <typename T, int DK, int DV>
@@ -607,8 +612,9 @@ __global__ void __launch_bounds__(576) state_kernel(const float* __restrict__ s0
         mma_commit(ds_full);
         GD_TRACE_ONE(ws, lay, 1024 + 8 * c + 5);
         if (out) {
-          const Tile tM{smem_u32(stg + S::s_m), 64};
+          const Tile tM{smem_u32(stg + S::s_m), 64}, tMl{smem_u32(stg + S::s_m + 64 * 64 * 2), 64};
           mma_tiles(tm + 192 + 64 * s, DVH, 64, 64, tVh, true, 0, 0, tM, false, 0, false);
+          mma_tiles(tm + 192 + 64 * s, DVH, 64, 64, tVh, true, 0, 0, tMl, false, 0, true);
           mma_tiles(tm + 192 + 64 * s, DVH, 64, 64, tVl, true, 0, 0, tM, false, 0, true);
           mma_commit(mv_full + s);
         }

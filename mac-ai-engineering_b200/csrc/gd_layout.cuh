@@ -7,7 +7,7 @@
 //                             k half only for the backward
 //   kt   [2][64 x DK] image   K~ = diag(e) K, e_i = exp(G_last - G_i): hi, then lo (the state updates' operand)
 //   wt   [DK x 64]    image   W^T, W = A diag(beta gamma) K
-//   m    [64 x 64]    image   M = (Q K^T) * exp(G_i - G_j), lower with the diagonal
+//   m    [2][64 x 64] image   M = (Q K^T) * exp(G_i - G_j), lower with the diagonal: hi, then lo
 //   u    [64][DV]     fp32    U = A diag(beta) V
 //   gc   [64]         fp32    G, the in-chunk inclusive cumulative sum of g
 // and for the backward also
@@ -61,7 +61,8 @@ struct Layout {
 
   __host__ __device__ size_t qk_bytes() const { return (size_t)2 * 64 * DK * 2; }   // a [2][64 x DK] image pair
   __host__ __device__ size_t wt_bytes() const { return (size_t)DK * 64 * 2; }
-  __host__ __device__ size_t m_bytes() const { return (size_t)64 * 64 * 2; }
+  __host__ __device__ size_t m_bytes() const { return (size_t)64 * 64 * 2; }       // one C x C image
+  __host__ __device__ size_t mm_bytes() const { return (size_t)2 * 64 * 64 * 2; }  // the M hi / lo pair
   __host__ __device__ size_t u_bytes() const { return (size_t)64 * DV * 4; }
   __host__ __device__ size_t gc_bytes() const { return (size_t)64 * 4; }
   __host__ __device__ size_t vi_bytes() const { return (size_t)64 * DV * 2; }
@@ -103,7 +104,7 @@ struct Layout {
     L.qk = take(L.nch * L.qk_bytes());
     L.kt = take(L.nch * L.qk_bytes());
     L.wt = take(L.nch * L.wt_bytes());
-    L.m = take(L.nch * L.m_bytes());
+    L.m = take(L.nch * L.mm_bytes());
     L.u = take(L.nch * L.u_bytes());
     L.gc = take(L.nch * L.gc_bytes());
     if (backward) {

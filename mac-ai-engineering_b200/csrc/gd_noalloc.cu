@@ -27,7 +27,7 @@
 
 namespace {
 
-// the fixed workspace: about 540 chunks of 64 tokens x one value head (e.g. 16 value heads x 2,176 tokens)
+// the fixed workspace: about 510 chunks of 64 tokens x one value head (e.g. 16 value heads x 1,984 tokens)
 constexpr size_t kScratchBytes = size_t(64) << 20;
 
 static __device__ __align__(256) unsigned char g_scratch[kScratchBytes];

@@ -28,6 +28,15 @@ CALLS: collections.Counter = collections.Counter()
 # writes them into a workspace the autograd context keeps until the backward (gd_workspace_bytes(..., 1) of device
 # memory per call), and the backward skips the recompute. Outputs and gradients are the same bits either way.
 RECOMPUTE_STATES = True
+# The kernels compute every product with bf16 tensor-core operands (fp32 accumulation; the operands whose rounding would
+# break the bf16 parity bar are carried as bf16 hi + lo pairs). That meets the reference's bar for bf16 queries, not its
+# float16 or float32 bars: measured against transformers' own error on the same inputs, fp16 queries come out 2-8x and
+# fp32 queries 300-20,000x less accurate. So a float16 / float32 query is refused (NotImplementedError), as the
+# reference refuses what it cannot compute exactly, unless ALLOW_BF16_COMPUTE is True: then such inputs run through the
+# same kernels (read in their own dtype, results in the query's dtype) with bf16-grade accuracy. A bfloat16 query with
+# a float32 value (the reference layer's convolution path writes v in fp32) is accepted: v is rounded to bf16, and the
+# results meet the bf16 bar against transformers run on the same mixed inputs.
+ALLOW_BF16_COMPUTE = False
 
 _DTYPES = {torch.float32: _lib.GD_FLOAT32, torch.float16: _lib.GD_FLOAT16, torch.bfloat16: _lib.GD_BFLOAT16}
 
@@ -44,6 +53,18 @@ def _dims(q: torch.Tensor, v: torch.Tensor):
     B, T, HK, DK = q.shape
     H, DV = v.shape[2], v.shape[3]
     return B, T, H, HK, DK, DV
+
+
+def check_dtype(dt) -> None:
+    """The query dtypes the kernels serve at the reference's accuracy (bfloat16), or any of float16 / float32 /
+    bfloat16 with ALLOW_BF16_COMPUTE; TypeError for other dtypes, NotImplementedError for the refused ones."""
+    if dt not in _DTYPES:
+        raise TypeError(f"query dtype {dt} is not supported (float32, float16, bfloat16)")
+    if dt != torch.bfloat16 and not ALLOW_BF16_COMPUTE:
+        raise NotImplementedError(
+            f"{dt} queries: the B200 kernels compute with bf16 tensor-core operands, whose results miss the reference's "
+            f"{dt} accuracy; pass bfloat16 inputs, or set macai_b200.gated_delta.op.ALLOW_BF16_COMPUTE = True to "
+            "accept bf16-grade results in the input dtype")
 
 
 def check_shapes(q, k, v, g, beta, s0=None) -> None:
@@ -455,6 +476,7 @@ class GatedDeltaRule:
     @staticmethod
     def apply(q, k, v, g, beta, s0, save: bool = True):
         dt = q.dtype
+        check_dtype(dt)
         k, v = k.to(dt), v.to(dt)
         check_shapes(q, k, v, g, beta, s0)
         return _forward(q.contiguous(), k.contiguous(), v.contiguous(), g.float().contiguous(),
@@ -477,8 +499,7 @@ def chunk_gated_delta_rule(query, key, value, g, beta, chunk_size: int = 64, ini
     semantics; the reference refuses it (op.py:270-273)."""
     cu_seqlens = kwargs.get("cu_seqlens")
     dt = query.dtype
-    if dt not in _DTYPES:
-        raise TypeError(f"query dtype {dt} is not supported (float32, float16, bfloat16)")
+    check_dtype(dt)
     # the kernels read q, k, v in one dtype: key and value follow the query's (differentiably, so their gradients
     # come back in their own dtypes)
     k, v = key.to(dt), value.to(dt)

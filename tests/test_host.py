@@ -14,38 +14,38 @@ def test_packed_rows_checked_before_any_launch():
     """cu_seqlens (which the reference refuses, op.py:270-273) is taken with fla's semantics; wrong boundary lists,
     a batch size other than 1 and a per-sequence initial state of the wrong shape are refused on the host, and there
     is still no CPU path."""
-    x = torch.zeros(1, 4, 1, 128)
+    x = torch.zeros(1, 4, 1, 128, dtype=torch.bfloat16)
     for bad in ([0, 2, 3], [1, 2, 4], [0, 3, 2, 4], [4], [[0, 4]]):
         with pytest.raises(ValueError):
             chunk_gated_delta_rule(x, x, x, x[..., 0], x[..., 0], cu_seqlens=torch.tensor(bad))
-    x2 = torch.zeros(2, 4, 1, 128)
+    x2 = torch.zeros(2, 4, 1, 128, dtype=torch.bfloat16)
     with pytest.raises(ValueError, match="batch size must be 1"):
         chunk_gated_delta_rule(x2, x2, x2, x2[..., 0], x2[..., 0], cu_seqlens=torch.tensor([0, 2, 4]))
     with pytest.raises(ValueError, match="initial_state"):
         chunk_gated_delta_rule(x, x, x, x[..., 0], x[..., 0], cu_seqlens=torch.tensor([0, 2, 4]),
-                               initial_state=torch.zeros(1, 1, 128, 128))
+                               initial_state=torch.zeros(1, 1, 128, 128, dtype=torch.bfloat16))
     with pytest.raises(RuntimeError, match="CUDA"):
         chunk_gated_delta_rule(x, x, x, x[..., 0], x[..., 0], cu_seqlens=torch.tensor([0, 2, 4]))
 
 
 def test_unsupported_head_width_refused():
-    x = torch.zeros(1, 4, 1, 64)
+    x = torch.zeros(1, 4, 1, 64, dtype=torch.bfloat16)
     with pytest.raises(NotImplementedError):
         chunk_gated_delta_rule(x, x, x, x[..., 0], x[..., 0])
 
 
 def test_shape_errors():
-    q = torch.zeros(1, 4, 2, 128)
-    v = torch.zeros(1, 4, 3, 128)
+    q = torch.zeros(1, 4, 2, 128, dtype=torch.bfloat16)
+    v = torch.zeros(1, 4, 3, 128, dtype=torch.bfloat16)
     with pytest.raises(ValueError):
         chunk_gated_delta_rule(q, q, v, v[..., 0], v[..., 0])               # 3 value heads, 2 key heads
-    v = torch.zeros(1, 4, 2, 128)
+    v = torch.zeros(1, 4, 2, 128, dtype=torch.bfloat16)
     with pytest.raises(ValueError):
         chunk_gated_delta_rule(q, q, v, v[..., 0, 0], v[..., 0])             # g of the wrong shape
 
 
 def test_no_cpu_path():
-    x = torch.zeros(1, 4, 1, 128)
+    x = torch.zeros(1, 4, 1, 128, dtype=torch.bfloat16)
     with pytest.raises(RuntimeError, match="CUDA"):
         chunk_gated_delta_rule(x, x, x, x[..., 0], x[..., 0])
 
@@ -100,3 +100,21 @@ def test_qwen3_5_layer_binds_patched_rule():
         if layer is None:
             pytest.skip("the layer's constructor places a module on the current CUDA device")
         assert layer.chunk_gated_delta_rule is chunk_gated_delta_rule
+
+
+def test_wide_query_dtypes_refused_by_default(monkeypatch):
+    """fp16 / fp32 queries: NotImplementedError before any launch unless op.ALLOW_BF16_COMPUTE (the kernels' bf16
+    operands miss those dtypes' accuracy); other dtypes: TypeError."""
+    import torch
+    from macai_b200.gated_delta import chunk_gated_delta_rule, op
+    for dt in (torch.float16, torch.float32):
+        x = torch.zeros(1, 4, 1, 128, dtype=dt)
+        with pytest.raises(NotImplementedError, match="ALLOW_BF16_COMPUTE"):
+            chunk_gated_delta_rule(x, x, x, x[..., 0].float(), x[..., 0].float())
+    with pytest.raises(TypeError):
+        x = torch.zeros(1, 4, 1, 128, dtype=torch.float64)
+        chunk_gated_delta_rule(x, x, x, x[..., 0], x[..., 0])
+    monkeypatch.setattr(op, "ALLOW_BF16_COMPUTE", True)
+    x = torch.zeros(1, 4, 1, 128, dtype=torch.float32)
+    with pytest.raises(RuntimeError, match="no CPU path"):   # past the dtype check: only the device is wrong now
+        chunk_gated_delta_rule(x, x, x, x[..., 0], x[..., 0])
