@@ -1,60 +1,35 @@
 // The gated RMSNorm on the rule's output (transformers' Qwen3_5RMSNormGated over rows of one value head), one pass
-// each way, mirroring the reference's gnorm_fwd / gnorm_bwd kernels (src/macai/layer/_gated_norm.py:1-16 formulas,
-// :28-104 kernels, :127-137 column sum) and its autograd function (:154-197), with transformers' rounding points:
+// each way. The reference's formulas (src/macai/layer/_gated_norm.py:1-16) and autograd contract (:154-197), with
+// transformers' rounding points:
 //   x_hat = x rsqrt(mean(x^2) + eps)                        (fp32)
 //   h     = w x_hat.to(T)                                   (rounded to T again when w has x's dtype)
 //   o     = (h silu(z)).to(T)
 // backward in fp32, one rounding per gradient (s = silu(z), sig = sigmoid(z)):
 //   dz = do h sig (1 + z (1 - sig)),  dx = r (dxh - x_hat <x_hat, dxh> / D) with dxh = do s w,
 //   dw = sum over rows of do s x_hat.to(T)                  (only when asked: fixed-order partial rows, then a sum)
-// x, z, o, dout, dx, dz: [rows, D] in T (fp32 / fp16 / bf16); w and dw: [D] in T or fp32. Any width: one warp a row,
-// 4 adjacent elements a lane per 128 columns. D = 128 at 16 bits (the Qwen3.5 value heads): half a warp a row, 16-byte
-// loads and stores, 4 rows a warp in flight. The row sums are warp shuffles. HBM-bound: the forward reads x
-// and z and writes o (3 x 2 B per element at bf16), the backward reads x, z, dout and writes dx, dz (5 x 2 B).
+// x, z, o, dout, dx, dz: [rows, D] in T (fp32 / fp16 / bf16); w and dw: [D] in T or fp32.
+//
+// Every width runs on one design: a row belongs to a team of TEAM consecutive lanes of a warp (TEAM a power of two,
+// 32 / TEAM rows a warp at once), lane i of a team holding the row's 16-byte (or, for 16-bit widths that are not a
+// multiple of 8, 8-byte) chunks i, i + TEAM, ... in registers; the row's sums are xor shuffles inside the team.
+// D = 128 at 16 bits (the Qwen3.5 value heads) has its own kernels: half a warp a row, two rows a lane in flight,
+// streaming 16-byte loads and stores. HBM-bound: the forward reads x and z and writes o (3 x 2 B per element at
+// bf16), the backward reads x, z, dout and writes dx, dz (5 x 2 B).
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <type_traits>
 
 #include "gated_delta_b200.h"
 
 namespace {
 
-constexpr int kThreads = 256;       // 8 warps, one row each at a time
+constexpr int kThreads = 256;       // 8 warps
 constexpr int kWarps = kThreads / 32;
 constexpr int kMaxPartials = 1024;  // CTAs of the backward with dw (its fixed-order partial rows)
 constexpr int kMaxD = 1024;
-
-// 4 consecutive elements <-> float4 (8-byte aligned start for 16-bit types, 16-byte for fp32)
-__device__ __forceinline__ float4 ld4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
-__device__ __forceinline__ float4 ld4(const __nv_bfloat16* p) {
-  const uint2 u = __ldg(reinterpret_cast<const uint2*>(p));
-  const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
-  const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
-  return make_float4(a.x, a.y, b.x, b.y);
-}
-__device__ __forceinline__ float4 ld4(const __half* p) {
-  const uint2 u = __ldg(reinterpret_cast<const uint2*>(p));
-  const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
-  const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
-  return make_float4(a.x, a.y, b.x, b.y);
-}
-__device__ __forceinline__ void st4(float* p, float4 v) { *reinterpret_cast<float4*>(p) = v; }
-__device__ __forceinline__ void st4(__nv_bfloat16* p, float4 v) {
-  const __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y), b = __floats2bfloat162_rn(v.z, v.w);
-  uint2 u;
-  u.x = *reinterpret_cast<const uint32_t*>(&a);
-  u.y = *reinterpret_cast<const uint32_t*>(&b);
-  *reinterpret_cast<uint2*>(p) = u;
-}
-__device__ __forceinline__ void st4(__half* p, float4 v) {
-  const __half2 a = __floats2half2_rn(v.x, v.y), b = __floats2half2_rn(v.z, v.w);
-  uint2 u;
-  u.x = *reinterpret_cast<const uint32_t*>(&a);
-  u.y = *reinterpret_cast<const uint32_t*>(&b);
-  *reinterpret_cast<uint2*>(p) = u;
-}
 
 // x rounded to T and back (the .to(input_dtype) of the torch expression)
 template <typename T>
@@ -65,10 +40,6 @@ template <>
 __device__ __forceinline__ float rnd<__nv_bfloat16>(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 template <>
 __device__ __forceinline__ float rnd<__half>(float x) { return __half2float(__float2half_rn(x)); }
-template <typename T>
-__device__ __forceinline__ float4 rnd4(float4 v) {
-  return make_float4(rnd<T>(v.x), rnd<T>(v.y), rnd<T>(v.z), rnd<T>(v.w));
-}
 
 template <typename T>
 __device__ __forceinline__ T cvt(float x);
@@ -79,14 +50,6 @@ __device__ __forceinline__ __half cvt<__half>(float x) { return __float2half_rn(
 template <>
 __device__ __forceinline__ __nv_bfloat16 cvt<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
 
-__device__ __forceinline__ float warp_sum(float v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  return v;
-}
-__device__ __forceinline__ float dot4(float4 a, float4 b) { return a.x * b.x + a.y * b.y + a.z * b.z + a.w * b.w; }
-__device__ __forceinline__ float4 mul4(float4 a, float4 b) { return make_float4(a.x * b.x, a.y * b.y, a.z * b.z, a.w * b.w); }
-__device__ __forceinline__ float4 scale4(float4 a, float s) { return make_float4(a.x * s, a.y * s, a.z * s, a.w * s); }
 // sigmoid with the fast divide (2 ulp; a denominator past 2^126, z < -87, gives 0): the division's full-precision
 // sequence made the kernels instruction-bound
 __device__ __forceinline__ float sigmoid(float z) { return __fdividef(1.f, 1.f + expf(-z)); }
@@ -95,141 +58,234 @@ __device__ __forceinline__ float sigmoid(float z) { return __fdividef(1.f, 1.f +
 // way to within an ulp)
 __device__ __forceinline__ float inv_rms(float ss, int D, float eps) { return 1.f / sqrtf(ss / (float)D + eps); }
 
-// the CH column groups (128 elements each) of one row: element offset of this lane's 4 in group j
-__device__ __forceinline__ int col(int j, int lane) { return j * 128 + lane * 4; }
-
-// ---- any width (D % 4 == 0, D <= 1024): one warp a row
-template <typename T, typename TW, int CH>
-__global__ void __launch_bounds__(kThreads) gnorm_fwd_kernel(const T* __restrict__ x, const T* __restrict__ z,
-                                                             const TW* __restrict__ w, T* __restrict__ o,
-                                                             long long rows, int D, float eps, bool round_h) {
-  const int lane = threadIdx.x & 31;
-  const long long row = (long long)blockIdx.x * kWarps + (threadIdx.x >> 5);
-  if (row >= rows) return;
-  const T* xr = x + row * D;
-  const T* zr = z + row * D;
-  float4 xv[CH], zv[CH];
-  float ss = 0.f;
+// ---- E consecutive elements of T <-> floats (E * sizeof(T) = 8 or 16 bytes, aligned to that)
+template <typename T, int E>
+struct Chunk {
+  static_assert(E * sizeof(T) == 8 || E * sizeof(T) == 16, "8- or 16-byte chunks");
+  using Raw = typename std::conditional<E * sizeof(T) == 16, uint4, uint2>::type;
+  __device__ __forceinline__ static void load(const T* p, float (&f)[E]) {
+    const Raw r = *reinterpret_cast<const Raw*>(p);
+    const uint32_t* u = reinterpret_cast<const uint32_t*>(&r);
+    if constexpr (std::is_same<T, float>::value) {
 #pragma unroll
-  for (int j = 0; j < CH; ++j) {  // every load in flight before any arithmetic
-    const int i = col(j, lane);
-    const bool in = i < D;
-    xv[j] = in ? ld4(xr + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-    zv[j] = in ? ld4(zr + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int e = 0; e < E; ++e) f[e] = __uint_as_float(u[e]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < E / 2; ++i) {
+        float2 v;
+        if constexpr (std::is_same<T, __half>::value) {
+          v = __half22float2(*reinterpret_cast<const __half2*>(u + i));
+        } else {
+          v = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(u + i));
+        }
+        f[2 * i] = v.x;
+        f[2 * i + 1] = v.y;
+      }
+    }
   }
+  __device__ __forceinline__ static void store(T* p, const float (&f)[E]) {
+    Raw r;
+    uint32_t* u = reinterpret_cast<uint32_t*>(&r);
+    if constexpr (std::is_same<T, float>::value) {
 #pragma unroll
-  for (int j = 0; j < CH; ++j) ss += dot4(xv[j], xv[j]);
-  const float r = inv_rms(warp_sum(ss), D, eps);
-  T* orow = o + row * D;
+      for (int e = 0; e < E; ++e) u[e] = __float_as_uint(f[e]);
+    } else {
 #pragma unroll
-  for (int j = 0; j < CH; ++j) {
-    const int i = col(j, lane);
-    if (i < D) {
-      float4 h = mul4(ld4(w + i), rnd4<T>(scale4(xv[j], r)));
-      if (round_h) h = rnd4<T>(h);
-      const float4 zf = zv[j];
-      const float4 s = make_float4(zf.x * sigmoid(zf.x), zf.y * sigmoid(zf.y), zf.z * sigmoid(zf.z), zf.w * sigmoid(zf.w));
-      st4(orow + i, mul4(h, s));
+      for (int i = 0; i < E / 2; ++i) {
+        if constexpr (std::is_same<T, __half>::value) {
+          const __half2 v = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
+          u[i] = *reinterpret_cast<const uint32_t*>(&v);
+        } else {
+          const __nv_bfloat162 v = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+          u[i] = *reinterpret_cast<const uint32_t*>(&v);
+        }
+      }
+    }
+    *reinterpret_cast<Raw*>(p) = r;
+  }
+};
+
+// the weight's E elements at p (w in T or fp32; element-wise loads: w is tiny and stays in L1)
+template <typename TW, int E>
+__device__ __forceinline__ void load_weights(const TW* p, float (&f)[E]) {
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    if constexpr (std::is_same<TW, float>::value) {
+      f[e] = __ldg(p + e);
+    } else if constexpr (std::is_same<TW, __half>::value) {
+      f[e] = __half2float(p[e]);
+    } else {
+      f[e] = __bfloat162float(p[e]);
     }
   }
 }
 
-// One row's backward; accumulates do s x_hat.to(T) into dwa when DW.
-template <typename T, typename TW, int CH, bool DW>
-__device__ __forceinline__ void gnorm_bwd_row(const T* __restrict__ x, const T* __restrict__ z,
-                                              const TW* __restrict__ w, const T* __restrict__ dout,
-                                              T* __restrict__ dx, T* __restrict__ dz, long long row, int D, float eps,
-                                              bool round_h, int lane, float4 (&dwa)[CH]) {
-  const size_t base = (size_t)row * D;
-  float4 xv[CH], zv[CH], gv[CH];
+// sum over the team (lanes that differ only in the low team_log2 bits); every lane of the warp takes part
+__device__ __forceinline__ float team_sum(float v, int team_log2) {
+  for (int o = (1 << team_log2) >> 1; o >= 1; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// A team's view of the grid: the row it owns, its lane inside the team
+struct Team {
+  int log2, sub;
+  long long row;
+  __device__ __forceinline__ Team(int team_log2, long long first_row_of_warp) {
+    const int lane = threadIdx.x & 31;
+    log2 = team_log2;
+    sub = lane & ((1 << team_log2) - 1);
+    row = first_row_of_warp + (lane >> team_log2);
+  }
+  __device__ __forceinline__ int elem(int j, int E) const { return (sub + (j << log2)) * E; }  // chunk j's first element
+};
+
+// ---- forward, any width: warp w of CTA b owns rows (8 b + w) R .. + R - 1, R = 32 / TEAM
+template <typename T, typename TW, int E, int NCH>
+__global__ void __launch_bounds__(kThreads) gnorm_team_fwd(const T* __restrict__ x, const T* __restrict__ z,
+                                                           const TW* __restrict__ w, T* __restrict__ o,
+                                                           long long rows, int D, int team_log2, float eps,
+                                                           bool round_h) {
+  const long long warp_row0 = ((long long)blockIdx.x * kWarps + (threadIdx.x >> 5)) << (5 - team_log2);
+  const Team tm(team_log2, warp_row0);
+  const bool live = tm.row < rows;
+  float xs[NCH][E], zs[NCH][E];
   float ss = 0.f;
 #pragma unroll
-  for (int j = 0; j < CH; ++j) {
-    const int i = col(j, lane);
-    const bool in = i < D;
-    xv[j] = in ? ld4(x + base + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-    zv[j] = in ? ld4(z + base + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-    gv[j] = in ? ld4(dout + base + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-  }
+  for (int j = 0; j < NCH; ++j) {  // all of the row's loads in flight before any arithmetic
+    const int e0 = tm.elem(j, E);
+    if (live && e0 < D) {
+      Chunk<T, E>::load(x + tm.row * D + e0, xs[j]);
+      Chunk<T, E>::load(z + tm.row * D + e0, zs[j]);
+    } else {
 #pragma unroll
-  for (int j = 0; j < CH; ++j) ss += dot4(xv[j], xv[j]);
-  const float r = inv_rms(warp_sum(ss), D, eps);
-  float acc = 0.f;
-#pragma unroll
-  for (int j = 0; j < CH; ++j) {
-    const int i = col(j, lane);
-    if (i < D) {
-      const float4 wv = ld4(w + i);
-      const float4 xn = scale4(xv[j], r);  // x_hat (fp32)
-      const float4 xr4 = rnd4<T>(xn);      // x_hat.to(T)
-      float4 h = mul4(wv, xr4);
-      if (round_h) h = rnd4<T>(h);
-      const float zz[4] = {zv[j].x, zv[j].y, zv[j].z, zv[j].w};
-      const float hh[4] = {h.x, h.y, h.z, h.w};
-      const float gg[4] = {gv[j].x, gv[j].y, gv[j].z, gv[j].w};
-      float dzv[4], gs[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float sg = sigmoid(zz[e]);
-        dzv[e] = gg[e] * hh[e] * sg * (1.f + zz[e] * (1.f - sg));
-        gs[e] = gg[e] * (zz[e] * sg);  // do silu(z)
-      }
-      st4(dz + base + i, make_float4(dzv[0], dzv[1], dzv[2], dzv[3]));
-      const float4 g4 = make_float4(gs[0], gs[1], gs[2], gs[3]);
-      gv[j] = mul4(g4, wv);  // dxh, kept in gv
-      acc += dot4(xn, gv[j]);
-      if constexpr (DW) {
-        const float4 t = mul4(g4, xr4);
-        dwa[j].x += t.x;
-        dwa[j].y += t.y;
-        dwa[j].z += t.z;
-        dwa[j].w += t.w;
-      }
+      for (int e = 0; e < E; ++e) xs[j][e] = zs[j][e] = 0.f;
     }
   }
-  const float c = warp_sum(acc) / (float)D;
 #pragma unroll
-  for (int j = 0; j < CH; ++j) {
-    const int i = col(j, lane);
-    if (i < D) {
-      const float4 xn = scale4(xv[j], r);
-      st4(dx + base + i, make_float4(r * (gv[j].x - xn.x * c), r * (gv[j].y - xn.y * c), r * (gv[j].z - xn.z * c),
-                                     r * (gv[j].w - xn.w * c)));
+  for (int j = 0; j < NCH; ++j)
+#pragma unroll
+    for (int e = 0; e < E; ++e) ss = fmaf(xs[j][e], xs[j][e], ss);
+  const float r = inv_rms(team_sum(ss, team_log2), D, eps);
+#pragma unroll
+  for (int j = 0; j < NCH; ++j) {
+    const int e0 = tm.elem(j, E);
+    if (!live || e0 >= D) continue;
+    float wv[E], out[E];
+    load_weights<TW, E>(w + e0, wv);
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      float h = wv[e] * rnd<T>(xs[j][e] * r);
+      if (round_h) h = rnd<T>(h);
+      out[e] = h * (zs[j][e] * sigmoid(zs[j][e]));
     }
+    Chunk<T, E>::store(o + tm.row * D + e0, out);
   }
 }
 
-// No dw: one row a warp. With dw: CTA p takes rows [p rpb, (p + 1) rpb), warp k rows k, k + 8, ...; the CTA's column
-// sums (warps in order) go to partial row p.
-template <typename T, typename TW, int CH, bool DW>
-__global__ void __launch_bounds__(kThreads) gnorm_bwd_kernel(const T* __restrict__ x, const T* __restrict__ z,
-                                                             const TW* __restrict__ w, const T* __restrict__ dout,
-                                                             T* __restrict__ dx, T* __restrict__ dz,
-                                                             float* __restrict__ part, long long rows, int D,
-                                                             float eps, bool round_h, long long rpb) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  float4 dwa[CH];
+// ---- backward, any width. No dw: rows as the forward. With dw: CTA p takes rows [p rpb, (p + 1) rpb) (rpb a
+// multiple of 8 R), warp w the blocks of R rows w, w + 8, ...; a lane keeps its chunks' dw sums, the CTA's teams are
+// added in team order into partial row p (dynamic shared memory [8 R][D] floats).
+template <typename T, typename TW, int E, int NCH, bool DW>
+__global__ void __launch_bounds__(kThreads) gnorm_team_bwd(const T* __restrict__ x, const T* __restrict__ z,
+                                                           const TW* __restrict__ w, const T* __restrict__ dout,
+                                                           T* __restrict__ dx, T* __restrict__ dz,
+                                                           float* __restrict__ part, long long rows, int D,
+                                                           int team_log2, float eps, bool round_h, long long rpb) {
+  const int warp = threadIdx.x >> 5;
+  const int R = 32 >> team_log2;
+  float wsum[NCH][E];
 #pragma unroll
-  for (int j = 0; j < CH; ++j) dwa[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-  if constexpr (!DW) {
-    const long long row = (long long)blockIdx.x * kWarps + warp;
-    if (row < rows) gnorm_bwd_row<T, TW, CH, false>(x, z, w, dout, dx, dz, row, D, eps, round_h, lane, dwa);
+  for (int j = 0; j < NCH; ++j)
+#pragma unroll
+    for (int e = 0; e < E; ++e) wsum[j][e] = 0.f;
+  long long first, end, step;
+  if constexpr (DW) {
+    first = (long long)blockIdx.x * rpb + (long long)warp * R;
+    end = (long long)blockIdx.x * rpb + rpb < rows ? (long long)blockIdx.x * rpb + rpb : rows;
+    step = (long long)kWarps * R;
   } else {
-    __shared__ __align__(16) float red[kWarps][kMaxD];
-    const long long r0 = (long long)blockIdx.x * rpb;
-    const long long r1 = r0 + rpb < rows ? r0 + rpb : rows;
-    for (long long row = r0 + warp; row < r1; row += kWarps)
-      gnorm_bwd_row<T, TW, CH, true>(x, z, w, dout, dx, dz, row, D, eps, round_h, lane, dwa);
+    first = ((long long)blockIdx.x * kWarps + warp) * R;
+    end = rows;
+    step = rows;  // one block of rows
+  }
+  int sub = 0;
+  for (long long base = first; base < end; base += step) {
+    const Team tm(team_log2, base);
+    sub = tm.sub;
+    const bool live = tm.row < end;
+    float xs[NCH][E], zs[NCH][E], gs[NCH][E];
+    float ss = 0.f;
 #pragma unroll
-    for (int j = 0; j < CH; ++j) {
-      const int i = col(j, lane);
-      if (i < D) *reinterpret_cast<float4*>(&red[warp][i]) = dwa[j];
+    for (int j = 0; j < NCH; ++j) {
+      const int e0 = tm.elem(j, E);
+      if (live && e0 < D) {
+        Chunk<T, E>::load(x + tm.row * D + e0, xs[j]);
+        Chunk<T, E>::load(z + tm.row * D + e0, zs[j]);
+        Chunk<T, E>::load(dout + tm.row * D + e0, gs[j]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < E; ++e) xs[j][e] = zs[j][e] = gs[j][e] = 0.f;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < NCH; ++j)
+#pragma unroll
+      for (int e = 0; e < E; ++e) ss = fmaf(xs[j][e], xs[j][e], ss);
+    const float r = inv_rms(team_sum(ss, team_log2), D, eps);
+    float dot = 0.f;  // <x_hat, dxh> over the lane's elements
+#pragma unroll
+    for (int j = 0; j < NCH; ++j) {
+      const int e0 = tm.elem(j, E);
+      float wv[E];
+      if (e0 < D) {
+        load_weights<TW, E>(w + e0, wv);
+      } else {
+#pragma unroll
+        for (int e = 0; e < E; ++e) wv[e] = 0.f;
+      }
+      float dzv[E];
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        const float xn = xs[j][e] * r;
+        const float xq = rnd<T>(xn);
+        float h = wv[e] * xq;
+        if (round_h) h = rnd<T>(h);
+        const float zz = zs[j][e], sg = sigmoid(zz);
+        dzv[e] = gs[j][e] * h * sg * (1.f + zz * (1.f - sg));
+        const float gsl = gs[j][e] * (zz * sg);  // dout silu(z)
+        if constexpr (DW) wsum[j][e] = fmaf(gsl, xq, wsum[j][e]);
+        gs[j][e] = gsl * wv[e];                  // dxh
+        dot = fmaf(xn, gs[j][e], dot);
+        xs[j][e] = xn;
+      }
+      if (live && e0 < D) Chunk<T, E>::store(dz + tm.row * D + e0, dzv);
+    }
+    const float cmean = team_sum(dot, team_log2) / (float)D;
+#pragma unroll
+    for (int j = 0; j < NCH; ++j) {
+      const int e0 = tm.elem(j, E);
+      if (!live || e0 >= D) continue;
+      float out[E];
+#pragma unroll
+      for (int e = 0; e < E; ++e) out[e] = r * (gs[j][e] - xs[j][e] * cmean);
+      Chunk<T, E>::store(dx + tm.row * D + e0, out);
+    }
+  }
+  if constexpr (DW) {
+    extern __shared__ __align__(16) float red[];  // [8 R teams][D]
+    const int team = warp * R + ((threadIdx.x & 31) >> team_log2);
+    if (first >= end) sub = (threadIdx.x & 31) & ((1 << team_log2) - 1);
+#pragma unroll
+    for (int j = 0; j < NCH; ++j) {
+      const int e0 = (sub + (j << team_log2)) * E;
+      if (e0 < D)
+#pragma unroll
+        for (int e = 0; e < E; ++e) red[(size_t)team * D + e0 + e] = wsum[j][e];
     }
     __syncthreads();
     for (int i = threadIdx.x; i < D; i += kThreads) {
       float s = 0.f;
-#pragma unroll
-      for (int k = 0; k < kWarps; ++k) s += red[k][i];
+      for (int k = 0; k < kWarps * R; ++k) s += red[(size_t)k * D + i];
       part[(size_t)blockIdx.x * D + i] = s;
     }
   }
@@ -446,10 +502,89 @@ void partition(long long rows, long long unit, long long& rpb, int& P) {
 int status_of(cudaError_t e) { return e == cudaSuccess ? GD_OK : GD_ERR_LAUNCH; }
 bool aligned16(const void* p) { return p == nullptr || (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-template <typename T, typename TW, int CH>
-int fwd_c(const void* x, const void* z, const void* w, void* o, long long rows, int D, float eps, bool round_h,
-          cudaStream_t st) {
-  if constexpr (sizeof(T) == 2 && CH == 1) {
+// The team shape for width D: chunk E elements (16 bytes, or 8 when a 16-bit width is not a multiple of 8), D / E
+// chunks a row; up to 32 chunks: a team of the next power of two lanes, one chunk each; more: 32 lanes, NCH chunks each
+struct Shape {
+  int E, nch, team_log2;
+};
+template <typename T>
+Shape shape_for(int D) {
+  Shape s;
+  s.E = (sizeof(T) == 2 && D % 8 == 0) ? 8 : 4;
+  const int chunks = D / s.E;
+  if (chunks <= 32) {
+    s.nch = 1;
+    s.team_log2 = 0;
+    while ((1 << s.team_log2) < chunks) ++s.team_log2;
+  } else {
+    s.team_log2 = 5;
+    s.nch = chunks <= 64 ? 2 : (chunks <= 128 ? 4 : 8);
+  }
+  return s;
+}
+
+template <typename T, typename TW, int E, int NCH>
+int team_fwd(const void* x, const void* z, const void* w, void* o, long long rows, int D, int tl, float eps,
+             bool round_h, cudaStream_t st) {
+  const long long per = (long long)kWarps << (5 - tl);  // rows a CTA
+  gnorm_team_fwd<T, TW, E, NCH><<<(unsigned)((rows + per - 1) / per), kThreads, 0, st>>>(
+      static_cast<const T*>(x), static_cast<const T*>(z), static_cast<const TW*>(w), static_cast<T*>(o), rows, D, tl,
+      eps, round_h);
+  return status_of(cudaGetLastError());
+}
+
+template <typename T, typename TW, int E, int NCH>
+int team_bwd(const void* x, const void* z, const void* w, const void* dout, void* dx, void* dz, void* dw,
+             long long rows, int D, int tl, float eps, bool round_h, void* ws, cudaStream_t st) {
+  const T* xp = static_cast<const T*>(x);
+  const T* zp = static_cast<const T*>(z);
+  const TW* wp = static_cast<const TW*>(w);
+  const T* gp = static_cast<const T*>(dout);
+  const long long per = (long long)kWarps << (5 - tl);
+  if (dw == nullptr) {
+    gnorm_team_bwd<T, TW, E, NCH, false><<<(unsigned)((rows + per - 1) / per), kThreads, 0, st>>>(
+        xp, zp, wp, gp, static_cast<T*>(dx), static_cast<T*>(dz), nullptr, rows, D, tl, eps, round_h, 0);
+    return status_of(cudaGetLastError());
+  }
+  long long rpb;
+  int P;
+  partition(rows, per, rpb, P);
+  const size_t smem = (size_t)per * D * sizeof(float);
+  gnorm_team_bwd<T, TW, E, NCH, true><<<P, kThreads, smem, st>>>(xp, zp, wp, gp, static_cast<T*>(dx),
+                                                                   static_cast<T*>(dz), static_cast<float*>(ws), rows,
+                                                                   D, tl, eps, round_h, rpb);
+  if (cudaGetLastError() != cudaSuccess) return GD_ERR_LAUNCH;
+  gnorm_dw_sum_kernel<TW><<<(D + 31) / 32, dim3(32, 32), 0, st>>>(static_cast<float*>(ws), P, D,
+                                                                   static_cast<TW*>(dw));
+  return status_of(cudaGetLastError());
+}
+
+// the chunk width E and chunks a lane NCH as template arguments
+template <typename T, typename TW, int E>
+int fwd_e(const Shape& s, const void* x, const void* z, const void* w, void* o, long long rows, int D, float eps,
+          bool round_h, cudaStream_t st) {
+  switch (s.nch) {
+    case 1: return team_fwd<T, TW, E, 1>(x, z, w, o, rows, D, s.team_log2, eps, round_h, st);
+    case 2: return team_fwd<T, TW, E, 2>(x, z, w, o, rows, D, s.team_log2, eps, round_h, st);
+    case 4: return team_fwd<T, TW, E, 4>(x, z, w, o, rows, D, s.team_log2, eps, round_h, st);
+    default: return team_fwd<T, TW, E, 8>(x, z, w, o, rows, D, s.team_log2, eps, round_h, st);
+  }
+}
+template <typename T, typename TW, int E>
+int bwd_e(const Shape& s, const void* x, const void* z, const void* w, const void* dout, void* dx, void* dz, void* dw,
+          long long rows, int D, float eps, bool round_h, void* ws, cudaStream_t st) {
+  switch (s.nch) {
+    case 1: return team_bwd<T, TW, E, 1>(x, z, w, dout, dx, dz, dw, rows, D, s.team_log2, eps, round_h, ws, st);
+    case 2: return team_bwd<T, TW, E, 2>(x, z, w, dout, dx, dz, dw, rows, D, s.team_log2, eps, round_h, ws, st);
+    case 4: return team_bwd<T, TW, E, 4>(x, z, w, dout, dx, dz, dw, rows, D, s.team_log2, eps, round_h, ws, st);
+    default: return team_bwd<T, TW, E, 8>(x, z, w, dout, dx, dz, dw, rows, D, s.team_log2, eps, round_h, ws, st);
+  }
+}
+
+template <typename T, typename TW>
+int fwd_t(const void* x, const void* z, const void* w, void* o, long long rows, int D, float eps, cudaStream_t st) {
+  const bool round_h = sizeof(T) == sizeof(TW);
+  if constexpr (sizeof(T) == 2) {
     if (D == 128) {
       const long long per = (long long)kWarps * 2 * kRP;
       gnorm_fwd128_kernel<T, TW><<<(unsigned)((rows + per - 1) / per), kThreads, 0, st>>>(
@@ -458,71 +593,46 @@ int fwd_c(const void* x, const void* z, const void* w, void* o, long long rows, 
       return status_of(cudaGetLastError());
     }
   }
-  const long long blocks = (rows + kWarps - 1) / kWarps;
-  gnorm_fwd_kernel<T, TW, CH><<<(unsigned)blocks, kThreads, 0, st>>>(
-      static_cast<const T*>(x), static_cast<const T*>(z), static_cast<const TW*>(w), static_cast<T*>(o), rows, D, eps,
-      round_h);
-  return status_of(cudaGetLastError());
-}
-
-template <typename T, typename TW, int CH>
-int bwd_c(const void* x, const void* z, const void* w, const void* dout, void* dx, void* dz, void* dw, long long rows,
-          int D, float eps, bool round_h, void* ws, cudaStream_t st) {
-  const T* xp = static_cast<const T*>(x);
-  const T* zp = static_cast<const T*>(z);
-  const TW* wp = static_cast<const TW*>(w);
-  const T* gp = static_cast<const T*>(dout);
-  T* dxp = static_cast<T*>(dx);
-  T* dzp = static_cast<T*>(dz);
-  float* part = static_cast<float*>(ws);
-  long long rpb = 0;
-  int P = 0;
-  if (dw) partition(rows, sizeof(T) == 2 && D == 128 ? (long long)kWarps * 2 * kRP : kWarps, rpb, P);
-  bool done = false;
-  if constexpr (sizeof(T) == 2 && CH == 1) {
-    if (D == 128) {
-      const long long per = (long long)kWarps * 2 * kRP;
-      if (dw == nullptr)
-        gnorm_bwd128_kernel<T, TW, false><<<(unsigned)((rows + per - 1) / per), kThreads, 0, st>>>(
-            xp, zp, wp, gp, dxp, dzp, nullptr, rows, eps, round_h, 0);
-      else
-        gnorm_bwd128_kernel<T, TW, true><<<P, kThreads, 0, st>>>(xp, zp, wp, gp, dxp, dzp, part, rows, eps, round_h,
-                                                                 rpb);
-      done = true;
-    }
+  const Shape s = shape_for<T>(D);
+  if constexpr (sizeof(T) == 2) {
+    if (s.E == 8) return fwd_e<T, TW, 8>(s, x, z, w, o, rows, D, eps, round_h, st);
   }
-  if (!done) {
-    if (dw == nullptr)
-      gnorm_bwd_kernel<T, TW, CH, false><<<(unsigned)((rows + kWarps - 1) / kWarps), kThreads, 0, st>>>(
-          xp, zp, wp, gp, dxp, dzp, nullptr, rows, D, eps, round_h, 0);
-    else
-      gnorm_bwd_kernel<T, TW, CH, true><<<P, kThreads, 0, st>>>(xp, zp, wp, gp, dxp, dzp, part, rows, D, eps,
-                                                                round_h, rpb);
-  }
-  if (cudaGetLastError() != cudaSuccess) return GD_ERR_LAUNCH;
-  if (dw == nullptr) return GD_OK;
-  gnorm_dw_sum_kernel<TW><<<(D + 31) / 32, dim3(32, 32), 0, st>>>(part, P, D, static_cast<TW*>(dw));
-  return status_of(cudaGetLastError());
-}
-
-// CH = ceil(D / 128) column groups: 1, 2, 4 or 8 (D <= 1024)
-template <typename T, typename TW>
-int fwd_t(const void* x, const void* z, const void* w, void* o, long long rows, int D, float eps, cudaStream_t st) {
-  const bool round_h = sizeof(T) == sizeof(TW);
-  if (D <= 128) return fwd_c<T, TW, 1>(x, z, w, o, rows, D, eps, round_h, st);
-  if (D <= 256) return fwd_c<T, TW, 2>(x, z, w, o, rows, D, eps, round_h, st);
-  if (D <= 512) return fwd_c<T, TW, 4>(x, z, w, o, rows, D, eps, round_h, st);
-  return fwd_c<T, TW, 8>(x, z, w, o, rows, D, eps, round_h, st);
+  return fwd_e<T, TW, 4>(s, x, z, w, o, rows, D, eps, round_h, st);
 }
 
 template <typename T, typename TW>
 int bwd_t(const void* x, const void* z, const void* w, const void* dout, void* dx, void* dz, void* dw, long long rows,
           int D, float eps, void* ws, cudaStream_t st) {
   const bool round_h = sizeof(T) == sizeof(TW);
-  if (D <= 128) return bwd_c<T, TW, 1>(x, z, w, dout, dx, dz, dw, rows, D, eps, round_h, ws, st);
-  if (D <= 256) return bwd_c<T, TW, 2>(x, z, w, dout, dx, dz, dw, rows, D, eps, round_h, ws, st);
-  if (D <= 512) return bwd_c<T, TW, 4>(x, z, w, dout, dx, dz, dw, rows, D, eps, round_h, ws, st);
-  return bwd_c<T, TW, 8>(x, z, w, dout, dx, dz, dw, rows, D, eps, round_h, ws, st);
+  if constexpr (sizeof(T) == 2) {
+    if (D == 128) {
+      const T* xp = static_cast<const T*>(x);
+      const T* zp = static_cast<const T*>(z);
+      const TW* wp = static_cast<const TW*>(w);
+      const T* gp = static_cast<const T*>(dout);
+      const long long per = (long long)kWarps * 2 * kRP;
+      if (dw == nullptr) {
+        gnorm_bwd128_kernel<T, TW, false><<<(unsigned)((rows + per - 1) / per), kThreads, 0, st>>>(
+            xp, zp, wp, gp, static_cast<T*>(dx), static_cast<T*>(dz), nullptr, rows, eps, round_h, 0);
+        return status_of(cudaGetLastError());
+      }
+      long long rpb;
+      int P;
+      partition(rows, per, rpb, P);
+      gnorm_bwd128_kernel<T, TW, true><<<P, kThreads, 0, st>>>(xp, zp, wp, gp, static_cast<T*>(dx),
+                                                               static_cast<T*>(dz), static_cast<float*>(ws), rows, eps,
+                                                               round_h, rpb);
+      if (cudaGetLastError() != cudaSuccess) return GD_ERR_LAUNCH;
+      gnorm_dw_sum_kernel<TW><<<(D + 31) / 32, dim3(32, 32), 0, st>>>(static_cast<float*>(ws), P, D,
+                                                                       static_cast<TW*>(dw));
+      return status_of(cudaGetLastError());
+    }
+  }
+  const Shape s = shape_for<T>(D);
+  if constexpr (sizeof(T) == 2) {
+    if (s.E == 8) return bwd_e<T, TW, 8>(s, x, z, w, dout, dx, dz, dw, rows, D, eps, round_h, ws, st);
+  }
+  return bwd_e<T, TW, 4>(s, x, z, w, dout, dx, dz, dw, rows, D, eps, round_h, ws, st);
 }
 
 // w has x's dtype or is fp32 (the reference's supported(), _gated_norm.py:148-151)

@@ -89,6 +89,15 @@ def test_other_widths_and_float32_weight(d):
     check(300, d, torch.bfloat16, True, wdtype=torch.float32, seed=20)
 
 
+@pytest.mark.parametrize("dtype", DTYPES, ids=DT.get)
+@pytest.mark.parametrize("d", [4, 20, 100, 520])
+def test_team_shapes(d, dtype):
+    """Every row-team shape of the generic kernels: one lane a row (d = 4), teams of 8 and 32 lanes with 8-byte chunks
+    at 16 bits (20, 100: not multiples of 8), and 32-lane teams holding several chunks each with the last ones past
+    the row (520), trained weight included."""
+    check(257, d, dtype, True, seed=50 + d)
+
+
 def test_large_rows_weight_gradient():
     """More rows than the backward's partial rows (1024 CTAs): every CTA sums several rows per warp."""
     check(70_000, 128, torch.bfloat16, True, seed=30)
