@@ -48,11 +48,17 @@ METRIC = "gated-delta fwd+bwd tokens/s (B4 T1024 H16 d128 bf16)"
 # the reference's own published number for this shape and pass (Apple M3 Max, Metal; not re-measurable here): 10.210 ms fwd+bwd at B4 T1024 H16 -> 401,175 tokens/s (docs/series_layer.md:1679-1684 of the reference)
 PUBLISHED_TOKENS_S = 4 * 1024 / 10.210e-3
 CONFIGS = {
-    # name: (B, T, H value heads, HK key heads, D, with s0 / final state, forward only)
-    1: dict(B=4, T=1024, H=16, HK=16, D=128, s0=False, fwd_only=False, tag="c1: B4 T1024 H16 d128 fwd+bwd"),
-    2: dict(B=2, T=1024, H=32, HK=16, D=128, s0=True, fwd_only=False, tag="c2: B2 T1024 Hk16 Hv32 d128 fwd+bwd, s0"),
-    3: dict(B=1, T=32768, H=32, HK=32, D=128, s0=False, fwd_only=True, tag="c3: B1 T32768 H32 d128 forward"),
-    4: dict(B=64, T=4096, H=32, HK=32, D=128, s0=False, fwd_only=False, tag="c4: B64 T4096 H32 d128 fwd+bwd"),
+    # B, T, H value heads, HK key heads, D; s0: an initial state (and its gradient); final: the final state is
+    # returned (output_final_state); forward only. Config 1 is called as the reference's benchmark calls it
+    # (bench/bench_gated_delta.py:64-83: the output only, no initial or final state).
+    1: dict(B=4, T=1024, H=16, HK=16, D=128, s0=False, final=False, fwd_only=False,
+            tag="c1: B4 T1024 H16 d128 fwd+bwd"),
+    2: dict(B=2, T=1024, H=32, HK=16, D=128, s0=True, final=True, fwd_only=False,
+            tag="c2: B2 T1024 Hk16 Hv32 d128 fwd+bwd, s0"),
+    3: dict(B=1, T=32768, H=32, HK=32, D=128, s0=False, final=True, fwd_only=True,
+            tag="c3: B1 T32768 H32 d128 forward"),
+    4: dict(B=64, T=4096, H=32, HK=32, D=128, s0=False, final=False, fwd_only=False,
+            tag="c4: B64 T4096 H32 d128 fwd+bwd"),
 }
 # per token-head algorithmic work, D = 128, C = 64 (fixed formula; the backward's recompute is not credited)
 FLOP_FWD, FLOP_BWD = 181_589, 409_600
@@ -157,7 +163,7 @@ def cpu_reference(cfg, steps, warmup, sample_batch=1, threads=None):
         t0 = time.perf_counter()
         qx = xs[0].repeat_interleave(rep, 2) if rep > 1 else xs[0]
         kx = xs[1].repeat_interleave(rep, 2) if rep > 1 else xs[1]
-        o, sT = f(qx, kx, xs[2], xs[3], xs[4], chunk_size=64, initial_state=s0, output_final_state=True,
+        o, sT = f(qx, kx, xs[2], xs[3], xs[4], chunk_size=64, initial_state=s0, output_final_state=cfg["final"],
                   use_qk_l2norm_in_kernel=True)
         if not cfg["fwd_only"]:
             loss = (o.float() * t["do"].float()).sum()
@@ -276,12 +282,12 @@ def main():
     nbytes = lib.gd_workspace_bytes(B, T, H, HK, D, D, 0 if cfg["fwd_only"] else 1)
     ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
     o = torch.empty(B, T, H, D, dtype=torch.bfloat16, device=dev)
-    sT = torch.empty(B, H, D, D, dtype=torch.float32, device=dev)
+    sT = torch.empty(B, H, D, D, dtype=torch.float32, device=dev) if cfg["final"] else None
     dq, dk = torch.empty_like(t["q"]), torch.empty_like(t["k"])
     dv = torch.empty_like(t["v"])
     dg = torch.empty(B, T, H, dtype=torch.float32, device=dev)
     db = torch.empty_like(dg)
-    ds0 = torch.empty(B, H, D, D, dtype=torch.float32, device=dev)
+    ds0 = torch.empty(B, H, D, D, dtype=torch.float32, device=dev) if cfg["s0"] else None
     P = lambda x: None if x is None else ctypes.c_void_p(x.data_ptr())
     stream = torch.cuda.Stream(device=dev)
     sp = ctypes.c_void_p(stream.cuda_stream)
@@ -1124,10 +1130,11 @@ def end_to_end(lib, t, cfg, flags, ws, nbytes, stream, args):
         names_in = [n for n in names_in if n not in ("do", "dsT")]
     specs_in = [(n, t[n].shape, t[n].dtype) for n in names_in]
     f32, bf = torch.float32, torch.bfloat16
-    specs_out = [("o", (B, T, H, D), bf), ("sT", (B, H, D, D), f32)]
+    specs_out = [("o", (B, T, H, D), bf)] + ([("sT", (B, H, D, D), f32)] if cfg["final"] else [])
     if not cfg["fwd_only"]:
         specs_out += [("dq", tuple(t["q"].shape), bf), ("dk", tuple(t["k"].shape), bf), ("dv", tuple(t["v"].shape), bf),
-                      ("dg", tuple(t["g"].shape), f32), ("db", tuple(t["g"].shape), f32), ("ds0", (B, H, D, D), f32)]
+                      ("dg", tuple(t["g"].shape), f32), ("db", tuple(t["g"].shape), f32)]
+        specs_out += [("ds0", (B, H, D, D), f32)] if cfg["s0"] else []
 
     def packed_set(specs, **kw):
         """One uint8 buffer and a view per tensor (256-byte aligned offsets)."""
@@ -1171,12 +1178,12 @@ def end_to_end(lib, t, cfg, flags, ws, nbytes, stream, args):
         if used[b]:
             stream.wait_event(out_done[b])  # step i - 2's outputs have been copied out
         st = lib.gd_forward(P(d["q"]), P(d["k"]), P(d["v"]), P(d["g"]), P(d["beta"]), P(d.get("s0")), P(o["o"]),
-                            P(o["sT"]), BF, B, T, H, HK, D, D, flags, P(ws), nbytes, sp)
+                            P(o.get("sT")), BF, B, T, H, HK, D, D, flags, P(ws), nbytes, sp)
         _lib.check(st, "gd_forward")
         if not cfg["fwd_only"]:
             st = lib.gd_backward(P(d["q"]), P(d["k"]), P(d["v"]), P(d["g"]), P(d["beta"]), P(d.get("s0")),
                                  P(d["do"]), P(d.get("dsT")), P(o["dq"]), P(o["dk"]), P(o["dv"]), P(o["dg"]),
-                                 P(o["db"]), P(o["ds0"]), BF, B, T, H, HK, D, D, flags, P(ws), nbytes, sp)
+                                 P(o["db"]), P(o.get("ds0")), BF, B, T, H, HK, D, D, flags, P(ws), nbytes, sp)
             _lib.check(st, "gd_backward")
         comp_done[b].record(stream)
         with torch.cuda.stream(s_out):
