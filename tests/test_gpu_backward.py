@@ -67,3 +67,24 @@ def test_backward_is_deterministic():
     for i in (1, 2):
         for a, b in zip(runs[0], runs[i]):
             assert parity.identical(a, b)
+
+
+def test_backward_many_heads():
+    """B * H = 80 value heads (160 state-pass CTAs on 148 SMs: a second wave): forward and backward against float64
+    with the bar, and bitwise equal to the same heads run two at a time (one wave)."""
+    q, k, v, g, beta, st = inputs(1, 130, 80, seed=17)
+    gen = torch.Generator().manual_seed(18)
+    do = torch.randn(1, 130, 80, 128, generator=gen).to(torch.bfloat16)
+    dsT = torch.randn(1, 80, 128, 128, generator=gen) * 0.1
+    got = run_grads(q, k, v, g, beta, st, do, dsT)
+    truth = ref.dropin(q, k, v, g, beta, st, do.double(), dsT)
+    theirs = transformers_ref.run(q, k, v, g, beta, st, do=do, dsT=dsT)
+    rep = parity.check(got, theirs, truth, names=NAMES)
+    assert not parity.failures(rep), {k_: round(v_["ratio"], 3) for k_, v_ in rep.items()}
+    sl = slice(40, 42)   # two of the heads alone
+    few = run_grads(q[:, :, sl], k[:, :, sl], v[:, :, sl], g[:, :, sl], beta[:, :, sl], st[:, sl], do[:, :, sl],
+                    dsT[:, sl])
+    part = lambda x, dim: x.narrow(dim, 40, 2)
+    dims = (2, 1, 2, 2, 2, 2, 2, 1)   # head dimension of o, S_T, dq, dk, dv, dg, dbeta, ds0
+    for a, b, d in zip(got, few, dims):
+        assert parity.identical(part(a, d), b)
