@@ -1001,12 +1001,15 @@ def kernel_times(lib, t, cfg, flags, ws, nbytes, o, sT, dq, dk, dv, dg, db, ds0,
     sp = ctypes.c_void_p(stream.cuda_stream)
     B, T, H, HK, D = cfg["B"], cfg["T"], cfg["H"], cfg["HK"], cfg["D"]
     BF = _lib.GD_BFLOAT16
+    # the forward pair in the forward-only layout, as gd_forward runs it (the layout follows the size passed)
+    nf = lib.gd_workspace_bytes(B, T, H, HK, D, D, 0)
     seq = [("prep", lambda: lib.gd_prep(P(t["q"]), P(t["k"]), P(t["v"]), P(t["g"]), P(t["beta"]), BF, B, T, H, HK, D, D,
-                                        flags, P(ws), nbytes, sp)),
-           ("fwd_state", lambda: lib.gd_fwd_state(P(t["s0"]), P(o), P(sT), BF, B, T, H, HK, D, D, flags, P(ws), nbytes,
+                                        flags, P(ws), nf, sp)),
+           ("fwd_state", lambda: lib.gd_fwd_state(P(t["s0"]), P(o), P(sT), BF, B, T, H, HK, D, D, flags, P(ws), nf,
                                                   sp))]
     if not cfg["fwd_only"]:
-        seq += [("prep(bwd)", seq[0][1]),
+        seq += [("prep(bwd)", lambda: lib.gd_prep(P(t["q"]), P(t["k"]), P(t["v"]), P(t["g"]), P(t["beta"]), BF, B, T,
+                                                  H, HK, D, D, flags, P(ws), nbytes, sp)),
                 ("fwd_state(store)", lambda: lib.gd_fwd_state(P(t["s0"]), None, None, BF, B, T, H, HK, D, D,
                                                               flags | _lib.GD_STORE_STATES, P(ws), nbytes, sp)),
                 ("bwd_state", lambda: lib.gd_bwd_state(P(t["do"]), P(t["dsT"]), P(ds0), BF, B, T, H, HK, D, D, flags,

@@ -14,8 +14,8 @@
 // the per-chunk images to global memory straight from registers), one MMA thread and one loader thread (every refill
 // waits on the product that frees its buffer, which is also the product whose next phase needs that refill); all
 // hand-offs are mbarriers. Per chunk the MMA thread issues only: K~ dS (chain) -> -W^T dVn (chain, added onto the
-// chunk's (gamma Q)^T dO) -> the next chunk's dS-independent products. Precision: dS and K~ split into bf16 hi + lo
-// (three products), gamma Q and M split, the rest bf16.
+// chunk's (gamma Q)^T dO) -> the next chunk's dS-independent products. Precision: dS and K~, dVn and W split into
+// bf16 hi + lo (three products each), gamma Q and M split, dO exact in bf16.
 #include "gd_common.cuh"
 #include "gd_layout.cuh"
 
@@ -27,18 +27,20 @@ struct BwdStateSmem {
   static constexpr size_t dsh = 0;                         // [DVH x DK] dS^T hi (rows v, cols dk)
   static constexpr size_t dsl = dsh + DVH * DK * 2;        //             lo
   static constexpr size_t dvh = dsl + DVH * DK * 2;        // [DVH x 64] dVn^T hi
-  static constexpr size_t crit0 = dvh + DVH * 64 * 2;      // two stages of the sequential chain, each:
+  static constexpr size_t dvl = dvh + DVH * 64 * 2;        //              lo
+  static constexpr size_t crit0 = dvl + DVH * 64 * 2;      // two stages of the sequential chain, each:
   static constexpr size_t c_kt = 0;                        //   [2][64 x DK] K~ hi, lo
   static constexpr size_t c_g = c_kt + 2 * 64 * DK * 2;    //   [64] G
   static constexpr size_t crit_bytes = c_g + 64 * 4;
-  static constexpr size_t wt = crit0 + 2 * crit_bytes;     // [DK x 64] W^T (one buffer)
-  static constexpr size_t m = wt + DK * 64 * 2;            // [2][64 x 64] M hi, lo } inputs of the dS-independent
+  static constexpr size_t wt = crit0 + 2 * crit_bytes;     // [2][DK x 64] W^T hi, lo (one buffer)
+  static constexpr size_t m = wt + 2 * DK * 64 * 2;        // [2][64 x 64] M hi, lo } inputs of the dS-independent
   static constexpr size_t gq = m + 2 * 64 * 64 * 2;        // [2][64 x DK] gamma Q }  products, one chunk ahead
   static constexpr size_t dO = gq + 2 * 64 * DK * 2;       // [64 x DVH] dO      }
   static constexpr size_t bar = dO + 64 * DVH * 2;
   static constexpr int NBAR = 12;
   static constexpr size_t tmem = bar + NBAR * 8;
   static constexpr size_t total = tmem + 8;
+  static_assert(total <= 232448, "within the 227 KB a CTA can have");
 };
 
 template <typename T, int DK, int DV>
@@ -103,8 +105,10 @@ __global__ void __launch_bounds__(576) bwd_state_kernel(const T* __restrict__ d_
     bulk_g2s(st + S::c_g, ws + lay.gc + (row0 + c) * lay.gc_bytes(), (uint32_t)lay.gc_bytes(), crit_full + s);
   };
   auto load_wt = [&](int c) {
-    mbar_arrive_expect_tx(wt_full, (uint32_t)lay.wt_bytes());
+    mbar_arrive_expect_tx(wt_full, 2 * (uint32_t)lay.wt_bytes());
     bulk_g2s(smem + S::wt, ws + lay.wt + (row0 + c) * lay.wt_bytes(), (uint32_t)lay.wt_bytes(), wt_full);
+    bulk_g2s(smem + S::wt + DK * 64 * 2, ws + lay.wtl + (row0 + c) * lay.wt_bytes(), (uint32_t)lay.wt_bytes(),
+             wt_full);
   };
   auto load_pre = [&](int c) {
     mbar_arrive_expect_tx(pre_full, (uint32_t)(lay.mm_bytes() + lay.qk_bytes()));
@@ -149,9 +153,16 @@ __global__ void __launch_bounds__(576) bwd_state_kernel(const T* __restrict__ d_
         if (!ok) break;
         GD_TRACE_ONE(ws, lay, 1024 + 8 * n + 3);
         tc_fence_after();
-        // * -(W^T dVn)^T = -dVn^T W [DVH x DK], onto this chunk's ((gamma Q)^T dO)^T
-        mma_tiles(tm + 192 + 128 * (n & 1), DVH, DK, 64, Tile{smem_u32(smem + S::dvh), 64}, true, 0, 0,
-                  Tile{smem_u32(smem + S::wt), 64}, false, 0, true, true);
+        // * -(W^T dVn)^T = -dVn^T W [DVH x DK], onto this chunk's ((gamma Q)^T dO)^T, dVn and W split (three
+        // products: with nearly parallel keys W^T dVn cancels to a small fraction of its terms)
+        {
+          const uint32_t tC = tm + 192 + 128 * (n & 1);
+          const Tile tVh{smem_u32(smem + S::dvh), 64}, tVl{smem_u32(smem + S::dvl), 64};
+          const Tile tWh{smem_u32(smem + S::wt), 64}, tWl{smem_u32(smem + S::wt + DK * 64 * 2), 64};
+          mma_tiles(tC, DVH, DK, 64, tVh, true, 0, 0, tWh, false, 0, true, true);
+          mma_tiles(tC, DVH, DK, 64, tVl, true, 0, 0, tWh, false, 0, true, true);
+          mma_tiles(tC, DVH, DK, 64, tVh, true, 0, 0, tWl, false, 0, true, true);
+        }
         mma_commit(d_full);
         GD_TRACE_ONE(ws, lay, 1024 + 8 * n + 4);
         if (c > 0) {  // the next chunk's dS-independent products, under this chunk's dS update
@@ -273,6 +284,7 @@ __global__ void __launch_bounds__(576) bwd_state_kernel(const T* __restrict__ d_
 #pragma unroll
         for (int j = 0; j < 8; ++j) split_bf16(a[j] + (bb[j] + b2[j]), a[j], bb[j]);  // in place: a = hi, bb = lo
         store8_bf16(smem + S::dvh, vl_, tk, 64, a);
+        store8_bf16(smem + S::dvl, vl_, tk, 64, bb);
         tc_fence_before();
         fence_async_smem();
         mbar_arrive_warp(dvn_full);

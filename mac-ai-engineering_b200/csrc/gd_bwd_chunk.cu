@@ -5,17 +5,17 @@
 // in a fixed order (one writer per gradient element: no atomics, bitwise reproducible).
 //
 // Inputs per sub-item, all bf16 images from the workspace copied whole by the bulk-copy engine: S_c^T and Vn^T (the
-// forward recompute), dS_{c+1}^T (hi, lo), dVn^T (hi, lo) and dO (the reverse pass), A, V^T and the transposed q / k
-// images (prep); G (prep) and the partial sums of <S_c, dS_{c+1}> (reverse pass) in fp32. From the caller:
+// forward recompute), dS_{c+1}^T (hi, lo), dVn^T (hi, lo) and dO (the reverse pass), A (hi, lo), V^T and the
+// transposed q / k images (prep); G (prep) and the partial sums of <S_c, dS_{c+1}> (reverse pass) in fp32. From the caller:
 // beta and, for the l2 prologue's backward, q and k.
 //
 // Products, all tcgen05 from blocked shared-memory tiles into TMEM ("[D x 64]" accumulators put the head dimension on
 // the 128 TMEM lanes; C x C ones use M = 64). TMEM blocks of 64 columns B0..B7:
-//   G1:  B0 dO Vn^T, B1 (dO S^T)^T, B2 (dVn S^T)^T, B3 (A^T dVn)^T (dVn split), B4 dVn V^T
-//   G3:  B6 (dM K)^T, B7 (dM^T Q)^T (dM, q and k split), B2 (A^T dW)^T (one commit), B1 dW K^T,
+//   G1:  B0 dO Vn^T, B1 (dO S^T)^T, B2 (dVn S^T)^T, B3 (A^T dVn)^T (dVn and A split), B4 dVn V^T (dVn split)
+//   G3:  B6 (dM K)^T, B7 (dM^T Q)^T (dM, q and k split), B2 (A^T dW)^T (A split; one commit), B1 dW K^T,
 //        B3 Q K^T (q and k split: M = Q K^T * Gamma in fp32 precision for R);   dW = -dVn S^T
 //   G2:  B5 (Vn dS^T)^T (Vn and dS split); after e2: B1 K K^T (k split, for L and the dbeta term)
-//   tail: B6 T1 = dA A^T, B7 A^T T1 (dL = -A^T T1; T1 split, its low half in the dA tile), B5 (K^T (P_beta + P_beta^T))
+//   tail: B6 T1 = dA A^T, B7 A^T T1 (dL = -A^T T1; dA, A and T1 split), B5 (K^T (P_beta + P_beta^T))
 //         with P_beta = diag(beta) (dL * Gamma)
 // Equations: tools/check_chunk_equations.py:49-76 and src/macai/gated_delta/_chunked.py:20-34 of the reference; dg is
 // summed without cancellation (the regrouping of _chunked.py:1138-1142, extended to the decay-mask terms):
@@ -27,9 +27,13 @@
 // thread issuing every MMA (in dependency order, whichever is ready first); warp 17 one thread issuing every bulk copy.
 // Shared memory holds one sub-item's tiles; each region is refilled for the next sub-item as soon as its last reader is
 // done (the TMEM block plan lets the next sub-item's G1 run under this one's tail):
-//   IN1 (S_c^T, dO, V^T; then dS^T)   free after G2        IN2 (dVn^T; then dM, dW^T)   free after G3
-//   IN3 (Vn^T)                        free after G2        A                            free after A^T T1
+//   IN1 (S_c^T, dO, V^T; then dS^T)   free after G2
+//   IN2 first half (dVn^T hi; then dM hi + lo)                          free after G3
+//   IN2 second half (dVn^T lo; then dW^T; then dA lo; then T1 lo)       free after A^T T1
+//   IN3 (Vn^T)                        free after G2        A hi, A lo (tail)            free after A^T T1
+//   tail (dA hi; then T1 hi; then P_beta)                               free after K^T P_beta
 //   QK (q^T, k^T hi + lo, rsqrt)      free after the item's last sub-item (the l2 backward reads x_hat from it)
+// dV, dq and dk (16-bit) are staged row-major in regions free at that moment and leave by tensor store.
 // All hand-offs are mbarriers; every wait is bounded and reports GD_ERR_TIMEOUT.
 #include "gd_common.cuh"
 #include "gd_layout.cuh"
@@ -56,9 +60,10 @@ struct ChunkSmem {
   static constexpr size_t in3 = in2 + 2 * DV * 64 * 2;      // 32 KB: [DV x 64] Vn^T hi, lo
   static constexpr size_t vnh = in3;
   static constexpr size_t vnl = in3 + DV * 64 * 2;
+  static constexpr size_t lo2 = dwt;                        // then [64 x 64] dA lo, then T1 lo (after G3)
   static constexpr size_t tail = in3 + 2 * DV * 64 * 2;     // 16 KB
-  static constexpr size_t da = tail;                        //   [64 x 64] dA, then P_beta
-  static constexpr size_t t1 = tail + 64 * 64 * 2;          //   [64 x 64] T1
+  static constexpr size_t alo = tail;                       //   [64 x 64] A lo
+  static constexpr size_t da = tail + 64 * 64 * 2;          //   [64 x 64] dA hi, then T1 hi, then P_beta
   static constexpr size_t g = tail + 2 * 64 * 64 * 2;       // fp32 [2][64] G (by sub-item parity)
   static constexpr size_t beta = g + 2 * 64 * 4;            // fp32 [64]
   static constexpr size_t part = beta + 64 * 4;             // fp32 [6][4][64] per-token partial sums (see kernel)
@@ -67,7 +72,7 @@ struct ChunkSmem {
   static constexpr size_t sl = rqk + 2 * 64 * 4;            // fp32 [2][32] <S_c, dS_{c+1}> partials (by parity)
   static constexpr size_t tok = sl + 2 * 32 * 4;            // fp32 [3][64] the sub-item's gamma_t, e_t, beta_t gamma_t
   static constexpr size_t bar = tok + 3 * 64 * 4;
-  static constexpr int NBAR = 22;
+  static constexpr int NBAR = 23;
   static constexpr size_t tmem = bar + NBAR * 8;
   static constexpr size_t total = tmem + 16;
   static_assert(dwt + DK * 64 * 2 <= in3, "dM and dW^T fit in the dVn region");
@@ -190,8 +195,8 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
   ErrorWord* err = reinterpret_cast<ErrorWord*>(ws + lay.err);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::bar);
-  uint64_t* in_full = bars + 0;    // IN1 + IN2 + IN3 + G of a sub-item (bulk-copy bytes)
-  uint64_t* a_full = bars + 1;
+  uint64_t* in_full = bars + 0;    // IN1, IN2's first half, IN3, G of a sub-item (bulk-copy bytes)
+  uint64_t* a_full = bars + 1;     // A hi and lo, IN2's second half (dVn^T lo)
   uint64_t* qk_full = bars + 2;    // once per item
   uint64_t* ds_full = bars + 3;
   uint64_t* g1_full = bars + 4;    // MMA commits
@@ -210,6 +215,7 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
   uint64_t* qk_free = bars + 18;   // 16 epilogue warps, once per item
   uint64_t* kk_full = bars + 20;   // MMA commit: K K^T
   uint64_t* g3a_full = bars + 21;  // MMA commit: the first part of G3 (B6, B7, B2)
+  uint64_t* dv_read = bars + 22;   // thread 0: the dV tensor store has read its staging rows (the dO tile)
   uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + S::tmem);
 
   const int NG = lay.B * lay.HK * lay.NT;
@@ -227,6 +233,7 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
     mbar_init(qk_free, 16);
     mbar_init(kk_full, 1);
     mbar_init(g3a_full, 1);
+    mbar_init(dv_read, 1);
     fence_mbar_init();
   }
   tc_fence_before();
@@ -246,8 +253,10 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
     if (lane == 0) {
       bool ok = true;
       int last_in = -1, last_a = -1, last_qk = -1, last_ds = -1;
+      const uint32_t half_vn = (uint32_t)lay.vn_bytes() / 2;  // one [DV x 64] image
       const uint32_t in_bytes =
-          (uint32_t)(lay.si_bytes() + 2 * lay.vi_bytes() + 2 * lay.vn_bytes() + lay.gc_bytes() + lay.sl_bytes());
+          (uint32_t)(lay.si_bytes() + 2 * lay.vi_bytes() + lay.vn_bytes() + lay.gc_bytes() + lay.sl_bytes()) +
+          half_vn;
       for (int n = 0; n < nsub && ok; ++n) {
         const Item it = item_of(lay, n);
         if (n >= 1) ok = mbar_wait(g3_full, (n - 1) & 1, err, 60);  // dM / dW^T (the IN2 region) consumed
@@ -255,7 +264,11 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
         mbar_arrive_expect_tx(in_full, in_bytes);
         GD_TRACE_ONE(ws, lay, 3500 + 4 * n + 0);
         last_in = n;
-        bulk_g2s(smem + S::in2, ws + lay.dvni + it.cidx * lay.vn_bytes(), (uint32_t)lay.vn_bytes(), in_full);
+        // dVn^T hi now; its lo half (the IN2 slot that carries dW^T, dA lo and T1 lo until dL) with A: both into L2 now
+        const unsigned char* dvn = ws + lay.dvni + it.cidx * lay.vn_bytes();
+        bulk_g2s(smem + S::dvh, dvn, half_vn, in_full);
+        prefetch_l2(dvn + half_vn, half_vn);
+        prefetch_l2(ws + lay.ai + it.cidx * lay.mm_bytes(), (uint32_t)lay.mm_bytes());
         if (n >= 1) ok = mbar_wait(g2_full, (n - 1) & 1, err, 61);                // dS^T and Vn^T consumed
         if (ok && n >= 2) ok = mbar_wait(epi_done + (n & 1), ((n - 2) >> 1) & 1, err, 62);  // G buffer n & 1 read
         if (!ok) break;
@@ -267,12 +280,15 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
         bulk_g2s(smem + S::g + (n & 1) * 256, ws + lay.gc + it.cidx * lay.gc_bytes(), (uint32_t)lay.gc_bytes(),
                  in_full);
         bulk_g2s(smem + S::sl + (n & 1) * 128, ws + lay.sl + it.cidx * lay.sl_bytes(), (uint32_t)lay.sl_bytes(), in_full);
-        if (n >= 1) ok = mbar_wait(dl_full, (n - 1) & 1, err, 63);  // A consumed
+        if (n >= 1) ok = mbar_wait(dl_full, (n - 1) & 1, err, 63);  // A hi / lo and T1 lo consumed
         if (!ok) break;
-        mbar_arrive_expect_tx(a_full, (uint32_t)lay.m_bytes());
+        mbar_arrive_expect_tx(a_full, (uint32_t)lay.mm_bytes() + half_vn);
         GD_TRACE_ONE(ws, lay, 3500 + 4 * n + 2);
         last_a = n;
-        bulk_g2s(smem + S::a, ws + lay.ai + it.cidx * lay.m_bytes(), (uint32_t)lay.m_bytes(), a_full);
+        const unsigned char* aimg = ws + lay.ai + it.cidx * lay.mm_bytes();
+        bulk_g2s(smem + S::a, aimg, (uint32_t)lay.m_bytes(), a_full);
+        bulk_g2s(smem + S::alo, aimg + lay.m_bytes(), (uint32_t)lay.m_bytes(), a_full);
+        bulk_g2s(smem + S::dvl, dvn + half_vn, half_vn, a_full);
         if (it.r == 0) {
           const int m = n / lay.rep;
           if (m >= 1) ok = mbar_wait(qk_free, (m - 1) & 1, err, 64);  // the previous item's q / k consumed
@@ -287,6 +303,7 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
           bulk_g2s(smem + S::rqk + 256, ws + lay.rk + rrow, 256, qk_full);
         }
         ok = mbar_wait(e1_done, n & 1, err, 65);  // S_c^T, dO, V^T consumed (G1 and e1): dS^T goes over them
+        ok = ok && mbar_wait(dv_read, n & 1, err, 66);  // and the dV rows staged in the dO tile are out
         if (!ok) break;
         mbar_arrive_expect_tx(ds_full, 2 * (uint32_t)lay.si_bytes());
         GD_TRACE_ONE(ws, lay, 3900 + n);
@@ -316,14 +333,17 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
       const Tile tDsh{smem_u32(smem + S::dsh), DK}, tDsl{smem_u32(smem + S::dsl), DK};
       const Tile tDmh{smem_u32(smem + S::dmh), 64}, tDml{smem_u32(smem + S::dml), 64};
       const Tile tDwt{smem_u32(smem + S::dwt), 64};
-      const Tile tDa{smem_u32(smem + S::da), 64}, tT1{smem_u32(smem + S::t1), 64};
+      const Tile tDa{smem_u32(smem + S::da), 64}, tLo2{smem_u32(smem + S::lo2), 64};
+      const Tile tAl{smem_u32(smem + S::alo), 64};
       auto issue_g1 = [&]() {
         mma_tiles(B0, 64, 64, DV, tDO, true, 0, 0, tVnh, true, 0, false);    // dO Vn^T
         mma_tiles(B1, DK, 64, DV, tSc, false, 0, 0, tDO, false, 0, false);   // S dO^T
         mma_tiles(B2, DK, 64, DV, tSc, false, 0, 0, tDvh, true, 0, false);   // S dVn^T
-        mma_tiles(B3, DV, 64, 64, tDvh, true, 0, 0, tA, true, 0, false);     // dVn^T A
+        mma_tiles(B3, DV, 64, 64, tDvh, true, 0, 0, tA, true, 0, false);     // dVn^T A (dVn and A split)
         mma_tiles(B3, DV, 64, 64, tDvl, true, 0, 0, tA, true, 0, true);
-        mma_tiles(B4, 64, 64, DV, tDvh, false, 0, 0, tVt, true, 0, false);   // dVn V^T
+        mma_tiles(B3, DV, 64, 64, tDvh, true, 0, 0, tAl, true, 0, true);
+        mma_tiles(B4, 64, 64, DV, tDvh, false, 0, 0, tVt, true, 0, false);   // dVn V^T (dVn split)
+        mma_tiles(B4, 64, 64, DV, tDvl, false, 0, 0, tVt, true, 0, true);
         mma_commit(g1_full);
       };
       bool ok = nsub > 0;
@@ -350,7 +370,8 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
             mma_tiles(B7, DK, 64, 64, tQ, true, 0, 0, tDmh, true, 0, false);     // (dM^T Q)^T = Q^T dM
             mma_tiles(B7, DK, 64, 64, tQl, true, 0, 0, tDmh, true, 0, true);
             mma_tiles(B7, DK, 64, 64, tQ, true, 0, 0, tDml, true, 0, true);
-            mma_tiles(B2, DK, 64, 64, tDwt, true, 0, 0, tA, true, 0, false);     // (A^T dW)^T = dW^T A
+            mma_tiles(B2, DK, 64, 64, tDwt, true, 0, 0, tA, true, 0, false);     // (A^T dW)^T = dW^T A (A split)
+            mma_tiles(B2, DK, 64, 64, tDwt, true, 0, 0, tAl, true, 0, true);
             mma_commit(g3a_full);
             mma_tiles(B1, 64, 64, DK, tDwt, false, 0, 0, tK, true, 0, false);    // dW K^T
             mma_tiles(B3, 64, 64, DK, tQ, false, 0, 0, tK, true, 0, false);      // Q K^T
@@ -374,7 +395,9 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
           if (g3 && !t1 && mbar_test(e2_done, par)) {
             tc_fence_after();
             GD_TRACE_ONE(ws, lay, 3000 + 8 * n + 4);
-            mma_tiles(B6, 64, 64, 64, tDa, true, 0, 0, tA, false, 0, false);     // T1 = dA A^T
+            mma_tiles(B6, 64, 64, 64, tDa, true, 0, 0, tA, false, 0, false);     // T1 = dA A^T (dA and A split)
+            mma_tiles(B6, 64, 64, 64, tLo2, true, 0, 0, tA, false, 0, true);
+            mma_tiles(B6, 64, 64, 64, tDa, true, 0, 0, tAl, false, 0, true);
             mma_commit(t1_full);
             t1 = progressed = true;
           }
@@ -392,8 +415,9 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
           if (t1 && !dl && mbar_test(e3_done, par)) {
             tc_fence_after();
             GD_TRACE_ONE(ws, lay, 3000 + 8 * n + 5);
-            mma_tiles(B7, 64, 64, 64, tA, false, 0, 0, tT1, true, 0, false);     // A^T T1 (T1 hi + lo: with
-            mma_tiles(B7, 64, 64, 64, tA, false, 0, 0, tDa, true, 0, true);      //  nearly parallel keys)
+            mma_tiles(B7, 64, 64, 64, tA, false, 0, 0, tDa, true, 0, false);     // A^T T1 (A and T1 split: with
+            mma_tiles(B7, 64, 64, 64, tA, false, 0, 0, tLo2, true, 0, true);     //  nearly parallel keys the
+            mma_tiles(B7, 64, 64, 64, tAl, false, 0, 0, tDa, true, 0, true);     //  chain dA -> T1 -> dL cancels)
             mma_commit(dl_full);
             dl = progressed = true;
           }
@@ -510,8 +534,9 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
         sGam[64 + tid] = __expf(sG[63] - sG[tid]);
         sGam[128 + tid] = sB[tid] * gt;
       }
-      // dV rows: 16-bit outputs are staged row-major ([64 tokens][DV]) in the tail buffer (free until e2 writes dA)
-      // and leave by one tensor store after the next barrier; fp32 rows are stored after the e1 hand-off (its proxy
+      // dV rows: 16-bit outputs are staged row-major ([64 tokens][DV]) in the dO tile (dead once G1 is done) and
+      // leave by one tensor store after the next barrier, so no later proxy fence waits for them; the dS refill of
+      // IN1 waits for the store to have read them (dv_read). fp32 rows are stored after the e1 hand-off (its proxy
       // fence would wait for global stores in flight)
       float dvr[16];
       float dec[8];  // exp(G_ri - G_j) for this thread's row ri, columns c8 .. c8 + 7: dM, R and dL all use it
@@ -527,7 +552,7 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
         const float s = warp_reduce_scatter16(x);
         if (lane < 16) P(P_VY, qd, tok0 + lane) = s;
         if constexpr (sizeof(T) == 2) {
-          T* sv = reinterpret_cast<T*>(smem + S::tail);
+          T* sv = reinterpret_cast<T*>(smem + S::dO);
 #pragma unroll
           for (int j = 0; j < 16; ++j) sv[(tok0 + j) * DV + dcol] = cvt_out<T>(dvr[j]);
           fence_async_smem();
@@ -553,7 +578,7 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
       ok = mbar_wait(qk_full, (n / lay.rep) & 1, err, 82);
       if (!(ok = epi_all(ok))) break;
       if (sizeof(T) == 2 && tid == 0) {  // every warp's dV rows are staged
-        tma_store_4d(&tm_dv, 0, it.h, t0, it.b, smem + S::tail);
+        tma_store_4d(&tm_dv, 0, it.h, t0, it.b, smem + S::dO);
         bulk_commit();
       }
       GD_TRACE_AT(ws, lay, 32 * n + 2);
@@ -577,10 +602,13 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
         const float s = warp_reduce_scatter16(av);
         if (lane < 16) P(P_A, qd, tok0 + lane) = s;
       }
+      if (tid == 0) {  // the dV store has read the staging rows (no-op for fp32): IN1 may take dS
+        bulk_wait_read0();
+        mbar_arrive(dv_read);
+      }
       GD_TRACE_AT(ws, lay, 32 * n + 3);
       // ---- e2: dQ / dK terms, dA (and R's first term)
       ok = mbar_wait(g3a_full, par, err, 83);
-      if (sizeof(T) == 2 && tid == 0) bulk_wait_read0();  // the dV store has read the tail buffer before dA goes in
       if (!(ok = epi_all(ok))) break;
       tc_fence_after();
       GD_TRACE_AT(ws, lay, 32 * n + 4);
@@ -616,7 +644,7 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
           const int jj = c8 + j;
           a10[j] = keep_if(sB[jj] * fmaf(sGam[jj], a10[j], a5[j]), jj < ri);
         }
-        store8_bf16(smem + S::da, ri, c8, 64, a10);
+        store8_split(smem + S::da, smem + S::lo2, ri, c8, 64, a10);  // dW^T's last reader (G3) is done
       }
       GD_TRACE_AT(ws, lay, 32 * n + 7);
       tc_fence_before();
@@ -649,11 +677,11 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
       if (!(ok = epi_all(ok))) break;
       tc_fence_after();
       GD_TRACE_AT(ws, lay, 32 * n + 13);
-      {  // T1 hi, and its lo in the dA tile (dA's last reader, the T1 product, is complete; P_beta overwrites the lo
-         // half only after dl_full, when the dL product has read it)
+      {  // T1 hi and lo over dA hi and lo (their last reader, the T1 product, is complete; P_beta overwrites T1 hi
+         // only after dl_full, when the dL product has read it)
         float x[8];
         tmem_ld8h(tmem_lane_addr(B6, warp, tok0), x);
-        store8_split(smem + S::t1, smem + S::da, ri, c8, 64, x);
+        store8_split(smem + S::da, smem + S::lo2, ri, c8, 64, x);
       }
       tc_fence_before();
       fence_async_smem();

@@ -8,8 +8,9 @@
 //   L = diag(beta) (K K^T) * exp(G_i - G_j) (i > j),  M = (Q K^T) * exp(G_i - G_j) (i >= j),  A = (I + L)^-1
 //   W = A diag(beta gamma) K,  U = A diag(beta) V
 //   Vn = U - W S,  O = diag(gamma) Q S + M Vn,  S <- exp(G_last) S + K^T diag(e) Vn
-// Precision: bf16 operands with fp32 accumulation; A diag(beta) (in U), Vn (in M Vn) and e * Vn (in the state update)
-// are split into bf16 hi + lo pairs (two MMAs into one accumulator), the state is carried in fp32.
+// Precision: bf16 operands with fp32 accumulation; q and k (in Q K^T, K K^T), A diag(beta gamma) (in W), A diag(beta)
+// (in U), K~ and Vn (in the state update), M and Vn (in M Vn) are split into bf16 hi + lo pairs (two or three MMAs into
+// one accumulator); the backward's A and W^T images carry their low halves too; the state is carried in fp32.
 #include <type_traits>
 
 #include "gd_common.cuh"
@@ -126,7 +127,8 @@ __device__ __forceinline__ void unit_lower_inverse(const float* L, float* A, flo
   GD_TRACE_AT(ws, lay, 20);
 }
 
-template <typename T, int DK, int DV>
+// BWD: the backward layout (its extra images); the forward instance carries none of that code
+template <typename T, int DK, int DV, bool BWD>
 __global__ void __launch_bounds__(256, 2) prep_kernel(const T* __restrict__ q, const T* __restrict__ k,
                                                    const T* __restrict__ v, const float* __restrict__ g,
                                                    const float* __restrict__ beta, Layout lay, int flags,
@@ -184,7 +186,7 @@ __global__ void __launch_bounds__(256, 2) prep_kernel(const T* __restrict__ q, c
 
   // l2 prologue and operand tiles: every row load in flight before any is converted
   const bool norm = (flags & GD_L2NORM) != 0;
-  const bool bwd = lay.backward() && (h % lay.rep == 0);
+  const bool bwd = BWD && (h % lay.rep == 0);
   const size_t rrow = (((size_t)b * lay.HK + hk) * lay.NT + c) * 64;  // this chunk's 64 rsqrt slots
   float* rq = bwd ? reinterpret_cast<float*>(ws + lay.rq) + rrow : nullptr;
   float* rk = bwd ? reinterpret_cast<float*>(ws + lay.rk) + rrow : nullptr;
@@ -250,12 +252,12 @@ __global__ void __launch_bounds__(256, 2) prep_kernel(const T* __restrict__ q, c
     mma_commit(bar);
   }
   GD_TRACE_AT(ws, lay, 2);
-  if (lay.backward()) {  // the low halves go out (transposed images) before L and A overwrite them
+  if constexpr (BWD) {  // the low halves go out (transposed images) before L and A overwrite them
     unsigned char* dst = ws + lay.qkl + cidx * lay.qk_bytes();
     store_tile_transposed<64, DK, 8>(smem + S::ql, dst);
     store_tile_transposed<64, DK, 8>(smem + S::kl, dst + 64 * DK * 2);
   }
-  if (lay.backward()) {  // diag(gamma) Q from q's hi + lo, split again: the reverse pass's operand
+  if constexpr (BWD) {  // diag(gamma) Q from q's hi + lo, split again: the reverse pass's operand
     unsigned char* gqh = ws + lay.gq + cidx * lay.qk_bytes();
     unsigned char* gql = gqh + 64 * DK * 2;
     for (int idx = tid; idx < 64 * DK / 8; idx += 256) {
@@ -393,13 +395,13 @@ __global__ void __launch_bounds__(256, 2) prep_kernel(const T* __restrict__ q, c
   if (ok) {
     unsigned char* dst = ws + lay.qk + cidx * lay.qk_bytes();  // transposed images ([DK x 64], rows d)
     store_tile_transposed<64, DK, 8>(smem + S::q, dst);
-    if (lay.backward()) {
+    if constexpr (BWD) {
       store_tile_transposed<64, DK, 8>(smem + S::k, dst + 64 * DK * 2);
       store_tile_transposed<64, DV, 8>(smem + S::v, ws + lay.vi + cidx * lay.vi_bytes());
-      unsigned char* aimg = ws + lay.ai + cidx * lay.m_bytes();
+      unsigned char* aimg = ws + lay.ai + cidx * lay.mm_bytes();  // A hi, then lo
       const int i = tid >> 2, j0 = 16 * (tid & 3);
 #pragma unroll
-      for (int q8 = 0; q8 < 2; ++q8) store8_bf16(aimg, i, j0 + 8 * q8, 64, sAi + i * 68 + j0 + 8 * q8);
+      for (int q8 = 0; q8 < 2; ++q8) store8_split(aimg, aimg + lay.m_bytes(), i, j0 + 8 * q8, 64, sAi + i * 68 + j0 + 8 * q8);
     }
     if (tid < 64) reinterpret_cast<float*>(ws + lay.gc + cidx * lay.gc_bytes())[tid] = sG[tid];
   }
@@ -410,13 +412,19 @@ __global__ void __launch_bounds__(256, 2) prep_kernel(const T* __restrict__ q, c
   if (ok) {
     float acc[32];
     const int row = tid & 127;
-    if (warp < 4) {  // W^T row dk = row -> blocked [DK x 64] image, 16-byte stores
+    if (warp < 4) {  // W^T row dk = row -> blocked [DK x 64] image (and its low half for the backward), 16-byte stores
       unsigned char* wimg = ws + lay.wt + cidx * lay.wt_bytes();
+      unsigned char* wlimg = ws + lay.wtl + cidx * lay.wt_bytes();
 #pragma unroll 1
       for (int half = 0; half < 2; ++half) {
         tmem_ld32(tmem_lane_addr(tm, warp, 64 + 32 * half), acc);
+        if constexpr (BWD) {
 #pragma unroll
-        for (int q8 = 0; q8 < 4; ++q8) store8_bf16(wimg, row, 32 * half + 8 * q8, 64, acc + 8 * q8);
+          for (int q8 = 0; q8 < 4; ++q8) store8_split(wimg, wlimg, row, 32 * half + 8 * q8, 64, acc + 8 * q8);
+        } else {
+#pragma unroll
+          for (int q8 = 0; q8 < 4; ++q8) store8_bf16(wimg, row, 32 * half + 8 * q8, 64, acc + 8 * q8);
+        }
       }
     } else {  // U^T row v = row -> U [64][DV] fp32
       float* u = reinterpret_cast<float*>(ws + lay.u + cidx * lay.u_bytes());
@@ -807,9 +815,9 @@ template <typename T, int DK, int DV>
 cudaError_t launch_prep(const void* q, const void* k, const void* v, const float* g, const float* beta,
                         const Layout& lay, int flags, unsigned char* ws, cudaStream_t st) {
   using S = PrepSmem<DK, DV>;
-  auto kern = prep_kernel<T, DK, DV>;
-  static bool attr_done[kMaxDevices] = {};  // once per device: no attribute call inside a graph capture
-  cudaError_t e = set_smem_once(kern, S::total, attr_done);
+  auto kern = lay.backward() ? prep_kernel<T, DK, DV, true> : prep_kernel<T, DK, DV, false>;
+  static bool attr_done[2][kMaxDevices] = {};  // once per device and instance: no attribute call inside a capture
+  cudaError_t e = set_smem_once(kern, S::total, attr_done[lay.backward() ? 1 : 0]);
   if (e != cudaSuccess) return e;
   CUtensorMap mq{}, mk{}, mv{};  // 16-bit inputs only (fp32 rows are read by plain loads)
   if (sizeof(T) == 2) {

@@ -8,8 +8,7 @@ bar (max error <= 2x transformers' own error against float64 on the same inputs,
 - a long sequence (T = 2048, one head);
 - the committed float64 stress fixtures (tests/golden/recurrence_stress.npz: beta = 1 - 1e-6, g = 0, correlated
   keys; recurrence_strong_decay.npz: g = -20): their recipes at head width 128, and their own inputs zero-padded
-  from their head widths to 128 (the l2 prologue leaves a zero-padded row's direction unchanged); the padded stress
-  fixture is the one case whose dg / dbeta / ds0 exceed the bar, pinned as the known limit.
+  from their head widths to 128 (the l2 prologue leaves a zero-padded row's direction unchanged).
 
 Inputs are built as the reference's make() builds them (q, k, v ~ N(0, 1), g = -U(0, 1), beta = U(0, 1),
 s0 ~ N(0, 0.1)) and rounded to bf16 for q, k, v, dO; the rule normalises q and k itself (use_qk_l2norm_in_kernel).
@@ -126,15 +125,11 @@ def test_golden_strong_decay_inputs():
     assert not parity.failures(rep), ratios(rep)
 
 
-def test_golden_stress_inputs_known_limit():
+def test_golden_stress_inputs():
     """recurrence_stress.npz (beta = 1 - 1e-6, g = 0, keys with k_i . k_j ~ 0.99, T = 40, D = 32) zero-padded to 128:
-    the hardest case here. o, S_T, dquery, dkey and dvalue meet the 2x bar; dg, dbeta and ds0 do not: the per-chunk
-    gradient's chain dA -> T1 = dA A^T -> dL = -A^T T1 and the reverse pass's W^T dVn run with bf16 operands
-    (T1 and M carried as hi + lo, dA, A, W and dVn's low half not), and with nearly parallel keys at beta ~ 1 these
-    products cancel to a small fraction of their terms, while transformers (fp32 on bf16-rounded inputs that are
-    exact here) is unusually exact. The measured ratios are pinned here as the known limit (a CPU emulation of the
-    kernels' rounding puts the remedy at eight more hi + lo operand sites)."""
+    the hardest case here. The per-chunk gradient's chain dA -> T1 = dA A^T -> dL = -A^T T1, A^T dVn and dVn V^T, and
+    the reverse pass's W^T dVn cancel to a small fraction of their terms with nearly parallel keys at beta ~ 1 while
+    transformers (fp32 on bf16-rounded inputs that are exact here) is unusually exact: every one of those operands is
+    carried as bf16 hi + lo for this case to meet the bar."""
     rep = report(golden_inputs("recurrence_stress.npz"))
-    bad = parity.failures(rep)
-    assert set(bad) <= {"dg", "dbeta", "ds0"}, ratios(rep)
-    assert all(rep[n]["ratio"] < 20 for n in ("dg", "dbeta", "ds0")), ratios(rep)
+    assert not parity.failures(rep), ratios(rep)
