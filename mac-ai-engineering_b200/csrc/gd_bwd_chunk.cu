@@ -71,7 +71,8 @@ struct ChunkSmem {
   static constexpr size_t rqk = scr + 2 * 4 * 64 * 4;       // fp32 [2][64] the item's l2 rsqrt of q, k rows
   static constexpr size_t sl = rqk + 2 * 64 * 4;            // fp32 [2][32] <S_c, dS_{c+1}> partials (by parity)
   static constexpr size_t tok = sl + 2 * 32 * 4;            // fp32 [3][64] the sub-item's gamma_t, e_t, beta_t gamma_t
-  static constexpr size_t bar = tok + 3 * 64 * 4;
+  static constexpr size_t xch = tok + 3 * 64 * 4;           // fp32 [4] the dg scans' cross-warp totals
+  static constexpr size_t bar = xch + 16;
   static constexpr int NBAR = 23;
   static constexpr size_t tmem = bar + NBAR * 8;
   static constexpr size_t total = tmem + 16;
@@ -756,10 +757,8 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
           rc += P(P_RECT, w, t);
           pk += P(P_PK, w, t);
         }
-        float sl = 0.f;
-        const float* slp = reinterpret_cast<const float*>(smem + S::sl + (n & 1) * 128);
-#pragma unroll
-        for (int w = 0; w < 32; ++w) sl += slp[w];
+        // <S_c, dS_{c+1}> from its 32 partial sums: one per lane, a butterfly (the same order in both warps)
+        const float sl = warp_sum(reinterpret_cast<const float*>(smem + S::sl + (n & 1) * 128)[lane]);
         const float gt = sGam[t];
         const float w_ = sB[t] * gt * kx;
         const float db = fmaf(gt, kx, vy) + pk;
@@ -772,7 +771,8 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
           const float z = __shfl_up_sync(0xffffffffu, pre, o);
           if (lane >= o) pre += z;
         }
-        float* xch = scr + 4 * 64;  // [2] cross-warp totals
+        float* xch = reinterpret_cast<float*>(smem + S::xch);  // [2] cross-warp totals (not in scr: the other
+                                                                 // warps' l2 dot products may be writing it now)
         if (lane == 0 && warp == 1) xch[0] = suf;
         if (lane == 31 && warp == 0) xch[1] = pre;
         float pre_excl = __shfl_up_sync(0xffffffffu, pre, 1);
@@ -797,21 +797,20 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
         float* dotq = scr;  // [64 tokens][4 head-dimension quarters]: one 16-byte read per token below
         float* dotk = scr + 4 * 64;
         const float inv_qscale = 1.f / qscale;
-        float x[16];
-        epi_sync();  // the dg / dbeta threads are done with scr
         GD_TRACE_AT(ws, lay, 32 * n + 24);
-        if (norm) {
+        // no barrier after the dg / dbeta threads: they read part, sl and xch, none of which is written here
+        float x[16];
+        if (norm) {  // x_hat . dy per token for q and k at once: lanes 0-15 get q's tokens, lanes 16-31 k's
+          float v[32];
           row16<true>(qh, ql, dcol, tok0, x);
 #pragma unroll
-          for (int j = 0; j < 16; ++j) x[j] *= inv_qscale * dQ[j];
-          float s = warp_reduce_scatter16(x);
-          if (lane < 16) dotq[(tok0 + lane) * 4 + qd] = s;
-          GD_TRACE_AT(ws, lay, 32 * n + 25);
+          for (int j = 0; j < 16; ++j) v[j] = x[j] * (inv_qscale * dQ[j]);
           row16<true>(kh, kl, dcol, tok0, x);
 #pragma unroll
-          for (int j = 0; j < 16; ++j) x[j] *= dK[j];
-          s = warp_reduce_scatter16(x);
-          if (lane < 16) dotk[(tok0 + lane) * 4 + qd] = s;
+          for (int j = 0; j < 16; ++j) v[16 + j] = x[j] * dK[j];
+          const float s = warp_reduce_scatter32(v);
+          ((lane < 16) ? dotq : dotk)[(tok0 + (lane & 15)) * 4 + qd] = s;
+          GD_TRACE_AT(ws, lay, 32 * n + 25);
         }
         epi_sync();
         GD_TRACE_AT(ws, lay, 32 * n + 21);
