@@ -541,17 +541,17 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
       // fence would wait for global stores in flight)
       float dvr[16];
       float dec[8];  // exp(G_ri - G_j) for this thread's row ri, columns c8 .. c8 + 7: dM, R and dL all use it
+      // two row-dot partials share one 32-value reduce-scatter (31 shuffles for both): v . Y with q . (dO S^T) in
+      // e1, k . X with k . (Vn dS^T) across e2 / eg2; the first of each pair waits in registers
+      float vy[16], kx[16];
       {
-        float x[16];
         tmem_ld16(tmem_lane_addr(B3, warp, tok0), dvr);  // Y^T: v . Y, and dV = diag(beta) Y
-        row16<false>(smem + S::vt, nullptr, dcol, tok0, x);
+        row16<false>(smem + S::vt, nullptr, dcol, tok0, vy);
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
-          x[j] *= dvr[j];
+          vy[j] *= dvr[j];
           dvr[j] *= sB[tok0 + j];
         }
-        const float s = warp_reduce_scatter16(x);
-        if (lane < 16) P(P_VY, qd, tok0 + lane) = s;
         if constexpr (sizeof(T) == 2) {
           T* sv = reinterpret_cast<T*>(smem + S::dO);
 #pragma unroll
@@ -598,10 +598,14 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
           store_token_rows<T>(dvr, dv + ((size_t)it.b * lay.T * lay.H + it.h) * DV, (size_t)lay.H * DV, t0 + tok0,
                               lay.T, 32 * qd + 8 * (lane >> 3));
         row16<true>(qh, ql, dcol, tok0, x);
+        float v[32];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) av[j] *= x[j];
-        const float s = warp_reduce_scatter16(av);
-        if (lane < 16) P(P_A, qd, tok0 + lane) = s;
+        for (int j = 0; j < 16; ++j) {
+          v[j] = vy[j];
+          v[16 + j] = av[j] * x[j];
+        }
+        const float s = warp_reduce_scatter32(v);
+        P(lane < 16 ? P_VY : P_A, qd, tok0 + (lane & 15)) = s;
       }
       if (tid == 0) {  // the dV store has read the staging rows (no-op for fp32): IN1 may take dS
         bulk_wait_read0();
@@ -623,15 +627,13 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
           dK[j] += y[j];
         }
         tmem_ld16(tmem_lane_addr(B2, warp, tok0), x);  // X^T
-        row16<true>(kh, kl, dcol, tok0, y);
+        row16<true>(kh, kl, dcol, tok0, kx);
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           const int i = tok0 + j;
           dK[j] = fmaf(sGam[128 + i], x[j], dK[j]);  // beta_i gamma_i
-          y[j] *= x[j];
+          kx[j] *= x[j];
         }
-        const float s = warp_reduce_scatter16(y);
-        if (lane < 16) P(P_KX, qd, tok0 + lane) = s;
         GD_TRACE_AT(ws, lay, 32 * n + 6);
       }
       ok = mbar_wait(g3_full, par, err, 89);
@@ -659,17 +661,18 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
       tc_fence_after();
       GD_TRACE_AT(ws, lay, 32 * n + 10);
       {
-        float x[16], y[16];
+        float x[16], y[16], v[32];
         tmem_ld16(tmem_lane_addr(B5, warp, tok0), x);
         row16<true>(kh, kl, dcol, tok0, y);
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           x[j] *= sGam[64 + tok0 + j];  // e_t
           dK[j] += x[j];
-          y[j] *= x[j];
+          v[j] = kx[j];
+          v[16 + j] = y[j] * x[j];
         }
-        const float s = warp_reduce_scatter16(y);
-        if (lane < 16) P(P_E, qd, tok0 + lane) = s;
+        const float s = warp_reduce_scatter32(v);
+        P(lane < 16 ? P_KX : P_E, qd, tok0 + (lane & 15)) = s;
       }
       GD_TRACE_AT(ws, lay, 32 * n + 11);
       // ---- e3: T1 tile
