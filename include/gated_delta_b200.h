@@ -49,6 +49,12 @@ extern "C" {
 #define GD_STORE_STATES 2  /* the state pass keeps each chunk's entering state S_c and Vn for the backward */
 #define GD_SCALE_Q 4       /* q is multiplied by DK^-1/2 (after the l2 norm): the drop-in's query scaling */
 #define GD_STATES_STORED 8 /* gd_backward: the workspace already holds the states (gd_forward with GD_STORE_STATES) */
+/* gd_fwd_state: the value split of the sequential pass. Without this flag the forward pass with O (no
+ * GD_STORE_STATES) runs four CTAs per (value head, batch row or sequence), 32 value columns each, when all of them fit
+ * on the GPU at once (4 x heads x rows <= SMs), else two CTAs of 64 columns (the reference's VALUE_SPLIT chosen from
+ * the head-rows and the SM count, src/macai/gated_delta/op.py:75-87); with it, always two. The high-level entry points
+ * (gd_forward, ...) use the automatic choice. */
+#define GD_WIDE_STATE_PASS 16
 /* Test only (never set in production): gd_fwd_state's MMA-issuing thread first waits on a barrier that nothing
  * signals, with a ~1 ms budget. The wait expires, the kernel records GD_ERR_TIMEOUT at stage 28 in the error word,
  * every role of the CTA gives up in its own bounded wait (~2 s) with no product or copy left in flight, and the CTA
@@ -99,7 +105,10 @@ int gd_bwd_chunk(const void* q, const void* k, const void* v, const float* beta,
 /* The forward of the autograd function: gd_prep then gd_fwd_state. flags & GD_STORE_STATES: the training forward of
  * the stored-states mode (the reference's op.RECOMPUTE_STATES = False, op.py:27-33, :142, :151-155, :165-167): the
  * workspace must hold gd_workspace_bytes(..., 1), and afterwards holds every chunk matrix, state and Vn the backward
- * reads; keep it unchanged for gd_backward(GD_STATES_STORED). Outputs are the same bits in both modes.
+ * reads; keep it unchanged for gd_backward(GD_STATES_STORED). Outputs are the same bits in both modes when the plain
+ * training forward passes GD_WIDE_STATE_PASS (as the drop-in does when autograd records the call): the stored-states
+ * forward always runs the two-CTA state pass. Without GD_WIDE_STATE_PASS and GD_STORE_STATES the state pass picks its
+ * value split from the head-rows and the SM count (GD_WIDE_STATE_PASS above).
  * Replaces: GatedDeltaRule.forward (src/macai/gated_delta/op.py:119-185) as called by the drop-in (op.py:296). */
 int gd_forward(const void* q, const void* k, const void* v, const float* g, const float* beta, const float* s0,
                void* o, float* sT, int dtype, int B, int T, int H, int HK, int DK, int DV, int flags, void* workspace,

@@ -216,8 +216,8 @@ int gd_forward(const void* q, const void* k, const void* v, const float* g, cons
   const int f = flags & (GD_L2NORM | GD_SCALE_Q);
   s = gd_prep(q, k, v, g, beta, dtype, B, T, H, HK, DK, DV, f, workspace, bytes, stream);
   if (s) return s;
-  return gd_fwd_state(s0, o, sT, dtype, B, T, H, HK, DK, DV, f | (keep ? GD_STORE_STATES : 0), workspace, bytes,
-                      stream);
+  return gd_fwd_state(s0, o, sT, dtype, B, T, H, HK, DK, DV,
+                      f | (keep ? GD_STORE_STATES : 0) | (flags & GD_WIDE_STATE_PASS), workspace, bytes, stream);
 }
 
 int gd_backward(const void* q, const void* k, const void* v, const float* g, const float* beta, const float* s0,
@@ -269,7 +269,8 @@ int gd_forward_packed(const void* q, const void* k, const void* v, const float* 
   if ((s = launched(gd::launch_chunk_table(cu_seqlens, L, ws, st)))) return s;
   const int f = flags & (GD_L2NORM | GD_SCALE_Q);
   if ((s = prep(q, k, v, g, beta, dtype, L, f, workspace, st))) return s;
-  if ((s = fwd_state(s0, ws + L.opad, sT, dtype, L, f | (keep ? GD_STORE_STATES : 0), workspace, st))) return s;
+  const int fs = f | (keep ? GD_STORE_STATES : 0) | (flags & GD_WIDE_STATE_PASS);
+  if ((s = fwd_state(s0, ws + L.opad, sT, dtype, L, fs, workspace, st))) return s;
   return launched(gd::launch_scatter(ws + L.opad, o, H * DV * elem_bytes(dtype), L, ws, st));
 }
 

@@ -403,6 +403,19 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// 8 consecutive 32-bit columns of the thread's own lane (shape 32x32b: M = 128 accumulators, row = lane).
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
+  uint32_t r[8];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 // Two such loads in flight under one wait.
 __device__ __forceinline__ void tmem_ld16x2(uint32_t a0, float (&v0)[16], uint32_t a1, float (&v1)[16]) {
   uint32_t r[32];
@@ -438,6 +451,36 @@ __device__ __forceinline__ void tmem_ld8h(uint32_t taddr, float (&v)[8]) {
       : "memory");
 #pragma unroll
   for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// The same with 4 columns a half-warp: thread t < 16 gets row (quadrant base + t), columns [col, col + 4); thread
+// t >= 16 the same row t - 16, columns [col + 4, col + 8). Two loads under one wait.
+__device__ __forceinline__ void tmem_ld4hx2(uint32_t a0, float (&v0)[4], uint32_t a1, float (&v1)[4]) {
+  uint32_t r[8];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.16x32bx2.x4.b32 {%0,%1,%2,%3}, [%8], 4;\n\t"
+      "tcgen05.ld.sync.aligned.16x32bx2.x4.b32 {%4,%5,%6,%7}, [%9], 4;\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+      : "r"(a0), "r"(a1)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    v0[i] = __uint_as_float(r[i]);
+    v1[i] = __uint_as_float(r[4 + i]);
+  }
+}
+
+__device__ __forceinline__ void tmem_ld4h(uint32_t taddr, float (&v)[4]) {
+  uint32_t r[4];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.16x32bx2.x4.b32 {%0,%1,%2,%3}, [%4], 4;\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 4; ++i) v[i] = __uint_as_float(r[i]);
 }
 
 // Two such loads under one wait.
@@ -549,6 +592,19 @@ __device__ __forceinline__ void store8_bf16(unsigned char* tile, int r, int c0, 
   u.z = pack_bf16(v[4], v[5]);
   u.w = pack_bf16(v[6], v[7]);
   *reinterpret_cast<uint4*>(tile + blk_off(r, c0, cols)) = u;
+}
+
+// Four bf16 (8 bytes) at (r, c0 .. c0 + 3) of a blocked tile, c0 % 4 == 0; and the same with a hi / lo split
+__device__ __forceinline__ void store4_bf16(unsigned char* tile, int r, int c0, int cols, const float* v) {
+  *reinterpret_cast<uint2*>(tile + blk_off(r, c0, cols)) = make_uint2(pack_bf16(v[0], v[1]), pack_bf16(v[2], v[3]));
+}
+__device__ __forceinline__ void store4_split(unsigned char* hi_tile, unsigned char* lo_tile, int r, int c0, int cols,
+                                             const float* v) {
+  float h[4], l[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) split_bf16(v[i], h[i], l[i]);
+  store4_bf16(hi_tile, r, c0, cols, h);
+  store4_bf16(lo_tile, r, c0, cols, l);
 }
 
 // the same with a hi / lo split into two tiles

@@ -833,8 +833,25 @@ cudaError_t launch_prep(const void* q, const void* k, const void* v, const float
 }
 
 template <typename T, int DK, int DV>
+cudaError_t launch_state_narrow(const float* s0, void* o, float* sT, const Layout& lay, int flags, unsigned char* ws,
+                                cudaStream_t st);
+
+template <typename T, int DK, int DV>
 cudaError_t launch_state(const float* s0, void* o, float* sT, const Layout& lay, int flags, unsigned char* ws,
                          cudaStream_t st) {
+  // the value split: four CTAs per (head, row) for the forward with O when they all fit at once (gd_state_narrow.cu),
+  // else two
+  if (o != nullptr && !(flags & (GD_STORE_STATES | GD_WIDE_STATE_PASS))) {
+    static int sms[kMaxDevices] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    if (sms[dev] == 0 && (e = cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
+      return e;
+    const long long pairs = (long long)lay.H * (lay.packed() ? lay.N : lay.B);
+    if (4 * pairs <= sms[dev]) return launch_state_narrow<T, DK, DV>(s0, o, sT, lay, flags, ws, st);
+  }
   using S = StateSmem<DK, DV>;
   auto kern = state_kernel<T, DK, DV>;
   static bool attr_done[kMaxDevices] = {};  // once per device: no attribute call inside a graph capture

@@ -102,7 +102,7 @@ def workspace_bytes(B, T, H, HK, DK, DV, backward: bool) -> int:
 def gated_delta_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Tensor, beta: torch.Tensor,
                     s0: Optional[torch.Tensor], flags: int) -> tuple[torch.Tensor, torch.Tensor]:
     """o [B, T, H, DV] (q's dtype) and S_T [B, H, DK, DV] fp32. q, k [B, T, HK, DK]; v [B, T, H, DV] in q's dtype;
-    g, beta fp32 [B, T, H]; s0 fp32 or None. flags: GD_L2NORM | GD_SCALE_Q."""
+    g, beta fp32 [B, T, H]; s0 fp32 or None. flags: GD_L2NORM | GD_SCALE_Q (| GD_WIDE_STATE_PASS)."""
     B, T, H, HK, DK, DV = _dims(q, v)
     lib = _lib.load()
     dev = q.device
@@ -445,22 +445,32 @@ def check_cu_seqlens(cu_seqlens, T: int, device) -> torch.Tensor:
     return c.to(torch.int32).contiguous()
 
 
+def _training(*xs) -> bool:
+    """Autograd will record this call (some input needs a gradient)."""
+    return torch.is_grad_enabled() and any(t is not None and t.requires_grad for t in xs)
+
+
 def _forward(q, k, v, g, beta, s0, flags):
     """The forward op for this call: the stored-states one when RECOMPUTE_STATES is False and autograd will record
-    the call (the reference keeps states only for a backward, op.py:108, :141-142), else the plain one."""
-    if not RECOMPUTE_STATES and torch.is_grad_enabled() and any(
-            t is not None and t.requires_grad for t in (q, k, v, g, beta, s0)):
-        o, sT, _ = gated_delta_fwd_stored(q, k, v, g, beta, s0, flags)
-        return o, sT
+    the call (the reference keeps states only for a backward, op.py:108, :141-142), else the plain one. A training
+    forward keeps the two-CTA state pass (GD_WIDE_STATE_PASS), the one the stored-states forward and the backward's
+    recompute run, so that o has the same bits in both modes and however many heads share the call; a forward for
+    inference may take the four-CTA pass when its (head, row) pairs leave SMs idle."""
+    if _training(q, k, v, g, beta, s0):
+        if not RECOMPUTE_STATES:
+            o, sT, _ = gated_delta_fwd_stored(q, k, v, g, beta, s0, flags)
+            return o, sT
+        return gated_delta_fwd(q, k, v, g, beta, s0, flags | _lib.GD_WIDE_STATE_PASS)
     return gated_delta_fwd(q, k, v, g, beta, s0, flags)
 
 
 def _forward_packed(q, k, v, g, beta, s0, cu, flags):
     """_forward over packed rows."""
-    if not RECOMPUTE_STATES and torch.is_grad_enabled() and any(
-            t is not None and t.requires_grad for t in (q, k, v, g, beta, s0)):
-        o, sT, _ = gated_delta_fwd_packed_stored(q, k, v, g, beta, s0, cu, flags)
-        return o, sT
+    if _training(q, k, v, g, beta, s0):
+        if not RECOMPUTE_STATES:
+            o, sT, _ = gated_delta_fwd_packed_stored(q, k, v, g, beta, s0, cu, flags)
+            return o, sT
+        return gated_delta_fwd_packed(q, k, v, g, beta, s0, cu, flags | _lib.GD_WIDE_STATE_PASS)
     return gated_delta_fwd_packed(q, k, v, g, beta, s0, cu, flags)
 
 

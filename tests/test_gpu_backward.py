@@ -71,7 +71,8 @@ def test_backward_is_deterministic():
 
 def test_backward_many_heads():
     """B * H = 80 value heads (160 state-pass CTAs on 148 SMs: a second wave): forward and backward against float64
-    with the bar, and bitwise equal to the same heads run two at a time (one wave)."""
+    with the bar, and bitwise equal to half of the heads run alone (80 CTAs, one wave; both head counts take the
+    two-CTA state pass, so the same arithmetic runs on every head)."""
     q, k, v, g, beta, st = inputs(1, 130, 80, seed=17)
     gen = torch.Generator().manual_seed(18)
     do = torch.randn(1, 130, 80, 128, generator=gen).to(torch.bfloat16)
@@ -81,10 +82,10 @@ def test_backward_many_heads():
     theirs = transformers_ref.run(q, k, v, g, beta, st, do=do, dsT=dsT)
     rep = parity.check(got, theirs, truth, names=NAMES)
     assert not parity.failures(rep), {k_: round(v_["ratio"], 3) for k_, v_ in rep.items()}
-    sl = slice(40, 42)   # two of the heads alone
+    sl = slice(40, 80)   # half of the heads alone
     few = run_grads(q[:, :, sl], k[:, :, sl], v[:, :, sl], g[:, :, sl], beta[:, :, sl], st[:, sl], do[:, :, sl],
                     dsT[:, sl])
-    part = lambda x, dim: x.narrow(dim, 40, 2)
+    part = lambda x, dim: x.narrow(dim, 40, 40)
     dims = (2, 1, 2, 2, 2, 2, 2, 1)   # head dimension of o, S_T, dq, dk, dv, dg, dbeta, ds0
     for a, b, d in zip(got, few, dims):
         assert parity.identical(part(a, d), b)

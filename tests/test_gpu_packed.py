@@ -136,5 +136,14 @@ def test_packed_forward_only_and_int64_boundaries():
     with torch.no_grad():
         o, sT = chunk_gated_delta_rule(q.cuda(), k.cuda(), v.cuda(), g.cuda(), beta.cuda(), initial_state=s0.cuda(),
                                        output_final_state=True, use_qk_l2norm_in_kernel=True, cu_seqlens=cu)
-    want = separate(q, k, v, g, beta, s0, torch.zeros(1, T, H, 128), torch.zeros_like(s0), lengths)
+    # the separate calls forward-only as well (a forward for inference may take the four-CTA state pass, a training
+    # forward keeps the two-CTA one)
+    outs = []
+    with torch.no_grad():
+        for n, (a, b) in enumerate(zip(cu_of(lengths)[:-1], cu_of(lengths)[1:])):
+            sl = slice(a, b)
+            outs.append(chunk_gated_delta_rule(q[:, sl].cuda(), k[:, sl].cuda(), v[:, sl].cuda(), g[:, sl].cuda(),
+                                               beta[:, sl].cuda(), initial_state=s0[n:n + 1].cuda(),
+                                               output_final_state=True, use_qk_l2norm_in_kernel=True))
+    want = (torch.cat([x[0].cpu() for x in outs], dim=1), torch.cat([x[1].cpu() for x in outs], dim=0))
     assert parity.identical(o.cpu(), want[0]) and parity.identical(sT.cpu(), want[1])
