@@ -55,6 +55,12 @@ extern "C" {
  * the head-rows and the SM count, src/macai/gated_delta/op.py:75-87); with it, always two. The high-level entry points
  * (gd_forward, ...) use the automatic choice. */
 #define GD_WIDE_STATE_PASS 16
+/* Bits 16-23 (with GD_SCALE_Q): the caller's key head width when its q and k rows are zero-padded to the built width
+ * 128 (a width of 32, 64 or 96 runs exactly in the 128-wide kernels: zero key dimensions change neither the l2 norms
+ * nor the states, zero value columns stay zero); the query scale is then that width^-1/2. 0: the built width. The
+ * high-level entry points pass these bits on. */
+#define GD_KEY_WIDTH(dk) (((dk) & 0xff) << 16)
+#define GD_KEY_WIDTH_MASK 0x00ff0000
 /* Test only (never set in production): gd_fwd_state's MMA-issuing thread first waits on a barrier that nothing
  * signals, with a ~1 ms budget. The wait expires, the kernel records GD_ERR_TIMEOUT at stage 28 in the error word,
  * every role of the CTA gives up in its own bounded wait (~2 s) with no product or copy left in flight, and the CTA

@@ -213,7 +213,7 @@ int gd_forward(const void* q, const void* k, const void* v, const float* g, cons
   if (workspace_bytes < bytes) return GD_ERR_WORKSPACE;
   if (!o) return GD_ERR_ARG;
   if (!aligned16(o)) return GD_ERR_ALIGN;
-  const int f = flags & (GD_L2NORM | GD_SCALE_Q);
+  const int f = flags & (GD_L2NORM | GD_SCALE_Q | GD_KEY_WIDTH_MASK);
   s = gd_prep(q, k, v, g, beta, dtype, B, T, H, HK, DK, DV, f, workspace, bytes, stream);
   if (s) return s;
   return gd_fwd_state(s0, o, sT, dtype, B, T, H, HK, DK, DV,
@@ -229,7 +229,7 @@ int gd_backward(const void* q, const void* k, const void* v, const float* g, con
   if (!workspace) return GD_ERR_ARG;
   if (!aligned16(workspace)) return GD_ERR_ALIGN;
   if (workspace_bytes < Layout::make(B, T, H, HK, DK, DV, true).total) return GD_ERR_WORKSPACE;
-  const int f = flags & (GD_L2NORM | GD_SCALE_Q);
+  const int f = flags & (GD_L2NORM | GD_SCALE_Q | GD_KEY_WIDTH_MASK);
   if (flags & GD_STATES_STORED) {
     // the workspace holds what gd_forward(GD_STORE_STATES) wrote for these inputs: no recompute; the error word is
     // cleared here as gd_prep would
@@ -267,7 +267,7 @@ int gd_forward_packed(const void* q, const void* k, const void* v, const float* 
   auto ws = static_cast<unsigned char*>(workspace);
   if (cudaMemsetAsync(workspace, 0, sizeof(gd::ErrorWord), st) != cudaSuccess) return GD_ERR_LAUNCH;
   if ((s = launched(gd::launch_chunk_table(cu_seqlens, L, ws, st)))) return s;
-  const int f = flags & (GD_L2NORM | GD_SCALE_Q);
+  const int f = flags & (GD_L2NORM | GD_SCALE_Q | GD_KEY_WIDTH_MASK);
   if ((s = prep(q, k, v, g, beta, dtype, L, f, workspace, st))) return s;
   const int fs = f | (keep ? GD_STORE_STATES : 0) | (flags & GD_WIDE_STATE_PASS);
   if ((s = fwd_state(s0, ws + L.opad, sT, dtype, L, fs, workspace, st))) return s;
@@ -292,7 +292,7 @@ int gd_backward_packed(const void* q, const void* k, const void* v, const float*
   auto ws = static_cast<unsigned char*>(workspace);
   if (cudaMemsetAsync(workspace, 0, sizeof(gd::ErrorWord), st) != cudaSuccess) return GD_ERR_LAUNCH;
   if ((s = launched(gd::launch_chunk_table(cu_seqlens, L, ws, st)))) return s;
-  const int f = flags & (GD_L2NORM | GD_SCALE_Q);
+  const int f = flags & (GD_L2NORM | GD_SCALE_Q | GD_KEY_WIDTH_MASK);
   if (!(flags & GD_STATES_STORED)) {  // recompute the chunk states from the inputs
     if ((s = prep(q, k, v, g, beta, dtype, L, f, workspace, st))) return s;
     if ((s = fwd_state(s0, nullptr, nullptr, dtype, L, f | GD_STORE_STATES, workspace, st))) return s;

@@ -468,7 +468,7 @@ __global__ void __launch_bounds__(576, 1) bwd_chunk_kernel(const T* __restrict__
     float* scr = reinterpret_cast<float*>(smem + S::scr);
     auto P = [&](int which, int row, int t) -> float& { return part[(which * 4 + row) * 64 + t]; };
     const bool norm = (flags & GD_L2NORM) != 0;
-    const float qscale = (flags & GD_SCALE_Q) ? rsqrtf((float)DK) : 1.f;
+    const float qscale = q_scale(flags, DK);
     const unsigned char* qh = smem + S::qk;
     const unsigned char* ql = smem + S::qkl;
     const unsigned char* kh = smem + S::qk + DK * 64 * 2;

@@ -109,6 +109,14 @@ inline cudaError_t set_smem_once(K kern, size_t bytes, bool (&done)[kMaxDevices]
   return e;
 }
 
+// The query scale of GD_SCALE_Q: (key head width)^-1/2, the width from the flags' GD_KEY_WIDTH bits when the caller
+// zero-padded narrower heads to DK, else DK; 1 without GD_SCALE_Q.
+__device__ __forceinline__ float q_scale(int flags, int DK) {
+  if (!(flags & GD_SCALE_Q)) return 1.f;
+  const int w = (flags & GD_KEY_WIDTH_MASK) >> 16;
+  return rsqrtf((float)(w ? w : DK));
+}
+
 // ------------------------------------------------------------------------------------------------------------------
 // shared memory, fences, mbarriers, bulk copies
 

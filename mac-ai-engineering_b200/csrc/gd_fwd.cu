@@ -190,7 +190,7 @@ __global__ void __launch_bounds__(256, 2) prep_kernel(const T* __restrict__ q, c
   const size_t rrow = (((size_t)b * lay.HK + hk) * lay.NT + c) * 64;  // this chunk's 64 rsqrt slots
   float* rq = bwd ? reinterpret_cast<float*>(ws + lay.rq) + rrow : nullptr;
   float* rk = bwd ? reinterpret_cast<float*>(ws + lay.rk) + rrow : nullptr;
-  const float qscale = (flags & GD_SCALE_Q) ? rsqrtf((float)DK) : 1.f;
+  const float qscale = q_scale(flags, DK);
   Rows<T, DK, 8, staged> rq_rows, rk_rows;
   Rows<T, DV, 8, staged> rv_rows;
   GD_TRACE_AT(ws, lay, 21);

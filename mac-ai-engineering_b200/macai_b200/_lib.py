@@ -14,6 +14,14 @@ GD_OK, GD_ERR_ARG, GD_ERR_SHAPE, GD_ERR_ALIGN, GD_ERR_WORKSPACE, GD_ERR_LAUNCH, 
 GD_ERR_SCRATCH = 8
 GD_FLOAT32, GD_FLOAT16, GD_BFLOAT16 = 0, 1, 2
 GD_L2NORM, GD_STORE_STATES, GD_SCALE_Q, GD_STATES_STORED = 1, 2, 4, 8
+GD_KEY_WIDTH_MASK = 0x00FF0000
+
+
+def GD_KEY_WIDTH(dk: int) -> int:
+    """Flags bits carrying the caller's key head width when q / k are zero-padded to 128 (the query scale's width)."""
+    return (dk & 0xFF) << 16
+
+
 GD_WIDE_STATE_PASS = 16  # gd_fwd_state: always two CTAs per (head, row) (the default picks four when they fit)
 GD_TEST_WAIT_EXPIRES = 0x40000000  # test only: gd_fwd_state's first wait expires (the failure path's tests)
 

@@ -19,7 +19,8 @@ from .. import _lib
 # The chunk length of every kernel (tokens). The drop-in accepts `chunk_size` for signature compatibility and, like the
 # reference (op.py:268-269), runs its own chunking; 64 is also the value every caller passes.
 CHUNK = 64
-# Head widths the kernels are built for (the Qwen3.5 / Qwen3-Next linear-attention shapes).
+# Head widths the kernels are built for (the Qwen3.5 / Qwen3-Next linear-attention shapes); narrower multiples of 32
+# are zero-padded to it by the drop-in (_pad_heads).
 HEAD_DIMS = (128,)
 # What each call ran, as the reference's op.CALLS (op.py:44-46): "fwd", "fwd stored", "bwd", "bwd stored".
 CALLS: collections.Counter = collections.Counter()
@@ -78,8 +79,11 @@ def check_shapes(q, k, v, g, beta, s0=None) -> None:
         raise ValueError("query and value must share batch and sequence dimensions")
     if H % HK != 0:
         raise ValueError(f"value heads ({H}) must be a multiple of key heads ({HK})")
-    if DK not in HEAD_DIMS or DV not in HEAD_DIMS:
-        raise NotImplementedError(f"the B200 kernels are built for head widths {HEAD_DIMS}; got DK={DK}, DV={DV}")
+    if DK % 32 != 0 or DV % 32 != 0:
+        raise ValueError(f"head widths must be multiples of 32 (the reference's op.py:124-125); got DK={DK}, DV={DV}")
+    if DK > max(HEAD_DIMS) or DV > max(HEAD_DIMS):
+        raise NotImplementedError(f"the B200 kernels are built for head widths up to {max(HEAD_DIMS)} (narrower heads "
+                                  f"are zero-padded to it); got DK={DK}, DV={DV}")
     if g.shape != (B, T, H) or beta.shape != (B, T, H):
         raise ValueError(f"g and beta must be [B, T, H] = {(B, T, H)}; got {tuple(g.shape)}, {tuple(beta.shape)}")
     if s0 is not None and s0.shape != (B, H, DK, DV):
@@ -474,6 +478,30 @@ def _forward_packed(q, k, v, g, beta, s0, cu, flags):
     return gated_delta_fwd_packed(q, k, v, g, beta, s0, cu, flags)
 
 
+def _pad_heads(q, k, v, s0, flags):
+    """Heads narrower than the built width (multiples of 32 below 128) zero-padded to it, differentiably (autograd
+    slices the gradients back): zero key dimensions change neither the l2 norms nor the states, zero value columns stay
+    zero, and the query scale keeps the caller's key width (GD_KEY_WIDTH). Returns the padded tensors, the flags and
+    the caller's (DK, DV), or the inputs unchanged when they are built-width already."""
+    DK, DV, W = q.shape[-1], v.shape[-1], max(HEAD_DIMS)
+    if DK == W and DV == W:
+        return q, k, v, s0, flags, None
+    pad = torch.nn.functional.pad
+    q, k, v = pad(q, (0, W - DK)), pad(k, (0, W - DK)), pad(v, (0, W - DV))
+    s0 = None if s0 is None else pad(s0, (0, W - DV, 0, W - DK))
+    if flags & _lib.GD_SCALE_Q:
+        flags |= _lib.GD_KEY_WIDTH(DK)
+    return q, k, v, s0, flags, (DK, DV)
+
+
+def _unpad(o, sT, widths):
+    """The outputs of a padded call cut back to the caller's widths."""
+    if widths is None:
+        return o, sT
+    DK, DV = widths
+    return o[..., :DV], (None if sT is None else sT[..., :DK, :DV])
+
+
 # ------------------------------------------------------------------------------------------------------------------
 # the reference's Python surface
 
@@ -489,8 +517,10 @@ class GatedDeltaRule:
         check_dtype(dt)
         k, v = k.to(dt), v.to(dt)
         check_shapes(q, k, v, g, beta, s0)
-        return _forward(q.contiguous(), k.contiguous(), v.contiguous(), g.float().contiguous(),
-                        beta.float().contiguous(), None if s0 is None else s0.float().contiguous(), 0)
+        q, k, v, s0, flags, widths = _pad_heads(q, k, v, None if s0 is None else s0.float(), 0)
+        o, sT = _forward(q.contiguous(), k.contiguous(), v.contiguous(), g.float().contiguous(),
+                         beta.float().contiguous(), None if s0 is None else s0.contiguous(), flags)
+        return _unpad(o, sT, widths)
 
 
 def l2norm(x: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
@@ -526,14 +556,19 @@ def chunk_gated_delta_rule(query, key, value, g, beta, chunk_size: int = 64, ini
             raise ValueError(f"with cu_seqlens initial_state must be [N, H, DK, DV] = {(N, H, DK, DV)}; got "
                              f"{tuple(initial_state.shape)}")
         check_shapes(query, k, v, g, beta, None)
-        s0 = None if initial_state is None else initial_state.to(torch.float32).contiguous()
-        o, sT = _forward_packed(query.contiguous(), k.contiguous(), v.contiguous(), g.to(torch.float32).contiguous(),
-                                beta.to(torch.float32).contiguous(), s0, cu, flags)
+        s0 = None if initial_state is None else initial_state.to(torch.float32)
+        q, k, v, s0, flags, widths = _pad_heads(query, k, v, s0, flags)
+        o, sT = _forward_packed(q.contiguous(), k.contiguous(), v.contiguous(), g.to(torch.float32).contiguous(),
+                                beta.to(torch.float32).contiguous(), None if s0 is None else s0.contiguous(), cu,
+                                flags)
+        o, sT = _unpad(o, sT, widths)
         return o, (sT if output_final_state else None)
     check_shapes(query, k, v, g, beta, initial_state)
-    s0 = None if initial_state is None else initial_state.to(torch.float32).contiguous()
-    o, sT = _forward(query.contiguous(), k.contiguous(), v.contiguous(), g.to(torch.float32).contiguous(),
-                     beta.to(torch.float32).contiguous(), s0, flags)
+    s0 = None if initial_state is None else initial_state.to(torch.float32)
+    q, k, v, s0, flags, widths = _pad_heads(query, k, v, s0, flags)
+    o, sT = _forward(q.contiguous(), k.contiguous(), v.contiguous(), g.to(torch.float32).contiguous(),
+                     beta.to(torch.float32).contiguous(), None if s0 is None else s0.contiguous(), flags)
+    o, sT = _unpad(o, sT, widths)
     return o, (sT if output_final_state else None)
 
 

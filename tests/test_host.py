@@ -29,8 +29,13 @@ def test_packed_rows_checked_before_any_launch():
 
 
 def test_unsupported_head_width_refused():
-    x = torch.zeros(1, 4, 1, 64, dtype=torch.bfloat16)
+    """Widths above the built 128 are refused (NotImplementedError), widths that are not multiples of 32 rejected
+    (ValueError, as the reference's op.py:124-125); 32-96 are padded (tests/test_gpu_head_widths.py)."""
+    x = torch.zeros(1, 4, 1, 256, dtype=torch.bfloat16)
     with pytest.raises(NotImplementedError):
+        chunk_gated_delta_rule(x, x, x, x[..., 0], x[..., 0])
+    x = torch.zeros(1, 4, 1, 80, dtype=torch.bfloat16)
+    with pytest.raises(ValueError):
         chunk_gated_delta_rule(x, x, x, x[..., 0], x[..., 0])
 
 
