@@ -7,7 +7,7 @@
 // (tools/check_chunk_equations.py:51-52 and src/macai/gated_delta/_chunked.py:20-24 of the reference). Only K~ dS and
 // W^T dVn are on the sequential chain; M^T dO and (gamma Q)^T dO do not depend on dS and are issued one chunk ahead.
 // It keeps, per chunk, the images the per-chunk gradient kernel reads: dS_{c+1}^T (hi, lo), dVn^T (hi, lo), dO, and
-// the 16 partial sums of <S_c, dS_{c+1}> (from the forward recompute's fp32 S_c^T).
+// the 16 partial sums of <S_c, dS_{c+1}> (S_c = hi + lo from the forward recompute's two bf16 images).
 //
 // Warp specialisation as in the forward pass: 16 epilogue warps reading the M = 64 products whole-warp (thread t of
 // warp w: local value column 16 (w % 4) + t % 16, 8 tokens and 16 key rows of dS held in registers; they also write
@@ -110,6 +110,14 @@ __global__ void __launch_bounds__(576) bwd_state_kernel(const T* __restrict__ d_
     bulk_g2s(smem + S::wt + DK * 64 * 2, ws + lay.wtl + (row0 + c) * lay.wt_bytes(), (uint32_t)lay.wt_bytes(),
              wt_full);
   };
+  auto prefetch_state = [&](int c) {  // S_c's hi and lo images into L2, for the epilogue's <S_c, dS_{c+1}> partials
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(ws + lay.sci + (row0 + c) * lay.si_bytes()),
+                 "r"((uint32_t)lay.si_bytes())
+                 : "memory");
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(ws + lay.scl + (row0 + c) * lay.si_bytes()),
+                 "r"((uint32_t)lay.si_bytes())
+                 : "memory");
+  };
   auto load_pre = [&](int c) {
     mbar_arrive_expect_tx(pre_full, (uint32_t)(lay.mm_bytes() + lay.qk_bytes()));
     bulk_g2s(smem + S::m, ws + lay.m + (row0 + c) * lay.mm_bytes(), (uint32_t)lay.mm_bytes(), pre_full);
@@ -188,9 +196,7 @@ __global__ void __launch_bounds__(576) bwd_state_kernel(const T* __restrict__ d_
       }
       load_wt(NT - 1);
       load_pre(NT - 1);
-      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(ws + lay.scf + (row0 + NT - 1) * lay.s_bytes()),
-                   "r"((uint32_t)lay.s_bytes())
-                   : "memory");
+      prefetch_state(NT - 1);
       ++nw;
       ++np;
       for (int n = 0; n + 1 < NT && ok; ++n) {
@@ -198,9 +204,7 @@ __global__ void __launch_bounds__(576) bwd_state_kernel(const T* __restrict__ d_
         ok = mbar_wait(a_full, n & 1, err, 34);  // chunk c's dS-independent products have read M and gamma Q
         if (!ok) break;
         // the next chunk's fp32 state into L2, for the epilogue's <S, dS> partial sums
-        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(ws + lay.scf + (row0 + c - 1) * lay.s_bytes()),
-                     "r"((uint32_t)lay.s_bytes())
-                     : "memory");
+        prefetch_state(c - 1);
         load_pre(c - 1);
         ++np;
         ok = mbar_wait(d_full, n & 1, err, 38);  // -W^T dVn of chunk c has read W^T; K~ dS read stage n & 1
@@ -295,23 +299,32 @@ __global__ void __launch_bounds__(576) bwd_state_kernel(const T* __restrict__ d_
       // the next chunk's dO tile (this chunk's dO products are done: a_full), published before any new load is in
       // flight
       if (c > 0) put_do(c - 1);
-      // partial <S_c, dS_{c+1}> of this thread's 16 entries (fp32 S_c from the forward recompute, prefetched into L2 a
-      // chunk ahead; lanes read adjacent 16-byte pieces): loads in flight through the wait for -(W^T dVn)^T
-      const float4* sc = reinterpret_cast<const float4*>(ws + lay.scf + cidx * lay.s_bytes()) +
-                         (size_t)(quarter * 8 + 4 * (lane >> 4)) * DV + v;
-      float4 sx[4];
-#pragma unroll
-      for (int q4 = 0; q4 < 4; ++q4) sx[q4] = __ldg(sc + (size_t)q4 * DV);
+      // partial <S_c, dS_{c+1}> of this thread's 16 entries: S_c = hi + lo from the forward recompute's two bf16
+      // images (row v, key rows dk0 .. dk0 + 15: two 16-byte pieces each; prefetched into L2 a chunk ahead), dS_{c+1}
+      // exact in registers; loads in flight through the wait for -(W^T dVn)^T
+      const unsigned char* sch = ws + lay.sci + cidx * lay.si_bytes();
+      const unsigned char* scl = ws + lay.scl + cidx * lay.si_bytes();
+      const uint4 sh0 = __ldg(reinterpret_cast<const uint4*>(sch + blk_off(v, dk0, DK)));
+      const uint4 sh1 = __ldg(reinterpret_cast<const uint4*>(sch + blk_off(v, dk0 + 8, DK)));
+      const uint4 sl0 = __ldg(reinterpret_cast<const uint4*>(scl + blk_off(v, dk0, DK)));
+      const uint4 sl1 = __ldg(reinterpret_cast<const uint4*>(scl + blk_off(v, dk0 + 8, DK)));
       // * dS_c = exp(G_last) dS_{c+1} + (gamma Q)^T dO - W^T dVn
       GD_TRACE_AT(ws, lay, 8 * n + 3);
       if (!mbar_wait(d_full, n & 1, err, 43)) { ok = false; break; }
       tc_fence_after();
       GD_TRACE_AT(ws, lay, 8 * n + 4);
       float sacc = 0.f;
+      {
+        const uint32_t wh[8] = {sh0.x, sh0.y, sh0.z, sh0.w, sh1.x, sh1.y, sh1.z, sh1.w};  // bf16 pairs, low half first
+        const uint32_t wl[8] = {sl0.x, sl0.y, sl0.z, sl0.w, sl1.x, sl1.y, sl1.z, sl1.w};
 #pragma unroll
-      for (int q4 = 0; q4 < 4; ++q4)
-        sacc = fmaf(sx[q4].x, Dr[4 * q4], fmaf(sx[q4].y, Dr[4 * q4 + 1], fmaf(sx[q4].z, Dr[4 * q4 + 2],
-                                                                              fmaf(sx[q4].w, Dr[4 * q4 + 3], sacc))));
+        for (int e = 0; e < 8; ++e) {
+          const float s0 = __uint_as_float(wh[e] << 16) + __uint_as_float(wl[e] << 16);
+          const float s1 = __uint_as_float(wh[e] & 0xffff0000u) + __uint_as_float(wl[e] & 0xffff0000u);
+          sacc = fmaf(s0, Dr[2 * e], sacc);
+          sacc = fmaf(s1, Dr[2 * e + 1], sacc);
+        }
+      }
       {
         float cc[16];
         tmem_ld16h(tmem_lane_addr(tm + 192 + 128 * (n & 1), warp, 32 * quarter), cc);

@@ -469,8 +469,8 @@ __global__ void __launch_bounds__(256, 2) prep_kernel(const T* __restrict__ q, c
 //        rows after an 8 x 8 transpose): it runs under chunk c's state-update product, off the chain
 //   EPI: wait ds_full -> S <- exp(G_last) S + K~^T Vn -> S tile -> st_full
 // With GD_STORE_STATES (the backward's recompute, or a training forward that keeps its states) the pass also keeps S_c
-// (fp32 and a bf16 S_c^T image) and the Vn^T hi / lo images of every chunk for the backward kernels (each CTA its 64
-// rows of them); O is formed when o is not null.
+// (a bf16 S_c^T image and its low half) and the Vn^T hi / lo images of every chunk for the backward kernels (each CTA
+// its 64 rows of them); O is formed when o is not null.
 
 constexpr int kVsplit = 2;  // CTAs per (value head, batch row)
 
@@ -662,15 +662,17 @@ __global__ void __launch_bounds__(576) state_kernel(const float* __restrict__ s0
       fence_async_smem();
       mbar_arrive_warp(st_full);
     }
-    // the fp32 state entering chunk c, for the backward (lanes 0-15 / 16-31 write adjacent 16-byte pieces)
-    auto store_scf = [&](int c) {
-      float4* sc = reinterpret_cast<float4*>(ws + lay.scf + (row0 + c) * lay.s_bytes()) +
-                   (size_t)(quarter * 8 + 4 * (lane >> 4)) * DV + v;
+    // the low half of the state entering chunk c, for the backward's <S_c, dS_{c+1}> (its high half is the S_c^T image
+    // the MMA thread copies out of the S tile): this CTA's rows of the [DV x DK] image, 16-byte pieces
+    auto store_slo = [&](int c) {
+      unsigned char* lo = ws + lay.scl + (row0 + c) * lay.si_bytes();
+      float hi[16], l[16];
 #pragma unroll
-      for (int q4 = 0; q4 < 4; ++q4)
-        sc[(size_t)q4 * DV] = make_float4(Sr[4 * q4], Sr[4 * q4 + 1], Sr[4 * q4 + 2], Sr[4 * q4 + 3]);
+      for (int j = 0; j < 16; ++j) split_bf16(Sr[j], hi[j], l[j]);
+#pragma unroll
+      for (int q8 = 0; q8 < 2; ++q8) store8_bf16(lo, v, dk0 + 8 * q8, DK, l + 8 * q8);
     };
-    if (store) store_scf(0);
+    if (store) store_slo(0);
     // U of the next chunk, and G (cumulative log gates) at tokens tk .. tk + 7 and the chunk's last token: read from L2
     // one pass ahead so that no stage holds G for the late O product
     float Ur[8], gcur[8], gcur_last, gprev[8];
@@ -784,7 +786,7 @@ __global__ void __launch_bounds__(576) state_kernel(const float* __restrict__ s0
         GD_TRACE_AT(ws, lay, 2048 + 8 * c + 5);
         mbar_arrive_warp(st_full);
       }
-      if (store && c + 1 < NT) store_scf(c + 1);  // off the chain: the next MMAs are already unblocked
+      if (store && c + 1 < NT) store_slo(c + 1);  // off the chain: the next MMAs are already unblocked
       if (out && c >= 1 && !store_o(c - 1)) {  // likewise
         ok = false;
         break;

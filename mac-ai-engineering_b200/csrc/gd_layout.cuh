@@ -17,10 +17,9 @@
 //   wtl  [DK x 64]    image   the low half of wt (W^T = hi + lo)
 //   vi   [DV x 64]    image   V^T
 //   rq, rk [B][HK][NT * 64] fp32  the l2 prologue's rsqrt per raw q / k row (a chunk's 64 rows contiguous)
-// The state pass with GD_STORE_STATES writes per chunk
-//   scf  [DK/32][8][DV][4] fp32  S_c, the state entering the chunk: element (dk, v) at float
-//                               ((dk / 32 * 8 + dk % 32 / 4) * DV + v) * 4 + dk % 4 (a warp's 16-byte pieces adjacent)
-//   sci  [DV x DK]    image   S_c^T (bf16)
+// The state pass with GD_STORE_STATES writes per chunk (S_c the state entering the chunk)
+//   sci  [DV x DK]    image   S_c^T, bf16 (its high half)
+//   scl  [DV x DK]    image   the low half of S_c^T (S_c = hi + lo to ~16 significant bits)
 //   vni  [2][DV x 64] image   Vn^T: hi, then lo
 // and the reverse pass
 //   dsi  [2][DV x DK] image   dS_{c+1}^T: hi, then lo
@@ -56,7 +55,7 @@ struct Layout {
   int Tin;  // rows a batch row has in the caller's token arrays (T, or the packed total)
   size_t nch;  // B * H * NT chunks
   size_t err, trace, ctab, seg, ord, opad, dqpad, dkpad, dvpad, qk, qkl, kt, wt, m, u, gc;
-  size_t gq, ai, wtl, vi, rq, rk, scf, sci, vni, dsi, dvni, doi, sl, total;
+  size_t gq, ai, wtl, vi, rq, rk, sci, scl, vni, dsi, dvni, doi, sl, total;
 
   __host__ __device__ static size_t up(size_t x) { return (x + 255) & ~size_t(255); }
 
@@ -67,7 +66,6 @@ struct Layout {
   __host__ __device__ size_t u_bytes() const { return (size_t)64 * DV * 4; }
   __host__ __device__ size_t gc_bytes() const { return (size_t)64 * 4; }
   __host__ __device__ size_t vi_bytes() const { return (size_t)64 * DV * 2; }
-  __host__ __device__ size_t s_bytes() const { return (size_t)DK * DV * 4; }       // fp32 state
   __host__ __device__ size_t si_bytes() const { return (size_t)DK * DV * 2; }      // one state image
   __host__ __device__ size_t vn_bytes() const { return (size_t)2 * DV * 64 * 2; }  // a [2][DV x 64] image pair
   __host__ __device__ size_t sl_bytes() const { return (size_t)32 * 4; }           // <S, dS> partial sums
@@ -116,20 +114,20 @@ struct Layout {
       L.vi = take(L.nch * L.vi_bytes());
       L.rq = take((size_t)B * HK * L.NT * 64 * 4);
       L.rk = take((size_t)B * HK * L.NT * 64 * 4);
-      L.scf = take(L.nch * L.s_bytes());
       L.sci = take(L.nch * L.si_bytes());
+      L.scl = take(L.nch * L.si_bytes());
       L.vni = take(L.nch * L.vn_bytes());
       L.dsi = take(L.nch * 2 * L.si_bytes());
       L.dvni = take(L.nch * L.vn_bytes());
       L.doi = take(L.nch * L.vi_bytes());
       L.sl = take(L.nch * L.sl_bytes());
     } else {
-      L.qkl = L.gq = L.ai = L.wtl = L.vi = L.rq = L.rk = L.scf = L.sci = L.vni = L.dsi = L.dvni = L.doi = L.sl = 0;
+      L.qkl = L.gq = L.ai = L.wtl = L.vi = L.rq = L.rk = L.sci = L.scl = L.vni = L.dsi = L.dvni = L.doi = L.sl = 0;
     }
     L.total = o;
     return L;
   }
-  __host__ __device__ bool backward() const { return scf != 0; }
+  __host__ __device__ bool backward() const { return sci != 0; }
   __host__ __device__ bool packed() const { return N > 0; }
 
   // chunk c's rows (regular batches: c * 64 up to T; packed rows: from the chunk table)
