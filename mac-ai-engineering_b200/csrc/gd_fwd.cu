@@ -493,15 +493,18 @@ struct StateSmem {
   static constexpr size_t total = tmem + 8;
 };
 
+// A chunk's stage: W^T and K~ always, the q and M images only when O is formed (the Q S and M Vn products)
 template <int DK, int DV>
 __device__ __forceinline__ void issue_stage(unsigned char* stg, const unsigned char* ws, const Layout& lay,
-                                            size_t cidx, uint64_t* bar) {
+                                            size_t cidx, uint64_t* bar, bool out) {
   using S = StateSmem<DK, DV>;
-  mbar_arrive_expect_tx(bar, (uint32_t)S::stage_bytes);
+  mbar_arrive_expect_tx(bar, (uint32_t)(out ? S::stage_bytes : lay.wt_bytes() + lay.qk_bytes()));
   bulk_g2s(stg + S::s_wt, ws + lay.wt + cidx * lay.wt_bytes(), (uint32_t)lay.wt_bytes(), bar);
-  bulk_g2s(stg + S::s_q, ws + lay.qk + cidx * lay.qk_bytes(), 64 * DK * 2, bar);
   bulk_g2s(stg + S::s_kt, ws + lay.kt + cidx * lay.qk_bytes(), (uint32_t)lay.qk_bytes(), bar);
-  bulk_g2s(stg + S::s_m, ws + lay.m + cidx * lay.mm_bytes(), (uint32_t)lay.mm_bytes(), bar);
+  if (out) {
+    bulk_g2s(stg + S::s_q, ws + lay.qk + cidx * lay.qk_bytes(), 64 * DK * 2, bar);
+    bulk_g2s(stg + S::s_m, ws + lay.m + cidx * lay.mm_bytes(), (uint32_t)lay.mm_bytes(), bar);
+  }
 }
 
 template <typename T, int DK, int DV>
@@ -639,7 +642,7 @@ __global__ void __launch_bounds__(576) state_kernel(const float* __restrict__ s0
       for (; c < NT; ++c) {
         const int s = c & 1;
         if (c >= 2 && !mbar_wait(stage_free + s, ((c - 2) >> 1) & 1, err, 23)) break;
-        issue_stage<DK, DV>(smem + S::stage0 + s * S::stage_bytes, ws, lay, row0 + c, full + s);
+        issue_stage<DK, DV>(smem + S::stage0 + s * S::stage_bytes, ws, lay, row0 + c, full + s, out);
       }
       // every copy issued here lands before the CTA may exit, also after a failed wait
       for (int l = c >= 2 ? c - 2 : 0; l < c; ++l) mbar_wait(full + (l & 1), (l >> 1) & 1, err, 29);
