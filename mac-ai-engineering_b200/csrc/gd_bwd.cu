@@ -15,7 +15,8 @@
 // waits on the product that frees its buffer, which is also the product whose next phase needs that refill); all
 // hand-offs are mbarriers. Per chunk the MMA thread issues only: K~ dS (chain) -> -W^T dVn (chain, added onto the
 // chunk's (gamma Q)^T dO) -> the next chunk's dS-independent products. Precision: dS and K~, dVn and W split into
-// bf16 hi + lo (three products each), gamma Q and M split, dO exact in bf16.
+// bf16 hi + lo (three products each); (gamma Q)^T dO as q^T (diag(gamma) dO) with q and gamma dO split; M split, dO
+// exact in bf16.
 #include "gd_common.cuh"
 #include "gd_layout.cuh"
 
@@ -34,9 +35,11 @@ struct BwdStateSmem {
   static constexpr size_t crit_bytes = c_g + 64 * 4;
   static constexpr size_t wt = crit0 + 2 * crit_bytes;     // [2][DK x 64] W^T hi, lo (one buffer)
   static constexpr size_t m = wt + 2 * DK * 64 * 2;        // [2][64 x 64] M hi, lo } inputs of the dS-independent
-  static constexpr size_t gq = m + 2 * 64 * 64 * 2;        // [2][64 x DK] gamma Q }  products, one chunk ahead
-  static constexpr size_t dO = gq + 2 * 64 * DK * 2;       // [64 x DVH] dO      }
-  static constexpr size_t bar = dO + 64 * DVH * 2;
+  static constexpr size_t qh = m + 2 * 64 * 64 * 2;        // [DK x 64] q^T hi  } inputs of the dS-independent
+  static constexpr size_t ql = qh + DK * 64 * 2;           // [DK x 64] q^T lo  }  products, one chunk ahead
+  static constexpr size_t dO = ql + DK * 64 * 2;           // [64 x DVH] dO     }
+  static constexpr size_t gdo = dO + 64 * DVH * 2;         // [2][64 x DVH] diag(gamma) dO hi, lo }
+  static constexpr size_t bar = gdo + 2 * 64 * DVH * 2;
   static constexpr int NBAR = 12;
   static constexpr size_t tmem = bar + NBAR * 8;
   static constexpr size_t total = tmem + 8;
@@ -121,16 +124,21 @@ __global__ void __launch_bounds__(576) bwd_state_kernel(const T* __restrict__ d_
   auto load_pre = [&](int c) {
     mbar_arrive_expect_tx(pre_full, (uint32_t)(lay.mm_bytes() + lay.qk_bytes()));
     bulk_g2s(smem + S::m, ws + lay.m + (row0 + c) * lay.mm_bytes(), (uint32_t)lay.mm_bytes(), pre_full);
-    bulk_g2s(smem + S::gq, ws + lay.gq + (row0 + c) * lay.qk_bytes(), (uint32_t)lay.qk_bytes(), pre_full);
+    bulk_g2s(smem + S::qh, ws + lay.qk + (row0 + c) * lay.qk_bytes(), DK * 64 * 2, pre_full);   // the q halves of
+    bulk_g2s(smem + S::ql, ws + lay.qkl + (row0 + c) * lay.qk_bytes(), DK * 64 * 2, pre_full);  //  the q / k images
   };
   const Tile tDO{smem_u32(smem + S::dO), DVH};
-  // (M^T dO)^T = dO^T M [DVH x 64] (M hi + lo); ((gamma Q)^T dO)^T = dO^T (gamma Q) [DVH x DK], gamma Q split
+  // (M^T dO)^T = dO^T M [DVH x 64] (M hi + lo); ((gamma Q)^T dO)^T [DVH x DK] as below
   auto issue_pre = [&](int n) {
     mma_tiles(tA, DVH, 64, 64, tDO, false, 0, 0, Tile{smem_u32(smem + S::m), 64}, true, 0, false);
     mma_tiles(tA, DVH, 64, 64, tDO, false, 0, 0, Tile{smem_u32(smem + S::m + 64 * 64 * 2), 64}, true, 0, true);
     const uint32_t tC = tm + 192 + 128 * (n & 1);
-    mma_tiles(tC, DVH, DK, 64, tDO, false, 0, 0, Tile{smem_u32(smem + S::gq), DK}, true, 0, false);
-    mma_tiles(tC, DVH, DK, 64, tDO, false, 0, 0, Tile{smem_u32(smem + S::gq + 64 * DK * 2), DK}, true, 0, true);
+    // ((gamma Q)^T dO)^T = (diag(gamma) dO)^T Q: gamma dO and q split, q^T images as K-major B
+    const Tile tGh{smem_u32(smem + S::gdo), DVH}, tGl{smem_u32(smem + S::gdo + 64 * DVH * 2), DVH};
+    const Tile tQh{smem_u32(smem + S::qh), 64}, tQl{smem_u32(smem + S::ql), 64};
+    mma_tiles(tC, DVH, DK, 64, tGh, false, 0, 0, tQh, false, 0, false);
+    mma_tiles(tC, DVH, DK, 64, tGh, false, 0, 0, tQl, false, 0, true);
+    mma_tiles(tC, DVH, DK, 64, tGl, false, 0, 0, tQh, false, 0, true);
     mma_commit(a_full);
   };
 
@@ -244,6 +252,7 @@ __global__ void __launch_bounds__(576) bwd_state_kernel(const T* __restrict__ d_
     // a chunk's dO tile (this CTA's 64 columns): 512 16-byte pieces, one per thread, eight consecutive threads per
     // 128-byte core matrix; fetched raw into registers early, written to the tile once the tile's readers are done
     Piece<T> dox;
+    float dog = 0.f;  // G of the piece's token
     const int prl = tid & 7, pcb = (tid >> 3) & 7, prb = tid >> 6;
     auto fetch_do = [&](int c) {  // rows of the chunk's span in the caller's dO (zero past the sequence's end)
       const ChunkSpan sp = lay.span(ws, cfirst + c);
@@ -253,11 +262,18 @@ __global__ void __launch_bounds__(576) bwd_state_kernel(const T* __restrict__ d_
       } else {
         dox.zero();
       }
+      dog = __ldg(reinterpret_cast<const float*>(ws + lay.gc + (row0 + c) * lay.gc_bytes()) + 8 * prb + prl);
     };
-    auto put_do = [&](int c) {  // chunk c's dO: the tile, then this CTA's columns of the [64 x DV] image
-      float x[8];
+    // chunk c's dO: the tile and diag(gamma) dO split hi / lo (with q's images, (gamma Q)^T dO without a gamma Q
+    // image), then this CTA's columns of the [64 x DV] dO image
+    auto put_do = [&](int c) {
+      float x[8], y[8];
       dox.to_f32(x);
+      const float gam = __expf(dog);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) y[j] = gam * x[j];
       store8_bf16(smem + S::dO, 8 * prb + prl, 8 * pcb, DVH, x);
+      store8_split(smem + S::gdo, smem + S::gdo + 64 * DVH * 2, 8 * prb + prl, 8 * pcb, DVH, y);
       fence_async_smem();
       mbar_arrive_warp(do_full);
       store8_bf16(ws + lay.doi + (row0 + c) * lay.vi_bytes(), 8 * prb + prl, vbase + 8 * pcb, DV, x);

@@ -257,27 +257,6 @@ __global__ void __launch_bounds__(256, 2) prep_kernel(const T* __restrict__ q, c
     store_tile_transposed<64, DK, 8>(smem + S::ql, dst);
     store_tile_transposed<64, DK, 8>(smem + S::kl, dst + 64 * DK * 2);
   }
-  if constexpr (BWD) {  // diag(gamma) Q from q's hi + lo, split again: the reverse pass's operand
-    unsigned char* gqh = ws + lay.gq + cidx * lay.qk_bytes();
-    unsigned char* gql = gqh + 64 * DK * 2;
-    for (int idx = tid; idx < 64 * DK / 8; idx += 256) {
-      const int rl = idx & 7, cb = (idx >> 3) % (DK / 8), rb = idx / (8 * (DK / 8));
-      const int r = 8 * rb + rl;
-      const uint4 uh = *reinterpret_cast<const uint4*>(smem + S::q + blk_off(r, 8 * cb, DK));
-      const uint4 ul = *reinterpret_cast<const uint4*>(smem + S::ql + blk_off(r, 8 * cb, DK));
-      const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&uh);
-      const __nv_bfloat162* l2 = reinterpret_cast<const __nv_bfloat162*>(&ul);
-      const float gr = sGam[r];
-      float x[8];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 fh = __bfloat1622float2(h2[e]), fl = __bfloat1622float2(l2[e]);
-        x[2 * e] = gr * (fh.x + fl.x);
-        x[2 * e + 1] = gr * (fh.y + fl.y);
-      }
-      store8_split(gqh, gql, r, 8 * cb, DK, x);
-    }
-  }
   {  // K~ = diag(e) K (e_i = exp(G_last - G_i) <= 1) from k's hi + lo, split again: the state update's operand
     unsigned char* kth = ws + lay.kt + cidx * lay.qk_bytes();
     unsigned char* ktl = kth + 64 * DK * 2;

@@ -12,7 +12,6 @@
 //   gc   [64]         fp32    G, the in-chunk inclusive cumulative sum of g
 // and for the backward also
 //   qkl  [2][DK x 64] image   the low halves of qk (q = hi + lo to ~16 significant bits)
-//   gq   [2][64 x DK] image   diag(gamma) Q: hi, then lo
 //   ai   [2][64 x 64] image   A = (I + L)^-1: hi, then lo
 //   wtl  [DK x 64]    image   the low half of wt (W^T = hi + lo)
 //   vi   [DV x 64]    image   V^T
@@ -55,7 +54,7 @@ struct Layout {
   int Tin;  // rows a batch row has in the caller's token arrays (T, or the packed total)
   size_t nch;  // B * H * NT chunks
   size_t err, trace, ctab, seg, ord, opad, dqpad, dkpad, dvpad, qk, qkl, kt, wt, m, u, gc;
-  size_t gq, ai, wtl, vi, rq, rk, sci, scl, vni, dsi, dvni, doi, sl, total;
+  size_t ai, wtl, vi, rq, rk, sci, scl, vni, dsi, dvni, doi, sl, total;
 
   __host__ __device__ static size_t up(size_t x) { return (x + 255) & ~size_t(255); }
 
@@ -108,7 +107,6 @@ struct Layout {
     L.gc = take(L.nch * L.gc_bytes());
     if (backward) {
       L.qkl = take(L.nch * L.qk_bytes());
-      L.gq = take(L.nch * L.qk_bytes());
       L.ai = take(L.nch * L.mm_bytes());
       L.wtl = take(L.nch * L.wt_bytes());
       L.vi = take(L.nch * L.vi_bytes());
@@ -122,7 +120,7 @@ struct Layout {
       L.doi = take(L.nch * L.vi_bytes());
       L.sl = take(L.nch * L.sl_bytes());
     } else {
-      L.qkl = L.gq = L.ai = L.wtl = L.vi = L.rq = L.rk = L.sci = L.scl = L.vni = L.dsi = L.dvni = L.doi = L.sl = 0;
+      L.qkl = L.ai = L.wtl = L.vi = L.rq = L.rk = L.sci = L.scl = L.vni = L.dsi = L.dvni = L.doi = L.sl = 0;
     }
     L.total = o;
     return L;
