@@ -1,6 +1,7 @@
 // Forward kernels of the chunked gated delta rule on B200 (sm_100a):
-//   prep_kernel   one CTA of 256 threads per (chunk, value head, batch row): l2 prologue, cumulative decay, the C x C products
-//                 on tcgen05, the unit-lower-triangular inverse, W and U;
+//   prep_kernel   persistent CTAs of 256 threads (two per SM), each taking (chunk, value head, batch row) items in turn:
+//                 l2 prologue, cumulative decay, the C x C products on tcgen05, the unit-lower-triangular inverse, W and
+//                 U;
 //   state_kernel  one CTA per (value head, batch row): the sequential chunk pass with the state in registers (fp32) and
 //                 every product on tcgen05 from shared memory, chunk inputs streamed in by the bulk-copy engine.
 // Equations (per chunk; src/macai/gated_delta/_chunked.py:1-35, tools/check_chunk_equations.py:29-46 of the reference):
@@ -40,7 +41,9 @@ struct PrepSmem {
   static constexpr size_t gam = beta + 64 * 4;            // [64] gamma = exp(G)
   static constexpr size_t bgam = gam + 64 * 4;            // [64] beta gamma
   static constexpr size_t scan = bgam + 64 * 4;           // [2] warp totals of the scan
-  static constexpr size_t bar = (scan + 16 + 7) & ~size_t(7);  // [2] MMA commits; raw rows landed (16-bit types)
+  static constexpr size_t rng = scan + 16;                // [2][2] per-warp max, min of G
+  static constexpr size_t colf = rng + 16;                // [64] exp(G_ref - G_j): the decay's column factors
+  static constexpr size_t bar = (colf + 64 * 4 + 7) & ~size_t(7);  // [2] MMA commits; raw rows landed (16-bit types)
   static constexpr size_t tmem = bar + 2 * 8;
   static constexpr size_t total = tmem + 16;
 };
@@ -76,7 +79,7 @@ __device__ __forceinline__ void strip(const float* X, int xs, const float* Z, in
 }
 
 __device__ __forceinline__ void unit_lower_inverse(const float* L, float* A, float* Y, unsigned char* ws,
-                                                   const Layout& lay) {
+                                                   const Layout& lay, int tb) {
   const int tid = threadIdx.x;
   if (tid < 64) {
     const int b = tid >> 4, j = tid & 15, r0 = 16 * b;
@@ -105,9 +108,9 @@ __device__ __forceinline__ void unit_lower_inverse(const float* L, float* A, flo
       *reinterpret_cast<float4*>(A + (16 * bi + r) * 68 + 16 * bj + 4 * c4) = make_float4(0.f, 0.f, 0.f, 0.f);
     }
   }
-  GD_TRACE_AT(ws, lay, 16);
+  GD_TRACE_AT(ws, lay, tb + 16);
   __syncthreads();
-  GD_TRACE_AT(ws, lay, 17);
+  GD_TRACE_AT(ws, lay, tb + 17);
   // 2. pairs p = 0, 1: blocks lo = 2p, hi = 2p + 1 (rows / columns 16 lo .., 16 hi ..)
   const int p = tid >> 6, i16 = (tid >> 2) & 15, j4 = 4 * (tid & 3);
   if (tid < 128)  // Y_p = L[hi][lo] T_lo
@@ -117,14 +120,14 @@ __device__ __forceinline__ void unit_lower_inverse(const float* L, float* A, flo
     strip<16>(A + (32 * p + 16) * 68 + 32 * p + 16, 68, Y + 16 * p * 36, 36, A + (32 * p + 16) * 68 + 32 * p, 68, -1.f,
               i16, j4);
   __syncthreads();
-  GD_TRACE_AT(ws, lay, 18);
+  GD_TRACE_AT(ws, lay, tb + 18);
   // 3. Y = L[32:64][0:32] A_11 ; A[32:64][0:32] = -A_22 Y
   const int i32 = tid >> 3, j8 = 4 * (tid & 7);
   strip<32>(L + 32 * 68, 68, A, 68, Y, 36, 1.f, i32, j8);
   __syncthreads();
-  GD_TRACE_AT(ws, lay, 19);
+  GD_TRACE_AT(ws, lay, tb + 19);
   strip<32>(A + 32 * 68 + 32, 68, Y, 36, A + 32 * 68, 68, -1.f, i32, j8);
-  GD_TRACE_AT(ws, lay, 20);
+  GD_TRACE_AT(ws, lay, tb + 20);
 }
 
 // BWD: the backward layout (its extra images); the forward instance carries none of that code
@@ -139,288 +142,379 @@ __global__ void __launch_bounds__(256, 2) prep_kernel(const T* __restrict__ q, c
   using S = PrepSmem<DK, DV>;
   extern __shared__ __align__(1024) unsigned char smem[];
   ErrorWord* err = reinterpret_cast<ErrorWord*>(ws + lay.err);
-  const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const int hk = h / lay.rep;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  // the chunk's rows in the caller's arrays: t0 .. t0 + 63, those below tend valid (the sequence's end)
-  const ChunkSpan span = lay.span(ws, c);
-  const int t0 = span.t0, tend = span.end;
-  const size_t cidx = ((size_t)b * lay.H + h) * lay.NT + c;
   float* sL = reinterpret_cast<float*>(smem + S::L);
   float* sAi = reinterpret_cast<float*>(smem + S::Ai);
   float* sG = reinterpret_cast<float*>(smem + S::G);
   float* sB = reinterpret_cast<float*>(smem + S::beta);
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + S::bar);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + S::tmem);
+  constexpr bool staged = sizeof(T) == 2;
+  // Persistent: CTA x takes the chunks x, x + gridDim.x, ... of the B x H x NT items (chunk index fastest). The next
+  // item's raw rows, g and beta are requested as soon as the current item's W / U products have read the tiles, so
+  // their latency hides under the W / U epilogue.
+  const long long n_items = (long long)lay.NT * lay.H * lay.B;
+  auto item_of = [&](long long it, int& c, int& h, int& b) {
+    c = (int)(it % lay.NT);
+    const long long r = it / lay.NT;
+    h = (int)(r % lay.H);
+    b = (int)(r / lay.H);
+  };
+  // this chunk's g and beta (threads 0-63, one token each; padding rows: g = 0, beta = 0, which leaves G constant
+  // past the last token)
+  auto load_gb = [&](int c, int h, int b, float& gv, float& bv) {
+    const ChunkSpan sp = lay.span(ws, c);
+    gv = 0.f;
+    bv = 0.f;
+    if (tid < 64 && sp.t0 + tid < sp.end) {
+      gv = __ldg(g + ((size_t)b * lay.Tin + sp.t0 + tid) * lay.H + h);
+      bv = __ldg(beta + ((size_t)b * lay.Tin + sp.t0 + tid) * lay.H + h);
+    }
+  };
+  // 16-bit inputs: the chunk's raw q, k, v rows land row-major ([64][D], 256-byte rows) in the q, k, v tile buffers,
+  // one tensor-map copy each; rows past T arrive as zeros (thread 0)
+  auto issue_rows = [&](int c, int h, int b) {
+    const int t0 = lay.span(ws, c).t0, hk = h / lay.rep;
+    mbar_arrive_expect_tx(bar + 1, (uint32_t)(64 * (2 * DK + DV) * 2));
+    tma_load_4d(smem + S::q, &tm_q, 0, hk, t0, b, bar + 1);
+    tma_load_4d(smem + S::k, &tm_k, 0, hk, t0, b, bar + 1);
+    tma_load_4d(smem + S::v, &tm_v, 0, h, t0, b, bar + 1);
+  };
 
   GD_TRACE_AT(ws, lay, 0);
   GD_TRACE_CTA(ws, lay, 0);
+  long long it = blockIdx.x;
+  int c, h, b;
+  item_of(it, c, h, b);
+  float gi, bi;
+  load_gb(c, h, b, gi, bi);
   if (tid == 0) {
     mbar_init(bar, 1);      // MMA commits
     mbar_init(bar + 1, 1);  // raw q / k / v rows landed
     fence_mbar_init();
+    if (staged) issue_rows(c, h, b);
   }
-  constexpr bool staged = sizeof(T) == 2;
-  // this chunk's g and beta (threads 0-63, one token each; padding rows: g = 0, beta = 0, which leaves G constant
-  // past the last token), loaded now so that their latency hides under the row loads
-  float gi = 0.f, bi = 0.f;
-  if (tid < 64 && t0 + tid < tend) {
-    gi = __ldg(g + ((size_t)b * lay.Tin + t0 + tid) * lay.H + h);
-    bi = __ldg(beta + ((size_t)b * lay.Tin + t0 + tid) * lay.H + h);
-  }
-  if constexpr (staged) {
-    // 16-bit inputs: the chunk's raw q, k, v rows land row-major ([64][D], 256-byte rows) in the q, k, v tile buffers,
-    // one tensor-map copy each; rows past T arrive as zeros
-    if (tid == 0) {
-      mbar_arrive_expect_tx(bar + 1, (uint32_t)(64 * (2 * DK + DV) * 2));
-      tma_load_4d(smem + S::q, &tm_q, 0, hk, t0, b, bar + 1);
-      tma_load_4d(smem + S::k, &tm_k, 0, hk, t0, b, bar + 1);
-      tma_load_4d(smem + S::v, &tm_v, 0, h, t0, b, bar + 1);
-    }
-    __syncthreads();  // the barrier is initialised before anyone waits on it
-  }
+  __syncthreads();  // the barriers are initialised before anyone waits on them
   if (warp == 0) {
     tmem_alloc(tslot, 256);
     tmem_relinquish();
   }
-
-  // l2 prologue and operand tiles: every row load in flight before any is converted
+  GD_TRACE_AT(ws, lay, 15);
   const bool norm = (flags & GD_L2NORM) != 0;
-  const bool bwd = BWD && (h % lay.rep == 0);
-  const size_t rrow = (((size_t)b * lay.HK + hk) * lay.NT + c) * 64;  // this chunk's 64 rsqrt slots
-  float* rq = bwd ? reinterpret_cast<float*>(ws + lay.rq) + rrow : nullptr;
-  float* rk = bwd ? reinterpret_cast<float*>(ws + lay.rk) + rrow : nullptr;
   const float qscale = q_scale(flags, DK);
-  Rows<T, DK, 8, staged> rq_rows, rk_rows;
-  Rows<T, DV, 8, staged> rv_rows;
-  GD_TRACE_AT(ws, lay, 21);
-  bool landed = true;
-  if constexpr (staged) {
-    // each warp converts its own 8 rows in place: raw rows 8 w .. 8 w + 7 and tile row block w are the same 2 KB
-    landed = mbar_wait(bar + 1, 0, err, 13);
-    rq_rows.issue_staged(smem + S::q, t0, tend);
-    rk_rows.issue_staged(smem + S::k, t0, tend);
-    rv_rows.issue_staged(smem + S::v, t0, tend);
-    __syncwarp();
-  } else {
-    rq_rows.issue(q, b, t0, lay.Tin, tend, lay.HK, hk);
-    rk_rows.issue(k, b, t0, lay.Tin, tend, lay.HK, hk);
-  }
-  GD_TRACE_AT(ws, lay, 22);
-  rq_rows.finish(t0, tend, norm, qscale, smem + S::q, rq, smem + S::ql);
-  GD_TRACE_AT(ws, lay, 23);
-  rk_rows.finish(t0, tend, norm, 1.f, smem + S::k, rk, smem + S::kl);
-  GD_TRACE_AT(ws, lay, 24);
-  if (!staged) rv_rows.issue(v, b, t0, lay.Tin, tend, lay.H, h);
-  rv_rows.finish(t0, tend, false, 1.f, smem + S::v, nullptr, nullptr);
-  GD_TRACE_AT(ws, lay, 1);
 
-  // cumulative log decay
-  if (tid < 64) {
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const float y = __shfl_up_sync(0xffffffffu, gi, o);
-      if (lane >= o) gi += y;
+  for (int n = 0;; ++n) {
+    const int tb = 64 * (n < 3 ? n : 3);  // trace slots of the item (the fourth and later share the last set)
+    const int hk = h / lay.rep;
+    // the chunk's rows in the caller's arrays: t0 .. t0 + 63, those below tend valid (the sequence's end)
+    const ChunkSpan span = lay.span(ws, c);
+    const int t0 = span.t0, tend = span.end;
+    const size_t cidx = ((size_t)b * lay.H + h) * lay.NT + c;
+
+    // l2 prologue and operand tiles: every row load in flight before any is converted
+    const bool bwd = BWD && (h % lay.rep == 0);
+    const size_t rrow = (((size_t)b * lay.HK + hk) * lay.NT + c) * 64;  // this chunk's 64 rsqrt slots
+    float* rq = bwd ? reinterpret_cast<float*>(ws + lay.rq) + rrow : nullptr;
+    float* rk = bwd ? reinterpret_cast<float*>(ws + lay.rk) + rrow : nullptr;
+    Rows<T, DK, 8, staged> rq_rows, rk_rows;
+    Rows<T, DV, 8, staged> rv_rows;
+    GD_TRACE_AT(ws, lay, tb + 21);
+    bool landed = true;
+    if constexpr (staged) {
+      // each warp converts its own 8 rows in place: raw rows 8 w .. 8 w + 7 and tile row block w are the same 2 KB
+      landed = mbar_wait(bar + 1, n & 1, err, 13);
+      rq_rows.issue_staged(smem + S::q, t0, tend);
+      rk_rows.issue_staged(smem + S::k, t0, tend);
+      rv_rows.issue_staged(smem + S::v, t0, tend);
+      __syncwarp();
+    } else {
+      rq_rows.issue(q, b, t0, lay.Tin, tend, lay.HK, hk);
+      rk_rows.issue(k, b, t0, lay.Tin, tend, lay.HK, hk);
     }
-    float* scan = reinterpret_cast<float*>(smem + S::scan);
-    if (lane == 31) scan[warp] = gi;
-    sB[tid] = bi;
-    sG[tid] = gi;  // warp 1 adds warp 0's total below
-  }
-  fence_async_smem();
-  tc_fence_before();
-  __syncthreads();
-  float* sGam = reinterpret_cast<float*>(smem + S::gam);
-  float* sBG = reinterpret_cast<float*>(smem + S::bgam);
-  if (tid < 64) {  // each thread finishes its own token: G, gamma, beta gamma
-    if (tid >= 32) sG[tid] += reinterpret_cast<float*>(smem + S::scan)[0];
-    sGam[tid] = __expf(sG[tid]);
-    sBG[tid] = sB[tid] * sGam[tid];
-  }
-  tc_fence_after();
-  const uint32_t tm = *tslot;
-  __syncthreads();  // G, gamma complete for everyone
+    GD_TRACE_AT(ws, lay, tb + 22);
+    rq_rows.finish(t0, tend, norm, qscale, smem + S::q, rq, smem + S::ql);
+    GD_TRACE_AT(ws, lay, tb + 23);
+    rk_rows.finish(t0, tend, norm, 1.f, smem + S::k, rk, smem + S::kl);
+    GD_TRACE_AT(ws, lay, tb + 24);
+    if (!staged) rv_rows.issue(v, b, t0, lay.Tin, tend, lay.H, h);
+    rv_rows.finish(t0, tend, false, 1.f, smem + S::v, nullptr, nullptr);
+    GD_TRACE_AT(ws, lay, tb + 1);
 
-  // [Q; K] K^T with q and k carried as bf16 hi + lo (three products): lanes 0-63 hold Q K^T rows, 64-127 K K^T rows.
-  // Issued after the barrier: the issue blocks thread 0 while the other warps write the images below.
-  if (tid == 0) {
-    const Tile qkh{smem_u32(smem + S::q), DK}, qkl{smem_u32(smem + S::ql), DK};
-    const Tile kh{smem_u32(smem + S::k), DK}, kl{smem_u32(smem + S::kl), DK};
-    mma_tiles(tm, 128, 64, DK, qkh, true, 0, 0, kh, false, 0, false);
-    mma_tiles(tm, 128, 64, DK, qkh, true, 0, 0, kl, false, 0, true);
-    mma_tiles(tm, 128, 64, DK, qkl, true, 0, 0, kh, false, 0, true);
-    mma_commit(bar);
-  }
-  GD_TRACE_AT(ws, lay, 2);
-  if constexpr (BWD) {  // the low halves go out (transposed images) before L and A overwrite them
-    unsigned char* dst = ws + lay.qkl + cidx * lay.qk_bytes();
-    store_tile_transposed<64, DK, 8>(smem + S::ql, dst);
-    store_tile_transposed<64, DK, 8>(smem + S::kl, dst + 64 * DK * 2);
-  }
-  {  // K~ = diag(e) K (e_i = exp(G_last - G_i) <= 1) from k's hi + lo, split again: the state update's operand
-    unsigned char* kth = ws + lay.kt + cidx * lay.qk_bytes();
-    unsigned char* ktl = kth + 64 * DK * 2;
-    const float Glast = sG[63];
-    for (int idx = tid; idx < 64 * DK / 8; idx += 256) {
-      const int rl = idx & 7, cb = (idx >> 3) % (DK / 8), rb = idx / (8 * (DK / 8));
-      const int r = 8 * rb + rl;
-      const uint4 uh = *reinterpret_cast<const uint4*>(smem + S::k + blk_off(r, 8 * cb, DK));
-      const uint4 ul = *reinterpret_cast<const uint4*>(smem + S::kl + blk_off(r, 8 * cb, DK));
-      const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&uh);
-      const __nv_bfloat162* l2 = reinterpret_cast<const __nv_bfloat162*>(&ul);
-      const float er = __expf(Glast - sG[r]);
-      float x[8];
+    // cumulative log decay
+    if (tid < 64) {
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 fh = __bfloat1622float2(h2[e]), fl = __bfloat1622float2(l2[e]);
-        x[2 * e] = er * (fh.x + fl.x);
-        x[2 * e + 1] = er * (fh.y + fl.y);
+      for (int o = 1; o < 32; o <<= 1) {
+        const float y = __shfl_up_sync(0xffffffffu, gi, o);
+        if (lane >= o) gi += y;
       }
-      store8_split(kth, ktl, r, 8 * cb, DK, x);
+      float* scan = reinterpret_cast<float*>(smem + S::scan);
+      if (lane == 31) scan[warp] = gi;
+      sB[tid] = bi;
+      sG[tid] = gi;  // warp 1 adds warp 0's total below
     }
-  }
-  GD_TRACE_AT(ws, lay, 3);
-  bool ok = mbar_wait(bar, 0, err, 10) && landed;
-  GD_TRACE_AT(ws, lay, 4);
-  ok = __syncthreads_and(ok);
-  tc_fence_after();
-  if (ok) {
-    // warp w: accumulator rows 32 (w % 4) + lane (Q K^T for w % 4 < 2, K K^T otherwise), columns 32 (w / 4) .. + 31
-    const int i = tid & 63;
-    const float Gi = sG[i];
-    float acc[32];
-    unsigned char* mimg = ws + lay.m + cidx * lay.mm_bytes();
-    {
-      const int half = warp >> 2;
-      GD_TRACE_WARP(ws, lay, 0);
-      tmem_ld32(tmem_lane_addr(tm, warp, 32 * half), acc);
-      GD_TRACE_AT(ws, lay, 25);
-      GD_TRACE_WARP(ws, lay, 1);
-      // the decay exp(G_i - G_j), computed for every column and then masked by keep_if (no branches)
-      const bool is_m = (warp & 3) < 2;
-      const int jmax = is_m ? i : i - 1;  // M keeps j <= i, L keeps j < i
-      const float bi = is_m ? 1.f : sB[i];
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    float* sGam = reinterpret_cast<float*>(smem + S::gam);
+    float* sBG = reinterpret_cast<float*>(smem + S::bgam);
+    float* sRng = reinterpret_cast<float*>(smem + S::rng);
+    float* sColf = reinterpret_cast<float*>(smem + S::colf);
+    if (tid < 64) {  // each thread finishes its own token: G, gamma, beta gamma, and its warp's range of G
+      if (tid >= 32) sG[tid] += reinterpret_cast<float*>(smem + S::scan)[0];
+      sGam[tid] = __expf(sG[tid]);
+      sBG[tid] = sB[tid] * sGam[tid];
+      float mx = sG[tid], mn = mx;
 #pragma unroll
-      for (int q4 = 0; q4 < 8; ++q4) {
-        const float4 g4 = *reinterpret_cast<const float4*>(sG + 32 * half + 4 * q4);
-        const float gv[4] = {g4.x, g4.y, g4.z, g4.w};
+      for (int o = 16; o > 0; o >>= 1) {
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+      }
+      if (lane == 0) {
+        sRng[2 * warp] = mx;
+        sRng[2 * warp + 1] = mn;
+      }
+    }
+    tc_fence_after();
+    const uint32_t tm = *tslot;
+    __syncthreads();  // G, gamma complete for everyone
+    // The decay exp(G_i - G_j) of the C x C products factors as exp(G_i - G_ref) exp(G_ref - G_j) with G_ref the middle
+    // of the chunk's range of G: 64 column factors here and one row factor per thread below instead of 32 exponentials
+    // per thread. Taken when the range is at most 80 (every factor within e^-40 .. e^40, so no product of two factors
+    // leaves the normal fp32 range); wider ranges (or NaN) take one exponential per element.
+    const float gmax = fmaxf(sRng[0], sRng[2]), gmin = fminf(sRng[1], sRng[3]);
+    const float gref = 0.5f * gmax + 0.5f * gmin;
+    const bool factored = gmax - gmin <= 80.f;
+
+    // [Q; K] K^T with q and k carried as bf16 hi + lo (three products): lanes 0-63 hold Q K^T rows, 64-127 K K^T rows.
+    // Issued after the barrier: the issue blocks thread 0 while the other warps write the images below.
+    if (tid == 0) {
+      const Tile qkh{smem_u32(smem + S::q), DK}, qkl{smem_u32(smem + S::ql), DK};
+      const Tile kh{smem_u32(smem + S::k), DK}, kl{smem_u32(smem + S::kl), DK};
+      mma_tiles(tm, 128, 64, DK, qkh, true, 0, 0, kh, false, 0, false);
+      mma_tiles(tm, 128, 64, DK, qkh, true, 0, 0, kl, false, 0, true);
+      mma_tiles(tm, 128, 64, DK, qkl, true, 0, 0, kh, false, 0, true);
+      mma_commit(bar);
+    }
+    GD_TRACE_AT(ws, lay, tb + 2);
+    if (factored && tid >= 192) sColf[tid - 192] = __expf(gref - sG[tid - 192]);
+    if constexpr (BWD) {  // the low halves go out (transposed images) before L and A overwrite them
+      unsigned char* dst = ws + lay.qkl + cidx * lay.qk_bytes();
+      store_tile_transposed<64, DK, 8>(smem + S::ql, dst);
+      store_tile_transposed<64, DK, 8>(smem + S::kl, dst + 64 * DK * 2);
+    }
+    {  // K~ = diag(e) K (e_i = exp(G_last - G_i) <= 1) from k's hi + lo, split again: the state update's operand
+      unsigned char* kth = ws + lay.kt + cidx * lay.qk_bytes();
+      unsigned char* ktl = kth + 64 * DK * 2;
+      const float Glast = sG[63];
+      for (int idx = tid; idx < 64 * DK / 8; idx += 256) {
+        const int rl = idx & 7, cb = (idx >> 3) % (DK / 8), rb = idx / (8 * (DK / 8));
+        const int r = 8 * rb + rl;
+        const uint4 uh = *reinterpret_cast<const uint4*>(smem + S::k + blk_off(r, 8 * cb, DK));
+        const uint4 ul = *reinterpret_cast<const uint4*>(smem + S::kl + blk_off(r, 8 * cb, DK));
+        const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&uh);
+        const __nv_bfloat162* l2 = reinterpret_cast<const __nv_bfloat162*>(&ul);
+        const float er = __expf(Glast - sG[r]);
+        float x[8];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int jj = 4 * q4 + u;
-          acc[jj] = keep_if(bi * acc[jj] * __expf(Gi - gv[u]), 32 * half + jj <= jmax);
+        for (int e = 0; e < 4; ++e) {
+          const float2 fh = __bfloat1622float2(h2[e]), fl = __bfloat1622float2(l2[e]);
+          x[2 * e] = er * (fh.x + fl.x);
+          x[2 * e + 1] = er * (fh.y + fl.y);
         }
-      }
-      GD_TRACE_WARP(ws, lay, 2);
-      if (is_m) {
-#pragma unroll
-        for (int q8 = 0; q8 < 4; ++q8)
-          store8_split(mimg, mimg + lay.m_bytes(), i, 32 * half + 8 * q8, 64, acc + 8 * q8);
-      } else {
-        float4* lrow = reinterpret_cast<float4*>(sL + i * 68 + 32 * half);
-#pragma unroll
-        for (int q4 = 0; q4 < 8; ++q4)
-          lrow[q4] = make_float4(acc[4 * q4], acc[4 * q4 + 1], acc[4 * q4 + 2], acc[4 * q4 + 3]);
+        store8_split(kth, ktl, r, 8 * cb, DK, x);
       }
     }
-  }
-  GD_TRACE_AT(ws, lay, 26);
-  GD_TRACE_WARP(ws, lay, 3);
-  __syncthreads();
-  GD_TRACE_AT(ws, lay, 5);
-  // (ok is the same in every thread: the barriers inside are reached by all or none)
-  if (ok) unit_lower_inverse(sL, sAi, reinterpret_cast<float*>(smem + S::a1), ws, lay);
-  __syncthreads();  // A complete for everyone
-  GD_TRACE_AT(ws, lay, 6);
-
-  if (ok) {
-    // A diag(beta gamma) and the hi/lo split of A diag(beta) as K-major B operands (rows i, cols j)
-    const int i = tid >> 2, j0 = 16 * (tid & 3);
+    GD_TRACE_AT(ws, lay, tb + 3);
+    bool ok = mbar_wait(bar, 0, err, 10) && landed;
+    GD_TRACE_AT(ws, lay, tb + 4);
+    ok = __syncthreads_and(ok);
+    tc_fence_after();
+    if (ok) {
+      // warp w: accumulator rows 32 (w % 4) + lane (Q K^T for w % 4 < 2, K K^T otherwise), columns 32 (w / 4) .. + 31
+      const int i = tid & 63;
+      const float Gi = sG[i];
+      float acc[32];
+      unsigned char* mimg = ws + lay.m + cidx * lay.mm_bytes();
+      {
+        const int half = warp >> 2;
+        GD_TRACE_WARP(ws, lay, 0);
+        tmem_ld32(tmem_lane_addr(tm, warp, 32 * half), acc);
+        GD_TRACE_AT(ws, lay, tb + 25);
+        GD_TRACE_WARP(ws, lay, 1);
+        // the decay exp(G_i - G_j), computed for every column and then masked by keep_if (no branches)
+        const bool is_m = (warp & 3) < 2;
+        const int jmax = is_m ? i : i - 1;  // M keeps j <= i, L keeps j < i
+        const float bi = is_m ? 1.f : sB[i];
+        if (factored) {
+          const float rf = bi * __expf(Gi - gref);
 #pragma unroll
-    for (int q8 = 0; q8 < 2; ++q8) {
-      float a0[8], a1[8], a2[8];
+          for (int q4 = 0; q4 < 8; ++q4) {
+            const float4 c4 = *reinterpret_cast<const float4*>(sColf + 32 * half + 4 * q4);
+            const float cv[4] = {c4.x, c4.y, c4.z, c4.w};
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const int j = j0 + 8 * q8 + e;
-        a0[e] = sAi[i * 68 + j];
-        a1[e] = a0[e] * sBG[j];
-        a2[e] = a0[e] * sB[j];
-      }
-      store8_split(smem + S::a1, smem + S::a1l, i, j0 + 8 * q8, 64, a1);
-      store8_split(smem + S::a2h, smem + S::a2l, i, j0 + 8 * q8, 64, a2);
-    }
-  }
-  // (the backward's A and V^T images go out after the MMAs are issued: global stores ahead of this proxy fence would
-  // hold it until they complete)
-  fence_async_smem();
-  GD_TRACE_AT(ws, lay, 7);
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  if (ok && tid == 0) {
-    // W^T [DK x 64] = K^T (A diag(beta gamma))^T ; U^T [DV x 64] = V^T (A diag(beta))^T (both A factors hi + lo:
-    // with nearly parallel keys W is a difference of nearly equal rows, which a one-bf16 A diag(beta gamma) loses)
-    mma_tiles(tm + 64, DK, 64, 64, Tile{smem_u32(smem + S::k), DK}, false, 0, 0, Tile{smem_u32(smem + S::a1), 64},
-              false, 0, false);
-    mma_tiles(tm + 64, DK, 64, 64, Tile{smem_u32(smem + S::k), DK}, false, 0, 0, Tile{smem_u32(smem + S::a1l), 64},
-              false, 0, true);
-    mma_tiles(tm + 128, DV, 64, 64, Tile{smem_u32(smem + S::v), DV}, false, 0, 0, Tile{smem_u32(smem + S::a2h), 64},
-              false, 0, false);
-    mma_tiles(tm + 128, DV, 64, 64, Tile{smem_u32(smem + S::v), DV}, false, 0, 0, Tile{smem_u32(smem + S::a2l), 64},
-              false, 0, true);
-    mma_commit(bar);
-  }
-  // the q / k images and G go out while the MMAs run (the k image only for the backward), and for the backward the
-  // A image and the transposed V image ([DV x 64], rows v)
-  if (ok) {
-    unsigned char* dst = ws + lay.qk + cidx * lay.qk_bytes();  // transposed images ([DK x 64], rows d)
-    store_tile_transposed<64, DK, 8>(smem + S::q, dst);
-    if constexpr (BWD) {
-      store_tile_transposed<64, DK, 8>(smem + S::k, dst + 64 * DK * 2);
-      store_tile_transposed<64, DV, 8>(smem + S::v, ws + lay.vi + cidx * lay.vi_bytes());
-      unsigned char* aimg = ws + lay.ai + cidx * lay.mm_bytes();  // A hi, then lo
-      const int i = tid >> 2, j0 = 16 * (tid & 3);
-#pragma unroll
-      for (int q8 = 0; q8 < 2; ++q8) store8_split(aimg, aimg + lay.m_bytes(), i, j0 + 8 * q8, 64, sAi + i * 68 + j0 + 8 * q8);
-    }
-    if (tid < 64) reinterpret_cast<float*>(ws + lay.gc + cidx * lay.gc_bytes())[tid] = sG[tid];
-  }
-  if (ok) ok = mbar_wait(bar, 1, err, 11);
-  GD_TRACE_AT(ws, lay, 8);
-  ok = __syncthreads_and(ok);
-  tc_fence_after();
-  if (ok) {
-    float acc[32];
-    const int row = tid & 127;
-    if (warp < 4) {  // W^T row dk = row -> blocked [DK x 64] image (and its low half for the backward), 16-byte stores
-      unsigned char* wimg = ws + lay.wt + cidx * lay.wt_bytes();
-      unsigned char* wlimg = ws + lay.wtl + cidx * lay.wt_bytes();
-#pragma unroll 1
-      for (int half = 0; half < 2; ++half) {
-        tmem_ld32(tmem_lane_addr(tm, warp, 64 + 32 * half), acc);
-        if constexpr (BWD) {
-#pragma unroll
-          for (int q8 = 0; q8 < 4; ++q8) store8_split(wimg, wlimg, row, 32 * half + 8 * q8, 64, acc + 8 * q8);
+            for (int u = 0; u < 4; ++u) {
+              const int jj = 4 * q4 + u;
+              acc[jj] = keep_if(acc[jj] * (rf * cv[u]), 32 * half + jj <= jmax);
+            }
+          }
         } else {
 #pragma unroll
-          for (int q8 = 0; q8 < 4; ++q8) store8_bf16(wimg, row, 32 * half + 8 * q8, 64, acc + 8 * q8);
+          for (int q4 = 0; q4 < 8; ++q4) {
+            const float4 g4 = *reinterpret_cast<const float4*>(sG + 32 * half + 4 * q4);
+            const float gv[4] = {g4.x, g4.y, g4.z, g4.w};
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const int jj = 4 * q4 + u;
+              acc[jj] = keep_if(bi * acc[jj] * __expf(Gi - gv[u]), 32 * half + jj <= jmax);
+            }
+          }
+        }
+        GD_TRACE_WARP(ws, lay, 2);
+        if (is_m) {
+#pragma unroll
+          for (int q8 = 0; q8 < 4; ++q8)
+            store8_split(mimg, mimg + lay.m_bytes(), i, 32 * half + 8 * q8, 64, acc + 8 * q8);
+        } else {
+          float4* lrow = reinterpret_cast<float4*>(sL + i * 68 + 32 * half);
+#pragma unroll
+          for (int q4 = 0; q4 < 8; ++q4)
+            lrow[q4] = make_float4(acc[4 * q4], acc[4 * q4 + 1], acc[4 * q4 + 2], acc[4 * q4 + 3]);
         }
       }
-    } else {  // U^T row v = row -> U [64][DV] fp32
-      float* u = reinterpret_cast<float*>(ws + lay.u + cidx * lay.u_bytes());
-#pragma unroll 1
-      for (int half = 0; half < 2; ++half) {
-        tmem_ld32(tmem_lane_addr(tm, warp, 128 + 32 * half), acc);
+    }
+    GD_TRACE_AT(ws, lay, tb + 26);
+    GD_TRACE_WARP(ws, lay, 3);
+    __syncthreads();
+    GD_TRACE_AT(ws, lay, tb + 5);
+    // (ok is the same in every thread: the barriers inside are reached by all or none)
+    if (ok) unit_lower_inverse(sL, sAi, reinterpret_cast<float*>(smem + S::a1), ws, lay, tb);
+    __syncthreads();  // A complete for everyone
+    GD_TRACE_AT(ws, lay, tb + 6);
+
+    if (ok) {
+      // A diag(beta gamma) and the hi/lo split of A diag(beta) as K-major B operands (rows i, cols j). A warp takes 32
+      // consecutive rows at one column block: its 16-byte reads of A (row stride 68 floats) and its 16-byte writes of
+      // the blocked tiles both fall on distinct banks in every group of eight lanes.
+      const int i = tid & 63, j0 = 16 * (tid >> 6);
 #pragma unroll
-        for (int jj = 0; jj < 32; ++jj) u[(32 * half + jj) * DV + row] = acc[jj];
+      for (int q8 = 0; q8 < 2; ++q8) {
+        const int jb = j0 + 8 * q8;
+        const float4 x0 = *reinterpret_cast<const float4*>(sAi + i * 68 + jb);
+        const float4 x1 = *reinterpret_cast<const float4*>(sAi + i * 68 + jb + 4);
+        const float a0[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+        float a1[8], a2[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          a1[e] = a0[e] * sBG[jb + e];
+          a2[e] = a0[e] * sB[jb + e];
+        }
+        store8_split(smem + S::a1, smem + S::a1l, i, jb, 64, a1);
+        store8_split(smem + S::a2h, smem + S::a2l, i, jb, 64, a2);
       }
     }
+    // (the backward's A and V^T images go out after the MMAs are issued: global stores ahead of this proxy fence would
+    // hold it until they complete)
+    fence_async_smem();
+    GD_TRACE_AT(ws, lay, tb + 7);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (ok && tid == 0) {
+      // W^T [DK x 64] = K^T (A diag(beta gamma))^T ; U^T [DV x 64] = V^T (A diag(beta))^T (both A factors hi + lo:
+      // with nearly parallel keys W is a difference of nearly equal rows, which a one-bf16 A diag(beta gamma) loses)
+      mma_tiles(tm + 64, DK, 64, 64, Tile{smem_u32(smem + S::k), DK}, false, 0, 0, Tile{smem_u32(smem + S::a1), 64},
+                false, 0, false);
+      mma_tiles(tm + 64, DK, 64, 64, Tile{smem_u32(smem + S::k), DK}, false, 0, 0, Tile{smem_u32(smem + S::a1l), 64},
+                false, 0, true);
+      mma_tiles(tm + 128, DV, 64, 64, Tile{smem_u32(smem + S::v), DV}, false, 0, 0, Tile{smem_u32(smem + S::a2h), 64},
+                false, 0, false);
+      mma_tiles(tm + 128, DV, 64, 64, Tile{smem_u32(smem + S::v), DV}, false, 0, 0, Tile{smem_u32(smem + S::a2l), 64},
+                false, 0, true);
+      mma_commit(bar);
+    }
+    GD_TRACE_AT(ws, lay, tb + 10);
+    // the q / k images and G go out while the MMAs run (the k image only for the backward), and for the backward the
+    // A image and the transposed V image ([DV x 64], rows v)
+    if (ok) {
+      unsigned char* dst = ws + lay.qk + cidx * lay.qk_bytes();  // transposed images ([DK x 64], rows d)
+      store_tile_transposed<64, DK, 8>(smem + S::q, dst);
+      GD_TRACE_AT(ws, lay, tb + 11);
+      if constexpr (BWD) {
+        store_tile_transposed<64, DK, 8>(smem + S::k, dst + 64 * DK * 2);
+        store_tile_transposed<64, DV, 8>(smem + S::v, ws + lay.vi + cidx * lay.vi_bytes());
+        unsigned char* aimg = ws + lay.ai + cidx * lay.mm_bytes();  // A hi, then lo
+        const int i = tid & 63, j0 = 16 * (tid >> 6);
+#pragma unroll
+        for (int q8 = 0; q8 < 2; ++q8) {
+          const float4 x0 = *reinterpret_cast<const float4*>(sAi + i * 68 + j0 + 8 * q8);
+          const float4 x1 = *reinterpret_cast<const float4*>(sAi + i * 68 + j0 + 8 * q8 + 4);
+          const float a0[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+          store8_split(aimg, aimg + lay.m_bytes(), i, j0 + 8 * q8, 64, a0);
+        }
+      }
+      GD_TRACE_AT(ws, lay, tb + 12);
+      if (tid < 64) reinterpret_cast<float*>(ws + lay.gc + cidx * lay.gc_bytes())[tid] = sG[tid];
+    }
+    GD_TRACE_AT(ws, lay, tb + 27);
+    if (ok) ok = mbar_wait(bar, 1, err, 11);
+    GD_TRACE_AT(ws, lay, tb + 8);
+    ok = __syncthreads_and(ok);
+    tc_fence_after();
+    // the W / U products have read k and v and every image store has read q, k, v: the next item's rows may land
+    const long long nx = it + gridDim.x;
+    const bool more = ok && nx < n_items;
+    int cn = 0, hn = 0, bn = 0;
+    float g_next = 0.f, beta_next = 0.f;
+    if (more) {
+      item_of(nx, cn, hn, bn);
+      if (staged && tid == 0) {
+        fence_async_smem();
+        issue_rows(cn, hn, bn);
+      }
+      load_gb(cn, hn, bn, g_next, beta_next);
+    }
+    if (ok) {
+      float acc[32];
+      const int row = tid & 127;
+      if (warp < 4) {  // W^T row dk = row -> blocked [DK x 64] image (and its low half for the backward), 16-byte stores
+        unsigned char* wimg = ws + lay.wt + cidx * lay.wt_bytes();
+        unsigned char* wlimg = ws + lay.wtl + cidx * lay.wt_bytes();
+#pragma unroll 1
+        for (int half = 0; half < 2; ++half) {
+          tmem_ld32(tmem_lane_addr(tm, warp, 64 + 32 * half), acc);
+          if constexpr (BWD) {
+#pragma unroll
+            for (int q8 = 0; q8 < 4; ++q8) store8_split(wimg, wlimg, row, 32 * half + 8 * q8, 64, acc + 8 * q8);
+          } else {
+#pragma unroll
+            for (int q8 = 0; q8 < 4; ++q8) store8_bf16(wimg, row, 32 * half + 8 * q8, 64, acc + 8 * q8);
+          }
+        }
+      } else {  // U^T row v = row -> U [64][DV] fp32
+        float* u = reinterpret_cast<float*>(ws + lay.u + cidx * lay.u_bytes());
+#pragma unroll 1
+        for (int half = 0; half < 2; ++half) {
+          tmem_ld32(tmem_lane_addr(tm, warp, 128 + 32 * half), acc);
+#pragma unroll
+          for (int jj = 0; jj < 32; ++jj) u[(32 * half + jj) * DV + row] = acc[jj];
+        }
+      }
+    }
+    GD_TRACE_AT(ws, lay, tb + 9);
+    tc_fence_before();
+    __syncthreads();  // the accumulators are read before the next item's products overwrite them
+    GD_TRACE_AT(ws, lay, tb + 28);
+    if (!more) break;
+    it = nx;
+    c = cn;
+    h = hn;
+    b = bn;
+    gi = g_next;
+    bi = beta_next;
   }
-  GD_TRACE_AT(ws, lay, 9);
-  tc_fence_before();
-  __syncthreads();
   if (warp == 0) {
     tc_fence_after();
-    tmem_dealloc(tm, 256);
+    tmem_dealloc(*tslot, 256);
   }
   GD_TRACE_CTA(ws, lay, 1);
 }
@@ -810,7 +904,24 @@ cudaError_t launch_prep(const void* q, const void* k, const void* v, const float
         !rows_map(&mv, v, dt, lay.B, lay.Tin, lay.H, DV))
       return cudaErrorInvalidValue;
   }
-  dim3 grid(lay.NT, lay.H, lay.B);
+  // persistent: as many CTAs as fit on the GPU at once, at most one per item. Two per SM by the launch bounds
+  // (registers), fewer if the SM's shared memory (less the per-block reservation) holds fewer.
+  static int slots[kMaxDevices] = {};
+  int dev = 0;
+  if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  if (slots[dev] == 0) {
+    int sms = 0, smem_sm = 0, reserved = 0;
+    if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
+    if ((e = cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev)) != cudaSuccess)
+      return e;
+    if ((e = cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev)) != cudaSuccess) return e;
+    const int fit = smem_sm / (int)(S::total + reserved);
+    slots[dev] = sms * (fit < 2 ? (fit < 1 ? 1 : fit) : 2);
+  }
+  const int n_slots = slots[dev];
+  const long long items = (long long)lay.NT * lay.H * lay.B;
+  const int grid = (int)(items < n_slots ? items : n_slots);
   kern<<<grid, 256, S::total, st>>>(static_cast<const T*>(q), static_cast<const T*>(k), static_cast<const T*>(v), g,
                                     beta, lay, flags, ws, mq, mk, mv);
   return cudaGetLastError();
