@@ -78,6 +78,34 @@ __device__ __forceinline__ void strip(const float* X, int xs, const float* Z, in
   *reinterpret_cast<float4*>(out + i * os + j0) = make_float4(sign * acc.x, sign * acc.y, sign * acc.z, sign * acc.w);
 }
 
+// The same for rows i and i + 16 at once: each 16-byte read of Z feeds both rows (8 FMAs), so a 32 x 32 product takes
+// 128 threads and ~40 % fewer shared-memory reads than four-column strips on 256 threads.
+template <int N>
+__device__ __forceinline__ void strip2(const float* X, int xs, const float* Z, int zs, float* out, int os, float sign,
+                                       int i, int j0) {
+  float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0;
+#pragma unroll
+  for (int m4 = 0; m4 < N; m4 += 4) {
+    const float4 x0 = *reinterpret_cast<const float4*>(X + i * xs + m4);
+    const float4 x1 = *reinterpret_cast<const float4*>(X + (i + 16) * xs + m4);
+    const float xv0[4] = {x0.x, x0.y, x0.z, x0.w}, xv1[4] = {x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const float4 z = *reinterpret_cast<const float4*>(Z + (m4 + u) * zs + j0);
+      a0.x = fmaf(xv0[u], z.x, a0.x);
+      a0.y = fmaf(xv0[u], z.y, a0.y);
+      a0.z = fmaf(xv0[u], z.z, a0.z);
+      a0.w = fmaf(xv0[u], z.w, a0.w);
+      a1.x = fmaf(xv1[u], z.x, a1.x);
+      a1.y = fmaf(xv1[u], z.y, a1.y);
+      a1.z = fmaf(xv1[u], z.z, a1.z);
+      a1.w = fmaf(xv1[u], z.w, a1.w);
+    }
+  }
+  *reinterpret_cast<float4*>(out + i * os + j0) = make_float4(sign * a0.x, sign * a0.y, sign * a0.z, sign * a0.w);
+  *reinterpret_cast<float4*>(out + (i + 16) * os + j0) = make_float4(sign * a1.x, sign * a1.y, sign * a1.z, sign * a1.w);
+}
+
 __device__ __forceinline__ void unit_lower_inverse(const float* L, float* A, float* Y, unsigned char* ws,
                                                    const Layout& lay, int tb) {
   const int tid = threadIdx.x;
@@ -121,12 +149,12 @@ __device__ __forceinline__ void unit_lower_inverse(const float* L, float* A, flo
               i16, j4);
   __syncthreads();
   GD_TRACE_AT(ws, lay, tb + 18);
-  // 3. Y = L[32:64][0:32] A_11 ; A[32:64][0:32] = -A_22 Y
-  const int i32 = tid >> 3, j8 = 4 * (tid & 7);
-  strip<32>(L + 32 * 68, 68, A, 68, Y, 36, 1.f, i32, j8);
+  // 3. Y = L[32:64][0:32] A_11 ; A[32:64][0:32] = -A_22 Y (threads 0-127: rows i16 and i16 + 16)
+  const int i16b = tid >> 3, j8 = 4 * (tid & 7);
+  if (tid < 128) strip2<32>(L + 32 * 68, 68, A, 68, Y, 36, 1.f, i16b, j8);
   __syncthreads();
   GD_TRACE_AT(ws, lay, tb + 19);
-  strip<32>(A + 32 * 68 + 32, 68, Y, 36, A + 32 * 68, 68, -1.f, i32, j8);
+  if (tid < 128) strip2<32>(A + 32 * 68 + 32, 68, Y, 36, A + 32 * 68, 68, -1.f, i16b, j8);
   GD_TRACE_AT(ws, lay, tb + 20);
 }
 
