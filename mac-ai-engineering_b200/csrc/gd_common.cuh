@@ -606,23 +606,31 @@ __device__ __forceinline__ void store8_bf16(unsigned char* tile, int r, int c0, 
 __device__ __forceinline__ void store4_bf16(unsigned char* tile, int r, int c0, int cols, const float* v) {
   *reinterpret_cast<uint2*>(tile + blk_off(r, c0, cols)) = make_uint2(pack_bf16(v[0], v[1]), pack_bf16(v[2], v[3]));
 }
+// (a, b) -> their bf16 high halves packed (low 16 bits: a) and the packed bf16 remainders a - hi(a), b - hi(b): the
+// values of split_bf16, with one paired conversion for the high halves (read back by shift and mask)
+__device__ __forceinline__ void split_pack_bf16(float a, float b, uint32_t& hi, uint32_t& lo) {
+  hi = pack_bf16(a, b);
+  lo = pack_bf16(a - __uint_as_float(hi << 16), b - __uint_as_float(hi & 0xffff0000u));
+}
 __device__ __forceinline__ void store4_split(unsigned char* hi_tile, unsigned char* lo_tile, int r, int c0, int cols,
                                              const float* v) {
-  float h[4], l[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) split_bf16(v[i], h[i], l[i]);
-  store4_bf16(hi_tile, r, c0, cols, h);
-  store4_bf16(lo_tile, r, c0, cols, l);
+  uint2 h, l;
+  split_pack_bf16(v[0], v[1], h.x, l.x);
+  split_pack_bf16(v[2], v[3], h.y, l.y);
+  *reinterpret_cast<uint2*>(hi_tile + blk_off(r, c0, cols)) = h;
+  *reinterpret_cast<uint2*>(lo_tile + blk_off(r, c0, cols)) = l;
 }
 
 // the same with a hi / lo split into two tiles
 __device__ __forceinline__ void store8_split(unsigned char* hi_tile, unsigned char* lo_tile, int r, int c0, int cols,
                                              const float* v) {
-  float h[8], l[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) split_bf16(v[i], h[i], l[i]);
-  store8_bf16(hi_tile, r, c0, cols, h);
-  store8_bf16(lo_tile, r, c0, cols, l);
+  uint4 h, l;
+  split_pack_bf16(v[0], v[1], h.x, l.x);
+  split_pack_bf16(v[2], v[3], h.y, l.y);
+  split_pack_bf16(v[4], v[5], h.z, l.z);
+  split_pack_bf16(v[6], v[7], h.w, l.w);
+  *reinterpret_cast<uint4*>(hi_tile + blk_off(r, c0, cols)) = h;
+  *reinterpret_cast<uint4*>(lo_tile + blk_off(r, c0, cols)) = l;
 }
 
 // A blocked [R x Cc] bf16 tile in shared memory -> its transpose, a blocked [Cc x R] image in global memory. Each warp
