@@ -241,13 +241,17 @@ __global__ void __launch_bounds__(576) bwd_state_kernel(const T* __restrict__ d_
     // the dS tiles for the next K~ dS, then (after the hand-off: the proxy fence would wait for global stores in
     // flight) this CTA's rows of chunk ci's dS_{ci+1}^T images (hi, lo) for the per-chunk kernel, from registers
     auto write_ds = [&](int ci) {
+      uint4 h[2], l[2];
 #pragma unroll
-      for (int q8 = 0; q8 < 2; ++q8) store8_split(smem + S::dsh, smem + S::dsl, vl_, dk0 + 8 * q8, DK, Dr + 8 * q8);
+      for (int q8 = 0; q8 < 2; ++q8) {
+        split8_bf16(Dr + 8 * q8, h[q8], l[q8]);
+        store8_pair(smem + S::dsh, smem + S::dsl, vl_, dk0 + 8 * q8, DK, h[q8], l[q8]);
+      }
       fence_async_smem();
       mbar_arrive_warp(ds_ready);
       unsigned char* gh = ws + lay.dsi + (row0 + ci) * 2 * lay.si_bytes() + (size_t)vbase * DK * 2;
 #pragma unroll
-      for (int q8 = 0; q8 < 2; ++q8) store8_split(gh, gh + lay.si_bytes(), vl_, dk0 + 8 * q8, DK, Dr + 8 * q8);
+      for (int q8 = 0; q8 < 2; ++q8) store8_pair(gh, gh + lay.si_bytes(), vl_, dk0 + 8 * q8, DK, h[q8], l[q8]);
     };
     // a chunk's dO tile (this CTA's 64 columns): 512 16-byte pieces, one per thread, eight consecutive threads per
     // 128-byte core matrix; fetched raw into registers early, written to the tile once the tile's readers are done
@@ -302,14 +306,15 @@ __global__ void __launch_bounds__(576) bwd_state_kernel(const T* __restrict__ d_
         tmem_ld8hx3(tmem_lane_addr(tA, warp, 16 * quarter), a, tmem_lane_addr(tB, warp, 16 * quarter), bb,
                     tmem_lane_addr(tB + 64, warp, 16 * quarter), b2);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) split_bf16(a[j] + (bb[j] + b2[j]), a[j], bb[j]);  // in place: a = hi, bb = lo
-        store8_bf16(smem + S::dvh, vl_, tk, 64, a);
-        store8_bf16(smem + S::dvl, vl_, tk, 64, bb);
+        for (int j = 0; j < 8; ++j) a[j] += bb[j] + b2[j];
+        uint4 hi, lo;
+        split8_bf16(a, hi, lo);
+        store8_pair(smem + S::dvh, smem + S::dvl, vl_, tk, 64, hi, lo);
         tc_fence_before();
         fence_async_smem();
         mbar_arrive_warp(dvn_full);
-        store8_bf16(ws + lay.dvni + cidx * lay.vn_bytes(), v, tk, 64, a);  // the image's halves straight from registers
-        store8_bf16(ws + lay.dvni + cidx * lay.vn_bytes() + DV * 64 * 2, v, tk, 64, bb);
+        unsigned char* gi = ws + lay.dvni + cidx * lay.vn_bytes();  // the image's halves straight from registers
+        store8_pair(gi, gi + DV * 64 * 2, v, tk, 64, hi, lo);
       }
       GD_TRACE_AT(ws, lay, 8 * n + 2);
       // the next chunk's dO tile (this chunk's dO products are done: a_full), published before any new load is in

@@ -622,15 +622,23 @@ __device__ __forceinline__ void store4_split(unsigned char* hi_tile, unsigned ch
 }
 
 // the same with a hi / lo split into two tiles
-__device__ __forceinline__ void store8_split(unsigned char* hi_tile, unsigned char* lo_tile, int r, int c0, int cols,
-                                             const float* v) {
-  uint4 h, l;
+// 8 floats -> their packed bf16 high halves and remainders (split_bf16's values), for storing more than once
+__device__ __forceinline__ void split8_bf16(const float* v, uint4& h, uint4& l) {
   split_pack_bf16(v[0], v[1], h.x, l.x);
   split_pack_bf16(v[2], v[3], h.y, l.y);
   split_pack_bf16(v[4], v[5], h.z, l.z);
   split_pack_bf16(v[6], v[7], h.w, l.w);
+}
+__device__ __forceinline__ void store8_pair(unsigned char* hi_tile, unsigned char* lo_tile, int r, int c0, int cols,
+                                            const uint4& h, const uint4& l) {
   *reinterpret_cast<uint4*>(hi_tile + blk_off(r, c0, cols)) = h;
   *reinterpret_cast<uint4*>(lo_tile + blk_off(r, c0, cols)) = l;
+}
+__device__ __forceinline__ void store8_split(unsigned char* hi_tile, unsigned char* lo_tile, int r, int c0, int cols,
+                                             const float* v) {
+  uint4 h, l;
+  split8_bf16(v, h, l);
+  store8_pair(hi_tile, lo_tile, r, c0, cols, h, l);
 }
 
 // A blocked [R x Cc] bf16 tile in shared memory -> its transpose, a blocked [Cc x R] image in global memory. Each warp
