@@ -99,7 +99,8 @@ int gd_fwd_state(const float* s0, void* o, float* sT, int dtype, int B, int T, i
 int gd_bwd_state(const void* d_o, const float* dsT, float* ds0, int dtype, int B, int T, int H, int HK, int DK, int DV,
                  int flags, void* workspace, size_t workspace_bytes, void* stream);
 
-/* Every per-chunk gradient, one CTA per (chunk, key head, batch row), all independent and without atomics: dq, dk
+/* Every per-chunk gradient, per (chunk, key head, batch row) item (persistent CTAs, one per SM, walk the items), all
+ * independent and without atomics: dq, dk
  * (through the l2 prologue when GD_L2NORM; summed over the value heads of a key head in a fixed order), dv, dg (with
  * the in-chunk reverse cumulative sum) and dbeta. Requires gd_bwd_state on the same workspace.
  * Replaces: lib.gdc_bwd_chunk (src/macai/gated_delta/op.py:241-242, kernel _chunked.py:905-1177) and the fused
