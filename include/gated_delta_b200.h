@@ -100,9 +100,8 @@ int gd_bwd_state(const void* d_o, const float* dsT, float* ds0, int dtype, int B
                  int flags, void* workspace, size_t workspace_bytes, void* stream);
 
 /* Every per-chunk gradient, per (chunk, key head, batch row) item (persistent CTAs, one per SM, walk the items), all
- * independent and without atomics: dq, dk
- * (through the l2 prologue when GD_L2NORM; summed over the value heads of a key head in a fixed order), dv, dg (with
- * the in-chunk reverse cumulative sum) and dbeta. Requires gd_bwd_state on the same workspace.
+ * independent and without atomics: dq, dk (through the l2 prologue when GD_L2NORM; summed over the value heads of a
+ * key head in a fixed order), dv, dg (with the in-chunk reverse cumulative sum) and dbeta. Requires gd_bwd_state on the same workspace.
  * Replaces: lib.gdc_bwd_chunk (src/macai/gated_delta/op.py:241-242, kernel _chunked.py:905-1177) and the fused
  * prologue's backward l2n_bwd_* (src/macai/gated_delta/_norm.py:44-56, applied at :102-114). */
 int gd_bwd_chunk(const void* q, const void* k, const void* v, const float* beta, const void* d_o, void* dq, void* dk,
