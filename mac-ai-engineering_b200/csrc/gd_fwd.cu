@@ -2,8 +2,9 @@
 //   prep_kernel   persistent CTAs of 256 threads (two per SM), each taking (chunk, value head, batch row) items in turn:
 //                 l2 prologue, cumulative decay, the C x C products on tcgen05, the unit-lower-triangular inverse, W and
 //                 U;
-//   state_kernel  one CTA per (value head, batch row): the sequential chunk pass with the state in registers (fp32) and
-//                 every product on tcgen05 from shared memory, chunk inputs streamed in by the bulk-copy engine.
+//   state_kernel  two CTAs per (value head, batch row), 64 value columns each (four CTAs of 32 in gd_state_narrow.cu):
+//                 the sequential chunk pass with the state in registers (fp32) and every product on tcgen05 from shared
+//                 memory, chunk inputs streamed in by the bulk-copy engine.
 // Equations (per chunk; src/macai/gated_delta/_chunked.py:1-35, tools/check_chunk_equations.py:29-46 of the reference):
 //   G = cumsum(g), gamma = exp(G), e = exp(G_last - G)
 //   L = diag(beta) (K K^T) * exp(G_i - G_j) (i > j),  M = (Q K^T) * exp(G_i - G_j) (i >= j),  A = (I + L)^-1
