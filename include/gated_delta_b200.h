@@ -83,7 +83,8 @@ size_t gd_workspace_bytes(int B, int T, int H, int HK, int DK, int DV, int for_b
 int gd_prep(const void* q, const void* k, const void* v, const float* g, const float* beta, int dtype, int B, int T,
             int H, int HK, int DK, int DV, int flags, void* workspace, size_t workspace_bytes, void* stream);
 
-/* The sequential state pass, one CTA per (batch row, value head): for each chunk in order,
+/* The sequential state pass, per (batch row, value head) with its value columns split over two or four CTAs (see
+ * GD_WIDE_STATE_PASS): for each chunk in order,
  * Vn = U - W S, O = diag(gamma) Q S + M Vn, S <- exp(G_last) S + K^T diag(e) Vn; writes o (q's dtype) and, when sT is
  * not NULL, the final state. s0 NULL = zero initial state. flags & GD_STORE_STATES: also keeps S_c and Vn per chunk in
  * the workspace (the backward's recompute, o and sT then may be NULL; or the stored-states forward, with o).
@@ -91,7 +92,8 @@ int gd_prep(const void* q, const void* k, const void* v, const float* g, const f
 int gd_fwd_state(const float* s0, void* o, float* sT, int dtype, int B, int T, int H, int HK, int DK, int DV,
                  int flags, void* workspace, size_t workspace_bytes, void* stream);
 
-/* The reverse state pass, one CTA per (batch row, value head), chunks last to first, carrying dS:
+/* The reverse state pass, per (batch row, value head) with its value columns split over two CTAs, chunks last to
+ * first, carrying dS:
  * dVn = M^T dO + diag(e) K dS, dS <- exp(G_last) dS + (diag(gamma) Q)^T dO - W^T dVn; keeps dS_{c+1} and dVn per
  * chunk in the workspace and writes ds0 (may be NULL). dsT NULL = zero. Requires gd_prep and
  * gd_fwd_state(GD_STORE_STATES) on the same workspace.
